@@ -1,0 +1,87 @@
+"""deltakv_b200 — ΔKV's cache-maintenance hot path as hand-written sm_100a kernels.
+
+Operators keep the reference's names and signatures (adityaraj-09/DeltaKV), so a ΔKV
+deployment swaps them in (see :func:`install`):
+
+* ``scatter_into_paged`` / ``gather_from_paged``   (deltakv.paged)
+* ``exact_kv_patch`` / ``zeroth_order_patches``    (deltakv.patches.exact)
+* ``apply_layer_patches``                          (deltakv.patches.compose)
+
+plus the fused batched form the engine and connector use: :class:`ExactPatcher`.
+All computation runs in ``libdkv_b200.so``; a missing library raises (no CPU path).
+"""
+
+from __future__ import annotations
+
+from deltakv_b200._lib import DkvError
+from deltakv_b200.exact import (
+    ExactPatcher,
+    apply_layer_patches,
+    exact_kv_patch,
+    materialize_codes,
+    zeroth_order_patches,
+)
+from deltakv_b200.ops import SeqBatchTensors, quantize_rows
+from deltakv_b200.paged import gather_from_paged, scatter_into_paged, scatter_into_paged_batched
+from deltakv_b200.rope import RotaryEmbedding
+from deltakv_b200.types import KVCache, LayerDelta, LowRankFactors, LowRankKVPatch
+
+__version__ = "0.1.0"
+
+__all__ = [
+    "DkvError",
+    "ExactPatcher",
+    "KVCache",
+    "LayerDelta",
+    "LowRankFactors",
+    "LowRankKVPatch",
+    "RotaryEmbedding",
+    "SeqBatchTensors",
+    "apply_layer_patches",
+    "exact_kv_patch",
+    "gather_from_paged",
+    "install",
+    "materialize_codes",
+    "quantize_rows",
+    "scatter_into_paged",
+    "scatter_into_paged_batched",
+    "zeroth_order_patches",
+]
+
+# reference module -> {attribute: replacement}
+_INSTALL_MAP = {
+    "deltakv.paged": {"scatter_into_paged": scatter_into_paged, "gather_from_paged": gather_from_paged},
+    "deltakv.patches.exact": {"exact_kv_patch": exact_kv_patch, "zeroth_order_patches": zeroth_order_patches},
+    "deltakv.patches.compose": {"apply_layer_patches": apply_layer_patches},
+    # modules that imported the names with `from ... import`
+    "deltakv.engine": {"zeroth_order_patches": zeroth_order_patches, "exact_kv_patch": exact_kv_patch,
+                       "apply_layer_patches": apply_layer_patches},
+    "deltakv.connectors.vllm": {"scatter_into_paged": scatter_into_paged},
+    "deltakv.patches": {"exact_kv_patch": exact_kv_patch, "zeroth_order_patches": zeroth_order_patches,
+                        "apply_layer_patches": apply_layer_patches},
+}
+
+
+def install(modules: dict | None = None) -> list[str]:
+    """Point an imported ``deltakv`` package at these kernels.
+
+    Rebinds the operator names in the reference's modules (and in the modules that
+    imported them by name), so ``DeltaKVEngine`` and ``DeltaKVConnector`` run the B200
+    path unchanged.  Returns the ``module.attribute`` names that were replaced.
+    """
+    import importlib
+    import sys
+
+    done = []
+    for mod_name, attrs in (modules or _INSTALL_MAP).items():
+        mod = sys.modules.get(mod_name)
+        if mod is None:
+            try:
+                mod = importlib.import_module(mod_name)
+            except ImportError:
+                continue
+        for attr, fn in attrs.items():
+            if hasattr(mod, attr):
+                setattr(mod, attr, fn)
+                done.append(f"{mod_name}.{attr}")
+    return done

@@ -1,0 +1,177 @@
+"""ctypes binding of ``libdkv_b200.so`` (the C ABI declared in ``include/dkv_b200.h``).
+
+The library is built in-tree by :mod:`deltakv_b200.build`.  Loading never falls back to
+another implementation: a missing or stale library raises immediately.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libdkv_b200.so"
+
+# status codes (dkv_b200.h)
+DKV_OK = 0
+DKV_ERR_INVALID_ARGUMENT = -1
+DKV_ERR_BLOCK_TABLE_SHORT = -2
+DKV_ERR_LAYOUT = -3
+DKV_ERR_UNSUPPORTED = -4
+DKV_ERR_ALIGNMENT = -5
+DKV_ERR_ROPE_RANGE = -6
+DKV_ERR_BASIS_DIM = -7
+DKV_ERR_CUDA = -8
+DKV_ERR_TIMEOUT = -9
+DKV_ERR_PAGE_RANGE = -10
+DKV_ERR_WORKSPACE = -11
+
+# element types
+DKV_F32, DKV_F16, DKV_BF16, DKV_E4M3, DKV_I32, DKV_U8 = 0, 1, 2, 3, 4, 5
+DKV_MAX_LAYERS = 128
+
+EXPORTED = (
+    "dkv_status_string",
+    "dkv_abi_version",
+    "dkv_scatter_paged",
+    "dkv_gather_paged",
+    "dkv_quantize_rows",
+    "dkv_exact_packed_bytes",
+    "dkv_pack_exact_factors",
+    "dkv_exact_patch_paged",
+)
+
+
+class PagedCache(C.Structure):
+    _fields_ = [
+        ("base", C.c_void_p),
+        ("dtype", C.c_int32),
+        ("block_size", C.c_int32),
+        ("n_heads", C.c_int32),
+        ("head_dim", C.c_int32),
+        ("num_blocks", C.c_int64),
+        ("stride_block", C.c_int64),
+        ("stride_slot", C.c_int64),
+        ("stride_head", C.c_int64),
+    ]
+
+
+class SeqBatch(C.Structure):
+    _fields_ = [
+        ("cu_seqlens", C.c_void_p),
+        ("block_tables", C.c_void_p),
+        ("table_lens", C.c_void_p),
+        ("positions", C.c_void_p),
+        ("table_stride", C.c_int64),
+        ("n_seqs", C.c_int32),
+        ("max_seq_len", C.c_int32),
+    ]
+
+
+class LoraFactors(C.Structure):
+    _fields_ = [
+        ("a_k", C.c_void_p),
+        ("b_k", C.c_void_p),
+        ("a_v", C.c_void_p),
+        ("b_v", C.c_void_p),
+        ("dtype", C.c_int32),
+        ("rank_k", C.c_int32),
+        ("rank_v", C.c_int32),
+        ("n_layers", C.c_int32),
+        ("scale_k", C.c_float),
+        ("scale_v", C.c_float),
+        ("a_k_layer_stride", C.c_int64),
+        ("b_k_layer_stride", C.c_int64),
+        ("a_v_layer_stride", C.c_int64),
+        ("b_v_layer_stride", C.c_int64),
+        ("norm_weight", C.c_void_p),
+        ("norm_dtype", C.c_int32),
+        ("norm_layer_stride", C.c_int64),
+    ]
+
+
+class ExactGeometry(C.Structure):
+    _fields_ = [
+        ("d_model", C.c_int32),
+        ("n_kv_heads", C.c_int32),
+        ("head_dim", C.c_int32),
+        ("x_dtype", C.c_int32),
+        ("rank_k", C.c_int32),
+        ("rank_v", C.c_int32),
+    ]
+
+
+class ExactPatchArgs(C.Structure):
+    _fields_ = [
+        ("geom", ExactGeometry),
+        ("x", C.c_void_p),
+        ("x_layer_stride", C.c_int64),
+        ("x_row_stride", C.c_int64),
+        ("x_rows", C.c_int64),
+        ("x_scale", C.c_void_p),
+        ("x_scale_layer_stride", C.c_int64),
+        ("apply_norm", C.c_int32),
+        ("norm_eps", C.c_float),
+        ("packed", C.c_void_p),
+        ("packed_layer_stride", C.c_int64),
+        ("rope_cos", C.c_void_p),
+        ("rope_sin", C.c_void_p),
+        ("rope_max_pos", C.c_int32),
+        ("n_layers", C.c_int32),
+        ("seqs", SeqBatch),
+        ("k_pages", C.POINTER(PagedCache)),
+        ("v_pages", C.POINTER(PagedCache)),
+        ("accumulate", C.c_int32),
+        ("status", C.c_void_p),
+    ]
+
+
+_lib: C.CDLL | None = None
+
+
+def _declare(lib: C.CDLL) -> None:
+    P, I32, I64 = C.c_void_p, C.c_int32, C.c_int64
+    lib.dkv_status_string.restype = C.c_char_p
+    lib.dkv_status_string.argtypes = [C.c_int]
+    lib.dkv_abi_version.restype = C.c_int
+    lib.dkv_abi_version.argtypes = []
+    lib.dkv_scatter_paged.restype = C.c_int
+    lib.dkv_scatter_paged.argtypes = [P, I32, I64, I64, C.POINTER(PagedCache), C.POINTER(SeqBatch), P, P]
+    lib.dkv_gather_paged.restype = C.c_int
+    lib.dkv_gather_paged.argtypes = [C.POINTER(PagedCache), C.POINTER(SeqBatch), P, I32, I64, I64, P, P]
+    lib.dkv_quantize_rows.restype = C.c_int
+    lib.dkv_quantize_rows.argtypes = [P, I32, I64, I64, I64, P, I32, I64, I64, P, P]
+    lib.dkv_exact_packed_bytes.restype = C.c_int
+    lib.dkv_exact_packed_bytes.argtypes = [C.POINTER(ExactGeometry), C.POINTER(C.c_int64)]
+    lib.dkv_pack_exact_factors.restype = C.c_int
+    lib.dkv_pack_exact_factors.argtypes = [C.POINTER(ExactGeometry), C.POINTER(LoraFactors), P, I64, P]
+    lib.dkv_exact_patch_paged.restype = C.c_int
+    lib.dkv_exact_patch_paged.argtypes = [C.POINTER(ExactPatchArgs), P]
+
+
+def lib() -> C.CDLL:
+    """The loaded library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(
+                f"{LIB_PATH.name} is not built; run `python -m deltakv_b200.build` "
+                "(the CUDA path has no fallback)"
+            )
+        handle = C.CDLL(str(LIB_PATH))
+        _declare(handle)
+        if handle.dkv_abi_version() != 1:
+            raise ImportError(f"{LIB_PATH.name} ABI version mismatch; rebuild the library")
+        _lib = handle
+    return _lib
+
+
+class DkvError(RuntimeError):
+    def __init__(self, status: int, where: str = ""):
+        self.status = status
+        msg = lib().dkv_status_string(status).decode()
+        super().__init__(f"{where}: {msg} (status {status})" if where else msg)
+
+
+def check(status: int, where: str = "") -> None:
+    if status != DKV_OK:
+        raise DkvError(status, where)

@@ -1,0 +1,213 @@
+/*
+ * dkv_b200.h — C ABI of the B200 (sm_100a) KV-cache patch kernels.
+ *
+ * Every entry point is stream-ordered on the caller's stream, allocates nothing,
+ * synchronises nothing, and returns an int status (DKV_OK = 0, negative on error).
+ * All pointers are device pointers unless a field says "host".  Tensors are
+ * described by a base pointer plus element strides; no framework types appear.
+ *
+ * Reference interfaces replaced (file:line within adityaraj-09/DeltaKV):
+ *   dkv_scatter_paged      deltakv.paged.scatter_into_paged          src/deltakv/paged.py:8-43
+ *   dkv_gather_paged       deltakv.paged.gather_from_paged           src/deltakv/paged.py:46-70
+ *   dkv_pack_exact_factors LowRankFactors.codes/.apply operands      src/deltakv/deltas/factors.py:61-67
+ *   dkv_exact_patch_paged  exact_kv_patch + LowRankKVPatch.materialize + scatter_into_paged,
+ *                          as driven by DeltaKVEngine._patch (exact branch) and
+ *                          DeltaKVConnector.patch_paged
+ *                          src/deltakv/patches/exact.py:14-94, patches/tensors.py:105-123,
+ *                          patches/compose.py:29-34, engine.py:263-288, connectors/vllm.py:70-81
+ *
+ * The reference has no FFI of its own (it is pure Python/PyTorch); these are the
+ * entry points its Python operators bind through ctypes.
+ */
+#ifndef DKV_B200_H
+#define DKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* A cudaStream_t; NULL selects the legacy default stream. */
+typedef struct CUstream_st *dkv_stream_t;
+
+/* ---- status codes ------------------------------------------------------- */
+#define DKV_OK 0
+#define DKV_ERR_INVALID_ARGUMENT (-1)
+#define DKV_ERR_BLOCK_TABLE_SHORT (-2) /* "block_table shorter than prefix" (paged.py:27-28) */
+#define DKV_ERR_LAYOUT (-3)            /* "unsupported paged KV layout" (paged.py:36-37)   */
+#define DKV_ERR_UNSUPPORTED (-4)       /* shape / dtype combination not built             */
+#define DKV_ERR_ALIGNMENT (-5)         /* pointer or stride alignment (TMA needs 16 B)    */
+#define DKV_ERR_ROPE_RANGE (-6)        /* "seq_len exceeds RoPE cache" (rope.py:48-49)     */
+#define DKV_ERR_BASIS_DIM (-7)         /* "basis d != kv d" (subspace.py:76-77)            */
+#define DKV_ERR_CUDA (-8)              /* a CUDA runtime call failed                      */
+#define DKV_ERR_TIMEOUT (-9)           /* a bounded device-side wait gave up              */
+#define DKV_ERR_PAGE_RANGE (-10)       /* block id outside [0, num_blocks)                */
+#define DKV_ERR_WORKSPACE (-11)        /* workspace too small                             */
+
+/* ---- element types ------------------------------------------------------ */
+#define DKV_F32 0
+#define DKV_F16 1
+#define DKV_BF16 2
+#define DKV_E4M3 3 /* float8 e4m3fn */
+#define DKV_I32 4
+#define DKV_U8 5
+
+/* Upper bound on layers covered by one dkv_exact_patch_paged launch. */
+#define DKV_MAX_LAYERS 128
+
+/* Human-readable text of a status code (static storage). */
+const char *dkv_status_string(int status);
+/* ABI version: bumped when a struct below changes. */
+int dkv_abi_version(void);
+
+/*
+ * A paged KV cache of one layer for one of K or V.  Element (block, slot, head, dim)
+ * lives at base + block*stride_block + slot*stride_slot + head*stride_head + dim
+ * (strides in elements, dim stride 1).  The three layouts the reference accepts
+ * (paged.py:18-37) — [nb,bs,h,d], [2,nb,bs,h,d][kv], [nb,2,bs,h,d][:,kv] — are all
+ * this struct with different base/strides.  A dense [seq, h, d] tensor is the case
+ * num_blocks=1, block_size=seq, block table {0}.
+ */
+typedef struct dkv_paged_cache {
+  void *base;
+  int32_t dtype; /* DKV_F32 / DKV_F16 / DKV_BF16 */
+  int32_t block_size;
+  int32_t n_heads;
+  int32_t head_dim;
+  int64_t num_blocks;
+  int64_t stride_block;
+  int64_t stride_slot;
+  int64_t stride_head;
+} dkv_paged_cache;
+
+/*
+ * A batch of sequences.  Token i of sequence b is row cu_seqlens[b] + i of the
+ * token-major inputs, sits in block block_tables[b*table_stride + i/block_size]
+ * at slot i % block_size (paged.py:39-43), and has RoPE position positions[row]
+ * (or i when positions is NULL, rope.py:59-60).
+ */
+typedef struct dkv_seq_batch {
+  const int32_t *cu_seqlens;   /* [n_seqs+1], non-decreasing, cu_seqlens[0] = 0          */
+  const int32_t *block_tables; /* [n_seqs, table_stride]                                  */
+  const int32_t *table_lens;   /* [n_seqs] valid entries per row, or NULL = table_stride  */
+  const int32_t *positions;    /* [total rows] or NULL                                    */
+  int64_t table_stride;
+  int32_t n_seqs;
+  int32_t max_seq_len; /* host-known bound on any sequence length (grid sizing)           */
+} dkv_seq_batch;
+
+/*
+ * pages[block, slot] += delta[row]  (additive, in place), rounding once from
+ * fp32(page) + fp32(delta) to the page dtype — bit-identical to the reference's
+ * `pages[bid,:span] = pages[bid,:span] + delta[start:end]` (paged.py:43).
+ * delta element (row, head, dim) at delta + row*delta_stride_row + head*delta_stride_head + dim.
+ * Device-side range errors are written to *status (first error wins; may be NULL).
+ */
+int dkv_scatter_paged(const void *delta, int32_t delta_dtype, int64_t delta_stride_row,
+                      int64_t delta_stride_head, const dkv_paged_cache *cache,
+                      const dkv_seq_batch *seqs, int32_t *status, dkv_stream_t stream);
+
+/* out[row] = pages[block, slot]  (paged.py:46-70), converted to out_dtype. */
+int dkv_gather_paged(const dkv_paged_cache *cache, const dkv_seq_batch *seqs, void *out,
+                     int32_t out_dtype, int64_t out_stride_row, int64_t out_stride_head,
+                     int32_t *status, dkv_stream_t stream);
+
+/*
+ * Stored-activation writer.  The reference keeps HiddenSnapshot.h in the model dtype
+ * (model.py:157-164; config.py:31 names float16 storage but nothing applies it).  This
+ * quantises rows of x (F32/F16/BF16) into out (DKV_F16 with a power-of-two row scale, or
+ * DKV_E4M3 with scale = max|x|/448): out[r,c] = x[r,c]/scale[r]; columns
+ * [cols, out_cols) are zero-filled so rows can be padded to 16 bytes.
+ */
+int dkv_quantize_rows(const void *x, int32_t x_dtype, int64_t rows, int64_t cols,
+                      int64_t x_row_stride, void *out, int32_t out_dtype, int64_t out_row_stride,
+                      int64_t out_cols, float *scale, dkv_stream_t stream);
+
+/* ---- exact / zeroth-order patch (fused) --------------------------------- */
+
+/*
+ * LoRA factors of the k_proj / v_proj maps of n_layers layers (PEFT convention,
+ * factors.py:11-75): A [rank, d_model], B [n_kv*head_dim, rank], dW = scale*B@A.
+ * Layer l's A starts at a + l*a_layer_stride (elements), row-major contiguous.
+ * rank = 0 (or NULL pointers) means that projection has no delta (exact.py:46-53).
+ * norm_weight (optional, [n_layers, d_model] via norm_layer_stride) is the attn RMSNorm
+ * weight; when given it is folded into A so that the patch consumes pre-norm X
+ * (model.py:48-56,310-314).
+ */
+typedef struct dkv_lora_factors {
+  const void *a_k, *b_k, *a_v, *b_v;
+  int32_t dtype; /* DKV_F32 / DKV_F16 / DKV_BF16 for all four */
+  int32_t rank_k, rank_v;
+  int32_t n_layers;
+  float scale_k, scale_v;
+  int64_t a_k_layer_stride, b_k_layer_stride, a_v_layer_stride, b_v_layer_stride;
+  const void *norm_weight;
+  int32_t norm_dtype;
+  int64_t norm_layer_stride;
+} dkv_lora_factors;
+
+/* Geometry shared by packing and patching. */
+typedef struct dkv_exact_geometry {
+  int32_t d_model;
+  int32_t n_kv_heads;
+  int32_t head_dim; /* 16, 32 or a multiple of 64 up to 256 */
+  int32_t x_dtype;  /* DKV_E4M3 or DKV_F16: the stored-activation format */
+  int32_t rank_k;   /* 0..64 */
+  int32_t rank_v;   /* 0..64 */
+} dkv_exact_geometry;
+
+/* Bytes of the packed-factor image of one layer (a multiple of 256). */
+int dkv_exact_packed_bytes(const dkv_exact_geometry *geom, int64_t *bytes_per_layer);
+
+/*
+ * Convert factors to the kernel's tensor-core operand image: f16 with per-matrix
+ * power-of-two scaling, RMSNorm weight folded into A, fragment-ordered.  `packed`
+ * receives n_layers images, image l at packed + l*packed_layer_stride bytes.
+ */
+int dkv_pack_exact_factors(const dkv_exact_geometry *geom, const dkv_lora_factors *factors,
+                           void *packed, int64_t packed_layer_stride, dkv_stream_t stream);
+
+typedef struct dkv_exact_patch_args {
+  dkv_exact_geometry geom;
+  /* stored activations X: element (layer l, row t, k) at x + l*x_layer_stride + t*x_row_stride + k
+     (elements of x_dtype); rows are the tokens of `seqs`. Base 16-B aligned, strides*elem % 16 == 0. */
+  const void *x;
+  int64_t x_layer_stride, x_row_stride, x_rows;
+  /* optional per-token dequantisation scale (fp32), element (l, t) at x_scale + l*x_scale_layer_stride + t */
+  const float *x_scale;
+  int64_t x_scale_layer_stride;
+  int32_t apply_norm; /* 1: X is pre-norm; RMSNorm(x)*w is applied (w folded into packed) */
+  float norm_eps;
+  /* packed factor images (dkv_pack_exact_factors), layer l at packed + l*packed_layer_stride */
+  const void *packed;
+  int64_t packed_layer_stride;
+  /* RoPE tables [rope_max_pos, head_dim/2] fp32 (cos, sin of position*inv_freq) or NULL: no RoPE on K */
+  const float *rope_cos, *rope_sin;
+  int32_t rope_max_pos;
+  int32_t n_layers; /* <= DKV_MAX_LAYERS */
+  dkv_seq_batch seqs;
+  /* per-layer caches: K and V pages of layer l (host arrays of n_layers entries); only
+     base differs between layers, the rest is taken from k_pages[0] / v_pages[0] */
+  const dkv_paged_cache *k_pages;
+  const dkv_paged_cache *v_pages;
+  int32_t accumulate; /* 1: pages += delta (read-add-write); 0: pages = delta */
+  int32_t *status;    /* optional device status word */
+} dkv_exact_patch_args;
+
+/*
+ * For every layer l and token t of every sequence:
+ *   x  = dequant(X[l,t]) (optionally RMSNorm(x)*w_l)
+ *   dK = RoPE_pos(t)( scale_k * (x @ A_k^T) @ B_k^T ),  dV = scale_v * (x @ A_v^T) @ B_v^T
+ *   K_pages[l][block(t), slot(t)] (+)= dK,  V_pages[l][...] (+)= dV
+ * in one persistent launch: X streamed by TMA, both products on tensor cores with the
+ * rank-r codes kept in registers, RoPE and the page read-add-write fused.
+ */
+int dkv_exact_patch_paged(const dkv_exact_patch_args *args, dkv_stream_t stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* DKV_B200_H */

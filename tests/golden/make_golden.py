@@ -1,0 +1,308 @@
+"""Generate golden vectors by running the reference implementation (adityaraj-09/DeltaKV).
+
+Run in the build container, where the reference source is available:
+
+    python tests/golden/make_golden.py /root/reference/src
+
+It imports the reference read-only (no bytecode written), drives its own functions on
+seeded inputs and stores inputs and outputs as ``tests/golden/*.npz``.  The tests read
+only the .npz files, so they run where the reference is absent.
+
+Cases:
+  paged.npz        scatter_into_paged / gather_from_paged: the reference's own
+                   test_paged_roundtrip case (tests/test_engine.py:184-191) plus bf16
+                   caches in the three layouts of paged.py:18-37.
+  layer0.npz       the setup of tests/test_layer1_exact.py:37-55 (exact_kv_patch on
+                   layer 0 of the conftest toy, then apply_layer_patches, vs a fresh
+                   prefill under the new weights).
+  config1.npz      the CPU-toy configuration: 4 layers, d=64, GQA 4/2, 64 tokens, rank-4
+                   k/v LoRA on every layer at relative scale 0.01 -> rmsnorm_tensors ->
+                   zeroth_order_patches -> apply_layer_patches, fresh prefill, logits, KL,
+                   and the same patch scattered into bf16 pages through a permuted table.
+  fp8_paged.npz    ragged multi-sequence batch: fp8-e4m3 stored activations with per-token
+                   scales, RMSNorm with non-unit weight, ranks k=8 / v=16, RoPE, bf16 pages,
+                   computed per (layer, sequence) with the reference's RMSNorm,
+                   exact_kv_patch, materialize and scatter_into_paged.
+  subspace.npz     subspace_correct with a given basis (V path), with basis=None (K path,
+                   SVD of the probe residual) and the reference tests' two cases
+                   (tests/test_quality.py:32-64).
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+
+sys.dont_write_bytecode = True
+OUT = Path(__file__).resolve().parent
+
+
+def bf16_bits(t) -> np.ndarray:
+    import torch
+
+    return t.to(torch.bfloat16).contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def main(ref_src: str) -> None:
+    sys.path.insert(0, ref_src)
+    import torch
+
+    from deltakv.deltas.descriptor import LayerDelta, lora_layer
+    from deltakv.deltas.factors import LowRankFactors, random_lora_factors
+    from deltakv.deltas.lora import lora_delta
+    from deltakv.metrics import next_token_kl
+    from deltakv.model import RMSNorm, ToyConfig, ToyTransformer
+    from deltakv.paged import gather_from_paged, scatter_into_paged
+    from deltakv.patches.compose import apply_layer_patches
+    from deltakv.patches.exact import exact_kv_patch, zeroth_order_patches
+    from deltakv.patches.subspace import subspace_correct
+    from deltakv.rope import RotaryEmbedding
+    from deltakv.types import WeightVersion
+
+    torch.set_num_threads(4)
+    torch.set_grad_enabled(False)
+
+    # ------------------------------------------------------------------ paged
+    g = torch.Generator().manual_seed(0)
+    paged = {}
+    seq, h, d, bs = 20, 2, 8, 8
+    delta = torch.randn(seq, h, d, generator=g)
+    cache = torch.zeros(8, bs, h, d)
+    table = [3, 1, 5]
+    scatter_into_paged(delta, cache, table, bs)
+    paged["rt_delta"] = delta.numpy()
+    paged["rt_table"] = np.array(table, np.int32)
+    paged["rt_cache_out"] = cache.numpy()
+    paged["rt_gather"] = gather_from_paged(cache, table, seq, bs).numpy()
+    # bf16 caches in the three layouts
+    nb, bs2, seq2 = 9, 4, 13
+    table2 = [7, 2, 0, 5]
+    for name, shape, kv in (
+        ("l4", (nb, bs2, h, d), 0),
+        ("l5a", (2, nb, bs2, h, d), 1),
+        ("l5b", (nb, 2, bs2, h, d), 0),
+    ):
+        c = torch.randn(*shape, generator=g).to(torch.bfloat16)
+        dl = torch.randn(seq2, h, d, generator=g) * 0.01
+        paged[f"{name}_in"] = bf16_bits(c)
+        paged[f"{name}_delta"] = dl.numpy()
+        scatter_into_paged(dl, c, table2, bs2, kv_dim=kv)
+        paged[f"{name}_out"] = bf16_bits(c)
+        paged[f"{name}_kv"] = np.int32(kv)
+        paged[f"{name}_gather"] = bf16_bits(gather_from_paged(c, table2, seq2, bs2, kv_dim=kv))
+    paged["l_table"] = np.array(table2, np.int32)
+    paged["l_bs"] = np.int32(bs2)
+    np.savez_compressed(OUT / "paged.npz", **paged)
+
+    # ----------------------------------------------------------------- layer0
+    torch.manual_seed(0)
+    toy = ToyTransformer(ToyConfig(n_layers=4, d_model=64, n_heads=4, n_kv_heads=4, d_ff=128, vocab_size=128))
+    tokens = torch.arange(48) % toy.cfg.vocab_size
+    _, kv0, hidden = toy.prefill(tokens)
+    gl = torch.Generator().manual_seed(1)
+    c = toy.cfg
+    fk = random_lora_factors(c.d_model, c.n_kv_heads * c.head_dim, 4, scale=0.05, generator=gl, name="k_proj")
+    fv = random_lora_factors(c.d_model, c.n_kv_heads * c.head_dim, 4, scale=0.05, generator=gl, name="v_proj")
+    delta = lora_delta(source=WeightVersion(id="base"), target=WeightVersion(id="lora", parent_id="base", kind="lora"),
+                       layers={0: lora_layer(0, k=fk, v=fv)})
+    with torch.no_grad():
+        xn = toy.blocks[0].attn_norm(hidden.layer_in(0))
+        patch = exact_kv_patch(xn, delta.layers[0], n_kv_heads=c.n_kv_heads, head_dim=c.head_dim, rope=toy.rope)
+        dk, dv = patch.materialize(c.n_kv_heads, c.head_dim)
+        patched = apply_layer_patches(kv0, {0: patch})
+        toy.apply_delta(delta, version=WeightVersion(id="lora"))
+        _, kv1, _ = toy.prefill(tokens)
+    hd = c.head_dim
+    np.savez_compressed(
+        OUT / "layer0.npz",
+        xn=xn.numpy(), a_k=fk.A.numpy(), b_k=fk.B.numpy(), s_k=np.float32(fk.scale),
+        a_v=fv.A.numpy(), b_v=fv.B.numpy(), s_v=np.float32(fv.scale),
+        rope_cos=toy.rope.cos_cached[:, : hd // 2].numpy(), rope_sin=toy.rope.sin_cached[:, : hd // 2].numpy(),
+        dk=dk.numpy(), dv=dv.numpy(), k0=kv0.k[0].numpy(), v0=kv0.v[0].numpy(),
+        k_patched=patched.k[0].numpy(), v_patched=patched.v[0].numpy(),
+        k_fresh=kv1.k[0].numpy(), v_fresh=kv1.v[0].numpy(), n_kv=np.int32(c.n_kv_heads), hd=np.int32(hd),
+    )
+
+    # ---------------------------------------------------------------- config1
+    torch.manual_seed(0)
+    cfg = ToyConfig(n_layers=4, d_model=64, n_heads=4, n_kv_heads=2, d_ff=128, vocab_size=256)
+    model = ToyTransformer(cfg)
+    gt = torch.Generator().manual_seed(0)
+    tokens = torch.randint(0, 256, (64,), generator=gt)
+    with torch.no_grad():
+        logits0, kv_base, hidden = model.prefill(tokens)
+    gf = torch.Generator().manual_seed(1)
+    d_kv = cfg.n_kv_heads * cfg.head_dim
+    layers, A_k, B_k, A_v, B_v, S = {}, [], [], [], [], []
+    for i, blk in enumerate(model.blocks):
+        facs = {}
+        for name, lin in (("k", blk.k_proj), ("v", blk.v_proj)):
+            A = torch.randn(4, cfg.d_model, generator=gf) / cfg.d_model ** 0.5
+            B = torch.randn(d_kv, 4, generator=gf)
+            rel = 0.01 * lin.weight.norm() / (B @ A).norm()
+            facs[name] = LowRankFactors(A=A, B=B, scale=float(rel), name=f"{name}_proj")
+        layers[i] = lora_layer(i, k=facs["k"], v=facs["v"])
+        A_k.append(facs["k"].A.numpy()); B_k.append(facs["k"].B.numpy())
+        A_v.append(facs["v"].A.numpy()); B_v.append(facs["v"].B.numpy())
+        S.append((facs["k"].scale, facs["v"].scale))
+    delta = lora_delta(source=WeightVersion(id="base"), target=WeightVersion(id="lora", parent_id="base", kind="lora"),
+                       layers=layers)
+    with torch.no_grad():
+        xn = model.rmsnorm_tensors(hidden)
+        patches = zeroth_order_patches(xn, delta, n_kv_heads=cfg.n_kv_heads, head_dim=cfg.head_dim, rope=model.rope)
+        patched = apply_layer_patches(kv_base, patches)
+        deltas = {l: p.materialize(cfg.n_kv_heads, cfg.head_dim) for l, p in patches.items()}
+        model.apply_delta(delta, version=WeightVersion(id="lora"))
+        fresh_logits, kv_fresh, _ = model.prefill(tokens)
+        patched_logits = model.logits_from_kv(tokens, patched)
+        kl_ref = next_token_kl(fresh_logits, patched_logits)
+        kl_stale = next_token_kl(fresh_logits, model.logits_from_kv(tokens, kv_base))
+    # bf16 pages through a permuted block table (seed 2)
+    bs = 16
+    gp = torch.Generator().manual_seed(2)
+    nblk = 12
+    perm = torch.randperm(nblk, generator=gp)[: (64 + bs - 1) // bs].tolist()
+    k_pages_in, v_pages_in, k_pages_out, v_pages_out = [], [], [], []
+    for l in range(cfg.n_layers):
+        kp = torch.randn(nblk, bs, cfg.n_kv_heads, cfg.head_dim, generator=gp).to(torch.bfloat16)
+        vp = torch.randn(nblk, bs, cfg.n_kv_heads, cfg.head_dim, generator=gp).to(torch.bfloat16)
+        # the cached prefix itself
+        for i in range(64):
+            kp[perm[i // bs], i % bs] = kv_base.k[l, i].to(torch.bfloat16)
+            vp[perm[i // bs], i % bs] = kv_base.v[l, i].to(torch.bfloat16)
+        k_pages_in.append(bf16_bits(kp)); v_pages_in.append(bf16_bits(vp))
+        scatter_into_paged(deltas[l][0], kp, perm, bs)
+        scatter_into_paged(deltas[l][1], vp, perm, bs)
+        k_pages_out.append(bf16_bits(kp)); v_pages_out.append(bf16_bits(vp))
+    hd = cfg.head_dim
+    np.savez_compressed(
+        OUT / "config1.npz",
+        tokens=tokens.numpy().astype(np.int64),
+        h_in=np.stack([h.numpy() for h in hidden.h]),
+        norm_w=np.stack([b.attn_norm.weight.detach().numpy() for b in model.blocks]),
+        eps=np.float32(cfg.rms_eps),
+        a_k=np.stack(A_k), b_k=np.stack(B_k), a_v=np.stack(A_v), b_v=np.stack(B_v),
+        scales=np.array(S, np.float32),
+        rope_cos=model.rope.cos_cached[:, : hd // 2].numpy(), rope_sin=model.rope.sin_cached[:, : hd // 2].numpy(),
+        xn=np.stack([xn[l].numpy() for l in range(cfg.n_layers)]),
+        dk=np.stack([deltas[l][0].numpy() for l in range(cfg.n_layers)]),
+        dv=np.stack([deltas[l][1].numpy() for l in range(cfg.n_layers)]),
+        k_base=kv_base.k.numpy(), v_base=kv_base.v.numpy(),
+        k_patched=patched.k.numpy(), v_patched=patched.v.numpy(),
+        k_fresh=kv_fresh.k.numpy(), v_fresh=kv_fresh.v.numpy(),
+        patched_logits=patched_logits.numpy(), fresh_logits=fresh_logits.view(-1, cfg.vocab_size)[-1].numpy(),
+        kl_ref=np.float64(kl_ref), kl_stale=np.float64(kl_stale),
+        block_table=np.array(perm, np.int32), block_size=np.int32(bs),
+        k_pages_in=np.stack(k_pages_in), v_pages_in=np.stack(v_pages_in),
+        k_pages_out=np.stack(k_pages_out), v_pages_out=np.stack(v_pages_out),
+        n_kv=np.int32(cfg.n_kv_heads), hd=np.int32(hd),
+        n_heads=np.int32(cfg.n_heads), rope_base=np.float32(cfg.rope_base),
+        **{f"w_{k.replace('.', '_')}": v.detach().numpy() for k, v in model.state_dict().items()},
+    )
+
+    # -------------------------------------------------------------- fp8_paged
+    g8 = torch.Generator().manual_seed(3)
+    L_, dm, n_kv, hd, bs = 2, 128, 2, 64, 16
+    lens = [37, 16, 1, 70, 133]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    rows = int(cu[-1])
+    rope = RotaryEmbedding(hd, max_seq=512, base=10000.0)
+    x = torch.randn(L_, rows, dm, generator=g8) * 3.0
+    amax = x.abs().amax(dim=-1).clamp_min(1e-12)
+    xscale = (amax / 448.0).float()
+    xq = (x / xscale[..., None]).to(torch.float8_e4m3fn)
+    xdq = xq.float() * xscale[..., None]
+    norm_w = 1.0 + 0.1 * torch.randn(L_, dm, generator=g8)
+    rk, rv = 8, 16
+    a_k = torch.randn(L_, rk, dm, generator=g8) / dm ** 0.5
+    b_k = torch.randn(L_, n_kv * hd, rk, generator=g8)
+    a_v = torch.randn(L_, rv, dm, generator=g8) / dm ** 0.5
+    b_v = torch.randn(L_, n_kv * hd, rv, generator=g8)
+    s_k, s_v = 0.02, 0.015
+    max_blocks = max((n + bs - 1) // bs for n in lens)
+    nblk = sum((n + bs - 1) // bs for n in lens) + 3
+    perm = torch.randperm(nblk, generator=g8).tolist()
+    tables = np.full((len(lens), max_blocks), -1, np.int32)
+    k = 0
+    for b, n in enumerate(lens):
+        for i in range((n + bs - 1) // bs):
+            tables[b, i] = perm[k]
+            k += 1
+    kp_in = [torch.randn(nblk, bs, n_kv, hd, generator=g8).to(torch.bfloat16) for _ in range(L_)]
+    vp_in = [torch.randn(nblk, bs, n_kv, hd, generator=g8).to(torch.bfloat16) for _ in range(L_)]
+    kp_out = [t.clone() for t in kp_in]
+    vp_out = [t.clone() for t in vp_in]
+    for l in range(L_):
+        norm = RMSNorm(dm, 1e-6)
+        with torch.no_grad():
+            norm.weight.copy_(norm_w[l])
+        ld = LayerDelta(layer_idx=l, projections={
+            "k_proj": LowRankFactors(A=a_k[l], B=b_k[l], scale=s_k),
+            "v_proj": LowRankFactors(A=a_v[l], B=b_v[l], scale=s_v),
+        })
+        for b, n in enumerate(lens):
+            with torch.no_grad():
+                xn_b = norm(xdq[l, cu[b]:cu[b + 1]])
+                p = exact_kv_patch(xn_b, ld, n_kv_heads=n_kv, head_dim=hd, rope=rope)
+                dk, dv = p.materialize(n_kv, hd)
+            t = tables[b, : (n + bs - 1) // bs].tolist()
+            scatter_into_paged(dk, kp_out[l], t, bs)
+            scatter_into_paged(dv, vp_out[l], t, bs)
+    np.savez_compressed(
+        OUT / "fp8_paged.npz",
+        x_bits=xq.view(torch.uint8).numpy(), x_scale=xscale.numpy(), norm_w=norm_w.numpy(), eps=np.float32(1e-6),
+        a_k=a_k.numpy(), b_k=b_k.numpy(), a_v=a_v.numpy(), b_v=b_v.numpy(), s_k=np.float32(s_k), s_v=np.float32(s_v),
+        cu_seqlens=cu, block_tables=tables, block_size=np.int32(bs),
+        rope_cos=rope.cos_cached[:, : hd // 2].numpy(), rope_sin=rope.sin_cached[:, : hd // 2].numpy(),
+        k_pages_in=np.stack([bf16_bits(t) for t in kp_in]), v_pages_in=np.stack([bf16_bits(t) for t in vp_in]),
+        k_pages_out=np.stack([bf16_bits(t) for t in kp_out]), v_pages_out=np.stack([bf16_bits(t) for t in vp_out]),
+        n_kv=np.int32(n_kv), hd=np.int32(hd),
+    )
+
+    # --------------------------------------------------------------- subspace
+    sub = {}
+    torch.manual_seed(0)
+    seq, h, d, r = 32, 2, 8, 3
+    reused = torch.randn(seq, h, d)
+    basis = torch.randn(h * d, r)
+    codes = torch.randn(seq, r) * 0.05
+    mu = torch.randn(h * d)
+    gram_mu = torch.linalg.lstsq(basis, mu.unsqueeze(-1)).solution.squeeze(-1)
+    mu = mu - basis @ gram_mu
+    fresh = reused + (codes @ basis.T).view(seq, h, d) + mu.view(1, h, d)
+    probes = torch.arange(0, 16)
+    corr, subsp, orth = subspace_correct(reused, fresh, probes, basis=basis, rank=r)
+    sub.update(t1_reused=reused.numpy(), t1_fresh=fresh.numpy(), t1_probes=probes.numpy(), t1_basis=basis.numpy(),
+               t1_rank=np.int32(r), t1_corr=corr.numpy(), t1_sub=subsp.numpy(), t1_orth=orth.numpy())
+    torch.manual_seed(1)
+    reused = torch.randn(24, 2, 4)
+    mu = torch.randn(2, 4)
+    fresh = reused + mu
+    probes = torch.tensor([0, 2, 4, 6, 8, 10])
+    corr, subsp, orth = subspace_correct(reused, fresh, probes, basis=None, rank=1)
+    sub.update(t2_reused=reused.numpy(), t2_fresh=fresh.numpy(), t2_probes=probes.numpy(), t2_rank=np.int32(1),
+               t2_corr=corr.numpy(), t2_sub=subsp.numpy(), t2_orth=orth.numpy())
+    # larger V-path (given basis) and K-path (SVD basis) cases with structure + drift
+    gs = torch.Generator().manual_seed(4)
+    for tag, n, nkv, hdim, rr, use_basis in (("v", 300, 4, 32, 8, True), ("k", 300, 4, 32, 8, False)):
+        dkv = nkv * hdim
+        reused = torch.randn(n, nkv, hdim, generator=gs)
+        B = torch.randn(dkv, rr, generator=gs)
+        cds = torch.randn(n, rr, generator=gs) * 0.1
+        drift = torch.randn(dkv, generator=gs) * 0.05
+        noise = torch.randn(n, dkv, generator=gs) * 0.01
+        fresh = reused + (cds @ B.T + drift + noise).view(n, nkv, hdim)
+        probes = torch.unique(torch.randperm(n, generator=gs)[:30].sort().values)
+        probes = torch.unique(torch.cat([torch.zeros(1, dtype=torch.long), probes]))
+        corr, subsp, orth = subspace_correct(reused, fresh, probes, basis=B if use_basis else None, rank=rr)
+        sub.update({f"{tag}_reused": reused.numpy(), f"{tag}_fresh": fresh.numpy(), f"{tag}_probes": probes.numpy(),
+                    f"{tag}_basis": B.numpy(), f"{tag}_use_basis": np.int32(use_basis), f"{tag}_rank": np.int32(rr),
+                    f"{tag}_corr": corr.numpy(), f"{tag}_sub": subsp.numpy(), f"{tag}_orth": orth.numpy()})
+    np.savez_compressed(OUT / "subspace.npz", **sub)
+    print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")

@@ -1,0 +1,82 @@
+"""The C ABI library loads here (no GPU) and exports every symbol the header declares."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _declared() -> set[str]:
+    text = (ROOT / "include" / "dkv_b200.h").read_text()
+    return set(re.findall(r"^\s*(?:const\s+)?(?:int|void|char\s*\*|const char\s*\*)\s*\*?\s*(dkv_\w+)\s*\(", text, re.M))
+
+
+def test_header_declares_the_bound_symbols():
+    from deltakv_b200 import _lib
+
+    assert _declared() == set(_lib.EXPORTED)
+
+
+def test_library_loads_and_exports_all_symbols():
+    from deltakv_b200 import _lib
+
+    lib = _lib.lib()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    assert lib.dkv_abi_version() == 1
+    assert lib.dkv_status_string(-2).decode() == "block_table shorter than prefix"
+    assert lib.dkv_status_string(-3).decode() == "unsupported paged KV layout"
+
+
+def test_struct_layouts_match_the_header():
+    from deltakv_b200 import _lib as L
+
+    # sizes of the ABI structs under the x86-64 SysV layout of the C header
+    assert ctypes.sizeof(L.PagedCache) == 56
+    assert ctypes.sizeof(L.SeqBatch) == 48
+    assert ctypes.sizeof(L.ExactGeometry) == 24
+
+
+def test_packed_bytes_host_query():
+    from deltakv_b200 import ops
+
+    g = ops.exact_geometry(4096, 8, 128, torch.float8_e4m3fn, 16, 16)
+    n = ops.packed_bytes(g)
+    # header 256 + A (32 stages x 32 rows x 256 B) + 2 x B (16 passes x 1 kstep x 2 KiB)
+    assert n == 256 + 32 * 32 * 256 + 2 * 16 * 2048
+    with pytest.raises(Exception, match="unsupported"):
+        ops.packed_bytes(ops.exact_geometry(4096, 8, 96, torch.float8_e4m3fn, 16, 16))
+
+
+def test_calls_without_a_gpu_fail_cleanly_on_bad_arguments():
+    from deltakv_b200 import _lib as L
+
+    lib = L.lib()
+    assert lib.dkv_scatter_paged(None, 0, 0, 0, None, None, None, None) == L.DKV_ERR_INVALID_ARGUMENT
+    assert lib.dkv_exact_patch_paged(None, None) == L.DKV_ERR_INVALID_ARGUMENT
+
+
+def test_page_view_matches_reference_layout_dispatch():
+    from deltakv_b200.ops import page_view
+
+    c4 = torch.zeros(3, 4, 2, 8)
+    assert page_view(c4).shape == (3, 4, 2, 8)
+    c5a = torch.zeros(2, 3, 4, 2, 8)
+    assert page_view(c5a, 1).data_ptr() == c5a[1].data_ptr()
+    c5b = torch.zeros(3, 2, 4, 2, 8)
+    assert page_view(c5b, 1).stride() == c5b[:, 1].stride()
+    with pytest.raises(ValueError, match="unsupported paged KV layout"):
+        page_view(torch.zeros(3, 3, 4, 2, 8))
+
+
+def test_cpu_tensors_are_rejected():
+    import deltakv_b200 as dkv
+
+    with pytest.raises(ValueError, match="CUDA"):
+        dkv.scatter_into_paged(torch.zeros(4, 1, 8), torch.zeros(1, 8, 1, 8), [0], 8)

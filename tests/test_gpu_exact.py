@@ -1,0 +1,288 @@
+"""Fused exact patch on the GPU vs the reference's golden vectors and the oracle.
+
+Tolerances: patched bf16 pages within rel-L2 1e-3 of the reference result rounded to
+bf16 (the required bar; measured values are ~1e-5), untouched cache slots bit-identical,
+next-token KL within 1e-4 nats of the reference's.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import deltakv_b200 as dkv
+from deltakv_b200 import ops
+from oracle import exact as OX
+from oracle.numerics import bf16_bits_to_f32, f32_to_e4m3_bits
+from tests.conftest import golden
+from tests.helpers import bf16_from_bits, bits_from_bf16, e4m3_from_bits, rel_l2
+
+pytestmark = pytest.mark.gpu
+REL_TOL = 1e-3
+
+
+def _touched_mask(nb: int, tables: np.ndarray, lens) -> np.ndarray:
+    m = np.zeros(nb, bool)
+    for b, n in enumerate(lens):
+        nblk = (int(n) + 15) // 16
+        m[tables[b, :nblk]] = True
+    return m
+
+
+def test_fp8_paged_golden(cuda):
+    g = golden("fp8_paged")
+    n_kv, hd = int(g["n_kv"]), int(g["hd"])
+    L_, rows, d = g["x_bits"].shape
+    rk, rv = g["a_k"].shape[1], g["a_v"].shape[1]
+    patcher = dkv.ExactPatcher(d, n_kv, hd, rank_k=rk, rank_v=rv, x_dtype=torch.float8_e4m3fn,
+                               rope=(torch.from_numpy(g["rope_cos"]), torch.from_numpy(g["rope_sin"])),
+                               norm_eps=float(g["eps"]))
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    packed = patcher.pack(t(g["a_k"]), t(g["b_k"]), t(g["a_v"]), t(g["b_v"]), float(g["s_k"]), float(g["s_v"]),
+                          norm_weight=t(g["norm_w"]))
+    kp = [bf16_from_bits(g["k_pages_in"][l], cuda) for l in range(L_)]
+    vp = [bf16_from_bits(g["v_pages_in"][l], cuda) for l in range(L_)]
+    cu = g["cu_seqlens"]
+    seqs = ops.SeqBatchTensors(cu_seqlens=t(cu), block_tables=t(g["block_tables"]),
+                               max_seq_len=int(np.diff(cu).max()))
+    patcher.apply(e4m3_from_bits(g["x_bits"], cuda), packed, kp, vp, seqs, x_scale=t(g["x_scale"]),
+                  apply_norm=True, check=True)
+    torch.cuda.synchronize()
+    touched = _touched_mask(g["k_pages_in"].shape[1], g["block_tables"], np.diff(cu))
+    for l in range(L_):
+        for got_t, ref_bits, in_bits in ((kp[l], g["k_pages_out"][l], g["k_pages_in"][l]),
+                                         (vp[l], g["v_pages_out"][l], g["v_pages_in"][l])):
+            got = bits_from_bf16(got_t)
+            assert np.array_equal(got[~touched], in_bits[~touched])  # untouched slots
+            # relative error of the patch itself (pages minus their input) and of the pages
+            dg = bf16_bits_to_f32(got) - bf16_bits_to_f32(in_bits)
+            dr = bf16_bits_to_f32(ref_bits) - bf16_bits_to_f32(in_bits)
+            assert rel_l2(bf16_bits_to_f32(got), bf16_bits_to_f32(ref_bits)) < REL_TOL
+            assert rel_l2(dg, dr) < 2e-2  # delta alone, including bf16 rounding of both sides
+            assert (got == ref_bits).mean() > 0.98
+
+
+def test_layer0_exact_kv_patch_dropin(cuda):
+    g = golden("layer0")
+    n_kv, hd = int(g["n_kv"]), int(g["hd"])
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    layer = dkv.LayerDelta(0, {"k_proj": dkv.LowRankFactors(t(g["a_k"]), t(g["b_k"]), float(g["s_k"])),
+                               "v_proj": dkv.LowRankFactors(t(g["a_v"]), t(g["b_v"]), float(g["s_v"]))})
+    rope = (torch.from_numpy(g["rope_cos"]), torch.from_numpy(g["rope_sin"]))
+    patch = dkv.exact_kv_patch(t(g["xn"]), layer, n_kv_heads=n_kv, head_dim=hd, rope=rope)
+    dk, dv = patch.materialize(n_kv, hd)
+    dk, dv = dk.cpu().numpy(), dv.cpu().numpy()
+    assert rel_l2(dk, g["dk"]) < 2e-3 and rel_l2(dv, g["dv"]) < 2e-3
+    # the reference's own exactness claim, through the B200 path (test_layer1_exact.py:54-55)
+    assert np.abs(g["k0"] + dk - g["k_fresh"]).max() < 2e-5
+    assert np.abs(g["v0"] + dv - g["v_fresh"]).max() < 2e-5
+    kv = dkv.KVCache(t(g["k0"][None]), t(g["v0"][None]))
+    out = dkv.apply_layer_patches(kv, {0: patch})
+    assert np.abs(out.k[0].cpu().numpy() - g["k_patched"]).max() < 2e-5
+    assert np.abs(out.v[0].cpu().numpy() - g["v_patched"]).max() < 2e-5
+
+
+def test_config1_zeroth_order_and_kl(cuda):
+    from oracle.model import logits_from_kv, next_token_kl, weights_from_golden
+
+    g = golden("config1")
+    n_kv, hd = int(g["n_kv"]), int(g["hd"])
+    L_ = g["h_in"].shape[0]
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    layers = {}
+    for l in range(L_):
+        sk, sv = (float(s) for s in g["scales"][l])
+        layers[l] = dkv.LayerDelta(l, {"k_proj": dkv.LowRankFactors(t(g["a_k"][l]), t(g["b_k"][l]), sk),
+                                       "v_proj": dkv.LowRankFactors(t(g["a_v"][l]), t(g["b_v"][l]), sv)})
+
+    class Delta:
+        pass
+
+    delta = Delta()
+    delta.layers = layers
+    xn = {l: t(g["xn"][l]) for l in range(L_)}
+    rope = (torch.from_numpy(g["rope_cos"]), torch.from_numpy(g["rope_sin"]))
+    patches = dkv.zeroth_order_patches(xn, delta, n_kv_heads=n_kv, head_dim=hd, rope=rope)
+    kv = dkv.KVCache(t(g["k_base"]), t(g["v_base"]))
+    out = dkv.apply_layer_patches(kv, patches)
+    k, v = out.k.cpu().numpy(), out.v.cpu().numpy()
+    assert rel_l2(k, g["k_patched"]) < 1e-5 and rel_l2(v, g["v_patched"]) < 1e-5
+    w = weights_from_golden(g)
+    kw = dict(n_layers=L_, n_heads=int(g["n_heads"]), n_kv=n_kv, hd=hd, eps=float(g["eps"]),
+              rope=(g["rope_cos"], g["rope_sin"]))
+    ours = logits_from_kv(w, g["tokens"], k, v, **kw)
+    fresh = logits_from_kv(w, g["tokens"], g["k_fresh"], g["v_fresh"], **kw)
+    assert abs(next_token_kl(fresh, ours) - float(g["kl_ref"])) < 1e-4
+
+
+def test_config1_paged_from_prenorm_fp8(cuda):
+    """Engine path on pages: pre-norm h_in stored as fp8 + scale, RMSNorm folded in."""
+    g = golden("config1")
+    n_kv, hd = int(g["n_kv"]), int(g["hd"])
+    L_, seq, d = g["h_in"].shape
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    x = t(g["h_in"].astype(np.float32))
+    xq, xs = dkv.quantize_rows(x, torch.float8_e4m3fn)
+    rk = g["a_k"].shape[1]
+    patcher = dkv.ExactPatcher(d, n_kv, hd, rank_k=rk, rank_v=rk, x_dtype=torch.float8_e4m3fn,
+                               rope=(torch.from_numpy(g["rope_cos"]), torch.from_numpy(g["rope_sin"])),
+                               norm_eps=float(g["eps"]))
+    b_k = t(g["b_k"] * g["scales"][:, 0][:, None, None])
+    b_v = t(g["b_v"] * g["scales"][:, 1][:, None, None])
+    packed = patcher.pack(t(g["a_k"]), b_k, t(g["a_v"]), b_v, 1.0, 1.0, norm_weight=t(g["norm_w"]))
+    kp = [bf16_from_bits(g["k_pages_in"][l], cuda) for l in range(L_)]
+    vp = [bf16_from_bits(g["v_pages_in"][l], cuda) for l in range(L_)]
+    seqs = ops.SeqBatchTensors(cu_seqlens=torch.tensor([0, seq], dtype=torch.int32, device=cuda),
+                               block_tables=t(g["block_table"][None].astype(np.int32)), max_seq_len=seq)
+    patcher.apply(xq, packed, kp, vp, seqs, x_scale=xs, apply_norm=True, check=True)
+    # oracle on the same fp8 activations (the reference has no fp8: it is fed their dequantised value)
+    xq_np = xq.view(torch.uint8).cpu().numpy()
+    kref = [g["k_pages_in"][l].copy() for l in range(L_)]
+    vref = [g["v_pages_in"][l].copy() for l in range(L_)]
+    factors = [((g["a_k"][l], g["b_k"][l], float(g["scales"][l][0])), (g["a_v"][l], g["b_v"][l], float(g["scales"][l][1])))
+               for l in range(L_)]
+    OX.exact_patch_paged(x=xq_np[..., :d], x_dtype="e4m3", x_scale=xs.cpu().numpy(), norm_w=g["norm_w"],
+                         eps=float(g["eps"]), factors=factors, cu_seqlens=np.array([0, seq]),
+                         block_tables=g["block_table"][None], k_pages=kref, v_pages=vref, n_kv=n_kv, hd=hd,
+                         rope=(g["rope_cos"], g["rope_sin"]), kind="bf16")
+    for l in range(L_):
+        for got_t, ref, base in ((kp[l], kref[l], g["k_pages_in"][l]), (vp[l], vref[l], g["v_pages_in"][l])):
+            got = bits_from_bf16(got_t)
+            assert rel_l2(bf16_bits_to_f32(got), bf16_bits_to_f32(ref)) < REL_TOL
+            dg = bf16_bits_to_f32(got) - bf16_bits_to_f32(base)
+            dr = bf16_bits_to_f32(ref) - bf16_bits_to_f32(base)
+            assert rel_l2(dg, dr) < 2e-2
+    # and against the reference's fp32-activation result (fp8 storage error included)
+    for l in range(L_):
+        got = bf16_bits_to_f32(bits_from_bf16(kp[l]))
+        assert rel_l2(got, bf16_bits_to_f32(g["k_pages_out"][l])) < REL_TOL
+
+
+def _random_case(gen, *, d, n_kv, hd, rk, rv, lens, bs, xdt, pdt, norm, rope, accumulate, positions):
+    L_ = 2
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    rows = int(cu[-1])
+    x = torch.randn(L_, max(rows, 1), d, generator=gen) * 2.0
+    if xdt == "e4m3":
+        amax = x.abs().amax(-1).clamp_min(1e-12)
+        xs = (amax / 448.0).float()
+        xbits = f32_to_e4m3_bits((x / xs[..., None]).numpy())
+    else:
+        xs = (torch.rand(L_, max(rows, 1), generator=gen) + 0.5).float()
+        xbits = (x / xs[..., None]).numpy().astype(np.float16)
+    d_kv = n_kv * hd
+    fac = []
+    for l in range(L_):
+        fk = (torch.randn(rk, d, generator=gen).numpy() / d ** 0.5, torch.randn(d_kv, rk, generator=gen).numpy(), 0.05) if rk else None
+        fv = (torch.randn(rv, d, generator=gen).numpy() / d ** 0.5, torch.randn(d_kv, rv, generator=gen).numpy(), 0.03) if rv else None
+        fac.append((fk, fv))
+    norm_w = (1.0 + 0.2 * torch.randn(L_, d, generator=gen)).numpy() if norm else None
+    need = [(n + bs - 1) // bs for n in lens]
+    nb = sum(need) + 3
+    perm = torch.randperm(nb, generator=gen).numpy().astype(np.int32)
+    tables = np.zeros((len(lens), max(max(need), 1)), np.int32)
+    k = 0
+    for b, n in enumerate(need):
+        tables[b, :n] = perm[k:k + n]
+        k += n
+    max_pos = max(lens) + 64
+    pos = None
+    if positions:
+        pos = np.concatenate([np.arange(n) + 7 * b for b, n in enumerate(lens)]).astype(np.int32)
+        max_pos = int(pos.max()) + 1 if pos.size else 1
+    tabs = OX.rope_tables(hd, max_pos) if rope else None
+    return dict(L=L_, cu=cu, rows=rows, xbits=xbits, xs=xs.numpy(), fac=fac, norm_w=norm_w, tables=tables, nb=nb,
+                tabs=tabs, pos=pos)
+
+
+@pytest.mark.parametrize(
+    "d,n_kv,hd,rk,rv,bs,xdt,pdt,norm,rope,acc,positions",
+    [
+        (128, 2, 64, 16, 16, 16, "e4m3", torch.bfloat16, True, True, True, False),
+        (576, 3, 64, 8, 8, 16, "f16", torch.bfloat16, False, True, True, False),
+        (256, 2, 128, 16, 16, 16, "e4m3", torch.bfloat16, True, True, True, False),
+        (256, 1, 256, 32, 24, 32, "e4m3", torch.bfloat16, False, True, True, False),
+        (64, 4, 16, 4, 4, 8, "f16", torch.float32, True, True, False, False),
+        (96, 3, 32, 17, 33, 1, "e4m3", torch.float16, False, True, True, False),
+        (192, 2, 64, 64, 64, 16, "f16", torch.bfloat16, True, False, True, False),
+        (128, 4, 32, 0, 16, 16, "e4m3", torch.bfloat16, False, True, True, False),
+        (128, 2, 64, 16, 0, 16, "e4m3", torch.float32, False, True, False, True),
+        (80, 5, 16, 40, 8, 4, "f16", torch.bfloat16, True, True, True, True),
+    ],
+)
+def test_exact_patch_matches_oracle(cuda, d, n_kv, hd, rk, rv, bs, xdt, pdt, norm, rope, acc, positions):
+    gen = torch.Generator().manual_seed(d * 131 + hd * 7 + rk + 3 * rv + bs)
+    lens = [1, 37, 128, 130, 0, 257]
+    case = _random_case(gen, d=d, n_kv=n_kv, hd=hd, rk=rk, rv=rv, lens=lens, bs=bs, xdt=xdt, pdt=pdt, norm=norm,
+                        rope=rope, accumulate=acc, positions=positions)
+    L_, nb = case["L"], case["nb"]
+    kind = {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}[pdt]
+    base_k = [torch.randn(nb, bs, n_kv, hd, generator=gen).to(pdt) for _ in range(L_)]
+    base_v = [torch.randn(nb, bs, n_kv, hd, generator=gen).to(pdt) for _ in range(L_)]
+    to_np = (lambda tt: bits_from_bf16(tt)) if pdt == torch.bfloat16 else (lambda tt: tt.cpu().numpy())
+    kref = [to_np(tt).copy() for tt in base_k]
+    vref = [to_np(tt).copy() for tt in base_v]
+    # oracle (positions handled by restating exact_kv_delta with explicit positions)
+    for l in range(L_):
+        fk, fv = case["fac"][l]
+        for b in range(len(lens)):
+            r0, r1 = int(case["cu"][b]), int(case["cu"][b + 1])
+            if r1 == r0:
+                continue
+            xv = OX.dequant_x(case["xbits"][l, r0:r1], xdt, case["xs"][l, r0:r1])
+            if norm:
+                xv = OX.rmsnorm(xv, case["norm_w"][l], 1e-6)
+            pos = None if case["pos"] is None else case["pos"][r0:r1]
+            dk, dv = OX.exact_kv_delta(xv, fk, fv, n_kv, hd, case["tabs"], positions=pos)
+            tab = case["tables"][b]
+            for src, pg in ((dk, kref[l]), (dv, vref[l])):
+                if acc:
+                    OX.scatter_into_paged(src, pg, list(tab), bs, kind=kind)
+                else:
+                    for i in range(src.shape[0]):
+                        pg[tab[i // bs], i % bs] = OX._from_f32(src[i], kind)
+    # kernel
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    rope_t = (torch.from_numpy(case["tabs"][0]), torch.from_numpy(case["tabs"][1])) if rope else None
+    xdtype = torch.float8_e4m3fn if xdt == "e4m3" else torch.float16
+    patcher = dkv.ExactPatcher(d, n_kv, hd, rank_k=rk, rank_v=rv, x_dtype=xdtype, rope=rope_t)
+    stack = lambda i, j: t(np.stack([case["fac"][l][i][j] for l in range(L_)])) if case["fac"][0][i] is not None else None
+    packed = patcher.pack(stack(0, 0), stack(0, 1), stack(1, 0), stack(1, 1), 0.05, 0.03,
+                          norm_weight=t(case["norm_w"]) if norm else None)
+    if xdt == "e4m3":
+        x = e4m3_from_bits(case["xbits"], cuda)
+    else:
+        x = t(case["xbits"])
+    kp = [tt.to(cuda) for tt in base_k]
+    vp = [tt.to(cuda) for tt in base_v]
+    seqs = ops.SeqBatchTensors(cu_seqlens=t(case["cu"]), block_tables=t(case["tables"]), max_seq_len=max(lens),
+                               positions=t(case["pos"]) if case["pos"] is not None else None)
+    patcher.apply(x, packed, kp, vp, seqs, x_scale=t(case["xs"]), apply_norm=norm, accumulate=acc, check=True)
+    tol = REL_TOL if acc else 2e-3
+    for l in range(L_):
+        for got_t, ref in ((kp[l], kref[l]), (vp[l], vref[l])):
+            got = to_np(got_t)
+            if pdt == torch.bfloat16:
+                a, b = bf16_bits_to_f32(got), bf16_bits_to_f32(ref)
+            else:
+                a, b = got.astype(np.float32), ref.astype(np.float32)
+            assert rel_l2(a, b) < tol, (l, rel_l2(a, b))
+
+
+def test_rope_range_error_reported(cuda):
+    patcher = dkv.ExactPatcher(64, 1, 64, rank_k=16, rank_v=16, x_dtype=torch.float16,
+                               rope=(torch.ones(8, 32), torch.zeros(8, 32)))
+    packed = patcher.pack(torch.randn(16, 64, device=cuda), torch.randn(64, 16, device=cuda),
+                          torch.randn(16, 64, device=cuda), torch.randn(64, 16, device=cuda), 1.0, 1.0)
+    x = torch.randn(1, 20, 64, device=cuda).half()
+    kp = [torch.zeros(2, 16, 1, 64, device=cuda, dtype=torch.bfloat16)]
+    vp = [torch.zeros(2, 16, 1, 64, device=cuda, dtype=torch.bfloat16)]
+    seqs = ops.SeqBatchTensors(cu_seqlens=torch.tensor([0, 20], dtype=torch.int32, device=cuda),
+                               block_tables=torch.tensor([[0, 1]], dtype=torch.int32, device=cuda), max_seq_len=20)
+    with pytest.raises(dkv.DkvError, match="RoPE"):
+        patcher.apply(x, packed, kp, vp, seqs, check=True)
+    with pytest.raises(ValueError, match="exceeds RoPE cache"):
+        layer = dkv.LayerDelta(0, {"k_proj": dkv.LowRankFactors(torch.randn(4, 64, device=cuda), torch.randn(64, 4, device=cuda))})
+        dkv.exact_kv_patch(torch.randn(20, 64, device=cuda), layer, n_kv_heads=1, head_dim=64,
+                           rope=(torch.ones(8, 32), torch.zeros(8, 32)))

@@ -1,0 +1,137 @@
+"""Pin the CPU oracle to golden vectors produced by the reference implementation."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import exact as OX
+from oracle.numerics import bf16_bits_to_f32, e4m3_bits_to_f32, f32_to_bf16_bits, f32_to_e4m3_bits
+from tests.conftest import golden
+
+
+def test_bf16_rounding_matches_torch():
+    import torch
+
+    x = torch.randn(10000, dtype=torch.float32) * 1e3
+    x[:10] = torch.tensor([0.0, -0.0, 1.0, 1.00390625, 1.005859375, 3.0e38, -3.0e38, 1e-40, 65504.0, 2.0 ** -130])
+    ours = f32_to_bf16_bits(x.numpy())
+    ref = x.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(ours, ref)
+    assert np.array_equal(bf16_bits_to_f32(ref), x.to(torch.bfloat16).float().numpy())
+
+
+def test_e4m3_decode_and_encode_match_torch():
+    import torch
+
+    bits = torch.arange(256, dtype=torch.uint8)
+    ref = bits.view(torch.float8_e4m3fn).float().numpy()
+    ours = e4m3_bits_to_f32(bits.numpy())
+    finite = ~np.isnan(ref)
+    assert np.array_equal(ours[finite], ref[finite])
+    assert np.isnan(ours[~finite]).all()
+    x = (torch.randn(20000) * 100).clamp(-448, 448)
+    x[:6] = torch.tensor([0.0, 448.0, -448.0, 0.0009765625, 0.001953125 * 1.5, 17.0])
+    assert np.array_equal(f32_to_e4m3_bits(x.numpy()), x.to(torch.float8_e4m3fn).view(torch.uint8).numpy())
+
+
+def test_paged_roundtrip_golden():
+    g = golden("paged")
+    cache = np.zeros((8, 8, 2, 8), np.float32)
+    OX.scatter_into_paged(g["rt_delta"], cache, list(g["rt_table"]), 8)
+    assert np.array_equal(cache, g["rt_cache_out"])
+    got = OX.gather_from_paged(cache, list(g["rt_table"]), 20, 8)
+    assert np.array_equal(got, g["rt_gather"])
+    assert np.allclose(got, g["rt_delta"])
+
+
+@pytest.mark.parametrize("name", ["l4", "l5a", "l5b"])
+def test_paged_bf16_layouts_golden(name):
+    g = golden("paged")
+    c = g[f"{name}_in"].copy()
+    OX.scatter_into_paged(g[f"{name}_delta"], c, list(g["l_table"]), int(g["l_bs"]), kv_dim=int(g[f"{name}_kv"]), kind="bf16")
+    assert np.array_equal(c, g[f"{name}_out"])  # bit-exact
+    got = OX.gather_from_paged(c, list(g["l_table"]), 13, int(g["l_bs"]), kv_dim=int(g[f"{name}_kv"]))
+    assert np.array_equal(got, g[f"{name}_gather"])
+
+
+def test_paged_errors_match_reference_text():
+    with pytest.raises(ValueError, match="block_table shorter than prefix"):
+        OX.scatter_into_paged(np.zeros((20, 1, 4), np.float32), np.zeros((4, 8, 1, 4), np.float32), [0, 1], 8)
+    with pytest.raises(ValueError, match="unsupported paged KV layout"):
+        OX.scatter_into_paged(np.zeros((4, 1, 4), np.float32), np.zeros((3, 4, 8, 1, 4), np.float32), [0], 8)
+
+
+def test_rope_tables_match_reference():
+    g = golden("config1")
+    cos, sin = OX.rope_tables(int(g["hd"]), g["rope_cos"].shape[0])
+    assert np.abs(cos - g["rope_cos"]).max() <= 2e-7
+    assert np.abs(sin - g["rope_sin"]).max() <= 2e-7
+
+
+def test_layer0_exact_golden():
+    g = golden("layer0")
+    n_kv, hd = int(g["n_kv"]), int(g["hd"])
+    rope = (g["rope_cos"], g["rope_sin"])
+    dk, dv = OX.exact_kv_delta(g["xn"], (g["a_k"], g["b_k"], float(g["s_k"])),
+                               (g["a_v"], g["b_v"], float(g["s_v"])), n_kv, hd, rope)
+    assert np.abs(dk - g["dk"]).max() < 1e-6
+    assert np.abs(dv - g["dv"]).max() < 1e-6
+    kp = g["k0"] + dk
+    assert np.abs(kp - g["k_patched"]).max() < 1e-6
+    # the reference's own claim: layer-0 patch equals the fresh prefill (<2e-5)
+    assert np.abs(kp - g["k_fresh"]).max() < 2e-5
+    assert np.abs(g["v0"] + dv - g["v_fresh"]).max() < 2e-5
+
+
+def test_config1_exact_golden():
+    g = golden("config1")
+    n_kv, hd = int(g["n_kv"]), int(g["hd"])
+    rope = (g["rope_cos"], g["rope_sin"])
+    for l in range(g["h_in"].shape[0]):
+        xn = OX.rmsnorm(g["h_in"][l], g["norm_w"][l], float(g["eps"]))
+        assert np.abs(xn - g["xn"][l]).max() < 1e-5
+        sk, sv = g["scales"][l]
+        dk, dv = OX.exact_kv_delta(xn, (g["a_k"][l], g["b_k"][l], float(sk)), (g["a_v"][l], g["b_v"][l], float(sv)),
+                                   n_kv, hd, rope)
+        assert np.abs(dk - g["dk"][l]).max() < 1e-6
+        assert np.abs(dv - g["dv"][l]).max() < 1e-6
+    # paged bf16 through the permuted table: bit-exact given the reference's dK/dV
+    bs = int(g["block_size"])
+    for l in range(g["h_in"].shape[0]):
+        kp = g["k_pages_in"][l].copy()
+        OX.scatter_into_paged(g["dk"][l], kp, list(g["block_table"]), bs, kind="bf16")
+        assert np.array_equal(kp, g["k_pages_out"][l])
+
+
+def test_fp8_paged_golden():
+    g = golden("fp8_paged")
+    n_kv, hd = int(g["n_kv"]), int(g["hd"])
+    L_ = g["x_bits"].shape[0]
+    kp = [g["k_pages_in"][l].copy() for l in range(L_)]
+    vp = [g["v_pages_in"][l].copy() for l in range(L_)]
+    factors = [((g["a_k"][l], g["b_k"][l], float(g["s_k"])), (g["a_v"][l], g["b_v"][l], float(g["s_v"]))) for l in range(L_)]
+    OX.exact_patch_paged(x=g["x_bits"], x_dtype="e4m3", x_scale=g["x_scale"], norm_w=g["norm_w"], eps=float(g["eps"]),
+                         factors=factors, cu_seqlens=g["cu_seqlens"], block_tables=g["block_tables"], k_pages=kp,
+                         v_pages=vp, n_kv=n_kv, hd=hd, rope=(g["rope_cos"], g["rope_sin"]), kind="bf16")
+    for l in range(L_):
+        for ours, ref in ((kp[l], g["k_pages_out"][l]), (vp[l], g["v_pages_out"][l])):
+            a, b = bf16_bits_to_f32(ours), bf16_bits_to_f32(ref)
+            rel = np.linalg.norm(a - b) / np.linalg.norm(b)
+            assert rel < 1e-5
+            # fp32 summation order may flip a bf16 rounding; almost every element is identical
+            assert (ours == ref).mean() > 0.995
+
+
+def test_config1_logits_and_kl_golden():
+    from oracle.model import logits_from_kv, next_token_kl, weights_from_golden
+
+    g = golden("config1")
+    w = weights_from_golden(g)
+    kw = dict(n_layers=g["h_in"].shape[0], n_heads=int(g["n_heads"]), n_kv=int(g["n_kv"]), hd=int(g["hd"]),
+              eps=float(g["eps"]), rope=(g["rope_cos"], g["rope_sin"]))
+    fresh = logits_from_kv(w, g["tokens"], g["k_fresh"], g["v_fresh"], **kw)
+    patched = logits_from_kv(w, g["tokens"], g["k_patched"], g["v_patched"], **kw)
+    assert np.abs(fresh - g["fresh_logits"]).max() < 1e-5
+    assert np.abs(patched - g["patched_logits"]).max() < 1e-5
+    assert abs(next_token_kl(fresh, patched) - float(g["kl_ref"])) < 1e-6

@@ -32,6 +32,7 @@ DKV_MAX_LAYERS = 128
 EXPORTED = (
     "dkv_status_string",
     "dkv_abi_version",
+    "dkv_last_cuda_error",
     "dkv_scatter_paged",
     "dkv_gather_paged",
     "dkv_quantize_rows",
@@ -134,6 +135,8 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_status_string.argtypes = [C.c_int]
     lib.dkv_abi_version.restype = C.c_int
     lib.dkv_abi_version.argtypes = []
+    lib.dkv_last_cuda_error.restype = C.c_char_p
+    lib.dkv_last_cuda_error.argtypes = []
     lib.dkv_scatter_paged.restype = C.c_int
     lib.dkv_scatter_paged.argtypes = [P, I32, I64, I64, C.POINTER(PagedCache), C.POINTER(SeqBatch), P, P]
     lib.dkv_gather_paged.restype = C.c_int
@@ -169,6 +172,8 @@ class DkvError(RuntimeError):
     def __init__(self, status: int, where: str = ""):
         self.status = status
         msg = lib().dkv_status_string(status).decode()
+        if status == DKV_ERR_CUDA:
+            msg += f" [{lib().dkv_last_cuda_error().decode()}]"
         super().__init__(f"{where}: {msg} (status {status})" if where else msg)
 
 

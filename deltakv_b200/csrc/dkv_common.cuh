@@ -208,9 +208,17 @@ __device__ __forceinline__ float exp2i(int e) {  // exact 2^e for e in [-126, 12
 
 }  // namespace dkv
 
-// host-side helper: map cudaError to DKV status
-#define DKV_CUDA_CHECK(expr)                    \
-  do {                                          \
-    cudaError_t err__ = (expr);                 \
-    if (err__ != cudaSuccess) return DKV_ERR_CUDA; \
+namespace dkv {
+// Remembers the most recent failing CUDA runtime call of this thread (dkv_last_cuda_error).
+void note_cuda_error(cudaError_t err, const char *what);
+}  // namespace dkv
+
+// host-side helper: map cudaError to DKV status, remembering the cause
+#define DKV_CUDA_CHECK(expr)                      \
+  do {                                            \
+    cudaError_t err__ = (expr);                   \
+    if (err__ != cudaSuccess) {                   \
+      ::dkv::note_cuda_error(err__, #expr);       \
+      return DKV_ERR_CUDA;                        \
+    }                                             \
   } while (0)

@@ -30,7 +30,7 @@ namespace dkv {
 namespace exact {
 
 constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kThreads = kConsumerWarps * 32;
 constexpr int kMTile = 16 * kConsumerWarps;  // tokens per tile
 constexpr int kXStageBytes = kMTile * 128;   // one 128-byte k-slab of the tile
 constexpr int kHeaderBytes = 256;
@@ -501,8 +501,71 @@ __device__ __forceinline__ void expand_projection(const Params &p, const Tile &t
   }
 }
 
+// TMA producer run by one thread: walks the same (tile, k-slab) sequence the warps consume
+// and keeps every ring slot filled.  The X slab comes by a 3-D tensor copy (128-B swizzle),
+// the matching packed-A slab by a contiguous bulk copy; both complete on full[stage].
+template <int A_STAGE>
+struct Producer {
+  int64_t tile;
+  int kc, layer, row0, stage;
+  uint32_t phase, issued, parity;
+
+  __device__ void init(const Params &p) {
+    tile = static_cast<int64_t>(blockIdx.x) - gridDim.x;
+    kc = p.kc;
+    stage = 0;
+    phase = issued = parity = 0;
+  }
+  __device__ bool advance(const Params &p) {
+    if (kc < p.kc) return true;
+    for (;;) {
+      tile += gridDim.x;
+      if (tile >= p.n_tiles) return false;
+      Tile t;
+      if (decode_tile(p, tile, t)) {
+        kc = 0;
+        layer = t.layer;
+        row0 = t.row0;
+        return true;
+      }
+    }
+  }
+  // 1: issued one item; 0: nothing left; -1: gave up waiting for a free slot
+  __device__ int issue(const Params &p, uint8_t *sx, uint8_t *sa, uint64_t *full, uint64_t *empty,
+                       volatile int *abort) {
+    if (!advance(p)) return 0;
+    if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort)) return -1;
+    mbar_arrive_expect_tx(&full[stage], kXStageBytes + A_STAGE);
+    tma_load_3d(sx + stage * kXStageBytes, &p.x_map, &full[stage], kc * p.stage_k, row0, layer);
+    bulk_load(sa + stage * A_STAGE,
+              p.packed + layer * p.packed_stride + p.a_off + static_cast<int64_t>(kc) * A_STAGE,
+              A_STAGE, &full[stage]);
+    issued |= 1u << stage;
+    parity = (parity & ~(1u << stage)) | (phase << stage);
+    ++kc;
+    if (++stage == kStages) {
+      stage = 0;
+      phase ^= 1;
+    }
+    return 1;
+  }
+  // never let the CTA exit with a copy still landing in its shared memory
+  __device__ void drain(const Params &p, uint64_t *full) const {
+    for (int s = 0; s < kStages; ++s) {
+      if (!(issued & (1u << s))) continue;
+      const long long t0 = clock64();
+      while (!mbar_try_wait(&full[s], (parity >> s) & 1)) {
+        if (clock64() - t0 > kWaitLimitCycles) {
+          record_error(p.status, DKV_ERR_TIMEOUT);
+          break;
+        }
+      }
+    }
+  }
+};
+
 template <int XT, int R16, bool NORM, int PDT>
-__global__ void __maxnreg__(224) patch_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constant__ Params p) {
   constexpr int NT1 = 4 * R16;  // phase-1 n-tiles: K codes then V codes, 8 columns each
   constexpr int SROW = XT == 0 ? 256 : 128;
   constexpr int A_STAGE = 2 * 16 * R16 * SROW;
@@ -525,52 +588,22 @@ __global__ void __maxnreg__(224) patch_kernel(const __grid_constant__ Params p) 
   }
   __syncthreads();
 
-  if (warp == kConsumerWarps) {
-    // ------------------------------- producer -------------------------------
-    if (lane != 0) return;
+  // lane 0 of warp 0 drives the TMA ring, kStages (tile, k-slab) items ahead
+  const bool is_prod = threadIdx.x == 0;
+  Producer<A_STAGE> prod;
+  if (is_prod) {
     prefetch_tensormap(&p.x_map);
-    int stage = 0;
-    uint32_t phase = 0, issued = 0, parity = 0;
-    bool ok = true;
-    for (int64_t tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
-      Tile t;
-      if (!decode_tile(p, tile, t)) continue;
-      const uint8_t *asrc = p.packed + t.layer * p.packed_stride + p.a_off;
-      for (int kc = 0; kc < p.kc; ++kc) {
-        if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag)) {
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&full[stage], kXStageBytes + A_STAGE);
-        tma_load_3d(sx + stage * kXStageBytes, &p.x_map, &full[stage], kc * p.stage_k, t.row0,
-                    t.layer);
-        bulk_load(sa + stage * A_STAGE, asrc + static_cast<int64_t>(kc) * A_STAGE, A_STAGE,
-                  &full[stage]);
-        issued |= 1u << stage;
-        parity = (parity & ~(1u << stage)) | (phase << stage);
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1;
-        }
+    prod.init(p);
+    for (int i = 0; i < kStages; ++i) {
+      const int r = prod.issue(p, sx, sa, full, empty, abort_flag);
+      if (r < 0) {
+        record_error(p.status, DKV_ERR_TIMEOUT);
+        *abort_flag = 1;
       }
+      if (r <= 0) break;
     }
-    if (!ok) {
-      record_error(p.status, DKV_ERR_TIMEOUT);
-      *abort_flag = 1;
-    }
-    // never leave the CTA with a copy still landing in shared memory
-    for (int s = 0; s < kStages; ++s) {
-      if (!(issued & (1u << s))) continue;
-      const long long t0 = clock64();
-      while (!mbar_try_wait(&full[s], (parity >> s) & 1)) {
-        if (clock64() - t0 > kWaitLimitCycles) {
-          record_error(p.status, DKV_ERR_TIMEOUT);
-          break;
-        }
-      }
-    }
-    return;
   }
+  __syncwarp();
 
   // ------------------------------- consumers --------------------------------
   const int g = lane >> 2, q = lane & 3;
@@ -668,6 +701,7 @@ __global__ void __maxnreg__(224) patch_kernel(const __grid_constant__ Params p) 
       if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) {
         record_error(p.status, DKV_ERR_TIMEOUT);
         *abort_flag = 1;
+        if (is_prod) prod.drain(p, full);
         return;
       }
       const uint32_t xb = smem_u32(sx + stage * kXStageBytes) + xrow * 128;
@@ -730,6 +764,14 @@ __global__ void __maxnreg__(224) patch_kernel(const __grid_constant__ Params p) 
       if (++stage == kStages) {
         stage = 0;
         phase ^= 1;
+      }
+      if (warp == 0) {
+        // refill the slot just released by all warps with the item kStages ahead
+        if (is_prod && prod.issue(p, sx, sa, full, empty, abort_flag) < 0) {
+          record_error(p.status, DKV_ERR_TIMEOUT);
+          *abort_flag = 1;
+        }
+        __syncwarp();
       }
     }
 
@@ -799,6 +841,7 @@ __global__ void __maxnreg__(224) patch_kernel(const __grid_constant__ Params p) 
     if (p.do_k) expand_projection<R16, PDT, true>(p, t, ri, ck, om_k, lane);
     if (p.do_v) expand_projection<R16, PDT, false>(p, t, ri, cv, om_v, lane);
   }
+  if (is_prod) prod.drain(p, full);
 }
 
 // ----------------------------------------------------------------------------
@@ -949,7 +992,10 @@ extern "C" int dkv_exact_patch_paged(const dkv_exact_patch_args *a, dkv_stream_t
   Params p;
   memset(&p, 0, sizeof(p));
   auto enc = tensormap_encoder();
-  if (enc == nullptr) return DKV_ERR_CUDA;
+  if (enc == nullptr) {
+    note_cuda_error(cudaErrorNotSupported, "cuTensorMapEncodeTiled entry point");
+    return DKV_ERR_CUDA;
+  }
   {
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(g.d_model), static_cast<cuuint64_t>(a->x_rows),
                           static_cast<cuuint64_t>(a->n_layers)};

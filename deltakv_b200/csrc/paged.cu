@@ -6,6 +6,8 @@
 // `pages[bid, :span] = pages[bid, :span] + delta[start:end]`, i.e. fp32(page) +
 // fp32(delta) rounded once to the page dtype; this kernel does the same per element,
 // so results are bit-identical.
+#include <stdio.h>
+
 #include "dkv_common.cuh"
 
 namespace dkv {
@@ -183,3 +185,13 @@ extern "C" const char *dkv_status_string(int status) {
 }
 
 extern "C" int dkv_abi_version(void) { return 1; }
+
+namespace dkv {
+static thread_local char g_last_cuda_error[256] = "";
+void note_cuda_error(cudaError_t err, const char *what) {
+  snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s (%s)", cudaGetErrorName(err),
+           cudaGetErrorString(err), what);
+}
+}  // namespace dkv
+
+extern "C" const char *dkv_last_cuda_error(void) { return dkv::g_last_cuda_error; }

@@ -61,6 +61,8 @@ typedef struct CUstream_st *dkv_stream_t;
 const char *dkv_status_string(int status);
 /* ABI version: bumped when a struct below changes. */
 int dkv_abi_version(void);
+/* Text of the last CUDA runtime failure behind a DKV_ERR_CUDA on this thread ("" if none). */
+const char *dkv_last_cuda_error(void);
 
 /*
  * A paged KV cache of one layer for one of K or V.  Element (block, slot, head, dim)

@@ -1,0 +1,499 @@
+"""Throughput of the fused exact KV patch on the Llama-3-8B-shaped workload.
+
+One step = one pass of the exact/zeroth-order patch route over a full cache: pack the
+rank-16 k/v LoRA factors of 32 layers, then patch 64 sequences x 4096 tokens x 32 layers
+(8,388,608 token-layers) from fp8-e4m3 stored activations (per-token scale, RMSNorm
+folded in) into bf16 paged K/V (block 16, permuted block table), RoPE on K.
+
+    python bench.py [--gpus N --steps K --warmup W]          # this implementation
+    python bench.py --impl reference ...                       # CPU reference arm
+
+Under torchrun (N>1) every rank patches its own request shard of the same size (weak
+scaling; no data-path collective).  Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "patched token·layers/s (Llama-8B shape, rank-16 k/v LoRA)"
+UNIT = "token·layers/s"
+BYTES_PER_UNIT = 4096 + 4 + 4096 + 4096  # X fp8 + scale + K read/write + V read/write
+WORKLOAD = ("Llama-3-8B-shaped exact patch: 32 layers, d=4096, 8 KV heads x 128, 64 seqs x 4096 tokens, "
+            "rank-16 k/v LoRA (rel. norm 1e-2), fp8-e4m3 stored X + per-token scale, RMSNorm folded, "
+            "RoPE (theta 5e5), bf16 paged KV block 16")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--seqs", type=int, default=64)
+    ap.add_argument("--seq-len", type=int, default=4096)
+    ap.add_argument("--e2e-seqs", type=int, default=4)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+class Geo:
+    d_model, n_kv, hd, rank, bs, eps, rope_theta = 4096, 8, 128, 16, 16, 1e-5, 500000.0
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+def make_factors(n_layers, device, gen):
+    G = Geo
+    d, d_kv, r = G.d_model, G.n_kv * G.hd, G.rank
+    w_norm = 0.02 * math.sqrt(d_kv * d)  # ||W_k|| of an N(0, 0.02^2) projection
+    out = {}
+    for name in ("k", "v"):
+        A = torch.randn(n_layers, r, d, generator=gen, device=device) / math.sqrt(d)
+        B = torch.randn(n_layers, d_kv, r, generator=gen, device=device)
+        # scale so ||s B A||_F / ||W||_F = 1e-2 per layer (use the mean over layers)
+        ba = torch.stack([(B[l] @ A[l]).norm() for l in range(n_layers)]).mean().item()
+        out[name] = (A, B, 1e-2 * w_norm / ba)
+    norm_w = 1.0 + 0.05 * torch.randn(n_layers, d, generator=gen, device=device)
+    return out, norm_w
+
+
+def make_workload(n_layers, n_seqs, seq_len, device, seed):
+    import deltakv_b200 as dkv
+    from deltakv_b200 import ops
+
+    G = Geo
+    gen = torch.Generator(device=device).manual_seed(seed)
+    rows = n_seqs * seq_len
+    x = torch.empty(n_layers, rows, G.d_model, dtype=torch.float8_e4m3fn, device=device)
+    xs = torch.empty(n_layers, rows, dtype=torch.float32, device=device)
+    for l in range(n_layers):
+        # residual-stream-like rows: N(0,1) with a per-token magnitude spread
+        h = torch.randn(rows, G.d_model, generator=gen, device=device)
+        h *= (0.5 + torch.rand(rows, 1, generator=gen, device=device))
+        q, s = dkv.quantize_rows(h, torch.float8_e4m3fn)
+        x[l].copy_(q)
+        xs[l].copy_(s)
+        del h, q, s
+    blocks_per_seq = (seq_len + G.bs - 1) // G.bs
+    nb = n_seqs * blocks_per_seq
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(seed + 2)).to(torch.int32)
+    tables = perm.view(n_seqs, blocks_per_seq).to(device)
+    caches = []  # vLLM flash-attention layout per layer: [2, num_blocks, block, n_kv, head_dim]
+    for _ in range(n_layers):
+        c = torch.empty(2, nb, G.bs, G.n_kv, G.hd, dtype=torch.bfloat16, device=device)
+        c.normal_(generator=gen)
+        caches.append(c)
+    facs, norm_w = make_factors(n_layers, device, gen)
+    cu = torch.arange(0, n_seqs + 1, dtype=torch.int32, device=device) * seq_len
+    seqs = ops.SeqBatchTensors(cu_seqlens=cu, block_tables=tables, max_seq_len=seq_len)
+    rope = dkv.RotaryEmbedding(G.hd, max_seq=seq_len, base=G.rope_theta)
+    return dict(x=x, xs=xs, caches=caches, facs=facs, norm_w=norm_w, seqs=seqs, rope=rope, tables=tables)
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML, polled in a thread)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, device_index: int):
+        self.samples, self.reasons = [], 0
+        self.stop_evt = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = int(vis.split(",")[device_index]) if vis else device_index
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+
+    def _run(self):
+        while not self.stop_evt.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                fn = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    getattr(self.nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+                self.reasons |= fn(self.h)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self.stop_evt.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        names = [n for n, b in self.REASONS.items() if self.reasons & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": names,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle port (cpu_baseline and the reference arm)
+# ---------------------------------------------------------------------------
+def cpu_pool_threads() -> int:
+    """Host threads for the CPU arm: every core, capped so each worker's ~0.5 GB of
+    fp32 temporaries (one 4096-token sequence of one layer) fits in free memory."""
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except AttributeError:
+        cores = os.cpu_count() or 1
+    try:
+        import psutil
+
+        cap = int(psutil.virtual_memory().available * 0.6 // (512 << 20))
+        return max(1, min(cores, cap))
+    except Exception:
+        return cores
+
+
+class CpuSample:
+    """A bounded sample of the workload on the host: P distinct (layer, sequence) inputs,
+    one private paged K/V per worker thread (a single sequence's blocks)."""
+
+    def __init__(self, n_inputs: int, seq_len: int, seed: int = 5):
+        from oracle import exact as OX
+
+        G = Geo
+        g = torch.Generator().manual_seed(seed)
+        self.seq_len = seq_len
+        self.inputs = []
+        facs, norm_w = make_factors(n_inputs, "cpu", g)
+        for i in range(n_inputs):
+            h = torch.randn(seq_len, G.d_model, generator=g) * (0.5 + torch.rand(seq_len, 1, generator=g))
+            amax = h.abs().amax(-1).clamp_min(1e-12)
+            s = (amax / 448.0).float()
+            xb = (h / s[:, None]).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+            fk = (facs["k"][0][i].numpy(), facs["k"][1][i].numpy(), facs["k"][2])
+            fv = (facs["v"][0][i].numpy(), facs["v"][1][i].numpy(), facs["v"][2])
+            self.inputs.append((xb, s.numpy(), norm_w[i].numpy(), fk, fv))
+        self.rope = OX.rope_tables(G.hd, seq_len, G.rope_theta)
+        nblk = (seq_len + G.bs - 1) // G.bs
+        self.table = list(np.random.default_rng(seed).permutation(nblk))
+        self.nblk = nblk
+
+    def new_pages(self):
+        G = Geo
+        rng = np.random.default_rng(0)
+        shape = (self.nblk, G.bs, G.n_kv, G.hd)
+        return (rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16),
+                rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16))
+
+    def patch_one(self, i: int, kp, vp) -> int:
+        """The reference's exact branch on one (layer, sequence): dequant -> RMSNorm ->
+        exact_kv_patch -> materialize -> scatter_into_paged (K and V).  Returns units."""
+        from oracle import exact as OX
+
+        G = Geo
+        xb, s, w, fk, fv = self.inputs[i % len(self.inputs)]
+        x = OX.dequant_x(xb, "e4m3", s)
+        x = OX.rmsnorm(x, w, G.eps)
+        dk, dv = OX.exact_kv_delta(x, fk, fv, G.n_kv, G.hd, self.rope)
+        OX.scatter_into_paged(dk, kp, self.table, G.bs, kind="bf16")
+        OX.scatter_into_paged(dv, vp, self.table, G.bs, kind="bf16")
+        return self.seq_len
+
+    def run(self, threads: int, seconds: float | None = None, pairs: int | None = None):
+        """Process pairs on `threads` workers for `seconds` (or `pairs` pairs); returns
+        (units, elapsed_s)."""
+        from concurrent.futures import ThreadPoolExecutor
+
+        from threadpoolctl import threadpool_limits
+
+        pages = [self.new_pages() for _ in range(threads)]
+        counter = [0]
+        lock = threading.Lock()
+        deadline = None if seconds is None else time.perf_counter() + seconds
+
+        def worker(wi):
+            done = 0
+            while True:
+                with lock:
+                    if pairs is not None and counter[0] >= pairs:
+                        return done
+                    if deadline is not None and time.perf_counter() >= deadline:
+                        return done
+                    k = counter[0]
+                    counter[0] += 1
+                done += self.patch_one(k, *pages[wi])
+
+        with threadpool_limits(1):
+            t0 = time.perf_counter()
+            with ThreadPoolExecutor(threads) as ex:
+                units = sum(ex.map(worker, range(threads)))
+            el = time.perf_counter() - t0
+        return units, el
+
+
+def cpu_baseline(seconds: float, seq_len: int) -> dict:
+    threads = cpu_pool_threads()
+    sample = CpuSample(n_inputs=4, seq_len=seq_len)
+    sample.run(threads, pairs=threads)  # warm-up: every thread once
+    units, el = sample.run(threads, seconds=seconds)
+    return {"value": units / el, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{units // seq_len} (layer, sequence) pairs of {seq_len} tokens in {el:.1f} s "
+                      f"(oracle numpy port of the reference's exact branch, {threads} threads)"}
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def run_reference(args):
+    world, rank, _ = dist_setup(args)
+    if rank != 0:
+        return 0
+    threads = cpu_pool_threads()
+    sample = CpuSample(n_inputs=4, seq_len=args.seq_len)
+    for _ in range(args.warmup):
+        sample.run(threads, pairs=threads)
+    units_tot, el_tot = 0, 0.0
+    for _ in range(args.steps):
+        u, el = sample.run(threads, pairs=threads)
+        units_tot += u
+        el_tot += el
+    value = units_tot / el_tot
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el_tot / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "step": f"{threads} (layer, sequence) pairs of {args.seq_len} tokens "
+                   "(bounded sample of the workload)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{threads} (layer, sequence) pairs per step, oracle numpy port of the "
+                                   "reference's exact branch (dequant, RMSNorm, exact_kv_patch, materialize, "
+                                   "scatter_into_paged)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import deltakv_b200 as dkv
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    G = Geo
+    wl = make_workload(args.layers, args.seqs, args.seq_len, dev, seed=1000 + rank)
+    facs = wl["facs"]
+    patcher = dkv.ExactPatcher(G.d_model, G.n_kv, G.hd, rank_k=G.rank, rank_v=G.rank,
+                               x_dtype=torch.float8_e4m3fn, rope=wl["rope"], norm_eps=G.eps)
+    packed = torch.empty(args.layers, patcher.packed_bytes, dtype=torch.uint8, device=dev)
+    kpages = [c[0] for c in wl["caches"]]
+    vpages = [c[1] for c in wl["caches"]]
+    units = args.layers * args.seqs * args.seq_len
+    stream = torch.cuda.current_stream()
+
+    def step(ev=None):
+        patcher.pack(facs["k"][0], facs["k"][1], facs["v"][0], facs["v"][1], facs["k"][2], facs["v"][2],
+                     norm_weight=wl["norm_w"], out=packed)
+        if ev is not None:
+            ev[0].record(stream)
+        patcher.apply(wl["x"], packed, kpages, vpages, wl["seqs"], x_scale=wl["xs"], apply_norm=True)
+        if ev is not None:
+            ev[1].record(stream)
+
+    # correctness guard before timing: device status clean after one step
+    step()
+    torch.cuda.synchronize()
+    from deltakv_b200 import ops
+
+    ops.status_word(dev).raise_if_set("bench warm-up")
+    for _ in range(max(0, args.warmup - 1)):
+        step()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t_start.record(stream)
+        for i in range(args.steps):
+            step(kev[i])
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = t_start.elapsed_time(t_end)
+    kern_ms = [a.elapsed_time(b) for a, b in kev]
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ops.status_word(dev).raise_if_set("bench timed region")
+    ms_step = ms / args.steps
+    value = units * world / (ms_step / 1e3)
+    kmean = sum(kern_ms) / len(kern_ms)
+    achieved = units * BYTES_PER_UNIT / (kmean / 1e3) / 1e9
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    peak = peaks.get("hbm_gbs")
+    peak_kind = "of measured (MEASURED_PEAKS.json hbm_gbs, burst copy)" if peak else "of fallback (6650 GB/s)"
+    peak = peak or 6650.0
+    traffic = None
+    tfile = ROOT / "profiles" / "exact_patch_traffic.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get("bytes_per_launch_full_workload")
+        except Exception:
+            traffic = None
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, patcher, dev, world)
+    del wl, kpages, vpages
+    torch.cuda.empty_cache()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(args.cpu_seconds, args.seq_len)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 tensor-core products, fp32 accumulate (e4m3 X, bf16 pages)",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "layers": args.layers, "seqs_per_gpu": args.seqs,
+                       "seq_len": args.seq_len, "units_per_step_per_gpu": units,
+                       "parallelism": f"request shards x{world} (weak)",
+                       "l2": f"inputs {units * BYTES_PER_UNIT / 1e9:.1f} GB per GPU >> 126 MB L2, no flush needed",
+                       "launches_per_step": 2},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
+                         "kernel": "patch_kernel", "kernel_ms": kmean,
+                         "algorithmic_bytes_per_unit": BYTES_PER_UNIT},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def run_e2e(args, patcher, dev, world):
+    """Same metric through the public API with host buffers: every step copies the step's
+    stored activations, scales, factors, block tables and the touched pages host->device,
+    patches, and copies the pages back."""
+    import deltakv_b200 as dkv
+    from deltakv_b200 import ops
+
+    G = Geo
+    n_seqs = args.e2e_seqs
+    cpu = make_workload(args.layers, n_seqs, args.seq_len, dev, seed=77)
+    host = {
+        "x": cpu["x"].view(torch.uint8).cpu().pin_memory(),
+        "xs": cpu["xs"].cpu().pin_memory(),
+        "caches": torch.stack(cpu["caches"]).cpu().pin_memory(),
+        "tables": cpu["tables"].cpu().pin_memory(),
+        "a_k": cpu["facs"]["k"][0].cpu().pin_memory(), "b_k": cpu["facs"]["k"][1].cpu().pin_memory(),
+        "a_v": cpu["facs"]["v"][0].cpu().pin_memory(), "b_v": cpu["facs"]["v"][1].cpu().pin_memory(),
+        "norm_w": cpu["norm_w"].cpu().pin_memory(),
+    }
+    sk, sv = cpu["facs"]["k"][2], cpu["facs"]["v"][2]
+    del cpu
+    torch.cuda.empty_cache()
+    d = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
+    packed = torch.empty(args.layers, patcher.packed_bytes, dtype=torch.uint8, device=dev)
+    cu = torch.arange(0, n_seqs + 1, dtype=torch.int32, device=dev) * args.seq_len
+    stream = torch.cuda.current_stream()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = host["caches"].numel() * host["caches"].element_size()
+
+    def step():
+        for k, v in host.items():
+            d[k].copy_(v, non_blocking=True)
+        patcher.pack(d["a_k"], d["b_k"], d["a_v"], d["b_v"], sk, sv, norm_weight=d["norm_w"], out=packed)
+        seqs = ops.SeqBatchTensors(cu_seqlens=cu, block_tables=d["tables"], max_seq_len=args.seq_len)
+        patcher.apply(d["x"].view(torch.float8_e4m3fn), packed, [c[0] for c in d["caches"]],
+                      [c[1] for c in d["caches"]], seqs, x_scale=d["xs"], apply_norm=True)
+        host["caches"].copy_(d["caches"], non_blocking=True)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    n = 3
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    a.record(stream)
+    for _ in range(n):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / n
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    units = args.layers * n_seqs * args.seq_len * world
+    del d, host
+    torch.cuda.empty_cache()
+    return {"value": units / (ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": ms, "sample": f"{n_seqs} seqs x {args.layers} layers per GPU, pinned host buffers"}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -51,12 +51,14 @@ def apply_rope(x: np.ndarray, cos_half: np.ndarray, sin_half: np.ndarray, positi
 
 
 def rmsnorm(x: np.ndarray, w: np.ndarray | None, eps: float) -> np.ndarray:
-    x = x.astype(F32)
-    ms = (x * x).mean(axis=-1, keepdims=True, dtype=F32)
-    y = x * (F32(1.0) / np.sqrt(ms + F32(eps))).astype(F32)
+    """``x * rsqrt(mean(x^2) + eps) * w`` in fp32, multiplied in that order (model.py:55-56)."""
+    y = np.array(x, dtype=F32, copy=True)
+    ms = np.einsum("ij,ij->i", y, y, dtype=F32) / F32(y.shape[-1])
+    r = (F32(1.0) / np.sqrt(ms + F32(eps))).astype(F32)
+    y *= r[:, None]
     if w is not None:
-        y = y * w.astype(F32)
-    return y.astype(F32)
+        y *= w.astype(F32)
+    return y
 
 
 def lora_codes(x: np.ndarray, A: np.ndarray, scale: float) -> np.ndarray:
@@ -143,12 +145,9 @@ def gather_from_paged(cache: np.ndarray, block_table, seq_len: int, block_size: 
 
 def dequant_x(x: np.ndarray, x_dtype: str, scale: np.ndarray | None) -> np.ndarray:
     """Stored activations -> fp32: e4m3 bits (uint8) or float16, times a per-row scale."""
-    if x_dtype == "e4m3":
-        v = e4m3_bits_to_f32(x)
-    else:
-        v = x.astype(F32)
+    v = e4m3_bits_to_f32(x) if x_dtype == "e4m3" else x.astype(F32)
     if scale is not None:
-        v = (v * scale.astype(F32)[:, None]).astype(F32)
+        v *= scale.astype(F32)[:, None]
     return v
 
 

@@ -48,6 +48,8 @@ struct Geo {
   int stage_k;   // X elements per stage (128 fp8 / 64 f16)
   int kc;        // stages per token row
   int n_passes;  // expand passes per K (or V) row; each pass = 64 output columns
+  bool tc;       // codes on tcgen05 (rank <= 32): A image in the tensor-core layout
+  int terms;     // e4m3 terms per A entry in the tcgen05 image (3 for fp8 X, 1 for f16 X)
   int64_t a_off, a_stage_bytes, a_bytes, bk_off, b_bytes, bv_off, total;
 };
 
@@ -72,8 +74,11 @@ inline bool make_geo(const dkv_exact_geometry &g, Geo &o) {
   o.rpad = rk > rv ? rk : rv;
   if (o.rpad < 16) o.rpad = 16;
   o.r16 = o.rpad / 16;
-  o.n1 = 2 * o.rpad;
-  o.srow = g.x_dtype == DKV_E4M3 ? 256 : 128;
+  o.tc = o.rpad <= 32;
+  o.terms = (o.tc && g.x_dtype == DKV_E4M3) ? 3 : 1;
+  o.n1 = 2 * o.rpad * o.terms;
+  // mma.sync image: f16 rows of one stage's k-range; tcgen05 image: 128-byte rows
+  o.srow = o.tc ? 128 : (g.x_dtype == DKV_E4M3 ? 256 : 128);
   o.stage_k = 128 / esz;
   o.kc = ceil_div(g.d_model, o.stage_k);
   if (o.hd >= 64) o.n_passes = o.n_kv * (o.hd / 64);
@@ -182,7 +187,8 @@ __global__ void __launch_bounds__(256) pack_kernel(const PackParams pp) {
   }
   mx = block_max(mx, red);
   int e = 0;
-  if (mx > 0.f) e = 14 - ilogbf(mx);
+  const int top = (is_a && g.tc && g.x_dtype == DKV_E4M3) ? 7 : 14;  // e4m3 max 448, f16 max 65504
+  if (mx > 0.f) e = top - ilogbf(mx);
   e = max(-120, min(120, e));
   const float sc = exp2i(e);
   if (threadIdx.x == 0) {
@@ -199,7 +205,61 @@ __global__ void __launch_bounds__(256) pack_kernel(const PackParams pp) {
     }
   }
   // 2. write the operand image
-  if (is_a) {
+  if (is_a && g.tc) {
+    // tcgen05 image: row ng = (K|V block) + term * rpad + n, 128 bytes per stage, the 16-byte
+    // unit u of row ng stored at u ^ (ng & 7) (the SWIZZLE_128B K-major layout).  fp8 X:
+    // three e4m3 terms with A*2^E ~= t0 + t1/16 + t2/256; f16 X: one f16 term.
+    const int64_t units = static_cast<int64_t>(g.kc) * g.rpad * 8;
+    const int vblk = is_k ? 0 : g.terms * g.rpad;
+    for (int64_t i = threadIdx.x; i < units; i += blockDim.x) {
+      const int kci = static_cast<int>(i / (g.rpad * 8));
+      const int rem = static_cast<int>(i % (g.rpad * 8));
+      const int n = rem >> 3, u = rem & 7;
+      if (g.x_dtype == DKV_E4M3) {
+        uint32_t w[3][4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          uint32_t b[3] = {0, 0, 0};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int k = kci * g.stage_k + 16 * u + 4 * jj + t;
+            float v = (present && n < rank && k < g.d_model) ? aval(n, k) * sc : 0.f;
+#pragma unroll
+            for (int term = 0; term < 3; ++term) {
+              const uint32_t q = f32_to_e4m3(v);
+              b[term] |= q << (8 * t);
+              v = (v - e4m3_to_f32(q)) * 16.f;
+            }
+          }
+#pragma unroll
+          for (int term = 0; term < 3; ++term) w[term][jj] = b[term];
+        }
+#pragma unroll
+        for (int term = 0; term < 3; ++term) {
+          const int ng = vblk + term * g.rpad + n;
+          uint8_t *dst = img + g.a_off + kci * g.a_stage_bytes + static_cast<int64_t>(ng) * 128 +
+                         ((u ^ (ng & 7)) << 4);
+          *reinterpret_cast<uint4 *>(dst) = make_uint4(w[term][0], w[term][1], w[term][2], w[term][3]);
+        }
+      } else {
+        uint32_t w[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          float v2[2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int k = kci * g.stage_k + 8 * u + 2 * jj + t;
+            v2[t] = (present && n < rank && k < g.d_model) ? aval(n, k) * sc : 0.f;
+          }
+          w[jj] = pack_f16x2(v2[0], v2[1]);
+        }
+        const int ng = vblk + n;
+        uint8_t *dst = img + g.a_off + kci * g.a_stage_bytes + static_cast<int64_t>(ng) * 128 +
+                       ((u ^ (ng & 7)) << 4);
+        *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  } else if (is_a) {
     const int upr = g.srow / 16;  // 16-byte units per row per stage
     const int64_t units = static_cast<int64_t>(g.kc) * g.rpad * upr;
     const int row_base = is_k ? 0 : g.rpad;
@@ -307,6 +367,7 @@ template <>
 struct Chunk<DKV_BF16> {
   uint4 v;
   __device__ __forceinline__ void load(const void *p) { v = ldg128_stream(p); }
+  __device__ __forceinline__ void lds(uint32_t a) { v = lds128(a); }
   __device__ __forceinline__ void store(void *p) const { stg128_stream(p, v); }
   __device__ __forceinline__ float get(int j) const {
     const uint32_t w = j < 2 ? v.x : j < 4 ? v.y : j < 6 ? v.z : v.w;
@@ -324,6 +385,7 @@ template <>
 struct Chunk<DKV_F16> {
   uint4 v;
   __device__ __forceinline__ void load(const void *p) { v = ldg128_stream(p); }
+  __device__ __forceinline__ void lds(uint32_t a) { v = lds128(a); }
   __device__ __forceinline__ void store(void *p) const { stg128_stream(p, v); }
   __device__ __forceinline__ float get(int j) const {
     const uint32_t w = j < 2 ? v.x : j < 4 ? v.y : j < 6 ? v.z : v.w;
@@ -343,6 +405,11 @@ struct Chunk<DKV_F32> {
   __device__ __forceinline__ void load(const void *p) {
     a = ldg128_stream(p);
     b = ldg128_stream(static_cast<const uint8_t *>(p) + 16);
+  }
+  // the two 16-byte halves of a chunk sit 32 lanes apart in the page ring
+  __device__ __forceinline__ void lds(uint32_t addr) {
+    a = lds128(addr);
+    b = lds128(addr + 32 * 16);
   }
   __device__ __forceinline__ void store(void *p) const {
     stg128_stream(p, a);
@@ -369,26 +436,89 @@ struct RowInfo {
   bool valid[2];
 };
 
-// One expand pass: 64 output columns of K or V for this warp's 16 rows.
+// ----------------------------------------------------------------------------
+// phase 2: expand passes with the page rows streamed through a per-warp cp.async ring
+// ----------------------------------------------------------------------------
+// Pass i of a tile covers 64 output columns of K (first n_passes passes) or V.  For
+// head_dim >= 64 passes are ordered by (rope frequency block ip, head) so the cos/sin of a
+// frequency block are loaded once per tile.
+struct PassDesc {
+  bool is_k, hok;
+  int pk, clo, chi, ip;
+};
+
+__device__ __forceinline__ PassDesc pass_desc(const Params &p, int i, int q) {
+  PassDesc d;
+  const int np = p.n_passes;
+  d.is_k = p.do_k && i < np;
+  const int j = (p.do_k && !d.is_k) ? i - np : i;
+  if (p.hd >= 64) {
+    const int per = p.hd / 64;
+    d.ip = j / p.n_kv;
+    const int h = j - d.ip * p.n_kv;
+    d.pk = h * per + d.ip;
+    d.clo = h * (p.hd / 8) + 4 * d.ip + q;
+    d.hok = true;
+  } else {
+    d.ip = 0;
+    d.pk = j;
+    d.clo = chunk_lo(j, q, p.hd);
+    d.hok = head_of(j, q, p.hd) < p.n_kv;
+  }
+  d.chi = d.clo + p.hd / 16;
+  return d;
+}
+
+template <int PDT>
+struct PageRing {
+  static constexpr int EB = Chunk<PDT>::kElemBytes;
+  static constexpr int NH = EB / 2;              // 16-byte pieces per 8-element chunk
+  static constexpr int kSlotBytes = 4 * NH * 32 * 16;
+  uint32_t base;  // this warp's ring in shared memory
+  int total, depth;
+
+  __device__ __forceinline__ uint32_t piece(int i, int rh, int half, int lane) const {
+    return base + (i % depth) * kSlotBytes + (((rh * NH + half) * 32 + lane) << 4);
+  }
+  // start the copies of pass i's page chunks (rows g, g+8; chunks lo, hi)
+  __device__ __forceinline__ void issue(const Params &p, const Tile &t, const RowInfo &ri, int i,
+                                        int lane) const {
+    if (i < total && p.accumulate) {
+      const PassDesc d = pass_desc(p, i, lane & 3);
+      if (d.hok) {
+        const uint8_t *pg = static_cast<const uint8_t *>(d.is_k ? p.k_base[t.layer] : p.v_base[t.layer]);
+        const int64_t shead = d.is_k ? p.k_shead : p.v_shead;
+        const int64_t e_lo = static_cast<int64_t>((8 * d.clo) / p.hd) * shead + (8 * d.clo) % p.hd;
+        const int64_t e_hi = static_cast<int64_t>((8 * d.chi) / p.hd) * shead + (8 * d.chi) % p.hd;
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          if (!ri.valid[r]) continue;
+          const int64_t off = d.is_k ? ri.off_k[r] : ri.off_v[r];
+#pragma unroll
+          for (int half = 0; half < NH; ++half) {
+            cp_async_16(piece(i, 2 * r, half, lane), pg + (off + e_lo) * EB + 16 * half);
+            cp_async_16(piece(i, 2 * r + 1, half, lane), pg + (off + e_hi) * EB + 16 * half);
+          }
+        }
+      }
+    }
+    cp_async_commit();
+  }
+};
+
+// Expand, RoPE, scale and write back one pass.  `pg` holds the current page chunks when
+// accumulating.
 template <int R16, int PDT>
 __device__ __forceinline__ void expand_pass(const uint4 *__restrict__ bfrag,
                                             const uint32_t (&cf)[R16][4], const float (&cs)[2][8],
                                             const float (&sn)[2][8], bool rope, int clo, int chi,
                                             int hd, uint8_t *base, const int64_t (&off)[2],
                                             int64_t shead, const float (&om)[2],
-                                            const bool (&valid)[2], bool accumulate, int lane) {
+                                            const bool (&valid)[2], bool accumulate, int lane,
+                                            Chunk<PDT> (&pg)[2][2]) {
   constexpr int EB = Chunk<PDT>::kElemBytes;
   const int64_t e_lo = static_cast<int64_t>((8 * clo) / hd) * shead + (8 * clo) % hd;
   const int64_t e_hi = static_cast<int64_t>((8 * chi) / hd) * shead + (8 * chi) % hd;
-  Chunk<PDT> pg[2][2];
-  if (accumulate) {
-#pragma unroll
-    for (int r = 0; r < 2; ++r)
-      if (valid[r]) {
-        pg[r][0].load(base + (off[r] + e_lo) * EB);
-        pg[r][1].load(base + (off[r] + e_hi) * EB);
-      }
-  }
   float acc[8][4];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
@@ -438,10 +568,11 @@ __device__ __forceinline__ void expand_pass(const uint4 *__restrict__ bfrag,
         o_hi[j] = hi[j] * m;
       }
     }
-    pg[r][0].set_all(o_lo);
-    pg[r][1].set_all(o_hi);
-    pg[r][0].store(base + (off[r] + e_lo) * EB);
-    pg[r][1].store(base + (off[r] + e_hi) * EB);
+    Chunk<PDT> w0, w1;
+    w0.set_all(o_lo);
+    w1.set_all(o_hi);
+    w0.store(base + (off[r] + e_lo) * EB);
+    w1.store(base + (off[r] + e_hi) * EB);
   }
 }
 
@@ -463,48 +594,104 @@ __device__ __forceinline__ void load_rope(const Params &p, const RowInfo &ri, in
   }
 }
 
-// Expand + RoPE + read-add-write for one projection (K when IS_K, else V).
-template <int R16, int PDT, bool IS_K>
-__device__ __forceinline__ void expand_projection(const Params &p, const Tile &t,
-                                                  const RowInfo &ri, const uint32_t (&cf)[R16][4],
-                                                  const float (&om)[2], int lane) {
+// All expand passes of one tile (K then V), consuming the page ring started by the caller
+// (passes 0..depth-1 already issued).
+template <int R16, int PDT, int DEPTH>
+__device__ __forceinline__ void phase2(const Params &p, const Tile &t, const RowInfo &ri,
+                                       const PageRing<PDT> &ring, const uint32_t (&ck)[R16][4],
+                                       const uint32_t (&cv)[R16][4], const float (&om_k)[2],
+                                       const float (&om_v)[2], int lane) {
   const uint8_t *img = p.packed + t.layer * p.packed_stride;
-  const uint4 *bf = reinterpret_cast<const uint4 *>(img + (IS_K ? p.bk_off : p.bv_off));
-  uint8_t *base = static_cast<uint8_t *>(IS_K ? p.k_base[t.layer] : p.v_base[t.layer]);
-  const int64_t shead = IS_K ? p.k_shead : p.v_shead;
-  const int64_t(&off)[2] = IS_K ? ri.off_k : ri.off_v;
-  const bool rope = IS_K && p.has_rope;
-  const int q = lane & 3, hd = p.hd;
+  const uint4 *bfk = reinterpret_cast<const uint4 *>(img + p.bk_off);
+  const uint4 *bfv = reinterpret_cast<const uint4 *>(img + p.bv_off);
+  const int q = lane & 3;
   const bool acc = p.accumulate != 0;
   float cs[2][8], sn[2][8];
-  if (hd >= 64) {
-    const int per = hd / 64;
-    for (int ip = 0; ip < per; ++ip) {
-      if (rope) load_rope<R16>(p, ri, 32 * ip + 8 * q, cs, sn);
-      for (int h = 0; h < p.n_kv; ++h) {
-        const int pass = h * per + ip;
-        const int clo = h * (hd / 8) + 4 * ip + q;
-        expand_pass<R16, PDT>(bf + pass * R16 * 4 * 32, cf, cs, sn, rope, clo, clo + hd / 16, hd,
-                              base, off, shead, om, ri.valid, acc, lane);
-      }
+  int cur_ip = -1;
+  for (int i = 0; i < ring.total; ++i) {
+    const PassDesc d = pass_desc(p, i, q);
+    const bool rope = d.is_k && p.has_rope;
+    if (rope && d.ip != cur_ip) {
+      const int f0 = p.hd >= 64 ? 32 * d.ip + 8 * q : (p.hd == 32 ? 8 * (q & 1) : 0);
+      load_rope<R16>(p, ri, f0, cs, sn);
+      cur_ip = d.ip;
     }
-  } else {
-    if (rope) load_rope<R16>(p, ri, hd == 32 ? 8 * (q & 1) : 0, cs, sn);
-    for (int pass = 0; pass < p.n_passes; ++pass) {
-      const bool head_ok = head_of(pass, q, hd) < p.n_kv;
-      const bool v2[2] = {ri.valid[0] && head_ok, ri.valid[1] && head_ok};
-      const int clo = chunk_lo(pass, q, hd);
-      // mma needs all lanes; invalid lanes skip only their memory traffic
-      expand_pass<R16, PDT>(bf + pass * R16 * 4 * 32, cf, cs, sn, rope, clo, clo + hd / 16, hd,
-                            base, off, shead, om, v2, acc, lane);
+    cp_async_wait<DEPTH - 1>();
+    Chunk<PDT> pg[2][2];
+    const bool v2[2] = {ri.valid[0] && d.hok, ri.valid[1] && d.hok};
+    if (acc) {
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+        if (v2[r]) {
+          pg[r][0].lds(ring.piece(i, 2 * r, 0, lane));
+          pg[r][1].lds(ring.piece(i, 2 * r + 1, 0, lane));
+        }
     }
+    if (d.is_k)
+      expand_pass<R16, PDT>(bfk + d.pk * R16 * 4 * 32, ck, cs, sn, rope, d.clo, d.chi, p.hd,
+                            static_cast<uint8_t *>(p.k_base[t.layer]), ri.off_k, p.k_shead, om_k, v2,
+                            acc, lane, pg);
+    else
+      expand_pass<R16, PDT>(bfv + d.pk * R16 * 4 * 32, cv, cs, sn, false, d.clo, d.chi, p.hd,
+                            static_cast<uint8_t *>(p.v_base[t.layer]), ri.off_v, p.v_shead, om_v, v2,
+                            acc, lane, pg);
+    // the chunks read from slot i have been consumed: refill it with the pass DEPTH ahead
+    ring.issue(p, t, ri, i + DEPTH, lane);
   }
+  cp_async_wait<0>();
+}
+
+// Validity, RoPE position and page offsets of rows g and g+8 of warp `warp` in tile t;
+// range errors are recorded in the status word and the row is skipped.
+__device__ __forceinline__ RowInfo make_row_info(const Params &p, const Tile &t, int warp, int g) {
+  RowInfo ri;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int tok = t.c0 + 16 * warp + g + 8 * r;
+    const int64_t grow = static_cast<int64_t>(t.row0 - t.c0) + tok;
+    bool v = tok < t.len;
+    if (v && grow >= p.x_rows) {
+      record_error(p.status, DKV_ERR_INVALID_ARGUMENT);
+      v = false;
+    }
+    int pos = tok;
+    ri.off_k[r] = ri.off_v[r] = 0;
+    ri.xs[r] = 1.f;
+    if (v) {
+      if (p.positions) pos = __ldg(p.positions + grow);
+      if (p.has_rope && (pos < 0 || pos >= p.rope_max_pos)) {
+        record_error(p.status, DKV_ERR_ROPE_RANGE);
+        v = false;
+      }
+      const int bi = tok / p.block_size;
+      const int64_t tlen = p.table_lens ? __ldg(p.table_lens + t.seq) : p.table_stride;
+      if (v && bi >= tlen) {
+        record_error(p.status, DKV_ERR_BLOCK_TABLE_SHORT);
+        v = false;
+      }
+      if (v) {
+        const int bid = __ldg(p.block_tables + static_cast<int64_t>(t.seq) * p.table_stride + bi);
+        if (bid < 0 || bid >= p.k_nblocks || bid >= p.v_nblocks) {
+          record_error(p.status, DKV_ERR_PAGE_RANGE);
+          v = false;
+        } else {
+          const int slot = tok % p.block_size;
+          ri.off_k[r] = static_cast<int64_t>(bid) * p.k_sblock + static_cast<int64_t>(slot) * p.k_sslot;
+          ri.off_v[r] = static_cast<int64_t>(bid) * p.v_sblock + static_cast<int64_t>(slot) * p.v_sslot;
+        }
+      }
+      if (p.x_scale) ri.xs[r] = __ldg(p.x_scale + t.layer * p.xs_stride + grow);
+    }
+    ri.valid[r] = v;
+    ri.pos[r] = pos;
+  }
+  return ri;
 }
 
 // TMA producer run by one thread: walks the same (tile, k-slab) sequence the warps consume
 // and keeps every ring slot filled.  The X slab comes by a 3-D tensor copy (128-B swizzle),
 // the matching packed-A slab by a contiguous bulk copy; both complete on full[stage].
-template <int A_STAGE>
+template <int A_STAGE, int STAGES = kStages>
 struct Producer {
   int64_t tile;
   int kc, layer, row0, stage;
@@ -543,7 +730,7 @@ struct Producer {
     issued |= 1u << stage;
     parity = (parity & ~(1u << stage)) | (phase << stage);
     ++kc;
-    if (++stage == kStages) {
+    if (++stage == STAGES) {
       stage = 0;
       phase ^= 1;
     }
@@ -551,7 +738,7 @@ struct Producer {
   }
   // never let the CTA exit with a copy still landing in its shared memory
   __device__ void drain(const Params &p, uint64_t *full) const {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < STAGES; ++s) {
       if (!(issued & (1u << s))) continue;
       const long long t0 = clock64();
       while (!mbar_try_wait(&full[s], (parity >> s) & 1)) {
@@ -564,6 +751,15 @@ struct Producer {
   }
 };
 
+// Depth of the per-warp page ring: as deep as shared memory allows next to the X / A ring.
+template <int R16, int PDT>
+struct RingDepth {
+  static constexpr int slot = PageRing<PDT>::kSlotBytes;
+  static constexpr int value = (R16 <= 2) ? (PDT == DKV_F32 ? 2 : 4)
+                               : (R16 == 3) ? (PDT == DKV_F32 ? 2 : 4)
+                                            : (PDT == DKV_F32 ? 1 : 2);
+};
+
 template <int XT, int R16, bool NORM, int PDT>
 __global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constant__ Params p) {
   constexpr int NT1 = 4 * R16;  // phase-1 n-tiles: K codes then V codes, 8 columns each
@@ -573,7 +769,10 @@ __global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constan
   uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t *sx = smem;                          // [kStages][128 rows][128 B], 128-B swizzled
   uint8_t *sa = smem + kStages * kXStageBytes;  // [kStages][n1 rows][SROW]
-  uint64_t *full = reinterpret_cast<uint64_t *>(sa + kStages * A_STAGE);
+  constexpr int DEPTH = RingDepth<R16, PDT>::value;
+  constexpr int RING_BYTES = DEPTH * PageRing<PDT>::kSlotBytes;
+  uint8_t *sp = sa + kStages * A_STAGE;  // [warps][DEPTH] page-chunk slots
+  uint64_t *full = reinterpret_cast<uint64_t *>(sp + kConsumerWarps * RING_BYTES);
   uint64_t *empty = full + kStages;
   volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStages);
 
@@ -614,53 +813,17 @@ __global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constan
   const int xrow = 16 * warp + (lane & 7) + ((mat & 1) << 3);
   const int xsw = xrow & 7;
   const int bsw = (g & 1) << 2;
+  PageRing<PDT> ring;
+  ring.base = smem_u32(sp) + warp * RING_BYTES;
+  ring.depth = DEPTH;
+  ring.total = (p.do_k ? p.n_passes : 0) + (p.do_v ? p.n_passes : 0);
 
   for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
     Tile t;
     if (!decode_tile(p, tile, t)) continue;
 
     // ---- per-row metadata (rows g and g+8 of this warp) ----
-    RowInfo ri;
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int tok = t.c0 + 16 * warp + g + 8 * r;
-      const int64_t grow = static_cast<int64_t>(t.row0 - t.c0) + tok;
-      bool v = tok < t.len;
-      if (v && grow >= p.x_rows) {
-        record_error(p.status, DKV_ERR_INVALID_ARGUMENT);
-        v = false;
-      }
-      int pos = tok;
-      ri.off_k[r] = ri.off_v[r] = 0;
-      ri.xs[r] = 1.f;
-      if (v) {
-        if (p.positions) pos = __ldg(p.positions + grow);
-        if (p.has_rope && (pos < 0 || pos >= p.rope_max_pos)) {
-          record_error(p.status, DKV_ERR_ROPE_RANGE);
-          v = false;
-        }
-        const int bi = tok / p.block_size;
-        const int64_t tlen = p.table_lens ? __ldg(p.table_lens + t.seq) : p.table_stride;
-        if (v && bi >= tlen) {
-          record_error(p.status, DKV_ERR_BLOCK_TABLE_SHORT);
-          v = false;
-        }
-        if (v) {
-          const int bid = __ldg(p.block_tables + static_cast<int64_t>(t.seq) * p.table_stride + bi);
-          if (bid < 0 || bid >= p.k_nblocks || bid >= p.v_nblocks) {
-            record_error(p.status, DKV_ERR_PAGE_RANGE);
-            v = false;
-          } else {
-            const int slot = tok % p.block_size;
-            ri.off_k[r] = static_cast<int64_t>(bid) * p.k_sblock + static_cast<int64_t>(slot) * p.k_sslot;
-            ri.off_v[r] = static_cast<int64_t>(bid) * p.v_sblock + static_cast<int64_t>(slot) * p.v_sslot;
-          }
-        }
-        if (p.x_scale) ri.xs[r] = __ldg(p.x_scale + t.layer * p.xs_stride + grow);
-      }
-      ri.valid[r] = v;
-      ri.pos[r] = pos;
-    }
+    const RowInfo ri = make_row_info(p, t, warp, g);
 
     // ---- phase 1: codes = x . A^T (and sum x^2) over the streamed stages ----
     float acc[NT1][4];
@@ -698,9 +861,14 @@ __global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constan
           }
         }
       }
+      if (kc == p.kc - 1) {
+        // start streaming the first page chunks of phase 2 under the last X slab
+        for (int i = 0; i < DEPTH; ++i) ring.issue(p, t, ri, i, lane);
+      }
       if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) {
         record_error(p.status, DKV_ERR_TIMEOUT);
         *abort_flag = 1;
+        cp_async_wait<0>();
         if (is_prod) prod.drain(p, full);
         return;
       }
@@ -838,10 +1006,314 @@ __global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constan
     }
 
     // ---- phase 2: dK / dV, RoPE, page read-add-write ----
-    if (p.do_k) expand_projection<R16, PDT, true>(p, t, ri, ck, om_k, lane);
-    if (p.do_v) expand_projection<R16, PDT, false>(p, t, ri, cv, om_v, lane);
+    phase2<R16, PDT, DEPTH>(p, t, ri, ring, ck, cv, om_k, om_v, lane);
   }
   if (is_prod) prod.drain(p, full);
+}
+
+// ----------------------------------------------------------------------------
+// tcgen05 variant (rank <= 32): codes on the 5th-generation tensor cores
+// ----------------------------------------------------------------------------
+// Warp roles (12 warps):
+//   0-7  epilogue: per tile, read the codes out of tensor memory (warps 0-3, one TMEM lane
+//        quarter each), then all 8 run phase 2 exactly as the mma.sync kernel does;
+//   8    TMA producer (lane 0): X slab + packed-A slab per stage, STAGES-deep ring;
+//   9    MMA issuer (lane 0) and owner of the 512-column TMEM allocation;
+//   10,11 spare.
+// Per stage the issuer runs K=32 tcgen05.mma steps for codes (M=128 tokens, N = codes
+// columns, e4m3 x e4m3 or f16 x f16 -> fp32 in TMEM) and, with RMSNorm, for X.X^T whose
+// diagonal is sum(x^2).  Accumulators are double-buffered across tiles when they fit, so
+// the tensor cores and the X stream work on tile i+1 while the epilogue patches tile i.
+constexpr int kTcWarps = 12;
+constexpr int kTcThreads = kTcWarps * 32;
+constexpr int kEpiWarps = 8;
+
+template <int XT, int R16, bool NORM>
+struct TcCfg {
+  static constexpr int RPAD = 16 * R16;
+  static constexpr int TERMS = XT == 0 ? 3 : 1;
+  static constexpr int N1 = TERMS * 2 * RPAD;  // codes columns: K terms, then V terms
+  static constexpr int STAGES = R16 == 1 ? 4 : 3;
+  static constexpr int A_STAGE = N1 * 128;
+  static constexpr int DIAG = N1 <= 128 ? 128 : 256;  // column of the X.X^T accumulator
+  static constexpr int BUF = NORM ? DIAG + 128 : (N1 <= 128 ? 128 : 256);
+  static constexpr int NBUF = BUF <= 256 ? 2 : 1;
+  static constexpr int CROW = 4 * RPAD + 16;  // bytes per row of the f16 codes tile in smem
+  static constexpr uint32_t IDESC_CODES = umma_idesc(0, 128, N1);
+  static constexpr uint32_t IDESC_DIAG = umma_idesc(0, 128, 128);
+};
+
+template <int XT, int R16, bool NORM, int PDT>
+struct TcSmem {
+  using C = TcCfg<XT, R16, NORM>;
+  static constexpr int DEPTH = RingDepth<R16, PDT>::value;
+  static constexpr int RING = DEPTH * PageRing<PDT>::kSlotBytes;
+  static constexpr int X_OFF = 0;
+  static constexpr int A_OFF = X_OFF + C::STAGES * kXStageBytes;
+  static constexpr int P_OFF = A_OFF + C::STAGES * C::A_STAGE;
+  static constexpr int CODES_OFF = P_OFF + kEpiWarps * RING;
+  static constexpr int OM_OFF = CODES_OFF + 2 * 128 * C::CROW;
+  static constexpr int BAR_OFF = OM_OFF + 2 * 2 * 128 * 4;
+  static constexpr int N_BARS = 2 * C::STAGES + 4 + 1;
+  static constexpr int MISC_OFF = BAR_OFF + N_BARS * 8;
+  static constexpr int BYTES = MISC_OFF + 16;
+};
+
+template <int XT, int R16, bool NORM>
+__device__ __forceinline__ void issue_stage_mmas(uint32_t d_codes, uint32_t d_diag, uint32_t xs,
+                                                 uint32_t as, bool first) {
+  using C = TcCfg<XT, R16, NORM>;
+  const uint64_t adesc = umma_desc_k_sw128(xs);
+  const uint64_t bdesc = umma_desc_k_sw128(as);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {  // 4 x 32 bytes of K per 128-byte swizzled row
+    const uint32_t acc = (first && kk == 0) ? 0u : 1u;
+    const uint64_t a = adesc + static_cast<uint64_t>(2 * kk), b = bdesc + static_cast<uint64_t>(2 * kk);
+    if (XT == 0) {
+      umma_e4m3(d_codes, a, b, C::IDESC_CODES, acc);
+      if (NORM) umma_e4m3(d_diag, a, a, C::IDESC_DIAG, acc);
+    } else {
+      umma_f16(d_codes, a, b, C::IDESC_CODES, acc);
+      if (NORM) umma_f16(d_diag, a, a, C::IDESC_DIAG, acc);
+    }
+  }
+}
+
+template <int XT, int R16, bool NORM, int PDT>
+__global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_constant__ Params p) {
+  using C = TcCfg<XT, R16, NORM>;
+  using S = TcSmem<XT, R16, NORM, PDT>;
+  constexpr int RPAD = C::RPAD, STAGES = C::STAGES, NBUF = C::NBUF, DEPTH = S::DEPTH;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t *sx = smem + S::X_OFF;
+  uint8_t *sa = smem + S::A_OFF;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::BAR_OFF);
+  uint64_t *empty = full + STAGES;
+  uint64_t *tfull = empty + STAGES;  // [2]
+  uint64_t *tempty = tfull + 2;      // [2]
+  uint64_t *done = tempty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + S::MISC_OFF);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + S::MISC_OFF + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+
+  if (warp == 8) {
+    // ------------------------------ TMA producer ------------------------------
+    if (lane == 0) {
+      prefetch_tensormap(&p.x_map);
+      Producer<C::A_STAGE, STAGES> prod;
+      prod.init(p);
+      for (;;) {
+        const int r = prod.issue(p, sx, sa, full, empty, abort_flag);
+        if (r < 0) {
+          record_error(p.status, DKV_ERR_TIMEOUT);
+          *abort_flag = 1;
+        }
+        if (r <= 0) break;
+      }
+      prod.drain(p, full);
+    }
+  } else if (warp == 9) {
+    // ------------------------------- MMA issuer -------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t j = 0;  // tiles done by this CTA
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
+        Tile t;
+        if (!decode_tile(p, tile, t)) continue;
+        const int b = static_cast<int>(j % NBUF);
+        const int64_t use = j / NBUF;
+        if (use > 0 && !mbar_wait_bounded(&tempty[b], static_cast<uint32_t>((use - 1) & 1), abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_codes = tmem + b * C::BUF;
+        const uint32_t d_diag = d_codes + C::DIAG;
+        for (int kc = 0; kc < p.kc; ++kc) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_stage_mmas<XT, R16, NORM>(d_codes, d_diag, smem_u32(sx + stage * kXStageBytes),
+                                          smem_u32(sa + stage * C::A_STAGE), kc == 0);
+          umma_commit(&empty[stage]);  // the slot is free once these MMAs have read it
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[b]);
+        ++j;
+      }
+      if (!ok) {
+        record_error(p.status, DKV_ERR_TIMEOUT);
+        *abort_flag = 1;
+      }
+      umma_commit(done);
+    }
+  } else if (warp < kEpiWarps) {
+    // -------------------------------- epilogue --------------------------------
+    const int g = lane >> 2;
+    uint8_t *codes_base = smem + S::CODES_OFF;
+    float *om_base = reinterpret_cast<float *>(smem + S::OM_OFF);
+    PageRing<PDT> ring;
+    ring.base = smem_u32(smem + S::P_OFF) + warp * S::RING;
+    ring.depth = DEPTH;
+    ring.total = (p.do_k ? p.n_passes : 0) + (p.do_v ? p.n_passes : 0);
+    int64_t j = 0;
+    for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
+      Tile t;
+      if (!decode_tile(p, tile, t)) continue;
+      const int b = static_cast<int>(j % NBUF);
+      const int64_t use = j / NBUF;
+      const int par = static_cast<int>(j & 1);
+      const RowInfo ri = make_row_info(p, t, warp, g);
+      for (int i = 0; i < DEPTH; ++i) ring.issue(p, t, ri, i, lane);  // page chunks of phase 2
+
+      uint8_t *codes = codes_base + par * 128 * C::CROW;
+      float *om = om_base + par * 2 * 128;
+      // after an abort the warps keep walking the tile sequence (same barriers) without work
+      // (decisions are made warp-uniform: TMEM loads and mma.sync need every lane)
+      bool have_codes = __all_sync(0xffffffffu, *abort_flag == 0);
+      if (warp < 4 && have_codes) {
+        // codes of row 32*warp + lane out of TMEM: combine terms, scale, f16 with a per-row exponent
+        const bool ok = mbar_wait_bounded(&tfull[b], static_cast<uint32_t>(use & 1), abort_flag);
+        have_codes = __all_sync(0xffffffffu, ok);
+        if (!have_codes) {
+          record_error(p.status, DKV_ERR_TIMEOUT);
+          *abort_flag = 1;
+        }
+      }
+      if (warp < 4 && have_codes) {
+        tc_fence_after();
+        const int row = 32 * warp + lane;
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * warp) << 16) + b * C::BUF;
+        const int tok = t.c0 + row;
+        const int64_t grow = static_cast<int64_t>(t.row0) + row;
+        float xs = 1.f;
+        if (p.x_scale && tok < t.len && grow < p.x_rows) xs = __ldg(p.x_scale + t.layer * p.xs_stride + grow);
+        float rs = xs;
+        if (NORM) {
+          float dv[16];
+          float ss = 0.f;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            tmem_ld16(taddr + C::DIAG + 32 * warp + 16 * h, dv);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ss = (16 * h + i == lane) ? dv[i] : ss;
+          }
+          rs = xs * rsqrtf(xs * xs * ss * p.inv_d + p.norm_eps);
+        }
+        const float *hdr = reinterpret_cast<const float *>(p.packed + t.layer * p.packed_stride);
+#pragma unroll
+        for (int kv = 0; kv < 2; ++kv) {
+          float c[RPAD];
+#pragma unroll
+          for (int h = 0; h < R16; ++h) {
+            float v[16];
+            tmem_ld16(taddr + kv * C::TERMS * RPAD + 16 * h, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) c[16 * h + i] = v[i];
+            if (C::TERMS == 3) {
+              tmem_ld16(taddr + kv * C::TERMS * RPAD + RPAD + 16 * h, v);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) c[16 * h + i] = fmaf(v[i], 0.0625f, c[16 * h + i]);
+              tmem_ld16(taddr + kv * C::TERMS * RPAD + 2 * RPAD + 16 * h, v);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) c[16 * h + i] = fmaf(v[i], 0.00390625f, c[16 * h + i]);
+            }
+          }
+          const float cm = hdr[kv] * rs;
+          float m = 0.f;
+#pragma unroll
+          for (int i = 0; i < RPAD; ++i) {
+            c[i] *= cm;
+            m = fmaxf(m, fabsf(c[i]));
+          }
+          int e = (m > 0.f && isfinite(m)) ? 14 - ilogbf(m) : 0;
+          e = max(-120, min(120, e));
+          const float e2 = exp2i(e);
+          uint32_t w[RPAD / 2];
+#pragma unroll
+          for (int i = 0; i < RPAD / 2; ++i) w[i] = pack_f16x2(c[2 * i] * e2, c[2 * i + 1] * e2);
+          uint4 *dst = reinterpret_cast<uint4 *>(codes + row * C::CROW + kv * RPAD * 2);
+#pragma unroll
+          for (int i = 0; i < RPAD / 8; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          om[kv * 128 + row] = hdr[2 + kv] * exp2i(-e);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[b]);
+      }
+      // every epilogue warp reaches this barrier, also after a timeout, then all leave together
+      named_barrier_sync(1, kEpiWarps * 32);
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) continue;
+      // A fragments of this warp's 16 rows, K and V codes
+      uint32_t ck[R16][4], cv[R16][4];
+      {
+        const int frow = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const uint32_t fbase = smem_u32(codes) + frow * C::CROW + (lane >> 4) * 16;
+#pragma unroll
+        for (int ks = 0; ks < R16; ++ks) {
+          ldmatrix_x4(ck[ks][0], ck[ks][1], ck[ks][2], ck[ks][3], fbase + ks * 32);
+          ldmatrix_x4(cv[ks][0], cv[ks][1], cv[ks][2], cv[ks][3], fbase + RPAD * 2 + ks * 32);
+        }
+      }
+      const float om_k[2] = {om[16 * warp + g], om[16 * warp + g + 8]};
+      const float om_v[2] = {om[128 + 16 * warp + g], om[128 + 16 * warp + g + 8]};
+      phase2<R16, PDT, DEPTH>(p, t, ri, ring, ck, cv, om_k, om_v, lane);
+      ++j;
+    }
+    cp_async_wait<0>();
+  }
+
+  // ------------------------------- teardown -------------------------------
+  __syncthreads();
+  if (warp == 9) {
+    if (lane == 0) {
+      const long long t0 = clock64();
+      while (!mbar_try_wait(done, 0)) {
+        if (clock64() - t0 > kWaitLimitCycles) {
+          record_error(p.status, DKV_ERR_TIMEOUT);
+          break;
+        }
+      }
+    }
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
 }
 
 // ----------------------------------------------------------------------------
@@ -861,10 +1333,28 @@ PFN_cuTensorMapEncodeTiled_v12000 tensormap_encoder() {
 }
 
 template <int XT, int R16, bool NORM, int PDT>
+int launch_tc(const Params &p, cudaStream_t st, int grid) {
+  using S = TcSmem<XT, R16, NORM, PDT>;
+  const size_t smem = 1024 + S::BYTES;
+  auto kern = patch_kernel_tc<XT, R16, NORM, PDT>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(smem)));
+    attr_set = true;
+  }
+  kern<<<grid, kTcThreads, smem, st>>>(p);
+  DKV_CUDA_CHECK(cudaGetLastError());
+  return DKV_OK;
+}
+
+template <int XT, int R16, bool NORM, int PDT>
 int launch_t(const Params &p, cudaStream_t st, int grid) {
   constexpr int SROW = XT == 0 ? 256 : 128;
   constexpr int A_STAGE = 2 * 16 * R16 * SROW;
-  const size_t smem = 1024 + kStages * (kXStageBytes + A_STAGE) + 2 * kStages * 8 + 16;
+  constexpr int RING_BYTES = RingDepth<R16, PDT>::value * PageRing<PDT>::kSlotBytes;
+  const size_t smem = 1024 + kStages * (kXStageBytes + A_STAGE) + kConsumerWarps * RING_BYTES +
+                      2 * kStages * 8 + 16;
   auto kern = patch_kernel<XT, R16, NORM, PDT>;
   DKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(smem)));
@@ -875,6 +1365,15 @@ int launch_t(const Params &p, cudaStream_t st, int grid) {
 
 template <int XT, int R16, bool NORM>
 int launch_p(const Params &p, int pdt, cudaStream_t st, int grid) {
+  if (R16 <= 2) {
+    constexpr int RT = R16 <= 2 ? R16 : 2;
+    switch (pdt) {
+      case DKV_BF16: return launch_tc<XT, RT, NORM, DKV_BF16>(p, st, grid);
+      case DKV_F16: return launch_tc<XT, RT, NORM, DKV_F16>(p, st, grid);
+      case DKV_F32: return launch_tc<XT, RT, NORM, DKV_F32>(p, st, grid);
+      default: return DKV_ERR_UNSUPPORTED;
+    }
+  }
   switch (pdt) {
     case DKV_BF16: return launch_t<XT, R16, NORM, DKV_BF16>(p, st, grid);
     case DKV_F16: return launch_t<XT, R16, NORM, DKV_F16>(p, st, grid);

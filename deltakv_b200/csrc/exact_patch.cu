@@ -335,6 +335,8 @@ struct alignas(64) Params {
   const int32_t *cu_seqlens, *block_tables, *table_lens, *positions;
   int64_t table_stride;
   int32_t n_seqs, max_chunks, block_size, prefetch_lead;
+  int32_t nip, nh;  // expand passes = nip frequency blocks x nh heads (or head groups)
+  int32_t k_shead_i, v_shead_i;  // head strides as 32-bit ints (row offsets stay below 2^31)
   int64_t k_sblock, k_sslot, k_shead, k_nblocks;
   int64_t v_sblock, v_sslot, v_shead, v_nblocks;
   int32_t *status;
@@ -439,34 +441,70 @@ struct RowInfo {
 // ----------------------------------------------------------------------------
 // phase 2: expand passes with the page rows streamed through a per-warp cp.async ring
 // ----------------------------------------------------------------------------
-// Pass i of a tile covers 64 output columns of K (first n_passes passes) or V.  For
-// head_dim >= 64 passes are ordered by (rope frequency block ip, head) so the cos/sin of a
-// frequency block are loaded once per tile.
-struct PassDesc {
-  bool is_k, hok;
-  int pk, clo, chi, ip;
+// A tile's expand passes, in order: K then V; within a projection, frequency block ip
+// (head_dim >= 64) outer and head h inner, so a tile loads each cos/sin block once.  The
+// cursor advances without divisions; chunk offsets are closed forms of (ip, h, q).
+struct Cursor {
+  int kv, ip, h;  // kv: 0 = K, 1 = V, 2 = past the end
+  __device__ __forceinline__ void begin(const Params &p) {
+    kv = p.do_k ? 0 : (p.do_v ? 1 : 2);
+    ip = h = 0;
+  }
+  __device__ __forceinline__ void next(const Params &p) {
+    if (++h == p.nh) {
+      h = 0;
+      if (++ip == p.nip) {
+        ip = 0;
+        kv = (kv == 0 && p.do_v) ? 1 : 2;
+      }
+    }
+  }
 };
 
-__device__ __forceinline__ PassDesc pass_desc(const Params &p, int i, int q) {
-  PassDesc d;
-  const int np = p.n_passes;
-  d.is_k = p.do_k && i < np;
-  const int j = (p.do_k && !d.is_k) ? i - np : i;
+struct Chunks {
+  int e_lo, e_hi;  // element offsets of this lane's two 8-column chunks inside a page row
+  int pk;          // B-fragment block of the pass in the packed image
+  bool hok;        // this lane's head exists
+};
+
+__device__ __forceinline__ Chunks chunks_of(const Params &p, const Cursor &c, int q, int shead) {
+  Chunks o;
   if (p.hd >= 64) {
-    const int per = p.hd / 64;
-    d.ip = j / p.n_kv;
-    const int h = j - d.ip * p.n_kv;
-    d.pk = h * per + d.ip;
-    d.clo = h * (p.hd / 8) + 4 * d.ip + q;
-    d.hok = true;
-  } else {
-    d.ip = 0;
-    d.pk = j;
-    d.clo = chunk_lo(j, q, p.hd);
-    d.hok = head_of(j, q, p.hd) < p.n_kv;
+    o.e_lo = c.h * shead + 32 * c.ip + 8 * q;
+    o.e_hi = o.e_lo + (p.hd >> 1);
+    o.pk = c.h * p.nip + c.ip;
+    o.hok = true;
+  } else if (p.hd == 32) {
+    const int head = 2 * c.h + (q >> 1);
+    o.e_lo = head * shead + 8 * (q & 1);
+    o.e_hi = o.e_lo + 16;
+    o.pk = c.h;
+    o.hok = head < p.n_kv;
+  } else {  // 16
+    const int head = 4 * c.h + q;
+    o.e_lo = head * shead;
+    o.e_hi = o.e_lo + 8;
+    o.pk = c.h;
+    o.hok = head < p.n_kv;
   }
-  d.chi = d.clo + p.hd / 16;
-  return d;
+  return o;
+}
+
+// Row pointers of this lane's two rows in the layer's K and V pages (or null when invalid).
+struct RowPtrs {
+  uint8_t *k[2], *v[2];
+};
+
+template <int PDT>
+__device__ __forceinline__ RowPtrs row_ptrs(const Params &p, const Tile &t, const RowInfo &ri) {
+  constexpr int EB = Chunk<PDT>::kElemBytes;
+  RowPtrs rp;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    rp.k[r] = ri.valid[r] ? static_cast<uint8_t *>(p.k_base[t.layer]) + ri.off_k[r] * EB : nullptr;
+    rp.v[r] = ri.valid[r] ? static_cast<uint8_t *>(p.v_base[t.layer]) + ri.off_v[r] * EB : nullptr;
+  }
+  return rp;
 }
 
 template <int PDT>
@@ -475,34 +513,37 @@ struct PageRing {
   static constexpr int NH = EB / 2;              // 16-byte pieces per 8-element chunk
   static constexpr int kSlotBytes = 4 * NH * 32 * 16;
   uint32_t base;  // this warp's ring in shared memory
-  int total, depth;
+  int depth;
+  Cursor cur;     // next pass to issue
+  int slot;
 
-  __device__ __forceinline__ uint32_t piece(int i, int rh, int half, int lane) const {
-    return base + (i % depth) * kSlotBytes + (((rh * NH + half) * 32 + lane) << 4);
+  __device__ __forceinline__ uint32_t piece(int s, int rh, int half, int lane) const {
+    return base + s * kSlotBytes + (((rh * NH + half) * 32 + lane) << 4);
   }
-  // start the copies of pass i's page chunks (rows g, g+8; chunks lo, hi)
-  __device__ __forceinline__ void issue(const Params &p, const Tile &t, const RowInfo &ri, int i,
-                                        int lane) const {
-    if (i < total && p.accumulate) {
-      const PassDesc d = pass_desc(p, i, lane & 3);
-      if (d.hok) {
-        const uint8_t *pg = static_cast<const uint8_t *>(d.is_k ? p.k_base[t.layer] : p.v_base[t.layer]);
-        const int64_t shead = d.is_k ? p.k_shead : p.v_shead;
-        const int64_t e_lo = static_cast<int64_t>((8 * d.clo) / p.hd) * shead + (8 * d.clo) % p.hd;
-        const int64_t e_hi = static_cast<int64_t>((8 * d.chi) / p.hd) * shead + (8 * d.chi) % p.hd;
+  __device__ __forceinline__ void begin(const Params &p) {
+    cur.begin(p);
+    slot = 0;
+  }
+  // start the copies of the next pass's page chunks (rows g, g+8; chunks lo, hi)
+  __device__ __forceinline__ void issue(const Params &p, const RowPtrs &rp, int lane) {
+    if (cur.kv < 2 && p.accumulate) {
+      const Chunks c = chunks_of(p, cur, lane & 3, cur.kv == 0 ? p.k_shead_i : p.v_shead_i);
+      if (c.hok) {
 #pragma unroll
         for (int r = 0; r < 2; ++r) {
-          if (!ri.valid[r]) continue;
-          const int64_t off = d.is_k ? ri.off_k[r] : ri.off_v[r];
+          const uint8_t *row = cur.kv == 0 ? rp.k[r] : rp.v[r];
+          if (row == nullptr) continue;
 #pragma unroll
           for (int half = 0; half < NH; ++half) {
-            cp_async_16(piece(i, 2 * r, half, lane), pg + (off + e_lo) * EB + 16 * half);
-            cp_async_16(piece(i, 2 * r + 1, half, lane), pg + (off + e_hi) * EB + 16 * half);
+            cp_async_16(piece(slot, 2 * r, half, lane), row + c.e_lo * EB + 16 * half);
+            cp_async_16(piece(slot, 2 * r + 1, half, lane), row + c.e_hi * EB + 16 * half);
           }
         }
       }
     }
     cp_async_commit();
+    if (cur.kv < 2) cur.next(p);
+    if (++slot == depth) slot = 0;
   }
 };
 
@@ -511,14 +552,11 @@ struct PageRing {
 template <int R16, int PDT>
 __device__ __forceinline__ void expand_pass(const uint4 *__restrict__ bfrag,
                                             const uint32_t (&cf)[R16][4], const float (&cs)[2][8],
-                                            const float (&sn)[2][8], bool rope, int clo, int chi,
-                                            int hd, uint8_t *base, const int64_t (&off)[2],
-                                            int64_t shead, const float (&om)[2],
+                                            const float (&sn)[2][8], bool rope, int e_lo, int e_hi,
+                                            uint8_t *const (&rows)[2], const float (&om)[2],
                                             const bool (&valid)[2], bool accumulate, int lane,
                                             Chunk<PDT> (&pg)[2][2]) {
   constexpr int EB = Chunk<PDT>::kElemBytes;
-  const int64_t e_lo = static_cast<int64_t>((8 * clo) / hd) * shead + (8 * clo) % hd;
-  const int64_t e_hi = static_cast<int64_t>((8 * chi) / hd) * shead + (8 * chi) % hd;
   float acc[8][4];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
@@ -571,8 +609,8 @@ __device__ __forceinline__ void expand_pass(const uint4 *__restrict__ bfrag,
     Chunk<PDT> w0, w1;
     w0.set_all(o_lo);
     w1.set_all(o_hi);
-    w0.store(base + (off[r] + e_lo) * EB);
-    w1.store(base + (off[r] + e_hi) * EB);
+    w0.store(rows[r] + e_lo * EB);
+    w1.store(rows[r] + e_hi * EB);
   }
 }
 
@@ -594,13 +632,13 @@ __device__ __forceinline__ void load_rope(const Params &p, const RowInfo &ri, in
   }
 }
 
-// All expand passes of one tile (K then V), consuming the page ring started by the caller
-// (passes 0..depth-1 already issued).
+// All expand passes of one tile (K then V), consuming the page ring whose first `depth`
+// passes the caller has already issued.
 template <int R16, int PDT, int DEPTH>
 __device__ __forceinline__ void phase2(const Params &p, const Tile &t, const RowInfo &ri,
-                                       const PageRing<PDT> &ring, const uint32_t (&ck)[R16][4],
-                                       const uint32_t (&cv)[R16][4], const float (&om_k)[2],
-                                       const float (&om_v)[2], int lane) {
+                                       const RowPtrs &rp, PageRing<PDT> &ring,
+                                       const uint32_t (&ck)[R16][4], const uint32_t (&cv)[R16][4],
+                                       const float (&om_k)[2], const float (&om_v)[2], int lane) {
   const uint8_t *img = p.packed + t.layer * p.packed_stride;
   const uint4 *bfk = reinterpret_cast<const uint4 *>(img + p.bk_off);
   const uint4 *bfv = reinterpret_cast<const uint4 *>(img + p.bv_off);
@@ -608,35 +646,47 @@ __device__ __forceinline__ void phase2(const Params &p, const Tile &t, const Row
   const bool acc = p.accumulate != 0;
   float cs[2][8], sn[2][8];
   int cur_ip = -1;
-  for (int i = 0; i < ring.total; ++i) {
-    const PassDesc d = pass_desc(p, i, q);
-    const bool rope = d.is_k && p.has_rope;
-    if (rope && d.ip != cur_ip) {
-      const int f0 = p.hd >= 64 ? 32 * d.ip + 8 * q : (p.hd == 32 ? 8 * (q & 1) : 0);
+  Cursor c;
+  c.begin(p);
+  int slot = 0;
+  while (c.kv < 2) {
+    const bool is_k = c.kv == 0;
+    const Chunks ch = chunks_of(p, c, q, is_k ? p.k_shead_i : p.v_shead_i);
+    const bool rope = is_k && p.has_rope;
+    if (rope && c.ip != cur_ip) {
+      const int f0 = p.hd >= 64 ? 32 * c.ip + 8 * q : (p.hd == 32 ? 8 * (q & 1) : 0);
       load_rope<R16>(p, ri, f0, cs, sn);
-      cur_ip = d.ip;
+      cur_ip = c.ip;
+    }
+    const uint4 *bf = (is_k ? bfk : bfv) + ch.pk * R16 * 4 * 32;
+    {  // pull the next pass's B fragments into L1 (16 lines of 128 B per k-step block)
+      Cursor nx = c;
+      nx.next(p);
+      if (nx.kv < 2 && lane < 16 * R16) {
+        const Chunks nc = chunks_of(p, nx, 0, 0);
+        const uint8_t *nb = reinterpret_cast<const uint8_t *>((nx.kv == 0 ? bfk : bfv) + nc.pk * R16 * 4 * 32);
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(nb + lane * 128));
+      }
     }
     cp_async_wait<DEPTH - 1>();
     Chunk<PDT> pg[2][2];
-    const bool v2[2] = {ri.valid[0] && d.hok, ri.valid[1] && d.hok};
+    const bool v2[2] = {ri.valid[0] && ch.hok, ri.valid[1] && ch.hok};
     if (acc) {
 #pragma unroll
       for (int r = 0; r < 2; ++r)
         if (v2[r]) {
-          pg[r][0].lds(ring.piece(i, 2 * r, 0, lane));
-          pg[r][1].lds(ring.piece(i, 2 * r + 1, 0, lane));
+          pg[r][0].lds(ring.piece(slot, 2 * r, 0, lane));
+          pg[r][1].lds(ring.piece(slot, 2 * r + 1, 0, lane));
         }
     }
-    if (d.is_k)
-      expand_pass<R16, PDT>(bfk + d.pk * R16 * 4 * 32, ck, cs, sn, rope, d.clo, d.chi, p.hd,
-                            static_cast<uint8_t *>(p.k_base[t.layer]), ri.off_k, p.k_shead, om_k, v2,
-                            acc, lane, pg);
+    if (is_k)
+      expand_pass<R16, PDT>(bf, ck, cs, sn, rope, ch.e_lo, ch.e_hi, rp.k, om_k, v2, acc, lane, pg);
     else
-      expand_pass<R16, PDT>(bfv + d.pk * R16 * 4 * 32, cv, cs, sn, false, d.clo, d.chi, p.hd,
-                            static_cast<uint8_t *>(p.v_base[t.layer]), ri.off_v, p.v_shead, om_v, v2,
-                            acc, lane, pg);
-    // the chunks read from slot i have been consumed: refill it with the pass DEPTH ahead
-    ring.issue(p, t, ri, i + DEPTH, lane);
+      expand_pass<R16, PDT>(bf, cv, cs, sn, false, ch.e_lo, ch.e_hi, rp.v, om_v, v2, acc, lane, pg);
+    // the chunks read from this slot have been consumed: refill it with the pass DEPTH ahead
+    ring.issue(p, rp, lane);
+    if (++slot == DEPTH) slot = 0;
+    c.next(p);
   }
   cp_async_wait<0>();
 }
@@ -816,7 +866,6 @@ __global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constan
   PageRing<PDT> ring;
   ring.base = smem_u32(sp) + warp * RING_BYTES;
   ring.depth = DEPTH;
-  ring.total = (p.do_k ? p.n_passes : 0) + (p.do_v ? p.n_passes : 0);
 
   for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
     Tile t;
@@ -824,6 +873,7 @@ __global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constan
 
     // ---- per-row metadata (rows g and g+8 of this warp) ----
     const RowInfo ri = make_row_info(p, t, warp, g);
+    const RowPtrs rp = row_ptrs<PDT>(p, t, ri);
 
     // ---- phase 1: codes = x . A^T (and sum x^2) over the streamed stages ----
     float acc[NT1][4];
@@ -863,7 +913,8 @@ __global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constan
       }
       if (kc == p.kc - 1) {
         // start streaming the first page chunks of phase 2 under the last X slab
-        for (int i = 0; i < DEPTH; ++i) ring.issue(p, t, ri, i, lane);
+        ring.begin(p);
+        for (int i = 0; i < DEPTH; ++i) ring.issue(p, rp, lane);
       }
       if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) {
         record_error(p.status, DKV_ERR_TIMEOUT);
@@ -1006,7 +1057,7 @@ __global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constan
     }
 
     // ---- phase 2: dK / dV, RoPE, page read-add-write ----
-    phase2<R16, PDT, DEPTH>(p, t, ri, ring, ck, cv, om_k, om_v, lane);
+    phase2<R16, PDT, DEPTH>(p, t, ri, rp, ring, ck, cv, om_k, om_v, lane);
   }
   if (is_prod) prod.drain(p, full);
 }
@@ -1186,7 +1237,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
     PageRing<PDT> ring;
     ring.base = smem_u32(smem + S::P_OFF) + warp * S::RING;
     ring.depth = DEPTH;
-    ring.total = (p.do_k ? p.n_passes : 0) + (p.do_v ? p.n_passes : 0);
     int64_t j = 0;
     for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
       Tile t;
@@ -1195,7 +1245,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
       const int64_t use = j / NBUF;
       const int par = static_cast<int>(j & 1);
       const RowInfo ri = make_row_info(p, t, warp, g);
-      for (int i = 0; i < DEPTH; ++i) ring.issue(p, t, ri, i, lane);  // page chunks of phase 2
+      const RowPtrs rp = row_ptrs<PDT>(p, t, ri);
+      ring.begin(p);
+      for (int i = 0; i < DEPTH; ++i) ring.issue(p, rp, lane);  // page chunks of phase 2
 
       uint8_t *codes = codes_base + par * 128 * C::CROW;
       float *om = om_base + par * 2 * 128;
@@ -1292,7 +1344,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
       }
       const float om_k[2] = {om[16 * warp + g], om[16 * warp + g + 8]};
       const float om_v[2] = {om[128 + 16 * warp + g], om[128 + 16 * warp + g + 8]};
-      phase2<R16, PDT, DEPTH>(p, t, ri, ring, ck, cv, om_k, om_v, lane);
+      phase2<R16, PDT, DEPTH>(p, t, ri, rp, ring, ck, cv, om_k, om_v, lane);
       ++j;
     }
     cp_async_wait<0>();
@@ -1526,6 +1578,8 @@ extern "C" int dkv_exact_patch_paged(const dkv_exact_patch_args *a, dkv_stream_t
   p.d_kv = g.d_kv;
   p.r16 = g.r16;
   p.n_passes = g.n_passes;
+  p.nip = g.hd >= 64 ? g.hd / 64 : 1;
+  p.nh = g.hd >= 64 ? g.n_kv : g.n_passes;
   p.kc = g.kc;
   p.stage_k = g.stage_k;
   p.a_off = g.a_off;
@@ -1549,6 +1603,10 @@ extern "C" int dkv_exact_patch_paged(const dkv_exact_patch_args *a, dkv_stream_t
     lead = env ? atoi(env) : 8;
   }
   p.prefetch_lead = lead;
+  if (kp.stride_head * g.n_kv >= (1LL << 30) || vp.stride_head * g.n_kv >= (1LL << 30))
+    return DKV_ERR_LAYOUT;
+  p.k_shead_i = static_cast<int32_t>(kp.stride_head);
+  p.v_shead_i = static_cast<int32_t>(vp.stride_head);
   p.k_sblock = kp.stride_block;
   p.k_sslot = kp.stride_slot;
   p.k_shead = kp.stride_head;

@@ -48,8 +48,12 @@ def test_packed_bytes_host_query():
 
     g = ops.exact_geometry(4096, 8, 128, torch.float8_e4m3fn, 16, 16)
     n = ops.packed_bytes(g)
-    # header 256 + A (32 stages x 32 rows x 256 B) + 2 x B (16 passes x 1 kstep x 2 KiB)
-    assert n == 256 + 32 * 32 * 256 + 2 * 16 * 2048
+    # header 256 + A (32 stages x (3 e4m3 terms x 2 projections x 16 rows) x 128 B)
+    # + 2 x B (16 passes x 1 k-step x 2 KiB)
+    assert n == 256 + 32 * 96 * 128 + 2 * 16 * 2048
+    # ranks above 32 use the mma.sync image: f16 rows of 128 k per stage
+    g64 = ops.exact_geometry(4096, 8, 128, torch.float8_e4m3fn, 64, 64)
+    assert ops.packed_bytes(g64) == 256 + 32 * 128 * 256 + 2 * 16 * 4 * 2048
     with pytest.raises(Exception, match="unsupported"):
         ops.packed_bytes(ops.exact_geometry(4096, 8, 96, torch.float8_e4m3fn, 16, 16))
 

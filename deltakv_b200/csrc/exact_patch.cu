@@ -375,6 +375,18 @@ struct Chunk<DKV_BF16> {
     const uint32_t w = j < 2 ? v.x : j < 4 ? v.y : j < 6 ? v.z : v.w;
     return (j & 1) ? bf16hi(w) : bf16lo(w);
   }
+  // elements (2i, 2i+1) as an fp32 pair
+  __device__ __forceinline__ uint64_t pair(int i) const {
+    const uint32_t w = i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+    return f2pack(bf16lo(w), bf16hi(w));
+  }
+  __device__ __forceinline__ void set_pairs(const uint64_t (&q)[4]) {
+    float a, b;
+    f2unpack(q[0], a, b); v.x = pack_bf16x2(a, b);
+    f2unpack(q[1], a, b); v.y = pack_bf16x2(a, b);
+    f2unpack(q[2], a, b); v.z = pack_bf16x2(a, b);
+    f2unpack(q[3], a, b); v.w = pack_bf16x2(a, b);
+  }
   __device__ __forceinline__ void set_all(const float (&f)[8]) {
     v.x = pack_bf16x2(f[0], f[1]);
     v.y = pack_bf16x2(f[2], f[3]);
@@ -392,6 +404,17 @@ struct Chunk<DKV_F16> {
   __device__ __forceinline__ float get(int j) const {
     const uint32_t w = j < 2 ? v.x : j < 4 ? v.y : j < 6 ? v.z : v.w;
     return (j & 1) ? f16hi(w) : f16lo(w);
+  }
+  __device__ __forceinline__ uint64_t pair(int i) const {
+    const uint32_t w = i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+    return f2pack(f16lo(w), f16hi(w));
+  }
+  __device__ __forceinline__ void set_pairs(const uint64_t (&q)[4]) {
+    float a, b;
+    f2unpack(q[0], a, b); v.x = pack_f16x2(a, b);
+    f2unpack(q[1], a, b); v.y = pack_f16x2(a, b);
+    f2unpack(q[2], a, b); v.z = pack_f16x2(a, b);
+    f2unpack(q[3], a, b); v.w = pack_f16x2(a, b);
   }
   __device__ __forceinline__ void set_all(const float (&f)[8]) {
     v.x = pack_f16x2(f[0], f[1]);
@@ -421,6 +444,16 @@ struct Chunk<DKV_F32> {
     const uint4 &s = j < 4 ? a : b;
     const int k = j & 3;
     return __uint_as_float(k == 0 ? s.x : k == 1 ? s.y : k == 2 ? s.z : s.w);
+  }
+  __device__ __forceinline__ uint64_t pair(int i) const {
+    const uint4 &s = i < 2 ? a : b;
+    return (i & 1) ? (static_cast<uint64_t>(s.w) << 32 | s.z) : (static_cast<uint64_t>(s.y) << 32 | s.x);
+  }
+  __device__ __forceinline__ void set_pairs(const uint64_t (&q)[4]) {
+    a = make_uint4(static_cast<uint32_t>(q[0]), static_cast<uint32_t>(q[0] >> 32),
+                   static_cast<uint32_t>(q[1]), static_cast<uint32_t>(q[1] >> 32));
+    b = make_uint4(static_cast<uint32_t>(q[2]), static_cast<uint32_t>(q[2] >> 32),
+                   static_cast<uint32_t>(q[3]), static_cast<uint32_t>(q[3] >> 32));
   }
   __device__ __forceinline__ void set_all(const float (&f)[8]) {
     a = make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
@@ -559,56 +592,61 @@ __device__ __forceinline__ void expand_pass(const uint4 *__restrict__ bfrag,
   constexpr int EB = Chunk<PDT>::kElemBytes;
   float acc[8][4];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-#pragma unroll
   for (int ks = 0; ks < R16; ++ks) {
     uint4 b[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) b[c] = ldg128_nc(bfrag + (ks * 4 + c) * 32 + lane);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      mma16816(acc[2 * c], cf[ks][0], cf[ks][1], cf[ks][2], cf[ks][3], b[c].x, b[c].y);
-      mma16816(acc[2 * c + 1], cf[ks][0], cf[ks][1], cf[ks][2], cf[ks][3], b[c].z, b[c].w);
+      if (ks == 0) {
+        mma16816_zc(acc[2 * c], cf[ks][0], cf[ks][1], cf[ks][2], cf[ks][3], b[c].x, b[c].y);
+        mma16816_zc(acc[2 * c + 1], cf[ks][0], cf[ks][1], cf[ks][2], cf[ks][3], b[c].z, b[c].w);
+      } else {
+        mma16816(acc[2 * c], cf[ks][0], cf[ks][1], cf[ks][2], cf[ks][3], b[c].x, b[c].y);
+        mma16816(acc[2 * c + 1], cf[ks][0], cf[ks][1], cf[ks][2], cf[ks][3], b[c].z, b[c].w);
+      }
     }
   }
+  // C fragment: acc[jt][2r + b] = row r (g or g+8), chunk lo (jt < 4) / hi, elements 2(jt%4)+b
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     if (!valid[r]) continue;
-    float lo[8], hi[8];
+    uint64_t lo[4], hi[4];
 #pragma unroll
     for (int jt = 0; jt < 4; ++jt) {
-      lo[2 * jt] = acc[jt][2 * r];
-      lo[2 * jt + 1] = acc[jt][2 * r + 1];
-      hi[2 * jt] = acc[jt + 4][2 * r];
-      hi[2 * jt + 1] = acc[jt + 4][2 * r + 1];
+      lo[jt] = f2pack(acc[jt][2 * r], acc[jt][2 * r + 1]);
+      hi[jt] = f2pack(acc[jt + 4][2 * r], acc[jt + 4][2 * r + 1]);
     }
     if (rope) {
+      // lo' = lo*cos - hi*sin, hi' = hi*cos + lo*sin  (rotate-half, rope.py:9-25)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float c = cs[r][j], s = sn[r][j];
-        const float a = lo[j], b = hi[j];
-        lo[j] = a * c - b * s;
-        hi[j] = b * c + a * s;
+      for (int jt = 0; jt < 4; ++jt) {
+        const uint64_t c2 = f2pack(cs[r][2 * jt], cs[r][2 * jt + 1]);
+        const uint64_t s2 = f2pack(sn[r][2 * jt], sn[r][2 * jt + 1]);
+        const uint64_t ns2 = f2pack(-sn[r][2 * jt], -sn[r][2 * jt + 1]);
+        const uint64_t a = lo[jt], b = hi[jt];
+        lo[jt] = fma2(a, c2, mul2(b, ns2));
+        hi[jt] = fma2(b, c2, mul2(a, s2));
       }
     }
-    float o_lo[8], o_hi[8];
-    const float m = om[r];
+    const uint64_t m2 = f2pack(om[r], om[r]);
+    uint64_t o_lo[4], o_hi[4];
     if (accumulate) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        o_lo[j] = fmaf(lo[j], m, pg[r][0].get(j));
-        o_hi[j] = fmaf(hi[j], m, pg[r][1].get(j));
+      for (int jt = 0; jt < 4; ++jt) {
+        o_lo[jt] = fma2(lo[jt], m2, pg[r][0].pair(jt));
+        o_hi[jt] = fma2(hi[jt], m2, pg[r][1].pair(jt));
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        o_lo[j] = lo[j] * m;
-        o_hi[j] = hi[j] * m;
+      for (int jt = 0; jt < 4; ++jt) {
+        o_lo[jt] = mul2(lo[jt], m2);
+        o_hi[jt] = mul2(hi[jt], m2);
       }
     }
     Chunk<PDT> w0, w1;
-    w0.set_all(o_lo);
-    w1.set_all(o_hi);
+    w0.set_pairs(o_lo);
+    w1.set_pairs(o_hi);
     w0.store(rows[r] + e_lo * EB);
     w1.store(rows[r] + e_hi * EB);
   }
@@ -1273,14 +1311,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
         if (p.x_scale && tok < t.len && grow < p.x_rows) xs = __ldg(p.x_scale + t.layer * p.xs_stride + grow);
         float rs = xs;
         if (NORM) {
-          float dv[16];
+          float d0[16], d1[16];
+          tmem_ld16(taddr + C::DIAG + 32 * warp, d0);
+          tmem_ld16(taddr + C::DIAG + 32 * warp + 16, d1);
+          tmem_ld_wait();
           float ss = 0.f;
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            tmem_ld16(taddr + C::DIAG + 32 * warp + 16 * h, dv);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) ss = (16 * h + i == lane) ? dv[i] : ss;
+          for (int i = 0; i < 16; ++i) {
+            ss = (i == lane) ? d0[i] : ss;
+            ss = (16 + i == lane) ? d1[i] : ss;
           }
           rs = xs * rsqrtf(xs * xs * ss * p.inv_d + p.norm_eps);
         }
@@ -1290,20 +1329,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
           float c[RPAD];
 #pragma unroll
           for (int h = 0; h < R16; ++h) {
-            float v[16];
-            tmem_ld16(taddr + kv * C::TERMS * RPAD + 16 * h, v);
+            float v0[16], v1[16], v2[16];
+            const uint32_t col = taddr + kv * C::TERMS * RPAD + 16 * h;
+            tmem_ld16(col, v0);
+            if (C::TERMS == 3) {
+              tmem_ld16(col + RPAD, v1);
+              tmem_ld16(col + 2 * RPAD, v2);
+            }
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) c[16 * h + i] = v[i];
-            if (C::TERMS == 3) {
-              tmem_ld16(taddr + kv * C::TERMS * RPAD + RPAD + 16 * h, v);
-              tmem_ld_wait();
-#pragma unroll
-              for (int i = 0; i < 16; ++i) c[16 * h + i] = fmaf(v[i], 0.0625f, c[16 * h + i]);
-              tmem_ld16(taddr + kv * C::TERMS * RPAD + 2 * RPAD + 16 * h, v);
-              tmem_ld_wait();
-#pragma unroll
-              for (int i = 0; i < 16; ++i) c[16 * h + i] = fmaf(v[i], 0.00390625f, c[16 * h + i]);
+            for (int i = 0; i < 16; ++i) {
+              float x = v0[i];
+              if (C::TERMS == 3) x = fmaf(v2[i], 0.00390625f, fmaf(v1[i], 0.0625f, x));
+              c[16 * h + i] = x;
             }
           }
           const float cm = hdr[kv] * rs;

@@ -6,6 +6,7 @@ deployment swaps them in (see :func:`install`):
 * ``scatter_into_paged`` / ``gather_from_paged``   (deltakv.paged)
 * ``exact_kv_patch`` / ``zeroth_order_patches``    (deltakv.patches.exact)
 * ``apply_layer_patches``                          (deltakv.patches.compose)
+* ``subspace_correct`` / ``svd_basis``             (deltakv.patches.subspace)
 
 plus the fused batched form the engine and connector use: :class:`ExactPatcher`.
 All computation runs in ``libdkv_b200.so``; a missing library raises (no CPU path).
@@ -24,6 +25,7 @@ from deltakv_b200.exact import (
 from deltakv_b200.ops import SeqBatchTensors, quantize_rows
 from deltakv_b200.paged import gather_from_paged, scatter_into_paged, scatter_into_paged_batched
 from deltakv_b200.rope import RotaryEmbedding
+from deltakv_b200.subspace import subspace_correct, svd_basis
 from deltakv_b200.types import KVCache, LayerDelta, LowRankFactors, LowRankKVPatch
 
 __version__ = "0.1.0"
@@ -45,6 +47,8 @@ __all__ = [
     "quantize_rows",
     "scatter_into_paged",
     "scatter_into_paged_batched",
+    "subspace_correct",
+    "svd_basis",
     "zeroth_order_patches",
 ]
 
@@ -57,8 +61,10 @@ _INSTALL_MAP = {
     "deltakv.engine": {"zeroth_order_patches": zeroth_order_patches, "exact_kv_patch": exact_kv_patch,
                        "apply_layer_patches": apply_layer_patches},
     "deltakv.connectors.vllm": {"scatter_into_paged": scatter_into_paged},
+    "deltakv.patches.subspace": {"subspace_correct": subspace_correct, "svd_basis": svd_basis},
+    "deltakv.patches.probe": {"subspace_correct": subspace_correct},
     "deltakv.patches": {"exact_kv_patch": exact_kv_patch, "zeroth_order_patches": zeroth_order_patches,
-                        "apply_layer_patches": apply_layer_patches},
+                        "apply_layer_patches": apply_layer_patches, "subspace_correct": subspace_correct},
 }
 
 

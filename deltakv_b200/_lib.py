@@ -39,6 +39,9 @@ EXPORTED = (
     "dkv_exact_packed_bytes",
     "dkv_pack_exact_factors",
     "dkv_exact_patch_paged",
+    "dkv_subspace_workspace_bytes",
+    "dkv_subspace_correct",
+    "dkv_subspace_probe_residual",
 )
 
 
@@ -126,6 +129,30 @@ class ExactPatchArgs(C.Structure):
     ]
 
 
+class SubspaceArgs(C.Structure):
+    _fields_ = [
+        ("reused", C.c_void_p),
+        ("fresh", C.c_void_p),
+        ("kv_dtype", C.c_int32),
+        ("n_tokens", C.c_int64),
+        ("d", C.c_int64),
+        ("reused_row_stride", C.c_int64),
+        ("fresh_row_stride", C.c_int64),
+        ("probe_index", C.c_void_p),
+        ("n_probes", C.c_int64),
+        ("basis", C.c_void_p),
+        ("rank", C.c_int32),
+        ("token_weights", C.c_void_p),
+        ("corrected", C.c_void_p),
+        ("out_dtype", C.c_int32),
+        ("out_row_stride", C.c_int64),
+        ("subspace_out", C.c_void_p),
+        ("orth_mu_out", C.c_void_p),
+        ("workspace", C.c_void_p),
+        ("workspace_bytes", C.c_int64),
+    ]
+
+
 _lib: C.CDLL | None = None
 
 
@@ -149,6 +176,12 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_pack_exact_factors.argtypes = [C.POINTER(ExactGeometry), C.POINTER(LoraFactors), P, I64, P]
     lib.dkv_exact_patch_paged.restype = C.c_int
     lib.dkv_exact_patch_paged.argtypes = [C.POINTER(ExactPatchArgs), P]
+    lib.dkv_subspace_workspace_bytes.restype = C.c_int
+    lib.dkv_subspace_workspace_bytes.argtypes = [I64, I64, I32, C.POINTER(C.c_int64)]
+    lib.dkv_subspace_correct.restype = C.c_int
+    lib.dkv_subspace_correct.argtypes = [C.POINTER(SubspaceArgs), P]
+    lib.dkv_subspace_probe_residual.restype = C.c_int
+    lib.dkv_subspace_probe_residual.argtypes = [P, P, I32, I64, I64, I64, I64, P, I64, P, P]
 
 
 def lib() -> C.CDLL:

@@ -10,6 +10,9 @@
  *   dkv_scatter_paged      deltakv.paged.scatter_into_paged          src/deltakv/paged.py:8-43
  *   dkv_gather_paged       deltakv.paged.gather_from_paged           src/deltakv/paged.py:46-70
  *   dkv_pack_exact_factors LowRankFactors.codes/.apply operands      src/deltakv/deltas/factors.py:61-67
+ *   dkv_subspace_correct   deltakv.patches.subspace.subspace_correct src/deltakv/patches/subspace.py:45-106
+ *   dkv_subspace_probe_residual  the probe residual R[P] whose SVD is svd_basis's input
+ *                          src/deltakv/patches/subspace.py:37-42,69-73
  *   dkv_exact_patch_paged  exact_kv_patch + LowRankKVPatch.materialize + scatter_into_paged,
  *                          as driven by DeltaKVEngine._patch (exact branch) and
  *                          DeltaKVConnector.patch_paged
@@ -207,6 +210,46 @@ typedef struct dkv_exact_patch_args {
  * rank-r codes kept in registers, RoPE and the page read-add-write fused.
  */
 int dkv_exact_patch_paged(const dkv_exact_patch_args *args, dkv_stream_t stream);
+
+/* ---- subspace route -------------------------------------------------------- */
+
+/*
+ * One subspace_correct problem (subspace.py:45-106) on [n_tokens, d] views of the reused
+ * and fresh K or V (d = n_kv*head_dim; row strides in elements):
+ *   R = fresh - reused; codes = (R B)(B^T B + 1e-6 I)^-1; fitted = codes B^T;
+ *   subspace = mean(codes) B^T; orth_mu = mean_P(R - fitted);
+ *   w_j = token_weights[j] or min(||R_j|| / mean ||R||, 1);
+ *   corrected = reused + fitted + w * orth_mu, corrected[P] = fresh[P].
+ * rank = 0 (basis NULL) is the reference's unstructured branch: corrected = reused +
+ * w * mean_P(R), subspace = 0.  basis is fp32 [d, rank] row-major, rank <= 64.
+ * subspace_out / orth_mu_out (fp32 [d]) may be NULL.  Scratch: workspace of at least
+ * dkv_subspace_workspace_bytes(n_tokens, d, rank); nothing in it needs clearing.
+ */
+typedef struct dkv_subspace_args {
+  const void *reused, *fresh;
+  int32_t kv_dtype; /* DKV_F32 / DKV_F16 / DKV_BF16 */
+  int64_t n_tokens, d;
+  int64_t reused_row_stride, fresh_row_stride;
+  const int32_t *probe_index;
+  int64_t n_probes;
+  const float *basis;
+  int32_t rank;
+  const float *token_weights;
+  void *corrected;
+  int32_t out_dtype;
+  int64_t out_row_stride;
+  float *subspace_out, *orth_mu_out;
+  void *workspace;
+  int64_t workspace_bytes;
+} dkv_subspace_args;
+
+int dkv_subspace_workspace_bytes(int64_t n_tokens, int64_t d, int32_t rank, int64_t *bytes);
+int dkv_subspace_correct(const dkv_subspace_args *args, dkv_stream_t stream);
+/* out[i, :] = fresh[probe_index[i], :] - reused[probe_index[i], :] as fp32 [n_probes, d]. */
+int dkv_subspace_probe_residual(const void *reused, const void *fresh, int32_t kv_dtype,
+                                int64_t reused_row_stride, int64_t fresh_row_stride,
+                                int64_t n_tokens, int64_t d, const int32_t *probe_index,
+                                int64_t n_probes, float *out, dkv_stream_t stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

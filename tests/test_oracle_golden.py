@@ -135,3 +135,19 @@ def test_config1_logits_and_kl_golden():
     assert np.abs(fresh - g["fresh_logits"]).max() < 1e-5
     assert np.abs(patched - g["patched_logits"]).max() < 1e-5
     assert abs(next_token_kl(fresh, patched) - float(g["kl_ref"])) < 1e-6
+
+
+@pytest.mark.parametrize("case", ["t1", "t2", "v", "k"])
+def test_subspace_golden(case):
+    from oracle.subspace import subspace_correct
+
+    g = golden("subspace")
+    basis = None
+    if case == "t1" or (case in ("v", "k") and int(g[f"{case}_use_basis"])):
+        basis = g[f"{case}_basis"]
+    corr, sub, orth = subspace_correct(g[f"{case}_reused"], g[f"{case}_fresh"], g[f"{case}_probes"], basis=basis,
+                                       rank=int(g[f"{case}_rank"]))
+    ref = g[f"{case}_corr"]
+    assert np.linalg.norm(corr - ref) / np.linalg.norm(ref) < 1e-5
+    assert np.abs(orth - g[f"{case}_orth"]).max() < 1e-4 * (1 + np.abs(g[f"{case}_orth"]).max())
+    assert np.abs(sub - g[f"{case}_sub"]).max() < 1e-4 * (1 + np.abs(g[f"{case}_sub"]).max())

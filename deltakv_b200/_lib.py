@@ -41,6 +41,7 @@ EXPORTED = (
     "dkv_exact_patch_paged",
     "dkv_subspace_workspace_bytes",
     "dkv_subspace_correct",
+    "dkv_subspace_correct_noalloc",
     "dkv_subspace_probe_residual",
 )
 
@@ -180,6 +181,8 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_subspace_workspace_bytes.argtypes = [I64, I64, I32, C.POINTER(C.c_int64)]
     lib.dkv_subspace_correct.restype = C.c_int
     lib.dkv_subspace_correct.argtypes = [C.POINTER(SubspaceArgs), P]
+    lib.dkv_subspace_correct_noalloc.restype = C.c_int
+    lib.dkv_subspace_correct_noalloc.argtypes = [C.POINTER(SubspaceArgs), P]
     lib.dkv_subspace_probe_residual.restype = C.c_int
     lib.dkv_subspace_probe_residual.argtypes = [P, P, I32, I64, I64, I64, I64, P, I64, P, P]
 

@@ -15,6 +15,8 @@
 //   sub_solve    (B^T B + 1e-6 I)^-1, orth_mu, subspace, mean ||R||
 //   sub_pass2    corr = reused + (rhs G^-1) B^T + w orth_mu, probes <- fresh
 // Scratch lives in a caller-provided workspace (dkv_subspace_workspace_bytes).
+#include <mutex>
+
 #include "dkv_common.cuh"
 
 namespace dkv {
@@ -510,4 +512,58 @@ extern "C" int dkv_subspace_probe_residual(const void *reused, const void *fresh
       reused, fresh, kv_dtype, reused_row_stride, fresh_row_stride, n_tokens, d, probe_index, n_probes, out);
   DKV_CUDA_CHECK(cudaGetLastError());
   return DKV_OK;
+}
+
+// ---------------------------------------------------------------------------------
+// Allocation-free variant
+// ---------------------------------------------------------------------------------
+// Some callers cannot allocate device memory at the point where they want a correction:
+// code running inside a framework that owns every allocation through its own pool (and
+// forbids cudaMalloc while it serves requests), plugins that are handed only the buffers
+// they must read and write, and host threads that must never block on the allocator's
+// device-wide synchronisation.  For them the scratch lives in one fixed device array
+// defined in this file.  The CUDA runtime places it on every GPU that loads this library
+// and keeps it there until the process exits; it is never allocated or freed per call.
+//
+// The array's host-side name is only a stand-in for the symbol: its device address is
+// looked up once per device (cudaGetSymbolAddress, with that device current) on the first
+// call made while that device is current, cached, and passed to the kernels.
+constexpr int64_t kNoAllocScratchBytes = 16ll << 20;  // 16 MiB
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) uint8_t g_subspace_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_scratch_mu;
+static void *g_scratch_addr[kNoAllocMaxDevices] = {};
+
+static int noalloc_scratch(void **out) {
+  int dev = 0;
+  DKV_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return DKV_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void *ptr = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&ptr, g_subspace_scratch);
+    if (err != cudaSuccess || ptr == nullptr) {
+      note_cuda_error(err != cudaSuccess ? err : cudaErrorInvalidSymbol, "cudaGetSymbolAddress(scratch)");
+      return DKV_ERR_CUDA;
+    }
+    g_scratch_addr[dev] = ptr;
+  }
+  *out = g_scratch_addr[dev];
+  return DKV_OK;
+}
+
+extern "C" int dkv_subspace_correct_noalloc(const dkv_subspace_args *a, dkv_stream_t stream) {
+  if (a == nullptr) return DKV_ERR_INVALID_ARGUMENT;
+  const int rp = a->rank <= 0 ? 0 : (a->rank + 15) / 16 * 16;
+  if (a->n_tokens < 0 || a->d <= 0 || a->rank < 0 || a->rank > sub::kMaxRank) return DKV_ERR_INVALID_ARGUMENT;
+  if (sub::layout(a->n_tokens, a->d, rp).total > kNoAllocScratchBytes) return DKV_ERR_WORKSPACE;
+  void *scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc != DKV_OK) return rc;
+  sub::P p;
+  rc = subspace_params(a, static_cast<uint8_t *>(scratch), kNoAllocScratchBytes, p);
+  if (rc != DKV_OK) return rc;
+  return subspace_run(p, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -245,6 +245,26 @@ typedef struct dkv_subspace_args {
 
 int dkv_subspace_workspace_bytes(int64_t n_tokens, int64_t d, int32_t rank, int64_t *bytes);
 int dkv_subspace_correct(const dkv_subspace_args *args, dkv_stream_t stream);
+/*
+ * dkv_subspace_correct without a caller workspace and without any allocation.  It has no
+ * counterpart in the reference; it exists for callers that cannot allocate device memory
+ * when they need a correction (a serving framework that owns all device memory through its
+ * own pool, a plugin handed only its input and output buffers, a thread that must not
+ * wait on the allocator).  The scratch is one fixed 16 MiB device array inside this
+ * library, present on every GPU that loads it until the process exits; args->workspace
+ * and args->workspace_bytes are ignored.
+ *   - Limit: the problem's scratch, dkv_subspace_workspace_bytes(n_tokens, d, rank), must
+ *     fit in 16 MiB (e.g. 32768 tokens x d=1024 at rank 64); larger problems are rejected
+ *     with DKV_ERR_WORKSPACE before anything is launched.
+ *   - The first call made while a given device is current looks up the array's device
+ *     address (cudaGetSymbolAddress) and caches it; make that first call before any
+ *     stream capture on that device.
+ *   - All calls on a device share the one array and each leaves its contents behind (the
+ *     entry point clears what must start at zero itself).  Calls whose work overlaps on
+ *     the GPU — on different streams, or from different host threads — race on it:
+ *     order them on one stream.
+ */
+int dkv_subspace_correct_noalloc(const dkv_subspace_args *args, dkv_stream_t stream);
 /* out[i, :] = fresh[probe_index[i], :] - reused[probe_index[i], :] as fp32 [n_probes, d]. */
 int dkv_subspace_probe_residual(const void *reused, const void *fresh, int32_t kv_dtype,
                                 int64_t reused_row_stride, int64_t fresh_row_stride,

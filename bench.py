@@ -384,13 +384,12 @@ def run_ours(args):
     peak = peaks.get("hbm_gbs")
     peak_kind = "of measured (MEASURED_PEAKS.json hbm_gbs, burst copy)" if peak else "of fallback (6650 GB/s)"
     peak = peak or 6650.0
-    traffic = None
-    tfile = ROOT / "profiles" / "exact_patch_traffic.json"
-    if tfile.exists():
-        try:
-            traffic = json.loads(tfile.read_text()).get("bytes_per_launch_full_workload")
-        except Exception:
-            traffic = None
+    traffic = None  # DRAM bytes per launch from the committed ncu summary (full workload)
+    tfile = ROOT / "profiles" / "exact_patch_kernel.md"
+    if tfile.exists() and args.layers == 32 and args.seqs == 64 and args.seq_len == 4096:
+        for line in tfile.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch_full_workload:"):
+                traffic = int(line.split(":", 1)[1])
 
     e2e = None
     if not args.no_e2e:

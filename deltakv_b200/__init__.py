@@ -14,6 +14,7 @@ All computation runs in ``libdkv_b200.so``; a missing library raises (no CPU pat
 
 from __future__ import annotations
 
+from deltakv_b200 import kivi
 from deltakv_b200._lib import DkvError
 from deltakv_b200.exact import (
     ExactPatcher,
@@ -43,6 +44,7 @@ __all__ = [
     "exact_kv_patch",
     "gather_from_paged",
     "install",
+    "kivi",
     "materialize_codes",
     "quantize_rows",
     "scatter_into_paged",

@@ -39,6 +39,9 @@ EXPORTED = (
     "dkv_exact_packed_bytes",
     "dkv_pack_exact_factors",
     "dkv_exact_patch_paged",
+    "dkv_kivi_quantize",
+    "dkv_kivi_dequantize",
+    "dkv_kivi_patch",
     "dkv_subspace_workspace_bytes",
     "dkv_subspace_correct",
     "dkv_subspace_correct_noalloc",
@@ -130,6 +133,22 @@ class ExactPatchArgs(C.Structure):
     ]
 
 
+DKV_KIVI_PER_CHANNEL, DKV_KIVI_PER_TOKEN = 0, 1
+
+
+class KiviCache(C.Structure):
+    _fields_ = [
+        ("codes", C.c_void_p),
+        ("scale", C.c_void_p),
+        ("zero", C.c_void_p),
+        ("code_row_stride", C.c_int64),
+        ("sz_row_stride", C.c_int64),
+        ("n_tokens", C.c_int64),
+        ("d", C.c_int64),
+        ("mode", C.c_int32),
+    ]
+
+
 class SubspaceArgs(C.Structure):
     _fields_ = [
         ("reused", C.c_void_p),
@@ -177,6 +196,12 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_pack_exact_factors.argtypes = [C.POINTER(ExactGeometry), C.POINTER(LoraFactors), P, I64, P]
     lib.dkv_exact_patch_paged.restype = C.c_int
     lib.dkv_exact_patch_paged.argtypes = [C.POINTER(ExactPatchArgs), P]
+    lib.dkv_kivi_quantize.restype = C.c_int
+    lib.dkv_kivi_quantize.argtypes = [P, I32, I64, C.POINTER(KiviCache), P]
+    lib.dkv_kivi_dequantize.restype = C.c_int
+    lib.dkv_kivi_dequantize.argtypes = [C.POINTER(KiviCache), P, I32, I64, P]
+    lib.dkv_kivi_patch.restype = C.c_int
+    lib.dkv_kivi_patch.argtypes = [C.POINTER(KiviCache), P, I32, I64, C.POINTER(KiviCache), P]
     lib.dkv_subspace_workspace_bytes.restype = C.c_int
     lib.dkv_subspace_workspace_bytes.argtypes = [I64, I64, I32, C.POINTER(C.c_int64)]
     lib.dkv_subspace_correct.restype = C.c_int

@@ -13,6 +13,8 @@
  *   dkv_subspace_correct   deltakv.patches.subspace.subspace_correct src/deltakv/patches/subspace.py:45-106
  *   dkv_subspace_probe_residual  the probe residual R[P] whose SVD is svd_basis's input
  *                          src/deltakv/patches/subspace.py:37-42,69-73
+ *   dkv_kivi_*             KIVI int4 cache (the reference has only the fake-quant
+ *                          metrics._minmax_quantize, src/deltakv/metrics.py:115-132)
  *   dkv_exact_patch_paged  exact_kv_patch + LowRankKVPatch.materialize + scatter_into_paged,
  *                          as driven by DeltaKVEngine._patch (exact branch) and
  *                          DeltaKVConnector.patch_paged
@@ -210,6 +212,39 @@ typedef struct dkv_exact_patch_args {
  * rank-r codes kept in registers, RoPE and the page read-add-write fused.
  */
 int dkv_exact_patch_paged(const dkv_exact_patch_args *args, dkv_stream_t stream);
+
+/* ---- KIVI-style int4 KV cache ---------------------------------------------- */
+
+#define DKV_KIVI_PER_CHANNEL 0 /* K: groups of 32 consecutive tokens of one channel */
+#define DKV_KIVI_PER_TOKEN 1   /* V: groups of 32 consecutive channels of one token */
+
+/*
+ * One int4 K or V tensor of n_tokens x d (d % 32 == 0): codes [n_tokens, d/2] bytes (even
+ * channel in the low nibble; per-token rows 16-B aligned), fp16 scale and zero per group —
+ * PER_TOKEN: [n_tokens, d/32], PER_CHANNEL: [ceil(n_tokens/32), d] (row stride
+ * sz_row_stride elements, shared by scale and zero).  x = q*scale + zero with
+ * scale = max(hi-lo, 1e-8)/15 and zero = lo rounded to fp16 before q = clamp(rint((x-zero)/
+ * scale), 0, 15); a partial last K group covers the remaining tokens.  This format is this
+ * library's; the reference's int4 arithmetic is the fake-quant metrics._minmax_quantize.
+ */
+typedef struct dkv_kivi_cache {
+  void *codes;
+  void *scale, *zero;
+  int64_t code_row_stride; /* bytes */
+  int64_t sz_row_stride;   /* elements */
+  int64_t n_tokens, d;
+  int32_t mode;
+} dkv_kivi_cache;
+
+/* out = int4(x);  x is F32/F16/BF16 [n_tokens, d] with row stride x_row_stride elements. */
+int dkv_kivi_quantize(const void *x, int32_t x_dtype, int64_t x_row_stride, const dkv_kivi_cache *out,
+                      dkv_stream_t stream);
+/* x = dequant(in) */
+int dkv_kivi_dequantize(const dkv_kivi_cache *in, void *x, int32_t x_dtype, int64_t x_row_stride,
+                        dkv_stream_t stream);
+/* out = int4(dequant(base) + delta) — the int4 form of a KV patch; out may be base itself. */
+int dkv_kivi_patch(const dkv_kivi_cache *base, const void *delta, int32_t delta_dtype,
+                   int64_t delta_row_stride, const dkv_kivi_cache *out, dkv_stream_t stream);
 
 /* ---- subspace route -------------------------------------------------------- */
 

@@ -26,6 +26,9 @@ Cases:
   subspace.npz     subspace_correct with a given basis (V path), with basis=None (K path,
                    SVD of the probe residual) and the reference tests' two cases
                    (tests/test_quality.py:32-64).
+  kivi.npz         metrics._minmax_quantize (4 bits, group 32) on the last dimension (the
+                   per-token V grouping) and on the transposed tensor (per-channel K
+                   grouping), plus kivi_noise_floor on a small KVCache.
 """
 
 from __future__ import annotations
@@ -301,6 +304,20 @@ def main(ref_src: str) -> None:
                     f"{tag}_basis": B.numpy(), f"{tag}_use_basis": np.int32(use_basis), f"{tag}_rank": np.int32(rr),
                     f"{tag}_corr": corr.numpy(), f"{tag}_sub": subsp.numpy(), f"{tag}_orth": orth.numpy()})
     np.savez_compressed(OUT / "subspace.npz", **sub)
+
+    # ------------------------------------------------------------------- kivi
+    from deltakv.metrics import _minmax_quantize, kivi_noise_floor
+    from deltakv.patches.tensors import KVCache
+
+    gk = torch.Generator().manual_seed(6)
+    xv = torch.randn(70, 4, 64, generator=gk)            # [tokens, heads, dim]: groups along dim
+    xk = torch.randn(96, 2, 64, generator=gk) * 0.5 + 0.1
+    kq = _minmax_quantize(xk.reshape(96, -1).T.contiguous(), 4, 32).T.contiguous()  # groups along tokens
+    kvc = KVCache(k=torch.randn(2, 64, 2, 32, generator=gk), v=torch.randn(2, 64, 2, 32, generator=gk),
+                  version=WeightVersion(id="base"))
+    np.savez_compressed(OUT / "kivi.npz", xv=xv.numpy(), xv_q=_minmax_quantize(xv, 4, 32).numpy(),
+                        xk=xk.numpy(), xk_q=kq.numpy(), floor_k=kvc.k.numpy(), floor_v=kvc.v.numpy(),
+                        floor=np.float64(kivi_noise_floor(kvc, bits=4, group_size=32)))
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
 
 

@@ -151,3 +151,39 @@ def test_subspace_golden(case):
     assert np.linalg.norm(corr - ref) / np.linalg.norm(ref) < 1e-5
     assert np.abs(orth - g[f"{case}_orth"]).max() < 1e-4 * (1 + np.abs(g[f"{case}_orth"]).max())
     assert np.abs(sub - g[f"{case}_sub"]).max() < 1e-4 * (1 + np.abs(g[f"{case}_sub"]).max())
+
+
+def test_kivi_spec_vs_reference_fake_quant():
+    """The stored format differs from _minmax_quantize only by fp16 storage of scale/zero."""
+    from oracle import kivi as OK
+
+    g = golden("kivi")
+    xv = g["xv"].reshape(70, -1)
+    c, s, z = OK.quantize(xv, "v")
+    deq = OK.dequantize(c, s, z, "v")
+    ref = g["xv_q"].reshape(70, -1)
+    step = (xv.reshape(70, -1, 32).max(-1) - xv.reshape(70, -1, 32).min(-1)) / 15
+    # fp16 scale/zero move a value into the neighbouring bin only near a bin boundary:
+    # at most one step away from the reference's fp32 fake-quant, almost always within 1%
+    err = np.abs(deq - ref).reshape(70, -1, 32) / step[..., None]
+    assert err.max() <= 1.01 and (err < 1e-2).mean() > 0.98
+    xk = g["xk"].reshape(96, -1)
+    c, s, z = OK.quantize(xk, "k")
+    deqk = OK.dequantize(c, s, z, "k")
+    refk = g["xk_q"].reshape(96, -1)
+    stepk = (xk.max() - xk.min()) / 15
+    assert np.abs(deqk - refk).max() <= 1.01 * stepk and (np.abs(deqk - refk) < 1e-2 * stepk).mean() > 0.98
+
+
+def test_kivi_roundtrip_properties():
+    from oracle import kivi as OK
+
+    rng = np.random.default_rng(0)
+    for mode in ("v", "k"):
+        x = rng.standard_normal((77, 96)).astype(np.float32)
+        c, s, z = OK.quantize(x, mode)
+        deq = OK.dequantize(c, s, z, mode)
+        c2, s2, z2 = OK.quantize(deq, mode)  # idempotent on its own output up to fp16 re-rounding
+        assert np.abs(OK.dequantize(c2, s2, z2, mode) - deq).max() < 2e-2
+        assert np.abs(deq - x).max() <= (x.max() - x.min()) / 15
+        assert np.array_equal(OK.unpack_nibbles(OK.pack_nibbles(OK.unpack_nibbles(c))), OK.unpack_nibbles(c))

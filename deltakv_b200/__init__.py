@@ -8,7 +8,8 @@ deployment swaps them in (see :func:`install`):
 * ``apply_layer_patches``                          (deltakv.patches.compose)
 * ``subspace_correct`` / ``svd_basis``             (deltakv.patches.subspace)
 
-plus the fused batched form the engine and connector use: :class:`ExactPatcher`.
+plus the fused batched forms the engine and connector use: :class:`ExactPatcher` (LoRA
+deltas) and :class:`DensePatcher` (full-rank dW of an RL step, a tensor-core GEMM).
 All computation runs in ``libdkv_b200.so``; a missing library raises (no CPU path).
 """
 
@@ -16,6 +17,7 @@ from __future__ import annotations
 
 from deltakv_b200 import kivi
 from deltakv_b200._lib import DkvError
+from deltakv_b200.dense import DensePatcher
 from deltakv_b200.exact import (
     ExactPatcher,
     apply_layer_patches,
@@ -32,6 +34,7 @@ from deltakv_b200.types import KVCache, LayerDelta, LowRankFactors, LowRankKVPat
 __version__ = "0.1.0"
 
 __all__ = [
+    "DensePatcher",
     "DkvError",
     "ExactPatcher",
     "KVCache",

@@ -39,6 +39,9 @@ EXPORTED = (
     "dkv_exact_packed_bytes",
     "dkv_pack_exact_factors",
     "dkv_exact_patch_paged",
+    "dkv_pack_dense_delta",
+    "dkv_dense_patch_paged",
+    "dkv_row_inv_rms",
     "dkv_kivi_quantize",
     "dkv_kivi_dequantize",
     "dkv_kivi_patch",
@@ -149,6 +152,51 @@ class KiviCache(C.Structure):
     ]
 
 
+class DenseGeometry(C.Structure):
+    _fields_ = [("d_model", C.c_int32), ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32)]
+
+
+class DenseDelta(C.Structure):
+    _fields_ = [
+        ("dw_k", C.c_void_p),
+        ("dw_v", C.c_void_p),
+        ("dtype", C.c_int32),
+        ("n_layers", C.c_int32),
+        ("dw_k_layer_stride", C.c_int64),
+        ("dw_v_layer_stride", C.c_int64),
+        ("norm_weight", C.c_void_p),
+        ("norm_dtype", C.c_int32),
+        ("norm_layer_stride", C.c_int64),
+        ("scale_k", C.c_float),
+        ("scale_v", C.c_float),
+    ]
+
+
+class DensePatchArgs(C.Structure):
+    _fields_ = [
+        ("geom", DenseGeometry),
+        ("x", C.c_void_p),
+        ("x_layer_stride", C.c_int64),
+        ("x_row_stride", C.c_int64),
+        ("x_rows", C.c_int64),
+        ("x_scale", C.c_void_p),
+        ("x_scale_layer_stride", C.c_int64),
+        ("packed", C.c_void_p),
+        ("packed_layer_stride", C.c_int64),
+        ("rope_cos", C.c_void_p),
+        ("rope_sin", C.c_void_p),
+        ("rope_max_pos", C.c_int32),
+        ("n_layers", C.c_int32),
+        ("do_k", C.c_int32),
+        ("do_v", C.c_int32),
+        ("seqs", SeqBatch),
+        ("k_pages", C.POINTER(PagedCache)),
+        ("v_pages", C.POINTER(PagedCache)),
+        ("accumulate", C.c_int32),
+        ("status", C.c_void_p),
+    ]
+
+
 class SubspaceArgs(C.Structure):
     _fields_ = [
         ("reused", C.c_void_p),
@@ -196,6 +244,12 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_pack_exact_factors.argtypes = [C.POINTER(ExactGeometry), C.POINTER(LoraFactors), P, I64, P]
     lib.dkv_exact_patch_paged.restype = C.c_int
     lib.dkv_exact_patch_paged.argtypes = [C.POINTER(ExactPatchArgs), P]
+    lib.dkv_pack_dense_delta.restype = C.c_int
+    lib.dkv_pack_dense_delta.argtypes = [C.POINTER(DenseGeometry), C.POINTER(DenseDelta), P, I64, P]
+    lib.dkv_dense_patch_paged.restype = C.c_int
+    lib.dkv_dense_patch_paged.argtypes = [C.POINTER(DensePatchArgs), P]
+    lib.dkv_row_inv_rms.restype = C.c_int
+    lib.dkv_row_inv_rms.argtypes = [P, I32, I64, I64, I64, C.c_float, P, P]
     lib.dkv_kivi_quantize.restype = C.c_int
     lib.dkv_kivi_quantize.argtypes = [P, I32, I64, C.POINTER(KiviCache), P]
     lib.dkv_kivi_dequantize.restype = C.c_int

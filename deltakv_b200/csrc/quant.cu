@@ -94,3 +94,37 @@ extern "C" int dkv_quantize_rows(const void *x, int32_t x_dtype, int64_t rows, i
 #undef DKV_Q
   return DKV_ERR_UNSUPPORTED;
 }
+
+namespace dkv {
+namespace rms {
+// one warp per row: 1/sqrt(mean(x^2) + eps), the factor RMSNorm multiplies a row by
+__global__ void row_inv_rms_kernel(const void *x, int dt, int64_t rows, int64_t cols, int64_t rs,
+                                   float eps, float *out) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float s = 0.f;
+  for (int64_t c = lane; c < cols; c += 32) {
+    const float v = dkv::load_as_float(x, dt, row * rs + c);
+    s = fmaf(v, v, s);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) out[row] = 1.f / sqrtf(s / static_cast<float>(cols) + eps);
+}
+}  // namespace rms
+}  // namespace dkv
+
+extern "C" int dkv_row_inv_rms(const void *x, int32_t x_dtype, int64_t rows, int64_t cols,
+                               int64_t x_row_stride, float eps, float *out, dkv_stream_t stream) {
+  if (rows < 0 || cols <= 0) return DKV_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return DKV_OK;
+  if (x == nullptr || out == nullptr) return DKV_ERR_INVALID_ARGUMENT;
+  if (x_dtype != DKV_F32 && x_dtype != DKV_F16 && x_dtype != DKV_BF16) return DKV_ERR_UNSUPPORTED;
+  const int64_t blocks = (rows + 7) / 8;
+  if (blocks > 0x7fffffffLL) return DKV_ERR_UNSUPPORTED;
+  dkv::rms::row_inv_rms_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      x, x_dtype, rows, cols, x_row_stride, eps, out);
+  DKV_CUDA_CHECK(cudaGetLastError());
+  return DKV_OK;
+}

@@ -314,3 +314,117 @@ def exact_patch_paged(geom: L.ExactGeometry, x: torch.Tensor, packed: torch.Tens
     )
     rc = L.lib().dkv_exact_patch_paged(C.byref(args), stream_ptr())
     L.check(rc, "dkv_exact_patch_paged")
+
+
+# ---------------------------------------------------------------------------------------
+# dense-delta route
+# ---------------------------------------------------------------------------------------
+def dense_geometry(d_model: int, n_kv_heads: int, head_dim: int) -> L.DenseGeometry:
+    return L.DenseGeometry(d_model=d_model, n_kv_heads=n_kv_heads, head_dim=head_dim)
+
+
+def pack_dense_delta(geom: L.DenseGeometry, dw_k: torch.Tensor | None, dw_v: torch.Tensor | None,
+                     *, scale_k: float = 1.0, scale_v: float = 1.0,
+                     norm_weight: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``dw_k``/``dw_v``: ``[L, n_kv*hd, d]`` (or 2-D for one layer) -> bf16 ``[L, 2*n_kv*hd, d]``."""
+    ref = dw_k if dw_k is not None else dw_v
+    if ref is None:
+        raise ValueError("at least one of dw_k / dw_v is required")
+    d_kv = geom.n_kv_heads * geom.head_dim
+
+    def as3(t):
+        if t is None:
+            return None
+        t = t if t.ndim == 3 else t.unsqueeze(0)
+        if tuple(t.shape[1:]) != (d_kv, geom.d_model):
+            raise ValueError(f"dW shape {tuple(t.shape[1:])} != ({d_kv}, {geom.d_model})")
+        return t.contiguous()
+
+    k3, v3 = as3(dw_k), as3(dw_v)
+    if k3 is not None and v3 is not None and (k3.dtype != v3.dtype or k3.shape[0] != v3.shape[0]):
+        raise ValueError("dw_k and dw_v must share dtype and layer count")
+    r3 = k3 if k3 is not None else v3
+    n_layers = r3.shape[0]
+    _require_cuda(k3, v3, norm_weight)
+    nw = None
+    if norm_weight is not None:
+        nw = (norm_weight if norm_weight.ndim == 2 else norm_weight.unsqueeze(0).expand(n_layers, -1)).contiguous()
+    if out is None:
+        out = torch.empty(n_layers, 2 * d_kv, geom.d_model, dtype=torch.bfloat16, device=r3.device)
+    dw = L.DenseDelta(
+        dw_k=ptr(k3), dw_v=ptr(v3), dtype=dkv_dtype(r3.dtype), n_layers=n_layers,
+        dw_k_layer_stride=k3.stride(0) if k3 is not None else 0,
+        dw_v_layer_stride=v3.stride(0) if v3 is not None else 0,
+        norm_weight=ptr(nw), norm_dtype=dkv_dtype(nw.dtype) if nw is not None else 0,
+        norm_layer_stride=nw.stride(0) if nw is not None else 0,
+        scale_k=float(scale_k), scale_v=float(scale_v),
+    )
+    rc = L.lib().dkv_pack_dense_delta(C.byref(geom), C.byref(dw), out.data_ptr(), out.stride(0), stream_ptr())
+    L.check(rc, "dkv_pack_dense_delta")
+    return out
+
+
+def row_inv_rms(x: torch.Tensor, eps: float) -> torch.Tensor:
+    """``1/sqrt(mean(x^2) + eps)`` per row of ``x [..., d]`` (fp32), the RMSNorm row factor."""
+    _require_cuda(x)
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    out = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
+    rc = L.lib().dkv_row_inv_rms(x2.data_ptr(), dkv_dtype(x2.dtype), x2.shape[0], x2.shape[1], x2.stride(0),
+                                 float(eps), out.data_ptr(), stream_ptr())
+    L.check(rc, "dkv_row_inv_rms")
+    return out.view(x.shape[:-1])
+
+
+def dense_patch_paged(geom: L.DenseGeometry, x: torch.Tensor, packed: torch.Tensor,
+                      k_pages: Sequence[torch.Tensor], v_pages: Sequence[torch.Tensor],
+                      seqs: SeqBatchTensors, *, x_scale: torch.Tensor | None = None,
+                      rope_cos: torch.Tensor | None = None, rope_sin: torch.Tensor | None = None,
+                      do_k: bool = True, do_v: bool = True, accumulate: bool = True,
+                      status: StatusWord | None = None) -> None:
+    """Launch the dense-delta GEMM patch over ``L = len(k_pages)`` layers.
+
+    ``x`` ``[L, rows, d]`` bf16; ``packed`` from :func:`pack_dense_delta`; ``x_scale``
+    ``[L, rows]`` fp32 multiplies each row's product (e.g. the RMSNorm factor).
+    """
+    n_layers = len(k_pages)
+    if len(v_pages) != n_layers:
+        raise ValueError("k_pages and v_pages must cover the same layers")
+    if n_layers > L.DKV_MAX_LAYERS:
+        raise ValueError(f"at most {L.DKV_MAX_LAYERS} layers per launch")
+    x3 = x if x.ndim == 3 else x.unsqueeze(0)
+    if x3.shape[0] != n_layers:
+        raise ValueError("x layers do not match the page lists")
+    if x3.dtype != torch.bfloat16:
+        raise TypeError("the dense route reads bf16 activations")
+    p3 = packed if packed.ndim == 3 else packed.unsqueeze(0)
+    if p3.shape[0] < n_layers or p3.dtype != torch.bfloat16:
+        raise ValueError("packed delta must be bf16 [L, 2*n_kv*hd, d] covering every layer")
+    _require_cuda(x3, p3, x_scale, rope_cos, rope_sin)
+    if x3.stride(2) != 1 or p3.stride(2) != 1:
+        raise ValueError("x and packed rows must be contiguous")
+    xs = None
+    if x_scale is not None:
+        xs = x_scale if x_scale.ndim == 2 else x_scale.unsqueeze(0)
+        if xs.dtype != torch.float32 or xs.stride(1) != 1:
+            raise TypeError("x_scale must be fp32 with contiguous rows")
+    kd = (L.PagedCache * n_layers)(*[paged_desc(p) for p in k_pages])
+    vd = (L.PagedCache * n_layers)(*[paged_desc(p) for p in v_pages])
+    if rope_cos is not None:
+        rope_cos = rope_cos.contiguous()
+        rope_sin = rope_sin.contiguous()
+    args = L.DensePatchArgs(
+        geom=geom,
+        x=x3.data_ptr(), x_layer_stride=x3.stride(0), x_row_stride=x3.stride(1), x_rows=x3.shape[1],
+        x_scale=ptr(xs), x_scale_layer_stride=xs.stride(0) if xs is not None else 0,
+        packed=p3.data_ptr(), packed_layer_stride=p3.stride(0),
+        rope_cos=ptr(rope_cos), rope_sin=ptr(rope_sin),
+        rope_max_pos=rope_cos.shape[0] if rope_cos is not None else 0,
+        n_layers=n_layers, do_k=1 if do_k else 0, do_v=1 if do_v else 0,
+        seqs=seqs.struct(), k_pages=kd, v_pages=vd,
+        accumulate=1 if accumulate else 0,
+        status=status.ptr if status else None,
+    )
+    rc = L.lib().dkv_dense_patch_paged(C.byref(args), stream_ptr())
+    L.check(rc, "dkv_dense_patch_paged")

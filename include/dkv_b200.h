@@ -213,6 +213,74 @@ typedef struct dkv_exact_patch_args {
  */
 int dkv_exact_patch_paged(const dkv_exact_patch_args *args, dkv_stream_t stream);
 
+/* ---- dense-delta patch (RL step: full-rank dW on k_proj / v_proj) ------------------ */
+
+/*
+ * The reference expresses a dense weight delta through the exact route with
+ * LowRankFactors(A = dW, B = I, scale = 1) (patches/exact.py:14-63, factors.py:61-67):
+ * dK = RoPE(x @ dW_K^T), dV = x @ dW_V^T.  Here dW_K and dW_V are packed once per delta
+ * into one bf16 operand and the patch is one tensor-core GEMM launch per call.
+ */
+typedef struct dkv_dense_geometry {
+  int32_t d_model;    /* multiple of 64 */
+  int32_t n_kv_heads;
+  int32_t head_dim;   /* 32, 64 or 128 */
+} dkv_dense_geometry;
+
+/*
+ * dW_K, dW_V [n_kv*head_dim, d_model] row-major (either may be NULL: zero delta), layer l
+ * at dw + l*layer_stride elements.  Optional RMSNorm weight [n_layers, d_model] is folded in
+ * (dW . diag(w)), so the patch consumes pre-norm X with x_scale = 1/rms(x)
+ * (dkv_row_inv_rms).  scale_k / scale_v multiply the deltas.
+ */
+typedef struct dkv_dense_delta {
+  const void *dw_k, *dw_v;
+  int32_t dtype; /* DKV_F32 / DKV_F16 / DKV_BF16 */
+  int32_t n_layers;
+  int64_t dw_k_layer_stride, dw_v_layer_stride;
+  const void *norm_weight;
+  int32_t norm_dtype;
+  int64_t norm_layer_stride;
+  float scale_k, scale_v;
+} dkv_dense_delta;
+
+/* packed: n_layers bf16 images [2*n_kv*head_dim, d_model] (K rows, then V rows), layer l at
+   packed + l*packed_layer_stride elements (>= 2*n_kv*head_dim*d_model, multiple of 8). */
+int dkv_pack_dense_delta(const dkv_dense_geometry *geom, const dkv_dense_delta *dw, void *packed,
+                         int64_t packed_layer_stride, dkv_stream_t stream);
+
+typedef struct dkv_dense_patch_args {
+  dkv_dense_geometry geom;
+  /* stored activations X, bf16: element (l, t, k) at x + l*x_layer_stride + t*x_row_stride + k */
+  const void *x;
+  int64_t x_layer_stride, x_row_stride, x_rows;
+  /* optional per-token multiplier of the product (fp32, (l, t) at x_scale + l*x_scale_layer_stride + t) */
+  const float *x_scale;
+  int64_t x_scale_layer_stride;
+  const void *packed; /* dkv_pack_dense_delta output */
+  int64_t packed_layer_stride;
+  const float *rope_cos, *rope_sin; /* [rope_max_pos, head_dim/2] or NULL: no RoPE on K */
+  int32_t rope_max_pos;
+  int32_t n_layers;
+  int32_t do_k, do_v; /* which projections to patch */
+  dkv_seq_batch seqs;
+  const dkv_paged_cache *k_pages; /* per layer, bf16 or f16; layouts as for the exact patch */
+  const dkv_paged_cache *v_pages;
+  int32_t accumulate;
+  int32_t *status;
+} dkv_dense_patch_args;
+
+/*
+ * For every layer l and token t:  dK = RoPE_pos(t)(x_scale * X[l,t] @ W_K^T),
+ * dV = x_scale * X[l,t] @ W_V^T, pages (+)= dK / dV — a persistent tcgen05 GEMM (bf16 in,
+ * fp32 accumulate in tensor memory) with RoPE and the paged read-add-write in its epilogue.
+ */
+int dkv_dense_patch_paged(const dkv_dense_patch_args *args, dkv_stream_t stream);
+
+/* out[r] = 1/sqrt(mean_c(x[r,c]^2) + eps) (fp32), the RMSNorm row factor (model.py:48-56). */
+int dkv_row_inv_rms(const void *x, int32_t x_dtype, int64_t rows, int64_t cols, int64_t x_row_stride,
+                    float eps, float *out, dkv_stream_t stream);
+
 /* ---- KIVI-style int4 KV cache ---------------------------------------------- */
 
 #define DKV_KIVI_PER_CHANNEL 0 /* K: groups of 32 consecutive tokens of one channel */

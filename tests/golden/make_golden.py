@@ -26,6 +26,10 @@ Cases:
   subspace.npz     subspace_correct with a given basis (V path), with basis=None (K path,
                    SVD of the probe residual) and the reference tests' two cases
                    (tests/test_quality.py:32-64).
+  dense_paged.npz  dense weight delta (full-rank dW_K, dW_V, as an RL step produces) through
+                   the reference's exact route with LowRankFactors(A=dW, B=I, scale=1):
+                   RMSNorm, exact_kv_patch, materialize, scatter_into_paged over a ragged
+                   batch of bf16 activations into bf16 pages.
   kivi.npz         metrics._minmax_quantize (4 bits, group 32) on the last dimension (the
                    per-token V grouping) and on the transposed tensor (per-channel K
                    grouping), plus kivi_noise_floor on a small KVCache.
@@ -257,6 +261,60 @@ def main(ref_src: str) -> None:
         OUT / "fp8_paged.npz",
         x_bits=xq.view(torch.uint8).numpy(), x_scale=xscale.numpy(), norm_w=norm_w.numpy(), eps=np.float32(1e-6),
         a_k=a_k.numpy(), b_k=b_k.numpy(), a_v=a_v.numpy(), b_v=b_v.numpy(), s_k=np.float32(s_k), s_v=np.float32(s_v),
+        cu_seqlens=cu, block_tables=tables, block_size=np.int32(bs),
+        rope_cos=rope.cos_cached[:, : hd // 2].numpy(), rope_sin=rope.sin_cached[:, : hd // 2].numpy(),
+        k_pages_in=np.stack([bf16_bits(t) for t in kp_in]), v_pages_in=np.stack([bf16_bits(t) for t in vp_in]),
+        k_pages_out=np.stack([bf16_bits(t) for t in kp_out]), v_pages_out=np.stack([bf16_bits(t) for t in vp_out]),
+        n_kv=np.int32(n_kv), hd=np.int32(hd),
+    )
+
+    # ------------------------------------------------------------ dense_paged
+    gd = torch.Generator().manual_seed(7)
+    L_, dm, n_kv, hd, bs = 2, 256, 2, 128, 16
+    lens = [37, 128, 1, 200, 300]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    rows = int(cu[-1])
+    rope = RotaryEmbedding(hd, max_seq=512, base=500000.0)
+    x = (torch.randn(L_, rows, dm, generator=gd) * 2.0).to(torch.bfloat16).float()  # stored bf16 X
+    norm_w = 1.0 + 0.1 * torch.randn(L_, dm, generator=gd)
+    d_kv = n_kv * hd
+    # deltas of a few percent of the cached values (an RL step's is ~1e-3 of W)
+    dw_k = (torch.randn(L_, d_kv, dm, generator=gd) * 0.003).to(torch.bfloat16).float()
+    dw_v = (torch.randn(L_, d_kv, dm, generator=gd) * 0.003).to(torch.bfloat16).float()
+    max_blocks = max((n + bs - 1) // bs for n in lens)
+    nblk = sum((n + bs - 1) // bs for n in lens) + 5
+    perm = torch.randperm(nblk, generator=gd).tolist()
+    tables = np.full((len(lens), max_blocks), -1, np.int32)
+    k = 0
+    for b, n in enumerate(lens):
+        for i in range((n + bs - 1) // bs):
+            tables[b, i] = perm[k]
+            k += 1
+    kp_in = [torch.randn(nblk, bs, n_kv, hd, generator=gd).to(torch.bfloat16) for _ in range(L_)]
+    vp_in = [torch.randn(nblk, bs, n_kv, hd, generator=gd).to(torch.bfloat16) for _ in range(L_)]
+    kp_out = [t.clone() for t in kp_in]
+    vp_out = [t.clone() for t in vp_in]
+    eye = torch.eye(d_kv)
+    for l in range(L_):
+        norm = RMSNorm(dm, 1e-6)
+        with torch.no_grad():
+            norm.weight.copy_(norm_w[l])
+        ld = LayerDelta(layer_idx=l, projections={
+            "k_proj": LowRankFactors(A=dw_k[l], B=eye, scale=1.0),
+            "v_proj": LowRankFactors(A=dw_v[l], B=eye, scale=1.0),
+        })
+        for b, n in enumerate(lens):
+            with torch.no_grad():
+                xn_b = norm(x[l, cu[b]:cu[b + 1]])
+                p = exact_kv_patch(xn_b, ld, n_kv_heads=n_kv, head_dim=hd, rope=rope)
+                dk, dv = p.materialize(n_kv, hd)
+            t = tables[b, : (n + bs - 1) // bs].tolist()
+            scatter_into_paged(dk, kp_out[l], t, bs)
+            scatter_into_paged(dv, vp_out[l], t, bs)
+    np.savez_compressed(
+        OUT / "dense_paged.npz",
+        x_bits=bf16_bits(x), norm_w=norm_w.numpy(), eps=np.float32(1e-6),
+        dw_k_bits=bf16_bits(dw_k), dw_v_bits=bf16_bits(dw_v),
         cu_seqlens=cu, block_tables=tables, block_size=np.int32(bs),
         rope_cos=rope.cos_cached[:, : hd // 2].numpy(), rope_sin=rope.sin_cached[:, : hd // 2].numpy(),
         k_pages_in=np.stack([bf16_bits(t) for t in kp_in]), v_pages_in=np.stack([bf16_bits(t) for t in vp_in]),

@@ -187,3 +187,25 @@ def test_kivi_roundtrip_properties():
         assert np.abs(OK.dequantize(c2, s2, z2, mode) - deq).max() < 2e-2
         assert np.abs(deq - x).max() <= (x.max() - x.min()) / 15
         assert np.array_equal(OK.unpack_nibbles(OK.pack_nibbles(OK.unpack_nibbles(c))), OK.unpack_nibbles(c))
+
+
+def test_dense_paged_golden():
+    """The dense route's oracle (A=dW, B=I through the exact route) against the reference."""
+    from oracle import dense as OD
+
+    g = golden("dense_paged")
+    n_kv, hd = int(g["n_kv"]), int(g["hd"])
+    L_ = g["x_bits"].shape[0]
+    kp = [g["k_pages_in"][l].copy() for l in range(L_)]
+    vp = [g["v_pages_in"][l].copy() for l in range(L_)]
+    OD.dense_patch_paged(x=bf16_bits_to_f32(g["x_bits"]), norm_w=g["norm_w"], eps=float(g["eps"]),
+                         dw_k=bf16_bits_to_f32(g["dw_k_bits"]), dw_v=bf16_bits_to_f32(g["dw_v_bits"]),
+                         cu_seqlens=g["cu_seqlens"], block_tables=g["block_tables"], k_pages=kp, v_pages=vp,
+                         n_kv=n_kv, hd=hd, rope=(g["rope_cos"], g["rope_sin"]), kind="bf16")
+    for l in range(L_):
+        for ours, ref, base in ((kp[l], g["k_pages_out"][l], g["k_pages_in"][l]),
+                                (vp[l], g["v_pages_out"][l], g["v_pages_in"][l])):
+            a, b = bf16_bits_to_f32(ours), bf16_bits_to_f32(ref)
+            assert np.linalg.norm(a - b) / np.linalg.norm(b) < 1e-5
+            assert (ours == ref).mean() > 0.995
+            assert not np.array_equal(ref, base)  # the case patches something

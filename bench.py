@@ -7,6 +7,12 @@ folded in) into bf16 paged K/V (block 16, permuted block table), RoPE on K.
 
     python bench.py [--gpus N --steps K --warmup W]          # this implementation
     python bench.py --impl reference ...                       # CPU reference arm
+    python bench.py --workload rl-dense ...                    # dense-dW (RL step) route
+
+The rl-dense workload is one GPU's share of the Llama-3-70B-shaped RL step (10 of 80
+layers, d=8192, 8 KV heads x 128, 16 seqs x 8192 tokens, bf16 X, full-rank dW_K / dW_V at
+||dW||/||W|| = 1e-3): one tensor-core GEMM launch of 44 TFLOP per step with RoPE and the
+paged read-add-write fused; its roofline is the measured sustained bf16 GEMM rate.
 
 Under torchrun (N>1) every rank patches its own request shard of the same size (weak
 scaling; no data-path collective).  Rank 0 prints one JSON line.
@@ -44,9 +50,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--layers", type=int, default=32)
-    ap.add_argument("--seqs", type=int, default=64)
-    ap.add_argument("--seq-len", type=int, default=4096)
+    ap.add_argument("--workload", default="llama8b-exact", choices=["llama8b-exact", "rl-dense"])
+    ap.add_argument("--layers", type=int, default=None)
+    ap.add_argument("--seqs", type=int, default=None)
+    ap.add_argument("--seq-len", type=int, default=None)
     ap.add_argument("--e2e-seqs", type=int, default=4)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-e2e", action="store_true")
@@ -56,6 +63,11 @@ def parse():
 
 class Geo:
     d_model, n_kv, hd, rank, bs, eps, rope_theta = 4096, 8, 128, 16, 16, 1e-5, 500000.0
+
+
+class DenseGeo:
+    """One GPU's share (10 of 80 layers) of the Llama-3-70B-shaped RL step."""
+    layers, seqs, seq_len, d_model, n_kv, hd, bs, rope_theta = 10, 16, 8192, 8192, 8, 128, 16, 500000.0
 
 
 # ---------------------------------------------------------------------------
@@ -487,8 +499,324 @@ def run_e2e(args, patcher, dev, world):
             "ms_per_step": ms, "sample": f"{n_seqs} seqs x {args.layers} layers per GPU, pinned host buffers"}
 
 
+# ---------------------------------------------------------------------------
+# rl-dense workload: full-rank dW on k_proj / v_proj (tensor-core GEMM route)
+# ---------------------------------------------------------------------------
+DENSE_METRIC = "patched token·layers/s (Llama-70B shape, dense dW RL step)"
+DENSE_WORKLOAD = ("Llama-3-70B-shaped RL-step dense delta, one GPU's share: 10 of 80 layers, d=8192, 8 KV heads "
+                  "x 128, 16 seqs x 8192 tokens, bf16 stored X (post-norm), full-rank dW_K/dW_V Gaussian with "
+                  "||dW||/||W|| = 1e-3, RoPE (theta 5e5) on K, bf16 paged KV block 16, permuted block table")
+
+
+def dense_flops_per_unit() -> float:
+    G = DenseGeo
+    return 2.0 * G.d_model * 2 * G.n_kv * G.hd
+
+
+def make_dense_workload(n_layers, n_seqs, seq_len, device, seed):
+    import deltakv_b200 as dkv
+    from deltakv_b200 import ops
+
+    G = DenseGeo
+    gen = torch.Generator(device=device).manual_seed(seed)
+    rows = n_seqs * seq_len
+    d_kv = G.n_kv * G.hd
+    x = torch.empty(n_layers, rows, G.d_model, dtype=torch.bfloat16, device=device)
+    for l in range(n_layers):
+        x[l].normal_(generator=gen)
+    sigma = 1e-3 * 0.02  # ||dW|| / ||W|| = 1e-3 for W ~ N(0, 0.02^2)
+    dw_k = (torch.randn(n_layers, d_kv, G.d_model, generator=gen, device=device) * sigma).to(torch.bfloat16)
+    dw_v = (torch.randn(n_layers, d_kv, G.d_model, generator=gen, device=device) * sigma).to(torch.bfloat16)
+    blocks_per_seq = (seq_len + G.bs - 1) // G.bs
+    nb = n_seqs * blocks_per_seq
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(seed + 2)).to(torch.int32)
+    tables = perm.view(n_seqs, blocks_per_seq).to(device)
+    caches = []
+    for _ in range(n_layers):
+        c = torch.empty(2, nb, G.bs, G.n_kv, G.hd, dtype=torch.bfloat16, device=device)
+        c.normal_(generator=gen)
+        caches.append(c)
+    cu = torch.arange(0, n_seqs + 1, dtype=torch.int32, device=device) * seq_len
+    seqs = ops.SeqBatchTensors(cu_seqlens=cu, block_tables=tables, max_seq_len=seq_len)
+    rope = dkv.RotaryEmbedding(G.hd, max_seq=seq_len, base=G.rope_theta)
+    return dict(x=x, dw_k=dw_k, dw_v=dw_v, caches=caches, seqs=seqs, rope=rope, tables=tables)
+
+
+class DenseCpuSample:
+    """Bounded host sample of the dense route: (layer, 256-token chunk) items through the
+    oracle port of the reference's exact route with A = dW, B = I (one chunk per worker)."""
+
+    CHUNK = 256
+
+    def __init__(self, seed: int = 5):
+        from oracle import dense as OD
+        from oracle import exact as OX
+
+        G = DenseGeo
+        g = torch.Generator().manual_seed(seed)
+        d_kv = G.n_kv * G.hd
+        self.x = (torch.randn(self.CHUNK, G.d_model, generator=g)).to(torch.bfloat16).float().numpy()
+        sig = 1e-3 * 0.02
+        self.fk, self.fv = OD.dense_factors((torch.randn(d_kv, G.d_model, generator=g) * sig).numpy(),
+                                            (torch.randn(d_kv, G.d_model, generator=g) * sig).numpy())
+        self.rope = OX.rope_tables(G.hd, self.CHUNK, G.rope_theta)
+        self.nblk = self.CHUNK // G.bs
+        self.table = list(np.random.default_rng(seed).permutation(self.nblk))
+
+    def new_pages(self):
+        G = DenseGeo
+        rng = np.random.default_rng(0)
+        shape = (self.nblk, G.bs, G.n_kv, G.hd)
+        return (rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16),
+                rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16))
+
+    def patch_one(self, kp, vp) -> int:
+        from oracle import exact as OX
+
+        G = DenseGeo
+        dk, dv = OX.exact_kv_delta(self.x, self.fk, self.fv, G.n_kv, G.hd, self.rope)
+        OX.scatter_into_paged(dk, kp, self.table, G.bs, kind="bf16")
+        OX.scatter_into_paged(dv, vp, self.table, G.bs, kind="bf16")
+        return self.CHUNK
+
+    def run(self, threads: int, seconds: float | None = None, items: int | None = None):
+        from concurrent.futures import ThreadPoolExecutor
+
+        from threadpoolctl import threadpool_limits
+
+        pages = [self.new_pages() for _ in range(threads)]
+        counter = [0]
+        lock = threading.Lock()
+        deadline = None if seconds is None else time.perf_counter() + seconds
+
+        def worker(wi):
+            done = 0
+            while True:
+                with lock:
+                    if items is not None and counter[0] >= items:
+                        return done
+                    if deadline is not None and time.perf_counter() >= deadline:
+                        return done
+                    counter[0] += 1
+                done += self.patch_one(*pages[wi])
+
+        with threadpool_limits(1):
+            t0 = time.perf_counter()
+            with ThreadPoolExecutor(threads) as ex:
+                units = sum(ex.map(worker, range(threads)))
+            el = time.perf_counter() - t0
+        return units, el
+
+
+def dense_cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_dense_reference(args):
+    world, rank, _ = dist_setup(args)
+    if rank != 0:
+        return 0
+    threads = dense_cpu_threads()
+    sample = DenseCpuSample()
+    for _ in range(args.warmup):
+        sample.run(threads, items=threads)
+    units_tot, el_tot = 0, 0.0
+    for _ in range(args.steps):
+        u, el = sample.run(threads, items=threads)
+        units_tot += u
+        el_tot += el
+    value = units_tot / el_tot
+    line = {
+        "impl": "reference", "metric": DENSE_METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el_tot / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": DENSE_WORKLOAD, "step": f"{threads} (layer, {DenseCpuSample.CHUNK}-token chunk) "
+                   "items (bounded sample of the workload)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{threads} items per step, oracle numpy port of the reference's exact route "
+                                   "with A=dW, B=I (x @ dW^T, RoPE, scatter_into_paged)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_dense_ours(args):
+    import deltakv_b200 as dkv
+    from deltakv_b200 import ops
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    G = DenseGeo
+    wl = make_dense_workload(args.layers, args.seqs, args.seq_len, dev, seed=2000 + rank)
+    patcher = dkv.DensePatcher(G.d_model, G.n_kv, G.hd, rope=wl["rope"])
+    packed = torch.empty(args.layers, 2 * G.n_kv * G.hd, G.d_model, dtype=torch.bfloat16, device=dev)
+    kpages = [c[0] for c in wl["caches"]]
+    vpages = [c[1] for c in wl["caches"]]
+    units = args.layers * args.seqs * args.seq_len
+    stream = torch.cuda.current_stream()
+
+    def step(ev=None):
+        patcher.pack(wl["dw_k"], wl["dw_v"], out=packed)
+        if ev is not None:
+            ev[0].record(stream)
+        patcher.apply(wl["x"], packed, kpages, vpages, wl["seqs"])
+        if ev is not None:
+            ev[1].record(stream)
+
+    step()
+    torch.cuda.synchronize()
+    ops.status_word(dev).raise_if_set("bench warm-up")
+    for _ in range(max(0, args.warmup - 1)):
+        step()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t_start.record(stream)
+        for i in range(args.steps):
+            step(kev[i])
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = t_start.elapsed_time(t_end)
+    kern_ms = [a.elapsed_time(b) for a, b in kev]
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ops.status_word(dev).raise_if_set("bench timed region")
+    ms_step = ms / args.steps
+    value = units * world / (ms_step / 1e3)
+    kmean = sum(kern_ms) / len(kern_ms)
+    achieved = units * dense_flops_per_unit() / (kmean / 1e3) / 1e12
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    peak = peaks.get("bf16_tflops_sustained")
+    peak_kind = ("of measured (MEASURED_PEAKS.json bf16_tflops_sustained: a seconds-long step)" if peak
+                 else "of fallback (1400 TFLOP/s sustained)")
+    peak = peak or 1400.0
+    traffic = None
+    tfile = ROOT / "profiles" / "dense_patch_kernel.md"
+    if tfile.exists() and args.layers == G.layers and args.seqs == G.seqs and args.seq_len == G.seq_len:
+        for line in tfile.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch_full_workload:"):
+                traffic = int(line.split(":", 1)[1])
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_dense_e2e(args, patcher, dev, world)
+    del wl, kpages, vpages
+    torch.cuda.empty_cache()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = dense_cpu_threads()
+        sample = DenseCpuSample()
+        sample.run(threads, items=threads)
+        u, el = sample.run(threads, seconds=args.cpu_seconds)
+        cpu = {"value": u / el, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{u // DenseCpuSample.CHUNK} (layer, {DenseCpuSample.CHUNK}-token chunk) items in "
+                         f"{el:.1f} s (oracle numpy port of the reference's exact route with A=dW, B=I, "
+                         f"{threads} threads)"}
+    if rank == 0:
+        line = {
+            "metric": DENSE_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 tensor-core products, fp32 accumulate (bf16 X and pages)",
+            "data": "synthetic",
+            "config": {"workload": DENSE_WORKLOAD, "layers": args.layers, "seqs_per_gpu": args.seqs,
+                       "seq_len": args.seq_len, "units_per_step_per_gpu": units,
+                       "parallelism": f"layer shards x{world} (weak)",
+                       "l2": f"X {units * G.d_model * 2 / 1e9:.1f} GB per GPU >> 126 MB L2, no flush needed",
+                       "launches_per_step": 2},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
+                         "kernel": "dense_patch_kernel", "kernel_ms": kmean,
+                         "algorithmic_flops_per_unit": dense_flops_per_unit()},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def run_dense_e2e(args, patcher, dev, world):
+    """Same metric through DensePatcher with pinned host buffers: X, dW, tables and pages
+    copied in, pages copied back, every step (1 layer x 2 sequences per GPU)."""
+    from deltakv_b200 import ops
+
+    n_layers, n_seqs = 1, 2
+    cpu = make_dense_workload(n_layers, n_seqs, args.seq_len, dev, seed=78)
+    host = {k: cpu[k].cpu().pin_memory() for k in ("x", "dw_k", "dw_v", "tables")}
+    host["caches"] = torch.stack(cpu["caches"]).cpu().pin_memory()
+    del cpu
+    torch.cuda.empty_cache()
+    d = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
+    G = DenseGeo
+    packed = torch.empty(n_layers, 2 * G.n_kv * G.hd, G.d_model, dtype=torch.bfloat16, device=dev)
+    cu = torch.arange(0, n_seqs + 1, dtype=torch.int32, device=dev) * args.seq_len
+    stream = torch.cuda.current_stream()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = host["caches"].numel() * host["caches"].element_size()
+
+    def step():
+        for k, v in host.items():
+            d[k].copy_(v, non_blocking=True)
+        patcher.pack(d["dw_k"], d["dw_v"], out=packed)
+        seqs = ops.SeqBatchTensors(cu_seqlens=cu, block_tables=d["tables"], max_seq_len=args.seq_len)
+        patcher.apply(d["x"], packed, [c[0] for c in d["caches"]], [c[1] for c in d["caches"]], seqs)
+        host["caches"].copy_(d["caches"], non_blocking=True)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    n = 3
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    a.record(stream)
+    for _ in range(n):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / n
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    units = n_layers * n_seqs * args.seq_len * world
+    del d, host
+    torch.cuda.empty_cache()
+    return {"value": units / (ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": ms, "sample": f"{n_seqs} seqs x {n_layers} layer per GPU, pinned host buffers"}
+
+
 def main():
     args = parse()
+    dense = args.workload == "rl-dense"
+    for k, v in (("layers", DenseGeo.layers if dense else 32), ("seqs", DenseGeo.seqs if dense else 64),
+                 ("seq_len", DenseGeo.seq_len if dense else 4096)):
+        if getattr(args, k) is None:
+            setattr(args, k, v)
+    if dense:
+        return run_dense_reference(args) if args.impl == "reference" else run_dense_ours(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -403,6 +403,7 @@ def run_ours(args):
             if line.startswith("traffic_bytes_per_launch_full_workload:"):
                 traffic = int(line.split(":", 1)[1])
 
+    layer_errors = measure_layer_errors(args, wl["seqs"], kpages, vpages, step, dev, world)
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, patcher, dev, world)
@@ -430,11 +431,42 @@ def run_ours(args):
             "e2e": e2e,
             "gpu_launches": 2 * args.steps,
             "clocks": clk.summary(),
+            "layer_errors": layer_errors,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
     return 0
+
+
+def measure_layer_errors(args, seqs, kpages, vpages, step, dev, world):
+    """After the timed region: per-layer measured error (compose.py:147-163 formula) of one
+    more patch step on sequence 0 — the stale pages against the patched ones, i.e. the error a
+    cache would carry without the patch — then the NCCL all-gather of those scalars over the
+    ranks (the path's only collective)."""
+    from deltakv_b200 import metrics, ops
+
+    n = args.seq_len
+    one = ops.SeqBatchTensors(cu_seqlens=seqs.cu_seqlens[:2].clone(), block_tables=seqs.block_tables[:1].contiguous(),
+                              max_seq_len=n)
+    L_ = len(kpages)
+    nkv, hd = kpages[0].shape[2], kpages[0].shape[3]
+    stale_k = torch.empty(L_, n, nkv, hd, dtype=kpages[0].dtype, device=dev)
+    stale_v = torch.empty_like(stale_k)
+    for l in range(L_):
+        ops.gather_paged(kpages[l], one, stale_k[l])
+        ops.gather_paged(vpages[l], one, stale_v[l])
+    step()
+    local = metrics.measured_error_paged(kpages, vpages, stale_k, stale_v, one, check=True)
+    t0 = time.perf_counter()
+    gathered = metrics.gather_layer_errors(local)
+    torch.cuda.synchronize()
+    gather_ms = 1e3 * (time.perf_counter() - t0)
+    g = gathered.cpu()
+    return {"what": "per-layer relative KV change of one patch step on sequence 0 (stale vs patched)",
+            "max": float(g.max()), "mean": float(g.mean()), "ranks": world, "layers_per_rank": L_,
+            "collective": "all_gather_into_tensor (nccl)" if world > 1 else "none (single rank)",
+            "gather_wall_ms": gather_ms}
 
 
 def run_e2e(args, patcher, dev, world):

@@ -89,6 +89,68 @@ __global__ void __launch_bounds__(kThreads) gather_kernel(dkv_paged_cache cache,
   }
 }
 
+// Per-layer sums for the measured error of patched pages against fresh KV (the reference's
+// measured_error, src/deltakv/patches/compose.py:147-163): sums[2l] += sum (page - fresh)^2,
+// sums[2l+1] += sum fresh^2 over every token of every sequence.  One CTA per 16 tokens of a
+// (layer, sequence); fp32 partial sums per thread, one fp64 atomic pair per CTA.
+struct ErrLayers {
+  const void *base[DKV_MAX_LAYERS];
+};
+
+template <int PDT, int FDT>
+__global__ void __launch_bounds__(kThreads) error_sums_kernel(dkv_paged_cache cache, ErrLayers layers,
+                                                              const void *__restrict__ fresh, int64_t f_layer,
+                                                              int64_t f_row, int64_t f_head,
+                                                              dkv_seq_batch seqs, double *sums,
+                                                              int32_t *status) {
+  using PT = typename Elem<PDT>::T;
+  using FT = typename Elem<FDT>::T;
+  __shared__ float red[2][kThreads / 32];
+  const int l = blockIdx.z, b = blockIdx.y;
+  const int row0 = seqs.cu_seqlens[b];
+  const int len = seqs.cu_seqlens[b + 1] - row0;
+  const int hd = cache.head_dim;
+  const int row_elems = cache.n_heads * hd;
+  const PT *pages = static_cast<const PT *>(layers.base[l]);
+  const FT *fr = static_cast<const FT *>(fresh) + static_cast<int64_t>(l) * f_layer;
+  float s0 = 0.f, s1 = 0.f;
+  for (int k = 0; k < 16; ++k) {
+    const int i = blockIdx.x * 16 + k;
+    if (i >= len) break;
+    const int64_t off = page_row_offset(seqs, cache, b, i, status);
+    if (off < 0) continue;
+    const int64_t frow = static_cast<int64_t>(row0 + i) * f_row;
+    for (int e = threadIdx.x; e < row_elems; e += blockDim.x) {
+      const int h = e / hd, j = e - h * hd;
+      const float pv = Elem<PDT>::to_f(pages[off + h * cache.stride_head + j]);
+      const float fv = Elem<FDT>::to_f(fr[frow + h * f_head + j]);
+      const float dv = pv - fv;
+      s0 = fmaf(dv, dv, s0);
+      s1 = fmaf(fv, fv, s1);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+  }
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    red[0][w] = s0;
+    red[1][w] = s1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double a = 0.0, c = 0.0;
+    for (int i = 0; i < kThreads / 32; ++i) {
+      a += red[0][i];
+      c += red[1][i];
+    }
+    atomicAdd(sums + 2 * l, a);
+    atomicAdd(sums + 2 * l + 1, c);
+  }
+}
+
 bool valid_float_dtype(int dt) { return dt == DKV_F32 || dt == DKV_F16 || dt == DKV_BF16; }
 
 int check_common(const dkv_paged_cache *cache, const dkv_seq_batch *seqs) {
@@ -163,6 +225,42 @@ extern "C" int dkv_gather_paged(const dkv_paged_cache *cache, const dkv_seq_batc
   DKV_GATHER_CASE(DKV_F16, DKV_F32)
   DKV_GATHER_CASE(DKV_F32, DKV_F32)
 #undef DKV_GATHER_CASE
+  return DKV_ERR_UNSUPPORTED;
+}
+
+extern "C" int dkv_paged_error_sums(const dkv_paged_cache *pages, int32_t n_layers, const void *fresh,
+                                    int32_t fresh_dtype, int64_t fresh_layer_stride,
+                                    int64_t fresh_row_stride, int64_t fresh_head_stride,
+                                    const dkv_seq_batch *seqs, double *sums, int32_t *status,
+                                    dkv_stream_t stream) {
+  if (pages == nullptr || n_layers <= 0 || n_layers > DKV_MAX_LAYERS) return DKV_ERR_INVALID_ARGUMENT;
+  int rc = check_common(&pages[0], seqs);
+  if (rc != DKV_OK) return rc;
+  if (!valid_float_dtype(fresh_dtype)) return DKV_ERR_UNSUPPORTED;
+  if (seqs->n_seqs == 0 || seqs->max_seq_len == 0) return DKV_OK;
+  if (fresh == nullptr || sums == nullptr) return DKV_ERR_INVALID_ARGUMENT;
+  ErrLayers layers;
+  for (int l = 0; l < n_layers; ++l) {
+    if (pages[l].base == nullptr) return DKV_ERR_INVALID_ARGUMENT;
+    layers.base[l] = pages[l].base;
+  }
+  dim3 grid((seqs->max_seq_len + 15) / 16, seqs->n_seqs, n_layers);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+#define DKV_ERR_CASE(P, F)                                                                           \
+  if (pages[0].dtype == P && fresh_dtype == F) {                                                    \
+    error_sums_kernel<P, F><<<grid, kThreads, 0, st>>>(pages[0], layers, fresh, fresh_layer_stride, \
+                                                       fresh_row_stride, fresh_head_stride, *seqs,  \
+                                                       sums, status);                               \
+    DKV_CUDA_CHECK(cudaGetLastError());                                                             \
+    return DKV_OK;                                                                                  \
+  }
+  DKV_ERR_CASE(DKV_BF16, DKV_BF16)
+  DKV_ERR_CASE(DKV_BF16, DKV_F32)
+  DKV_ERR_CASE(DKV_F16, DKV_F16)
+  DKV_ERR_CASE(DKV_F16, DKV_F32)
+  DKV_ERR_CASE(DKV_F32, DKV_F32)
+  DKV_ERR_CASE(DKV_F32, DKV_BF16)
+#undef DKV_ERR_CASE
   return DKV_ERR_UNSUPPORTED;
 }
 

@@ -1,0 +1,103 @@
+"""Per-layer measured error of a patch and its cross-rank gather.
+
+``measured_error`` follows src/deltakv/patches/compose.py:147-163: for each layer,
+``(||K_p - K_f|| + ||V_p - V_f||) / (||K_f|| + ||V_f|| + 1e-8)`` and the maximum over layers.
+Here the sums run in one kernel launch per projection over every layer, reading the patched
+KV straight from its pages (no gather), and :func:`gather_layer_errors` is the path's only
+collective: each rank's per-layer scalars are all-gathered (NCCL over NVLink on GPUs, gloo on
+CPU tensors), so no KV crosses GPUs.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Sequence
+
+import torch
+from torch import Tensor
+
+from deltakv_b200 import _lib as L
+from deltakv_b200 import ops
+
+
+@dataclass(frozen=True)
+class ErrorEstimate:
+    """Field names of the reference's ErrorEstimate (src/deltakv/patches/compose.py)."""
+
+    relative_kv_l2: float
+    per_layer: tuple[float, ...]
+    measured: bool = True
+    notes: str = ""
+
+
+def _error_sums(pages: Sequence[Tensor], fresh: Tensor, seqs: ops.SeqBatchTensors, sums: Tensor,
+                status: ops.StatusWord | None) -> None:
+    n_layers = len(pages)
+    if fresh.ndim != 4 or fresh.shape[0] != n_layers:
+        raise ValueError("fresh must be [n_layers, rows, n_kv, head_dim] matching the page list")
+    if fresh.stride(3) != 1:
+        raise ValueError("fresh rows must be contiguous along head_dim")
+    ops._require_cuda(fresh, sums)
+    descs = (L.PagedCache * n_layers)(*[ops.paged_desc(p) for p in pages])
+    geo = lambda d: (d.dtype, d.block_size, d.n_heads, d.head_dim, d.stride_block, d.stride_slot, d.stride_head)
+    if any(geo(d) != geo(descs[0]) for d in descs):
+        raise ValueError("every layer's pages must share dtype, shape and strides")
+    rc = L.lib().dkv_paged_error_sums(descs, n_layers, fresh.data_ptr(), ops.dkv_dtype(fresh.dtype), fresh.stride(0),
+                                      fresh.stride(1), fresh.stride(2), C.byref(seqs.struct()), sums.data_ptr(),
+                                      status.ptr if status else None, ops.stream_ptr())
+    L.check(rc, "dkv_paged_error_sums")
+
+
+def measured_error_paged(k_pages: Sequence[Tensor], v_pages: Sequence[Tensor], k_fresh: Tensor, v_fresh: Tensor,
+                         seqs: ops.SeqBatchTensors, *, check: bool = False) -> Tensor:
+    """Per-layer relative error ``[n_layers]`` (fp64, on the device) of paged K/V against
+    dense fresh K/V ``[n_layers, rows, n_kv, head_dim]`` (rows = the tokens of ``seqs``)."""
+    dev = k_fresh.device
+    n_layers = len(k_pages)
+    if len(v_pages) != n_layers:
+        raise ValueError("k_pages and v_pages must cover the same layers")
+    sums = torch.zeros(2, n_layers, 2, dtype=torch.float64, device=dev)
+    st = ops.status_word(dev)
+    _error_sums(k_pages, k_fresh, seqs, sums[0], st)
+    _error_sums(v_pages, v_fresh, seqs, sums[1], st)
+    if check:
+        st.raise_if_set("measured_error_paged")
+    num = sums[0, :, 0].sqrt() + sums[1, :, 0].sqrt()
+    den = sums[0, :, 1].sqrt() + sums[1, :, 1].sqrt() + 1e-8
+    return num / den
+
+
+def measured_error(patched, fresh) -> ErrorEstimate:
+    """Drop-in for ``deltakv.patches.compose.measured_error`` on dense CUDA KV caches
+    (``.k`` / ``.v`` of shape ``[n_layers, seq, n_kv, head_dim]``)."""
+    pk, pv, fk, fv = patched.k, patched.v, fresh.k, fresh.v
+    n_layers, seq, n_kv, hd = pk.shape
+    if seq == 0:
+        per = [0.0] * n_layers
+        return ErrorEstimate(relative_kv_l2=0.0, per_layer=tuple(per))
+    dev = pk.device
+    # each layer's dense [seq, n_kv, hd] viewed as one block of `seq` slots
+    seqs = ops.SeqBatchTensors.single(seq, [0], dev)
+    kp = [pk[l].unsqueeze(0) for l in range(n_layers)]
+    vp = [pv[l].unsqueeze(0) for l in range(n_layers)]
+    per = measured_error_paged(kp, vp, fk, fv, seqs, check=True).tolist()
+    return ErrorEstimate(relative_kv_l2=float(max(per)) if per else 0.0, per_layer=tuple(per))
+
+
+def gather_layer_errors(local: Tensor, group=None) -> Tensor:
+    """All-gather every rank's per-layer error scalars: ``[n_local]`` -> ``[world, n_local]``.
+
+    One ``all_gather_into_tensor`` on the default (or given) process group: NCCL when
+    ``local`` is on a GPU, gloo for CPU tensors.  Every rank must pass the same ``n_local``
+    (pad with NaN for layers a rank does not hold).
+    """
+    import torch.distributed as dist
+
+    if not dist.is_available() or not dist.is_initialized():
+        return local.reshape(1, -1).clone()
+    world = dist.get_world_size(group)
+    flat = local.reshape(-1).contiguous()
+    out = torch.empty(world * flat.numel(), dtype=flat.dtype, device=flat.device)
+    dist.all_gather_into_tensor(out, flat, group=group)
+    return out.view(world, -1)

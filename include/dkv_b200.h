@@ -122,6 +122,19 @@ int dkv_gather_paged(const dkv_paged_cache *cache, const dkv_seq_batch *seqs, vo
                      int32_t *status, dkv_stream_t stream);
 
 /*
+ * Per-layer sums of the measured patch error (compose.py:147-163 measured_error): for layer l
+ * (pages[l], same geometry as pages[0]) and every token of `seqs`,
+ *   sums[2l]   += sum (page - fresh)^2,   sums[2l+1] += sum fresh^2
+ * with fresh element (l, row, head, dim) at fresh + l*fresh_layer_stride + row*fresh_row_stride
+ * + head*fresh_head_stride + dim.  The caller zeroes sums; the per-layer error is
+ * (sqrt(sK0) + sqrt(sV0)) / (sqrt(sK1) + sqrt(sV1) + 1e-8) over a K call and a V call.
+ */
+int dkv_paged_error_sums(const dkv_paged_cache *pages, int32_t n_layers, const void *fresh,
+                         int32_t fresh_dtype, int64_t fresh_layer_stride, int64_t fresh_row_stride,
+                         int64_t fresh_head_stride, const dkv_seq_batch *seqs, double *sums,
+                         int32_t *status, dkv_stream_t stream);
+
+/*
  * Stored-activation writer.  The reference keeps HiddenSnapshot.h in the model dtype
  * (model.py:157-164; config.py:31 names float16 storage but nothing applies it).  This
  * quantises rows of x (F32/F16/BF16) into out (DKV_F16 with a power-of-two row scale, or

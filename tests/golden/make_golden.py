@@ -30,6 +30,7 @@ Cases:
                    the reference's exact route with LowRankFactors(A=dW, B=I, scale=1):
                    RMSNorm, exact_kv_patch, materialize, scatter_into_paged over a ragged
                    batch of bf16 activations into bf16 pages.
+  errors.npz       patches.compose.measured_error of a patched vs a fresh KVCache (per layer).
   kivi.npz         metrics._minmax_quantize (4 bits, group 32) on the last dimension (the
                    per-token V grouping) and on the transposed tensor (per-channel K
                    grouping), plus kivi_noise_floor on a small KVCache.
@@ -362,6 +363,18 @@ def main(ref_src: str) -> None:
                     f"{tag}_basis": B.numpy(), f"{tag}_use_basis": np.int32(use_basis), f"{tag}_rank": np.int32(rr),
                     f"{tag}_corr": corr.numpy(), f"{tag}_sub": subsp.numpy(), f"{tag}_orth": orth.numpy()})
     np.savez_compressed(OUT / "subspace.npz", **sub)
+
+    # ----------------------------------------------------------------- errors
+    from deltakv.patches.compose import measured_error
+    from deltakv.patches.tensors import KVCache as RefKV
+
+    ge = torch.Generator().manual_seed(8)
+    fk, fv = torch.randn(3, 50, 2, 16, generator=ge), torch.randn(3, 50, 2, 16, generator=ge)
+    pk = fk + 0.01 * torch.randn(3, 50, 2, 16, generator=ge) * torch.tensor([1.0, 3.0, 0.0]).view(3, 1, 1, 1)
+    pv = fv + 0.02 * torch.randn(3, 50, 2, 16, generator=ge)
+    est = measured_error(RefKV(k=pk, v=pv, version=WeightVersion(id="p")), RefKV(k=fk, v=fv, version=WeightVersion(id="f")))
+    np.savez_compressed(OUT / "errors.npz", pk=pk.numpy(), pv=pv.numpy(), fk=fk.numpy(), fv=fv.numpy(),
+                        per_layer=np.array(est.per_layer, np.float64), rel=np.float64(est.relative_kv_l2))
 
     # ------------------------------------------------------------------- kivi
     from deltakv.metrics import _minmax_quantize, kivi_noise_floor

@@ -1,0 +1,57 @@
+"""Per-layer measured error on the GPU vs the reference's golden values and the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from deltakv_b200 import metrics, ops
+from deltakv_b200.types import KVCache
+from oracle.metrics import measured_error as oracle_error
+from tests.conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+
+def test_measured_error_golden(cuda):
+    g = golden("errors")
+    t = lambda a: torch.from_numpy(a).to(cuda)
+    est = metrics.measured_error(KVCache(k=t(g["pk"]), v=t(g["pv"])), KVCache(k=t(g["fk"]), v=t(g["fv"])))
+    assert np.allclose(est.per_layer, g["per_layer"], rtol=1e-5, atol=1e-9)
+    assert abs(est.relative_kv_l2 - float(g["rel"])) <= 1e-5 * float(g["rel"])
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_measured_error_paged_matches_oracle(cuda, dtype):
+    gen = torch.Generator().manual_seed(3)
+    L_, n_kv, hd, bs = 3, 2, 64, 16
+    lens = [5, 40, 0, 33]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    rows = int(cu[-1])
+    need = [(n + bs - 1) // bs for n in lens]
+    nb = sum(need) + 2
+    perm = torch.randperm(nb, generator=gen).numpy().astype(np.int32)
+    tables = np.zeros((len(lens), max(need)), np.int32)
+    k = 0
+    for b, n in enumerate(need):
+        tables[b, :n] = perm[k:k + n]
+        k += n
+    caches = [torch.randn(2, nb, bs, n_kv, hd, generator=gen).to(dtype) for _ in range(L_)]
+    fresh_k = torch.randn(L_, rows, n_kv, hd, generator=gen).to(dtype)
+    fresh_v = torch.randn(L_, rows, n_kv, hd, generator=gen).to(dtype)
+    # dense patched view through the block tables (oracle input)
+    pk = np.zeros((L_, rows, n_kv, hd), np.float32)
+    pv = np.zeros_like(pk)
+    for l in range(L_):
+        for b, n in enumerate(lens):
+            for i in range(n):
+                pk[l, cu[b] + i] = caches[l][0, tables[b, i // bs], i % bs].float().numpy()
+                pv[l, cu[b] + i] = caches[l][1, tables[b, i // bs], i % bs].float().numpy()
+    _, want = oracle_error(pk, pv, fresh_k.float().numpy(), fresh_v.float().numpy())
+    seqs = ops.SeqBatchTensors(cu_seqlens=torch.from_numpy(cu).to(cuda), block_tables=torch.from_numpy(tables).to(cuda),
+                               max_seq_len=max(lens))
+    dev_caches = [c.to(cuda) for c in caches]
+    got = metrics.measured_error_paged([c[0] for c in dev_caches], [c[1] for c in dev_caches], fresh_k.to(cuda),
+                                       fresh_v.to(cuda), seqs, check=True).cpu().numpy()
+    assert np.allclose(got, want, rtol=1e-5)

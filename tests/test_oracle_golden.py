@@ -209,3 +209,12 @@ def test_dense_paged_golden():
             assert np.linalg.norm(a - b) / np.linalg.norm(b) < 1e-5
             assert (ours == ref).mean() > 0.995
             assert not np.array_equal(ref, base)  # the case patches something
+
+
+def test_measured_error_golden():
+    from oracle.metrics import measured_error
+
+    g = golden("errors")
+    rel, per = measured_error(g["pk"], g["pv"], g["fk"], g["fv"])
+    assert np.allclose(per, g["per_layer"], rtol=1e-5, atol=1e-9)
+    assert abs(rel - float(g["rel"])) <= 1e-5 * float(g["rel"])

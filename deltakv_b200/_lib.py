@@ -46,6 +46,8 @@ EXPORTED = (
     "dkv_kivi_quantize",
     "dkv_kivi_dequantize",
     "dkv_kivi_patch",
+    "dkv_kivi_subspace_workspace_bytes",
+    "dkv_kivi_subspace_correct",
     "dkv_subspace_workspace_bytes",
     "dkv_subspace_correct",
     "dkv_subspace_correct_noalloc",
@@ -150,6 +152,22 @@ class KiviCache(C.Structure):
         ("n_tokens", C.c_int64),
         ("d", C.c_int64),
         ("mode", C.c_int32),
+    ]
+
+
+class KiviSubspaceProblem(C.Structure):
+    _fields_ = [
+        ("base", KiviCache),
+        ("out", KiviCache),
+        ("fresh", C.c_void_p),
+        ("fresh_dtype", C.c_int32),
+        ("fresh_row_stride", C.c_int64),
+        ("probe_index", C.c_void_p),
+        ("n_probes", C.c_int64),
+        ("basis", C.c_void_p),
+        ("rank", C.c_int32),
+        ("subspace_out", C.c_void_p),
+        ("orth_mu_out", C.c_void_p),
     ]
 
 
@@ -260,6 +278,10 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_kivi_dequantize.argtypes = [C.POINTER(KiviCache), P, I32, I64, P]
     lib.dkv_kivi_patch.restype = C.c_int
     lib.dkv_kivi_patch.argtypes = [C.POINTER(KiviCache), P, I32, I64, C.POINTER(KiviCache), P]
+    lib.dkv_kivi_subspace_workspace_bytes.restype = C.c_int
+    lib.dkv_kivi_subspace_workspace_bytes.argtypes = [C.POINTER(KiviSubspaceProblem), I32, C.POINTER(C.c_int64)]
+    lib.dkv_kivi_subspace_correct.restype = C.c_int
+    lib.dkv_kivi_subspace_correct.argtypes = [C.POINTER(KiviSubspaceProblem), I32, P, I64, P, P]
     lib.dkv_subspace_workspace_bytes.restype = C.c_int
     lib.dkv_subspace_workspace_bytes.argtypes = [I64, I64, I32, C.POINTER(C.c_int64)]
     lib.dkv_subspace_correct.restype = C.c_int

@@ -9,42 +9,16 @@
 // IEEE fp32 operation (explicit _rn intrinsics, no contraction), so results are bit-exact
 // against the numpy restatement.
 #include "dkv_common.cuh"
+#include "kivi_math.cuh"
 
 namespace dkv {
 namespace kivi {
-
-constexpr int kG = 32;
 
 struct Cache {
   uint8_t *codes;
   __half *scale, *zero;
   int64_t crs, szrs, n, d;
 };
-
-__device__ __forceinline__ void quant_group(const float (&x)[kG], int cnt, uint8_t (&q)[kG], __half &s16,
-                                            __half &z16) {
-  float lo = x[0], hi = x[0];
-#pragma unroll
-  for (int i = 1; i < kG; ++i)
-    if (i < cnt) {
-      lo = fminf(lo, x[i]);
-      hi = fmaxf(hi, x[i]);
-    }
-  const float rng = fmaxf(__fsub_rn(hi, lo), 1e-8f);
-  s16 = __float2half_rn(__fdiv_rn(rng, 15.f));
-  z16 = __float2half_rn(lo);
-  const float s = __half2float(s16), z = __half2float(z16);
-#pragma unroll
-  for (int i = 0; i < kG; ++i) {
-    float v = 0.f;
-    if (s > 0.f) v = fminf(fmaxf(rintf(__fdiv_rn(__fsub_rn(x[i], z), s)), 0.f), 15.f);
-    q[i] = static_cast<uint8_t>(v);
-  }
-}
-
-__device__ __forceinline__ float deq(uint32_t q, float s, float z) {
-  return __fadd_rn(__fmul_rn(static_cast<float>(q), s), z);
-}
 
 // ---- per-token groups (V): one thread per (token, 32-channel group) ----
 // SRC: 0 = dense x, 1 = dequantised base (+ dense delta when delta != null)

@@ -101,3 +101,86 @@ def patch(base: KiviTensor, delta: Tensor | None, out: KiviTensor | None = None)
     rc = L.lib().dkv_kivi_patch(C.byref(bd), dptr, ddt, drs, C.byref(od), ops.stream_ptr())
     L.check(rc, "dkv_kivi_patch")
     return out
+
+
+@dataclass
+class SubspaceProblem:
+    """One int4 view to correct: a layer's K or V of one adapter.
+
+    ``basis`` ``[d, r]`` is the column space (V: the adapter's LoRA ``B``); ``None`` takes
+    the top-``rank`` (at least 1) right singular vectors of the probe residual when there are
+    two or more probes, as the reference's K path does (``svd_basis``,
+    src/deltakv/patches/subspace.py:37-42, 91-93); with fewer probes the correction is the
+    mean shift alone.
+    ``out=None`` corrects ``base`` in place.
+    """
+
+    base: KiviTensor
+    fresh: Tensor
+    probe_index: Tensor
+    basis: Tensor | None = None
+    rank: int = 8
+    out: KiviTensor | None = None
+
+
+def probe_residual(base: KiviTensor, fresh: Tensor, probe_index: Tensor) -> Tensor:
+    """``fresh[P] - dequant(base)[P]`` as fp32 ``[|P|, d]``."""
+    rows = probe_index.to(device=fresh.device, dtype=torch.long)
+    reused = dequantize(base)
+    return _rows(fresh).index_select(0, rows).float() - reused.index_select(0, rows)
+
+
+def subspace_correct(problems: list[SubspaceProblem], *, stats: bool = False, check: bool = True):
+    """Batched subspace correction of int4 caches: one launch per pass for every problem.
+
+    Returns, per problem, ``(out, subspace, orth_mu)`` (the last two ``[d]`` fp32, or None
+    unless ``stats``) — the int4 form of ``subspace_correct``'s ``(corrected, subspace,
+    orth_mu)``.
+    """
+    from deltakv_b200 import subspace as dense_sub
+
+    if not problems:
+        return []
+    dev = problems[0].fresh.device
+    keep = []  # tensors that must stay alive until the launches are queued
+    descs = []
+    results = []
+    for pb in problems:
+        fresh = _rows(pb.fresh)
+        ops._require_cuda(fresh, pb.probe_index)
+        n, d = pb.base.n_tokens, pb.base.d
+        if fresh.shape != (n, d):
+            raise ValueError(f"fresh {tuple(fresh.shape)} does not match the int4 base ({n}, {d})")
+        probes = pb.probe_index.to(device=dev, dtype=torch.int32).contiguous()
+        basis = pb.basis
+        rank = int(pb.rank)
+        if basis is None and probes.numel() >= 2:  # reference: svd_basis keeps at least rank 1
+            r_eff = min(rank, max(1, probes.numel() - 1), d)
+            basis = dense_sub.svd_basis(probe_residual(pb.base, fresh, probes), r_eff)
+        if basis is not None:
+            if basis.shape[0] != d:
+                raise ValueError(f"basis d={basis.shape[0]} != kv d={d}")
+            basis = basis.to(device=dev, dtype=torch.float32).contiguous()
+            rank = basis.shape[1]
+        else:
+            rank = 0
+        out = pb.out if pb.out is not None else pb.base
+        sub = torch.empty(d, dtype=torch.float32, device=dev) if stats else None
+        mu = torch.empty(d, dtype=torch.float32, device=dev) if stats else None
+        keep += [fresh, probes, basis, sub, mu]
+        descs.append(L.KiviSubspaceProblem(
+            base=pb.base.desc(), out=out.desc(), fresh=fresh.data_ptr(), fresh_dtype=ops.dkv_dtype(fresh.dtype),
+            fresh_row_stride=fresh.stride(0), probe_index=probes.data_ptr(), n_probes=probes.numel(),
+            basis=ops.ptr(basis), rank=rank, subspace_out=ops.ptr(sub), orth_mu_out=ops.ptr(mu)))
+        results.append((out, sub, mu))
+    arr = (L.KiviSubspaceProblem * len(descs))(*descs)
+    nbytes = C.c_int64()
+    L.check(L.lib().dkv_kivi_subspace_workspace_bytes(arr, len(descs), C.byref(nbytes)),
+            "dkv_kivi_subspace_workspace_bytes")
+    ws = torch.empty(max(nbytes.value, 1), dtype=torch.uint8, device=dev)
+    st = ops.status_word(dev)
+    rc = L.lib().dkv_kivi_subspace_correct(arr, len(descs), ws.data_ptr(), ws.numel(), st.ptr, ops.stream_ptr())
+    L.check(rc, "dkv_kivi_subspace_correct")
+    if check:
+        st.raise_if_set("kivi.subspace_correct")
+    return results

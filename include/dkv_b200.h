@@ -330,6 +330,37 @@ int dkv_kivi_patch(const dkv_kivi_cache *base, const void *delta, int32_t delta_
 /* ---- subspace route -------------------------------------------------------- */
 
 /*
+ * Subspace correction of a KIVI int4 cache (the multi-adapter maintenance step): for each
+ * problem (one layer's K or V of one adapter view), reused = dequant(base), then exactly
+ * subspace_correct (patches/subspace.py:45-106) — R = fresh - reused, codes =
+ * solve(B^T B + 1e-6 I, (R B)^T)^T, orth_mu = mean_P(R - codes B^T),
+ * w = min(||R|| / mean ||R||, 1), corr = reused + codes B^T + w orth_mu, corr[P] = fresh[P] —
+ * and out = KIVI-quantised corr (same grouping as base; out may be base itself).  Without a
+ * basis, or with no probe, corr = reused + w mean_P(R) as in the reference.  Probe indices
+ * are deduplicated.  All problems of one call share d (a multiple of 64) and the fresh
+ * dtype; at most 128 problems, ranks <= 64.  The basis products run on tensor cores with
+ * bf16 operands (the basis, R and the codes rounded to bf16) and fp32 accumulation.
+ */
+typedef struct dkv_kivi_subspace_problem {
+  dkv_kivi_cache base; /* reused KV, int4 */
+  dkv_kivi_cache out;  /* corrected KV, int4, same mode and size */
+  const void *fresh;   /* [n_tokens, d], row stride fresh_row_stride elements */
+  int32_t fresh_dtype; /* DKV_F32 / DKV_F16 / DKV_BF16 */
+  int64_t fresh_row_stride;
+  const int32_t *probe_index;
+  int64_t n_probes;
+  const float *basis; /* [d, rank] fp32 row-major, or NULL */
+  int32_t rank;
+  float *subspace_out, *orth_mu_out; /* optional [d] fp32 */
+} dkv_kivi_subspace_problem;
+
+int dkv_kivi_subspace_workspace_bytes(const dkv_kivi_subspace_problem *problems, int32_t n_problems,
+                                      int64_t *bytes);
+int dkv_kivi_subspace_correct(const dkv_kivi_subspace_problem *problems, int32_t n_problems,
+                              void *workspace, int64_t workspace_bytes, int32_t *status,
+                              dkv_stream_t stream);
+
+/*
  * One subspace_correct problem (subspace.py:45-106) on [n_tokens, d] views of the reused
  * and fresh K or V (d = n_kv*head_dim; row strides in elements):
  *   R = fresh - reused; codes = (R B)(B^T B + 1e-6 I)^-1; fitted = codes B^T;

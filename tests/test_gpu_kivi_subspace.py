@@ -1,0 +1,146 @@
+"""Batched subspace correction of KIVI int4 caches on the GPU vs the oracle composition
+(oracle KIVI dequantise -> oracle subspace_correct -> oracle KIVI quantise).
+
+The kernel rounds the basis, the residual and the codes to bf16 as tensor-core operands,
+so its corrected values differ from the fp32 oracle by ~1e-3 of the fitted part — far
+below the int4 step.  Tolerances (stated per check below): requantised codes equal to the
+oracle's for >= 97 % of elements, fp16 scales within 5e-3 relative of the oracle's (their
+fp16 rounding flips on such small differences, so bit equality is not expected), dequantised
+output within 0.5 step (+1e-3 of the value range) of the oracle's fp32 corrected KV, probes
+exact up to the int4 step, orth_mu and subspace within 2e-2 relative (L2) plus 2e-3 of the
+mean residual norm (both are means of per-token quantities that largely cancel, so their
+bf16-operand error is set by the per-token scale, not by their own size).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from deltakv_b200 import kivi as K
+from oracle import kivi as OK
+from oracle import subspace as OS
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(gen, n, n_kv, hd, r, mode, probe_ratio=0.1, drift=0.05):
+    d = n_kv * hd
+    base_f = torch.randn(n, d, generator=gen)
+    B = torch.randn(d, max(r, 1), generator=gen) / d ** 0.5
+    codes = torch.randn(n, max(r, 1), generator=gen) * 0.3
+    fresh = base_f + codes @ B.T + drift * torch.randn(d, generator=gen) + 0.01 * torch.randn(n, d, generator=gen)
+    n_p = max(0, int(round(probe_ratio * n)))
+    probes = torch.unique(torch.cat([torch.zeros(1, dtype=torch.long), torch.randperm(n, generator=gen)[:n_p]]))
+    c, s, z = OK.quantize(base_f.numpy(), mode)
+    return dict(d=d, n_kv=n_kv, hd=hd, c=c, s=s, z=z, fresh=fresh, probes=probes, B=B[:, :r] if r else None, mode=mode)
+
+
+def _oracle(cs):
+    reused = OK.dequantize(cs["c"], cs["s"], cs["z"], cs["mode"])
+    n = reused.shape[0]
+    corr, sub, mu = OS.subspace_correct(reused.reshape(n, cs["n_kv"], cs["hd"]),
+                                        cs["fresh"].numpy().reshape(n, cs["n_kv"], cs["hd"]),
+                                        cs["probes"].numpy(), basis=None if cs["B"] is None else cs["B"].numpy(),
+                                        rank=0 if cs["B"] is None else cs["B"].shape[1])
+    corr = corr.reshape(n, -1)
+    return corr, sub, mu, OK.quantize(corr, cs["mode"])
+
+
+def _device_base(cs, dev):
+    kt = K.KiviTensor(torch.from_numpy(cs["c"]).to(dev), torch.from_numpy(cs["s"]).to(dev),
+                      torch.from_numpy(cs["z"]).to(dev), cs["mode"])
+    return kt
+
+
+def _check(cs, out, sub, mu, tag):
+    corr, osub, omu, (oc, osc, oz) = _oracle(cs)
+    got_c = out.codes.cpu().numpy()
+    got_s = out.scale.cpu().numpy()
+    got_z = out.zero.cpu().numpy()
+    eq_codes = (OK.unpack_nibbles(got_c) == OK.unpack_nibbles(oc)).mean()
+    assert eq_codes >= 0.97, (tag, eq_codes)
+    gs, os_ = got_s.astype(np.float32), osc.astype(np.float32)
+    assert (np.abs(gs - os_) <= 5e-3 * np.abs(os_) + 1e-7).all(), (tag, float(np.abs(gs - os_).max()))
+    deq = OK.dequantize(got_c, got_s, got_z, cs["mode"])
+    n, d = deq.shape
+    if cs["mode"] == "v":
+        step = np.repeat(got_s.astype(np.float32), 32, axis=1)
+    else:
+        step = np.repeat(got_s.astype(np.float32), 32, axis=0)[:n]
+    span = float(np.abs(corr).max())
+    assert (np.abs(deq - corr) <= 0.5 * step * 1.01 + 1e-3 * span).all(), tag
+    if sub is not None and cs["B"] is not None and cs["probes"].numel() > 0:
+        reused = OK.dequantize(cs["c"], cs["s"], cs["z"], cs["mode"])
+        mean_dist = float(np.linalg.norm(cs["fresh"].numpy() - reused, axis=1).mean())
+        for got, want in ((mu.cpu().numpy(), omu), (sub.cpu().numpy(), osub)):
+            err = float(np.linalg.norm(got - want))
+            assert err < 2e-2 * np.linalg.norm(want) + 2e-3 * mean_dist, (tag, err, float(np.linalg.norm(want)))
+
+
+@pytest.mark.parametrize("mode", ["v", "k"])
+@pytest.mark.parametrize("n,n_kv,hd,r,fdt,inplace", [
+    (300, 2, 64, 8, torch.float32, False),
+    (1000, 8, 128, 16, torch.bfloat16, True),
+    (77, 4, 32, 64, torch.float32, False),
+    (256, 1, 64, 48, torch.float16, False),
+    (130, 2, 64, 0, torch.float32, False),     # one probe, no basis: mean shift only
+])
+def test_kivi_subspace_matches_oracle(cuda, mode, n, n_kv, hd, r, fdt, inplace):
+    gen = torch.Generator().manual_seed(n * 7 + r + (mode == "k"))
+    cs = _case(gen, n, n_kv, hd, r, mode, probe_ratio=0.1 if r else 0.0)
+    if fdt != torch.float32:  # the oracle sees exactly the values the kernel reads
+        cs["fresh"] = cs["fresh"].to(fdt).float()
+    base = _device_base(cs, cuda)
+    out = None if inplace else K.KiviTensor.empty(n, cs["d"], mode, cuda)
+    pb = K.SubspaceProblem(base=base, fresh=cs["fresh"].to(fdt).to(cuda), probe_index=cs["probes"].to(cuda),
+                           basis=cs["B"].to(cuda) if cs["B"] is not None else None, rank=r, out=out)
+    (o, sub, mu), = K.subspace_correct([pb], stats=True)
+    torch.cuda.synchronize()
+    _check(cs, o, sub, mu, (mode, n, r))
+
+
+def test_kivi_subspace_batch_of_mixed_problems(cuda):
+    """K and V views of several layers with different lengths and ranks in one call."""
+    gen = torch.Generator().manual_seed(5)
+    specs = [(500, 4, 64, 8, "v"), (500, 4, 64, 8, "k"), (97, 4, 64, 32, "v"), (64, 4, 64, 16, "k"),
+             (1, 4, 64, 8, "v"), (333, 4, 64, 0, "k")]
+    cases, probs = [], []
+    for n, n_kv, hd, r, mode in specs:
+        cs = _case(gen, n, n_kv, hd, r, mode)
+        cases.append(cs)
+        probs.append(K.SubspaceProblem(base=_device_base(cs, cuda), fresh=cs["fresh"].to(cuda),
+                                       probe_index=cs["probes"].to(cuda),
+                                       basis=cs["B"].to(cuda) if cs["B"] is not None else None, rank=r,
+                                       out=K.KiviTensor.empty(n, cs["d"], mode, cuda)))
+    res = K.subspace_correct(probs, stats=True)
+    torch.cuda.synchronize()
+    for i, (cs, (o, sub, mu)) in enumerate(zip(cases, res)):
+        _check(cs, o, sub, mu, i)
+
+
+def test_kivi_subspace_no_probes_and_svd_basis(cuda):
+    gen = torch.Generator().manual_seed(6)
+    # no probes: reference keeps reused (w * 0) -> output equals the requantised base
+    cs = _case(gen, 200, 2, 64, 8, "v", probe_ratio=0.0)
+    cs["probes"] = torch.zeros(0, dtype=torch.long)
+    base = _device_base(cs, cuda)
+    (o, _, _), = K.subspace_correct([K.SubspaceProblem(base=base, fresh=cs["fresh"].to(cuda),
+                                                       probe_index=cs["probes"].to(cuda), basis=cs["B"].to(cuda),
+                                                       rank=8, out=K.KiviTensor.empty(200, cs["d"], "v", cuda))])
+    _check(cs, o, None, None, "no-probes")
+    # K path with the basis from the probe residual's SVD (basis=None, rank=r): compare with
+    # the oracle given the same basis
+    cs = _case(gen, 400, 2, 64, 8, "k")
+    base = _device_base(cs, cuda)
+    fresh = cs["fresh"].to(cuda)
+    res = K.probe_residual(base, fresh, cs["probes"].to(cuda))
+    from deltakv_b200.subspace import svd_basis
+    basis = svd_basis(res, 8)
+    cs["B"] = basis.cpu()
+    (o, sub, mu), = K.subspace_correct([K.SubspaceProblem(base=base, fresh=fresh, probe_index=cs["probes"].to(cuda),
+                                                          basis=None, rank=8,
+                                                          out=K.KiviTensor.empty(400, cs["d"], "k", cuda))],
+                                       stats=True)
+    _check(cs, o, sub, mu, "svd")

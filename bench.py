@@ -8,6 +8,7 @@ folded in) into bf16 paged K/V (block 16, permuted block table), RoPE on K.
     python bench.py [--gpus N --steps K --warmup W]          # this implementation
     python bench.py --impl reference ...                       # CPU reference arm
     python bench.py --workload rl-dense ...                    # dense-dW (RL step) route
+    python bench.py --workload multi-lora-kivi ...             # int4 KIVI subspace route
 
 The rl-dense workload is one GPU's share of the Llama-3-70B-shaped RL step (10 of 80
 layers, d=8192, 8 KV heads x 128, 16 seqs x 8192 tokens, bf16 X, full-rank dW_K / dW_V at
@@ -50,7 +51,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="llama8b-exact", choices=["llama8b-exact", "rl-dense"])
+    ap.add_argument("--workload", default="llama8b-exact", choices=["llama8b-exact", "rl-dense", "multi-lora-kivi"])
+    ap.add_argument("--adapters", type=int, default=8)
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--seqs", type=int, default=None)
     ap.add_argument("--seq-len", type=int, default=None)
@@ -840,8 +842,261 @@ def run_dense_e2e(args, patcher, dev, world):
             "ms_per_step": ms, "sample": f"{n_seqs} seqs x {n_layers} layer per GPU, pinned host buffers"}
 
 
+
+# ---------------------------------------------------------------------------
+# multi-lora-kivi workload: int4 KIVI shared prefix corrected per adapter view
+# ---------------------------------------------------------------------------
+KIVI_METRIC = "patched token·layers/s (Llama-8B shape, int4 KIVI prefix, subspace route per adapter view)"
+KIVI_WORKLOAD = ("Multi-LoRA shared prefix on the Llama-3-8B shape: 32 layers, 8 KV heads x 128, one 32768-token "
+                 "prefix stored KIVI int4 (K per-channel, V per-token, group 32, fp16 scale/zero); adapter views "
+                 "with k/v ranks {8,8,16,16,32,32,64,64}; per view and layer: K basis = top-r right singular "
+                 "subspace of the probe residual, V basis = the adapter's LoRA B; probes 10 %; dequant -> subspace "
+                 "correction -> requant into the view's own int4 cache")
+KIVI_BYTES_PER_UNIT = 1024 + 256 + 4096 + 1024 + 256  # base int4 K+V, scale/zero, fresh bf16 K+V, out int4, scale/zero
+KIVI_RANKS = (8, 8, 16, 16, 32, 32, 64, 64)
+
+
+class KiviGeo:
+    layers, seq_len, n_kv, hd, probe_ratio = 32, 32768, 8, 128, 0.10
+
+
+def make_kivi_workload(args, device, rank_ids):
+    """Base int4 prefix (shared), and per adapter view: fresh bf16 K/V per layer, V basis,
+    probes.  fresh = dequant(base) + rank-r structure + 10 % drift on the non-probes."""
+    from deltakv_b200 import kivi as K
+
+    G = KiviGeo
+    n, d = args.seq_len, G.n_kv * G.hd
+    gen = torch.Generator(device=device).manual_seed(4000)
+    base = []
+    for _ in range(args.layers):
+        kv = []
+        for mode in ("k", "v"):
+            x = torch.randn(n, d, generator=gen, device=device)
+            kv.append(K.quantize(x, mode))
+            del x
+        base.append(kv)
+    n_p = int(round(G.probe_ratio * n))
+    adapters = []
+    for a in rank_ids:
+        r = KIVI_RANKS[a % len(KIVI_RANKS)]
+        g = torch.Generator(device=device).manual_seed(5000 + a)
+        probes = torch.unique(torch.cat([torch.zeros(1, dtype=torch.long, device=device),
+                                         torch.randperm(n, generator=g, device=device)[: n_p - 1]]))
+        layers = []
+        for l in range(args.layers):
+            views = []
+            for m, mode in enumerate(("k", "v")):
+                B = torch.randn(d, r, generator=g, device=device) / math.sqrt(d)
+                codes = torch.randn(n, r, generator=g, device=device) * 0.5
+                fresh = K.dequantize(base[l][m])
+                fresh += codes @ B.T
+                drift = 0.1 * fresh.std() * torch.randn(n, d, generator=g, device=device)
+                drift[probes] = 0
+                fresh += drift
+                views.append({"fresh": fresh.to(torch.bfloat16), "basis": B if mode == "v" else None,
+                              "out": K.KiviTensor.empty(n, d, mode, device)})
+                del codes, drift, fresh
+            layers.append(views)
+        adapters.append({"rank": r, "probes": probes, "layers": layers})
+    return base, adapters
+
+
+def kivi_problems(base, adapter, k_bases=None):
+    from deltakv_b200 import kivi as K
+
+    probs = []
+    for l, views in enumerate(adapter["layers"]):
+        for m in range(2):
+            v = views[m]
+            basis = v["basis"] if m == 1 else (None if k_bases is None else k_bases[l])
+            probs.append(K.SubspaceProblem(base=base[l][m], fresh=v["fresh"], probe_index=adapter["probes"],
+                                           basis=basis, rank=adapter["rank"], out=v["out"]))
+    return probs
+
+
+def kivi_k_bases(base, adapter):
+    """The K path's basis per layer: top-r right singular subspace of the probe residual,
+    all layers of the view in one batched subspace iteration."""
+    from deltakv_b200 import kivi as K
+    from deltakv_b200.subspace import topr_basis
+
+    r = adapter["rank"]
+    p = adapter["probes"]
+    layers = adapter["layers"]
+    res = torch.empty(len(layers), p.numel(), base[0][0].d, dtype=torch.float32, device=p.device)
+    for l, views in enumerate(layers):
+        K.probe_residual(base[l][0], views[0]["fresh"], p, out=res[l])
+    bases = topr_basis(res, min(r, max(1, p.numel() - 1)))
+    return [bases[l] for l in range(len(layers))]
+
+
+def run_kivi_ours(args):
+    from deltakv_b200 import kivi as K
+    from deltakv_b200 import ops
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    # adapter views are sharded over the ranks
+    per_rank = max(1, args.adapters // world)
+    ids = [rank * per_rank + i for i in range(per_rank)]
+    base, adapters = make_kivi_workload(args, dev, ids)
+    units = args.layers * args.seq_len * per_rank
+    stream = torch.cuda.current_stream()
+
+    def step(evs=None):
+        for i, ad in enumerate(adapters):
+            if evs is not None:
+                evs[i][0].record(stream)
+            kb = kivi_k_bases(base, ad)
+            if evs is not None:
+                evs[i][1].record(stream)
+            K.subspace_correct(kivi_problems(base, ad, kb), check=False)
+            if evs is not None:
+                evs[i][2].record(stream)
+
+    step()
+    torch.cuda.synchronize()
+    ops.status_word(dev).raise_if_set("bench warm-up")
+    for _ in range(max(0, args.warmup - 1)):
+        step()
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in adapters] for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t_start.record(stream)
+        for i in range(args.steps):
+            step(evs[i])
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = t_start.elapsed_time(t_end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ops.status_word(dev).raise_if_set("bench timed region")
+    basis_ms = sum(e[0].elapsed_time(e[1]) for st in evs for e in st) / args.steps
+    route_ms = sum(e[1].elapsed_time(e[2]) for st in evs for e in st) / args.steps
+    ms_step = ms / args.steps
+    value = units * world / (ms_step / 1e3)
+    achieved = units * KIVI_BYTES_PER_UNIT / (route_ms / 1e3) / 1e9
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    peak = peaks.get("hbm_gbs") or 6650.0
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = kivi_cpu_sample(args.cpu_seconds)
+    if rank == 0:
+        line = {
+            "metric": KIVI_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int4 KIVI cache, bf16 tensor-core products, fp32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": KIVI_WORKLOAD, "layers": args.layers, "prefix_tokens": args.seq_len,
+                       "adapter_views_per_gpu": per_rank, "ranks": [a["rank"] for a in adapters],
+                       "units_per_step_per_gpu": units, "parallelism": f"adapter shards x{world}",
+                       "l2": f"{units * KIVI_BYTES_PER_UNIT / 1e9:.1f} GB per step per GPU >> 126 MB L2",
+                       "k_basis_ms_per_step": basis_ms, "subspace_route_ms_per_step": route_ms},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs, burst copy)",
+                         "kernel": "int4 subspace route (flags, pack, pass1 x2, psum, solve, pass2 x2) per view",
+                         "kernel_ms": route_ms, "algorithmic_bytes_per_unit": KIVI_BYTES_PER_UNIT},
+            "cpu_baseline": cpu,
+            "e2e": None,
+            "gpu_launches": args.steps * len(adapters) * 8,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def kivi_cpu_sample(seconds: float, n: int = 4096) -> dict:
+    """Oracle port of the route (dequant, subspace_correct, requant) on (layer, view) items of
+    `n` tokens, one item per worker thread."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from threadpoolctl import threadpool_limits
+
+    from oracle import kivi as OK
+    from oracle import subspace as OS
+
+    G = KiviGeo
+    d = G.n_kv * G.hd
+    rng = np.random.default_rng(7)
+    base = OK.quantize(rng.standard_normal((n, d), dtype=np.float32), "v")
+    B = (rng.standard_normal((d, 16), dtype=np.float32) / np.sqrt(d)).astype(np.float32)
+    fresh = (OK.dequantize(*base, "v") + (rng.standard_normal((n, 16), dtype=np.float32) * 0.5) @ B.T).astype(np.float32)
+    probes = np.unique(np.concatenate([[0], rng.permutation(n)[: int(0.1 * n)]]))
+    threads = dense_cpu_threads()
+
+    def item():
+        reused = OK.dequantize(*base, "v")
+        corr, _, _ = OS.subspace_correct(reused.reshape(n, G.n_kv, G.hd), fresh.reshape(n, G.n_kv, G.hd), probes,
+                                         basis=B, rank=16)
+        OK.quantize(corr.reshape(n, d), "v")
+        return n
+
+    deadline = time.perf_counter() + seconds
+    lock = threading.Lock()
+    done = [0]
+
+    def worker(_):
+        u = 0
+        while time.perf_counter() < deadline:
+            u += item()
+        with lock:
+            done[0] += u
+        return u
+
+    with threadpool_limits(1):
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(threads) as ex:
+            list(ex.map(worker, range(threads)))
+        el = time.perf_counter() - t0
+    return {"value": done[0] / el, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{done[0] // n} (layer, view) items of {n} tokens, rank 16, V grouping, in {el:.1f} s "
+                      f"(oracle numpy port: dequant, subspace_correct, requant; {threads} threads)"}
+
+
+def run_kivi_reference(args):
+    world, rank, _ = dist_setup(args)
+    if rank != 0:
+        return 0
+    res = [kivi_cpu_sample(max(2.0, args.cpu_seconds / max(1, args.steps))) for _ in range(args.steps)]
+    value = sum(r["value"] for r in res) / len(res)
+    line = {
+        "impl": "reference", "metric": KIVI_METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": KIVI_WORKLOAD, "step": res[0]["sample"]},
+        "cpu_baseline": {**res[0], "value": value},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "multi-lora-kivi":
+        for k, v in (("layers", KiviGeo.layers), ("seqs", 1), ("seq_len", KiviGeo.seq_len)):
+            if getattr(args, k) is None:
+                setattr(args, k, v)
+        return run_kivi_reference(args) if args.impl == "reference" else run_kivi_ours(args)
     dense = args.workload == "rl-dense"
     for k, v in (("layers", DenseGeo.layers if dense else 32), ("seqs", DenseGeo.seqs if dense else 64),
                  ("seq_len", DenseGeo.seq_len if dense else 4096)):

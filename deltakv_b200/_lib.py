@@ -46,6 +46,7 @@ EXPORTED = (
     "dkv_kivi_quantize",
     "dkv_kivi_dequantize",
     "dkv_kivi_patch",
+    "dkv_kivi_probe_residual",
     "dkv_kivi_subspace_workspace_bytes",
     "dkv_kivi_subspace_correct",
     "dkv_subspace_workspace_bytes",
@@ -278,6 +279,8 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_kivi_dequantize.argtypes = [C.POINTER(KiviCache), P, I32, I64, P]
     lib.dkv_kivi_patch.restype = C.c_int
     lib.dkv_kivi_patch.argtypes = [C.POINTER(KiviCache), P, I32, I64, C.POINTER(KiviCache), P]
+    lib.dkv_kivi_probe_residual.restype = C.c_int
+    lib.dkv_kivi_probe_residual.argtypes = [C.POINTER(KiviCache), P, I32, I64, P, I64, P, I64, P, P]
     lib.dkv_kivi_subspace_workspace_bytes.restype = C.c_int
     lib.dkv_kivi_subspace_workspace_bytes.argtypes = [C.POINTER(KiviSubspaceProblem), I32, C.POINTER(C.c_int64)]
     lib.dkv_kivi_subspace_correct.restype = C.c_int

@@ -138,6 +138,28 @@ __global__ void deq_kernel(Cache c, int mode, void *x, int xdt, int64_t xrs) {
   }
 }
 
+// out[i, c] = fresh[rows[i], c] - dequant(base)[rows[i], c]: one thread per (row, 2 channels)
+__global__ void probe_residual_kernel(Cache c, int mode, const void *fresh, int fdt, int64_t frs, const int32_t *rows,
+                                      int64_t n_rows, float *out, int64_t ors, int32_t *status) {
+  const int64_t half = c.d / 2;
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i >= n_rows * half) return;
+  const int64_t k = i / half, cp = i % half;
+  const int64_t t = rows[k];
+  if (t < 0 || t >= c.n) {
+    record_error(status, DKV_ERR_INVALID_ARGUMENT);
+    return;
+  }
+  const uint32_t b = c.codes[t * c.crs + cp];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int64_t ch = 2 * cp + e;
+    const int64_t si = mode == DKV_KIVI_PER_TOKEN ? t * c.szrs + ch / kG : (t / kG) * c.szrs + ch;
+    const float v = deq((b >> (4 * e)) & 0xFu, __half2float(c.scale[si]), __half2float(c.zero[si]));
+    out[k * ors + ch] = load_as_float(fresh, fdt, t * frs + ch) - v;
+  }
+}
+
 int check(const dkv_kivi_cache *c, Cache &o) {
   if (c == nullptr) return DKV_ERR_INVALID_ARGUMENT;
   if (c->mode != DKV_KIVI_PER_CHANNEL && c->mode != DKV_KIVI_PER_TOKEN) return DKV_ERR_INVALID_ARGUMENT;
@@ -184,6 +206,7 @@ int launch(int mode, int src, const void *x, int xdt, int64_t xrs, const Cache &
 }  // namespace dkv
 
 using namespace dkv;
+using namespace dkv::kivi;
 
 extern "C" int dkv_kivi_quantize(const void *x, int32_t x_dtype, int64_t x_row_stride, const dkv_kivi_cache *out,
                                  dkv_stream_t stream) {
@@ -222,4 +245,21 @@ extern "C" int dkv_kivi_patch(const dkv_kivi_cache *base, const void *delta, int
   if (delta != nullptr && !kivi::float_dtype(delta_dtype)) return DKV_ERR_UNSUPPORTED;
   return kivi::launch(out->mode, 1, nullptr, 0, 0, b, delta, delta_dtype, delta_row_stride, o,
                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int dkv_kivi_probe_residual(const dkv_kivi_cache *base, const void *fresh, int32_t fresh_dtype,
+                                       int64_t fresh_row_stride, const int32_t *rows, int64_t n_rows, float *out,
+                                       int64_t out_row_stride, int32_t *status, dkv_stream_t stream) {
+  Cache c;
+  int rc = check(base, c);
+  if (rc) return rc;
+  if (fresh_dtype != DKV_F32 && fresh_dtype != DKV_F16 && fresh_dtype != DKV_BF16) return DKV_ERR_UNSUPPORTED;
+  if (n_rows < 0 || out_row_stride < c.d) return DKV_ERR_INVALID_ARGUMENT;
+  if (n_rows == 0) return DKV_OK;
+  if (fresh == nullptr || rows == nullptr || out == nullptr) return DKV_ERR_INVALID_ARGUMENT;
+  const int64_t work = n_rows * (c.d / 2);
+  probe_residual_kernel<<<static_cast<unsigned>((work + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      c, base->mode, fresh, fresh_dtype, fresh_row_stride, rows, n_rows, out, out_row_stride, status);
+  DKV_CUDA_CHECK(cudaGetLastError());
+  return DKV_OK;
 }

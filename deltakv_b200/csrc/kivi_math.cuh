@@ -25,6 +25,21 @@ __device__ __forceinline__ uint32_t quant_one(float x, float s, float z) {
   return static_cast<uint32_t>(v);
 }
 
+// Same result as quant_one, with the group's reciprocal: y = (x - z) * (1/s) is within 2 ulp
+// of the IEEE quotient (|y| < 16, so 2 ulp < 4e-6), hence rint(y) equals rint(quotient) unless
+// y lies within that distance of a rounding tie; there (|frac(y) - 1/2| < 1e-5) the quotient
+// is formed exactly.  `inv` = 1/s rounded to nearest.
+__device__ __forceinline__ uint32_t quant_one_fast(float x, float s, float z, float inv) {
+  if (!(s > 0.f)) return 0u;
+  const float a = __fsub_rn(x, z);
+  float y = __fmul_rn(a, inv);
+  if (fabsf(y - floorf(y) - 0.5f) < 1e-5f) y = __fdiv_rn(a, s);
+  return static_cast<uint32_t>(fminf(fmaxf(rintf(y), 0.f), 15.f));
+}
+
+// a 4-bit code as a float (exact): 2^23 + q built in the mantissa, minus 2^23
+__device__ __forceinline__ float code_to_f(uint32_t q) { return __int_as_float(0x4B000000u | q) - 8388608.f; }
+
 __device__ __forceinline__ void quant_group(const float (&x)[kG], int cnt, uint8_t (&q)[kG], __half &s16,
                                             __half &z16) {
   float lo = x[0], hi = x[0];
@@ -36,12 +51,13 @@ __device__ __forceinline__ void quant_group(const float (&x)[kG], int cnt, uint8
     }
   group_params(lo, hi, s16, z16);
   const float s = __half2float(s16), z = __half2float(z16);
+  const float inv = s > 0.f ? __frcp_rn(s) : 0.f;
 #pragma unroll
-  for (int i = 0; i < kG; ++i) q[i] = static_cast<uint8_t>(quant_one(x[i], s, z));
+  for (int i = 0; i < kG; ++i) q[i] = static_cast<uint8_t>(quant_one_fast(x[i], s, z, inv));
 }
 
 __device__ __forceinline__ float deq(uint32_t q, float s, float z) {
-  return __fadd_rn(__fmul_rn(static_cast<float>(q), s), z);
+  return __fadd_rn(__fmul_rn(code_to_f(q), s), z);
 }
 
 }  // namespace kivi

@@ -9,12 +9,21 @@
 //   orth_mu = mean_P(R - fitted);  w = min(||R|| / mean ||R||, 1)
 //   corr = reused + fitted + w orth_mu;  corr[P] = fresh[P];  out = quant(corr)
 // All problems of a call share d; each has its own token count, probes, basis (rank <= 64)
-// and caches.  Launches (all problems at once):
-//   flags   probe flags and probe count (probe indices are deduplicated)
-//   pack    basis -> bf16, transposed copy for the first product, row copy for the second
-//   pass1   dequant, R, ||R||, rhs = R B (mma.sync bf16, fp32 accumulate), sums
+// and caches.  Launches (all problems at once; the two passes once per grouping mode):
+//   flags   probe flags, deduplicated probe list and count
+//   pack    basis -> bf16 in the two MMA fragment orders below, and a plain row copy
+//   pass1   per warp of 32 tokens: dequant, R, ||R||, rhs = R B (mma.sync bf16, fp32
+//           accumulate), per-tile column sums — no shared memory, no block barrier
+//   psum    sums over the probes of R and of rhs
 //   solve   one CTA per problem: (B^T B + 1e-6 I)^-1 in fp64, orth_mu, subspace, mean ||R||
-//   pass2   codes = rhs G^-1, fitted = codes B^T (mma.sync bf16), corr, requantise
+//   pass2   per warp of 32 tokens: codes = rhs G^-1 (fp32), fitted = codes B^T (mma.sync),
+//           corr, requantise — V groups reduced across the 4 lanes of a row, K groups
+//           across the 8 row-lanes of the warp (a warp tile is exactly one K group)
+// Lane (g, q) of a warp owns rows g + 8i (i = 0..3) and, in every block of 32 channels, the
+// 8 contiguous channels 8q..8q+7: pass1 forms its R directly as MMA A fragments by
+// permuting k inside the block (both operands use the same permutation, which leaves R B
+// unchanged), and pass2's basis image permutes output columns so that the accumulator
+// fragments land on those same 8 channels.
 // The products use the basis rounded to bf16 (B~) throughout — G is formed from B~ as well —
 // so `fitted` is the least-squares projection onto col(B~); R and the codes are rounded to
 // bf16 as MMA operands.  These roundings sit far below the int4 step of the output.
@@ -27,11 +36,13 @@
 namespace dkv {
 namespace ksub {
 
-constexpr int kTM = 64;  // tokens per tile (two K groups)
-constexpr int kKC = 64;  // channels per chunk
-constexpr int kThreads = 256;
+constexpr int kWT = 32;  // tokens per warp tile (one K group)
+constexpr int kWarps = 4;
+constexpr int kThreads = 32 * kWarps;
+constexpr int kTM = kWT * kWarps;  // tokens per CTA
+constexpr int kCB = 32;            // channels per block
 constexpr int kMaxRank = 64;
-constexpr int kBP = 8;  // bf16 row padding (16 bytes) against ldmatrix bank conflicts
+constexpr int kPsumSplit = 16;  // probe-sum CTAs per channel slice
 
 struct Prob {
   const uint8_t *codes;
@@ -47,15 +58,16 @@ struct Prob {
   int64_t n_probes;
   float *sub_out, *mu_out;
   // workspace
-  float *rhs, *dist, *sums, *ginv, *mu, *subv;
+  float *rhs, *dist, *part, *sums, *ginv, *mu, *subv;
   uint32_t *flag;
-  __nv_bfloat16 *bt, *bb;
+  int32_t *uprobe, *ucount;
+  __nv_bfloat16 *b1, *b2, *bb;
   const float *basis;
   int64_t tile0;
   int r, mode;
 };
 
-constexpr int kMaxProblems = 128;
+constexpr int kMaxProblems = 112;
 
 // The problem table travels in the kernel parameters (read through the constant cache).
 struct Batch {
@@ -66,8 +78,8 @@ struct Batch {
 };
 static_assert(sizeof(Batch) <= 32000, "kernel parameter limit");
 
-// sums layout: [0] sum ||R||, [1] probe count, [2, 2+RP) sum rhs (all tokens),
-// [2+RP, 2+2RP) sum rhs (probes), [2+2RP, 2+2RP+d) sum_P R
+// sums (zeroed per call): [0, RP) sum_P rhs, [RP, RP + d) sum_P R
+// part: [ceil(n/32) tiles][RP + 1]: per-tile column sums of rhs, then the tile's sum of ||R||
 __device__ __forceinline__ int find_prob(const Batch &b, int64_t tile) {
   int lo = 0, hi = b.n_probs - 1;
   while (lo < hi) {
@@ -79,62 +91,46 @@ __device__ __forceinline__ int find_prob(const Batch &b, int64_t tile) {
 }
 
 template <int FDT>
-__device__ __forceinline__ void load16(const void *base, int64_t off, float (&v)[16]) {
-  if (FDT == DKV_F32) {
-    const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(base) + off);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float4 q = p[i];
-      v[4 * i] = q.x, v[4 * i + 1] = q.y, v[4 * i + 2] = q.z, v[4 * i + 3] = q.w;
-    }
-  } else {
-    const uint4 *p = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(base) + off);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const uint4 q = p[i];
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        v[8 * i + 2 * j] = FDT == DKV_BF16 ? bf16lo(w[j]) : f16lo(w[j]);
-        v[8 * i + 2 * j + 1] = FDT == DKV_BF16 ? bf16hi(w[j]) : f16hi(w[j]);
-      }
-    }
-  }
-}
-
-template <int FDT>
 __device__ __forceinline__ float load1(const void *base, int64_t off) {
   if (FDT == DKV_F32) return static_cast<const float *>(base)[off];
   if (FDT == DKV_BF16) return __bfloat162float(static_cast<const __nv_bfloat16 *>(base)[off]);
   return __half2float(static_cast<const __half *>(base)[off]);
 }
 
-// 16 dequantised values of token t, channels [c, c+16) (c % 16 == 0)
-__device__ __forceinline__ void deq16(const Prob &P, int64_t t, int64_t c, float (&v)[16]) {
-  const uint2 q = *reinterpret_cast<const uint2 *>(P.codes + t * P.crs + c / 2);
-  const uint32_t w[2] = {q.x, q.y};
-  if (P.mode == DKV_KIVI_PER_TOKEN) {
-    const float s = __half2float(P.scale[t * P.szrs + c / kivi::kG]);
-    const float z = __half2float(P.zero[t * P.szrs + c / kivi::kG]);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = kivi::deq((w[i >> 3] >> (4 * (i & 7))) & 0xFu, s, z);
+// 8 consecutive fresh values (16 B of bf16/f16, 32 B of f32)
+template <int FDT>
+__device__ __forceinline__ void load8(const void *base, int64_t off, float (&v)[8]) {
+  if (FDT == DKV_F32) {
+    const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(base) + off);
+    const float4 a = p[0], c = p[1];
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = c.x, v[5] = c.y, v[6] = c.z, v[7] = c.w;
   } else {
-    const int64_t so = (t / kivi::kG) * P.szrs + c;
-    const uint4 *sp = reinterpret_cast<const uint4 *>(P.scale + so);
-    const uint4 *zp = reinterpret_cast<const uint4 *>(P.zero + so);
-    uint32_t sw[8], zw[8];
-    {
-      const uint4 a = sp[0], b = sp[1], e = zp[0], f = zp[1];
-      sw[0] = a.x, sw[1] = a.y, sw[2] = a.z, sw[3] = a.w, sw[4] = b.x, sw[5] = b.y, sw[6] = b.z, sw[7] = b.w;
-      zw[0] = e.x, zw[1] = e.y, zw[2] = e.z, zw[3] = e.w, zw[4] = f.x, zw[5] = f.y, zw[6] = f.z, zw[7] = f.w;
-    }
+    const uint4 a = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(base) + off);
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float s = (i & 1) ? f16hi(sw[i >> 1]) : f16lo(sw[i >> 1]);
-      const float z = (i & 1) ? f16hi(zw[i >> 1]) : f16lo(zw[i >> 1]);
-      v[i] = kivi::deq((w[i >> 3] >> (4 * (i & 7))) & 0xFu, s, z);
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = FDT == DKV_BF16 ? bf16lo(w[j]) : f16lo(w[j]);
+      v[2 * j + 1] = FDT == DKV_BF16 ? bf16hi(w[j]) : f16hi(w[j]);
     }
   }
+}
+
+// 8 halves (16 B) -> floats
+__device__ __forceinline__ void halves8(const __half *p, float (&v)[8]) {
+  const uint4 a = *reinterpret_cast<const uint4 *>(p);
+  const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[2 * j] = f16lo(w[j]);
+    v[2 * j + 1] = f16hi(w[j]);
+  }
+}
+
+// dequantised value of one element
+__device__ __forceinline__ float deq1(const Prob &P, int64_t t, int64_t c) {
+  const uint32_t b = P.codes[t * P.crs + c / 2];
+  const int64_t si = P.mode == DKV_KIVI_PER_TOKEN ? t * P.szrs + c / kivi::kG : (t / kivi::kG) * P.szrs + c;
+  return kivi::deq((b >> (4 * (c & 1))) & 0xFu, __half2float(P.scale[si]), __half2float(P.zero[si]));
 }
 
 // ---------------------------------------------------------------------------------------
@@ -147,171 +143,195 @@ __global__ void flags_kernel(const __grid_constant__ Batch b) {
       record_error(b.status, DKV_ERR_INVALID_ARGUMENT);
       continue;
     }
-    if (atomicExch(&P.flag[t], 1u) == 0u) atomicAdd(&P.sums[1], 1.f);
+    if (atomicExch(&P.flag[t], 1u) == 0u) P.uprobe[atomicAdd(P.ucount, 1)] = static_cast<int32_t>(t);
   }
 }
 
-// basis fp32 [d, r] -> bt [RP, d] and bb [d, RP] bf16, zero beyond r
+// basis value B~[c][k] (zero beyond the problem's rank)
+__device__ __forceinline__ __nv_bfloat16 basis_at(const Prob &P, int64_t c, int k) {
+  return __float2bfloat16_rn((k < P.r && P.basis != nullptr) ? P.basis[c * P.r + k] : 0.f);
+}
+
+// b1 (pass1 B operand): [block][n-tile][lane][8]: B~[32 block + 8q + j][8 nt + g]
+// b2 (pass2 B operand): [block][k-step][n-tile][lane][4]: B~[ch][16 ks + 2q + {0, 1, 8, 9}],
+//     ch = 32 block + 8 (g >> 1) + 2 nt + (g & 1)
+// bb: [d][RP] rows
 __global__ void pack_kernel(const __grid_constant__ Batch b, int rp) {
   const Prob &P = b.probs[blockIdx.y];
   const int64_t total = b.d * rp;
+  const int nt_n = rp / 8, ks_n = rp / 16;
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t c = e / rp;
-    const int k = static_cast<int>(e - c * rp);
-    const float v = (k < P.r && P.basis != nullptr) ? P.basis[c * P.r + k] : 0.f;
-    const __nv_bfloat16 h = __float2bfloat16_rn(v);
-    P.bb[c * rp + k] = h;
-    P.bt[static_cast<int64_t>(k) * b.d + c] = h;
+    {
+      const int64_t c = e / rp;
+      const int k = static_cast<int>(e - c * rp);
+      P.bb[e] = basis_at(P, c, k);
+    }
+    {
+      const int j = static_cast<int>(e & 7);
+      const int lane = static_cast<int>((e >> 3) & 31);
+      const int64_t rest = e >> 8;
+      const int nt = static_cast<int>(rest % nt_n);
+      const int64_t blk = rest / nt_n;
+      const int g = lane >> 2, q = lane & 3;
+      P.b1[e] = basis_at(P, kCB * blk + 8 * q + j, 8 * nt + g);
+    }
+    {
+      const int x = static_cast<int>(e & 3);
+      const int lane = static_cast<int>((e >> 2) & 31);
+      const int64_t rest = e >> 7;
+      const int nt = static_cast<int>(rest & 3);
+      const int ks = static_cast<int>((rest >> 2) % ks_n);
+      const int64_t blk = (rest >> 2) / ks_n;
+      const int g = lane >> 2, q = lane & 3;
+      const int64_t ch = kCB * blk + 8 * (g >> 1) + 2 * nt + (g & 1);
+      const int k = 16 * ks + 2 * q + (x & 1) + 8 * (x >> 1);
+      P.b2[e] = basis_at(P, ch, k);
+    }
   }
 }
 
 // ---------------------------------------------------------------------------------------
 // pass 1
 // ---------------------------------------------------------------------------------------
-template <int RP, int FDT>
-__global__ void __launch_bounds__(kThreads) pass1_kernel(const __grid_constant__ Batch b) {
-  __shared__ __align__(16) __nv_bfloat16 Rs[kTM][kKC + kBP];
-  __shared__ __align__(16) __nv_bfloat16 Bts[RP][kKC + kBP];
-  __shared__ float sPR[kKC];
-  __shared__ float sRhs[2][RP];
-  __shared__ float red[kThreads / 32];
-  __shared__ uint32_t sflag[kTM];
-  __shared__ int any_probe;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const Prob &P = b.probs[find_prob(b, blockIdx.x)];
-  const int64_t t0 = (blockIdx.x - P.tile0) * kTM;
+template <int RP, int FDT, int MODE>
+__global__ void __launch_bounds__(kThreads) pass1_kernel(const __grid_constant__ Batch b, int64_t tile_lo) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const Prob &P = b.probs[find_prob(b, tile_lo + blockIdx.x)];
+  const int64_t t0 = (tile_lo + blockIdx.x - P.tile0) * kTM + warp * kWT;
   const int64_t n = P.n;
-  if (tid == 0) any_probe = 0;
-  __syncthreads();
-  if (tid < kTM) {
-    const uint32_t f = (t0 + tid < n) ? P.flag[t0 + tid] : 0u;
-    sflag[tid] = f;
-    if (f) any_probe = 1;
-  }
-  if (tid < kKC) sPR[tid] = 0.f;
-  for (int e = tid; e < 2 * RP; e += kThreads) sRhs[e / RP][e % RP] = 0.f;
-  __syncthreads();
-
-  const int lt = tid >> 2, lc = (tid & 3) * 16;
-  const int64_t tok = t0 + lt;
-  const bool tv = tok < n;
-  const bool myflag = tv && sflag[lt] != 0u;
-  float dist2 = 0.f;
-  const int mb = warp & 3, nb = warp >> 2;
-  constexpr int NT = RP / 16;  // 8-wide n-tiles per warp (half of RP each)
-  float acc[NT][4];
+  if (t0 >= n) return;
+  constexpr int NT = RP / 8;
+  constexpr bool kmode = MODE == DKV_KIVI_PER_CHANNEL;
+  float acc[2][NT][4];
 #pragma unroll
-  for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-
-  for (int64_t c0 = 0; c0 < b.d; c0 += kKC) {
-    {
-      float f[16], rv[16];
-      if (tv) {
-        load16<FDT>(P.fresh, tok * P.frs + c0 + lc, f);
-        deq16(P, tok, c0 + lc, rv);
+  for (int m = 0; m < 2; ++m)
+#pragma unroll
+    for (int i = 0; i < NT; ++i) acc[m][i][0] = acc[m][i][1] = acc[m][i][2] = acc[m][i][3] = 0.f;
+  float d2[4] = {0.f, 0.f, 0.f, 0.f};
+  int64_t row[4];
+  bool rv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    row[i] = t0 + g + 8 * i;
+    rv[i] = row[i] < n;
+  }
+  const uint4 *b1 = reinterpret_cast<const uint4 *>(P.b1) + lane;
+  const int n_blocks = static_cast<int>(b.d / kCB);
+  for (int cb = 0; cb < n_blocks; ++cb) {
+    const int64_t c = static_cast<int64_t>(cb) * kCB + 8 * q;
+    float ks8[8], kz8[8];
+    if (kmode) {
+      halves8(P.scale + (t0 / kivi::kG) * P.szrs + c, ks8);
+      halves8(P.zero + (t0 / kivi::kG) * P.szrs + c, kz8);
+    }
+    uint32_t a[2][2][4];  // [m-tile][k-step][reg]
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float r[8];
+      if (rv[i]) {
+        float f[8];
+        load8<FDT>(P.fresh, row[i] * P.frs + c, f);
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(P.codes + row[i] * P.crs + c / 2);
+        float vs = 0.f, vz = 0.f;
+        if (!kmode) {
+          vs = __half2float(P.scale[row[i] * P.szrs + cb]);
+          vz = __half2float(P.zero[row[i] * P.szrs + cb]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float reused = kivi::deq((w >> (4 * j)) & 0xFu, kmode ? ks8[j] : vs, kmode ? kz8[j] : vz);
+          r[j] = f[j] - reused;
+          d2[i] = fmaf(r[j], r[j], d2[i]);
+        }
       } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) f[i] = rv[i] = 0.f;
+        for (int j = 0; j < 8; ++j) r[j] = 0.f;
       }
-      uint32_t pk[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float r0 = f[2 * i] - rv[2 * i], r1 = f[2 * i + 1] - rv[2 * i + 1];
-        dist2 = fmaf(r0, r0, dist2);
-        dist2 = fmaf(r1, r1, dist2);
-        pk[i] = pack_bf16x2(r0, r1);
-        if (myflag) {
-          atomicAdd(&sPR[lc + 2 * i], r0);
-          atomicAdd(&sPR[lc + 2 * i + 1], r1);
-        }
-      }
-      uint4 *dst = reinterpret_cast<uint4 *>(&Rs[lt][lc]);
-      dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-    }
-    for (int e = tid; e < RP * (kKC / 8); e += kThreads) {
-      const int k = e / (kKC / 8), j = e % (kKC / 8);
-      *reinterpret_cast<uint4 *>(&Bts[k][8 * j]) =
-          *reinterpret_cast<const uint4 *>(P.bt + static_cast<int64_t>(k) * b.d + c0 + 8 * j);
-    }
-    __syncthreads();
-    if (any_probe && tid < kKC) {
-      atomicAdd(&P.sums[2 + 2 * RP + c0 + tid], sPR[tid]);
-      sPR[tid] = 0.f;
+      const int m = i >> 1, h = i & 1;
+      a[m][0][h] = pack_bf16x2(r[0], r[1]);
+      a[m][0][2 + h] = pack_bf16x2(r[2], r[3]);
+      a[m][1][h] = pack_bf16x2(r[4], r[5]);
+      a[m][1][2 + h] = pack_bf16x2(r[6], r[7]);
     }
 #pragma unroll
-    for (int ks = 0; ks < kKC / 16; ++ks) {
-      uint32_t a0, a1, a2, a3;
-      ldmatrix_x4(a0, a1, a2, a3, smem_u32(&Rs[16 * mb + (lane & 15)][16 * ks + ((lane >> 4) << 3)]));
-      const int nbase = nb * (RP / 2);
+    for (int nt = 0; nt < NT; ++nt) {
+      const uint4 bv = b1[(static_cast<int64_t>(cb) * NT + nt) * 32];
 #pragma unroll
-      for (int np = 0; np < NT / 2; ++np) {
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(b0, b1, b2, b3,
-                    smem_u32(&Bts[nbase + 16 * np + ((lane >> 4) << 3) + (lane & 7)][16 * ks + (((lane >> 3) & 1) << 3)]));
-        mma16816_bf16(acc[2 * np], a0, a1, a2, a3, b0, b1);
-        mma16816_bf16(acc[2 * np + 1], a0, a1, a2, a3, b2, b3);
-      }
-      if (NT & 1) {
-        uint32_t b0, b1;
-        ldmatrix_x2(b0, b1, smem_u32(&Bts[nbase + 16 * (NT / 2) + (lane & 7)][16 * ks + (((lane >> 3) & 1) << 3)]));
-        mma16816_bf16(acc[NT - 1], a0, a1, a2, a3, b0, b1);
+      for (int m = 0; m < 2; ++m) {
+        mma16816_bf16(acc[m][nt], a[m][0][0], a[m][0][1], a[m][0][2], a[m][0][3], bv.x, bv.y);
+        mma16816_bf16(acc[m][nt], a[m][1][0], a[m][1][1], a[m][1][2], a[m][1][3], bv.z, bv.w);
       }
     }
-    __syncthreads();
   }
 
-  // ||R|| per token (4 loader threads per token)
-  dist2 += __shfl_xor_sync(0xffffffffu, dist2, 1);
-  dist2 += __shfl_xor_sync(0xffffffffu, dist2, 2);
+  // ||R|| per row (4 lanes per row) and the tile's sum
   float dsum = 0.f;
-  if ((tid & 3) == 0 && tv) {
-    const float dd = sqrtf(dist2);
-    P.dist[tok] = dd;
-    dsum = dd;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float v = d2[i];
+    v += __shfl_xor_sync(0xffffffffu, v, 1);
+    v += __shfl_xor_sync(0xffffffffu, v, 2);
+    const float dd = sqrtf(v);
+    if (q == 0 && rv[i]) P.dist[row[i]] = dd;
+    if (rv[i]) dsum += dd;
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, o);
-  if (lane == 0) red[warp] = dsum;
-
-  // rhs rows and column sums (all tokens, probes)
-  const int g = lane >> 2, q = lane & 3;
-  const int ra = 16 * mb + g, rb = ra + 8;
-  const bool va = t0 + ra < n, vb = t0 + rb < n;
-  const bool fa = va && sflag[ra] != 0u, fb = vb && sflag[rb] != 0u;
+  for (int o = 4; o < 32; o <<= 1) dsum += __shfl_xor_sync(0xffffffffu, dsum, o);
+  float *part = P.part + (t0 / kWT) * (RP + 1);
+  if (lane == 0) part[RP] = dsum;
+  // rhs rows and the tile's column sums
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    const int col = nb * (RP / 2) + 8 * nt + 2 * q;
-    if (va) *reinterpret_cast<float2 *>(P.rhs + (t0 + ra) * RP + col) = make_float2(acc[nt][0], acc[nt][1]);
-    if (vb) *reinterpret_cast<float2 *>(P.rhs + (t0 + rb) * RP + col) = make_float2(acc[nt][2], acc[nt][3]);
-    float s0 = (va ? acc[nt][0] : 0.f) + (vb ? acc[nt][2] : 0.f);
-    float s1 = (va ? acc[nt][1] : 0.f) + (vb ? acc[nt][3] : 0.f);
-    float p0 = (fa ? acc[nt][0] : 0.f) + (fb ? acc[nt][2] : 0.f);
-    float p1 = (fa ? acc[nt][1] : 0.f) + (fb ? acc[nt][3] : 0.f);
+    float s0 = 0.f, s1 = 0.f;
+    const int col = 8 * nt + 2 * q;
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      if (rv[2 * m]) {
+        *reinterpret_cast<float2 *>(P.rhs + row[2 * m] * RP + col) = make_float2(acc[m][nt][0], acc[m][nt][1]);
+        s0 += acc[m][nt][0];
+        s1 += acc[m][nt][1];
+      }
+      if (rv[2 * m + 1]) {
+        *reinterpret_cast<float2 *>(P.rhs + row[2 * m + 1] * RP + col) = make_float2(acc[m][nt][2], acc[m][nt][3]);
+        s0 += acc[m][nt][2];
+        s1 += acc[m][nt][3];
+      }
+    }
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
       s0 += __shfl_xor_sync(0xffffffffu, s0, o);
       s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-      p0 += __shfl_xor_sync(0xffffffffu, p0, o);
-      p1 += __shfl_xor_sync(0xffffffffu, p1, o);
     }
     if (g == 0) {
-      atomicAdd(&sRhs[0][col], s0);
-      atomicAdd(&sRhs[0][col + 1], s1);
-      atomicAdd(&sRhs[1][col], p0);
-      atomicAdd(&sRhs[1][col + 1], p1);
+      part[col] = s0;
+      part[col + 1] = s1;
     }
   }
-  __syncthreads();
-  if (tid == 0) {
-    float s = 0.f;
-    for (int i = 0; i < kThreads / 32; ++i) s += red[i];
-    atomicAdd(&P.sums[0], s);
-  }
-  if (tid < RP) {
-    atomicAdd(&P.sums[2 + tid], sRhs[0][tid]);
-    if (any_probe) atomicAdd(&P.sums[2 + RP + tid], sRhs[1][tid]);
+}
+
+// ---------------------------------------------------------------------------------------
+// probe sums: sum_P R (128-channel slices) and sum_P rhs (the last slice), the probes split
+// over kPsumSplit CTAs per slice
+// ---------------------------------------------------------------------------------------
+template <int RP, int FDT>
+__global__ void __launch_bounds__(128) psum_kernel(const __grid_constant__ Batch b) {
+  const Prob &P = b.probs[blockIdx.z];
+  const int cnt = *P.ucount;
+  const int slices = static_cast<int>((b.d + 127) / 128);
+  const int sl = blockIdx.x;
+  float s = 0.f;
+  if (sl < slices) {
+    const int64_t c = static_cast<int64_t>(sl) * 128 + threadIdx.x;
+    if (c >= b.d) return;
+    for (int i = blockIdx.y; i < cnt; i += gridDim.y) {
+      const int64_t t = P.uprobe[i];
+      s += load1<FDT>(P.fresh, t * P.frs + c) - deq1(P, t, c);
+    }
+    atomicAdd(&P.sums[RP + c], s);
+  } else if (threadIdx.x < RP) {
+    for (int i = blockIdx.y; i < cnt; i += gridDim.y) s += P.rhs[static_cast<int64_t>(P.uprobe[i]) * RP + threadIdx.x];
+    atomicAdd(&P.sums[threadIdx.x], s);
   }
 }
 
@@ -319,17 +339,24 @@ __global__ void __launch_bounds__(kThreads) pass1_kernel(const __grid_constant__
 // solve: one CTA per problem
 // ---------------------------------------------------------------------------------------
 template <int RP>
-__global__ void __launch_bounds__(kThreads) solve_kernel(const __grid_constant__ Batch b) {
+__global__ void __launch_bounds__(256) solve_kernel(const __grid_constant__ Batch b) {
   extern __shared__ double Mdyn[];  // [r][2r + 1]: [G | I]
-  __shared__ float cp[RP], ca[RP];
+  __shared__ float cp[RP], ca[RP], colsum[RP + 1];
   __shared__ double fac[RP];
   __shared__ int piv_row;
   const Prob &P = b.probs[blockIdx.x];
   const int r = P.r;
   const int ldm = 2 * r + 1;
-  const float np = P.sums[1];
+  const float np = static_cast<float>(*P.ucount);
+  const int64_t tiles = (P.n + kWT - 1) / kWT;
   for (int e = threadIdx.x; e < RP * RP; e += blockDim.x) P.ginv[e] = 0.f;
   if (threadIdx.x < RP) cp[threadIdx.x] = ca[threadIdx.x] = 0.f;
+  // column sums of rhs and the sum of ||R|| from the per-tile partials
+  for (int k = threadIdx.x; k <= RP; k += blockDim.x) {
+    float s = 0.f;
+    for (int64_t t = 0; t < tiles; ++t) s += P.part[t * (RP + 1) + k];
+    colsum[k] = s;
+  }
   __syncthreads();
   if (r > 0) {
     for (int e = threadIdx.x; e < r * r; e += blockDim.x) {
@@ -378,8 +405,8 @@ __global__ void __launch_bounds__(kThreads) solve_kernel(const __grid_constant__
       const int j = threadIdx.x;
       double sp = 0.0, sa = 0.0;
       for (int i = 0; i < r; ++i) {
-        sp += static_cast<double>(P.sums[2 + RP + i]) * Mdyn[i * ldm + r + j];
-        sa += static_cast<double>(P.sums[2 + i]) * Mdyn[i * ldm + r + j];
+        sp += static_cast<double>(P.sums[i]) * Mdyn[i * ldm + r + j];
+        sa += static_cast<double>(colsum[i]) * Mdyn[i * ldm + r + j];
       }
       cp[j] = np > 0 ? static_cast<float>(sp / np) : 0.f;
       ca[j] = P.n > 0 ? static_cast<float>(sa / static_cast<double>(P.n)) : 0.f;
@@ -393,212 +420,202 @@ __global__ void __launch_bounds__(kThreads) solve_kernel(const __grid_constant__
       fp = fmaf(cp[i], bv, fp);
       fa = fmaf(ca[i], bv, fa);
     }
-    const float meanR = np > 0 ? P.sums[2 + 2 * RP + c] / np : 0.f;
+    const float meanR = np > 0 ? P.sums[RP + c] / np : 0.f;
     P.mu[c] = meanR - fp;
     P.subv[c] = fa;
     if (P.mu_out) P.mu_out[c] = meanR - fp;
     if (P.sub_out) P.sub_out[c] = fa;
   }
-  if (threadIdx.x == 0) P.subv[b.d] = fmaxf(P.n > 0 ? P.sums[0] / static_cast<float>(P.n) : 0.f, 1e-8f);
+  if (threadIdx.x == 0) P.subv[b.d] = fmaxf(P.n > 0 ? colsum[RP] / static_cast<float>(P.n) : 0.f, 1e-8f);
 }
 
 // ---------------------------------------------------------------------------------------
 // pass 2
 // ---------------------------------------------------------------------------------------
-template <int RP>
-struct Pass2Smem {
-  union {
-    struct {
-      float G[RP][RP + 1];   // G^-1
-      float Rt[kTM][RP + 1];  // rhs rows of the tile
-    } pro;
-    struct {
-      float Y[kTM][kKC + 1];                       // reused, then corrected values of a chunk
-      __nv_bfloat16 Bb[kKC][RP + kBP];             // basis rows of the chunk
-    } loop;
-  } u;
-  __nv_bfloat16 Cb[kTM][RP + kBP];  // codes of the tile (mma A operand)
-  float w[kTM], mus[kKC];
-  uint32_t fl[kTM];
-};
-
-template <int RP, int FDT>
-__global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__ Batch b) {
-  __shared__ __align__(16) Pass2Smem<RP> S;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const Prob &P = b.probs[find_prob(b, blockIdx.x)];
-  const int64_t t0 = (blockIdx.x - P.tile0) * kTM;
+template <int RP, int FDT, int MODE>
+__global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__ Batch b, int64_t tile_lo) {
+  __shared__ float Gs[RP][RP + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const Prob &P = b.probs[find_prob(b, tile_lo + blockIdx.x)];
+  for (int e = threadIdx.x; e < RP * RP; e += kThreads) Gs[e / RP][e % RP] = P.ginv[e];
+  __syncthreads();
+  const int64_t t0 = (tile_lo + blockIdx.x - P.tile0) * kTM + warp * kWT;
   const int64_t n = P.n;
+  if (t0 >= n) return;
+  constexpr int KS = RP / 16;
+  constexpr bool kmode = MODE == DKV_KIVI_PER_CHANNEL;
   const float mean_dist = P.subv[b.d];
-
-  // ---- prologue: codes = rhs G^-1 (fp32), token weights, probe flags ----
-  for (int e = tid; e < RP * RP; e += kThreads) S.u.pro.G[e / RP][e % RP] = P.ginv[e];
-  for (int e = tid; e < kTM * RP; e += kThreads) {
-    const int t = e / RP, k = e % RP;
-    S.u.pro.Rt[t][k] = (t0 + t < n) ? P.rhs[(t0 + t) * RP + k] : 0.f;
+  int64_t row[4];
+  bool rv[4], fl[4];
+  float w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    row[i] = t0 + g + 8 * i;
+    rv[i] = row[i] < n;
+    fl[i] = rv[i] && P.flag[row[i]] != 0u;
+    w[i] = rv[i] ? fminf(P.dist[row[i]] / mean_dist, 1.f) : 0.f;
   }
-  if (tid < kTM) {
-    const int64_t t = t0 + tid;
-    const bool v = t < n;
-    S.fl[tid] = v ? P.flag[t] : 0u;
-    S.w[tid] = v ? fminf(P.dist[t] / mean_dist, 1.f) : 0.f;
-  }
-  __syncthreads();
-  for (int e = tid; e < kTM * RP; e += kThreads) {
-    const int t = e / RP, k = e % RP;
-    float s = 0.f;
-#pragma unroll 8
-    for (int i = 0; i < RP; ++i) s = fmaf(S.u.pro.Rt[t][i], S.u.pro.G[i][k], s);
-    S.Cb[t][k] = __float2bfloat16_rn(s);
-  }
-  __syncthreads();
-
-  const int lt = tid >> 2, lc = (tid & 3) * 16;
-  const int64_t tok = t0 + lt;
-  const bool tv = tok < n;
-  const int mb = warp & 3, nb = warp >> 2;
-  const int g = lane >> 2, q = lane & 3;
-  const bool per_token = P.mode == DKV_KIVI_PER_TOKEN;
-
-  for (int64_t c0 = 0; c0 < b.d; c0 += kKC) {
-    // ---- reused values of the chunk, basis rows, orth_mu ----
-    {
-      float rv[16];
-      if (tv) deq16(P, tok, c0 + lc, rv);
-      else
+  // codes = rhs G^-1 at this lane's A-fragment positions (fp32), then bf16
+  uint32_t a[2][KS][4];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) rv[i] = 0.f;
+  for (int i = 0; i < 4; ++i) {
+    float cv[KS][4];  // k = 16 ks + 2q + {0, 1, 8, 9}
 #pragma unroll
-      for (int i = 0; i < 16; ++i) S.u.loop.Y[lt][lc + i] = rv[i];
-    }
-    for (int e = tid; e < kKC * (RP / 8); e += kThreads) {
-      const int c = e / (RP / 8), j = e % (RP / 8);
-      *reinterpret_cast<uint4 *>(&S.u.loop.Bb[c][8 * j]) =
-          *reinterpret_cast<const uint4 *>(P.bb + (c0 + c) * RP + 8 * j);
-    }
-    if (tid < kKC) S.mus[tid] = P.mu[c0 + tid];
-    __syncthreads();
-
-    // ---- fitted = codes B^T for 16 tokens x 32 channels per warp ----
-    float acc[4][4];
+    for (int ks = 0; ks < KS; ++ks) cv[ks][0] = cv[ks][1] = cv[ks][2] = cv[ks][3] = 0.f;
+    if (rv[i]) {
+      const float4 *rr = reinterpret_cast<const float4 *>(P.rhs + row[i] * RP);
+#pragma unroll 4
+      for (int i4 = 0; i4 < RP / 4; ++i4) {
+        const float4 x4 = rr[i4];
+        const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+        for (int u = 0; u < 4; ++u) {
+          const float x = xs[u];
+          const float *gr = Gs[4 * i4 + u];
 #pragma unroll
-    for (int ks = 0; ks < RP / 16; ++ks) {
-      uint32_t a0, a1, a2, a3;
-      ldmatrix_x4(a0, a1, a2, a3, smem_u32(&S.Cb[16 * mb + (lane & 15)][16 * ks + ((lane >> 4) << 3)]));
-#pragma unroll
-      for (int np = 0; np < 2; ++np) {
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4(b0, b1, b2, b3,
-                    smem_u32(&S.u.loop.Bb[32 * nb + 16 * np + ((lane >> 4) << 3) + (lane & 7)]
-                                         [16 * ks + (((lane >> 3) & 1) << 3)]));
-        mma16816_bf16(acc[2 * np], a0, a1, a2, a3, b0, b1);
-        mma16816_bf16(acc[2 * np + 1], a0, a1, a2, a3, b2, b3);
-      }
-    }
-    // ---- corr = reused + fitted + w orth_mu; probes take fresh ----
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int row = 16 * mb + g + 8 * h;
-        const int col = 32 * nb + 8 * nt + 2 * q;
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          float v;
-          if (S.fl[row]) {
-            v = load1<FDT>(P.fresh, (t0 + row) * P.frs + c0 + col + e);
-          } else {
-            v = __fadd_rn(__fadd_rn(S.u.loop.Y[row][col + e], acc[nt][2 * h + e]),
-                          __fmul_rn(S.w[row], S.mus[col + e]));
+          for (int ks = 0; ks < KS; ++ks) {
+            const int k0 = 16 * ks + 2 * q;
+            cv[ks][0] = fmaf(x, gr[k0], cv[ks][0]);
+            cv[ks][1] = fmaf(x, gr[k0 + 1], cv[ks][1]);
+            cv[ks][2] = fmaf(x, gr[k0 + 8], cv[ks][2]);
+            cv[ks][3] = fmaf(x, gr[k0 + 9], cv[ks][3]);
           }
-          S.u.loop.Y[row][col + e] = v;
         }
       }
     }
-    __syncthreads();
+    const int m = i >> 1, h = i & 1;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      a[m][ks][h] = pack_bf16x2(cv[ks][0], cv[ks][1]);
+      a[m][ks][2 + h] = pack_bf16x2(cv[ks][2], cv[ks][3]);
+    }
+  }
 
-    // ---- requantise the chunk ----
-    if (per_token) {
-      // (token, 32-channel group) per thread pair, 16 channels each
-      const int item = tid >> 1, half = tid & 1;
-      const int rt = item >> 1, gg = item & 1;
-      const int cb = 32 * gg + 16 * half;
-      float x[16];
-      float lo = INFINITY, hi = -INFINITY;
+  const uint2 *b2 = reinterpret_cast<const uint2 *>(P.b2) + lane;
+  const int n_blocks = static_cast<int>(b.d / kCB);
+  const int64_t krow = t0 / kivi::kG;
+  for (int cb = 0; cb < n_blocks; ++cb) {
+    const int64_t c = static_cast<int64_t>(cb) * kCB + 8 * q;
+    float acc[2][4][4];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        x[j] = S.u.loop.Y[rt][cb + j];
-        lo = fminf(lo, x[j]);
-        hi = fmaxf(hi, x[j]);
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) acc[m][nt][0] = acc[m][nt][1] = acc[m][nt][2] = acc[m][nt][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const uint2 bv = b2[((static_cast<int64_t>(cb) * KS + ks) * 4 + nt) * 32];
+#pragma unroll
+        for (int m = 0; m < 2; ++m) mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], bv.x, bv.y);
       }
-      lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, 1));
-      hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, 1));
-      __half s16, z16;
-      kivi::group_params(lo, hi, s16, z16);
-      const float s = __half2float(s16), z = __half2float(z16);
-      uint32_t wq[2] = {0u, 0u};
+    }
+    float mu8[8];
+    {
+      const float4 *mp = reinterpret_cast<const float4 *>(P.mu + c);
+      const float4 x = mp[0], y = mp[1];
+      mu8[0] = x.x, mu8[1] = x.y, mu8[2] = x.z, mu8[3] = x.w, mu8[4] = y.x, mu8[5] = y.y, mu8[6] = y.z, mu8[7] = y.w;
+    }
+    float ks8[8], kz8[8];
+    if (kmode) {
+      halves8(P.scale + krow * P.szrs + c, ks8);
+      halves8(P.zero + krow * P.szrs + c, kz8);
+    }
+    float v[4][8];  // corrected values: rows g + 8i, channels 8q + j
 #pragma unroll
-      for (int j = 0; j < 16; ++j) wq[j >> 3] |= kivi::quant_one(x[j], s, z) << (4 * (j & 7));
-      const int64_t t = t0 + rt;
-      if (t < n) {
-        *reinterpret_cast<uint2 *>(P.o_codes + t * P.o_crs + (c0 + cb) / 2) = make_uint2(wq[0], wq[1]);
-        if (half == 0) {
-          P.o_scale[t * P.o_szrs + (c0 + 32 * gg) / kivi::kG] = s16;
-          P.o_zero[t * P.o_szrs + (c0 + 32 * gg) / kivi::kG] = z16;
+    for (int i = 0; i < 4; ++i) {
+      const int m = i >> 1, h = i & 1;
+      if (fl[i]) {
+        float f[8];
+        load8<FDT>(P.fresh, row[i] * P.frs + c, f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = f[j];
+      } else if (rv[i]) {
+        const uint32_t wq = *reinterpret_cast<const uint32_t *>(P.codes + row[i] * P.crs + c / 2);
+        float vs = 0.f, vz = 0.f;
+        if (!kmode) {
+          vs = __half2float(P.scale[row[i] * P.szrs + cb]);
+          vz = __half2float(P.zero[row[i] * P.szrs + cb]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float reused = kivi::deq((wq >> (4 * j)) & 0xFu, kmode ? ks8[j] : vs, kmode ? kz8[j] : vz);
+          v[i][j] = __fadd_rn(__fadd_rn(reused, acc[m][j >> 1][2 * h + (j & 1)]), __fmul_rn(w[i], mu8[j]));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+      }
+    }
+    // requantise
+    if (!kmode) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float lo = v[i][0], hi = v[i][0];
+#pragma unroll
+        for (int j = 1; j < 8; ++j) {
+          lo = fminf(lo, v[i][j]);
+          hi = fmaxf(hi, v[i][j]);
+        }
+        lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, 1));
+        hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, 1));
+        lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, 2));
+        hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, 2));
+        __half s16, z16;
+        kivi::group_params(lo, hi, s16, z16);
+        const float s = __half2float(s16), z = __half2float(z16);
+        const float inv = s > 0.f ? __frcp_rn(s) : 0.f;
+        uint32_t wq = 0u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wq |= kivi::quant_one_fast(v[i][j], s, z, inv) << (4 * j);
+        if (rv[i]) {
+          *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = wq;
+          if (q == 0) {
+            P.o_scale[row[i] * P.o_szrs + cb] = s16;
+            P.o_zero[row[i] * P.o_szrs + cb] = z16;
+          }
         }
       }
     } else {
-      // (channel pair, 32-token group) per 4 threads, 8 tokens each
-      const int item = tid >> 2, quarter = tid & 3;
-      const int cp2 = item & 31, tg = item >> 5;
-      const int64_t gt0 = t0 + 32 * tg;
-      const int cnt = static_cast<int>(n - gt0 < 32 ? (n - gt0 > 0 ? n - gt0 : 0) : 32);
-      float x0[8], x1[8];
-      float lo0 = INFINITY, hi0 = -INFINITY, lo1 = INFINITY, hi1 = -INFINITY;
+      uint32_t wq[4] = {0u, 0u, 0u, 0u};
+      uint32_t sh[4], zh[4];  // packed fp16 scale / zero of the lane's 8 channels
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int rt = 32 * tg + 8 * quarter + j;
-        x0[j] = S.u.loop.Y[rt][2 * cp2];
-        x1[j] = S.u.loop.Y[rt][2 * cp2 + 1];
-        if (8 * quarter + j < cnt) {
-          lo0 = fminf(lo0, x0[j]);
-          hi0 = fmaxf(hi0, x0[j]);
-          lo1 = fminf(lo1, x1[j]);
-          hi1 = fmaxf(hi1, x1[j]);
-        }
-      }
+        float lo = INFINITY, hi = -INFINITY;
 #pragma unroll
-      for (int o = 1; o < 4; o <<= 1) {
-        lo0 = fminf(lo0, __shfl_xor_sync(0xffffffffu, lo0, o));
-        hi0 = fmaxf(hi0, __shfl_xor_sync(0xffffffffu, hi0, o));
-        lo1 = fminf(lo1, __shfl_xor_sync(0xffffffffu, lo1, o));
-        hi1 = fmaxf(hi1, __shfl_xor_sync(0xffffffffu, hi1, o));
-      }
-      if (cnt > 0) {
-        __half s0h, z0h, s1h, z1h;
-        kivi::group_params(lo0, hi0, s0h, z0h);
-        kivi::group_params(lo1, hi1, s1h, z1h);
-        const float s0 = __half2float(s0h), z0 = __half2float(z0h);
-        const float s1 = __half2float(s1h), z1 = __half2float(z1h);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (8 * quarter + j < cnt) {
-            const uint32_t byte = kivi::quant_one(x0[j], s0, z0) | (kivi::quant_one(x1[j], s1, z1) << 4);
-            P.o_codes[(gt0 + 8 * quarter + j) * P.o_crs + c0 / 2 + cp2] = static_cast<uint8_t>(byte);
+        for (int i = 0; i < 4; ++i)
+          if (rv[i]) {
+            lo = fminf(lo, v[i][j]);
+            hi = fmaxf(hi, v[i][j]);
           }
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+          hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
         }
-        if (quarter == 0) {
-          const int64_t so = (gt0 / kivi::kG) * P.o_szrs + c0 + 2 * cp2;
-          P.o_scale[so] = s0h;
-          P.o_scale[so + 1] = s1h;
-          P.o_zero[so] = z0h;
-          P.o_zero[so + 1] = z1h;
+        __half s16, z16;
+        kivi::group_params(lo, hi, s16, z16);
+        const float s = __half2float(s16), z = __half2float(z16);
+        const float inv = s > 0.f ? __frcp_rn(s) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) wq[i] |= kivi::quant_one_fast(v[i][j], s, z, inv) << (4 * j);
+        const uint32_t sb = __half_as_ushort(s16), zb = __half_as_ushort(z16);
+        if (j & 1) {
+          sh[j >> 1] |= sb << 16;
+          zh[j >> 1] |= zb << 16;
+        } else {
+          sh[j >> 1] = sb;
+          zh[j >> 1] = zb;
         }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (rv[i]) *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = wq[i];
+      if (g == 0) {
+        *reinterpret_cast<uint4 *>(P.o_scale + krow * P.o_szrs + c) = make_uint4(sh[0], sh[1], sh[2], sh[3]);
+        *reinterpret_cast<uint4 *>(P.o_zero + krow * P.o_szrs + c) = make_uint4(zh[0], zh[1], zh[2], zh[3]);
       }
     }
-    __syncthreads();
   }
 }
 
@@ -609,7 +626,7 @@ inline int64_t al(int64_t x) { return (x + 255) / 256 * 256; }
 
 struct Layout {
   int64_t zero_begin, zero_end, total;
-  std::vector<int64_t> flag, sums, rhs, dist, ginv, mu, subv, bt, bb;
+  std::vector<int64_t> flag, ucount, sums, uprobe, rhs, dist, part, ginv, mu, subv, b1, b2, bb;
 };
 
 inline int padded_rank(const dkv_kivi_subspace_problem *p, int np) {
@@ -627,23 +644,32 @@ inline Layout layout(const dkv_kivi_subspace_problem *p, int np, int64_t d, int 
     const int64_t n = p[i].base.n_tokens;
     L.flag.push_back(o);
     o = al(o + n * 4);
+    L.ucount.push_back(o);
+    o = al(o + 4);
     L.sums.push_back(o);
-    o = al(o + (2 + 2 * rp + d) * 4);
+    o = al(o + (rp + d) * 4);
   }
   L.zero_end = o;
   for (int i = 0; i < np; ++i) {
     const int64_t n = p[i].base.n_tokens;
+    const int64_t npr = p[i].n_probes > 0 ? p[i].n_probes : 1;
+    L.uprobe.push_back(o);
+    o = al(o + npr * 4);
     L.rhs.push_back(o);
     o = al(o + n * rp * 4);
     L.dist.push_back(o);
     o = al(o + n * 4);
+    L.part.push_back(o);
+    o = al(o + ((n + kWT - 1) / kWT) * (rp + 1) * 4);
     L.ginv.push_back(o);
     o = al(o + static_cast<int64_t>(rp) * rp * 4);
     L.mu.push_back(o);
     o = al(o + d * 4);
     L.subv.push_back(o);
     o = al(o + (d + 1) * 4);
-    L.bt.push_back(o);
+    L.b1.push_back(o);
+    o = al(o + rp * d * 2);
+    L.b2.push_back(o);
     o = al(o + rp * d * 2);
     L.bb.push_back(o);
     o = al(o + rp * d * 2);
@@ -669,7 +695,7 @@ int validate(const dkv_kivi_subspace_problem *p, int np, int64_t &d, int &fdt) {
   if (p == nullptr || np <= 0 || np > kMaxProblems) return DKV_ERR_INVALID_ARGUMENT;
   d = p[0].base.d;
   fdt = p[0].fresh_dtype;
-  if (d <= 0 || d % kKC) return DKV_ERR_UNSUPPORTED;
+  if (d <= 0 || d % kCB) return DKV_ERR_UNSUPPORTED;
   if (fdt != DKV_F32 && fdt != DKV_F16 && fdt != DKV_BF16) return DKV_ERR_UNSUPPORTED;
   const int esz = fdt == DKV_F32 ? 4 : 2;
   for (int i = 0; i < np; ++i) {
@@ -687,13 +713,14 @@ int validate(const dkv_kivi_subspace_problem *p, int np, int64_t &d, int &fdt) {
     if (q.out.mode != q.base.mode) return DKV_ERR_INVALID_ARGUMENT;
     if (q.fresh == nullptr || !a16(q.fresh) || (q.fresh_row_stride * esz) % 16 || q.fresh_row_stride < d)
       return DKV_ERR_ALIGNMENT;
-    if (q.n_probes < 0 || (q.n_probes > 0 && q.probe_index == nullptr)) return DKV_ERR_INVALID_ARGUMENT;
+    if (q.n_probes < 0 || q.n_probes > n || (q.n_probes > 0 && q.probe_index == nullptr))
+      return DKV_ERR_INVALID_ARGUMENT;
   }
   return DKV_OK;
 }
 
 template <int RP, int FDT>
-int launch(const Batch &b, int np, int64_t max_probes, cudaStream_t st) {
+int launch(const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStream_t st) {
   if (max_probes > 0) {
     const int bx = static_cast<int>((max_probes + 255) / 256 < 64 ? (max_probes + 255) / 256 : 64);
     flags_kernel<<<dim3(bx, np), 256, 0, st>>>(b);
@@ -705,28 +732,42 @@ int launch(const Batch &b, int np, int64_t max_probes, cudaStream_t st) {
     pack_kernel<<<dim3(bx, np), 256, 0, st>>>(b, RP);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
-  if (b.n_tiles > 0) {
-    pass1_kernel<RP, FDT><<<static_cast<unsigned>(b.n_tiles), kThreads, 0, st>>>(b);
+  // the table holds the K (per-channel) problems first (tiles [0, k_tiles)), then the V ones
+  if (k_tiles > 0) {
+    pass1_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL><<<static_cast<unsigned>(k_tiles), kThreads, 0, st>>>(b, 0);
+    DKV_CUDA_CHECK(cudaGetLastError());
+  }
+  if (b.n_tiles > k_tiles) {
+    pass1_kernel<RP, FDT, DKV_KIVI_PER_TOKEN><<<static_cast<unsigned>(b.n_tiles - k_tiles), kThreads, 0, st>>>(b, k_tiles);
+    DKV_CUDA_CHECK(cudaGetLastError());
+  }
+  if (max_probes > 0) {
+    const int slices = static_cast<int>((b.d + 127) / 128) + 1;
+    psum_kernel<RP, FDT><<<dim3(slices, kPsumSplit, np), 128, 0, st>>>(b);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   const int solve_smem = kMaxRank * (2 * kMaxRank + 1) * 8;
   DKV_CUDA_CHECK(cudaFuncSetAttribute(solve_kernel<RP>, cudaFuncAttributeMaxDynamicSharedMemorySize, solve_smem));
-  solve_kernel<RP><<<np, kThreads, solve_smem, st>>>(b);
+  solve_kernel<RP><<<np, 256, solve_smem, st>>>(b);
   DKV_CUDA_CHECK(cudaGetLastError());
-  if (b.n_tiles > 0) {
-    pass2_kernel<RP, FDT><<<static_cast<unsigned>(b.n_tiles), kThreads, 0, st>>>(b);
+  if (k_tiles > 0) {
+    pass2_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL><<<static_cast<unsigned>(k_tiles), kThreads, 0, st>>>(b, 0);
+    DKV_CUDA_CHECK(cudaGetLastError());
+  }
+  if (b.n_tiles > k_tiles) {
+    pass2_kernel<RP, FDT, DKV_KIVI_PER_TOKEN><<<static_cast<unsigned>(b.n_tiles - k_tiles), kThreads, 0, st>>>(b, k_tiles);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   return DKV_OK;
 }
 
 template <int FDT>
-int launch_rp(int rp, const Batch &b, int np, int64_t max_probes, cudaStream_t st) {
+int launch_rp(int rp, const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStream_t st) {
   switch (rp) {
-    case 16: return launch<16, FDT>(b, np, max_probes, st);
-    case 32: return launch<32, FDT>(b, np, max_probes, st);
-    case 48: return launch<48, FDT>(b, np, max_probes, st);
-    case 64: return launch<64, FDT>(b, np, max_probes, st);
+    case 16: return launch<16, FDT>(b, np, max_probes, k_tiles, st);
+    case 32: return launch<32, FDT>(b, np, max_probes, k_tiles, st);
+    case 48: return launch<48, FDT>(b, np, max_probes, k_tiles, st);
+    case 64: return launch<64, FDT>(b, np, max_probes, k_tiles, st);
     default: return DKV_ERR_UNSUPPORTED;
   }
 }
@@ -759,13 +800,18 @@ extern "C" int dkv_kivi_subspace_correct(const dkv_kivi_subspace_problem *proble
   const Layout L = layout(problems, n_problems, d, rp);
   if (workspace == nullptr || workspace_bytes < L.total || !a16(workspace)) return DKV_ERR_WORKSPACE;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
-  static thread_local Batch b;  // ~25 KB: not on the caller's stack
+  static thread_local Batch b;  // ~30 KB: not on the caller's stack
   memset(&b, 0, sizeof(b));
-  int64_t tiles = 0, max_probes = 0;
-  for (int i = 0; i < n_problems; ++i) {
+  // the table holds the K (per-channel) problems first, then the V ones: one launch per mode
+  std::vector<int> order;
+  for (int pass = 0; pass < 2; ++pass)
+    for (int i = 0; i < n_problems; ++i)
+      if ((problems[i].base.mode == DKV_KIVI_PER_CHANNEL) == (pass == 0)) order.push_back(i);
+  int64_t tiles = 0, max_probes = 0, k_tiles = 0;
+  for (int slot = 0; slot < n_problems; ++slot) {
+    const int i = order[slot];
     const dkv_kivi_subspace_problem &q = problems[i];
-    Prob &P = b.probs[i];
-    memset(&P, 0, sizeof(P));
+    Prob &P = b.probs[slot];
     P.codes = static_cast<const uint8_t *>(q.base.codes);
     P.scale = static_cast<const __half *>(q.base.scale);
     P.zero = static_cast<const __half *>(q.base.zero);
@@ -788,16 +834,21 @@ extern "C" int dkv_kivi_subspace_correct(const dkv_kivi_subspace_problem *proble
     P.r = (q.n_probes > 0 && q.basis != nullptr) ? q.rank : 0;
     P.basis = q.basis;
     P.flag = reinterpret_cast<uint32_t *>(ws + L.flag[i]);
+    P.ucount = reinterpret_cast<int32_t *>(ws + L.ucount[i]);
     P.sums = reinterpret_cast<float *>(ws + L.sums[i]);
+    P.uprobe = reinterpret_cast<int32_t *>(ws + L.uprobe[i]);
     P.rhs = reinterpret_cast<float *>(ws + L.rhs[i]);
     P.dist = reinterpret_cast<float *>(ws + L.dist[i]);
+    P.part = reinterpret_cast<float *>(ws + L.part[i]);
     P.ginv = reinterpret_cast<float *>(ws + L.ginv[i]);
     P.mu = reinterpret_cast<float *>(ws + L.mu[i]);
     P.subv = reinterpret_cast<float *>(ws + L.subv[i]);
-    P.bt = reinterpret_cast<__nv_bfloat16 *>(ws + L.bt[i]);
+    P.b1 = reinterpret_cast<__nv_bfloat16 *>(ws + L.b1[i]);
+    P.b2 = reinterpret_cast<__nv_bfloat16 *>(ws + L.b2[i]);
     P.bb = reinterpret_cast<__nv_bfloat16 *>(ws + L.bb[i]);
     P.tile0 = tiles;
     tiles += (P.n + kTM - 1) / kTM;
+    if (P.mode == DKV_KIVI_PER_CHANNEL) k_tiles = tiles;
     if (P.n_probes > max_probes) max_probes = P.n_probes;
   }
   if (tiles > 0x7fffffffLL) return DKV_ERR_UNSUPPORTED;
@@ -808,9 +859,9 @@ extern "C" int dkv_kivi_subspace_correct(const dkv_kivi_subspace_problem *proble
   b.n_tiles = tiles;
   b.status = status;
   switch (fdt) {
-    case DKV_BF16: rc = launch_rp<DKV_BF16>(rp, b, n_problems, max_probes, st); break;
-    case DKV_F16: rc = launch_rp<DKV_F16>(rp, b, n_problems, max_probes, st); break;
-    default: rc = launch_rp<DKV_F32>(rp, b, n_problems, max_probes, st); break;
+    case DKV_BF16: rc = launch_rp<DKV_BF16>(rp, b, n_problems, max_probes, k_tiles, st); break;
+    case DKV_F16: rc = launch_rp<DKV_F16>(rp, b, n_problems, max_probes, k_tiles, st); break;
+    default: rc = launch_rp<DKV_F32>(rp, b, n_problems, max_probes, k_tiles, st); break;
   }
   return rc;
 }

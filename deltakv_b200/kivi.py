@@ -110,8 +110,10 @@ class SubspaceProblem:
     ``basis`` ``[d, r]`` is the column space (V: the adapter's LoRA ``B``); ``None`` takes
     the top-``rank`` (at least 1) right singular vectors of the probe residual when there are
     two or more probes, as the reference's K path does (``svd_basis``,
-    src/deltakv/patches/subspace.py:37-42, 91-93); with fewer probes the correction is the
-    mean shift alone.
+    src/deltakv/patches/subspace.py:37-42, 91-93) — computed for all such problems of a
+    call by one batched subspace iteration (:func:`deltakv_b200.subspace.topr_basis`, exact
+    SVD where its gap estimate says the iteration is not converged); with fewer probes the
+    correction is the mean shift alone.
     ``out=None`` corrects ``base`` in place.
     """
 
@@ -123,11 +125,19 @@ class SubspaceProblem:
     out: KiviTensor | None = None
 
 
-def probe_residual(base: KiviTensor, fresh: Tensor, probe_index: Tensor) -> Tensor:
-    """``fresh[P] - dequant(base)[P]`` as fp32 ``[|P|, d]``."""
-    rows = probe_index.to(device=fresh.device, dtype=torch.long)
-    reused = dequantize(base)
-    return _rows(fresh).index_select(0, rows).float() - reused.index_select(0, rows)
+def probe_residual(base: KiviTensor, fresh: Tensor, probe_index: Tensor, out: Tensor | None = None) -> Tensor:
+    """``fresh[P] - dequant(base)[P]`` as fp32 ``[|P|, d]``, read straight from the int4 cache."""
+    f = _rows(fresh)
+    rows = probe_index.to(device=f.device, dtype=torch.int32).contiguous()
+    if out is None:
+        out = torch.empty(rows.numel(), base.d, dtype=torch.float32, device=f.device)
+    desc = base.desc()
+    st = ops.status_word(f.device)
+    rc = L.lib().dkv_kivi_probe_residual(C.byref(desc), f.data_ptr(), ops.dkv_dtype(f.dtype), f.stride(0),
+                                         rows.data_ptr(), rows.numel(), out.data_ptr(), out.stride(0), st.ptr,
+                                         ops.stream_ptr())
+    L.check(rc, "dkv_kivi_probe_residual")
+    return out
 
 
 def subspace_correct(problems: list[SubspaceProblem], *, stats: bool = False, check: bool = True):
@@ -145,18 +155,28 @@ def subspace_correct(problems: list[SubspaceProblem], *, stats: bool = False, ch
     keep = []  # tensors that must stay alive until the launches are queued
     descs = []
     results = []
-    for pb in problems:
+    # bases from the probe residual (the K path): one batched subspace iteration per shape
+    need = {}
+    for i, pb in enumerate(problems):
+        if pb.basis is None and pb.probe_index.numel() >= 2:
+            m, d = pb.probe_index.numel(), pb.base.d
+            need.setdefault((m, d, min(int(pb.rank), max(1, m - 1), d)), []).append(i)
+    svd = {}
+    for (m, d, r), idx in need.items():
+        res = torch.empty(len(idx), m, d, dtype=torch.float32, device=dev)
+        for j, i in enumerate(idx):
+            probe_residual(problems[i].base, problems[i].fresh, problems[i].probe_index, out=res[j])
+        bases = dense_sub.topr_basis(res, r)
+        for j, i in enumerate(idx):
+            svd[i] = bases[j]
+    for i, pb in enumerate(problems):
         fresh = _rows(pb.fresh)
         ops._require_cuda(fresh, pb.probe_index)
         n, d = pb.base.n_tokens, pb.base.d
         if fresh.shape != (n, d):
             raise ValueError(f"fresh {tuple(fresh.shape)} does not match the int4 base ({n}, {d})")
         probes = pb.probe_index.to(device=dev, dtype=torch.int32).contiguous()
-        basis = pb.basis
-        rank = int(pb.rank)
-        if basis is None and probes.numel() >= 2:  # reference: svd_basis keeps at least rank 1
-            r_eff = min(rank, max(1, probes.numel() - 1), d)
-            basis = dense_sub.svd_basis(probe_residual(pb.base, fresh, probes), r_eff)
+        basis = pb.basis if pb.basis is not None else svd.get(i)  # svd_basis keeps at least rank 1
         if basis is not None:
             if basis.shape[0] != d:
                 raise ValueError(f"basis d={basis.shape[0]} != kv d={d}")

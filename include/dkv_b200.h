@@ -327,6 +327,12 @@ int dkv_kivi_dequantize(const dkv_kivi_cache *in, void *x, int32_t x_dtype, int6
 int dkv_kivi_patch(const dkv_kivi_cache *base, const void *delta, int32_t delta_dtype,
                    int64_t delta_row_stride, const dkv_kivi_cache *out, dkv_stream_t stream);
 
+/* out[i, :] = fresh[rows[i], :] - dequant(base)[rows[i], :] as fp32 (the probe residual of
+   the subspace route's K basis, subspace.py:86-93, read straight from the int4 cache). */
+int dkv_kivi_probe_residual(const dkv_kivi_cache *base, const void *fresh, int32_t fresh_dtype,
+                            int64_t fresh_row_stride, const int32_t *rows, int64_t n_rows, float *out,
+                            int64_t out_row_stride, int32_t *status, dkv_stream_t stream);
+
 /* ---- subspace route -------------------------------------------------------- */
 
 /*
@@ -338,7 +344,7 @@ int dkv_kivi_patch(const dkv_kivi_cache *base, const void *delta, int32_t delta_
  * and out = KIVI-quantised corr (same grouping as base; out may be base itself).  Without a
  * basis, or with no probe, corr = reused + w mean_P(R) as in the reference.  Probe indices
  * are deduplicated.  All problems of one call share d (a multiple of 64) and the fresh
- * dtype; at most 128 problems, ranks <= 64.  The basis products run on tensor cores with
+ * dtype; at most 112 problems, ranks <= 64.  The basis products run on tensor cores with
  * bf16 operands (the basis, R and the codes rounded to bf16) and fp32 accumulation.
  */
 typedef struct dkv_kivi_subspace_problem {

@@ -25,6 +25,9 @@ __device__ __forceinline__ uint32_t quant_one(float x, float s, float z) {
   return static_cast<uint32_t>(v);
 }
 
+// the exact quotient, kept out of line so the common path does not carry the division
+static __device__ __noinline__ float exact_quotient(float a, float s) { return __fdiv_rn(a, s); }
+
 // Same result as quant_one, with the group's reciprocal: y = (x - z) * (1/s) is within 2 ulp
 // of the IEEE quotient (|y| < 16, so 2 ulp < 4e-6), hence rint(y) equals rint(quotient) unless
 // y lies within that distance of a rounding tie; there (|frac(y) - 1/2| < 1e-5) the quotient
@@ -33,12 +36,27 @@ __device__ __forceinline__ uint32_t quant_one_fast(float x, float s, float z, fl
   if (!(s > 0.f)) return 0u;
   const float a = __fsub_rn(x, z);
   float y = __fmul_rn(a, inv);
-  if (fabsf(y - floorf(y) - 0.5f) < 1e-5f) y = __fdiv_rn(a, s);
+  if (__builtin_expect(fabsf(y - floorf(y) - 0.5f) < 1e-5f, 0)) y = exact_quotient(a, s);
   return static_cast<uint32_t>(fminf(fmaxf(rintf(y), 0.f), 15.f));
 }
 
 // a 4-bit code as a float (exact): 2^23 + q built in the mantissa, minus 2^23
 __device__ __forceinline__ float code_to_f(uint32_t q) { return __int_as_float(0x4B000000u | q) - 8388608.f; }
+
+// codes 2p, 2p+1 of a packed word as an fp32 pair (exact)
+__device__ __forceinline__ uint64_t codes_to_f2(uint32_t w, int p) {
+  const uint32_t lo = 0x4B000000u | ((w >> (8 * p)) & 0xFu), hi = 0x4B000000u | ((w >> (8 * p + 4)) & 0xFu);
+  return sub2(f2pack(__uint_as_float(lo), __uint_as_float(hi)), f2pack(8388608.f, 8388608.f));
+}
+
+// quant_one_fast for y = (x - z) / s already formed with the reciprocal: rint, the tie fallback,
+// saturating conversion (negative -> 0) and the clamp to 15
+__device__ __forceinline__ uint32_t quant_from_y(float y, float a, float s) {
+  if (!(s > 0.f)) return 0u;
+  if (__builtin_expect(fabsf(y - floorf(y) - 0.5f) < 1e-5f, 0)) y = exact_quotient(a, s);
+  const uint32_t q = __float2uint_rn(y);
+  return q < 15u ? q : 15u;
+}
 
 __device__ __forceinline__ void quant_group(const float (&x)[kG], int cnt, uint8_t (&q)[kG], __half &s16,
                                             __half &z16) {

@@ -42,7 +42,7 @@ constexpr int kThreads = 32 * kWarps;
 constexpr int kTM = kWT * kWarps;  // tokens per CTA
 constexpr int kCB = 32;            // channels per block
 constexpr int kMaxRank = 64;
-constexpr int kPsumSplit = 16;  // probe-sum CTAs per channel slice
+constexpr int kPsumSplit = 64;  // probe-sum CTAs per channel slice
 
 struct Prob {
   const uint8_t *codes;
@@ -238,12 +238,19 @@ __global__ void __launch_bounds__(kThreads) pass1_kernel(const __grid_constant__
           vs = __half2float(P.scale[row[i] * P.szrs + cb]);
           vz = __half2float(P.zero[row[i] * P.szrs + cb]);
         }
+        uint64_t dd2 = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float reused = kivi::deq((w >> (4 * j)) & 0xFu, kmode ? ks8[j] : vs, kmode ? kz8[j] : vz);
-          r[j] = f[j] - reused;
-          d2[i] = fmaf(r[j], r[j], d2[i]);
+        for (int p = 0; p < 4; ++p) {
+          const uint64_t s2 = kmode ? f2pack(ks8[2 * p], ks8[2 * p + 1]) : f2pack(vs, vs);
+          const uint64_t z2 = kmode ? f2pack(kz8[2 * p], kz8[2 * p + 1]) : f2pack(vz, vz);
+          const uint64_t reused2 = add2(mul2(kivi::codes_to_f2(w, p), s2), z2);
+          const uint64_t r2 = sub2(f2pack(f[2 * p], f[2 * p + 1]), reused2);
+          dd2 = fma2(r2, r2, dd2);
+          f2unpack(r2, r[2 * p], r[2 * p + 1]);
         }
+        float e0, e1;
+        f2unpack(dd2, e0, e1);
+        d2[i] += e0 + e1;
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) r[j] = 0.f;
@@ -359,13 +366,42 @@ __global__ void __launch_bounds__(256) solve_kernel(const __grid_constant__ Batc
   }
   __syncthreads();
   if (r > 0) {
-    for (int e = threadIdx.x; e < r * r; e += blockDim.x) {
-      const int i = e / r, j = e % r;
-      double s = 0.0;
-      for (int64_t c = 0; c < b.d; ++c)
-        s += static_cast<double>(__bfloat162float(P.bb[c * RP + i])) * __bfloat162float(P.bb[c * RP + j]);
-      Mdyn[i * ldm + j] = s + (i == j ? 1e-6 : 0.0);
-      Mdyn[i * ldm + r + j] = (i == j) ? 1.0 : 0.0;
+    // G = B~^T B~ + 1e-6 I: 64-channel tiles of B~ staged in shared memory (fp64 accumulation);
+    // the tile area is the not yet used part of Mdyn past [G | I]
+    double *tile = Mdyn + r * ldm;  // [64][RP] as float
+    float *tf = reinterpret_cast<float *>(tile);
+    constexpr int EPT = (RP * RP + 255) / 256;
+    double accg[EPT];
+#pragma unroll
+    for (int u = 0; u < EPT; ++u) accg[u] = 0.0;
+    for (int64_t c0 = 0; c0 < b.d; c0 += 64) {
+      for (int e = threadIdx.x; e < 64 * RP; e += blockDim.x) {
+        const int64_t c = c0 + e / RP;
+        tf[e] = c < b.d ? __bfloat162float(P.bb[c * RP + e % RP]) : 0.f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int u = 0; u < EPT; ++u) {
+        const int e = threadIdx.x + 256 * u;
+        if (e < RP * RP) {
+          const int i = e / RP, j = e % RP;
+          double s = 0.0;
+          for (int cc = 0; cc < 64; ++cc) s += static_cast<double>(tf[cc * RP + i]) * tf[cc * RP + j];
+          accg[u] += s;
+        }
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int u = 0; u < EPT; ++u) {
+      const int e = threadIdx.x + 256 * u;
+      if (e < RP * RP) {
+        const int i = e / RP, j = e % RP;
+        if (i < r && j < r) {
+          Mdyn[i * ldm + j] = accg[u] + (i == j ? 1e-6 : 0.0);
+          Mdyn[i * ldm + r + j] = (i == j) ? 1.0 : 0.0;
+        }
+      }
     }
     __syncthreads();
     for (int col = 0; col < r; ++col) {
@@ -510,18 +546,26 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
         for (int m = 0; m < 2; ++m) mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], bv.x, bv.y);
       }
     }
-    float mu8[8];
+    uint64_t mu2[4];
     {
       const float4 *mp = reinterpret_cast<const float4 *>(P.mu + c);
       const float4 x = mp[0], y = mp[1];
-      mu8[0] = x.x, mu8[1] = x.y, mu8[2] = x.z, mu8[3] = x.w, mu8[4] = y.x, mu8[5] = y.y, mu8[6] = y.z, mu8[7] = y.w;
+      mu2[0] = f2pack(x.x, x.y), mu2[1] = f2pack(x.z, x.w), mu2[2] = f2pack(y.x, y.y), mu2[3] = f2pack(y.z, y.w);
     }
-    float ks8[8], kz8[8];
+    uint64_t ks2[4], kz2[4];  // K: scale / zero of channels (2p, 2p+1)
     if (kmode) {
+      float ks8[8], kz8[8];
       halves8(P.scale + krow * P.szrs + c, ks8);
       halves8(P.zero + krow * P.szrs + c, kz8);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        ks2[p] = f2pack(ks8[2 * p], ks8[2 * p + 1]);
+        kz2[p] = f2pack(kz8[2 * p], kz8[2 * p + 1]);
+      }
     }
-    float v[4][8];  // corrected values: rows g + 8i, channels 8q + j
+    // corrected values: rows g + 8i, channels 8q + j; (reused + fitted) + w orth_mu in packed
+    // fp32 pairs, each operation rounded as the scalar form
+    float v[4][8];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int m = i >> 1, h = i & 1;
@@ -532,15 +576,19 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
         for (int j = 0; j < 8; ++j) v[i][j] = f[j];
       } else if (rv[i]) {
         const uint32_t wq = *reinterpret_cast<const uint32_t *>(P.codes + row[i] * P.crs + c / 2);
-        float vs = 0.f, vz = 0.f;
+        uint64_t vs2 = 0, vz2 = 0;
         if (!kmode) {
-          vs = __half2float(P.scale[row[i] * P.szrs + cb]);
-          vz = __half2float(P.zero[row[i] * P.szrs + cb]);
+          const float vs = __half2float(P.scale[row[i] * P.szrs + cb]);
+          const float vz = __half2float(P.zero[row[i] * P.szrs + cb]);
+          vs2 = f2pack(vs, vs);
+          vz2 = f2pack(vz, vz);
         }
+        const uint64_t w2 = f2pack(w[i], w[i]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float reused = kivi::deq((wq >> (4 * j)) & 0xFu, kmode ? ks8[j] : vs, kmode ? kz8[j] : vz);
-          v[i][j] = __fadd_rn(__fadd_rn(reused, acc[m][j >> 1][2 * h + (j & 1)]), __fmul_rn(w[i], mu8[j]));
+        for (int p = 0; p < 4; ++p) {
+          const uint64_t r2 = add2(mul2(kivi::codes_to_f2(wq, p), kmode ? ks2[p] : vs2), kmode ? kz2[p] : vz2);
+          const uint64_t c2 = add2(add2(r2, f2pack(acc[m][p][2 * h], acc[m][p][2 * h + 1])), mul2(w2, mu2[p]));
+          f2unpack(c2, v[i][2 * p], v[i][2 * p + 1]);
         }
       } else {
 #pragma unroll
@@ -565,9 +613,17 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
         kivi::group_params(lo, hi, s16, z16);
         const float s = __half2float(s16), z = __half2float(z16);
         const float inv = s > 0.f ? __frcp_rn(s) : 0.f;
+        const uint64_t z2 = f2pack(z, z), inv2 = f2pack(inv, inv);
         uint32_t wq = 0u;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) wq |= kivi::quant_one_fast(v[i][j], s, z, inv) << (4 * j);
+        for (int p = 0; p < 4; ++p) {
+          const uint64_t a2 = sub2(f2pack(v[i][2 * p], v[i][2 * p + 1]), z2);
+          float a0, a1, y0, y1;
+          f2unpack(a2, a0, a1);
+          f2unpack(mul2(a2, inv2), y0, y1);
+          wq |= kivi::quant_from_y(y0, a0, s) << (8 * p);
+          wq |= kivi::quant_from_y(y1, a1, s) << (8 * p + 4);
+        }
         if (rv[i]) {
           *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = wq;
           if (q == 0) {
@@ -597,8 +653,16 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
         kivi::group_params(lo, hi, s16, z16);
         const float s = __half2float(s16), z = __half2float(z16);
         const float inv = s > 0.f ? __frcp_rn(s) : 0.f;
+        const uint64_t z2 = f2pack(z, z), inv2 = f2pack(inv, inv);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) wq[i] |= kivi::quant_one_fast(v[i][j], s, z, inv) << (4 * j);
+        for (int i = 0; i < 4; i += 2) {
+          const uint64_t a2 = sub2(f2pack(v[i][j], v[i + 1][j]), z2);
+          float a0, a1, y0, y1;
+          f2unpack(a2, a0, a1);
+          f2unpack(mul2(a2, inv2), y0, y1);
+          wq[i] |= kivi::quant_from_y(y0, a0, s) << (4 * j);
+          wq[i + 1] |= kivi::quant_from_y(y1, a1, s) << (4 * j);
+        }
         const uint32_t sb = __half_as_ushort(s16), zb = __half_as_ushort(z16);
         if (j & 1) {
           sh[j >> 1] |= sb << 16;
@@ -746,7 +810,7 @@ int launch(const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStre
     psum_kernel<RP, FDT><<<dim3(slices, kPsumSplit, np), 128, 0, st>>>(b);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
-  const int solve_smem = kMaxRank * (2 * kMaxRank + 1) * 8;
+  const int solve_smem = kMaxRank * (2 * kMaxRank + 1) * 8 + 64 * RP * 4;
   DKV_CUDA_CHECK(cudaFuncSetAttribute(solve_kernel<RP>, cudaFuncAttributeMaxDynamicSharedMemorySize, solve_smem));
   solve_kernel<RP><<<np, 256, solve_smem, st>>>(b);
   DKV_CUDA_CHECK(cudaGetLastError());

@@ -70,7 +70,7 @@ def _orthonormalize(z: Tensor) -> Tensor:
     return q.float()
 
 
-def topr_basis(residual: Tensor, rank: int, *, iters: int = 6, oversample: int = 8) -> Tensor:
+def topr_basis(residual: Tensor, rank: int, *, iters: int = 3, oversample: int = 8) -> Tensor:
     """Leading-``rank`` right singular subspace of ``residual [..., m, d]`` as ``[..., d, rank]``,
     batched over a leading dimension.
 

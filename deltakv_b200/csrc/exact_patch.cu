@@ -1193,7 +1193,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], kEpiWarps);  // every epilogue warp reads its share of the codes
     }
     mbar_init(done, 1);
     *abort_flag = 0;
@@ -1292,8 +1292,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
       // after an abort the warps keep walking the tile sequence (same barriers) without work
       // (decisions are made warp-uniform: TMEM loads and mma.sync need every lane)
       bool have_codes = __all_sync(0xffffffffu, *abort_flag == 0);
-      if (warp < 4 && have_codes) {
-        // codes of row 32*warp + lane out of TMEM: combine terms, scale, f16 with a per-row exponent
+      // TMEM readout split over all 8 epilogue warps: warp w reads lane quarter w & 3 (rows
+      // 32 (w & 3) + lane), the K codes for w < 4 and the V codes for w >= 4
+      const int qw = warp & 3, kv_w = warp >> 2;
+      if (have_codes) {
+        // codes of row 32*qw + lane out of TMEM: combine terms, scale, f16 with a per-row exponent
         const bool ok = mbar_wait_bounded(&tfull[b], static_cast<uint32_t>(use & 1), abort_flag);
         have_codes = __all_sync(0xffffffffu, ok);
         if (!have_codes) {
@@ -1301,10 +1304,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
           *abort_flag = 1;
         }
       }
-      if (warp < 4 && have_codes) {
+      if (have_codes) {
         tc_fence_after();
-        const int row = 32 * warp + lane;
-        const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * warp) << 16) + b * C::BUF;
+        const int row = 32 * qw + lane;
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * qw) << 16) + b * C::BUF;
         const int tok = t.c0 + row;
         const int64_t grow = static_cast<int64_t>(t.row0) + row;
         float xs = 1.f;
@@ -1312,8 +1315,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
         float rs = xs;
         if (NORM) {
           float d0[16], d1[16];
-          tmem_ld16(taddr + C::DIAG + 32 * warp, d0);
-          tmem_ld16(taddr + C::DIAG + 32 * warp + 16, d1);
+          tmem_ld16(taddr + C::DIAG + 32 * qw, d0);
+          tmem_ld16(taddr + C::DIAG + 32 * qw + 16, d1);
           tmem_ld_wait();
           float ss = 0.f;
 #pragma unroll
@@ -1324,8 +1327,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
           rs = xs * rsqrtf(xs * xs * ss * p.inv_d + p.norm_eps);
         }
         const float *hdr = reinterpret_cast<const float *>(p.packed + t.layer * p.packed_stride);
-#pragma unroll
-        for (int kv = 0; kv < 2; ++kv) {
+        {
+          const int kv = kv_w;
           float c[RPAD];
 #pragma unroll
           for (int h = 0; h < R16; ++h) {

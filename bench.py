@@ -7,6 +7,7 @@ folded in) into bf16 paged K/V (block 16, permuted block table), RoPE on K.
 
     python bench.py [--gpus N --steps K --warmup W]          # this implementation
     python bench.py --impl reference ...                       # CPU reference arm
+    python bench.py --workload smollm2-exact ...               # exact route, SmolLM2-135M shape
     python bench.py --workload rl-dense ...                    # dense-dW (RL step) route
     python bench.py --workload multi-lora-kivi ...             # int4 KIVI subspace route
 
@@ -51,7 +52,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="llama8b-exact", choices=["llama8b-exact", "rl-dense", "multi-lora-kivi"])
+    ap.add_argument("--workload", default="llama8b-exact",
+                    choices=["llama8b-exact", "smollm2-exact", "rl-dense", "multi-lora-kivi"])
     ap.add_argument("--adapters", type=int, default=8)
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--seqs", type=int, default=None)
@@ -64,7 +66,24 @@ def parse():
 
 
 class Geo:
+    """The exact-route workload being measured (rebound by --workload)."""
     d_model, n_kv, hd, rank, bs, eps, rope_theta = 4096, 8, 128, 16, 16, 1e-5, 500000.0
+    layers, seqs, seq_len = 32, 64, 4096
+    x_torch, x_kind = torch.float8_e4m3fn, "e4m3"
+
+
+class SmolGeo(Geo):
+    """SmolLM2-135M shape: 30 layers, d=576, 3 KV heads x 64, rank-8 k/v LoRA, fp16 stored X."""
+    d_model, n_kv, hd, rank, bs, eps, rope_theta = 576, 3, 64, 8, 16, 1e-5, 10000.0
+    layers, seqs, seq_len = 30, 32, 2048
+    x_torch, x_kind = torch.float16, "f16"
+
+
+SMOL_METRIC = "patched token·layers/s (SmolLM2-135M shape, rank-8 k/v LoRA)"
+SMOL_BYTES_PER_UNIT = 1152 + 4 + 768 + 768  # X f16 + row scale + K read/write + V read/write
+SMOL_WORKLOAD = ("SmolLM2-135M-shaped exact patch: 30 layers, d=576, 3 KV heads x 64, 32 seqs x 2048 tokens, "
+                 "rank-8 k/v LoRA (rel. norm 1e-2), f16 stored X + power-of-two row scale, RMSNorm folded, "
+                 "RoPE (theta 1e4), bf16 paged KV block 16")
 
 
 class DenseGeo:
@@ -97,13 +116,13 @@ def make_workload(n_layers, n_seqs, seq_len, device, seed):
     G = Geo
     gen = torch.Generator(device=device).manual_seed(seed)
     rows = n_seqs * seq_len
-    x = torch.empty(n_layers, rows, G.d_model, dtype=torch.float8_e4m3fn, device=device)
+    x = torch.empty(n_layers, rows, G.d_model, dtype=G.x_torch, device=device)
     xs = torch.empty(n_layers, rows, dtype=torch.float32, device=device)
     for l in range(n_layers):
         # residual-stream-like rows: N(0,1) with a per-token magnitude spread
         h = torch.randn(rows, G.d_model, generator=gen, device=device)
         h *= (0.5 + torch.rand(rows, 1, generator=gen, device=device))
-        q, s = dkv.quantize_rows(h, torch.float8_e4m3fn)
+        q, s = dkv.quantize_rows(h, G.x_torch)
         x[l].copy_(q)
         xs[l].copy_(s)
         del h, q, s
@@ -215,7 +234,10 @@ class CpuSample:
             h = torch.randn(seq_len, G.d_model, generator=g) * (0.5 + torch.rand(seq_len, 1, generator=g))
             amax = h.abs().amax(-1).clamp_min(1e-12)
             s = (amax / 448.0).float()
-            xb = (h / s[:, None]).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+            if G.x_kind == "e4m3":
+                xb = (h / s[:, None]).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+            else:
+                xb = (h / s[:, None]).to(torch.float16).numpy()
             fk = (facs["k"][0][i].numpy(), facs["k"][1][i].numpy(), facs["k"][2])
             fv = (facs["v"][0][i].numpy(), facs["v"][1][i].numpy(), facs["v"][2])
             self.inputs.append((xb, s.numpy(), norm_w[i].numpy(), fk, fv))
@@ -238,7 +260,7 @@ class CpuSample:
 
         G = Geo
         xb, s, w, fk, fv = self.inputs[i % len(self.inputs)]
-        x = OX.dequant_x(xb, "e4m3", s)
+        x = OX.dequant_x(xb, G.x_kind, s)
         x = OX.rmsnorm(x, w, G.eps)
         dk, dv = OX.exact_kv_delta(x, fk, fv, G.n_kv, G.hd, self.rope)
         OX.scatter_into_paged(dk, kp, self.table, G.bs, kind="bf16")
@@ -342,7 +364,7 @@ def run_ours(args):
     wl = make_workload(args.layers, args.seqs, args.seq_len, dev, seed=1000 + rank)
     facs = wl["facs"]
     patcher = dkv.ExactPatcher(G.d_model, G.n_kv, G.hd, rank_k=G.rank, rank_v=G.rank,
-                               x_dtype=torch.float8_e4m3fn, rope=wl["rope"], norm_eps=G.eps)
+                               x_dtype=G.x_torch, rope=wl["rope"], norm_eps=G.eps)
     packed = torch.empty(args.layers, patcher.packed_bytes, dtype=torch.uint8, device=dev)
     kpages = [c[0] for c in wl["caches"]]
     vpages = [c[1] for c in wl["caches"]]
@@ -505,7 +527,7 @@ def run_e2e(args, patcher, dev, world):
             d[k].copy_(v, non_blocking=True)
         patcher.pack(d["a_k"], d["b_k"], d["a_v"], d["b_v"], sk, sv, norm_weight=d["norm_w"], out=packed)
         seqs = ops.SeqBatchTensors(cu_seqlens=cu, block_tables=d["tables"], max_seq_len=args.seq_len)
-        patcher.apply(d["x"].view(torch.float8_e4m3fn), packed, [c[0] for c in d["caches"]],
+        patcher.apply(d["x"].view(G.x_torch), packed, [c[0] for c in d["caches"]],
                       [c[1] for c in d["caches"]], seqs, x_scale=d["xs"], apply_norm=True)
         host["caches"].copy_(d["caches"], non_blocking=True)
 
@@ -1097,9 +1119,12 @@ def main():
             if getattr(args, k) is None:
                 setattr(args, k, v)
         return run_kivi_reference(args) if args.impl == "reference" else run_kivi_ours(args)
+    if args.workload == "smollm2-exact":
+        global Geo, METRIC, WORKLOAD, BYTES_PER_UNIT
+        Geo, METRIC, WORKLOAD, BYTES_PER_UNIT = SmolGeo, SMOL_METRIC, SMOL_WORKLOAD, SMOL_BYTES_PER_UNIT
     dense = args.workload == "rl-dense"
-    for k, v in (("layers", DenseGeo.layers if dense else 32), ("seqs", DenseGeo.seqs if dense else 64),
-                 ("seq_len", DenseGeo.seq_len if dense else 4096)):
+    for k, v in (("layers", DenseGeo.layers if dense else Geo.layers), ("seqs", DenseGeo.seqs if dense else Geo.seqs),
+                 ("seq_len", DenseGeo.seq_len if dense else Geo.seq_len)):
         if getattr(args, k) is None:
             setattr(args, k, v)
     if dense:

@@ -7,6 +7,8 @@ deployment swaps them in (see :func:`install`):
 * ``exact_kv_patch`` / ``zeroth_order_patches``    (deltakv.patches.exact)
 * ``apply_layer_patches``                          (deltakv.patches.compose)
 * ``subspace_correct`` / ``svd_basis``             (deltakv.patches.subspace)
+* ``apply_probe_to_cache`` / ``select_probes`` / ``weight_axis_scores`` / ``residual_gate``
+  (deltakv.patches.probe), ``lora_activation_scores`` (deltakv.patches.exact)
 
 plus the fused batched forms the engine and connector use: :class:`ExactPatcher` (LoRA
 deltas) and :class:`DensePatcher` (full-rank dW of an RL step, a tensor-core GEMM).
@@ -21,11 +23,20 @@ from deltakv_b200.dense import DensePatcher
 from deltakv_b200.exact import (
     ExactPatcher,
     apply_layer_patches,
+    apply_layer_patches_,
+    replay,
     exact_kv_patch,
     materialize_codes,
     zeroth_order_patches,
 )
 from deltakv_b200.ops import SeqBatchTensors, quantize_rows
+from deltakv_b200.probe import (
+    apply_probe_to_cache,
+    lora_activation_scores,
+    residual_gate,
+    select_probes,
+    weight_axis_scores,
+)
 from deltakv_b200.paged import gather_from_paged, scatter_into_paged, scatter_into_paged_batched
 from deltakv_b200.rope import RotaryEmbedding
 from deltakv_b200.subspace import subspace_correct, svd_basis
@@ -44,30 +55,41 @@ __all__ = [
     "RotaryEmbedding",
     "SeqBatchTensors",
     "apply_layer_patches",
+    "apply_layer_patches_",
+    "apply_probe_to_cache",
     "exact_kv_patch",
     "gather_from_paged",
     "install",
     "kivi",
+    "lora_activation_scores",
     "materialize_codes",
     "quantize_rows",
+    "replay",
+    "residual_gate",
     "scatter_into_paged",
     "scatter_into_paged_batched",
+    "select_probes",
     "subspace_correct",
     "svd_basis",
+    "weight_axis_scores",
     "zeroth_order_patches",
 ]
 
 # reference module -> {attribute: replacement}
 _INSTALL_MAP = {
     "deltakv.paged": {"scatter_into_paged": scatter_into_paged, "gather_from_paged": gather_from_paged},
-    "deltakv.patches.exact": {"exact_kv_patch": exact_kv_patch, "zeroth_order_patches": zeroth_order_patches},
+    "deltakv.patches.exact": {"exact_kv_patch": exact_kv_patch, "zeroth_order_patches": zeroth_order_patches,
+                              "lora_activation_scores": lora_activation_scores},
     "deltakv.patches.compose": {"apply_layer_patches": apply_layer_patches},
     # modules that imported the names with `from ... import`
     "deltakv.engine": {"zeroth_order_patches": zeroth_order_patches, "exact_kv_patch": exact_kv_patch,
-                       "apply_layer_patches": apply_layer_patches},
+                       "apply_layer_patches": apply_layer_patches, "apply_probe_to_cache": apply_probe_to_cache,
+                       "select_probes": select_probes, "weight_axis_scores": weight_axis_scores},
     "deltakv.connectors.vllm": {"scatter_into_paged": scatter_into_paged},
     "deltakv.patches.subspace": {"subspace_correct": subspace_correct, "svd_basis": svd_basis},
-    "deltakv.patches.probe": {"subspace_correct": subspace_correct},
+    "deltakv.patches.probe": {"subspace_correct": subspace_correct, "apply_probe_to_cache": apply_probe_to_cache,
+                              "select_probes": select_probes, "weight_axis_scores": weight_axis_scores,
+                              "residual_gate": residual_gate, "lora_activation_scores": lora_activation_scores},
     "deltakv.patches": {"exact_kv_patch": exact_kv_patch, "zeroth_order_patches": zeroth_order_patches,
                         "apply_layer_patches": apply_layer_patches, "subspace_correct": subspace_correct},
 }

@@ -49,6 +49,8 @@ EXPORTED = (
     "dkv_kivi_probe_residual",
     "dkv_kivi_subspace_workspace_bytes",
     "dkv_kivi_subspace_correct",
+    "dkv_lora_scores",
+    "dkv_row_diff_norms",
     "dkv_subspace_workspace_bytes",
     "dkv_subspace_correct",
     "dkv_subspace_correct_noalloc",
@@ -285,6 +287,10 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_kivi_subspace_workspace_bytes.argtypes = [C.POINTER(KiviSubspaceProblem), I32, C.POINTER(C.c_int64)]
     lib.dkv_kivi_subspace_correct.restype = C.c_int
     lib.dkv_kivi_subspace_correct.argtypes = [C.POINTER(KiviSubspaceProblem), I32, P, I64, P, P]
+    lib.dkv_lora_scores.restype = C.c_int
+    lib.dkv_lora_scores.argtypes = [P, I32, I64, I64, I64, P, I32, C.c_float, P, I32, P]
+    lib.dkv_row_diff_norms.restype = C.c_int
+    lib.dkv_row_diff_norms.argtypes = [P, P, I32, I64, I64, I64, I64, P, I64, P, P, P]
     lib.dkv_subspace_workspace_bytes.restype = C.c_int
     lib.dkv_subspace_workspace_bytes.argtypes = [I64, I64, I32, C.POINTER(C.c_int64)]
     lib.dkv_subspace_correct.restype = C.c_int

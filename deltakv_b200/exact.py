@@ -235,3 +235,39 @@ def apply_layer_patches(kv, patches: dict[int, LowRankKVPatch]) -> KVCache:
             _add_dense(out.k[idx], dk)
             _add_dense(out.v[idx], dv)
     return out
+
+
+def apply_layer_patches_(kv, patches: dict[int, LowRankKVPatch]):
+    """``apply_layer_patches`` without the clone: every layer's dK / dV is added to ``kv`` in
+    place (dense parts by the paged add, codes @ basis by the fused kernel's expand half, which
+    accumulates straight into the cache layer).  Returns ``kv``."""
+    n_kv, hd = kv.k.shape[2], kv.k.shape[3]
+    seq = kv.k.shape[1]
+    if seq == 0:
+        return kv
+    for idx, p in patches.items():
+        for dst, dense, codes, basis in ((kv.k[idx], p.k_dense, p.k_codes, p.k_basis),
+                                         (kv.v[idx], p.v_dense, p.v_codes, p.v_basis)):
+            if dense is not None:
+                _add_dense(dst, dense)
+            elif codes is not None and basis is not None:
+                r = codes.shape[1]
+                eye = torch.eye(r, dtype=torch.float32, device=dst.device)
+                scratch = torch.empty_like(dst)
+                _dense_delta([codes.float()], [(None, (eye, basis.float(), 1.0))], n_kv, hd, None, None,
+                             [scratch], [dst], accumulate_first=True)
+            else:
+                raise ValueError("patch is empty")
+    return kv
+
+
+def replay(base, chain, *, inplace: bool = False):
+    """The engine's STRICT-hit replay (engine.py:205-210) — base plus every stage of the patch
+    chain — with one copy of the base at most (none with ``inplace=True``) instead of a clone
+    per stage; each stage's patches are added in place."""
+    kv = base if inplace else (base.clone() if hasattr(base, "clone") else KVCache(base.k.clone(), base.v.clone(),
+                                                                                   base.version))
+    for applied in chain:
+        apply_layer_patches_(kv, applied.layer_patches)
+        kv.version = applied.target
+    return kv

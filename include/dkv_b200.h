@@ -335,6 +335,21 @@ int dkv_kivi_probe_residual(const dkv_kivi_cache *base, const void *fresh, int32
 
 /* ---- subspace route -------------------------------------------------------- */
 
+/* ---- probe scoring and the residual gate ------------------------------------------ */
+
+/* out[t] (+)= || scale * x[t] @ A^T ||  for A [rank, d] fp32 row-major (rank <= 64): the per-token
+   adapter activation of lora_activation_scores (patches/exact.py:111-115); summed over the
+   projections of a layer it is weight_axis_scores (patches/probe.py:30-47). */
+int dkv_lora_scores(const void *x, int32_t x_dtype, int64_t rows, int64_t d, int64_t x_row_stride,
+                    const float *a, int32_t rank, float scale, float *out, int32_t accumulate,
+                    dkv_stream_t stream);
+
+/* out[i] = || a[r_i] - b[r_i] || (fp32), r_i = rows[i] or i when rows is NULL: the per-token
+   residual estimates of residual_gate (patches/probe.py:85-109). */
+int dkv_row_diff_norms(const void *a, const void *b, int32_t dtype, int64_t n_rows, int64_t cols,
+                       int64_t a_row_stride, int64_t b_row_stride, const int32_t *rows, int64_t n_out,
+                       float *out, int32_t *status, dkv_stream_t stream);
+
 /*
  * Subspace correction of a KIVI int4 cache (the multi-adapter maintenance step): for each
  * problem (one layer's K or V of one adapter view), reused = dequant(base), then exactly

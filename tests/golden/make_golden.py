@@ -30,6 +30,10 @@ Cases:
                    the reference's exact route with LowRankFactors(A=dW, B=I, scale=1):
                    RMSNorm, exact_kv_patch, materialize, scatter_into_paged over a ragged
                    batch of bf16 activations into bf16 pages.
+  probe.npz        weight_axis_scores + select_probes on a LoRA delta, residual_gate, and
+                   apply_probe_to_cache over two layers (gated and ungated) with LoRA bases.
+  replay.npz       the engine's replay loop (engine.py:205-210): base KV plus a two-stage chain
+                   of apply_layer_patches (codes @ basis patches, then dense patches).
   errors.npz       patches.compose.measured_error of a patched vs a fresh KVCache (per layer).
   kivi.npz         metrics._minmax_quantize (4 bits, group 32) on the last dimension (the
                    per-token V grouping) and on the transposed tensor (per-channel K
@@ -375,6 +379,73 @@ def main(ref_src: str) -> None:
     est = measured_error(RefKV(k=pk, v=pv, version=WeightVersion(id="p")), RefKV(k=fk, v=fv, version=WeightVersion(id="f")))
     np.savez_compressed(OUT / "errors.npz", pk=pk.numpy(), pv=pv.numpy(), fk=fk.numpy(), fv=fv.numpy(),
                         per_layer=np.array(est.per_layer, np.float64), rel=np.float64(est.relative_kv_l2))
+
+    # ------------------------------------------------------------------ probe
+    from deltakv.patches.probe import apply_probe_to_cache, residual_gate, select_probes, weight_axis_scores
+    from deltakv.patches.tensors import KVCache as RefKVCache
+    from deltakv.patches.tensors import LowRankKVPatch as RefPatch
+
+    gp = torch.Generator().manual_seed(9)
+    n, dm, n_kv, hd, r = 96, 64, 2, 32, 4
+    d_kv = n_kv * hd
+    x_norm = torch.randn(n, dm, generator=gp)
+    fk = LowRankFactors(A=torch.randn(r, dm, generator=gp) / dm ** 0.5, B=torch.randn(d_kv, r, generator=gp),
+                        scale=0.5, name="k_proj")
+    fv = LowRankFactors(A=torch.randn(r, dm, generator=gp) / dm ** 0.5, B=torch.randn(d_kv, r, generator=gp),
+                        scale=0.25, name="v_proj")
+    pdelta = lora_delta(source=WeightVersion(id="base"), target=WeightVersion(id="lora", parent_id="base", kind="lora"),
+                        layers={0: lora_layer(0, k=fk, v=fv), 1: lora_layer(1, k=fk, v=fv)})
+    scores = weight_axis_scores(x_norm, pdelta, 0)
+    probes = select_probes(scores, 0.15, 4, 0.5)
+    base_k = torch.randn(2, n, n_kv, hd, generator=gp)
+    base_v = torch.randn(2, n, n_kv, hd, generator=gp)
+    fresh = {}
+    for l in range(2):
+        ck = torch.randn(n, r, generator=gp) * 0.2
+        cv = torch.randn(n, r, generator=gp) * 0.2
+        noise = torch.randn(n, n_kv, hd, generator=gp) * 0.02
+        outl = torch.zeros(n)
+        outl[torch.randperm(n, generator=gp)[:6]] = 1.0  # a few tokens with a large unexplained residual
+        fk_l = base_k[l] + (ck @ fk.B.T).view(n, n_kv, hd) + noise * (1 + 20 * outl.view(n, 1, 1))
+        fv_l = base_v[l] + (cv @ fv.B.T).view(n, n_kv, hd) + noise
+        fresh[l] = (fk_l, fv_l)
+    kvp = RefKVCache(k=base_k.clone(), v=base_v.clone(), version=WeightVersion(id="base"))
+    out_kv, ppatches, extra = apply_probe_to_cache(kvp, fresh, probes, 0.15, 0.40, layer_deltas=pdelta.layers,
+                                                   subspace_rank=4, probe_layers={0})
+    k_c0 = out_kv.k[0].clone()
+    gate = residual_gate(base_k[0], k_c0, fresh[0][0], probes, 0.15, 0.40)
+    np.savez_compressed(
+        OUT / "probe.npz", x_norm=x_norm.numpy(), a_k=fk.A.numpy(), b_k=fk.B.numpy(), s_k=np.float32(fk.scale),
+        a_v=fv.A.numpy(), b_v=fv.B.numpy(), s_v=np.float32(fv.scale), scores=scores.numpy(),
+        probes=probes.numpy(), base_k=base_k.numpy(), base_v=base_v.numpy(),
+        fresh_k=np.stack([fresh[l][0].numpy() for l in range(2)]), fresh_v=np.stack([fresh[l][1].numpy() for l in range(2)]),
+        out_k=out_kv.k.numpy(), out_v=out_kv.v.numpy(), extra=extra.numpy(), gate=gate.numpy(),
+        patch_k0=ppatches[0].k_dense.numpy(),
+    )
+
+    # ----------------------------------------------------------------- replay
+    gr = torch.Generator().manual_seed(10)
+    rb_k = torch.randn(3, 40, 2, 16, generator=gr)
+    rb_v = torch.randn(3, 40, 2, 16, generator=gr)
+    st1 = {0: RefPatch(layer_idx=0, k_codes=torch.randn(40, 3, generator=gr), k_basis=torch.randn(32, 3, generator=gr),
+                       v_codes=torch.randn(40, 5, generator=gr), v_basis=torch.randn(32, 5, generator=gr)),
+           2: RefPatch(layer_idx=2, k_codes=None, k_basis=None, v_codes=None, v_basis=None,
+                       k_dense=torch.randn(40, 2, 16, generator=gr) * 0.1, v_dense=torch.randn(40, 2, 16, generator=gr) * 0.1)}
+    st2 = {0: RefPatch(layer_idx=0, k_codes=None, k_basis=None, v_codes=None, v_basis=None,
+                       k_dense=torch.randn(40, 2, 16, generator=gr) * 0.1, v_dense=torch.randn(40, 2, 16, generator=gr) * 0.1),
+           1: RefPatch(layer_idx=1, k_codes=torch.randn(40, 2, generator=gr), k_basis=torch.randn(32, 2, generator=gr),
+                       v_codes=torch.randn(40, 2, generator=gr), v_basis=torch.randn(32, 2, generator=gr))}
+    rkv = RefKVCache(k=rb_k.clone(), v=rb_v.clone(), version=WeightVersion(id="base"))
+    for stage in (st1, st2):  # the loop of engine._replay
+        rkv = apply_layer_patches(rkv, stage)
+    rep = {"base_k": rb_k.numpy(), "base_v": rb_v.numpy(), "out_k": rkv.k.numpy(), "out_v": rkv.v.numpy()}
+    for si, stage in enumerate((st1, st2)):
+        for l, ptc in stage.items():
+            for nm in ("k_codes", "k_basis", "v_codes", "v_basis", "k_dense", "v_dense"):
+                t = getattr(ptc, nm)
+                if t is not None:
+                    rep[f"s{si}_l{l}_{nm}"] = t.numpy()
+    np.savez_compressed(OUT / "replay.npz", **rep)
 
     # ------------------------------------------------------------------- kivi
     from deltakv.metrics import _minmax_quantize, kivi_noise_floor

@@ -218,3 +218,37 @@ def test_measured_error_golden():
     rel, per = measured_error(g["pk"], g["pv"], g["fk"], g["fv"])
     assert np.allclose(per, g["per_layer"], rtol=1e-5, atol=1e-9)
     assert abs(rel - float(g["rel"])) <= 1e-5 * float(g["rel"])
+
+
+def _replay_chain(g):
+    chain = []
+    for si in range(2):
+        stage = {}
+        for key in list(g.keys()):
+            if key.startswith(f"s{si}_l"):
+                l = int(key.split("_")[1][1:])
+                nm = key.split("_", 2)[2]
+                stage.setdefault(l, {})[nm] = g[key]
+        chain.append(stage)
+    return chain
+
+
+def test_probe_and_replay_oracle_golden():
+    from oracle import probe as OP
+
+    g = golden("probe")
+    sc = OP.weight_axis_scores(g["x_norm"], [(g["a_k"], float(g["s_k"])), (g["a_v"], float(g["s_v"]))])
+    assert np.allclose(sc, g["scores"], rtol=1e-5, atol=1e-6)
+    assert np.array_equal(OP.select_probes(g["scores"], 0.15, 4, 0.5), g["probes"])
+    ko, vo, extra = OP.apply_probe_to_cache(
+        g["base_k"], g["base_v"], {l: (g["fresh_k"][l], g["fresh_v"][l]) for l in range(2)}, g["probes"], 0.15, 0.40,
+        v_bases={0: g["b_v"], 1: g["b_v"]}, k_ranks={0: g["b_k"].shape[1], 1: g["b_k"].shape[1]}, subspace_rank=4,
+        probe_layers={0})
+    assert np.array_equal(extra, g["extra"])
+    assert np.abs(ko - g["out_k"]).max() < 1e-4 and np.abs(vo - g["out_v"]).max() < 1e-4
+    gate = OP.residual_gate(g["base_k"][0], g["out_k"][0], g["fresh_k"][0], g["probes"], 0.15, 0.40)
+    assert np.array_equal(np.sort(gate), np.sort(g["gate"]))
+
+    r = golden("replay")
+    k, v = OP.replay(r["base_k"], r["base_v"], _replay_chain(r))
+    assert np.abs(k - r["out_k"]).max() < 1e-5 and np.abs(v - r["out_v"]).max() < 1e-5

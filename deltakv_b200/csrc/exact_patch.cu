@@ -1143,7 +1143,7 @@ struct TcSmem {
   static constexpr int CODES_OFF = P_OFF + kEpiWarps * RING;
   static constexpr int OM_OFF = CODES_OFF + 2 * 128 * C::CROW;
   static constexpr int BAR_OFF = OM_OFF + 2 * 2 * 128 * 4;
-  static constexpr int N_BARS = 2 * C::STAGES + 4 + 1;
+  static constexpr int N_BARS = 2 * C::STAGES + 4 + 1 + 4;
   static constexpr int MISC_OFF = BAR_OFF + N_BARS * 8;
   static constexpr int BYTES = MISC_OFF + 16;
 };
@@ -1168,6 +1168,89 @@ __device__ __forceinline__ void issue_stage_mmas(uint32_t d_codes, uint32_t d_di
   }
 }
 
+// TMEM -> shared-memory codes of one tile, one lane quarter and one projection per warp: warp
+// w reads rows 32 (w & 3) + lane, the K codes for w < 4 and the V codes for w >= 4; combines
+// the e4m3 terms, applies the dequantisation / RMSNorm / LoRA scales and stores f16 codes with
+// a per-row power-of-two exponent.  Returns false (abort raised) when the accumulator never
+// became ready.
+template <int XT, int R16, bool NORM>
+__device__ __forceinline__ bool tc_readout(const Params &p, const Tile &t, int b, int64_t use, uint8_t *codes,
+                                           float *om, uint32_t tmem, uint64_t *tfull, uint64_t *tempty,
+                                           volatile int *abort_flag, int warp, int lane) {
+  using C = TcCfg<XT, R16, NORM>;
+  constexpr int RPAD = C::RPAD;
+  const int qw = warp & 3, kv = warp >> 2;
+  const bool ok = mbar_wait_bounded(&tfull[b], static_cast<uint32_t>(use & 1), abort_flag);
+  if (!__all_sync(0xffffffffu, ok)) {
+    record_error(p.status, DKV_ERR_TIMEOUT);
+    *abort_flag = 1;
+    return false;
+  }
+  tc_fence_after();
+  const int row = 32 * qw + lane;
+  const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * qw) << 16) + b * C::BUF;
+  const int tok = t.c0 + row;
+  const int64_t grow = static_cast<int64_t>(t.row0) + row;
+  float xs = 1.f;
+  if (p.x_scale && tok < t.len && grow < p.x_rows) xs = __ldg(p.x_scale + t.layer * p.xs_stride + grow);
+  float rs = xs;
+  if (NORM) {
+    float d0[16], d1[16];
+    tmem_ld16(taddr + C::DIAG + 32 * qw, d0);
+    tmem_ld16(taddr + C::DIAG + 32 * qw + 16, d1);
+    tmem_ld_wait();
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      ss = (i == lane) ? d0[i] : ss;
+      ss = (16 + i == lane) ? d1[i] : ss;
+    }
+    rs = xs * rsqrtf(xs * xs * ss * p.inv_d + p.norm_eps);
+  }
+  const float *hdr = reinterpret_cast<const float *>(p.packed + t.layer * p.packed_stride);
+  {
+    float c[RPAD];
+#pragma unroll
+    for (int h = 0; h < R16; ++h) {
+      float v0[16], v1[16], v2[16];
+      const uint32_t col = taddr + kv * C::TERMS * RPAD + 16 * h;
+      tmem_ld16(col, v0);
+      if (C::TERMS == 3) {
+        tmem_ld16(col + RPAD, v1);
+        tmem_ld16(col + 2 * RPAD, v2);
+      }
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float x = v0[i];
+        if (C::TERMS == 3) x = fmaf(v2[i], 0.00390625f, fmaf(v1[i], 0.0625f, x));
+        c[16 * h + i] = x;
+      }
+    }
+    const float cm = hdr[kv] * rs;
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < RPAD; ++i) {
+      c[i] *= cm;
+      m = fmaxf(m, fabsf(c[i]));
+    }
+    int e = (m > 0.f && isfinite(m)) ? 14 - ilogbf(m) : 0;
+    e = max(-120, min(120, e));
+    const float e2 = exp2i(e);
+    uint32_t w[RPAD / 2];
+#pragma unroll
+    for (int i = 0; i < RPAD / 2; ++i) w[i] = pack_f16x2(c[2 * i] * e2, c[2 * i + 1] * e2);
+    uint4 *dst = reinterpret_cast<uint4 *>(codes + row * C::CROW + kv * RPAD * 2);
+#pragma unroll
+    for (int i = 0; i < RPAD / 8; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    om[kv * 128 + row] = hdr[2 + kv] * exp2i(-e);
+  }
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(&tempty[b]);
+  return true;
+}
+
 template <int XT, int R16, bool NORM, int PDT>
 __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_constant__ Params p) {
   using C = TcCfg<XT, R16, NORM>;
@@ -1182,6 +1265,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
   uint64_t *tfull = empty + STAGES;  // [2]
   uint64_t *tempty = tfull + 2;      // [2]
   uint64_t *done = tempty + 2;
+  uint64_t *cready = done + 1;   // [2] codes buffer written by all epilogue warps
+  uint64_t *cfree = cready + 2;  // [2] codes buffer read by all epilogue warps
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + S::MISC_OFF);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + S::MISC_OFF + 4);
 
@@ -1196,6 +1281,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
       mbar_init(&tempty[b], kEpiWarps);  // every epilogue warp reads its share of the codes
     }
     mbar_init(done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&cready[b], kEpiWarps);
+      mbar_init(&cfree[b], kEpiWarps);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -1269,109 +1358,48 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
     }
   } else if (warp < kEpiWarps) {
     // -------------------------------- epilogue --------------------------------
+    // The codes of tile j+1 are read out of TMEM (all 8 warps, one lane quarter and projection
+    // each) right after this warp has loaded its fragments of tile j, while tile j's first page
+    // copies are in flight; codes_ready / codes_free (8 arrivals each, one pair per codes buffer)
+    // replace a per-tile barrier of all epilogue warps.
     const int g = lane >> 2;
     uint8_t *codes_base = smem + S::CODES_OFF;
     float *om_base = reinterpret_cast<float *>(smem + S::OM_OFF);
     PageRing<PDT> ring;
     ring.base = smem_u32(smem + S::P_OFF) + warp * S::RING;
     ring.depth = DEPTH;
+    auto next_valid = [&](int64_t tile, Tile &t) -> int64_t {
+      for (; tile < p.n_tiles; tile += gridDim.x)
+        if (decode_tile(p, tile, t)) return tile;
+      return p.n_tiles;
+    };
+    auto wait_all = [&](uint64_t *bar, uint32_t parity) -> bool {
+      const bool ok = mbar_wait_bounded(bar, parity, abort_flag);
+      if (__all_sync(0xffffffffu, ok)) return true;
+      record_error(p.status, DKV_ERR_TIMEOUT);
+      *abort_flag = 1;
+      return false;
+    };
+    Tile tc;
+    int64_t tile = next_valid(blockIdx.x, tc);
+    bool ok = true;
+    if (tile < p.n_tiles) {
+      ok = tc_readout<XT, R16, NORM>(p, tc, 0, 0, codes_base, om_base, tmem, tfull, tempty, abort_flag, warp, lane);
+      if (ok) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&cready[0]);
+      }
+    }
     int64_t j = 0;
-    for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
-      Tile t;
-      if (!decode_tile(p, tile, t)) continue;
-      const int b = static_cast<int>(j % NBUF);
-      const int64_t use = j / NBUF;
+    while (ok && tile < p.n_tiles) {
       const int par = static_cast<int>(j & 1);
-      const RowInfo ri = make_row_info(p, t, warp, g);
-      const RowPtrs rp = row_ptrs<PDT>(p, t, ri);
+      const RowInfo ri = make_row_info(p, tc, warp, g);
+      const RowPtrs rp = row_ptrs<PDT>(p, tc, ri);
       ring.begin(p);
       for (int i = 0; i < DEPTH; ++i) ring.issue(p, rp, lane);  // page chunks of phase 2
-
-      uint8_t *codes = codes_base + par * 128 * C::CROW;
-      float *om = om_base + par * 2 * 128;
-      // after an abort the warps keep walking the tile sequence (same barriers) without work
-      // (decisions are made warp-uniform: TMEM loads and mma.sync need every lane)
-      bool have_codes = __all_sync(0xffffffffu, *abort_flag == 0);
-      // TMEM readout split over all 8 epilogue warps: warp w reads lane quarter w & 3 (rows
-      // 32 (w & 3) + lane), the K codes for w < 4 and the V codes for w >= 4
-      const int qw = warp & 3, kv_w = warp >> 2;
-      if (have_codes) {
-        // codes of row 32*qw + lane out of TMEM: combine terms, scale, f16 with a per-row exponent
-        const bool ok = mbar_wait_bounded(&tfull[b], static_cast<uint32_t>(use & 1), abort_flag);
-        have_codes = __all_sync(0xffffffffu, ok);
-        if (!have_codes) {
-          record_error(p.status, DKV_ERR_TIMEOUT);
-          *abort_flag = 1;
-        }
-      }
-      if (have_codes) {
-        tc_fence_after();
-        const int row = 32 * qw + lane;
-        const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * qw) << 16) + b * C::BUF;
-        const int tok = t.c0 + row;
-        const int64_t grow = static_cast<int64_t>(t.row0) + row;
-        float xs = 1.f;
-        if (p.x_scale && tok < t.len && grow < p.x_rows) xs = __ldg(p.x_scale + t.layer * p.xs_stride + grow);
-        float rs = xs;
-        if (NORM) {
-          float d0[16], d1[16];
-          tmem_ld16(taddr + C::DIAG + 32 * qw, d0);
-          tmem_ld16(taddr + C::DIAG + 32 * qw + 16, d1);
-          tmem_ld_wait();
-          float ss = 0.f;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            ss = (i == lane) ? d0[i] : ss;
-            ss = (16 + i == lane) ? d1[i] : ss;
-          }
-          rs = xs * rsqrtf(xs * xs * ss * p.inv_d + p.norm_eps);
-        }
-        const float *hdr = reinterpret_cast<const float *>(p.packed + t.layer * p.packed_stride);
-        {
-          const int kv = kv_w;
-          float c[RPAD];
-#pragma unroll
-          for (int h = 0; h < R16; ++h) {
-            float v0[16], v1[16], v2[16];
-            const uint32_t col = taddr + kv * C::TERMS * RPAD + 16 * h;
-            tmem_ld16(col, v0);
-            if (C::TERMS == 3) {
-              tmem_ld16(col + RPAD, v1);
-              tmem_ld16(col + 2 * RPAD, v2);
-            }
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              float x = v0[i];
-              if (C::TERMS == 3) x = fmaf(v2[i], 0.00390625f, fmaf(v1[i], 0.0625f, x));
-              c[16 * h + i] = x;
-            }
-          }
-          const float cm = hdr[kv] * rs;
-          float m = 0.f;
-#pragma unroll
-          for (int i = 0; i < RPAD; ++i) {
-            c[i] *= cm;
-            m = fmaxf(m, fabsf(c[i]));
-          }
-          int e = (m > 0.f && isfinite(m)) ? 14 - ilogbf(m) : 0;
-          e = max(-120, min(120, e));
-          const float e2 = exp2i(e);
-          uint32_t w[RPAD / 2];
-#pragma unroll
-          for (int i = 0; i < RPAD / 2; ++i) w[i] = pack_f16x2(c[2 * i] * e2, c[2 * i + 1] * e2);
-          uint4 *dst = reinterpret_cast<uint4 *>(codes + row * C::CROW + kv * RPAD * 2);
-#pragma unroll
-          for (int i = 0; i < RPAD / 8; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-          om[kv * 128 + row] = hdr[2 + kv] * exp2i(-e);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[b]);
-      }
-      // every epilogue warp reaches this barrier, also after a timeout, then all leave together
-      named_barrier_sync(1, kEpiWarps * 32);
-      if (__any_sync(0xffffffffu, *abort_flag != 0)) continue;
+      if (!wait_all(&cready[par], static_cast<uint32_t>((j >> 1) & 1))) break;
+      const uint8_t *codes = codes_base + par * 128 * C::CROW;
+      const float *om = om_base + par * 2 * 128;
       // A fragments of this warp's 16 rows, K and V codes
       uint32_t ck[R16][4], cv[R16][4];
       {
@@ -1385,7 +1413,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
       }
       const float om_k[2] = {om[16 * warp + g], om[16 * warp + g + 8]};
       const float om_v[2] = {om[128 + 16 * warp + g], om[128 + 16 * warp + g + 8]};
-      phase2<R16, PDT, DEPTH>(p, t, ri, rp, ring, ck, cv, om_k, om_v, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&cfree[par]);
+      // readout of the next tile into the other codes buffer, once every warp has read tile j-1
+      Tile tn;
+      const int64_t ntile = next_valid(tile + gridDim.x, tn);
+      if (ntile < p.n_tiles) {
+        const int np1 = static_cast<int>((j + 1) & 1);
+        if (j >= 1 && !wait_all(&cfree[np1], static_cast<uint32_t>(((j - 1) >> 1) & 1))) break;
+        if (!tc_readout<XT, R16, NORM>(p, tn, static_cast<int>((j + 1) % NBUF), (j + 1) / NBUF,
+                                       codes_base + np1 * 128 * C::CROW, om_base + np1 * 2 * 128, tmem, tfull,
+                                       tempty, abort_flag, warp, lane))
+          break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&cready[np1]);
+      }
+      phase2<R16, PDT, DEPTH>(p, tc, ri, rp, ring, ck, cv, om_k, om_v, lane);
+      tile = ntile;
+      tc = tn;
       ++j;
     }
     cp_async_wait<0>();

@@ -51,6 +51,7 @@ EXPORTED = (
     "dkv_kivi_subspace_correct",
     "dkv_lora_scores",
     "dkv_row_diff_norms",
+    "dkv_sym_eig_batched",
     "dkv_subspace_workspace_bytes",
     "dkv_subspace_correct",
     "dkv_subspace_correct_noalloc",
@@ -291,6 +292,8 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_lora_scores.argtypes = [P, I32, I64, I64, I64, P, I32, C.c_float, P, I32, P]
     lib.dkv_row_diff_norms.restype = C.c_int
     lib.dkv_row_diff_norms.argtypes = [P, P, I32, I64, I64, I64, I64, P, I64, P, P, P]
+    lib.dkv_sym_eig_batched.restype = C.c_int
+    lib.dkv_sym_eig_batched.argtypes = [P, I64, I32, I64, I32, P, P, P, P]
     lib.dkv_subspace_workspace_bytes.restype = C.c_int
     lib.dkv_subspace_workspace_bytes.argtypes = [I64, I64, I32, C.POINTER(C.c_int64)]
     lib.dkv_subspace_correct.restype = C.c_int

@@ -55,19 +55,51 @@ def svd_basis(residual: Tensor, rank: int) -> Tensor:
     return vh[:r].T.to(residual.dtype).contiguous()
 
 
-def _orthonormalize(z: Tensor) -> Tensor:
-    """Orthonormal basis of the columns of ``z [b, d, k]``: Cholesky QR applied twice in
-    fp64 (CholQR2: Fukaya, Nakatsukasa et al., 2014), with Householder QR for any batch
-    whose Gram matrix is not numerically positive definite."""
+def _orthonormalize(z: Tensor) -> tuple[Tensor, Tensor]:
+    """Orthonormal basis of the columns of ``z [b, d, k]``: Cholesky QR applied twice in fp64
+    (CholQR2: Fukaya, Nakatsukasa et al., 2014).  Returns the basis and a device flag per batch
+    element whose Gram matrix was not numerically positive definite (its basis is then
+    meaningless and the caller recomputes it) — no host synchronisation."""
     q = z.double()
+    bad = torch.zeros(q.shape[0], dtype=torch.bool, device=q.device)
     for _ in range(2):
         g = torch.matmul(q.transpose(1, 2), q)
         l, info = torch.linalg.cholesky_ex(g)
-        if bool((info != 0).any()):
-            q, _ = torch.linalg.qr(q)
-            continue
+        bad |= info != 0
         q = torch.linalg.solve_triangular(l, q.transpose(1, 2), upper=False).transpose(1, 2)
-    return q.float()
+    return q.float(), bad
+
+
+def sym_eig(t: Tensor, *, max_sweeps: int = 30) -> tuple[Tensor, Tensor, Tensor]:
+    """Eigendecomposition of the symmetric ``t [b, k, k]`` (k <= 96) on the device, fp64:
+    ``(evals [b, k] descending, evecs [b, k, k] with column j for evals[:, j], info [b])``,
+    info 0 converged, 1 not converged in ``max_sweeps`` Jacobi sweeps, 2 non-finite input."""
+    ops._require_cuda(t)
+    a = t.to(torch.float64).contiguous()
+    b, k = int(a.shape[0]), int(a.shape[-1])
+    ev = torch.empty(b, k, dtype=torch.float64, device=a.device)
+    vec = torch.empty(b, k, k, dtype=torch.float64, device=a.device)
+    info = torch.empty(b, dtype=torch.int32, device=a.device)
+    rc = L.lib().dkv_sym_eig_batched(a.data_ptr(), b, k, k * k, int(max_sweeps), ev.data_ptr(), vec.data_ptr(),
+                                     info.data_ptr(), ops.stream_ptr())
+    L.check(rc, "dkv_sym_eig_batched")
+    return ev, vec, info
+
+
+MAX_RITZ = 96  # largest rank + oversample the device eigensolver takes
+_start_cache: dict[tuple, tuple[Tensor, Tensor]] = {}
+
+
+def _start_block(n_b: int, d: int, k: int, device: torch.device) -> tuple[Tensor, Tensor]:
+    key = (str(device), n_b, d, k)
+    hit = _start_cache.get(key)
+    if hit is None:
+        if len(_start_cache) >= 8:
+            _start_cache.clear()
+        gen = torch.Generator(device=device).manual_seed(1234)
+        hit = _orthonormalize(torch.randn(n_b, d, k, generator=gen, device=device))
+        _start_cache[key] = hit
+    return hit
 
 
 def topr_basis(residual: Tensor, rank: int, *, iters: int = 3, oversample: int = 8) -> Tensor:
@@ -75,20 +107,20 @@ def topr_basis(residual: Tensor, rank: int, *, iters: int = 3, oversample: int =
     batched over a leading dimension.
 
     The same subspace as :func:`svd_basis` (the reference's ``svd_basis``,
-    src/deltakv/patches/subspace.py:37-42), computed by block subspace iteration on the Gram
-    matrix ``C = R^T R`` with re-orthonormalisation and a final Rayleigh-Ritz step
-    (Golub & Van Loan, Matrix Computations, 4th ed., Sec. 8.2.4; Halko, Martinsson & Tropp,
-    SIAM Review 2011, Alg. 4.4): ``iters`` products ``C Q`` on ``rank + oversample`` columns
-    instead of a full SVD; the small Rayleigh-Ritz eigenproblem runs in LAPACK on the host.
-    The subspace converges as ``(l_{k+1} / l_rank)^iters`` (eigenvalues of C, k = rank +
-    oversample); the least-squares correction depends on the basis only through its column
-    space, so the rotation within the subspace is immaterial.  Batch elements whose Ritz
-    values show a poor gap — estimated subspace error ``(l_k / l_rank)^iters`` above
-    ``1e-5`` — are recomputed with the exact SVD, so the result never depends on a
-    half-converged iteration.
+    src/deltakv/patches/subspace.py:37-42), computed by block subspace iteration on
+    ``C = R^T R`` — applied as ``R^T (R Q)``, never formed — with re-orthonormalisation and a
+    final Rayleigh-Ritz step (Golub & Van Loan, Matrix Computations, 4th ed., Sec. 8.2.4;
+    Halko, Martinsson & Tropp, SIAM Review 2011, Alg. 4.4): ``iters`` products on
+    ``k = rank + oversample`` columns instead of a full SVD; the k x k Rayleigh-Ritz
+    eigenproblem runs on the device (:func:`sym_eig`).  The subspace converges as
+    ``(l_k / l_rank)^iters`` (eigenvalues of C); the least-squares correction depends on the
+    basis only through its column space, so the rotation within the subspace is immaterial.
+    Batch elements whose Ritz values show a poor gap — estimated subspace error above
+    ``1e-5`` — or whose orthonormalisation or eigensolve failed are recomputed with the exact
+    SVD, so the result never depends on a half-converged iteration.  One host synchronisation
+    (the per-element fallback flags).
     """
-    import numpy as np
-
+    ops._require_cuda(residual)
     x = residual.float()
     batched = x.ndim == 3
     if not batched:
@@ -96,20 +128,25 @@ def topr_basis(residual: Tensor, rank: int, *, iters: int = 3, oversample: int =
     n_b, m, d = x.shape
     r = max(1, min(int(rank), m, d))
     k = min(d, r + oversample)
-    c = torch.matmul(x.transpose(1, 2), x)  # [b, d, d]
-    gen = torch.Generator(device=x.device).manual_seed(1234)
-    q = _orthonormalize(torch.randn(n_b, d, k, generator=gen, device=x.device))
+    if k >= m or k > MAX_RITZ:
+        basis = torch.stack([svd_basis(x[i], r) for i in range(n_b)])
+        return basis if batched else basis[0]
+    q, bad = _start_block(n_b, d, k, x.device)
+    xt = x.transpose(1, 2)
     for _ in range(iters):
-        q = _orthonormalize(torch.matmul(c, q))
-    t = torch.matmul(q.transpose(1, 2), torch.matmul(c, q)).double().cpu().numpy()
-    ev, v = np.linalg.eigh(0.5 * (t + t.transpose(0, 2, 1)))  # ascending eigenvalues
-    v_top = torch.from_numpy(np.ascontiguousarray(v[:, :, ::-1][:, :, :r])).to(device=x.device, dtype=torch.float32)
-    basis = torch.matmul(q, v_top).contiguous()
+        q, b2 = _orthonormalize(torch.matmul(xt, torch.matmul(x, q)))
+        bad = bad | b2
+    w = torch.matmul(x, q)
+    t = torch.matmul(w.transpose(1, 2), w)
+    ev, vec, info = sym_eig(t)
+    basis = torch.matmul(q, vec[:, :, :r].float())
+    redo = bad | (info != 0)
     if k < d:
-        lam_r = np.maximum(ev[:, k - r], 1e-300)
-        est = (np.maximum(ev[:, 0], 0.0) / lam_r) ** iters
-        for i in np.nonzero(est > 1e-5)[0].tolist():
-            basis[i] = svd_basis(x[i], r)
+        lam_r = ev[:, r - 1].clamp_min(1e-300)
+        est = (ev[:, k - 1].clamp_min(0.0) / lam_r) ** iters
+        redo = redo | ~torch.isfinite(est) | (est > 1e-5)
+    for i in torch.nonzero(redo).view(-1).tolist():  # the one host synchronisation
+        basis[i] = svd_basis(x[i], r)
     return basis if batched else basis[0]
 
 

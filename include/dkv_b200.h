@@ -350,6 +350,15 @@ int dkv_row_diff_norms(const void *a, const void *b, int32_t dtype, int64_t n_ro
                        int64_t a_row_stride, int64_t b_row_stride, const int32_t *rows, int64_t n_out,
                        float *out, int32_t *status, dkv_stream_t stream);
 
+/* Eigendecomposition of `batch` symmetric k x k fp64 matrices (k <= 96; matrix b at
+   a + b * a_stride, row-major, only its symmetric part is used) by parallel cyclic Jacobi:
+   evals [batch, k] descending, evecs [batch, k, k] row-major with column j the unit
+   eigenvector of evals[b, j], info[b] = 0 converged, 1 not converged within max_sweeps,
+   2 non-finite input.  The Rayleigh-Ritz step of the K basis that stands in for svd_basis
+   (patches/subspace.py:37-42) on the device. */
+int dkv_sym_eig_batched(const double *a, int64_t batch, int32_t k, int64_t a_stride, int32_t max_sweeps,
+                        double *evals, double *evecs, int32_t *info, dkv_stream_t stream);
+
 /*
  * Subspace correction of a KIVI int4 cache (the multi-adapter maintenance step): for each
  * problem (one layer's K or V of one adapter view), reused = dequant(base), then exactly

@@ -7,16 +7,17 @@
 // J. Sci. Stat. Comput. 1985; Golub & Van Loan, Matrix Computations 4th ed., Sec. 8.5.3 and
 // Alg. 8.5.1 for the 2x2 symmetric Schur rotation).  One CTA per matrix keeps A and the
 // accumulated rotations V in shared memory; each round rotates n/2 disjoint index pairs at
-// once (rows, then columns), n-1 rounds per sweep, and sweeps stop when the off-diagonal
-// Frobenius norm falls below 1e-13 of the matrix norm or after max_sweeps.  Odd n is padded
-// with a decoupled zero row/column that never rotates.
+// once — both sides of every 2x2 block in one pass, two barriers per round — n-1 rounds per
+// sweep, and sweeps stop when the off-diagonal Frobenius norm falls below 1e-13 of the matrix
+// norm or after max_sweeps.  Odd n is padded with a decoupled zero row/column that never
+// rotates.
 #include "dkv_common.cuh"
 
 namespace dkv {
 namespace eig {
 
 constexpr int kMaxN = 96;
-constexpr int kThreads = 256;
+constexpr int kThreads = 512;
 
 __device__ __forceinline__ double block_sum(double v, double *red) {
 #pragma unroll
@@ -37,20 +38,41 @@ __device__ __forceinline__ int player(int pos, int round, int n) {
   return pos == 0 ? 0 : ((pos - 1 + round) % (n - 1)) + 1;
 }
 
+// Jacobi rotation (c, s) that annihilates apq (Alg. 8.5.1): t = tan(theta) is formed in fp32
+// (relative error ~1e-7 leaves a'_pq ~ 1e-7 a_pq, which the next sweep removes), then
+// c = 1/sqrt(1 + t^2) to full fp64 accuracy by two Newton steps from the fp32 estimate, so the
+// rotation is orthogonal to fp64 rounding whatever the error in t.
+__device__ __forceinline__ void rotation(double app, double aqq, double apq, double &c, double &s) {
+  c = 1.0;
+  s = 0.0;
+  const float apq_f = static_cast<float>(apq);
+  if (fabsf(apq_f) < 1e-30f) return;  // below the matrix norm by far more than the tolerance
+  const float tau = static_cast<float>(aqq - app) / (2.0f * apq_f);
+  const float at = fabsf(tau);
+  const float tf = (at > 1e18f ? 0.5f / at : 1.0f / (at + sqrtf(fmaf(at, at, 1.0f))));
+  const double t = static_cast<double>(tau >= 0.0f ? tf : -tf);
+  const double x = fma(t, t, 1.0);
+  double y = static_cast<double>(rsqrtf(static_cast<float>(x)));
+  y = y * fma(-0.5 * x * y, y, 1.5);
+  y = y * fma(-0.5 * x * y, y, 1.5);
+  c = y;
+  s = t * y;
+}
+
 __global__ void __launch_bounds__(kThreads) jacobi_kernel(const double *a_in, int64_t a_stride, int k, int n,
                                                           int max_sweeps, double *evals, double *evecs,
                                                           int32_t *info) {
   extern __shared__ double sm[];
   const int ld = n + 1;
+  const int half = n / 2;
   double *A = sm;                    // [n][ld]
   double *V = A + n * ld;            // [n][ld]
-  double *cs = V + n * ld;           // [n/2] c, [n/2] s
+  double *cs = V + n * ld;           // [half] c, [half] s
   double *red = cs + n;              // [kThreads/32]
-  int *pq = reinterpret_cast<int *>(red + kThreads / 32);  // [n/2] p, [n/2] q
+  int *pq = reinterpret_cast<int *>(red + kThreads / 32);  // [half] p, [half] q
   const int tid = threadIdx.x;
   const int64_t bi = blockIdx.x;
   const double *src = a_in + bi * a_stride;
-  const int half = n / 2;
 
   double frob = 0.0;
   bool finite = true;
@@ -67,8 +89,13 @@ __global__ void __launch_bounds__(kThreads) jacobi_kernel(const double *a_in, in
     frob = fma(v, v, frob);
   }
   frob = block_sum(frob, red);
-  const int all_finite = __syncthreads_and(finite ? 1 : 0);
-  const double tol2 = 1e-26 * frob;  // (1e-13 ||A||_F)^2
+  const int all_finite = __syncthreads_and(finite ? 1 : 0) && isfinite(frob);
+  if (!isfinite(frob)) frob = 0.0;
+  // work on A / ||A||_F so that every entry that matters is far inside the fp32 range
+  const double norm = sqrt(frob);
+  const double inv = frob > 0.0 ? 1.0 / norm : 0.0;
+  for (int e = tid; e < n * n; e += kThreads) A[(e / n) * ld + e % n] *= inv;
+  __syncthreads();
 
   int converged = frob == 0.0 ? 1 : 0;
   for (int sweep = 0; sweep < max_sweeps && !converged; ++sweep) {
@@ -80,43 +107,39 @@ __global__ void __launch_bounds__(kThreads) jacobi_kernel(const double *a_in, in
           p = q;
           q = t;
         }
-        const double apq = A[p * ld + q];
-        double c = 1.0, s = 0.0;
-        if (apq != 0.0) {
-          const double tau = (A[q * ld + q] - A[p * ld + p]) / (2.0 * apq);
-          const double t = tau >= 0.0 ? 1.0 / (tau + sqrt(1.0 + tau * tau)) : -1.0 / (-tau + sqrt(1.0 + tau * tau));
-          c = 1.0 / sqrt(1.0 + t * t);
-          s = t * c;
-        }
+        double c, s;
+        rotation(A[p * ld + p], A[q * ld + q], A[p * ld + q], c, s);
         cs[tid] = c;
         cs[half + tid] = s;
         pq[tid] = p;
         pq[half + tid] = q;
       }
       __syncthreads();
-      // rows: A <- J^T A
-      for (int e = tid; e < half * n; e += kThreads) {
-        const int t = e / n, j = e % n;
-        const double c = cs[t], s = cs[half + t];
-        if (s == 0.0) continue;
-        const int p = pq[t], q = pq[half + t];
-        const double ap = A[p * ld + j], aq = A[q * ld + j];
-        A[p * ld + j] = c * ap - s * aq;
-        A[q * ld + j] = s * ap + c * aq;
-      }
-      __syncthreads();
-      // columns: A <- A J, V <- V J
-      for (int e = tid; e < 2 * half * n; e += kThreads) {
-        const int m = e >= half * n;
-        const int f = e - m * half * n;
-        const int t = f / n, i = f % n;
-        const double c = cs[t], s = cs[half + t];
-        if (s == 0.0) continue;
-        const int p = pq[t], q = pq[half + t];
-        double *M = m ? V : A;
-        const double ap = M[i * ld + p], aq = M[i * ld + q];
-        M[i * ld + p] = c * ap - s * aq;
-        M[i * ld + q] = s * ap + c * aq;
+      // A <- J^T A J one 2x2 block at a time: block (t, u) spans rows {p_t, q_t} and columns
+      // {p_u, q_u} and depends only on rotations t and u; V <- V J alongside.
+      for (int e = tid; e < half * half + n * half; e += kThreads) {
+        if (e < half * half) {
+          const int t = e / half, u = e % half;
+          const double ct = cs[t], st = cs[half + t], cu = cs[u], su = cs[half + u];
+          if (st == 0.0 && su == 0.0) continue;
+          const int pt = pq[t], qt = pq[half + t], pu = pq[u], qu = pq[half + u];
+          const double a = A[pt * ld + pu], b = A[pt * ld + qu], c = A[qt * ld + pu], d = A[qt * ld + qu];
+          const double r0 = ct * a - st * c, r1 = ct * b - st * d;
+          const double r2 = st * a + ct * c, r3 = st * b + ct * d;
+          A[pt * ld + pu] = cu * r0 - su * r1;
+          A[pt * ld + qu] = su * r0 + cu * r1;
+          A[qt * ld + pu] = cu * r2 - su * r3;
+          A[qt * ld + qu] = su * r2 + cu * r3;
+        } else {
+          const int f = e - half * half;
+          const int t = f / n, i = f % n;
+          const double c = cs[t], s = cs[half + t];
+          if (s == 0.0) continue;
+          const int p = pq[t], q = pq[half + t];
+          const double vp = V[i * ld + p], vq = V[i * ld + q];
+          V[i * ld + p] = c * vp - s * vq;
+          V[i * ld + q] = s * vp + c * vq;
+        }
       }
       __syncthreads();
     }
@@ -126,7 +149,7 @@ __global__ void __launch_bounds__(kThreads) jacobi_kernel(const double *a_in, in
       if (i != j) off = fma(A[i * ld + j], A[i * ld + j], off);
     }
     off = block_sum(off, red);
-    converged = off <= tol2 ? 1 : 0;
+    converged = off <= 1e-26 ? 1 : 0;  // ||offdiag|| <= 1e-13 ||A||_F
   }
 
   // descending order over the k real indices (padding excluded); NaN ranks last, ties by index
@@ -141,7 +164,7 @@ __global__ void __launch_bounds__(kThreads) jacobi_kernel(const double *a_in, in
       const double key_j = isnan(dj) ? -INFINITY : dj;
       rank += (key_j > key_i) || (key_j == key_i && j < i);
     }
-    ev_out[rank] = di;
+    ev_out[rank] = di * norm;
     for (int r = 0; r < k; ++r) vec_out[static_cast<int64_t>(r) * k + rank] = V[r * ld + i];
   }
   if (tid == 0) info[bi] = all_finite ? (converged ? 0 : 1) : 2;

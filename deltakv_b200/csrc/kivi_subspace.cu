@@ -595,24 +595,56 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
         for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
       }
     }
-    // requantise
+    // requantise.  Group extrema are reduce-scattered over the lanes that share a group, so
+    // each lane derives one group's scale / zero / reciprocal and broadcasts it back.
     if (!kmode) {
+      // V: group = (row g + 8i, 32 channels) spread over the 4 lanes q; lane q owns row i = q
+      float lo[4], hi[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        float lo = v[i][0], hi = v[i][0];
+        lo[i] = hi[i] = v[i][0];
 #pragma unroll
         for (int j = 1; j < 8; ++j) {
-          lo = fminf(lo, v[i][j]);
-          hi = fmaxf(hi, v[i][j]);
+          lo[i] = fminf(lo[i], v[i][j]);
+          hi[i] = fmaxf(hi[i], v[i][j]);
         }
-        lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, 1));
-        hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, 1));
-        lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, 2));
-        hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, 2));
-        __half s16, z16;
-        kivi::group_params(lo, hi, s16, z16);
-        const float s = __half2float(s16), z = __half2float(z16);
-        const float inv = s > 0.f ? __frcp_rn(s) : 0.f;
+      }
+      {
+        const bool up = (q & 2) != 0;
+#pragma unroll
+        for (int ii = 0; ii < 2; ++ii) {
+          const float rl = __shfl_xor_sync(0xffffffffu, up ? lo[ii] : lo[ii + 2], 2);
+          const float rh = __shfl_xor_sync(0xffffffffu, up ? hi[ii] : hi[ii + 2], 2);
+          lo[ii] = fminf(up ? lo[ii + 2] : lo[ii], rl);
+          hi[ii] = fmaxf(up ? hi[ii + 2] : hi[ii], rh);
+        }
+      }
+      {
+        const bool up = (q & 1) != 0;
+        const float rl = __shfl_xor_sync(0xffffffffu, up ? lo[0] : lo[1], 1);
+        const float rh = __shfl_xor_sync(0xffffffffu, up ? hi[0] : hi[1], 1);
+        lo[0] = fminf(up ? lo[1] : lo[0], rl);
+        hi[0] = fmaxf(up ? hi[1] : hi[0], rh);
+      }
+      __half s16, z16;
+      kivi::group_params(lo[0], hi[0], s16, z16);
+      const float s_own = __half2float(s16);
+      const float inv_own = s_own > 0.f ? __frcp_rn(s_own) : 0.f;
+      const uint32_t sz_own = static_cast<uint32_t>(__half_as_ushort(s16)) |
+                              (static_cast<uint32_t>(__half_as_ushort(z16)) << 16);
+      {
+        const int64_t orow = t0 + g + 8 * q;
+        if (orow < n) {
+          P.o_scale[orow * P.o_szrs + cb] = s16;
+          P.o_zero[orow * P.o_szrs + cb] = z16;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t sz = __shfl_sync(0xffffffffu, sz_own, 4 * g + i);
+        const float inv = __shfl_sync(0xffffffffu, inv_own, 4 * g + i);
+        const float s = __half2float(__ushort_as_half(static_cast<unsigned short>(sz & 0xffffu)));
+        const float z = __half2float(__ushort_as_half(static_cast<unsigned short>(sz >> 16)));
         const uint64_t z2 = f2pack(z, z), inv2 = f2pack(inv, inv);
         uint32_t wq = 0u;
 #pragma unroll
@@ -624,35 +656,65 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
           wq |= kivi::quant_from_y(y0, a0, s) << (8 * p);
           wq |= kivi::quant_from_y(y1, a1, s) << (8 * p + 4);
         }
-        if (rv[i]) {
-          *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = wq;
-          if (q == 0) {
-            P.o_scale[row[i] * P.o_szrs + cb] = s16;
-            P.o_zero[row[i] * P.o_szrs + cb] = z16;
-          }
-        }
+        if (rv[i]) *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = wq;
       }
     } else {
-      uint32_t wq[4] = {0u, 0u, 0u, 0u};
-      uint32_t sh[4], zh[4];  // packed fp16 scale / zero of the lane's 8 channels
+      // K: group = (32 rows of the warp tile, channel 8q + j) spread over the 8 lanes g;
+      // lane g owns channel j = g
+      float lo[8], hi[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float lo = INFINITY, hi = -INFINITY;
+        lo[j] = INFINITY;
+        hi[j] = -INFINITY;
 #pragma unroll
         for (int i = 0; i < 4; ++i)
           if (rv[i]) {
-            lo = fminf(lo, v[i][j]);
-            hi = fmaxf(hi, v[i][j]);
+            lo[j] = fminf(lo[j], v[i][j]);
+            hi[j] = fmaxf(hi[j], v[i][j]);
           }
+      }
+      {
+        const bool up = (g & 4) != 0;
 #pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-          lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-          hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+        for (int jj = 0; jj < 4; ++jj) {
+          const float rl = __shfl_xor_sync(0xffffffffu, up ? lo[jj] : lo[jj + 4], 16);
+          const float rh = __shfl_xor_sync(0xffffffffu, up ? hi[jj] : hi[jj + 4], 16);
+          lo[jj] = fminf(up ? lo[jj + 4] : lo[jj], rl);
+          hi[jj] = fmaxf(up ? hi[jj + 4] : hi[jj], rh);
         }
-        __half s16, z16;
-        kivi::group_params(lo, hi, s16, z16);
-        const float s = __half2float(s16), z = __half2float(z16);
-        const float inv = s > 0.f ? __frcp_rn(s) : 0.f;
+      }
+      {
+        const bool up = (g & 2) != 0;
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const float rl = __shfl_xor_sync(0xffffffffu, up ? lo[jj] : lo[jj + 2], 8);
+          const float rh = __shfl_xor_sync(0xffffffffu, up ? hi[jj] : hi[jj + 2], 8);
+          lo[jj] = fminf(up ? lo[jj + 2] : lo[jj], rl);
+          hi[jj] = fmaxf(up ? hi[jj + 2] : hi[jj], rh);
+        }
+      }
+      {
+        const bool up = (g & 1) != 0;
+        const float rl = __shfl_xor_sync(0xffffffffu, up ? lo[0] : lo[1], 4);
+        const float rh = __shfl_xor_sync(0xffffffffu, up ? hi[0] : hi[1], 4);
+        lo[0] = fminf(up ? lo[1] : lo[0], rl);
+        hi[0] = fmaxf(up ? hi[1] : hi[0], rh);
+      }
+      __half s16, z16;
+      kivi::group_params(lo[0], hi[0], s16, z16);
+      const float s_own = __half2float(s16);
+      const float inv_own = s_own > 0.f ? __frcp_rn(s_own) : 0.f;
+      const uint32_t sz_own = static_cast<uint32_t>(__half_as_ushort(s16)) |
+                              (static_cast<uint32_t>(__half_as_ushort(z16)) << 16);
+      P.o_scale[krow * P.o_szrs + c + g] = s16;
+      P.o_zero[krow * P.o_szrs + c + g] = z16;
+      uint32_t wq[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t sz = __shfl_sync(0xffffffffu, sz_own, 4 * j + q);
+        const float inv = __shfl_sync(0xffffffffu, inv_own, 4 * j + q);
+        const float s = __half2float(__ushort_as_half(static_cast<unsigned short>(sz & 0xffffu)));
+        const float z = __half2float(__ushort_as_half(static_cast<unsigned short>(sz >> 16)));
         const uint64_t z2 = f2pack(z, z), inv2 = f2pack(inv, inv);
 #pragma unroll
         for (int i = 0; i < 4; i += 2) {
@@ -663,22 +725,10 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
           wq[i] |= kivi::quant_from_y(y0, a0, s) << (4 * j);
           wq[i + 1] |= kivi::quant_from_y(y1, a1, s) << (4 * j);
         }
-        const uint32_t sb = __half_as_ushort(s16), zb = __half_as_ushort(z16);
-        if (j & 1) {
-          sh[j >> 1] |= sb << 16;
-          zh[j >> 1] |= zb << 16;
-        } else {
-          sh[j >> 1] = sb;
-          zh[j >> 1] = zb;
-        }
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i)
         if (rv[i]) *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = wq[i];
-      if (g == 0) {
-        *reinterpret_cast<uint4 *>(P.o_scale + krow * P.o_szrs + c) = make_uint4(sh[0], sh[1], sh[2], sh[3]);
-        *reinterpret_cast<uint4 *>(P.o_zero + krow * P.o_szrs + c) = make_uint4(zh[0], zh[1], zh[2], zh[3]);
-      }
     }
   }
 }

@@ -11,13 +11,16 @@
 // All problems of a call share d; each has its own token count, probes, basis (rank <= 64)
 // and caches.  Launches (all problems at once; the two passes once per grouping mode):
 //   flags   probe flags, deduplicated probe list and count
-//   pack    basis -> bf16 in the two MMA fragment orders below, and a plain row copy
+//   pack    basis -> bf16 in pass1's MMA fragment order, and a plain row copy
 //   pass1   per warp of 32 tokens: dequant, R, ||R||, rhs = R B (mma.sync bf16, fp32
 //           accumulate), per-tile column sums — no shared memory, no block barrier
 //   psum    sums over the probes of R and of rhs
-//   solve   one CTA per problem: (B^T B + 1e-6 I)^-1 in fp64, orth_mu, subspace, mean ||R||
-//   pass2   per warp of 32 tokens: codes = rhs G^-1 (fp32), fitted = codes B^T (mma.sync),
-//           corr, requantise — V groups reduced across the 4 lanes of a row, K groups
+//   solve   one CTA per problem: G^-1 = (B^T B + 1e-6 I)^-1 in fp64, orth_mu, subspace,
+//           mean ||R||
+//   fitb    B G^-1 (= B G^-T, G symmetric) -> bf16 in pass2's MMA fragment order, so that
+//           fitted = codes B^T = rhs (B G^-1)^T needs no per-token solve
+//   pass2   per warp of 32 tokens: fitted = rhs (B G^-1)^T (mma.sync), corr, requantise —
+//           V groups reduced across the 4 lanes of a row, K groups
 //           across the 8 row-lanes of the warp (a warp tile is exactly one K group)
 // Lane (g, q) of a warp owns rows g + 8i (i = 0..3) and, in every block of 32 channels, the
 // 8 contiguous channels 8q..8q+7: pass1 forms its R directly as MMA A fragments by
@@ -25,7 +28,7 @@
 // unchanged), and pass2's basis image permutes output columns so that the accumulator
 // fragments land on those same 8 channels.
 // The products use the basis rounded to bf16 (B~) throughout — G is formed from B~ as well —
-// so `fitted` is the least-squares projection onto col(B~); R and the codes are rounded to
+// so `fitted` is the least-squares projection onto col(B~); R, rhs and B~ G^-1 are rounded to
 // bf16 as MMA operands.  These roundings sit far below the int4 step of the output.
 #include <cstring>
 #include <vector>
@@ -153,13 +156,13 @@ __device__ __forceinline__ __nv_bfloat16 basis_at(const Prob &P, int64_t c, int 
 }
 
 // b1 (pass1 B operand): [block][n-tile][lane][8]: B~[32 block + 8q + j][8 nt + g]
-// b2 (pass2 B operand): [block][k-step][n-tile][lane][4]: B~[ch][16 ks + 2q + {0, 1, 8, 9}],
-//     ch = 32 block + 8 (g >> 1) + 2 nt + (g & 1)
+// b2 (pass2 B operand, written by fitb): [block][k-step][n-tile][lane][4]:
+//     (B~ G^-1)[ch][16 ks + 2q + {0, 1, 8, 9}], ch = 32 block + 8 (g >> 1) + 2 nt + (g & 1)
 // bb: [d][RP] rows
 __global__ void pack_kernel(const __grid_constant__ Batch b, int rp) {
   const Prob &P = b.probs[blockIdx.y];
   const int64_t total = b.d * rp;
-  const int nt_n = rp / 8, ks_n = rp / 16;
+  const int nt_n = rp / 8;
   for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     {
@@ -175,18 +178,6 @@ __global__ void pack_kernel(const __grid_constant__ Batch b, int rp) {
       const int64_t blk = rest / nt_n;
       const int g = lane >> 2, q = lane & 3;
       P.b1[e] = basis_at(P, kCB * blk + 8 * q + j, 8 * nt + g);
-    }
-    {
-      const int x = static_cast<int>(e & 3);
-      const int lane = static_cast<int>((e >> 2) & 31);
-      const int64_t rest = e >> 7;
-      const int nt = static_cast<int>(rest & 3);
-      const int ks = static_cast<int>((rest >> 2) % ks_n);
-      const int64_t blk = (rest >> 2) / ks_n;
-      const int g = lane >> 2, q = lane & 3;
-      const int64_t ch = kCB * blk + 8 * (g >> 1) + 2 * nt + (g & 1);
-      const int k = 16 * ks + 2 * q + (x & 1) + 8 * (x >> 1);
-      P.b2[e] = basis_at(P, ch, k);
     }
   }
 }
@@ -349,46 +340,64 @@ template <int RP>
 __global__ void __launch_bounds__(256) solve_kernel(const __grid_constant__ Batch b) {
   extern __shared__ double Mdyn[];  // [r][2r + 1]: [G | I]
   __shared__ float cp[RP], ca[RP], colsum[RP + 1];
+  __shared__ float wsum[8][RP + 1];
   __shared__ double fac[RP];
+  __shared__ double piv_val;
   __shared__ int piv_row;
   const Prob &P = b.probs[blockIdx.x];
   const int r = P.r;
   const int ldm = 2 * r + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float np = static_cast<float>(*P.ucount);
   const int64_t tiles = (P.n + kWT - 1) / kWT;
   for (int e = threadIdx.x; e < RP * RP; e += blockDim.x) P.ginv[e] = 0.f;
   if (threadIdx.x < RP) cp[threadIdx.x] = ca[threadIdx.x] = 0.f;
-  // column sums of rhs and the sum of ||R|| from the per-tile partials
-  for (int k = threadIdx.x; k <= RP; k += blockDim.x) {
-    float s = 0.f;
-    for (int64_t t = 0; t < tiles; ++t) s += P.part[t * (RP + 1) + k];
-    colsum[k] = s;
+  // column sums of rhs and the sum of ||R|| from the per-tile partials: warp w takes tiles
+  // w, w + 8, ..., lanes the columns
+  {
+    float acc[3] = {0.f, 0.f, 0.f};
+    for (int64_t t = warp; t < tiles; t += 8) {
+      const float *row = P.part + t * (RP + 1);
+#pragma unroll
+      for (int u = 0; u < 3; ++u)
+        if (lane + 32 * u <= RP) acc[u] += row[lane + 32 * u];
+    }
+#pragma unroll
+    for (int u = 0; u < 3; ++u)
+      if (lane + 32 * u <= RP) wsum[warp][lane + 32 * u] = acc[u];
+    __syncthreads();
+    for (int k = threadIdx.x; k <= RP; k += blockDim.x) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) sum += wsum[w][k];
+      colsum[k] = sum;
+    }
   }
   __syncthreads();
   if (r > 0) {
-    // G = B~^T B~ + 1e-6 I: 64-channel tiles of B~ staged in shared memory (fp64 accumulation);
-    // the tile area is the not yet used part of Mdyn past [G | I]
-    double *tile = Mdyn + r * ldm;  // [64][RP] as float
-    float *tf = reinterpret_cast<float *>(tile);
+    // G = B~^T B~ + 1e-6 I: 64-channel tiles of B~ staged in shared memory as fp64 (exact:
+    // bf16 values), fp64 accumulation; the tile area is the not yet used part of Mdyn past [G | I]
+    double *tile = Mdyn + r * ldm;  // [64][RP]
     constexpr int EPT = (RP * RP + 255) / 256;
     double accg[EPT];
+    int gi[EPT], gj[EPT];
 #pragma unroll
-    for (int u = 0; u < EPT; ++u) accg[u] = 0.0;
+    for (int u = 0; u < EPT; ++u) {
+      accg[u] = 0.0;
+      const int e = threadIdx.x + 256 * u;
+      gi[u] = e < RP * RP ? e / RP : 0;
+      gj[u] = e < RP * RP ? e % RP : 0;
+    }
     for (int64_t c0 = 0; c0 < b.d; c0 += 64) {
       for (int e = threadIdx.x; e < 64 * RP; e += blockDim.x) {
         const int64_t c = c0 + e / RP;
-        tf[e] = c < b.d ? __bfloat162float(P.bb[c * RP + e % RP]) : 0.f;
+        tile[e] = c < b.d ? static_cast<double>(__bfloat162float(P.bb[c * RP + e % RP])) : 0.0;
       }
       __syncthreads();
+      for (int cc = 0; cc < 64; ++cc) {
+        const double *tr = tile + cc * RP;
 #pragma unroll
-      for (int u = 0; u < EPT; ++u) {
-        const int e = threadIdx.x + 256 * u;
-        if (e < RP * RP) {
-          const int i = e / RP, j = e % RP;
-          double s = 0.0;
-          for (int cc = 0; cc < 64; ++cc) s += static_cast<double>(tf[cc * RP + i]) * tf[cc * RP + j];
-          accg[u] += s;
-        }
+        for (int u = 0; u < EPT; ++u) accg[u] = fma(tr[gi[u]], tr[gj[u]], accg[u]);
       }
       __syncthreads();
     }
@@ -396,7 +405,7 @@ __global__ void __launch_bounds__(256) solve_kernel(const __grid_constant__ Batc
     for (int u = 0; u < EPT; ++u) {
       const int e = threadIdx.x + 256 * u;
       if (e < RP * RP) {
-        const int i = e / RP, j = e % RP;
+        const int i = gi[u], j = gj[u];
         if (i < r && j < r) {
           Mdyn[i * ldm + j] = accg[u] + (i == j ? 1e-6 : 0.0);
           Mdyn[i * ldm + r + j] = (i == j) ? 1.0 : 0.0;
@@ -404,34 +413,58 @@ __global__ void __launch_bounds__(256) solve_kernel(const __grid_constant__ Batc
       }
     }
     __syncthreads();
+    // Gauss-Jordan with partial pivoting on [G | I]; three barriers per column
+    const int jj = threadIdx.x & 127, i0 = threadIdx.x >> 7;
     for (int col = 0; col < r; ++col) {
-      if (threadIdx.x == 0) {
-        int best = col;
-        double bv = fabs(Mdyn[col * ldm + col]);
-        for (int i = col + 1; i < r; ++i)
-          if (fabs(Mdyn[i * ldm + col]) > bv) {
-            bv = fabs(Mdyn[i * ldm + col]);
-            best = i;
+      if (warp == 0) {
+        // pivot: the first row of largest |G[i][col]|, i >= col (warp arg-max)
+        double bv = -1.0;
+        int bi = r;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int i = col + lane + 32 * u;
+          if (i < r) {
+            const double v = fabs(Mdyn[i * ldm + col]);
+            if (v > bv) {
+              bv = v;
+              bi = i;
+            }
           }
-        piv_row = best;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        const int pr = bi < r ? bi : col;
+        // column multipliers after the row swap
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int i = lane + 32 * u;
+          if (i < r) fac[i] = Mdyn[(i == pr ? col : (i == col ? pr : i)) * ldm + col];
+        }
+        if (lane == 0) {
+          piv_row = pr;
+          piv_val = Mdyn[pr * ldm + col];
+        }
       }
       __syncthreads();
       const int pr = piv_row;
-      if (pr != col)
-        for (int j = threadIdx.x; j < 2 * r; j += blockDim.x) {
-          const double t = Mdyn[col * ldm + j];
-          Mdyn[col * ldm + j] = Mdyn[pr * ldm + j];
-          Mdyn[pr * ldm + j] = t;
-        }
+      const double inv = 1.0 / piv_val;
+      if (i0 == 0 && jj < 2 * r) {
+        const double top = Mdyn[col * ldm + jj], prow = Mdyn[pr * ldm + jj];
+        Mdyn[col * ldm + jj] = prow * inv;
+        if (pr != col) Mdyn[pr * ldm + jj] = top;
+      }
       __syncthreads();
-      const double inv = 1.0 / Mdyn[col * ldm + col];
-      __syncthreads();
-      for (int j = threadIdx.x; j < 2 * r; j += blockDim.x) Mdyn[col * ldm + j] *= inv;
-      for (int i = threadIdx.x; i < r; i += blockDim.x) fac[i] = Mdyn[i * ldm + col];
-      __syncthreads();
-      for (int e = threadIdx.x; e < r * 2 * r; e += blockDim.x) {
-        const int i = e / (2 * r), j = e % (2 * r);
-        if (i != col) Mdyn[i * ldm + j] -= fac[i] * Mdyn[col * ldm + j];
+      if (jj < 2 * r && jj >= col) {
+        const double pv = Mdyn[col * ldm + jj];
+        for (int i = i0; i < r; i += 2)
+          if (i != col) Mdyn[i * ldm + jj] -= fac[i] * pv;
       }
       __syncthreads();
     }
@@ -466,15 +499,38 @@ __global__ void __launch_bounds__(256) solve_kernel(const __grid_constant__ Batc
 }
 
 // ---------------------------------------------------------------------------------------
+// fitb: pass2's B operand, B~ G^-1 in the b2 fragment order; one CTA per 32-channel block
+// ---------------------------------------------------------------------------------------
+template <int RP>
+__global__ void __launch_bounds__(256) fitb_kernel(const __grid_constant__ Batch b) {
+  __shared__ float Gf[RP][RP + 1];
+  __shared__ float Bs[kCB][RP + 1];
+  const Prob &P = b.probs[blockIdx.y];
+  const int64_t blk = blockIdx.x;
+  for (int e = threadIdx.x; e < RP * RP; e += blockDim.x) Gf[e / RP][e % RP] = P.ginv[e];  // zero past r
+  for (int e = threadIdx.x; e < kCB * RP; e += blockDim.x)
+    Bs[e / RP][e % RP] = __bfloat162float(P.bb[(blk * kCB + e / RP) * RP + e % RP]);
+  __syncthreads();
+  constexpr int KS = RP / 16;
+  for (int f = threadIdx.x; f < KS * 512; f += blockDim.x) {
+    const int x = f & 3, lane = (f >> 2) & 31, nt = (f >> 7) & 3, ks = f >> 9;
+    const int g = lane >> 2, q = lane & 3;
+    const int cl = 8 * (g >> 1) + 2 * nt + (g & 1);
+    const int k = 16 * ks + 2 * q + (x & 1) + 8 * (x >> 1);
+    float acc = 0.f;
+#pragma unroll 8
+    for (int j = 0; j < RP; ++j) acc = fmaf(Gf[k][j], Bs[cl][j], acc);
+    P.b2[blk * (KS * 512) + f] = __float2bfloat16_rn(acc);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
 // pass 2
 // ---------------------------------------------------------------------------------------
 template <int RP, int FDT, int MODE>
 __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__ Batch b, int64_t tile_lo) {
-  __shared__ float Gs[RP][RP + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   const Prob &P = b.probs[find_prob(b, tile_lo + blockIdx.x)];
-  for (int e = threadIdx.x; e < RP * RP; e += kThreads) Gs[e / RP][e % RP] = P.ginv[e];
-  __syncthreads();
   const int64_t t0 = (tile_lo + blockIdx.x - P.tile0) * kTM + warp * kWT;
   const int64_t n = P.n;
   if (t0 >= n) return;
@@ -491,39 +547,21 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
     fl[i] = rv[i] && P.flag[row[i]] != 0u;
     w[i] = rv[i] ? fminf(P.dist[row[i]] / mean_dist, 1.f) : 0.f;
   }
-  // codes = rhs G^-1 at this lane's A-fragment positions (fp32), then bf16
+  // A fragments: the row's rhs at this lane's positions k = 16 ks + 2q + {0, 1, 8, 9}, bf16
   uint32_t a[2][KS][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    float cv[KS][4];  // k = 16 ks + 2q + {0, 1, 8, 9}
-#pragma unroll
-    for (int ks = 0; ks < KS; ++ks) cv[ks][0] = cv[ks][1] = cv[ks][2] = cv[ks][3] = 0.f;
-    if (rv[i]) {
-      const float4 *rr = reinterpret_cast<const float4 *>(P.rhs + row[i] * RP);
-#pragma unroll 4
-      for (int i4 = 0; i4 < RP / 4; ++i4) {
-        const float4 x4 = rr[i4];
-        const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float x = xs[u];
-          const float *gr = Gs[4 * i4 + u];
-#pragma unroll
-          for (int ks = 0; ks < KS; ++ks) {
-            const int k0 = 16 * ks + 2 * q;
-            cv[ks][0] = fmaf(x, gr[k0], cv[ks][0]);
-            cv[ks][1] = fmaf(x, gr[k0 + 1], cv[ks][1]);
-            cv[ks][2] = fmaf(x, gr[k0 + 8], cv[ks][2]);
-            cv[ks][3] = fmaf(x, gr[k0 + 9], cv[ks][3]);
-          }
-        }
-      }
-    }
     const int m = i >> 1, h = i & 1;
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
-      a[m][ks][h] = pack_bf16x2(cv[ks][0], cv[ks][1]);
-      a[m][ks][2 + h] = pack_bf16x2(cv[ks][2], cv[ks][3]);
+      float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
+      if (rv[i]) {
+        const float *rr = P.rhs + row[i] * RP + 16 * ks + 2 * q;
+        lo = *reinterpret_cast<const float2 *>(rr);
+        hi = *reinterpret_cast<const float2 *>(rr + 8);
+      }
+      a[m][ks][h] = pack_bf16x2(lo.x, lo.y);
+      a[m][ks][2 + h] = pack_bf16x2(hi.x, hi.y);
     }
   }
 
@@ -860,9 +898,11 @@ int launch(const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStre
     psum_kernel<RP, FDT><<<dim3(slices, kPsumSplit, np), 128, 0, st>>>(b);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
-  const int solve_smem = kMaxRank * (2 * kMaxRank + 1) * 8 + 64 * RP * 4;
+  const int solve_smem = kMaxRank * (2 * kMaxRank + 1) * 8 + 64 * RP * 8;
   DKV_CUDA_CHECK(cudaFuncSetAttribute(solve_kernel<RP>, cudaFuncAttributeMaxDynamicSharedMemorySize, solve_smem));
   solve_kernel<RP><<<np, 256, solve_smem, st>>>(b);
+  DKV_CUDA_CHECK(cudaGetLastError());
+  fitb_kernel<RP><<<dim3(static_cast<unsigned>(b.d / kCB), np), 256, 0, st>>>(b);
   DKV_CUDA_CHECK(cudaGetLastError());
   if (k_tiles > 0) {
     pass2_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL><<<static_cast<unsigned>(k_tiles), kThreads, 0, st>>>(b, 0);

@@ -30,6 +30,7 @@
 // The products use the basis rounded to bf16 (B~) throughout — G is formed from B~ as well —
 // so `fitted` is the least-squares projection onto col(B~); R, rhs and B~ G^-1 are rounded to
 // bf16 as MMA operands.  These roundings sit far below the int4 step of the output.
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -45,7 +46,7 @@ constexpr int kThreads = 32 * kWarps;
 constexpr int kTM = kWT * kWarps;  // tokens per CTA
 constexpr int kCB = 32;            // channels per block
 constexpr int kMaxRank = 64;
-constexpr int kPsumSplit = 64;  // probe-sum CTAs per channel slice
+constexpr int kPsumCtas = 8;  // fewest probe-sum CTAs (of 8 warps) per problem
 
 struct Prob {
   const uint8_t *codes;
@@ -127,13 +128,6 @@ __device__ __forceinline__ void halves8(const __half *p, float (&v)[8]) {
     v[2 * j] = f16lo(w[j]);
     v[2 * j + 1] = f16hi(w[j]);
   }
-}
-
-// dequantised value of one element
-__device__ __forceinline__ float deq1(const Prob &P, int64_t t, int64_t c) {
-  const uint32_t b = P.codes[t * P.crs + c / 2];
-  const int64_t si = P.mode == DKV_KIVI_PER_TOKEN ? t * P.szrs + c / kivi::kG : (t / kivi::kG) * P.szrs + c;
-  return kivi::deq((b >> (4 * (c & 1))) & 0xFu, __half2float(P.scale[si]), __half2float(P.zero[si]));
 }
 
 // ---------------------------------------------------------------------------------------
@@ -309,27 +303,70 @@ __global__ void __launch_bounds__(kThreads) pass1_kernel(const __grid_constant__
 }
 
 // ---------------------------------------------------------------------------------------
-// probe sums: sum_P R (128-channel slices) and sum_P rhs (the last slice), the probes split
-// over kPsumSplit CTAs per slice
+// psum: sums over the (deduplicated) probes of R and of rhs.  `ctas` CTAs of 8 warps per
+// problem; warp w takes probes w, w + 8 ctas, ...; a probe row is read 256 channels at a
+// time with 16-byte loads (8 channels per lane), the CTA's warps are summed in shared memory
+// and one atomic per channel and CTA goes to the problem's sums.
 // ---------------------------------------------------------------------------------------
 template <int RP, int FDT>
-__global__ void __launch_bounds__(128) psum_kernel(const __grid_constant__ Batch b) {
-  const Prob &P = b.probs[blockIdx.z];
+__global__ void __launch_bounds__(256) psum_kernel(const __grid_constant__ Batch b, int ctas) {
+  __shared__ float red[8][256];
+  const Prob &P = b.probs[blockIdx.y];
   const int cnt = *P.ucount;
-  const int slices = static_cast<int>((b.d + 127) / 128);
-  const int sl = blockIdx.x;
-  float s = 0.f;
-  if (sl < slices) {
-    const int64_t c = static_cast<int64_t>(sl) * 128 + threadIdx.x;
-    if (c >= b.d) return;
-    for (int i = blockIdx.y; i < cnt; i += gridDim.y) {
-      const int64_t t = P.uprobe[i];
-      s += load1<FDT>(P.fresh, t * P.frs + c) - deq1(P, t, c);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wstep = 8 * ctas;
+  const int w0 = blockIdx.x * 8 + warp;
+  const bool kmode = P.mode == DKV_KIVI_PER_CHANNEL;
+  for (int64_t c0 = 0; c0 < b.d; c0 += 256) {
+    const int64_t c = c0 + 8 * lane;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (c < b.d) {
+      for (int i = w0; i < cnt; i += wstep) {
+        const int64_t t = P.uprobe[i];
+        float f[8], sc[8], zr[8];
+        load8<FDT>(P.fresh, t * P.frs + c, f);
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(P.codes + t * P.crs + c / 2);
+        if (kmode) {
+          halves8(P.scale + (t / kivi::kG) * P.szrs + c, sc);
+          halves8(P.zero + (t / kivi::kG) * P.szrs + c, zr);
+        } else {
+          const float vs = __half2float(P.scale[t * P.szrs + c / kivi::kG]);
+          const float vz = __half2float(P.zero[t * P.szrs + c / kivi::kG]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) sc[j] = vs, zr[j] = vz;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += f[j] - kivi::deq((w >> (4 * j)) & 0xFu, sc[j], zr[j]);
+      }
     }
-    atomicAdd(&P.sums[RP + c], s);
-  } else if (threadIdx.x < RP) {
-    for (int i = blockIdx.y; i < cnt; i += gridDim.y) s += P.rhs[static_cast<int64_t>(P.uprobe[i]) * RP + threadIdx.x];
-    atomicAdd(&P.sums[threadIdx.x], s);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) red[warp][8 * lane + j] = acc[j];
+    __syncthreads();
+    {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) sum += red[w][threadIdx.x];
+      if (c0 + threadIdx.x < b.d) atomicAdd(&P.sums[RP + c0 + threadIdx.x], sum);
+    }
+    __syncthreads();
+  }
+  // rhs rows: lanes 0 .. RP/4 - 1 take 4 codes each
+  float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (lane < RP / 4)
+    for (int i = w0; i < cnt; i += wstep) {
+      const float4 x = reinterpret_cast<const float4 *>(P.rhs + static_cast<int64_t>(P.uprobe[i]) * RP)[lane];
+      acc4.x += x.x, acc4.y += x.y, acc4.z += x.z, acc4.w += x.w;
+    }
+  if (lane < RP / 4) {
+    red[warp][4 * lane] = acc4.x, red[warp][4 * lane + 1] = acc4.y;
+    red[warp][4 * lane + 2] = acc4.z, red[warp][4 * lane + 3] = acc4.w;
+  }
+  __syncthreads();
+  if (threadIdx.x < RP) {
+    float sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) sum += red[w][threadIdx.x];
+    atomicAdd(&P.sums[threadIdx.x], sum);
   }
 }
 
@@ -894,8 +931,9 @@ int launch(const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStre
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   if (max_probes > 0) {
-    const int slices = static_cast<int>((b.d + 127) / 128) + 1;
-    psum_kernel<RP, FDT><<<dim3(slices, kPsumSplit, np), 128, 0, st>>>(b);
+    // about four CTAs per SM in all, at least kPsumCtas per problem
+    const int ctas = std::max(kPsumCtas, std::min(64, 4 * 148 / np));
+    psum_kernel<RP, FDT><<<dim3(ctas, np), 256, 0, st>>>(b, ctas);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   const int solve_smem = kMaxRank * (2 * kMaxRank + 1) * 8 + 64 * RP * 8;

@@ -51,9 +51,11 @@ __device__ __forceinline__ uint64_t codes_to_f2(uint32_t w, int p) {
 
 // quant_one_fast for y = (x - z) / s already formed with the reciprocal: rint, the tie fallback,
 // saturating conversion (negative -> 0) and the clamp to 15
-__device__ __forceinline__ uint32_t quant_from_y(float y, float a, float s) {
-  if (!(s > 0.f)) return 0u;
-  if (__builtin_expect(fabsf(y - floorf(y) - 0.5f) < 1e-5f, 0)) y = exact_quotient(a, s);
+// The reciprocal form alone: rint(y) clamped to [0, 15] for y = (x - z) * RN(1/s) (y = 0 when
+// s = 0).  Equal to the division form except where y lies within ~2 ulp of a rounding tie
+// (a few in a million codes); for outputs that are not held to bit equality with the
+// division form.
+__device__ __forceinline__ uint32_t quant_recip(float y) {
   const uint32_t q = __float2uint_rn(y);
   return q < 15u ? q : 15u;
 }

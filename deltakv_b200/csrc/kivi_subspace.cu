@@ -724,12 +724,10 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
         uint32_t wq = 0u;
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-          const uint64_t a2 = sub2(f2pack(v[i][2 * p], v[i][2 * p + 1]), z2);
-          float a0, a1, y0, y1;
-          f2unpack(a2, a0, a1);
-          f2unpack(mul2(a2, inv2), y0, y1);
-          wq |= kivi::quant_from_y(y0, a0, s) << (8 * p);
-          wq |= kivi::quant_from_y(y1, a1, s) << (8 * p + 4);
+          float y0, y1;
+          f2unpack(mul2(sub2(f2pack(v[i][2 * p], v[i][2 * p + 1]), z2), inv2), y0, y1);
+          wq |= kivi::quant_recip(y0) << (8 * p);
+          wq |= kivi::quant_recip(y1) << (8 * p + 4);
         }
         if (rv[i]) *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = wq;
       }
@@ -793,12 +791,10 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
         const uint64_t z2 = f2pack(z, z), inv2 = f2pack(inv, inv);
 #pragma unroll
         for (int i = 0; i < 4; i += 2) {
-          const uint64_t a2 = sub2(f2pack(v[i][j], v[i + 1][j]), z2);
-          float a0, a1, y0, y1;
-          f2unpack(a2, a0, a1);
-          f2unpack(mul2(a2, inv2), y0, y1);
-          wq[i] |= kivi::quant_from_y(y0, a0, s) << (4 * j);
-          wq[i + 1] |= kivi::quant_from_y(y1, a1, s) << (4 * j);
+          float y0, y1;
+          f2unpack(mul2(sub2(f2pack(v[i][j], v[i + 1][j]), z2), inv2), y0, y1);
+          wq[i] |= kivi::quant_recip(y0) << (4 * j);
+          wq[i + 1] |= kivi::quant_recip(y1) << (4 * j);
         }
       }
 #pragma unroll

@@ -102,23 +102,30 @@ def _start_block(n_b: int, d: int, k: int, device: torch.device) -> tuple[Tensor
     return hit
 
 
-def topr_basis(residual: Tensor, rank: int, *, iters: int = 3, oversample: int = 8) -> Tensor:
+def _ritz(x: Tensor, q: Tensor, r: int) -> tuple[Tensor, Tensor, Tensor]:
+    """Rayleigh-Ritz on span(q): the top-``r`` Ritz vectors of ``x^T x`` and all Ritz values."""
+    w = torch.matmul(x, q)
+    ev, vec, info = sym_eig(torch.matmul(w.transpose(1, 2), w))
+    return torch.matmul(q, vec[:, :, :r].float()), ev, info
+
+
+def topr_basis(residual: Tensor, rank: int, *, iters: int = 3, min_iters: int = 2, oversample: int = 8) -> Tensor:
     """Leading-``rank`` right singular subspace of ``residual [..., m, d]`` as ``[..., d, rank]``,
     batched over a leading dimension.
 
     The same subspace as :func:`svd_basis` (the reference's ``svd_basis``,
     src/deltakv/patches/subspace.py:37-42), computed by block subspace iteration on
     ``C = R^T R`` — applied as ``R^T (R Q)``, never formed — with re-orthonormalisation and a
-    final Rayleigh-Ritz step (Golub & Van Loan, Matrix Computations, 4th ed., Sec. 8.2.4;
-    Halko, Martinsson & Tropp, SIAM Review 2011, Alg. 4.4): ``iters`` products on
-    ``k = rank + oversample`` columns instead of a full SVD; the k x k Rayleigh-Ritz
-    eigenproblem runs on the device (:func:`sym_eig`).  The subspace converges as
-    ``(l_k / l_rank)^iters`` (eigenvalues of C); the least-squares correction depends on the
-    basis only through its column space, so the rotation within the subspace is immaterial.
-    Batch elements whose Ritz values show a poor gap — estimated subspace error above
-    ``1e-5`` — or whose orthonormalisation or eigensolve failed are recomputed with the exact
-    SVD, so the result never depends on a half-converged iteration.  One host synchronisation
-    (the per-element fallback flags).
+    Rayleigh-Ritz step (Golub & Van Loan, Matrix Computations, 4th ed., Sec. 8.2.4; Halko,
+    Martinsson & Tropp, SIAM Review 2011, Alg. 4.4) on ``k = rank + oversample`` columns
+    instead of a full SVD; the k x k Rayleigh-Ritz eigenproblem runs on the device
+    (:func:`sym_eig`).  The subspace converges as ``(l_k / l_rank)^i`` after ``i`` products
+    (eigenvalues of C); the least-squares correction depends on the basis only through its
+    column space, so the rotation within the subspace is immaterial.  Every element gets
+    ``min_iters`` iterations; those whose Ritz values then estimate a subspace error above
+    ``1e-5`` continue to ``iters``, and any still above it — or whose orthonormalisation or
+    eigensolve failed — are recomputed with the exact SVD, so the result never depends on a
+    half-converged iteration.  One host synchronisation per decision.
     """
     ops._require_cuda(residual)
     x = residual.float()
@@ -131,21 +138,33 @@ def topr_basis(residual: Tensor, rank: int, *, iters: int = 3, oversample: int =
     if k >= m or k > MAX_RITZ:
         basis = torch.stack([svd_basis(x[i], r) for i in range(n_b)])
         return basis if batched else basis[0]
-    q, bad = _start_block(n_b, d, k, x.device)
-    xt = x.transpose(1, 2)
-    for _ in range(iters):
-        q, b2 = _orthonormalize(torch.matmul(xt, torch.matmul(x, q)))
-        bad = bad | b2
-    w = torch.matmul(x, q)
-    t = torch.matmul(w.transpose(1, 2), w)
-    ev, vec, info = sym_eig(t)
-    basis = torch.matmul(q, vec[:, :, :r].float())
-    redo = bad | (info != 0)
-    if k < d:
-        lam_r = ev[:, r - 1].clamp_min(1e-300)
-        est = (ev[:, k - 1].clamp_min(0.0) / lam_r) ** iters
-        redo = redo | ~torch.isfinite(est) | (est > 1e-5)
-    for i in torch.nonzero(redo).view(-1).tolist():  # the one host synchronisation
+    first = max(1, min(int(min_iters), int(iters)))
+
+    def iterate(xb: Tensor, q: Tensor, bad: Tensor, n: int) -> tuple[Tensor, Tensor]:
+        xt = xb.transpose(1, 2)
+        for _ in range(n):
+            q, b2 = _orthonormalize(torch.matmul(xt, torch.matmul(xb, q)))
+            bad = bad | b2
+        return q, bad
+
+    def unsettled(ev: Tensor, info: Tensor, bad: Tensor, done: int) -> Tensor:
+        out = bad | (info != 0)
+        if k < d:
+            est = (ev[:, k - 1].clamp_min(0.0) / ev[:, r - 1].clamp_min(1e-300)) ** done
+            out = out | ~torch.isfinite(est) | (est > 1e-5)
+        return out
+
+    q0, bad0 = _start_block(n_b, d, k, x.device)
+    q, bad = iterate(x, q0, bad0, first)
+    basis, ev, info = _ritz(x, q, r)
+    idx = torch.nonzero(unsettled(ev, info, bad, first)).view(-1)
+    if idx.numel() and iters > first:  # continue only the undecided elements
+        xs = x[idx]
+        qs, bads = iterate(xs, q[idx], bad[idx], int(iters) - first)
+        bsub, evs, infos = _ritz(xs, qs, r)
+        basis[idx] = bsub
+        idx = idx[unsettled(evs, infos, bads, int(iters))]
+    for i in idx.tolist():
         basis[i] = svd_basis(x[i], r)
     return basis if batched else basis[0]
 

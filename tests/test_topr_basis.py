@@ -58,6 +58,27 @@ def test_topr_basis_falls_back_to_svd_without_a_gap(cuda):
     assert _proj_diff(svd_basis(x, 8), topr_basis(x, 8)) < 1e-5
 
 
+def test_topr_basis_iterates_further_before_falling_back(cuda, monkeypatch):
+    # eigenvalue ratio 1e-2 past the rank: two iterations estimate 1e-4 (too coarse), the
+    # third 1e-6 — settled by iterating, without the SVD
+    import deltakv_b200.subspace as S
+
+    calls = []
+    monkeypatch.setattr(S, "svd_basis", lambda x, r: calls.append(1) or svd_basis(x, r))
+    g = torch.Generator().manual_seed(4)
+    m, d, r = 600, 256, 8
+    u, _ = torch.linalg.qr(torch.randn(m, d, generator=g, dtype=torch.float64))
+    v, _ = torch.linalg.qr(torch.randn(d, d, generator=g, dtype=torch.float64))
+    sv = torch.cat([torch.linspace(2.0, 1.0, r, dtype=torch.float64), 0.1 * torch.linspace(1.0, 0.5, d - r, dtype=torch.float64)])
+    x = ((u * sv) @ v.T).float().to(cuda)
+    b = S.topr_basis(torch.stack([x, x]), r)
+    assert not calls
+    assert _proj_diff(v[:, :r].float().to(cuda), b[0]) < 1e-5
+    assert _proj_diff(v[:, :r].float().to(cuda), b[1]) < 1e-5
+    one = S.topr_basis(x, r, iters=2)  # capped at two: the estimate fails, the SVD is used
+    assert calls and _proj_diff(svd_basis(x, r), one) < 1e-6
+
+
 def test_topr_basis_few_rows_uses_svd(cuda):
     # m <= rank + oversample: the exact SVD directly
     g = torch.Generator().manual_seed(3)

@@ -179,8 +179,39 @@ __global__ void pack_kernel(const __grid_constant__ Batch b, int rp) {
 // ---------------------------------------------------------------------------------------
 // pass 1
 // ---------------------------------------------------------------------------------------
+constexpr int kP1Stages = 3;  // pass1 staging depth (blocks in flight per warp)
+
+// one block's operands for one warp in pass1: fresh (16 or 32 B per lane and row), codes
+// (4 B per lane and row) and, for K, the group's scale / zero (16 B each per lane)
+template <int FDT, int MODE>
+struct P1Stage {
+  static constexpr int kFB = FDT == DKV_F32 ? 2 : 1;
+  uint4 fr[4][kFB][32];
+  uint32_t cd[4][32];
+  uint4 sz[2][32];
+};
+template <int FDT>
+struct P1Stage<FDT, DKV_KIVI_PER_TOKEN> {  // V: the rows' scale / zero are read directly
+  static constexpr int kFB = FDT == DKV_F32 ? 2 : 1;
+  uint4 fr[4][kFB][32];
+  uint32_t cd[4][32];
+};
+
+template <int FDT, int MODE>
+constexpr int p1_smem_bytes() {
+  return static_cast<int>(sizeof(P1Stage<FDT, MODE>)) * kP1Stages * kWarps;
+}
+
+// CTAs per SM that pass1 is compiled for (its register budget; measured per rank tile)
+template <int RP, int MODE>
+constexpr int p1_min_blocks() {
+  constexpr bool k = MODE == DKV_KIVI_PER_CHANNEL;
+  return RP == 16 ? (k ? 4 : 6) : RP == 32 ? (k ? 4 : 5) : RP == 48 ? 4 : (k ? 3 : 4);
+}
+
 template <int RP, int FDT, int MODE>
-__global__ void __launch_bounds__(kThreads) pass1_kernel(const __grid_constant__ Batch b, int64_t tile_lo) {
+__global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
+    pass1_kernel(const __grid_constant__ Batch b, int64_t tile_lo) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   const Prob &P = b.probs[find_prob(b, tile_lo + blockIdx.x)];
   const int64_t t0 = (tile_lo + blockIdx.x - P.tile0) * kTM + warp * kWT;
@@ -203,12 +234,62 @@ __global__ void __launch_bounds__(kThreads) pass1_kernel(const __grid_constant__
   }
   const uint4 *b1 = reinterpret_cast<const uint4 *>(P.b1) + lane;
   const int n_blocks = static_cast<int>(b.d / kCB);
+  const int64_t krow = t0 / kivi::kG;
+  // per-warp staging ring: each lane copies (cp.async) and later reads back only its own
+  // bytes — fresh, codes and the K group's scale/zero of the block kP1Stages - 1 ahead — so
+  // no barrier is needed and the loads stay in flight across blocks without registers
+  using Stage = P1Stage<FDT, MODE>;
+  extern __shared__ __align__(16) unsigned char p1_smem[];
+  Stage *ring = reinterpret_cast<Stage *>(p1_smem) + warp * kP1Stages;
+  constexpr int kFB = Stage::kFB;
+  constexpr int kEs = FDT == DKV_F32 ? 4 : 2;
+  auto issue = [&](int cb) {
+    if (cb < n_blocks) {
+      Stage &S = ring[cb % kP1Stages];
+      const int64_t c = static_cast<int64_t>(cb) * kCB + 8 * q;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t rr = rv[i] ? row[i] : t0;
+        const unsigned char *fp = static_cast<const unsigned char *>(P.fresh) + (rr * P.frs + c) * kEs;
+#pragma unroll
+        for (int f = 0; f < kFB; ++f) cp_async16(&S.fr[i][f][lane], fp + 16 * f, rv[i] ? 16u : 0u);
+        cp_async4(&S.cd[i][lane], P.codes + rr * P.crs + c / 2, rv[i] ? 4u : 0u);
+      }
+      if constexpr (kmode) {
+        cp_async16(&S.sz[0][lane], P.scale + krow * P.szrs + c, 16u);
+        cp_async16(&S.sz[1][lane], P.zero + krow * P.szrs + c, 16u);
+      }
+    }
+    cp_async_commit();  // possibly empty: keeps the group count per block fixed
+  };
+#pragma unroll
+  for (int s0 = 0; s0 < kP1Stages - 1; ++s0) issue(s0);
+  // V: the rows' scale / zero — loaded one block ahead into registers for the wider rank
+  // tiles (latency-bound), at the point of use for RP 16 (occupancy-bound); measured choice
+  constexpr bool kVPre = !kmode && RP >= 32;
+  uint32_t vsz[4], vsz_next[4];
+  auto load_vsz = [&](int cb, uint32_t (&o)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      o[i] = (cb < n_blocks && rv[i]) ? (static_cast<uint32_t>(__half_as_ushort(P.scale[row[i] * P.szrs + cb])) |
+                                         (static_cast<uint32_t>(__half_as_ushort(P.zero[row[i] * P.szrs + cb])) << 16))
+                                      : 0u;
+  };
+  if constexpr (kVPre) load_vsz(0, vsz);
   for (int cb = 0; cb < n_blocks; ++cb) {
-    const int64_t c = static_cast<int64_t>(cb) * kCB + 8 * q;
+    issue(cb + kP1Stages - 1);
+    if constexpr (kVPre) load_vsz(cb + 1, vsz_next);
+    cp_async_wait<kP1Stages - 1>();
+    const Stage &S = ring[cb % kP1Stages];
     float ks8[8], kz8[8];
-    if (kmode) {
-      halves8(P.scale + (t0 / kivi::kG) * P.szrs + c, ks8);
-      halves8(P.zero + (t0 / kivi::kG) * P.szrs + c, kz8);
+    if constexpr (kmode) {
+      const uint4 sv = S.sz[0][lane], zv = S.sz[1][lane];
+      const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, zw[4] = {zv.x, zv.y, zv.z, zv.w};
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        ks8[2 * p] = f16lo(sw[p]), ks8[2 * p + 1] = f16hi(sw[p]);
+        kz8[2 * p] = f16lo(zw[p]), kz8[2 * p + 1] = f16hi(zw[p]);
+      }
     }
     uint32_t a[2][2][4];  // [m-tile][k-step][reg]
 #pragma unroll
@@ -216,10 +297,26 @@ __global__ void __launch_bounds__(kThreads) pass1_kernel(const __grid_constant__
       float r[8];
       if (rv[i]) {
         float f[8];
-        load8<FDT>(P.fresh, row[i] * P.frs + c, f);
-        const uint32_t w = *reinterpret_cast<const uint32_t *>(P.codes + row[i] * P.crs + c / 2);
+        if (FDT == DKV_F32) {
+          const uint4 u0 = S.fr[i][0][lane], u1 = S.fr[i][kFB - 1][lane];
+          f[0] = __uint_as_float(u0.x), f[1] = __uint_as_float(u0.y), f[2] = __uint_as_float(u0.z);
+          f[3] = __uint_as_float(u0.w), f[4] = __uint_as_float(u1.x), f[5] = __uint_as_float(u1.y);
+          f[6] = __uint_as_float(u1.z), f[7] = __uint_as_float(u1.w);
+        } else {
+          const uint4 u = S.fr[i][0][lane];
+          const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            f[2 * j] = FDT == DKV_BF16 ? bf16lo(w4[j]) : f16lo(w4[j]);
+            f[2 * j + 1] = FDT == DKV_BF16 ? bf16hi(w4[j]) : f16hi(w4[j]);
+          }
+        }
+        const uint32_t w = S.cd[i][lane];
         float vs = 0.f, vz = 0.f;
-        if (!kmode) {
+        if constexpr (kVPre) {
+          vs = f16lo(vsz[i]);
+          vz = f16hi(vsz[i]);
+        } else if constexpr (!kmode) {
           vs = __half2float(P.scale[row[i] * P.szrs + cb]);
           vz = __half2float(P.zero[row[i] * P.szrs + cb]);
         }
@@ -255,7 +352,12 @@ __global__ void __launch_bounds__(kThreads) pass1_kernel(const __grid_constant__
         mma16816_bf16(acc[m][nt], a[m][1][0], a[m][1][1], a[m][1][2], a[m][1][3], bv.z, bv.w);
       }
     }
+    if constexpr (kVPre) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) vsz[i] = vsz_next[i];
+    }
   }
+  cp_async_wait<0>();
 
   // ||R|| per row (4 lanes per row) and the tile's sum
   float dsum = 0.f;
@@ -919,11 +1021,18 @@ int launch(const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStre
   }
   // the table holds the K (per-channel) problems first (tiles [0, k_tiles)), then the V ones
   if (k_tiles > 0) {
-    pass1_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL><<<static_cast<unsigned>(k_tiles), kThreads, 0, st>>>(b, 0);
+    constexpr int sm = p1_smem_bytes<FDT, DKV_KIVI_PER_CHANNEL>();
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(pass1_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+    pass1_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL><<<static_cast<unsigned>(k_tiles), kThreads, sm, st>>>(b, 0);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   if (b.n_tiles > k_tiles) {
-    pass1_kernel<RP, FDT, DKV_KIVI_PER_TOKEN><<<static_cast<unsigned>(b.n_tiles - k_tiles), kThreads, 0, st>>>(b, k_tiles);
+    constexpr int sm = p1_smem_bytes<FDT, DKV_KIVI_PER_TOKEN>();
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(pass1_kernel<RP, FDT, DKV_KIVI_PER_TOKEN>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+    pass1_kernel<RP, FDT, DKV_KIVI_PER_TOKEN><<<static_cast<unsigned>(b.n_tiles - k_tiles), kThreads, sm, st>>>(
+        b, k_tiles);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   if (max_probes > 0) {

@@ -206,9 +206,13 @@ __device__ __forceinline__ void cp_async_16(uint32_t saddr, const void *g) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
 }
 // the same with a source size: bytes past `src_bytes` are zero-filled (0: nothing is read);
-// 16 bytes cached in L2 only, or 4 bytes
+// 16 bytes cached in L2 only, or 8 / 4 bytes
 __device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async8(void *dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
                : "memory");
 }
 __device__ __forceinline__ void cp_async4(void *dst, const void *src, uint32_t src_bytes) {

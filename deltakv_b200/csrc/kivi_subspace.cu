@@ -316,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
         if constexpr (kVPre) {
           vs = f16lo(vsz[i]);
           vz = f16hi(vsz[i]);
-        } else if constexpr (!kmode) {
+        } else if constexpr (!kmode) {  // small scattered reads: cheaper direct than as 4-byte async copies
           vs = __half2float(P.scale[row[i] * P.szrs + cb]);
           vz = __half2float(P.zero[row[i] * P.szrs + cb]);
         }
@@ -666,15 +666,58 @@ __global__ void __launch_bounds__(256) fitb_kernel(const __grid_constant__ Batch
 // ---------------------------------------------------------------------------------------
 // pass 2
 // ---------------------------------------------------------------------------------------
+constexpr int kP2Stages = 3;  // pass2 staging depth (blocks in flight per warp)
+
+// pass2's basis fragments are staged with the other operands while they are small (RP <= 32)
+template <int RP>
+constexpr int p2_bq() {
+  return RP / 16 <= 2 ? (RP / 16) * 4 : 1;
+}
+// one block's operands for one warp in pass2: codes (4 B per lane and row), the K group's
+// scale / zero (16 B each per lane), the lane's basis fragments (8 B each)
+template <int RP, bool K>
+struct P2Stage {
+  uint32_t cd[4][32];
+  uint4 sz[2][32];
+  uint2 bq[p2_bq<RP>()][32];
+};
+template <int RP>
+struct P2Stage<RP, false> {  // V: the rows' scale / zero are read directly
+  uint32_t cd[4][32];
+  uint2 bq[p2_bq<RP>()][32];
+};
+
+template <int RP, int MODE>
+constexpr int p2_ring_bytes() {
+  return static_cast<int>(sizeof(P2Stage<RP, MODE == DKV_KIVI_PER_CHANNEL>)) * kP2Stages * kWarps;
+}
+
+// CTAs per SM that pass2 is compiled for (its register budget; measured per rank tile)
+template <int RP, int MODE>
+constexpr int p2_min_blocks() {
+  constexpr bool k = MODE == DKV_KIVI_PER_CHANNEL;
+  return RP <= 32 ? (k ? 4 : 5) : RP == 48 ? 4 : 3;
+}
+
 template <int RP, int FDT, int MODE>
-__global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__ Batch b, int64_t tile_lo) {
+__global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
+    pass2_kernel(const __grid_constant__ Batch b, int64_t tile_lo) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   const Prob &P = b.probs[find_prob(b, tile_lo + blockIdx.x)];
   const int64_t t0 = (tile_lo + blockIdx.x - P.tile0) * kTM + warp * kWT;
   const int64_t n = P.n;
-  if (t0 >= n) return;
   constexpr int KS = RP / 16;
   constexpr bool kmode = MODE == DKV_KIVI_PER_CHANNEL;
+  constexpr bool kStageB = KS <= 2;
+  // shared: orth_mu [d] for the whole CTA, then each warp's staging ring
+  extern __shared__ __align__(16) unsigned char p2_smem[];
+  float *mu_s = reinterpret_cast<float *>(p2_smem);
+  for (int64_t e = threadIdx.x; e < b.d / 4; e += kThreads)
+    reinterpret_cast<float4 *>(mu_s)[e] = reinterpret_cast<const float4 *>(P.mu)[e];
+  __syncthreads();
+  if (t0 >= n) return;
+  using Stage = P2Stage<RP, kmode>;
+  Stage *ring = reinterpret_cast<Stage *>(p2_smem + b.d * 4) + warp * kP2Stages;
   const float mean_dist = P.subv[b.d];
   int64_t row[4];
   bool rv[4], fl[4];
@@ -707,7 +750,33 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
   const uint2 *b2 = reinterpret_cast<const uint2 *>(P.b2) + lane;
   const int n_blocks = static_cast<int>(b.d / kCB);
   const int64_t krow = t0 / kivi::kG;
+  // per-warp staging ring (cp.async, kP2Stages - 1 blocks ahead): each lane copies and later
+  // reads back only its own bytes, so no barrier is needed
+  auto issue = [&](int cb) {
+    if (cb < n_blocks) {
+      Stage &S = ring[cb % kP2Stages];
+      const int64_t c = static_cast<int64_t>(cb) * kCB + 8 * q;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        cp_async4(&S.cd[i][lane], P.codes + (rv[i] ? row[i] : t0) * P.crs + c / 2, rv[i] ? 4u : 0u);
+      if constexpr (kmode) {
+        cp_async16(&S.sz[0][lane], P.scale + krow * P.szrs + c, 16u);
+        cp_async16(&S.sz[1][lane], P.zero + krow * P.szrs + c, 16u);
+      }
+      if constexpr (kStageB) {
+#pragma unroll
+        for (int f = 0; f < KS * 4; ++f)
+          cp_async8(&S.bq[f][lane], b2 + (static_cast<int64_t>(cb) * KS * 4 + f) * 32, 8u);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int s0 = 0; s0 < kP2Stages - 1; ++s0) issue(s0);
   for (int cb = 0; cb < n_blocks; ++cb) {
+    issue(cb + kP2Stages - 1);
+    cp_async_wait<kP2Stages - 1>();
+    const Stage &S = ring[cb % kP2Stages];
     const int64_t c = static_cast<int64_t>(cb) * kCB + 8 * q;
     float acc[2][4][4];
 #pragma unroll
@@ -718,26 +787,27 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
     for (int ks = 0; ks < KS; ++ks) {
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
-        const uint2 bv = b2[((static_cast<int64_t>(cb) * KS + ks) * 4 + nt) * 32];
+        uint2 bv;
+        if constexpr (kStageB) bv = S.bq[kStageB ? ks * 4 + nt : 0][lane];
+        else bv = b2[((static_cast<int64_t>(cb) * KS + ks) * 4 + nt) * 32];
 #pragma unroll
         for (int m = 0; m < 2; ++m) mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], bv.x, bv.y);
       }
     }
     uint64_t mu2[4];
     {
-      const float4 *mp = reinterpret_cast<const float4 *>(P.mu + c);
+      const float4 *mp = reinterpret_cast<const float4 *>(mu_s + c);
       const float4 x = mp[0], y = mp[1];
       mu2[0] = f2pack(x.x, x.y), mu2[1] = f2pack(x.z, x.w), mu2[2] = f2pack(y.x, y.y), mu2[3] = f2pack(y.z, y.w);
     }
     uint64_t ks2[4], kz2[4];  // K: scale / zero of channels (2p, 2p+1)
-    if (kmode) {
-      float ks8[8], kz8[8];
-      halves8(P.scale + krow * P.szrs + c, ks8);
-      halves8(P.zero + krow * P.szrs + c, kz8);
+    if constexpr (kmode) {
+      const uint4 sv = S.sz[0][lane], zv = S.sz[1][lane];
+      const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, zw[4] = {zv.x, zv.y, zv.z, zv.w};
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
-        ks2[p] = f2pack(ks8[2 * p], ks8[2 * p + 1]);
-        kz2[p] = f2pack(kz8[2 * p], kz8[2 * p + 1]);
+        ks2[p] = f2pack(f16lo(sw[p]), f16hi(sw[p]));
+        kz2[p] = f2pack(f16lo(zw[p]), f16hi(zw[p]));
       }
     }
     // corrected values: rows g + 8i, channels 8q + j; (reused + fitted) + w orth_mu in packed
@@ -752,9 +822,9 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[i][j] = f[j];
       } else if (rv[i]) {
-        const uint32_t wq = *reinterpret_cast<const uint32_t *>(P.codes + row[i] * P.crs + c / 2);
+        const uint32_t wq = S.cd[i][lane];
         uint64_t vs2 = 0, vz2 = 0;
-        if (!kmode) {
+        if constexpr (!kmode) {  // small scattered reads: cheaper direct than as 4-byte async copies
           const float vs = __half2float(P.scale[row[i] * P.szrs + cb]);
           const float vz = __half2float(P.zero[row[i] * P.szrs + cb]);
           vs2 = f2pack(vs, vs);
@@ -904,6 +974,7 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(const __grid_constant__
         if (rv[i]) *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = wq[i];
     }
   }
+  cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1048,11 +1119,18 @@ int launch(const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStre
   fitb_kernel<RP><<<dim3(static_cast<unsigned>(b.d / kCB), np), 256, 0, st>>>(b);
   DKV_CUDA_CHECK(cudaGetLastError());
   if (k_tiles > 0) {
-    pass2_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL><<<static_cast<unsigned>(k_tiles), kThreads, 0, st>>>(b, 0);
+    const int sm = static_cast<int>(b.d * 4) + p2_ring_bytes<RP, DKV_KIVI_PER_CHANNEL>();
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(pass2_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+    pass2_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL><<<static_cast<unsigned>(k_tiles), kThreads, sm, st>>>(b, 0);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   if (b.n_tiles > k_tiles) {
-    pass2_kernel<RP, FDT, DKV_KIVI_PER_TOKEN><<<static_cast<unsigned>(b.n_tiles - k_tiles), kThreads, 0, st>>>(b, k_tiles);
+    const int sm = static_cast<int>(b.d * 4) + p2_ring_bytes<RP, DKV_KIVI_PER_TOKEN>();
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(pass2_kernel<RP, FDT, DKV_KIVI_PER_TOKEN>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+    pass2_kernel<RP, FDT, DKV_KIVI_PER_TOKEN><<<static_cast<unsigned>(b.n_tiles - k_tiles), kThreads, sm, st>>>(
+        b, k_tiles);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   return DKV_OK;

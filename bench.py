@@ -978,9 +978,8 @@ def kivi_k_bases(base, adapter):
     r = adapter["rank"]
     p = adapter["probes"]
     layers = adapter["layers"]
-    res = torch.empty(len(layers), p.numel(), base[0][0].d, dtype=torch.float32, device=p.device)
-    for l, views in enumerate(layers):
-        K.probe_residual(base[l][0], views[0]["fresh"], p, out=res[l])
+    res = K.probe_residuals([base[l][0] for l in range(len(layers))], [views[0]["fresh"] for views in layers],
+                            [p] * len(layers))
     bases = topr_basis(res, min(r, max(1, p.numel() - 1)))
     return [bases[l] for l in range(len(layers))]
 

@@ -47,6 +47,7 @@ EXPORTED = (
     "dkv_kivi_dequantize",
     "dkv_kivi_patch",
     "dkv_kivi_probe_residual",
+    "dkv_kivi_probe_residual_batched",
     "dkv_kivi_subspace_workspace_bytes",
     "dkv_kivi_subspace_correct",
     "dkv_lora_scores",
@@ -156,6 +157,15 @@ class KiviCache(C.Structure):
         ("n_tokens", C.c_int64),
         ("d", C.c_int64),
         ("mode", C.c_int32),
+    ]
+
+
+class KiviProbeJob(C.Structure):
+    _fields_ = [
+        ("base", KiviCache),
+        ("fresh", C.c_void_p),
+        ("fresh_row_stride", C.c_int64),
+        ("rows", C.c_void_p),
     ]
 
 
@@ -284,6 +294,8 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_kivi_patch.argtypes = [C.POINTER(KiviCache), P, I32, I64, C.POINTER(KiviCache), P]
     lib.dkv_kivi_probe_residual.restype = C.c_int
     lib.dkv_kivi_probe_residual.argtypes = [C.POINTER(KiviCache), P, I32, I64, P, I64, P, I64, P, P]
+    lib.dkv_kivi_probe_residual_batched.restype = C.c_int
+    lib.dkv_kivi_probe_residual_batched.argtypes = [C.POINTER(KiviProbeJob), I32, I32, I64, P, I64, I64, P, P]
     lib.dkv_kivi_subspace_workspace_bytes.restype = C.c_int
     lib.dkv_kivi_subspace_workspace_bytes.argtypes = [C.POINTER(KiviSubspaceProblem), I32, C.POINTER(C.c_int64)]
     lib.dkv_kivi_subspace_correct.restype = C.c_int

@@ -160,6 +160,80 @@ __global__ void probe_residual_kernel(Cache c, int mode, const void *fresh, int 
   }
 }
 
+// Batched probe residual: job j = (cache, fresh, probe rows); one warp per probe row, each
+// lane 8 channels at a time (16-byte fresh loads, 4-byte codes, 16-byte K scale/zero).
+constexpr int kMaxProbeJobs = 64;
+struct ProbeJob {
+  Cache c;
+  int mode;
+  const void *fresh;
+  int64_t frs;
+  const int32_t *rows;
+};
+struct ProbeJobs {
+  int n_jobs, fdt;
+  int64_t n_rows, ojs, ors;
+  float *out;
+  int32_t *status;
+  ProbeJob jobs[kMaxProbeJobs];
+};
+
+__device__ __forceinline__ void fresh8(const void *base, int fdt, int64_t off, float (&f)[8]) {
+  if (fdt == DKV_F32) {
+    const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(base) + off);
+    const float4 a = p[0], b = p[1];
+    f[0] = a.x, f[1] = a.y, f[2] = a.z, f[3] = a.w, f[4] = b.x, f[5] = b.y, f[6] = b.z, f[7] = b.w;
+  } else {
+    const uint4 a = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(base) + off);
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      f[2 * j] = fdt == DKV_BF16 ? bf16lo(w[j]) : f16lo(w[j]);
+      f[2 * j + 1] = fdt == DKV_BF16 ? bf16hi(w[j]) : f16hi(w[j]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) probe_residual_batched_kernel(const __grid_constant__ ProbeJobs J) {
+  const ProbeJob &P = J.jobs[blockIdx.y];
+  const int lane = threadIdx.x & 31;
+  const int64_t wstep = static_cast<int64_t>(gridDim.x) * 8;
+  for (int64_t k = blockIdx.x * 8 + (threadIdx.x >> 5); k < J.n_rows; k += wstep) {
+    const int64_t t = P.rows[k];
+    if (t < 0 || t >= P.c.n) {
+      if (lane == 0) record_error(J.status, DKV_ERR_INVALID_ARGUMENT);
+      continue;
+    }
+    float *o = J.out + blockIdx.y * J.ojs + k * J.ors;
+    for (int64_t c0 = 8 * lane; c0 < P.c.d; c0 += 256) {
+      float f[8], s[8], z[8];
+      fresh8(P.fresh, J.fdt, t * P.frs + c0, f);
+      const uint32_t w = *reinterpret_cast<const uint32_t *>(P.c.codes + t * P.c.crs + c0 / 2);
+      if (P.mode == DKV_KIVI_PER_CHANNEL) {
+        const uint4 sv = *reinterpret_cast<const uint4 *>(P.c.scale + (t / kG) * P.c.szrs + c0);
+        const uint4 zv = *reinterpret_cast<const uint4 *>(P.c.zero + (t / kG) * P.c.szrs + c0);
+        const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, zw[4] = {zv.x, zv.y, zv.z, zv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          s[2 * j] = f16lo(sw[j]), s[2 * j + 1] = f16hi(sw[j]);
+          z[2 * j] = f16lo(zw[j]), z[2 * j + 1] = f16hi(zw[j]);
+        }
+      } else {
+        const float vs = __half2float(P.c.scale[t * P.c.szrs + c0 / kG]);
+        const float vz = __half2float(P.c.zero[t * P.c.szrs + c0 / kG]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s[j] = vs, z[j] = vz;
+      }
+      float r[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) r[j] = f[j] - deq((w >> (4 * j)) & 0xFu, s[j], z[j]);
+      float4 *op = reinterpret_cast<float4 *>(o + c0);
+      op[0] = make_float4(r[0], r[1], r[2], r[3]);
+      op[1] = make_float4(r[4], r[5], r[6], r[7]);
+    }
+  }
+}
+
 int check(const dkv_kivi_cache *c, Cache &o) {
   if (c == nullptr) return DKV_ERR_INVALID_ARGUMENT;
   if (c->mode != DKV_KIVI_PER_CHANNEL && c->mode != DKV_KIVI_PER_TOKEN) return DKV_ERR_INVALID_ARGUMENT;
@@ -261,5 +335,48 @@ extern "C" int dkv_kivi_probe_residual(const dkv_kivi_cache *base, const void *f
   probe_residual_kernel<<<static_cast<unsigned>((work + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       c, base->mode, fresh, fresh_dtype, fresh_row_stride, rows, n_rows, out, out_row_stride, status);
   DKV_CUDA_CHECK(cudaGetLastError());
+  return DKV_OK;
+}
+
+extern "C" int dkv_kivi_probe_residual_batched(const dkv_kivi_probe_job *jobs, int32_t n_jobs, int32_t fresh_dtype,
+                                               int64_t n_rows, float *out, int64_t out_job_stride,
+                                               int64_t out_row_stride, int32_t *status, dkv_stream_t stream) {
+  if (n_jobs < 0 || n_rows < 0) return DKV_ERR_INVALID_ARGUMENT;
+  if (fresh_dtype != DKV_F32 && fresh_dtype != DKV_F16 && fresh_dtype != DKV_BF16) return DKV_ERR_UNSUPPORTED;
+  if (n_jobs == 0 || n_rows == 0) return DKV_OK;
+  if (jobs == nullptr || out == nullptr) return DKV_ERR_INVALID_ARGUMENT;
+  const int64_t d = jobs[0].base.d;
+  const int esz = fresh_dtype == DKV_F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (out_row_stride & 3) || (out_job_stride & 3)) return DKV_ERR_ALIGNMENT;
+  if (out_row_stride < d || out_job_stride < (n_rows - 1) * out_row_stride + d) return DKV_ERR_INVALID_ARGUMENT;
+  ProbeJobs J;
+  J.fdt = fresh_dtype;
+  J.n_rows = n_rows;
+  J.ojs = out_job_stride;
+  J.ors = out_row_stride;
+  J.status = status;
+  for (int32_t j0 = 0; j0 < n_jobs; j0 += kMaxProbeJobs) {
+    const int nj = n_jobs - j0 < kMaxProbeJobs ? n_jobs - j0 : kMaxProbeJobs;
+    for (int j = 0; j < nj; ++j) {
+      const dkv_kivi_probe_job &q = jobs[j0 + j];
+      Cache c;
+      const int rc = check(&q.base, c);
+      if (rc) return rc;
+      if (c.d != d) return DKV_ERR_INVALID_ARGUMENT;
+      if (q.fresh == nullptr || q.rows == nullptr || q.fresh_row_stride < d) return DKV_ERR_INVALID_ARGUMENT;
+      if ((reinterpret_cast<uintptr_t>(q.fresh) & 15) || ((q.fresh_row_stride * esz) & 15)) return DKV_ERR_ALIGNMENT;
+      if ((reinterpret_cast<uintptr_t>(c.codes) & 3) || (c.crs & 3)) return DKV_ERR_ALIGNMENT;
+      if (q.base.mode == DKV_KIVI_PER_CHANNEL &&
+          ((reinterpret_cast<uintptr_t>(c.scale) & 15) || (reinterpret_cast<uintptr_t>(c.zero) & 15) || (c.szrs & 7)))
+        return DKV_ERR_ALIGNMENT;
+      J.jobs[j] = ProbeJob{c, q.base.mode, q.fresh, q.fresh_row_stride, q.rows};
+    }
+    J.n_jobs = nj;
+    J.out = out + static_cast<int64_t>(j0) * out_job_stride;
+    const int64_t want = (n_rows + 7) / 8;  // one warp per row, 8 warps per CTA
+    const unsigned gx = static_cast<unsigned>(want < 64 ? want : 64);
+    probe_residual_batched_kernel<<<dim3(gx, nj), 256, 0, static_cast<cudaStream_t>(stream)>>>(J);
+    DKV_CUDA_CHECK(cudaGetLastError());
+  }
   return DKV_OK;
 }

@@ -140,6 +140,31 @@ def probe_residual(base: KiviTensor, fresh: Tensor, probe_index: Tensor, out: Te
     return out
 
 
+def probe_residuals(bases: list[KiviTensor], freshes: list[Tensor], probe_indices: list[Tensor],
+                    out: Tensor | None = None) -> Tensor:
+    """:func:`probe_residual` for many caches in one launch: ``out[j] = fresh_j[P_j] -
+    dequant(base_j)[P_j]`` as fp32 ``[jobs, |P|, d]`` (every ``P_j`` the same length, every
+    fresh the same dtype)."""
+    if not bases:
+        raise ValueError("no caches")
+    fr = [_rows(f) for f in freshes]
+    dev = fr[0].device
+    rows = [p.to(device=dev, dtype=torch.int32).contiguous() for p in probe_indices]
+    m, d = rows[0].numel(), bases[0].d
+    if any(r.numel() != m for r in rows) or any(f.dtype != fr[0].dtype for f in fr):
+        raise ValueError("probe_residuals: every job needs the same probe count and fresh dtype")
+    if out is None:
+        out = torch.empty(len(bases), m, d, dtype=torch.float32, device=dev)
+    jobs = (L.KiviProbeJob * len(bases))(*[
+        L.KiviProbeJob(base=b.desc(), fresh=f.data_ptr(), fresh_row_stride=f.stride(0), rows=r.data_ptr())
+        for b, f, r in zip(bases, fr, rows)])
+    st = ops.status_word(dev)
+    rc = L.lib().dkv_kivi_probe_residual_batched(jobs, len(bases), ops.dkv_dtype(fr[0].dtype), m, out.data_ptr(),
+                                                 out.stride(0), out.stride(1), st.ptr, ops.stream_ptr())
+    L.check(rc, "dkv_kivi_probe_residual_batched")
+    return out
+
+
 def subspace_correct(problems: list[SubspaceProblem], *, stats: bool = False, check: bool = True):
     """Batched subspace correction of int4 caches: one launch per pass for every problem.
 
@@ -160,12 +185,11 @@ def subspace_correct(problems: list[SubspaceProblem], *, stats: bool = False, ch
     for i, pb in enumerate(problems):
         if pb.basis is None and pb.probe_index.numel() >= 2:
             m, d = pb.probe_index.numel(), pb.base.d
-            need.setdefault((m, d, min(int(pb.rank), max(1, m - 1), d)), []).append(i)
+            need.setdefault((m, d, min(int(pb.rank), max(1, m - 1), d), pb.fresh.dtype), []).append(i)
     svd = {}
-    for (m, d, r), idx in need.items():
-        res = torch.empty(len(idx), m, d, dtype=torch.float32, device=dev)
-        for j, i in enumerate(idx):
-            probe_residual(problems[i].base, problems[i].fresh, problems[i].probe_index, out=res[j])
+    for (m, d, r, _), idx in need.items():
+        res = probe_residuals([problems[i].base for i in idx], [problems[i].fresh for i in idx],
+                              [problems[i].probe_index for i in idx])
         bases = dense_sub.topr_basis(res, r)
         for j, i in enumerate(idx):
             svd[i] = bases[j]

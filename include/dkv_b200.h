@@ -333,6 +333,20 @@ int dkv_kivi_probe_residual(const dkv_kivi_cache *base, const void *fresh, int32
                             int64_t fresh_row_stride, const int32_t *rows, int64_t n_rows, float *out,
                             int64_t out_row_stride, int32_t *status, dkv_stream_t stream);
 
+/* The same for many caches at once (all layers of an adapter view): job j reads jobs[j].base,
+   jobs[j].fresh and its own probe rows (n_rows each) and writes
+   out + j * out_job_stride (fp32 [n_rows, d], row stride out_row_stride).  All jobs share d
+   (a multiple of 32) and the fresh dtype; 16-byte aligned fresh rows and out. */
+typedef struct dkv_kivi_probe_job {
+  dkv_kivi_cache base;
+  const void *fresh;
+  int64_t fresh_row_stride; /* elements */
+  const int32_t *rows;
+} dkv_kivi_probe_job;
+int dkv_kivi_probe_residual_batched(const dkv_kivi_probe_job *jobs, int32_t n_jobs, int32_t fresh_dtype,
+                                    int64_t n_rows, float *out, int64_t out_job_stride, int64_t out_row_stride,
+                                    int32_t *status, dkv_stream_t stream);
+
 /* ---- subspace route -------------------------------------------------------- */
 
 /* ---- probe scoring and the residual gate ------------------------------------------ */

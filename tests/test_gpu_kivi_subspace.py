@@ -144,3 +144,28 @@ def test_kivi_subspace_no_probes_and_svd_basis(cuda):
                                                           out=K.KiviTensor.empty(400, cs["d"], "k", cuda))],
                                        stats=True)
     _check(cs, o, sub, mu, "svd")
+
+
+@pytest.mark.parametrize("fdt", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("d", [96, 1024])
+def test_kivi_probe_residuals_batched(cuda, fdt, d):
+    # one launch for several caches (both groupings, each job its own probe rows) equals the
+    # oracle's fresh[P] - dequant(base)[P] exactly (fp32 subtraction of the same values)
+    gen = torch.Generator().manual_seed(d + int(fdt == torch.float32))
+    bases, freshes, probes, want = [], [], [], []
+    n, m = 300, 37
+    for j, mode in enumerate(("k", "v", "k", "v", "v")):
+        x = torch.randn(n, d, generator=gen)
+        c, s, z = OK.quantize(x.numpy(), mode)
+        bases.append(K.KiviTensor(torch.from_numpy(c).to(cuda), torch.from_numpy(s).to(cuda),
+                                  torch.from_numpy(z).to(cuda), mode))
+        f = (x + 0.1 * torch.randn(n, d, generator=gen)).to(fdt)
+        freshes.append(f.to(cuda))
+        p = torch.randperm(n, generator=gen)[:m]
+        probes.append(p.to(cuda))
+        reused = OK.dequantize(c, s, z, mode)
+        want.append(f.float().numpy()[p.numpy()] - reused[p.numpy()])
+    got = K.probe_residuals(bases, freshes, probes).cpu().numpy()
+    for j in range(len(bases)):
+        np.testing.assert_array_equal(got[j], want[j])
+        np.testing.assert_array_equal(got[j], K.probe_residual(bases[j], freshes[j], probes[j]).cpu().numpy())

@@ -165,22 +165,13 @@ def probe_residuals(bases: list[KiviTensor], freshes: list[Tensor], probe_indice
     return out
 
 
-def subspace_correct(problems: list[SubspaceProblem], *, stats: bool = False, check: bool = True):
-    """Batched subspace correction of int4 caches: one launch per pass for every problem.
-
-    Returns, per problem, ``(out, subspace, orth_mu)`` (the last two ``[d]`` fp32, or None
-    unless ``stats``) — the int4 form of ``subspace_correct``'s ``(corrected, subspace,
-    orth_mu)``.
-    """
+def k_bases(problems: list[SubspaceProblem]) -> dict[int, Tensor]:
+    """The K path's bases: for every problem without a basis and with two or more probes, the
+    top-``rank`` right singular subspace of its probe residual (``svd_basis``,
+    src/deltakv/patches/subspace.py:37-42, 91-93), all problems of one shape in one batched
+    subspace iteration (:func:`deltakv_b200.subspace.topr_basis`).  Keyed by problem index."""
     from deltakv_b200 import subspace as dense_sub
 
-    if not problems:
-        return []
-    dev = problems[0].fresh.device
-    keep = []  # tensors that must stay alive until the launches are queued
-    descs = []
-    results = []
-    # bases from the probe residual (the K path): one batched subspace iteration per shape
     need = {}
     for i, pb in enumerate(problems):
         if pb.basis is None and pb.probe_index.numel() >= 2:
@@ -193,6 +184,24 @@ def subspace_correct(problems: list[SubspaceProblem], *, stats: bool = False, ch
         bases = dense_sub.topr_basis(res, r)
         for j, i in enumerate(idx):
             svd[i] = bases[j]
+    return svd
+
+
+def subspace_correct(problems: list[SubspaceProblem], *, stats: bool = False, check: bool = True,
+                     bases: dict[int, Tensor] | None = None):
+    """Batched subspace correction of int4 caches: one launch per pass for every problem.
+
+    Returns, per problem, ``(out, subspace, orth_mu)`` (the last two ``[d]`` fp32, or None
+    unless ``stats``) — the int4 form of ``subspace_correct``'s ``(corrected, subspace,
+    orth_mu)``.  ``bases`` (from :func:`k_bases`) skips computing the K bases here.
+    """
+    if not problems:
+        return []
+    dev = problems[0].fresh.device
+    keep = []  # tensors that must stay alive until the launches are queued
+    descs = []
+    results = []
+    svd = k_bases(problems) if bases is None else bases
     for i, pb in enumerate(problems):
         fresh = _rows(pb.fresh)
         ops._require_cuda(fresh, pb.probe_index)
@@ -228,3 +237,57 @@ def subspace_correct(problems: list[SubspaceProblem], *, stats: bool = False, ch
     if check:
         st.raise_if_set("kivi.subspace_correct")
     return results
+
+
+_side_streams: dict[str, torch.cuda.Stream] = {}
+
+
+def _side_stream(device: torch.device) -> torch.cuda.Stream:
+    key = str(device)
+    if key not in _side_streams:
+        # high priority: the bases' small latency-bound kernels are dispatched ahead of the
+        # route's queued CTAs instead of after them
+        lo, hi = torch.cuda.Stream.priority_range()
+        _side_streams[key] = torch.cuda.Stream(device=device, priority=hi)
+    return _side_streams[key]
+
+
+def subspace_correct_views(views: list[list[SubspaceProblem]], *, stats: bool = False, check: bool = True):
+    """:func:`subspace_correct` for several adapter views in turn (the reference's per-view
+    ``apply_probe_to_cache`` loop, src/deltakv/patches/probe.py:112-165), with the K bases of
+    view v + 1 computed on a side stream while view v's route runs: the bases' small solver
+    kernels fill the route's idle SM time.  A view that corrects a cache in place is finished
+    before the next view's bases read anything.  Returns one result list per view."""
+    views = [v for v in views]
+    if not views or not any(views):
+        return [[] for _ in views]
+    dev = next(v for v in views if v)[0].fresh.device
+    main = torch.cuda.current_stream(dev)
+    side = _side_stream(dev)
+
+    def launch_bases(v: int, after_main: bool):
+        if after_main:  # everything queued on main so far happens before these bases
+            side.wait_stream(main)
+        with torch.cuda.stream(side):
+            kb = k_bases(views[v]) if views[v] else {}
+        ev = torch.cuda.Event()
+        ev.record(side)
+        return kb, ev
+
+    def in_place(probs: list[SubspaceProblem]) -> bool:
+        return any(pb.out is None or pb.out.codes.data_ptr() == pb.base.codes.data_ptr() for pb in probs)
+
+    out = []
+    nxt = launch_bases(0, True)  # the inputs were produced on main
+    for v, probs in enumerate(views):
+        kb, ev = nxt
+        main.wait_event(ev)
+        for t in kb.values():
+            t.record_stream(main)
+        out.append(subspace_correct(probs, stats=stats, check=False, bases=kb) if probs else [])
+        if v + 1 < len(views):
+            nxt = launch_bases(v + 1, in_place(probs))
+    if check:
+        ops.status_word(dev).raise_if_set("kivi.subspace_correct_views")
+    return out
+

@@ -98,7 +98,11 @@ def _start_block(n_b: int, d: int, k: int, device: torch.device) -> tuple[Tensor
             _start_cache.clear()
         gen = torch.Generator(device=device).manual_seed(1234)
         hit = _orthonormalize(torch.randn(n_b, d, k, generator=gen, device=device))
+        torch.cuda.current_stream(device).synchronize()  # once per shape: usable from any stream
         _start_cache[key] = hit
+    cur = torch.cuda.current_stream(device)
+    for t in hit:
+        t.record_stream(cur)  # kept from reuse until this stream's work is done, if evicted
     return hit
 
 

@@ -169,3 +169,40 @@ def test_kivi_probe_residuals_batched(cuda, fdt, d):
     for j in range(len(bases)):
         np.testing.assert_array_equal(got[j], want[j])
         np.testing.assert_array_equal(got[j], K.probe_residual(bases[j], freshes[j], probes[j]).cpu().numpy())
+
+
+def test_kivi_subspace_views_pipelined_matches_sequential(cuda):
+    # three adapter views over one shared int4 prefix (K bases from the probe residual, V the
+    # adapter's B), the last correcting its own copy in place: the side-stream pipeline gives
+    # what view-by-view calls give (probe sums are atomics, so up to float summation order)
+    gen = torch.Generator().manual_seed(99)
+    n, n_kv, hd = 512, 2, 64
+    d = n_kv * hd
+    shared = {m: _case(gen, n, n_kv, hd, 8, m) for m in ("k", "v")}
+
+    def views():
+        out = []
+        for a in range(3):
+            g = torch.Generator().manual_seed(1000 + a)
+            probs = []
+            probes = torch.unique(torch.cat([torch.zeros(1, dtype=torch.long), torch.randperm(n, generator=g)[:40]]))
+            for m in ("k", "v"):
+                cs = shared[m]
+                base = _device_base(cs, cuda)
+                fresh = (cs["fresh"] + 0.05 * torch.randn(n, d, generator=g)).to(torch.bfloat16).to(cuda)
+                B = (torch.randn(d, 8, generator=g) / d ** 0.5).to(cuda)
+                dst = None if a == 2 else K.KiviTensor.empty(n, d, m, cuda)
+                probs.append(K.SubspaceProblem(base=base, fresh=fresh, probe_index=probes.to(cuda),
+                                               basis=None if m == "k" else B, rank=8, out=dst))
+            out.append(probs)
+        return out
+
+    seq = [[r[0] for r in K.subspace_correct(v)] for v in views()]
+    pip = [[r[0] for r in rs] for rs in K.subspace_correct_views(views())]
+    torch.cuda.synchronize()
+    for a in range(3):
+        for j in range(2):
+            x, y = seq[a][j], pip[a][j]
+            eq = (OK.unpack_nibbles(x.codes.cpu().numpy()) == OK.unpack_nibbles(y.codes.cpu().numpy())).mean()
+            assert eq >= 0.999, (a, j, eq)
+            torch.testing.assert_close(x.scale.float(), y.scale.float(), rtol=5e-3, atol=1e-6)

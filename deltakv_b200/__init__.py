@@ -5,7 +5,8 @@ deployment swaps them in (see :func:`install`):
 
 * ``scatter_into_paged`` / ``gather_from_paged``   (deltakv.paged)
 * ``exact_kv_patch`` / ``zeroth_order_patches``    (deltakv.patches.exact)
-* ``apply_layer_patches``                          (deltakv.patches.compose)
+* ``apply_layer_patches`` / ``measured_error``     (deltakv.patches.compose)
+* ``compare_kv``                                   (deltakv.metrics)
 * ``subspace_correct`` / ``svd_basis``             (deltakv.patches.subspace)
 * ``apply_probe_to_cache`` / ``select_probes`` / ``weight_axis_scores`` / ``residual_gate``
   (deltakv.patches.probe), ``lora_activation_scores`` (deltakv.patches.exact)
@@ -29,6 +30,7 @@ from deltakv_b200.exact import (
     materialize_codes,
     zeroth_order_patches,
 )
+from deltakv_b200.metrics import compare_kv, measured_error
 from deltakv_b200.ops import SeqBatchTensors, quantize_rows
 from deltakv_b200.probe import (
     apply_probe_to_cache,
@@ -57,12 +59,14 @@ __all__ = [
     "apply_layer_patches",
     "apply_layer_patches_",
     "apply_probe_to_cache",
+    "compare_kv",
     "exact_kv_patch",
     "gather_from_paged",
     "install",
     "kivi",
     "lora_activation_scores",
     "materialize_codes",
+    "measured_error",
     "quantize_rows",
     "replay",
     "residual_gate",
@@ -80,11 +84,13 @@ _INSTALL_MAP = {
     "deltakv.paged": {"scatter_into_paged": scatter_into_paged, "gather_from_paged": gather_from_paged},
     "deltakv.patches.exact": {"exact_kv_patch": exact_kv_patch, "zeroth_order_patches": zeroth_order_patches,
                               "lora_activation_scores": lora_activation_scores},
-    "deltakv.patches.compose": {"apply_layer_patches": apply_layer_patches},
+    "deltakv.patches.compose": {"apply_layer_patches": apply_layer_patches, "measured_error": measured_error},
+    "deltakv.metrics": {"compare_kv": compare_kv},
     # modules that imported the names with `from ... import`
     "deltakv.engine": {"zeroth_order_patches": zeroth_order_patches, "exact_kv_patch": exact_kv_patch,
                        "apply_layer_patches": apply_layer_patches, "apply_probe_to_cache": apply_probe_to_cache,
-                       "select_probes": select_probes, "weight_axis_scores": weight_axis_scores},
+                       "select_probes": select_probes, "weight_axis_scores": weight_axis_scores,
+                       "compare_kv": compare_kv, "measured_error": measured_error},
     "deltakv.connectors.vllm": {"scatter_into_paged": scatter_into_paged},
     "deltakv.patches.subspace": {"subspace_correct": subspace_correct, "svd_basis": svd_basis},
     "deltakv.patches.probe": {"subspace_correct": subspace_correct, "apply_probe_to_cache": apply_probe_to_cache,

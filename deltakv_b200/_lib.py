@@ -36,6 +36,7 @@ EXPORTED = (
     "dkv_scatter_paged",
     "dkv_gather_paged",
     "dkv_paged_error_sums",
+    "dkv_paged_compare_sums",
     "dkv_quantize_rows",
     "dkv_exact_packed_bytes",
     "dkv_pack_exact_factors",
@@ -272,6 +273,9 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_paged_error_sums.restype = C.c_int
     lib.dkv_paged_error_sums.argtypes = [C.POINTER(PagedCache), I32, P, I32, I64, I64, I64, C.POINTER(SeqBatch),
                                          P, P, P]
+    lib.dkv_paged_compare_sums.restype = C.c_int
+    lib.dkv_paged_compare_sums.argtypes = [C.POINTER(PagedCache), I32, P, I32, I64, I64, I64, C.POINTER(SeqBatch),
+                                           P, P, P]
     lib.dkv_quantize_rows.restype = C.c_int
     lib.dkv_quantize_rows.argtypes = [P, I32, I64, I64, I64, P, I32, I64, I64, P, P]
     lib.dkv_exact_packed_bytes.restype = C.c_int

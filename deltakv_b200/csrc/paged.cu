@@ -97,7 +97,8 @@ struct ErrLayers {
   const void *base[DKV_MAX_LAYERS];
 };
 
-template <int PDT, int FDT>
+// NS = 2: sum (p - f)^2, sum f^2 (measured_error); NS = 4: + sum p f, sum p^2 (compare_kv)
+template <int PDT, int FDT, int NS>
 __global__ void __launch_bounds__(kThreads) error_sums_kernel(dkv_paged_cache cache, ErrLayers layers,
                                                               const void *__restrict__ fresh, int64_t f_layer,
                                                               int64_t f_row, int64_t f_head,
@@ -105,7 +106,7 @@ __global__ void __launch_bounds__(kThreads) error_sums_kernel(dkv_paged_cache ca
                                                               int32_t *status) {
   using PT = typename Elem<PDT>::T;
   using FT = typename Elem<FDT>::T;
-  __shared__ float red[2][kThreads / 32];
+  __shared__ float red[NS][kThreads / 32];
   const int l = blockIdx.z, b = blockIdx.y;
   const int row0 = seqs.cu_seqlens[b];
   const int len = seqs.cu_seqlens[b + 1] - row0;
@@ -113,7 +114,9 @@ __global__ void __launch_bounds__(kThreads) error_sums_kernel(dkv_paged_cache ca
   const int row_elems = cache.n_heads * hd;
   const PT *pages = static_cast<const PT *>(layers.base[l]);
   const FT *fr = static_cast<const FT *>(fresh) + static_cast<int64_t>(l) * f_layer;
-  float s0 = 0.f, s1 = 0.f;
+  float s[NS];
+#pragma unroll
+  for (int k = 0; k < NS; ++k) s[k] = 0.f;
   for (int k = 0; k < 16; ++k) {
     const int i = blockIdx.x * 16 + k;
     if (i >= len) break;
@@ -125,29 +128,27 @@ __global__ void __launch_bounds__(kThreads) error_sums_kernel(dkv_paged_cache ca
       const float pv = Elem<PDT>::to_f(pages[off + h * cache.stride_head + j]);
       const float fv = Elem<FDT>::to_f(fr[frow + h * f_head + j]);
       const float dv = pv - fv;
-      s0 = fmaf(dv, dv, s0);
-      s1 = fmaf(fv, fv, s1);
+      s[0] = fmaf(dv, dv, s[0]);
+      s[1] = fmaf(fv, fv, s[1]);
+      if (NS == 4) {
+        s[NS - 2] = fmaf(pv, fv, s[NS - 2]);
+        s[NS - 1] = fmaf(pv, pv, s[NS - 1]);
+      }
     }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-  }
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int k = 0; k < NS; ++k) s[k] += __shfl_xor_sync(0xffffffffu, s[k], o);
   const int w = threadIdx.x >> 5;
-  if ((threadIdx.x & 31) == 0) {
-    red[0][w] = s0;
-    red[1][w] = s1;
-  }
+  if ((threadIdx.x & 31) == 0)
+#pragma unroll
+    for (int k = 0; k < NS; ++k) red[k][w] = s[k];
   __syncthreads();
-  if (threadIdx.x == 0) {
-    double a = 0.0, c = 0.0;
-    for (int i = 0; i < kThreads / 32; ++i) {
-      a += red[0][i];
-      c += red[1][i];
-    }
-    atomicAdd(sums + 2 * l, a);
-    atomicAdd(sums + 2 * l + 1, c);
+  if (threadIdx.x < NS) {
+    double a = 0.0;
+    for (int i = 0; i < kThreads / 32; ++i) a += red[threadIdx.x][i];
+    atomicAdd(sums + NS * l + threadIdx.x, a);
   }
 }
 
@@ -228,11 +229,11 @@ extern "C" int dkv_gather_paged(const dkv_paged_cache *cache, const dkv_seq_batc
   return DKV_ERR_UNSUPPORTED;
 }
 
-extern "C" int dkv_paged_error_sums(const dkv_paged_cache *pages, int32_t n_layers, const void *fresh,
-                                    int32_t fresh_dtype, int64_t fresh_layer_stride,
-                                    int64_t fresh_row_stride, int64_t fresh_head_stride,
-                                    const dkv_seq_batch *seqs, double *sums, int32_t *status,
-                                    dkv_stream_t stream) {
+namespace dkv {
+template <int NS>
+int error_sums(const dkv_paged_cache *pages, int32_t n_layers, const void *fresh, int32_t fresh_dtype,
+               int64_t fresh_layer_stride, int64_t fresh_row_stride, int64_t fresh_head_stride,
+               const dkv_seq_batch *seqs, double *sums, int32_t *status, dkv_stream_t stream) {
   if (pages == nullptr || n_layers <= 0 || n_layers > DKV_MAX_LAYERS) return DKV_ERR_INVALID_ARGUMENT;
   int rc = check_common(&pages[0], seqs);
   if (rc != DKV_OK) return rc;
@@ -246,13 +247,13 @@ extern "C" int dkv_paged_error_sums(const dkv_paged_cache *pages, int32_t n_laye
   }
   dim3 grid((seqs->max_seq_len + 15) / 16, seqs->n_seqs, n_layers);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-#define DKV_ERR_CASE(P, F)                                                                           \
-  if (pages[0].dtype == P && fresh_dtype == F) {                                                    \
-    error_sums_kernel<P, F><<<grid, kThreads, 0, st>>>(pages[0], layers, fresh, fresh_layer_stride, \
-                                                       fresh_row_stride, fresh_head_stride, *seqs,  \
-                                                       sums, status);                               \
-    DKV_CUDA_CHECK(cudaGetLastError());                                                             \
-    return DKV_OK;                                                                                  \
+#define DKV_ERR_CASE(P, F)                                                                             \
+  if (pages[0].dtype == P && fresh_dtype == F) {                                                      \
+    error_sums_kernel<P, F, NS><<<grid, kThreads, 0, st>>>(pages[0], layers, fresh, fresh_layer_stride, \
+                                                           fresh_row_stride, fresh_head_stride, *seqs,  \
+                                                           sums, status);                               \
+    DKV_CUDA_CHECK(cudaGetLastError());                                                               \
+    return DKV_OK;                                                                                    \
   }
   DKV_ERR_CASE(DKV_BF16, DKV_BF16)
   DKV_ERR_CASE(DKV_BF16, DKV_F32)
@@ -262,6 +263,25 @@ extern "C" int dkv_paged_error_sums(const dkv_paged_cache *pages, int32_t n_laye
   DKV_ERR_CASE(DKV_F32, DKV_BF16)
 #undef DKV_ERR_CASE
   return DKV_ERR_UNSUPPORTED;
+}
+}  // namespace dkv
+
+extern "C" int dkv_paged_error_sums(const dkv_paged_cache *pages, int32_t n_layers, const void *fresh,
+                                    int32_t fresh_dtype, int64_t fresh_layer_stride,
+                                    int64_t fresh_row_stride, int64_t fresh_head_stride,
+                                    const dkv_seq_batch *seqs, double *sums, int32_t *status,
+                                    dkv_stream_t stream) {
+  return dkv::error_sums<2>(pages, n_layers, fresh, fresh_dtype, fresh_layer_stride, fresh_row_stride,
+                            fresh_head_stride, seqs, sums, status, stream);
+}
+
+extern "C" int dkv_paged_compare_sums(const dkv_paged_cache *pages, int32_t n_layers, const void *fresh,
+                                      int32_t fresh_dtype, int64_t fresh_layer_stride,
+                                      int64_t fresh_row_stride, int64_t fresh_head_stride,
+                                      const dkv_seq_batch *seqs, double *sums, int32_t *status,
+                                      dkv_stream_t stream) {
+  return dkv::error_sums<4>(pages, n_layers, fresh, fresh_dtype, fresh_layer_stride, fresh_row_stride,
+                            fresh_head_stride, seqs, sums, status, stream);
 }
 
 extern "C" const char *dkv_status_string(int status) {

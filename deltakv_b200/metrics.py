@@ -1,7 +1,9 @@
-"""Per-layer measured error of a patch and its cross-rank gather.
+"""Per-layer measured error of a patch, the KV comparison report, and the cross-rank gather.
 
 ``measured_error`` follows src/deltakv/patches/compose.py:147-163: for each layer,
 ``(||K_p - K_f|| + ||V_p - V_f||) / (||K_f|| + ||V_f|| + 1e-8)`` and the maximum over layers.
+``compare_kv`` follows src/deltakv/metrics.py:60-81: per layer and projection the relative L2
+``||p - f|| / (||f|| + 1e-8)`` and the cosine, then their max / mean / min over layers.
 Here the sums run in one kernel launch per projection over every layer, reading the patched
 KV straight from its pages (no gather), and :func:`gather_layer_errors` is the path's only
 collective: each rank's per-layer scalars are all-gathered (NCCL over NVLink on GPUs, gloo on
@@ -32,7 +34,7 @@ class ErrorEstimate:
 
 
 def _error_sums(pages: Sequence[Tensor], fresh: Tensor, seqs: ops.SeqBatchTensors, sums: Tensor,
-                status: ops.StatusWord | None) -> None:
+                status: ops.StatusWord | None, fn: str = "dkv_paged_error_sums") -> None:
     n_layers = len(pages)
     if fresh.ndim != 4 or fresh.shape[0] != n_layers:
         raise ValueError("fresh must be [n_layers, rows, n_kv, head_dim] matching the page list")
@@ -43,10 +45,94 @@ def _error_sums(pages: Sequence[Tensor], fresh: Tensor, seqs: ops.SeqBatchTensor
     geo = lambda d: (d.dtype, d.block_size, d.n_heads, d.head_dim, d.stride_block, d.stride_slot, d.stride_head)
     if any(geo(d) != geo(descs[0]) for d in descs):
         raise ValueError("every layer's pages must share dtype, shape and strides")
-    rc = L.lib().dkv_paged_error_sums(descs, n_layers, fresh.data_ptr(), ops.dkv_dtype(fresh.dtype), fresh.stride(0),
-                                      fresh.stride(1), fresh.stride(2), C.byref(seqs.struct()), sums.data_ptr(),
-                                      status.ptr if status else None, ops.stream_ptr())
-    L.check(rc, "dkv_paged_error_sums")
+    rc = getattr(L.lib(), fn)(descs, n_layers, fresh.data_ptr(), ops.dkv_dtype(fresh.dtype), fresh.stride(0),
+                              fresh.stride(1), fresh.stride(2), C.byref(seqs.struct()), sums.data_ptr(),
+                              status.ptr if status else None, ops.stream_ptr())
+    L.check(rc, fn)
+
+
+@dataclass
+class LayerKVError:
+    """Field names of the reference's LayerKVError (src/deltakv/metrics.py:14-20)."""
+
+    layer: int
+    relative_l2_k: float
+    relative_l2_v: float
+    cosine_k: float
+    cosine_v: float
+
+
+@dataclass
+class CompareReport:
+    """Field names of the reference's CompareReport (src/deltakv/metrics.py:23-48)."""
+
+    layers: list[LayerKVError]
+    max_relative_l2: float
+    mean_relative_l2: float
+    min_cosine: float
+    next_token_kl: float | None = None
+    logprob_mae: float | None = None
+    logprob_max: float | None = None
+    logit_l2: float | None = None
+    kivi4_floor: float | None = None
+    within_kivi4: bool | None = None
+
+    def as_dict(self) -> dict[str, float | bool | None]:
+        return {
+            "max_relative_l2": self.max_relative_l2,
+            "mean_relative_l2": self.mean_relative_l2,
+            "min_cosine": self.min_cosine,
+            "next_token_kl": self.next_token_kl,
+            "logprob_mae": self.logprob_mae,
+            "logprob_max": self.logprob_max,
+            "logit_l2": self.logit_l2,
+            "kivi4_floor": self.kivi4_floor,
+            "within_kivi4": self.within_kivi4,
+        }
+
+
+def _compare_sums(pages: Sequence[Tensor], fresh: Tensor, seqs: ops.SeqBatchTensors, sums: Tensor,
+                  status: ops.StatusWord | None) -> None:
+    _error_sums(pages, fresh, seqs, sums, status, fn="dkv_paged_compare_sums")
+
+
+def compare_kv_paged(k_pages: Sequence[Tensor], v_pages: Sequence[Tensor], k_fresh: Tensor, v_fresh: Tensor,
+                     seqs: ops.SeqBatchTensors, *, check: bool = False) -> Tensor:
+    """Per-layer ``[n_layers, 4]`` (fp64, on the device): relative L2 of K, of V, cosine of K,
+    of V — paged K/V against dense fresh K/V ``[n_layers, rows, n_kv, head_dim]``."""
+    dev = k_fresh.device
+    n_layers = len(k_pages)
+    if len(v_pages) != n_layers:
+        raise ValueError("k_pages and v_pages must cover the same layers")
+    sums = torch.zeros(2, n_layers, 4, dtype=torch.float64, device=dev)
+    st = ops.status_word(dev)
+    _compare_sums(k_pages, k_fresh, seqs, sums[0], st)
+    _compare_sums(v_pages, v_fresh, seqs, sums[1], st)
+    if check:
+        st.raise_if_set("compare_kv_paged")
+    rel = sums[:, :, 0].sqrt() / (sums[:, :, 1].sqrt() + 1e-8)
+    cos = sums[:, :, 2] / (sums[:, :, 3] * sums[:, :, 1]).clamp_min(1e-16).sqrt()
+    return torch.stack([rel[0], rel[1], cos[0], cos[1]], dim=1)
+
+
+def compare_kv(patched, fresh) -> CompareReport:
+    """Drop-in for ``deltakv.metrics.compare_kv`` on dense CUDA KV caches (``.k`` / ``.v`` of
+    shape ``[n_layers, seq, n_kv, head_dim]``): one kernel launch per projection."""
+    pk, pv, fk, fv = patched.k, patched.v, fresh.k, fresh.v
+    n_layers, seq = pk.shape[0], pk.shape[1]
+    if seq == 0:
+        rows = [[0.0, 0.0, 0.0, 0.0] for _ in range(n_layers)]
+    else:
+        seqs = ops.SeqBatchTensors.single(seq, [0], pk.device)
+        kp = [pk[l].unsqueeze(0) for l in range(n_layers)]
+        vp = [pv[l].unsqueeze(0) for l in range(n_layers)]
+        rows = compare_kv_paged(kp, vp, fk, fv, seqs, check=True).tolist()
+    layers = [LayerKVError(layer=l, relative_l2_k=r[0], relative_l2_v=r[1], cosine_k=r[2], cosine_v=r[3])
+              for l, r in enumerate(rows)]
+    rels = [max(x.relative_l2_k, x.relative_l2_v) for x in layers]
+    cos = [min(x.cosine_k, x.cosine_v) for x in layers]
+    return CompareReport(layers=layers, max_relative_l2=max(rels) if rels else 0.0,
+                         mean_relative_l2=float(sum(rels) / max(len(rels), 1)), min_cosine=min(cos) if cos else 1.0)
 
 
 def measured_error_paged(k_pages: Sequence[Tensor], v_pages: Sequence[Tensor], k_fresh: Tensor, v_fresh: Tensor,

@@ -134,6 +134,15 @@ int dkv_paged_error_sums(const dkv_paged_cache *pages, int32_t n_layers, const v
                          int64_t fresh_head_stride, const dkv_seq_batch *seqs, double *sums,
                          int32_t *status, dkv_stream_t stream);
 
+/* The same walk with four sums per layer for compare_kv (metrics.py:60-81):
+   sums[4l] += sum (page - fresh)^2, sums[4l+1] += sum fresh^2, sums[4l+2] += sum page*fresh,
+   sums[4l+3] += sum page^2 — relative L2 = sqrt(s0) / (sqrt(s1) + 1e-8) and cosine =
+   s2 / max(sqrt(s3) sqrt(s1), 1e-8).  The caller zeroes sums. */
+int dkv_paged_compare_sums(const dkv_paged_cache *pages, int32_t n_layers, const void *fresh,
+                           int32_t fresh_dtype, int64_t fresh_layer_stride, int64_t fresh_row_stride,
+                           int64_t fresh_head_stride, const dkv_seq_batch *seqs, double *sums,
+                           int32_t *status, dkv_stream_t stream);
+
 /*
  * Stored-activation writer.  The reference keeps HiddenSnapshot.h in the model dtype
  * (model.py:157-164; config.py:31 names float16 storage but nothing applies it).  This

@@ -35,6 +35,7 @@ Cases:
   replay.npz       the engine's replay loop (engine.py:205-210): base KV plus a two-stage chain
                    of apply_layer_patches (codes @ basis patches, then dense patches).
   errors.npz       patches.compose.measured_error of a patched vs a fresh KVCache (per layer).
+  compare.npz      metrics.compare_kv of the same pair (per-layer relative L2 and cosine).
   kivi.npz         metrics._minmax_quantize (4 bits, group 32) on the last dimension (the
                    per-token V grouping) and on the transposed tensor (per-channel K
                    grouping), plus kivi_noise_floor on a small KVCache.
@@ -379,6 +380,16 @@ def main(ref_src: str) -> None:
     est = measured_error(RefKV(k=pk, v=pv, version=WeightVersion(id="p")), RefKV(k=fk, v=fv, version=WeightVersion(id="f")))
     np.savez_compressed(OUT / "errors.npz", pk=pk.numpy(), pv=pv.numpy(), fk=fk.numpy(), fv=fv.numpy(),
                         per_layer=np.array(est.per_layer, np.float64), rel=np.float64(est.relative_kv_l2))
+
+    # ---------------------------------------------------------------- compare
+    from deltakv.metrics import compare_kv
+
+    rep = compare_kv(RefKV(k=pk, v=pv, version=WeightVersion(id="p")), RefKV(k=fk, v=fv, version=WeightVersion(id="f")))
+    np.savez_compressed(
+        OUT / "compare.npz", pk=pk.numpy(), pv=pv.numpy(), fk=fk.numpy(), fv=fv.numpy(),
+        per_layer=np.array([[x.relative_l2_k, x.relative_l2_v, x.cosine_k, x.cosine_v] for x in rep.layers], np.float64),
+        max_rel=np.float64(rep.max_relative_l2), mean_rel=np.float64(rep.mean_relative_l2),
+        min_cos=np.float64(rep.min_cosine))
 
     # ------------------------------------------------------------------ probe
     from deltakv.patches.probe import apply_probe_to_cache, residual_gate, select_probes, weight_axis_scores

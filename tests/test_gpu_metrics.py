@@ -1,4 +1,5 @@
-"""Per-layer measured error on the GPU vs the reference's golden values and the oracle."""
+"""Per-layer measured error and compare_kv on the GPU vs the reference's golden values and the
+oracle (compare_kv within 1e-6 absolute: the reference computes its norms in fp32)."""
 
 from __future__ import annotations
 
@@ -20,6 +21,33 @@ def test_measured_error_golden(cuda):
     est = metrics.measured_error(KVCache(k=t(g["pk"]), v=t(g["pv"])), KVCache(k=t(g["fk"]), v=t(g["fv"])))
     assert np.allclose(est.per_layer, g["per_layer"], rtol=1e-5, atol=1e-9)
     assert abs(est.relative_kv_l2 - float(g["rel"])) <= 1e-5 * float(g["rel"])
+
+
+def test_compare_kv_golden(cuda):
+    g = golden("compare")
+    t = lambda a: torch.from_numpy(a).to(cuda)
+    rep = metrics.compare_kv(KVCache(k=t(g["pk"]), v=t(g["pv"])), KVCache(k=t(g["fk"]), v=t(g["fv"])))
+    got = np.array([[x.relative_l2_k, x.relative_l2_v, x.cosine_k, x.cosine_v] for x in rep.layers])
+    np.testing.assert_allclose(got, g["per_layer"], rtol=0, atol=1e-6)
+    assert abs(rep.max_relative_l2 - float(g["max_rel"])) <= 1e-6
+    assert abs(rep.mean_relative_l2 - float(g["mean_rel"])) <= 1e-6
+    assert abs(rep.min_cosine - float(g["min_cos"])) <= 1e-6
+    assert set(rep.as_dict()) >= {"max_relative_l2", "mean_relative_l2", "min_cosine", "next_token_kl"}
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_compare_kv_bf16_cache_matches_oracle(cuda, dtype):
+    from oracle.metrics import compare_kv as oracle_compare
+
+    gen = torch.Generator().manual_seed(21)
+    fk, fv = torch.randn(4, 300, 8, 128, generator=gen), torch.randn(4, 300, 8, 128, generator=gen)
+    pk = (fk + 0.02 * torch.randn(fk.shape, generator=gen)).to(dtype)
+    pv = (fv + 0.03 * torch.randn(fv.shape, generator=gen)).to(dtype)
+    rep = metrics.compare_kv(KVCache(k=pk.to(cuda), v=pv.to(cuda)), KVCache(k=fk.to(cuda), v=fv.to(cuda)))
+    rows, mx, mean, mn = oracle_compare(pk.float().numpy(), pv.float().numpy(), fk.numpy(), fv.numpy())
+    got = np.array([[x.relative_l2_k, x.relative_l2_v, x.cosine_k, x.cosine_v] for x in rep.layers])
+    np.testing.assert_allclose(got, rows, rtol=1e-5, atol=1e-7)
+    assert abs(rep.min_cosine - mn) <= 1e-7 and abs(rep.max_relative_l2 - mx) <= 1e-5 * mx
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])

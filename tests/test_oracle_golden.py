@@ -220,6 +220,18 @@ def test_measured_error_golden():
     assert abs(rel - float(g["rel"])) <= 1e-5 * float(g["rel"])
 
 
+def test_compare_kv_golden():
+    # the reference computes in fp32: its cosine of identical tensors is 0.99999976, so the
+    # fp64 restatement agrees to 1e-6
+    from oracle.metrics import compare_kv
+
+    g = golden("compare")
+    rows, mx, mean, mn = compare_kv(g["pk"], g["pv"], g["fk"], g["fv"])
+    np.testing.assert_allclose(rows, g["per_layer"], rtol=0, atol=1e-6)
+    assert abs(mx - float(g["max_rel"])) <= 1e-6 and abs(mean - float(g["mean_rel"])) <= 1e-6
+    assert abs(mn - float(g["min_cos"])) <= 1e-6
+
+
 def _replay_chain(g):
     chain = []
     for si in range(2):

@@ -980,8 +980,9 @@ def run_kivi_ours(args):
         import datetime
 
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    # adapter views are sharded over the ranks
-    per_rank = max(1, args.adapters // world)
+    # weak scaling: every rank maintains its own `--adapters` views (distinct adapters, the same
+    # rank mix {8, 8, 16, 16, 32, 32, 64, 64} on each GPU, so the ranks stay balanced)
+    per_rank = max(1, args.adapters)
     ids = [rank * per_rank + i for i in range(per_rank)]
     base, adapters = make_kivi_workload(args, dev, ids)
     units = args.layers * args.seq_len * per_rank

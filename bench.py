@@ -1060,7 +1060,9 @@ def run_kivi_ours(args):
                          "kernel_ms": route_ms, "algorithmic_bytes_per_unit": KIVI_BYTES_PER_UNIT},
             "cpu_baseline": cpu,
             "e2e": None,
-            "gpu_launches": args.steps * len(adapters) * 8,
+            # per view: flags, pack, pass1 K/V, psum, solve, fitb, pass2 K/V (9) + the K bases'
+            # batched probe residual and Jacobi eigensolver (2); library calls not counted
+            "gpu_launches": args.steps * len(adapters) * 11,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

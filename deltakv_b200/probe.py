@@ -120,6 +120,42 @@ def bases_for_layer(layer) -> tuple[Tensor | None, Tensor | None]:
     return (k_fac.B if k_fac is not None else None), (v_fac.B if v_fac is not None else None)
 
 
+def _k_bases(kv, fresh_layers: dict, probe_index: Tensor, layer_deltas: dict | None, subspace_rank: int,
+             skip_layers: set | None) -> dict[int, Tensor]:
+    """The K path's basis of every layer (``svd_basis`` of the probe residual at rank
+    ``B_k``'s width, subspace.py:91-93), all layers of one rank in one batched
+    :func:`~deltakv_b200.subspace.topr_basis` call.  Layers are independent, so the residuals
+    can be formed before any layer is corrected."""
+    from deltakv_b200.subspace import probe_residual, topr_basis
+
+    groups: dict[int, list[int]] = {}
+    idx = None
+    for l, (fk, _) in fresh_layers.items():
+        if skip_layers is not None and l in skip_layers:
+            continue
+        seq = int(kv.k[l].shape[0])
+        if idx is None:
+            idx = probe_index.to(device=fk.device, dtype=torch.int64).reshape(-1)
+            if idx.numel() < 2:
+                return {}
+            lo, hi = int(idx.min()), int(idx.max())
+            if lo < -seq or hi >= seq:
+                return {}  # subspace_correct raises the reference's IndexError for this layer
+            idx = torch.where(idx < 0, idx + seq, idx).to(torch.int32).contiguous()
+        k_b, _ = bases_for_layer(None if layer_deltas is None else layer_deltas.get(l))
+        k_rank = int(k_b.shape[1]) if k_b is not None else subspace_rank
+        d = int(kv.k[l][0].numel())
+        groups.setdefault(min(k_rank, max(1, idx.numel() - 1), d), []).append(l)
+    out: dict[int, Tensor] = {}
+    for r, ls in groups.items():
+        res = torch.stack([probe_residual(_rows2(kv.k[l]), _rows2(fresh_layers[l][0]).to(kv.k[l].dtype), idx)
+                           for l in ls])
+        bases = topr_basis(res, r)
+        for j, l in enumerate(ls):
+            out[l] = bases[j]
+    return out
+
+
 def apply_probe_to_cache(kv, fresh_layers: dict, probe_index: Tensor, blend_threshold: float = 0.15,
                          blend_max_ratio: float = 0.40, *, layer_deltas: dict | None = None, subspace_rank: int = 8,
                          probe_layers: set | None = None, skip_layers: set | None = None):
@@ -133,6 +169,7 @@ def apply_probe_to_cache(kv, fresh_layers: dict, probe_index: Tensor, blend_thre
     out = kv.clone() if hasattr(kv, "clone") else KVCache(kv.k.clone(), kv.v.clone(), kv.version)
     patches: dict[int, LowRankKVPatch] = {}
     extra_all: list[Tensor] = []
+    k_bases = _k_bases(out, fresh_layers, probe_index, layer_deltas, subspace_rank, skip_layers)
     for l, (fk, fv) in fresh_layers.items():
         if skip_layers is not None and l in skip_layers:
             continue
@@ -140,7 +177,7 @@ def apply_probe_to_cache(kv, fresh_layers: dict, probe_index: Tensor, blend_thre
         layer = None if layer_deltas is None else layer_deltas.get(l)
         k_b, v_b = bases_for_layer(layer)
         k_rank = int(k_b.shape[1]) if k_b is not None else subspace_rank
-        k_c, _, _ = subspace_correct(rk, fk, probe_index, basis=None, rank=k_rank)
+        k_c, _, _ = subspace_correct(rk, fk, probe_index, basis=k_bases.get(l), rank=k_rank)
         v_c, _, _ = subspace_correct(rv, fv, probe_index, basis=v_b, rank=subspace_rank)
         gated = probe_layers is None or l in probe_layers
         if gated:

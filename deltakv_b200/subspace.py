@@ -3,8 +3,9 @@
 Drop-in for ``deltakv.patches.subspace.subspace_correct`` (src/deltakv/patches/subspace.py:45-106)
 and ``svd_basis`` (37-42).  The per-token work (residual, least-squares codes onto col(B),
 fitted field, CacheBlend-style weights, probe override) runs in ``libdkv_b200.so``; the K
-path's basis — the top right singular vectors of the probe residual — is a library SVD
-(torch.linalg.svd on the device) of the gathered [n_probes, d] residual.
+path's basis — the top right singular subspace of the gathered [n_probes, d] probe residual —
+comes from :func:`topr_basis` (block subspace iteration with a device Rayleigh-Ritz step, the
+exact SVD where its convergence estimate is not met); :func:`svd_basis` is the library SVD.
 """
 
 from __future__ import annotations
@@ -203,7 +204,7 @@ def subspace_correct(reused: Tensor, fresh: Tensor, probe_index: Tensor, *, basi
     d = rf.shape[1]
     if basis is None:
         r_eff = min(rank, max(1, int(idx.numel()) - 1), d)
-        basis = svd_basis(probe_residual(rf, ff, idx), r_eff) if idx.numel() >= 2 else None
+        basis = topr_basis(probe_residual(rf, ff, idx), r_eff) if idx.numel() >= 2 else None
     structured = basis is not None and basis.numel() > 0 and idx.numel() >= 1
     if structured:
         if basis.shape[0] != d:

@@ -49,8 +49,6 @@ __device__ __forceinline__ uint64_t codes_to_f2(uint32_t w, int p) {
   return sub2(f2pack(__uint_as_float(lo), __uint_as_float(hi)), f2pack(8388608.f, 8388608.f));
 }
 
-// quant_one_fast for y = (x - z) / s already formed with the reciprocal: rint, the tie fallback,
-// saturating conversion (negative -> 0) and the clamp to 15
 // The reciprocal form alone: rint(y) clamped to [0, 15] for y = (x - z) * RN(1/s) (y = 0 when
 // s = 0).  Equal to the division form except where y lies within ~2 ulp of a rounding tie
 // (a few in a million codes); for outputs that are not held to bit equality with the

@@ -780,10 +780,6 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
     const int64_t c = static_cast<int64_t>(cb) * kCB + 8 * q;
     float acc[2][4][4];
 #pragma unroll
-    for (int m = 0; m < 2; ++m)
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt) acc[m][nt][0] = acc[m][nt][1] = acc[m][nt][2] = acc[m][nt][3] = 0.f;
-#pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
@@ -791,7 +787,12 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
         if constexpr (kStageB) bv = S.bq[kStageB ? ks * 4 + nt : 0][lane];
         else bv = b2[((static_cast<int64_t>(cb) * KS + ks) * 4 + nt) * 32];
 #pragma unroll
-        for (int m = 0; m < 2; ++m) mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], bv.x, bv.y);
+        for (int m = 0; m < 2; ++m) {
+          if (ks == 0)
+            mma16816_bf16_zc(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], bv.x, bv.y);
+          else
+            mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], bv.x, bv.y);
+        }
       }
     }
     uint64_t mu2[4];

@@ -7,6 +7,9 @@ deployment swaps them in (see :func:`install`):
 * ``exact_kv_patch`` / ``zeroth_order_patches``    (deltakv.patches.exact)
 * ``apply_layer_patches`` / ``measured_error``     (deltakv.patches.compose)
 * ``compare_kv``                                   (deltakv.metrics)
+* ``rmsnorm_first_order`` / ``attention_first_order`` / ``mlp_first_order`` /
+  ``rank_truncate`` / ``softmax_jacobian_product`` (deltakv.patches.analytic) and the engine's
+  analytic loop (``analytic.analytic_patches``)
 * ``subspace_correct`` / ``svd_basis``             (deltakv.patches.subspace)
 * ``apply_probe_to_cache`` / ``select_probes`` / ``weight_axis_scores`` / ``residual_gate``
   (deltakv.patches.probe), ``lora_activation_scores`` (deltakv.patches.exact)
@@ -18,7 +21,7 @@ All computation runs in ``libdkv_b200.so``; a missing library raises (no CPU pat
 
 from __future__ import annotations
 
-from deltakv_b200 import kivi
+from deltakv_b200 import analytic, kivi
 from deltakv_b200._lib import DkvError
 from deltakv_b200.dense import DensePatcher
 from deltakv_b200.exact import (
@@ -56,6 +59,7 @@ __all__ = [
     "LowRankKVPatch",
     "RotaryEmbedding",
     "SeqBatchTensors",
+    "analytic",
     "apply_layer_patches",
     "apply_layer_patches_",
     "apply_probe_to_cache",
@@ -86,11 +90,19 @@ _INSTALL_MAP = {
                               "lora_activation_scores": lora_activation_scores},
     "deltakv.patches.compose": {"apply_layer_patches": apply_layer_patches, "measured_error": measured_error},
     "deltakv.metrics": {"compare_kv": compare_kv},
+    "deltakv.patches.analytic": {"rmsnorm_first_order": analytic.rmsnorm_first_order,
+                                 "attention_first_order": analytic.attention_first_order,
+                                 "mlp_first_order": analytic.mlp_first_order,
+                                 "rank_truncate": analytic.rank_truncate,
+                                 "softmax_jacobian_product": analytic.softmax_jacobian_product},
     # modules that imported the names with `from ... import`
     "deltakv.engine": {"zeroth_order_patches": zeroth_order_patches, "exact_kv_patch": exact_kv_patch,
                        "apply_layer_patches": apply_layer_patches, "apply_probe_to_cache": apply_probe_to_cache,
                        "select_probes": select_probes, "weight_axis_scores": weight_axis_scores,
-                       "compare_kv": compare_kv, "measured_error": measured_error},
+                       "compare_kv": compare_kv, "measured_error": measured_error,
+                       "rmsnorm_first_order": analytic.rmsnorm_first_order,
+                       "attention_first_order": analytic.attention_first_order,
+                       "mlp_first_order": analytic.mlp_first_order, "rank_truncate": analytic.rank_truncate},
     "deltakv.connectors.vllm": {"scatter_into_paged": scatter_into_paged},
     "deltakv.patches.subspace": {"subspace_correct": subspace_correct, "svd_basis": svd_basis},
     "deltakv.patches.probe": {"subspace_correct": subspace_correct, "apply_probe_to_cache": apply_probe_to_cache,

@@ -54,6 +54,10 @@ EXPORTED = (
     "dkv_lora_scores",
     "dkv_row_diff_norms",
     "dkv_sym_eig_batched",
+    "dkv_attn_first_order",
+    "dkv_rmsnorm_first_order",
+    "dkv_swiglu_first_order",
+    "dkv_rope_rows",
     "dkv_subspace_workspace_bytes",
     "dkv_subspace_correct",
     "dkv_subspace_correct_noalloc",
@@ -310,6 +314,15 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_row_diff_norms.argtypes = [P, P, I32, I64, I64, I64, I64, P, I64, P, P, P]
     lib.dkv_sym_eig_batched.restype = C.c_int
     lib.dkv_sym_eig_batched.argtypes = [P, I64, I32, I64, I32, P, P, P, P]
+    lib.dkv_attn_first_order.restype = C.c_int
+    lib.dkv_attn_first_order.argtypes = [P, P, I64, P, P, P, P, I64, I32, I32, I32, I32, I32, C.c_float, P, P, I64,
+                                         P]
+    lib.dkv_rmsnorm_first_order.restype = C.c_int
+    lib.dkv_rmsnorm_first_order.argtypes = [P, P, P, C.c_float, I64, I32, I64, I64, P, P, I64, I64, P]
+    lib.dkv_swiglu_first_order.restype = C.c_int
+    lib.dkv_swiglu_first_order.argtypes = [P, P, P, P, I64, P, P, P]
+    lib.dkv_rope_rows.restype = C.c_int
+    lib.dkv_rope_rows.argtypes = [P, I64, I32, I32, I64, P, P, I64, P]
     lib.dkv_subspace_workspace_bytes.restype = C.c_int
     lib.dkv_subspace_workspace_bytes.argtypes = [I64, I64, I32, C.POINTER(C.c_int64)]
     lib.dkv_subspace_correct.restype = C.c_int

@@ -1,0 +1,223 @@
+"""Analytic route (Route A): first-order propagation of the hidden-state change through the
+stack, emitting per-layer dense ΔK / ΔV.
+
+Drop-ins for src/deltakv/patches/analytic.py (same names, arguments and results) and for the
+engine's per-layer loop ``DeltaKVEngine._analytic_patches`` (src/deltakv/engine.py:377-432):
+
+* ``rmsnorm_first_order`` (analytic.py:245-262) — ``dkv_rmsnorm_first_order``, one warp per row;
+* ``attention_first_order`` (analytic.py:38-95) — the q/k/v/o projections and the LoRA terms
+  are plain library GEMMs; RoPE is ``dkv_rope_rows``; the O(n^2) core (scores, softmax, its
+  Jacobian against dS, the two context products) is ``dkv_attn_first_order``, which never
+  materialises the [H, n, n] matrices, so the ``attn_probs`` the reference returns as its
+  fourth value (unused by its engine) is ``None`` unless ``return_attn=True`` asks for it;
+* ``mlp_first_order`` (analytic.py:108-138) — gate/up/down GEMMs and ``dkv_swiglu_first_order``;
+* ``rank_truncate`` (analytic.py:14-22) — the best rank-r approximation from the top-r right
+  singular subspace (:func:`deltakv_b200.subspace.topr_basis`, exact SVD where its estimate
+  is not converged); ``codes @ basis.T`` equals the reference's, the factors themselves may
+  differ by a rotation within the subspace;
+* ``analytic_patches`` — the engine loop, with ``model`` / ``config`` objects shaped like the
+  reference's (``cfg``, ``blocks``, ``rope``; ``hidden_stride``, ``propagator_rank``).
+
+All arithmetic is fp32 (the reference's model dtype for its toy), on the device.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from deltakv_b200 import _lib as L
+from deltakv_b200 import ops
+from deltakv_b200.rope import half_tables, max_positions
+from deltakv_b200.types import LowRankKVPatch
+
+
+def _f32(t: Tensor) -> Tensor:
+    t = t.float()
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def rmsnorm_first_order(x: Tensor, dx: Tensor, weight: Tensor, eps: float) -> tuple[Tensor, Tensor]:
+    """RMSNorm(x) and its first-order image under Δx (rows of ``[..., d]``)."""
+    ops._require_cuda(x, dx)
+    shape = x.shape
+    d = int(shape[-1])
+    x2, dx2 = _f32(x).reshape(-1, d), _f32(dx).reshape(-1, d)
+    w = _f32(weight.to(x2.device))
+    y, dy = torch.empty_like(x2), torch.empty_like(x2)
+    rc = L.lib().dkv_rmsnorm_first_order(x2.data_ptr(), dx2.data_ptr(), w.data_ptr(), float(eps), x2.shape[0], d,
+                                         x2.stride(0), dx2.stride(0), y.data_ptr(), dy.data_ptr(), y.stride(0),
+                                         dy.stride(0), ops.stream_ptr())
+    L.check(rc, "dkv_rmsnorm_first_order")
+    return y.view(shape), dy.view(shape)
+
+
+def softmax_jacobian_product(attn: Tensor, d_scores: Tensor) -> Tensor:
+    """``ΔA = J_softmax(A)[ΔS]`` row-wise: ``a ⊙ (δ − ⟨a, δ⟩)`` for materialised matrices (the
+    fused attention core applies it without forming them)."""
+    centered = d_scores - (attn * d_scores).sum(dim=-1, keepdim=True)
+    return attn * centered
+
+
+def silu(x: Tensor) -> Tensor:
+    return x * torch.sigmoid(x)
+
+
+def silu_grad(x: Tensor) -> Tensor:
+    s = torch.sigmoid(x)
+    return s + x * s * (1.0 - s)
+
+
+def _apply(fac, x: Tensor) -> Tensor:
+    """``LowRankFactors.apply``: ``(scale * x A^T) B^T`` (factors.py:61-67)."""
+    a = fac.A.to(device=x.device, dtype=torch.float32)
+    b = fac.B.to(device=x.device, dtype=torch.float32)
+    return (float(getattr(fac, "scale", 1.0)) * (x @ a.t())) @ b.t()
+
+
+def _rope_(x: Tensor, rope) -> None:
+    """In-place RoPE at positions 0..n-1 of a contiguous fp32 ``[n, heads, head_dim]``."""
+    n, heads, hd = x.shape
+    if n == 0:
+        return
+    cos, sin = half_tables(rope, x.device)
+    rc = L.lib().dkv_rope_rows(x.data_ptr(), n, heads, hd, x.stride(0), cos.data_ptr(), sin.data_ptr(),
+                               min(max_positions(rope), cos.shape[0]), ops.stream_ptr())
+    L.check(rc, "dkv_rope_rows")
+
+
+def attention_core(q: Tensor, dq: Tensor, k: Tensor, dk: Tensor, v: Tensor, dv: Tensor, *,
+                   want_ctx: bool) -> tuple[Tensor | None, Tensor]:
+    """``(ctx, dctx)`` ``[n, H, hd]`` fp32 of the causal first-order attention (see module)."""
+    n, H, hd = q.shape
+    Hkv = k.shape[1]
+    tensors = [q, dq, k, dk, v, dv]
+    dt = q.dtype if all(t.dtype == q.dtype for t in tensors) else torch.float32
+    q, dq, k, dk, v, dv = [t.to(dt).contiguous() for t in tensors]
+    dctx = torch.empty(n, H, hd, dtype=torch.float32, device=q.device)
+    ctx = torch.empty_like(dctx) if want_ctx else None
+    rc = L.lib().dkv_attn_first_order(q.data_ptr(), dq.data_ptr(), H * hd, k.data_ptr(), dk.data_ptr(), v.data_ptr(),
+                                      dv.data_ptr(), Hkv * hd, ops.dkv_dtype(dt), n, H, Hkv, hd, float(hd) ** -0.5,
+                                      ops.ptr(ctx), dctx.data_ptr(), H * hd, ops.stream_ptr())
+    L.check(rc, "dkv_attn_first_order")
+    return ctx, dctx
+
+
+def attention_first_order(x: Tensor, dx: Tensor, q_w: Tensor, k_w: Tensor, v_w: Tensor, o_w: Tensor, layer, *,
+                          n_heads: int, n_kv_heads: int, head_dim: int, rope, causal_mask: Tensor | None = None,
+                          base_weights: bool = False, return_attn: bool = False):
+    """``(Δh_attn, ΔK, ΔV, attn_probs)`` for one block (analytic.py:38-95).  ``causal_mask``
+    is accepted for signature compatibility; the core applies the causal mask itself."""
+    ops._require_cuda(x, dx)
+    n = int(x.shape[0])
+    xf, dxf = _f32(x), _f32(dx)
+    dev = xf.device
+    w_qkv = torch.cat([_f32(w.to(dev)) for w in (q_w, k_w, v_w)], dim=0)
+    dq_o, dk_o = n_heads * head_dim, n_kv_heads * head_dim
+    both = torch.cat([xf, dxf], dim=0) @ w_qkv.t()  # one GEMM for the base and the first-order terms
+    base, delta = both[:n], both[n:]
+    q = base[:, :dq_o].reshape(n, n_heads, head_dim).contiguous()
+    k = base[:, dq_o:dq_o + dk_o].reshape(n, n_kv_heads, head_dim).contiguous()
+    v = base[:, dq_o + dk_o:].reshape(n, n_kv_heads, head_dim).contiguous()
+    dq = delta[:, :dq_o].reshape(n, n_heads, head_dim).contiguous()
+    dk = delta[:, dq_o:dq_o + dk_o].reshape(n, n_kv_heads, head_dim).contiguous()
+    dv = delta[:, dq_o + dk_o:].reshape(n, n_kv_heads, head_dim).contiguous()
+    if layer is not None:
+        for t, name, heads in ((dq, "q_proj", n_heads), (dk, "k_proj", n_kv_heads), (dv, "v_proj", n_kv_heads)):
+            fac = layer.get(name)
+            if fac is None:
+                continue
+            t += _apply(fac, xf).view(n, heads, head_dim)
+            if base_weights:
+                t += _apply(fac, dxf).view(n, heads, head_dim)
+    for t in (q, k, dq, dk):
+        _rope_(t, rope)
+    o_fac = layer.get("o_proj") if layer is not None else None
+    ctx, dctx = attention_core(q, dq, k, dk, v, dv, want_ctx=o_fac is not None or return_attn)
+    dh = dctx.reshape(n, -1) @ _f32(o_w.to(dev)).t()
+    if o_fac is not None:
+        dh = dh + _apply(o_fac, ctx.reshape(n, -1))
+    attn = None
+    if return_attn:
+        rep = n_heads // n_kv_heads
+        kf = k.repeat_interleave(rep, dim=1)
+        scores = torch.einsum("qhd,khd->hqk", q, kf) * head_dim ** -0.5
+        mask = torch.triu(torch.full((n, n), float("-inf"), device=dev), diagonal=1)
+        attn = torch.softmax(scores + mask, dim=-1)
+    return dh, dk, dv, attn
+
+
+def mlp_first_order(x: Tensor, dx: Tensor, gate_w: Tensor, up_w: Tensor, down_w: Tensor, layer,
+                    base_weights: bool = False) -> Tensor:
+    """First-order SwiGLU block (analytic.py:108-138)."""
+    ops._require_cuda(x, dx)
+    n = int(x.shape[0])
+    xf, dxf = _f32(x), _f32(dx)
+    dev = xf.device
+    gw, uw = _f32(gate_w.to(dev)), _f32(up_w.to(dev))
+    ff = gw.shape[0]
+    both = torch.cat([xf, dxf], dim=0) @ torch.cat([gw, uw], dim=0).t()
+    g, u = both[:n, :ff].contiguous(), both[:n, ff:].contiguous()
+    dg, du = both[n:, :ff].contiguous(), both[n:, ff:].contiguous()
+    if layer is not None:
+        for t, name in ((dg, "gate_proj"), (du, "up_proj")):
+            fac = layer.get(name)
+            if fac is None:
+                continue
+            t += _apply(fac, xf)
+            if base_weights:
+                t += _apply(fac, dxf)
+    h, dh = torch.empty_like(g), torch.empty_like(g)
+    rc = L.lib().dkv_swiglu_first_order(g.data_ptr(), u.data_ptr(), dg.data_ptr(), du.data_ptr(), g.numel(),
+                                        h.data_ptr(), dh.data_ptr(), ops.stream_ptr())
+    L.check(rc, "dkv_swiglu_first_order")
+    y = dh @ _f32(down_w.to(dev)).t()
+    if layer is not None and layer.get("down_proj") is not None:
+        y = y + _apply(layer.get("down_proj"), h)
+    return y
+
+
+def rank_truncate(delta: Tensor, rank: int) -> tuple[Tensor, Tensor]:
+    """Δ ≈ codes @ basis.T with ``codes [n, r]``, ``basis [d, r]`` (the best rank-r
+    approximation, analytic.py:14-22)."""
+    from deltakv_b200.subspace import topr_basis
+
+    ops._require_cuda(delta)
+    flat = delta.reshape(delta.shape[0], -1).float()
+    r = max(1, min(int(rank), *flat.shape))
+    basis = topr_basis(flat, r)
+    codes = flat @ basis
+    return codes.to(delta.dtype), basis.to(delta.dtype)
+
+
+def analytic_patches(hidden, delta, model, config) -> dict[int, LowRankKVPatch]:
+    """The engine's analytic route (engine.py:377-432): per layer RMSNorm, first-order
+    attention (the dense ΔK / ΔV patch), the residual update, first-order SwiGLU on the
+    stored post-attention residual, and the rank-``propagator_rank`` truncation of ΔX;
+    ΔX restarts from zero every ``hidden_stride`` layers."""
+    cfg = model.cfg
+    seq = int(hidden.seq_len)
+    x0 = hidden.layer_in(0)
+    ops._require_cuda(x0)
+    dx = torch.zeros(seq, cfg.d_model, dtype=torch.float32, device=x0.device)
+    patches: dict[int, LowRankKVPatch] = {}
+    stride = max(1, int(config.hidden_stride))
+    prop_r = max(1, min(int(config.propagator_rank), cfg.d_model, seq))
+    for l, block in enumerate(model.blocks):
+        if l > 0 and l % stride == 0:
+            dx = torch.zeros_like(dx)
+        x = hidden.layer_in(l)
+        xn, dxn = rmsnorm_first_order(x, dx, block.attn_norm.weight, cfg.rms_eps)
+        layer = delta.layers.get(l)
+        dh, dk, dv, _ = attention_first_order(
+            xn, dxn, block.q_proj.weight, block.k_proj.weight, block.v_proj.weight, block.o_proj.weight, layer,
+            n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads, head_dim=cfg.head_dim, rope=model.rope)
+        patches[l] = LowRankKVPatch(layer_idx=l, k_codes=None, k_basis=None, v_codes=None, v_basis=None,
+                                    k_dense=dk, v_dense=dv)
+        dx = dx + dh
+        xm, dxm = rmsnorm_first_order(hidden.layer_mid(l), dx, block.mlp_norm.weight, cfg.rms_eps)
+        dx = dx + mlp_first_order(xm, dxm, block.gate_proj.weight, block.up_proj.weight, block.down_proj.weight,
+                                  layer)
+        codes, basis = rank_truncate(dx, prop_r)
+        dx = codes @ basis.t()
+    return patches

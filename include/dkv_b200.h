@@ -373,6 +373,34 @@ int dkv_row_diff_norms(const void *a, const void *b, int32_t dtype, int64_t n_ro
                        int64_t a_row_stride, int64_t b_row_stride, const int32_t *rows, int64_t n_out,
                        float *out, int32_t *status, dkv_stream_t stream);
 
+/*
+ * Analytic route (Route A, patches/analytic.py).  First-order causal attention without the
+ * [H, n, n] matrices (attention_first_order's core, analytic.py:85-99): for each query head h
+ * and its GQA kv head h / (n_heads / n_kv_heads), with S = q k^T * scale (causal),
+ * A = softmax(S), dS = (dq k^T + q dk^T) * scale, dA = A (.) (dS - rowsum(A (.) dS)):
+ *   dctx = dA v + A dv,  ctx = A v (ctx may be NULL).
+ * q, dq: [n, n_heads, head_dim] (row stride q_row_stride elements); k, dk, v, dv:
+ * [n, n_kv_heads, head_dim] (kv_row_stride); dtype F32, BF16 or F16 (fp32 arithmetic);
+ * outputs fp32 [n, n_heads, head_dim] with row stride out_row_stride; head_dim 16/32/64/128.
+ */
+int dkv_attn_first_order(const void *q, const void *dq, int64_t q_row_stride, const void *k, const void *dk,
+                         const void *v, const void *dv, int64_t kv_row_stride, int32_t dtype, int32_t n_tokens,
+                         int32_t n_heads, int32_t n_kv_heads, int32_t head_dim, float scale, float *ctx,
+                         float *dctx, int64_t out_row_stride, dkv_stream_t stream);
+/* y = RMSNorm(x) and its first-order image dy under dx (rmsnorm_first_order,
+   analytic.py:245-262); fp32 rows of d elements. */
+int dkv_rmsnorm_first_order(const float *x, const float *dx, const float *w, float eps, int64_t rows, int32_t d,
+                            int64_t x_row_stride, int64_t dx_row_stride, float *y, float *dy,
+                            int64_t y_row_stride, int64_t dy_row_stride, dkv_stream_t stream);
+/* h = silu(g) u, dh = silu'(g) dg u + silu(g) du, elementwise over n fp32 values
+   (mlp_first_order's SwiGLU, analytic.py:108-138). */
+int dkv_swiglu_first_order(const float *g, const float *u, const float *dg, const float *du, int64_t n, float *h,
+                           float *dh, dkv_stream_t stream);
+/* In place: x = x cos + rotate_half(x) sin at positions 0..rows-1 (rope.py:9-63) for fp32
+   x [rows, heads, head_dim] (row stride elements); cos/sin are half-width [table_rows, head_dim/2]. */
+int dkv_rope_rows(float *x, int64_t rows, int32_t heads, int32_t head_dim, int64_t row_stride,
+                  const float *cos_half, const float *sin_half, int64_t table_rows, dkv_stream_t stream);
+
 /* Eigendecomposition of `batch` symmetric k x k fp64 matrices (k <= 96; matrix b at
    a + b * a_stride, row-major, only its symmetric part is used) by parallel cyclic Jacobi:
    evals [batch, k] descending, evecs [batch, k, k] row-major with column j the unit

@@ -36,6 +36,10 @@ Cases:
                    of apply_layer_patches (codes @ basis patches, then dense patches).
   errors.npz       patches.compose.measured_error of a patched vs a fresh KVCache (per layer).
   compare.npz      metrics.compare_kv of the same pair (per-layer relative L2 and cosine).
+  analytic.npz     the analytic route on a GQA toy (4 layers, d=64, 4/2 heads, 48 tokens) with
+                   rank-4 LoRA on every projection of layers 0-2: the engine's per-layer loop
+                   (engine.py:377-432, hidden_stride 2, propagator_rank 8) and, on layer 1 with a
+                   seeded dx, rmsnorm_first_order, attention_first_order and mlp_first_order.
   kivi.npz         metrics._minmax_quantize (4 bits, group 32) on the last dimension (the
                    per-token V grouping) and on the transposed tensor (per-channel K
                    grouping), plus kivi_noise_floor on a small KVCache.
@@ -380,6 +384,67 @@ def main(ref_src: str) -> None:
     est = measured_error(RefKV(k=pk, v=pv, version=WeightVersion(id="p")), RefKV(k=fk, v=fv, version=WeightVersion(id="f")))
     np.savez_compressed(OUT / "errors.npz", pk=pk.numpy(), pv=pv.numpy(), fk=fk.numpy(), fv=fv.numpy(),
                         per_layer=np.array(est.per_layer, np.float64), rel=np.float64(est.relative_kv_l2))
+
+    # --------------------------------------------------------------- analytic
+    import types as _types
+
+    from deltakv.deltas.factors import random_lora_factors
+    from deltakv.engine import DeltaKVEngine
+    from deltakv.patches.analytic import attention_first_order, mlp_first_order, rmsnorm_first_order
+
+    torch.manual_seed(3)
+    acfg = ToyConfig(n_layers=4, d_model=64, n_heads=4, n_kv_heads=2, d_ff=128, vocab_size=256)
+    amodel = ToyTransformer(acfg)
+    ga = torch.Generator().manual_seed(5)
+    atok = torch.randint(0, 256, (48,), generator=ga)
+    with torch.no_grad():
+        _, _, ahidden = amodel.prefill(atok)
+    dkv_ = acfg.n_kv_heads * acfg.head_dim
+    dq_ = acfg.n_heads * acfg.head_dim
+    shapes = {"q": (acfg.d_model, dq_), "k": (acfg.d_model, dkv_), "v": (acfg.d_model, dkv_),
+              "o": (dq_, acfg.d_model), "gate": (acfg.d_model, acfg.d_ff), "up": (acfg.d_model, acfg.d_ff),
+              "down": (acfg.d_ff, acfg.d_model)}
+    alayers, fac_arrays = {}, {}
+    for li in (0, 1, 2):
+        kw = {}
+        for nm, (fin, fout) in shapes.items():
+            f = random_lora_factors(fin, fout, 4, scale=0.05, generator=ga, name=f"{nm}_proj")
+            kw[nm] = f
+            fac_arrays[f"lora_{li}_{nm}_A"] = f.A.numpy()
+            fac_arrays[f"lora_{li}_{nm}_B"] = f.B.numpy()
+            fac_arrays[f"lora_{li}_{nm}_scale"] = np.float32(f.scale)
+        alayers[li] = lora_layer(li, **kw)
+    adelta = lora_delta(source=WeightVersion(id="base"), target=WeightVersion(id="lora", parent_id="base", kind="lora"),
+                        layers=alayers)
+    fake = _types.SimpleNamespace(model=amodel, config=_types.SimpleNamespace(hidden_stride=2, propagator_rank=8))
+    with torch.no_grad():
+        apatches = DeltaKVEngine._analytic_patches(fake, ahidden, adelta)
+        # the module functions on layer 1 with a seeded dx
+        blk = amodel.blocks[1]
+        adx = 0.05 * torch.randn(48, acfg.d_model, generator=ga)
+        rn_y, rn_dy = rmsnorm_first_order(ahidden.h[1], adx, blk.attn_norm.weight, acfg.rms_eps)
+        causal = torch.triu(torch.full((1, 48, 48), float("-inf")), diagonal=1)
+        at_dh, at_dk, at_dv, _ = attention_first_order(
+            rn_y, rn_dy, blk.q_proj.weight, blk.k_proj.weight, blk.v_proj.weight, blk.o_proj.weight, alayers[1],
+            n_heads=acfg.n_heads, n_kv_heads=acfg.n_kv_heads, head_dim=acfg.head_dim, rope=amodel.rope,
+            causal_mask=causal)
+        mm_y, mm_dy = rmsnorm_first_order(ahidden.h_mid[1], adx, blk.mlp_norm.weight, acfg.rms_eps)
+        ml_out = mlp_first_order(mm_y, mm_dy, blk.gate_proj.weight, blk.up_proj.weight, blk.down_proj.weight,
+                                 alayers[1])
+    np.savez_compressed(
+        OUT / "analytic.npz",
+        n_layers=np.int32(acfg.n_layers), d_model=np.int32(acfg.d_model), n_heads=np.int32(acfg.n_heads),
+        n_kv=np.int32(acfg.n_kv_heads), hd=np.int32(acfg.head_dim), d_ff=np.int32(acfg.d_ff),
+        eps=np.float32(acfg.rms_eps), rope_base=np.float32(acfg.rope_base), rope_max=np.int32(amodel.rope.max_seq),
+        hidden_stride=np.int32(2), propagator_rank=np.int32(8),
+        h=np.stack([t.numpy() for t in ahidden.h]), h_mid=np.stack([t.numpy() for t in ahidden.h_mid]),
+        dk=np.stack([apatches[l].k_dense.numpy() for l in range(acfg.n_layers)]),
+        dv=np.stack([apatches[l].v_dense.numpy() for l in range(acfg.n_layers)]),
+        dx1=adx.numpy(), rn_y=rn_y.numpy(), rn_dy=rn_dy.numpy(), at_dh=at_dh.numpy(), at_dk=at_dk.numpy(),
+        at_dv=at_dv.numpy(), ml_out=ml_out.numpy(),
+        **fac_arrays,
+        **{f"w_{k.replace('.', '_')}": v.detach().numpy() for k, v in amodel.state_dict().items()},
+    )
 
     # ---------------------------------------------------------------- compare
     from deltakv.metrics import compare_kv

@@ -220,6 +220,24 @@ def test_measured_error_golden():
     assert abs(rel - float(g["rel"])) <= 1e-5 * float(g["rel"])
 
 
+def test_analytic_oracle_golden():
+    # the fp64 restatement of the analytic route against the reference's fp32 run
+    from oracle import analytic as OA
+    from tests._analytic_golden import load, rel
+
+    g, W, Ls, cfg = load()
+    for l, (dk, dv) in enumerate(OA.analytic_patches(g["h"], g["h_mid"], W, Ls, cfg)):
+        assert rel(dk, g["dk"][l]) < 1e-5 and rel(dv, g["dv"][l]) < 1e-5, l
+    cos, sin = OA.rope_tables(cfg["hd"], g["h"].shape[1], cfg["rope_base"])
+    y, dy = OA.rmsnorm_first_order(g["h"][1], g["dx1"], W[1]["attn_norm"], cfg["eps"])
+    assert rel(y, g["rn_y"]) < 1e-6 and rel(dy, g["rn_dy"]) < 1e-6
+    dh, dk, dv = OA.attention_first_order(g["rn_y"], g["rn_dy"], W[1]["q"], W[1]["k"], W[1]["v"], W[1]["o"], Ls[1],
+                                          cfg["n_heads"], cfg["n_kv"], cfg["hd"], cos, sin)
+    assert max(rel(dh, g["at_dh"]), rel(dk, g["at_dk"]), rel(dv, g["at_dv"])) < 1e-6
+    ym, dym = OA.rmsnorm_first_order(g["h_mid"][1], g["dx1"], W[1]["mlp_norm"], cfg["eps"])
+    assert rel(OA.mlp_first_order(ym, dym, W[1]["gate"], W[1]["up"], W[1]["down"], Ls[1]), g["ml_out"]) < 1e-6
+
+
 def test_compare_kv_golden():
     # the reference computes in fp32: its cosine of identical tensors is 0.99999976, so the
     # fp64 restatement agrees to 1e-6

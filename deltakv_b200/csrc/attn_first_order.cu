@@ -6,24 +6,21 @@
 //   ctx = A V,   dctx = dA V + A dV
 //
 // per query head h with its GQA key/value head h / (H / Hkv) (analytic.py:142-153), without
-// materialising the [H, n, n] matrices.  Two passes over the causal keys of each query row:
-// pass 1 forms the row statistics m = max S, l = sum exp(S - m), t = sum exp(S - m) dS
-// online; pass 2 recomputes S and dS and accumulates
-//   dctx = sum_k a_k (dS_k - t / l) v_k + a_k dv_k,   ctx = sum_k a_k v_k,   a_k = exp(S_k - m) / l.
-// fp32 arithmetic throughout (the reference runs the route in the model dtype, fp32 for the
-// toy).  Mapping: 64 query rows per CTA, a quad of 4 threads per row, each thread holding a
-// quarter of head_dim of Q, dQ and of the outputs; key blocks of 32 rows of K, dK, V, dV are
-// staged in shared memory; the quad reduces its partial dot products with two shuffles.
+// materialising the [H, n, n] matrices: one flash-style pass over the causal keys with an
+// online softmax, since dA V = (sum_k p_k dS_k v_k - (sum_k p_k dS_k / l) sum_k p_k v_k) / l
+// needs only per-row running sums.  fp32 arithmetic (the reference runs the route in the model
+// dtype, fp32 for its toy).  A CTA takes 64 query rows of one head with Q and dQ resident in
+// shared memory (transposed) and streams blocks of 32 keys of K, dK, V, dV; both the score
+// micro-GEMMs (4 x 2 per thread) and the output micro-GEMMs (4 rows x head_dim / 16 columns per
+// thread) read shared memory in 8- and 16-byte vectors.
 #include "dkv_common.cuh"
 
 namespace dkv {
 namespace afo {
 
-constexpr int kRows = 64;   // query rows per CTA
-constexpr int kKeys = 32;   // keys per staged block
-constexpr int kThreads = 4 * kRows;
-constexpr int kMaxHd = 128;
-constexpr int kMaxSlice = kMaxHd / 4;
+constexpr int kRows = 64;  // query rows per CTA
+constexpr int kKeys = 32;  // keys per staged block
+constexpr int kThreads = 256;
 
 template <int DT>
 __device__ __forceinline__ float ld(const void *p, int64_t i) {
@@ -41,138 +38,189 @@ struct Args {
   float scale;
 };
 
-template <int DT, int SL>  // SL: head_dim / 4 (values per thread)
-__global__ void __launch_bounds__(kThreads) afo_kernel(const Args a) {
-  extern __shared__ float sm[];
-  // staged key block: [4 tensors][kKeys][hd]
-  float *Ks = sm, *dKs = sm + kKeys * a.hd, *Vs = sm + 2 * kKeys * a.hd, *dVs = sm + 3 * kKeys * a.hd;
+// One pass over the causal keys with online softmax.  Thread (ty, tx) = (tid / 16, tid % 16)
+// owns query rows 4 ty .. 4 ty + 3: in the score phase keys 2 tx, 2 tx + 1 of the block (a
+// 4 x 2 micro-tile of S and dS), in the output phase head_dim columns tx + 16 j.  Per row the
+// 16 threads of a half-warp share the online statistics m (max), l (sum of p = exp(S - m)),
+// t (sum of p dS) and the three accumulators
+//   O = sum p v,  OS = sum p dS v,  OD = sum p dv
+// rescaled by exp(m_old - m_new) as m grows; at the end ctx = O / l and
+// dctx = (OS - (t / l) O) / l + OD / l.
+template <int DT, int HD>
+__global__ void __launch_bounds__(kThreads, 1) afo_kernel(const Args a) {
+  constexpr int CPT = HD / 16;  // output columns per thread
+  extern __shared__ __align__(16) float sm[];
+  float *Qt = sm;                       // [HD][kRows]  (q * scale)^T
+  float *dQt = Qt + HD * kRows;         // [HD][kRows]
+  float *Kt = dQt + HD * kRows;         // [HD][kKeys]
+  float *dKt = Kt + HD * kKeys;         // [HD][kKeys]
+  float *Vs = dKt + HD * kKeys;         // [kKeys][HD]
+  float *dVs = Vs + kKeys * HD;         // [kKeys][HD]
+  float *Pt = dVs + kKeys * HD;         // [kKeys][kRows]  p
+  float *PDt = Pt + kKeys * kRows;      // [kKeys][kRows]  p dS
+  const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
   const int h = blockIdx.y, hk = h / (a.n_heads / a.n_kv);
-  const int q0 = blockIdx.x * kRows;
-  const int r = threadIdx.x >> 2, part = threadIdx.x & 3;
-  const int row = q0 + r;
-  const bool valid = row < a.n;
-  const int d0 = part * SL;
-  float qv[SL], dqv[SL];
-#pragma unroll
-  for (int j = 0; j < SL; ++j) {
-    const int64_t o = static_cast<int64_t>(valid ? row : 0) * a.q_row + static_cast<int64_t>(h) * a.hd + d0 + j;
-    qv[j] = ld<DT>(a.q, o) * a.scale;  // the 1/sqrt(hd) of S and dS folded into Q and dQ
-    dqv[j] = ld<DT>(a.dq, o) * a.scale;
+  const int q0 = (gridDim.x - 1 - blockIdx.x) * kRows;  // the longest (latest) rows first
+  for (int e = tid; e < kRows * HD; e += kThreads) {
+    const int r = e / HD, d = e - r * HD;
+    const int row = q0 + r;
+    float x = 0.f, dx = 0.f;
+    if (row < a.n) {
+      const int64_t o = static_cast<int64_t>(row) * a.q_row + static_cast<int64_t>(h) * HD + d;
+      x = ld<DT>(a.q, o) * a.scale;  // the 1/sqrt(hd) of S and dS folded into Q and dQ
+      dx = ld<DT>(a.dq, o) * a.scale;
+    }
+    Qt[d * kRows + r] = x;
+    dQt[d * kRows + r] = dx;
   }
-  const int last_key = min(q0 + kRows, a.n);  // keys [0, last_key) reach some row of this CTA
+  float m[4], l[4], t[4], O[4][CPT], OS[4][CPT], OD[4][CPT];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY;
+    l[i] = t[i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < CPT; ++j) O[i][j] = OS[i][j] = OD[i][j] = 0.f;
+  }
+  const int last_key = min(q0 + kRows, a.n);
   const int n_blocks = (last_key + kKeys - 1) / kKeys;
-
-  auto stage = [&](int kb) {
-    const int k0 = kb * kKeys;
-    for (int e = threadIdx.x; e < kKeys * a.hd; e += kThreads) {
-      const int kk = e / a.hd, d = e - kk * a.hd;
-      const int key = k0 + kk;
-      const bool ok = key < a.n;
-      const int64_t o = static_cast<int64_t>(ok ? key : 0) * a.kv_row + static_cast<int64_t>(hk) * a.hd + d;
-      Ks[e] = ok ? ld<DT>(a.k, o) : 0.f;
-      dKs[e] = ok ? ld<DT>(a.dk, o) : 0.f;
-      Vs[e] = ok ? ld<DT>(a.v, o) : 0.f;
-      dVs[e] = ok ? ld<DT>(a.dv, o) : 0.f;
-    }
-  };
-  // s = q.k and ds = dq.k + q.dk for key kk of the staged block, summed over the quad
-  auto scores = [&](int kk, float &s, float &ds) {
-    const float *kr = Ks + kk * a.hd + d0, *dkr = dKs + kk * a.hd + d0;
-    float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-    for (int j = 0; j < SL; ++j) {
-      s0 = fmaf(qv[j], kr[j], s0);
-      s1 = fmaf(dqv[j], kr[j], s1);
-      s1 = fmaf(qv[j], dkr[j], s1);
-    }
-    s0 += __shfl_xor_sync(0xffffffffu, s0, 1);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, 1);
-    s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-    s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-    s = s0;
-    ds = s1;
-  };
-
-  // pass 1: row statistics
-  float m = -INFINITY, l = 0.f, t = 0.f;
   for (int kb = 0; kb < n_blocks; ++kb) {
-    __syncthreads();
-    stage(kb);
-    __syncthreads();
     const int k0 = kb * kKeys;
-    for (int kk = 0; kk < kKeys; ++kk) {
-      const int key = k0 + kk;
-      if (key >= last_key) break;  // uniform across the CTA
-      float s, ds;
-      scores(kk, s, ds);
-      if (!valid || key > row) continue;  // causal (the shuffles above ran on all lanes)
-      if (s > m) {
-        const float c = expf(m - s);
-        l *= c;
-        t *= c;
-        m = s;
+    __syncthreads();  // the previous block's tiles are consumed
+    for (int e = tid; e < kKeys * HD; e += kThreads) {
+      const int c = e / HD, d = e - c * HD;
+      const int key = k0 + c;
+      float kv = 0.f, dkv = 0.f, vv = 0.f, dvv = 0.f;
+      if (key < a.n) {
+        const int64_t o = static_cast<int64_t>(key) * a.kv_row + static_cast<int64_t>(hk) * HD + d;
+        kv = ld<DT>(a.k, o);
+        dkv = ld<DT>(a.dk, o);
+        vv = ld<DT>(a.v, o);
+        dvv = ld<DT>(a.dv, o);
       }
-      const float p = expf(s - m);
-      l += p;
-      t = fmaf(p, ds, t);
+      Kt[d * kKeys + c] = kv;
+      dKt[d * kKeys + c] = dkv;
+      Vs[e] = vv;
+      dVs[e] = dvv;
+    }
+    __syncthreads();
+    // scores: S and dS for rows 4 ty + i, keys 2 tx + c
+    float S[4][2], dS[4][2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) S[i][0] = S[i][1] = dS[i][0] = dS[i][1] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < HD; ++d) {
+      const float4 qv = *reinterpret_cast<const float4 *>(Qt + d * kRows + 4 * ty);
+      const float4 dqv = *reinterpret_cast<const float4 *>(dQt + d * kRows + 4 * ty);
+      const float2 kv = *reinterpret_cast<const float2 *>(Kt + d * kKeys + 2 * tx);
+      const float2 dkv = *reinterpret_cast<const float2 *>(dKt + d * kKeys + 2 * tx);
+      const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, dqa[4] = {dqv.x, dqv.y, dqv.z, dqv.w};
+      const float ka[2] = {kv.x, kv.y}, dka[2] = {dkv.x, dkv.y};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          S[i][c] = fmaf(qa[i], ka[c], S[i][c]);
+          dS[i][c] = fmaf(dqa[i], ka[c], dS[i][c]);
+          dS[i][c] = fmaf(qa[i], dka[c], dS[i][c]);
+        }
+    }
+    // online softmax over this block (causal: key <= row; keys past n are masked too)
+    float corr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = q0 + 4 * ty + i;
+      float bm = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int key = k0 + 2 * tx + c;
+        if (key > row || key >= a.n) S[i][c] = -INFINITY;
+        bm = fmaxf(bm, S[i][c]);
+      }
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+      const float mn = fmaxf(m[i], bm);
+      corr[i] = mn == -INFINITY ? 1.f : expf(m[i] - mn);
+      float ls = 0.f, ts = 0.f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const float p = S[i][c] == -INFINITY ? 0.f : expf(S[i][c] - mn);
+        const float pd = p * dS[i][c];
+        ls += p;
+        ts += pd;
+        Pt[(2 * tx + c) * kRows + 4 * ty + i] = p;
+        PDt[(2 * tx + c) * kRows + 4 * ty + i] = pd;
+      }
+#pragma unroll
+      for (int o = 1; o < 16; o <<= 1) {
+        ls += __shfl_xor_sync(0xffffffffu, ls, o);
+        ts += __shfl_xor_sync(0xffffffffu, ts, o);
+      }
+      m[i] = mn;
+      l[i] = fmaf(l[i], corr[i], ls);
+      t[i] = fmaf(t[i], corr[i], ts);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        O[i][j] *= corr[i];
+        OS[i][j] *= corr[i];
+        OD[i][j] *= corr[i];
+      }
+    __syncthreads();  // P / PdS complete
+    const int kmax = min(kKeys, last_key - k0);
+    for (int c = 0; c < kmax; ++c) {
+      const float4 pv = *reinterpret_cast<const float4 *>(Pt + c * kRows + 4 * ty);
+      const float4 pdv = *reinterpret_cast<const float4 *>(PDt + c * kRows + 4 * ty);
+      const float pa[4] = {pv.x, pv.y, pv.z, pv.w}, pda[4] = {pdv.x, pdv.y, pdv.z, pdv.w};
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        const float vv = Vs[c * HD + tx + 16 * j], dvv = dVs[c * HD + tx + 16 * j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          O[i][j] = fmaf(pa[i], vv, O[i][j]);
+          OS[i][j] = fmaf(pda[i], vv, OS[i][j]);
+          OD[i][j] = fmaf(pa[i], dvv, OD[i][j]);
+        }
+      }
     }
   }
-  const float inv_l = valid && l > 0.f ? 1.f / l : 0.f;
-  const float tbar = t * inv_l;  // rowsum(A (.) dS)
-
-  // pass 2: outputs
-  float oc[SL], od[SL];
 #pragma unroll
-  for (int j = 0; j < SL; ++j) oc[j] = od[j] = 0.f;
-  for (int kb = 0; kb < n_blocks; ++kb) {
-    __syncthreads();
-    stage(kb);
-    __syncthreads();
-    const int k0 = kb * kKeys;
-    for (int kk = 0; kk < kKeys; ++kk) {
-      const int key = k0 + kk;
-      if (key >= last_key) break;
-      float s, ds;
-      scores(kk, s, ds);
-      if (!valid || key > row) continue;
-      const float aa = expf(s - m) * inv_l;
-      const float da = aa * (ds - tbar);
-      const float *vr = Vs + kk * a.hd + d0, *dvr = dVs + kk * a.hd + d0;
+  for (int i = 0; i < 4; ++i) {
+    const int row = q0 + 4 * ty + i;
+    if (row >= a.n) continue;
+    const float inv = l[i] > 0.f ? 1.f / l[i] : 0.f;
+    const float tb = t[i] * inv;
+    float *o = a.dctx + static_cast<int64_t>(row) * a.out_row + static_cast<int64_t>(h) * HD;
+    float *c = a.ctx ? a.ctx + static_cast<int64_t>(row) * a.out_row + static_cast<int64_t>(h) * HD : nullptr;
 #pragma unroll
-      for (int j = 0; j < SL; ++j) {
-        od[j] = fmaf(da, vr[j], fmaf(aa, dvr[j], od[j]));
-        oc[j] = fmaf(aa, vr[j], oc[j]);
-      }
-    }
-  }
-  if (valid) {
-    float *o = a.dctx + static_cast<int64_t>(row) * a.out_row + static_cast<int64_t>(h) * a.hd + d0;
-#pragma unroll
-    for (int j = 0; j < SL; ++j) o[j] = od[j];
-    if (a.ctx) {
-      float *c = a.ctx + static_cast<int64_t>(row) * a.out_row + static_cast<int64_t>(h) * a.hd + d0;
-#pragma unroll
-      for (int j = 0; j < SL; ++j) c[j] = oc[j];
+    for (int j = 0; j < CPT; ++j) {
+      o[tx + 16 * j] = fmaf(OS[i][j] - tb * O[i][j], inv, OD[i][j] * inv);
+      if (c) c[tx + 16 * j] = O[i][j] * inv;
     }
   }
 }
 
+template <int HD>
+constexpr int smem_bytes() {
+  return (2 * HD * kRows + 2 * HD * kKeys + 2 * kKeys * HD + 2 * kKeys * kRows) * 4;
+}
+
 template <int DT>
 int launch(const Args &a, cudaStream_t st) {
-  const size_t smem = static_cast<size_t>(4) * kKeys * a.hd * sizeof(float);
   dim3 grid(static_cast<unsigned>((a.n + kRows - 1) / kRows), static_cast<unsigned>(a.n_heads));
-#define DKV_AFO(SL)                                                                                   \
-  if (a.hd == 4 * SL) {                                                                               \
-    DKV_CUDA_CHECK(cudaFuncSetAttribute(afo_kernel<DT, SL>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                        static_cast<int>(smem)));                                     \
-    afo_kernel<DT, SL><<<grid, kThreads, smem, st>>>(a);                                              \
+#define DKV_AFO(HD)                                                                                   \
+  if (a.hd == HD) {                                                                                   \
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(afo_kernel<DT, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                        smem_bytes<HD>()));                                           \
+    afo_kernel<DT, HD><<<grid, kThreads, smem_bytes<HD>(), st>>>(a);                                  \
     DKV_CUDA_CHECK(cudaGetLastError());                                                               \
     return DKV_OK;                                                                                    \
   }
-  DKV_AFO(4)
-  DKV_AFO(8)
   DKV_AFO(16)
   DKV_AFO(32)
+  DKV_AFO(64)
+  DKV_AFO(128)
 #undef DKV_AFO
   return DKV_ERR_UNSUPPORTED;
 }

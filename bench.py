@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama8b-exact",
-                    choices=["llama8b-exact", "smollm2-exact", "rl-dense", "multi-lora-kivi"])
+                    choices=["llama8b-exact", "smollm2-exact", "rl-dense", "multi-lora-kivi", "analytic"])
     ap.add_argument("--adapters", type=int, default=8)
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--seqs", type=int, default=None)
@@ -1138,8 +1138,226 @@ def run_kivi_reference(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# analytic route (Route A): first-order propagation through the stack
+# ---------------------------------------------------------------------------
+ANALYTIC_METRIC = "patched token·layers/s (analytic route, SmolLM2-135M shape)"
+FP32_FMA_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # SMs x FP32 lanes x 2 x max SM clock
+
+
+class AnalyticGeo:
+    layers, d_model, n_heads, n_kv, hd, d_ff, rank = 30, 576, 9, 3, 64, 1536, 8
+    seqs, seq_len, eps, rope_theta, propagator_rank, hidden_stride = 4, 2048, 1e-5, 10000.0, 64, 4
+
+
+ANALYTIC_WORKLOAD = ("SmolLM2-135M-shaped analytic route (engine loop of the reference): 30 layers, d=576, 9 query / 3 "
+                     "KV heads x 64, SwiGLU 1536, fp32 weights N(0, 0.02), rank-8 LoRA on q/k/v/o of every layer, "
+                     "stored hidden states N(0,1) (layer input and post-attention), 2048 tokens per sequence, "
+                     "propagator rank 64, hidden stride 4")
+
+
+def make_analytic_workload(args, device, seed):
+    import types as _t
+
+    from deltakv_b200.rope import RotaryEmbedding
+    from deltakv_b200.types import LayerDelta, LowRankFactors
+
+    G = AnalyticGeo
+    g = torch.Generator(device=device).manual_seed(seed)
+    rnd = lambda *shape, s=0.02: torch.randn(*shape, generator=g, device=device) * s
+    dq, dkv = G.n_heads * G.hd, G.n_kv * G.hd
+    blocks, layers = [], {}
+    for l in range(args.layers):
+        mod = lambda w: _t.SimpleNamespace(weight=w)
+        b = _t.SimpleNamespace(
+            attn_norm=mod(1 + rnd(G.d_model, s=0.1)), mlp_norm=mod(1 + rnd(G.d_model, s=0.1)),
+            q_proj=mod(rnd(dq, G.d_model)), k_proj=mod(rnd(dkv, G.d_model)), v_proj=mod(rnd(dkv, G.d_model)),
+            o_proj=mod(rnd(G.d_model, dq)), gate_proj=mod(rnd(G.d_ff, G.d_model)), up_proj=mod(rnd(G.d_ff, G.d_model)),
+            down_proj=mod(rnd(G.d_model, G.d_ff)))
+        blocks.append(b)
+        proj = {}
+        for name, (fin, fout) in (("q_proj", (G.d_model, dq)), ("k_proj", (G.d_model, dkv)),
+                                  ("v_proj", (G.d_model, dkv)), ("o_proj", (dq, G.d_model))):
+            proj[name] = LowRankFactors(A=rnd(G.rank, fin, s=fin ** -0.5), B=rnd(fout, G.rank, s=1.0), scale=0.01)
+        layers[l] = LayerDelta(layer_idx=l, projections=proj)
+    cfg = _t.SimpleNamespace(n_heads=G.n_heads, n_kv_heads=G.n_kv, head_dim=G.hd, d_model=G.d_model, rms_eps=G.eps)
+    model = _t.SimpleNamespace(cfg=cfg, blocks=blocks, rope=RotaryEmbedding(G.hd, max_seq=args.seq_len, base=G.rope_theta))
+    conf = _t.SimpleNamespace(hidden_stride=G.hidden_stride, propagator_rank=G.propagator_rank)
+    hidden = []
+    for _ in range(args.seqs):
+        h = torch.randn(args.layers, args.seq_len, G.d_model, generator=g, device=device)
+        hm = torch.randn(args.layers, args.seq_len, G.d_model, generator=g, device=device)
+        hidden.append((h, hm))
+    return model, _t.SimpleNamespace(layers=layers), conf, hidden
+
+
+def _snapshot(h, hm):
+    import types as _t
+
+    return _t.SimpleNamespace(layer_in=lambda l: h[l], layer_mid=lambda l: hm[l], seq_len=int(h.shape[1]))
+
+
+def analytic_cpu_sample(seconds: float, n: int = 2048, layers: int = 1) -> dict:
+    """The oracle port (numpy fp64) of the engine's analytic loop on ``layers`` layers of one
+    ``n``-token sequence of the same shape, repeated for about ``seconds``."""
+    from oracle import analytic as OA
+
+    G = AnalyticGeo
+    rng = np.random.default_rng(0)
+    rnd = lambda *shape, s=0.02: rng.standard_normal(shape) * s
+    dq, dkv = G.n_heads * G.hd, G.n_kv * G.hd
+    W, Ls = [], {}
+    for l in range(layers):
+        W.append({"q": rnd(dq, G.d_model), "k": rnd(dkv, G.d_model), "v": rnd(dkv, G.d_model), "o": rnd(G.d_model, dq),
+                  "gate": rnd(G.d_ff, G.d_model), "up": rnd(G.d_ff, G.d_model), "down": rnd(G.d_model, G.d_ff),
+                  "attn_norm": 1 + rnd(G.d_model, s=0.1), "mlp_norm": 1 + rnd(G.d_model, s=0.1)})
+        Ls[l] = {p: (rnd(G.rank, fin, s=fin ** -0.5), rnd(fout, G.rank, s=1.0), 0.01)
+                 for p, (fin, fout) in (("q", (G.d_model, dq)), ("k", (G.d_model, dkv)), ("v", (G.d_model, dkv)),
+                                        ("o", (dq, G.d_model)))}
+    cfg = dict(n_heads=G.n_heads, n_kv=G.n_kv, hd=G.hd, d_model=G.d_model, eps=G.eps, rope_base=G.rope_theta,
+               hidden_stride=G.hidden_stride, propagator_rank=G.propagator_rank)
+    h, hm = rng.standard_normal((layers, n, G.d_model)), rng.standard_normal((layers, n, G.d_model))
+    t0, done = time.perf_counter(), 0
+    while True:
+        OA.analytic_patches(h, hm, W, Ls, cfg)
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return {"value": done * layers * n / el, "unit": UNIT, "cores": cpu_pool_threads(), "kind": "port",
+            "sample": f"{done} x ({layers} layer x {n} tokens) of the engine's analytic loop in {el:.1f} s "
+                      "(oracle numpy fp64 port, attention materialised; BLAS threads for the matrix products)"}
+
+
+def run_analytic_ours(args):
+    from deltakv_b200 import analytic as AN
+    from deltakv_b200 import ops
+
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    G = AnalyticGeo
+    model, delta, conf, hidden = make_analytic_workload(args, dev, 7000 + rank)
+    units = args.layers * args.seq_len * args.seqs
+    stream = torch.cuda.current_stream()
+
+    def step():
+        for h, hm in hidden:
+            AN.analytic_patches(_snapshot(h, hm), delta, model, conf)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    ops.status_word(dev).raise_if_set("bench warm-up")
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t_start.record(stream)
+        for _ in range(args.steps):
+            step()
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = t_start.elapsed_time(t_end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    # the attention core alone on one layer's tensors (same shapes as inside the loop)
+    n = args.seq_len
+    gq = torch.Generator(device=dev).manual_seed(1)
+    mk = lambda hh: torch.randn(n, hh, G.hd, generator=gq, device=dev)
+    qs = [mk(G.n_heads), mk(G.n_heads), mk(G.n_kv), mk(G.n_kv), mk(G.n_kv), mk(G.n_kv)]
+    AN.attention_core(*qs, want_ctx=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    e0.record(stream)
+    for _ in range(reps):
+        AN.attention_core(*qs, want_ctx=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    core_ms = e0.elapsed_time(e1) / reps
+    core_flops = 2 * 6 * G.hd * (n * (n + 1) / 2) * G.n_heads  # S, dS (2), O, OS, OD MACs per causal pair
+    achieved = core_flops / (core_ms / 1e3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = analytic_cpu_sample(args.cpu_seconds)
+    e2e = None
+    if not args.no_e2e:
+        # through the public API from pinned host buffers: hidden states in, the K / V patches out
+        h_host = [(h.cpu().pin_memory(), hm.cpu().pin_memory()) for h, hm in hidden]
+        out_bytes = 2 * args.layers * n * G.n_kv * G.hd * 4
+        outs = [torch.empty(2, args.layers, n, G.n_kv, G.hd).pin_memory() for _ in hidden]
+        e2 = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        e2[0].record(stream)
+        for (hh, hmh), o in zip(h_host, outs):
+            h_d, hm_d = hh.to(dev, non_blocking=True), hmh.to(dev, non_blocking=True)
+            pt = AN.analytic_patches(_snapshot(h_d, hm_d), delta, model, conf)
+            o[0].copy_(torch.stack([pt[l].k_dense for l in range(args.layers)]), non_blocking=True)
+            o[1].copy_(torch.stack([pt[l].v_dense for l in range(args.layers)]), non_blocking=True)
+        e2[1].record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e2[0].elapsed_time(e2[1])
+        e2e = {"value": units / (e2e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": sum(a.numel() * 4 + b.numel() * 4 for a, b in h_host),
+               "d2h_bytes_per_step": out_bytes * len(hidden), "ms_per_step": e2e_ms}
+    if rank == 0:
+        line = {
+            "metric": ANALYTIC_METRIC, "value": units * world / (ms_step / 1e3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": ANALYTIC_WORKLOAD, "layers": args.layers, "seqs_per_gpu": args.seqs,
+                       "seq_len": n, "parallelism": f"request shards x{world}",
+                       "l2": "per sequence 283 MB of stored hidden states >> 126 MB L2"},
+            "roofline": {"bound": "fp32 FMA", "achieved": achieved, "peak": FP32_FMA_NOMINAL_TFLOPS,
+                         "unit": "TFLOP/s", "frac": achieved / FP32_FMA_NOMINAL_TFLOPS, "traffic": None,
+                         "peak_source": "of nominal (148 SMs x 128 fp32 lanes x 2 x 1965 MHz; no measured fp32 figure)",
+                         "kernel": "attention core (dkv_attn_first_order), one layer", "kernel_ms": core_ms,
+                         "algorithmic_flops_per_launch": core_flops},
+            "cpu_baseline": cpu, "e2e": e2e,
+            # per layer and sequence: rmsnorm x2, rope x4, attention core, swiglu, jacobi (rank truncation)
+            "gpu_launches": args.steps * args.seqs * args.layers * 9,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def run_analytic_reference(args):
+    world, rank, _ = dist_setup(args)
+    if rank != 0:
+        return 0
+    res = [analytic_cpu_sample(max(2.0, args.cpu_seconds / max(1, args.steps))) for _ in range(args.steps)]
+    value = sum(r["value"] for r in res) / len(res)
+    line = {
+        "impl": "reference", "metric": ANALYTIC_METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": ANALYTIC_WORKLOAD, "step": res[0]["sample"]},
+        "cpu_baseline": {**res[0], "value": value},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "analytic":
+        for k, v in (("layers", AnalyticGeo.layers), ("seqs", AnalyticGeo.seqs), ("seq_len", AnalyticGeo.seq_len)):
+            if getattr(args, k) is None:
+                setattr(args, k, v)
+        return run_analytic_reference(args) if args.impl == "reference" else run_analytic_ours(args)
     if args.workload == "multi-lora-kivi":
         for k, v in (("layers", KiviGeo.layers), ("seqs", 1), ("seq_len", KiviGeo.seq_len)):
             if getattr(args, k) is None:

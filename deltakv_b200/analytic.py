@@ -12,9 +12,8 @@ engine's per-layer loop ``DeltaKVEngine._analytic_patches`` (src/deltakv/engine.
   fourth value (unused by its engine) is ``None`` unless ``return_attn=True`` asks for it;
 * ``mlp_first_order`` (analytic.py:108-138) — gate/up/down GEMMs and ``dkv_swiglu_first_order``;
 * ``rank_truncate`` (analytic.py:14-22) — the best rank-r approximation from the top-r right
-  singular subspace (:func:`deltakv_b200.subspace.topr_basis`, exact SVD where its estimate
-  is not converged); ``codes @ basis.T`` equals the reference's, the factors themselves may
-  differ by a rotation within the subspace;
+  singular subspace (fp64 Gram matrix + eigensolver); ``codes @ basis.T`` equals the
+  reference's, the factors themselves may differ by a rotation within the subspace;
 * ``analytic_patches`` — the engine loop, with ``model`` / ``config`` objects shaped like the
   reference's (``cfg``, ``blocks``, ``rope``; ``hidden_stride``, ``propagator_rank``).
 
@@ -179,13 +178,15 @@ def mlp_first_order(x: Tensor, dx: Tensor, gate_w: Tensor, up_w: Tensor, down_w:
 
 def rank_truncate(delta: Tensor, rank: int) -> tuple[Tensor, Tensor]:
     """Δ ≈ codes @ basis.T with ``codes [n, r]``, ``basis [d, r]`` (the best rank-r
-    approximation, analytic.py:14-22)."""
-    from deltakv_b200.subspace import topr_basis
+    approximation, analytic.py:14-22).  The propagated ΔX has no spectral gap to exploit, so
+    the basis comes straight from the exact path (fp64 Gram matrix and eigensolver,
+    :func:`deltakv_b200.subspace.gram_basis`) rather than a subspace iteration."""
+    from deltakv_b200.subspace import gram_basis
 
     ops._require_cuda(delta)
     flat = delta.reshape(delta.shape[0], -1).float()
     r = max(1, min(int(rank), *flat.shape))
-    basis = topr_basis(flat, r)
+    basis = gram_basis(flat, r)
     codes = flat @ basis
     return codes.to(delta.dtype), basis.to(delta.dtype)
 

@@ -4,8 +4,8 @@ its device eigensolver (``dkv_sym_eig_batched``) against LAPACK.
 ``topr_basis`` must span the same subspace as the reference's ``svd_basis`` (a full SVD);
 the least-squares correction depends on the basis only through that column space, so the
 check is on the orthogonal projectors: relative Frobenius difference below 1e-5 from an fp64
-SVD (the fp32 device SVD itself is only good to ~5e-4 at 1500 x 1024, rank 64), and below
-1e-5 from ``svd_basis`` where the SVD fallback must take over.  The eigensolver: eigenvalues
+SVD (the fp32 device SVD itself is only good to ~5e-4 at 1500 x 1024, rank 64), also where the
+exact path (fp64 Gram matrix + eigensolver) must take over.  The eigensolver: eigenvalues
 within 1e-10 of the largest magnitude, eigenvectors orthonormal to 1e-10 and
 A V = V diag(ev) to 1e-9 (fp64).
 """
@@ -16,7 +16,7 @@ import numpy as np
 import pytest
 import torch
 
-from deltakv_b200.subspace import svd_basis, sym_eig, topr_basis
+from deltakv_b200.subspace import gram_basis, sym_eig, topr_basis
 
 pytestmark = pytest.mark.gpu
 
@@ -51,11 +51,19 @@ def test_topr_basis_batched_and_orthonormal(cuda):
         assert _proj_diff(_truth(x[i], 6), b[i]) < 1e-5
 
 
-def test_topr_basis_falls_back_to_svd_without_a_gap(cuda):
-    # isotropic noise has no spectral gap: the iteration cannot settle, the exact SVD is used
+def test_topr_basis_falls_back_without_a_gap(cuda, monkeypatch):
+    # isotropic noise has no spectral gap: the iteration cannot settle, the exact path is used
+    # right after the first estimate (the extrapolated one cannot reach the tolerance)
+    import deltakv_b200.subspace as S
+
+    calls = []
+    monkeypatch.setattr(S, "gram_basis", lambda x, r: calls.append(x.shape[0]) or gram_basis(x, r))
     g = torch.Generator().manual_seed(2)
     x = torch.randn(500, 256, generator=g).to(cuda)
-    assert _proj_diff(svd_basis(x, 8), topr_basis(x, 8)) < 1e-5
+    b = S.topr_basis(x, 8)
+    assert calls == [1]
+    # a gapless spectrum: compare the projectors of the exact paths (fp64 SVD vs fp64 Gram)
+    assert _proj_diff(_truth(x, 8), b) < 1e-5
 
 
 def test_topr_basis_iterates_further_before_falling_back(cuda, monkeypatch):
@@ -64,7 +72,7 @@ def test_topr_basis_iterates_further_before_falling_back(cuda, monkeypatch):
     import deltakv_b200.subspace as S
 
     calls = []
-    monkeypatch.setattr(S, "svd_basis", lambda x, r: calls.append(1) or svd_basis(x, r))
+    monkeypatch.setattr(S, "gram_basis", lambda x, r: calls.append(1) or gram_basis(x, r))
     g = torch.Generator().manual_seed(4)
     m, d, r = 600, 256, 8
     u, _ = torch.linalg.qr(torch.randn(m, d, generator=g, dtype=torch.float64))
@@ -75,17 +83,17 @@ def test_topr_basis_iterates_further_before_falling_back(cuda, monkeypatch):
     assert not calls
     assert _proj_diff(v[:, :r].float().to(cuda), b[0]) < 1e-5
     assert _proj_diff(v[:, :r].float().to(cuda), b[1]) < 1e-5
-    one = S.topr_basis(x, r, iters=2)  # capped at two: the estimate fails, the SVD is used
-    assert calls and _proj_diff(svd_basis(x, r), one) < 1e-6
+    one = S.topr_basis(x, r, iters=2)  # capped at two: the estimate fails, the exact path is used
+    assert calls and _proj_diff(v[:, :r].float().to(cuda), one) < 1e-5
 
 
-def test_topr_basis_few_rows_uses_svd(cuda):
-    # m <= rank + oversample: the exact SVD directly
+def test_topr_basis_few_rows_uses_the_exact_path(cuda):
+    # m <= rank + oversample: the fp64 Gram eigensolver directly
     g = torch.Generator().manual_seed(3)
     x = torch.randn(2, 10, 64, generator=g).to(cuda)
     b = topr_basis(x, 4)
     for i in range(2):
-        assert _proj_diff(svd_basis(x[i], 4), b[i]) < 1e-5
+        assert _proj_diff(_truth(x[i], 4), b[i]) < 1e-5
 
 
 def _check_eig(a, ev, vec):

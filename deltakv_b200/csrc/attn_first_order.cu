@@ -47,7 +47,7 @@ struct Args {
 // rescaled by exp(m_old - m_new) as m grows; at the end ctx = O / l and
 // dctx = (OS - (t / l) O) / l + OD / l.
 template <int DT, int HD>
-__global__ void __launch_bounds__(kThreads, 1) afo_kernel(const Args a) {
+__global__ void __launch_bounds__(kThreads, HD <= 64 ? 2 : 1) afo_kernel(const Args a) {
   constexpr int CPT = HD / 16;  // output columns per thread
   extern __shared__ __align__(16) float sm[];
   float *Qt = sm;                       // [HD][kRows]  (q * scale)^T

@@ -94,13 +94,6 @@ __device__ __forceinline__ int find_prob(const Batch &b, int64_t tile) {
   return lo;
 }
 
-template <int FDT>
-__device__ __forceinline__ float load1(const void *base, int64_t off) {
-  if (FDT == DKV_F32) return static_cast<const float *>(base)[off];
-  if (FDT == DKV_BF16) return __bfloat162float(static_cast<const __nv_bfloat16 *>(base)[off]);
-  return __half2float(static_cast<const __half *>(base)[off]);
-}
-
 // 8 consecutive fresh values (16 B of bf16/f16, 32 B of f32)
 template <int FDT>
 __device__ __forceinline__ void load8(const void *base, int64_t off, float (&v)[8]) {

@@ -206,3 +206,19 @@ def test_kivi_subspace_views_pipelined_matches_sequential(cuda):
             eq = (OK.unpack_nibbles(x.codes.cpu().numpy()) == OK.unpack_nibbles(y.codes.cpu().numpy())).mean()
             assert eq >= 0.999, (a, j, eq)
             torch.testing.assert_close(x.scale.float(), y.scale.float(), rtol=5e-3, atol=1e-6)
+
+
+def test_kivi_subspace_views_edge_cases(cuda):
+    assert K.subspace_correct_views([]) == []
+    assert K.subspace_correct_views([[], []]) == [[], []]
+    gen = torch.Generator().manual_seed(5)
+    cs = _case(gen, 96, 2, 64, 8, "v")
+    pb = lambda: K.SubspaceProblem(base=_device_base(cs, cuda), fresh=cs["fresh"].to(cuda),
+                                   probe_index=cs["probes"].to(cuda), basis=cs["B"].to(cuda), rank=8,
+                                   out=K.KiviTensor.empty(96, cs["d"], "v", cuda))
+    (a,), = [[r[0] for r in K.subspace_correct([pb()])]]
+    res = K.subspace_correct_views([[], [pb()]])
+    assert res[0] == [] and len(res[1]) == 1
+    torch.cuda.synchronize()
+    eq = (OK.unpack_nibbles(a.codes.cpu().numpy()) == OK.unpack_nibbles(res[1][0][0].codes.cpu().numpy())).mean()
+    assert eq >= 0.999

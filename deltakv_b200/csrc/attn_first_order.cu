@@ -201,6 +201,223 @@ __global__ void __launch_bounds__(kThreads, HD <= 64 ? 2 : 1) afo_kernel(const A
   }
 }
 
+// ---------------------------------------------------------------------------------------
+// Tensor-core form (head_dim 64 / 128): the same single pass, with every product on mma.sync
+// bf16 tensor cores in a three-term split — x = hi + lo with hi = bf16(x), lo = bf16(x - hi),
+// x y ~ hi_x hi_y + hi_x lo_y + lo_x hi_y (the lo_x lo_y term is below 2^-16 relative), fp32
+// accumulation — so scores keep ~2^-16 relative accuracy.  8 warps per CTA of 64 query rows:
+// warp w computes S and dS for rows 16 (w & 3) .. + 15 over each 32-key block (the two warps of
+// a row group duplicate this) and accumulates O, OS, OD for its half of head_dim (w >> 2).  The
+// score fragments become the A fragments of the output products in registers (FlashAttention-2
+// layout reuse); K / dK come as B fragments by ldmatrix, V / dV by ldmatrix.trans.
+template <int HD>
+struct TcLayout {
+  static constexpr int LD = HD + 8;  // bf16 per smem row (16-byte pad: conflict-free ldmatrix)
+  static constexpr int Q_ROWS = kRows, K_ROWS = kKeys;
+  static constexpr int bytes() { return (4 * Q_ROWS + 8 * K_ROWS) * LD * 2; }
+};
+
+__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16 &h, __nv_bfloat16 &l) {
+  h = __float2bfloat16_rn(x);
+  l = __float2bfloat16_rn(x - __bfloat162float(h));
+}
+// hi / lo bf16x2 pairs of two fp32 values (lower element in the low half)
+__device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t &lo) {
+  hi = pack_bf16x2(a, b);
+  const float ah = __uint_as_float(hi << 16), bh = __uint_as_float(hi & 0xffff0000u);
+  lo = pack_bf16x2(a - ah, b - bh);
+}
+__device__ __forceinline__ void mma3(float (&c)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4], uint32_t bh0,
+                                     uint32_t bh1, uint32_t bl0, uint32_t bl1) {
+  mma16816_bf16(c, ah[0], ah[1], ah[2], ah[3], bh0, bh1);
+  mma16816_bf16(c, ah[0], ah[1], ah[2], ah[3], bl0, bl1);
+  mma16816_bf16(c, al[0], al[1], al[2], al[3], bh0, bh1);
+}
+
+template <int DT, int HD>
+__global__ void __launch_bounds__(kThreads, 1) afo_tc_kernel(const Args a) {
+  using Lt = TcLayout<HD>;
+  constexpr int LD = Lt::LD;
+  constexpr int NT = HD / 16;  // 8-column output n-tiles in this warp's half of head_dim
+  extern __shared__ __align__(16) __nv_bfloat16 smb[];
+  __nv_bfloat16 *Qh = smb, *Ql = Qh + kRows * LD, *dQh = Ql + kRows * LD, *dQl = dQh + kRows * LD;
+  __nv_bfloat16 *Kh = dQl + kRows * LD, *Kl = Kh + kKeys * LD, *dKh = Kl + kKeys * LD, *dKl = dKh + kKeys * LD;
+  __nv_bfloat16 *Vh = dKl + kKeys * LD, *Vl = Vh + kKeys * LD, *dVh = Vl + kKeys * LD, *dVl = dVh + kKeys * LD;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, q = lane & 3;
+  const int rg = warp & 3, half = warp >> 2;
+  const int h = blockIdx.y, hk = h / (a.n_heads / a.n_kv);
+  const int q0 = (gridDim.x - 1 - blockIdx.x) * kRows;  // the longest (latest) rows first
+  for (int e = tid; e < kRows * HD; e += kThreads) {
+    const int r = e / HD, d = e - r * HD;
+    const int row = q0 + r;
+    float x = 0.f, dx = 0.f;
+    if (row < a.n) {
+      const int64_t o = static_cast<int64_t>(row) * a.q_row + static_cast<int64_t>(h) * HD + d;
+      x = ld<DT>(a.q, o) * a.scale;
+      dx = ld<DT>(a.dq, o) * a.scale;
+    }
+    split_bf16(x, Qh[r * LD + d], Ql[r * LD + d]);
+    split_bf16(dx, dQh[r * LD + d], dQl[r * LD + d]);
+  }
+  const int r0 = q0 + 16 * rg + g, r1 = r0 + 8;  // this lane's two rows
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f}, t[2] = {0.f, 0.f};
+  float O[NT][4], OS[NT][4], OD[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) O[j][c] = OS[j][c] = OD[j][c] = 0.f;
+  const int last_key = min(q0 + kRows, a.n);
+  const int n_blocks = (last_key + kKeys - 1) / kKeys;
+  // ldmatrix lane addressing
+  const int a_row = 16 * rg + (lane & 15), a_col = (lane >> 4) * 8;                 // A: rows x k
+  const int b_key = (lane & 7) + ((lane >> 4) << 3), b_col = ((lane >> 3) & 1) * 8;  // B from K rows
+  const int v_key = (lane & 7) + (((lane >> 3) & 1) << 3), v_col = (lane >> 4) * 8;  // B from V rows (trans)
+  for (int kb = 0; kb < n_blocks; ++kb) {
+    const int k0 = kb * kKeys;
+    __syncthreads();
+    for (int e = tid; e < kKeys * HD; e += kThreads) {
+      const int c = e / HD, d = e - c * HD;
+      const int key = k0 + c;
+      float kv = 0.f, dkv = 0.f, vv = 0.f, dvv = 0.f;
+      if (key < a.n) {
+        const int64_t o = static_cast<int64_t>(key) * a.kv_row + static_cast<int64_t>(hk) * HD + d;
+        kv = ld<DT>(a.k, o);
+        dkv = ld<DT>(a.dk, o);
+        vv = ld<DT>(a.v, o);
+        dvv = ld<DT>(a.dv, o);
+      }
+      split_bf16(kv, Kh[c * LD + d], Kl[c * LD + d]);
+      split_bf16(dkv, dKh[c * LD + d], dKl[c * LD + d]);
+      split_bf16(vv, Vh[c * LD + d], Vl[c * LD + d]);
+      split_bf16(dvv, dVh[c * LD + d], dVl[c * LD + d]);
+    }
+    __syncthreads();
+    // scores of 4 n-tiles (32 keys): S and dS
+    float S[4][4], dS[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) S[j][c] = dS[j][c] = 0.f;
+#pragma unroll 2
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      uint32_t qh[4], ql[4], dqh[4], dql[4];
+      const int ao = a_row * LD + 16 * ks + a_col;
+      ldmatrix_x4(qh[0], qh[1], qh[2], qh[3], smem_u32(Qh + ao));
+      ldmatrix_x4(ql[0], ql[1], ql[2], ql[3], smem_u32(Ql + ao));
+      ldmatrix_x4(dqh[0], dqh[1], dqh[2], dqh[3], smem_u32(dQh + ao));
+      ldmatrix_x4(dql[0], dql[1], dql[2], dql[3], smem_u32(dQl + ao));
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {  // n-tiles 2 np, 2 np + 1
+        const int bo = (16 * np + b_key) * LD + 16 * ks + b_col;
+        uint32_t kh[4], kl[4], dkh[4], dkl[4];
+        ldmatrix_x4(kh[0], kh[1], kh[2], kh[3], smem_u32(Kh + bo));
+        ldmatrix_x4(kl[0], kl[1], kl[2], kl[3], smem_u32(Kl + bo));
+        ldmatrix_x4(dkh[0], dkh[1], dkh[2], dkh[3], smem_u32(dKh + bo));
+        ldmatrix_x4(dkl[0], dkl[1], dkl[2], dkl[3], smem_u32(dKl + bo));
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int j = 2 * np + u;
+          mma3(S[j], qh, ql, kh[2 * u], kh[2 * u + 1], kl[2 * u], kl[2 * u + 1]);
+          mma3(dS[j], dqh, dql, kh[2 * u], kh[2 * u + 1], kl[2 * u], kl[2 * u + 1]);
+          mma3(dS[j], qh, ql, dkh[2 * u], dkh[2 * u + 1], dkl[2 * u], dkl[2 * u + 1]);
+        }
+      }
+    }
+    // online softmax: lane holds rows r0 (c = 0, 1) and r1 (c = 2, 3), keys k0 + 8 j + 2 q + (c & 1)
+    float corr[2];
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int row = hr ? r1 : r0;
+      float bm = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int key = k0 + 8 * j + 2 * q + c;
+          if (key > row || key >= a.n) S[j][2 * hr + c] = -INFINITY;
+          bm = fmaxf(bm, S[j][2 * hr + c]);
+        }
+      bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));
+      bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));
+      const float mn = fmaxf(m[hr], bm);
+      corr[hr] = mn == -INFINITY ? 1.f : expf(m[hr] - mn);
+      float ls = 0.f, ts = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const float sv = S[j][2 * hr + c];
+          const float pv = sv == -INFINITY ? 0.f : expf(sv - mn);
+          const float pd = pv * dS[j][2 * hr + c];
+          S[j][2 * hr + c] = pv;  // S now holds p
+          dS[j][2 * hr + c] = pd;  // dS now holds p dS
+          ls += pv;
+          ts += pd;
+        }
+      ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+      ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+      ts += __shfl_xor_sync(0xffffffffu, ts, 1);
+      ts += __shfl_xor_sync(0xffffffffu, ts, 2);
+      m[hr] = mn;
+      l[hr] = fmaf(l[hr], corr[hr], ls);
+      t[hr] = fmaf(t[hr], corr[hr], ts);
+    }
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      O[j][0] *= corr[0], O[j][1] *= corr[0], O[j][2] *= corr[1], O[j][3] *= corr[1];
+      OS[j][0] *= corr[0], OS[j][1] *= corr[0], OS[j][2] *= corr[1], OS[j][3] *= corr[1];
+      OD[j][0] *= corr[0], OD[j][1] *= corr[0], OD[j][2] *= corr[1], OD[j][3] *= corr[1];
+    }
+    // outputs: two 16-key k-steps; P / PdS fragments straight from the score accumulators
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t ph[4], pl[4], pdh[4], pdl[4];
+      split2(S[2 * kk][0], S[2 * kk][1], ph[0], pl[0]);
+      split2(S[2 * kk][2], S[2 * kk][3], ph[1], pl[1]);
+      split2(S[2 * kk + 1][0], S[2 * kk + 1][1], ph[2], pl[2]);
+      split2(S[2 * kk + 1][2], S[2 * kk + 1][3], ph[3], pl[3]);
+      split2(dS[2 * kk][0], dS[2 * kk][1], pdh[0], pdl[0]);
+      split2(dS[2 * kk][2], dS[2 * kk][3], pdh[1], pdl[1]);
+      split2(dS[2 * kk + 1][0], dS[2 * kk + 1][1], pdh[2], pdl[2]);
+      split2(dS[2 * kk + 1][2], dS[2 * kk + 1][3], pdh[3], pdl[3]);
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {
+        const int vo = (16 * kk + v_key) * LD + half * (HD / 2) + 16 * np + v_col;
+        uint32_t vh[4], vl[4], dvh[4], dvl[4];
+        ldmatrix_x4_trans(vh[0], vh[1], vh[2], vh[3], smem_u32(Vh + vo));
+        ldmatrix_x4_trans(vl[0], vl[1], vl[2], vl[3], smem_u32(Vl + vo));
+        ldmatrix_x4_trans(dvh[0], dvh[1], dvh[2], dvh[3], smem_u32(dVh + vo));
+        ldmatrix_x4_trans(dvl[0], dvl[1], dvl[2], dvl[3], smem_u32(dVl + vo));
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int j = 2 * np + u;
+          mma3(O[j], ph, pl, vh[2 * u], vh[2 * u + 1], vl[2 * u], vl[2 * u + 1]);
+          mma3(OS[j], pdh, pdl, vh[2 * u], vh[2 * u + 1], vl[2 * u], vl[2 * u + 1]);
+          mma3(OD[j], ph, pl, dvh[2 * u], dvh[2 * u + 1], dvl[2 * u], dvl[2 * u + 1]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const int row = hr ? r1 : r0;
+    if (row >= a.n) continue;
+    const float inv = l[hr] > 0.f ? 1.f / l[hr] : 0.f;
+    const float tb = t[hr] * inv;
+    float *o = a.dctx + static_cast<int64_t>(row) * a.out_row + static_cast<int64_t>(h) * HD + half * (HD / 2);
+    float *cx = a.ctx ? a.ctx + static_cast<int64_t>(row) * a.out_row + static_cast<int64_t>(h) * HD + half * (HD / 2)
+                      : nullptr;
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int col = 8 * j + 2 * q + c;
+        o[col] = fmaf(OS[j][2 * hr + c] - tb * O[j][2 * hr + c], inv, OD[j][2 * hr + c] * inv);
+        if (cx) cx[col] = O[j][2 * hr + c] * inv;
+      }
+  }
+}
+
 template <int HD>
 constexpr int smem_bytes() {
   return (2 * HD * kRows + 2 * HD * kKeys + 2 * kKeys * HD + 2 * kKeys * kRows) * 4;
@@ -219,9 +436,18 @@ int launch(const Args &a, cudaStream_t st) {
   }
   DKV_AFO(16)
   DKV_AFO(32)
-  DKV_AFO(64)
-  DKV_AFO(128)
 #undef DKV_AFO
+#define DKV_AFO_TC(HD)                                                                                   \
+  if (a.hd == HD) {                                                                                      \
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(afo_tc_kernel<DT, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                        TcLayout<HD>::bytes()));                                         \
+    afo_tc_kernel<DT, HD><<<grid, kThreads, TcLayout<HD>::bytes(), st>>>(a);                              \
+    DKV_CUDA_CHECK(cudaGetLastError());                                                                  \
+    return DKV_OK;                                                                                       \
+  }
+  DKV_AFO_TC(64)
+  DKV_AFO_TC(128)
+#undef DKV_AFO_TC
   return DKV_ERR_UNSUPPORTED;
 }
 

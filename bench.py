@@ -1287,6 +1287,12 @@ def run_analytic_ours(args):
     core_ms = e0.elapsed_time(e1) / reps
     core_flops = 2 * 6 * G.hd * (n * (n + 1) / 2) * G.n_heads  # S, dS (2), O, OS, OD MACs per causal pair
     achieved = core_flops / (core_ms / 1e3) / 1e12
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    bf16_peak = peaks.get("bf16_tflops") or 1590.0
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = analytic_cpu_sample(args.cpu_seconds)
@@ -1317,11 +1323,17 @@ def run_analytic_ours(args):
             "config": {"workload": ANALYTIC_WORKLOAD, "layers": args.layers, "seqs_per_gpu": args.seqs,
                        "seq_len": n, "parallelism": f"request shards x{world}",
                        "l2": "per sequence 283 MB of stored hidden states >> 126 MB L2"},
-            "roofline": {"bound": "fp32 FMA", "achieved": achieved, "peak": FP32_FMA_NOMINAL_TFLOPS,
-                         "unit": "TFLOP/s", "frac": achieved / FP32_FMA_NOMINAL_TFLOPS, "traffic": None,
-                         "peak_source": "of nominal (148 SMs x 128 fp32 lanes x 2 x 1965 MHz; no measured fp32 figure)",
-                         "kernel": "attention core (dkv_attn_first_order), one layer", "kernel_ms": core_ms,
-                         "algorithmic_flops_per_launch": core_flops},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16_peak, "unit": "TFLOP/s",
+                         "frac": achieved / bf16_peak, "traffic": None,
+                         "peak_source": "of measured (MEASURED_PEAKS.json bf16_tflops, burst)",
+                         "kernel": "attention core (dkv_attn_first_order, mma.sync bf16 three-term split), one layer",
+                         "kernel_ms": core_ms, "algorithmic_flops_per_launch": core_flops,
+                         # the split issues 3 bf16 products per fp32-level product; S / dS are formed by
+                         # both column-half warps of a row group
+                         "issued_mma_flops_per_launch": core_flops * (3 * 3 * 2 + 3 * 3) / 6,
+                         "fp32_fma_equivalent": {"peak": FP32_FMA_NOMINAL_TFLOPS,
+                                                 "frac": achieved / FP32_FMA_NOMINAL_TFLOPS,
+                                                 "peak_source": "of nominal (148 SMs x 128 lanes x 2 x 1965 MHz)"}},
             "cpu_baseline": cpu, "e2e": e2e,
             # per layer and sequence: rmsnorm x2, rope x4, attention core, swiglu, jacobi (rank truncation)
             "gpu_launches": args.steps * args.seqs * args.layers * 9,

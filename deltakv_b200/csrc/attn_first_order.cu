@@ -8,11 +8,10 @@
 // per query head h with its GQA key/value head h / (H / Hkv) (analytic.py:142-153), without
 // materialising the [H, n, n] matrices: one flash-style pass over the causal keys with an
 // online softmax, since dA V = (sum_k p_k dS_k v_k - (sum_k p_k dS_k / l) sum_k p_k v_k) / l
-// needs only per-row running sums.  fp32 arithmetic (the reference runs the route in the model
-// dtype, fp32 for its toy).  A CTA takes 64 query rows of one head with Q and dQ resident in
-// shared memory (transposed) and streams blocks of 32 keys of K, dK, V, dV; both the score
-// micro-GEMMs (4 x 2 per thread) and the output micro-GEMMs (4 rows x head_dim / 16 columns per
-// thread) read shared memory in 8- and 16-byte vectors.
+// needs only per-row running sums.  fp32-level arithmetic (the reference runs the route in the
+// model dtype, fp32 for its toy): head_dim 64 / 128 on tensor cores in a three-term bf16 split
+// (afo_tc_kernel below), 16 / 32 in fp32 SIMT (afo_kernel).  A CTA takes 64 query rows of one
+// head with Q and dQ resident in shared memory and streams blocks of 32 keys of K, dK, V, dV.
 #include "dkv_common.cuh"
 
 namespace dkv {
@@ -38,7 +37,7 @@ struct Args {
   float scale;
 };
 
-// One pass over the causal keys with online softmax.  Thread (ty, tx) = (tid / 16, tid % 16)
+// SIMT form.  One pass over the causal keys with online softmax.  Thread (ty, tx) = (tid / 16, tid % 16)
 // owns query rows 4 ty .. 4 ty + 3: in the score phase keys 2 tx, 2 tx + 1 of the block (a
 // 4 x 2 micro-tile of S and dS), in the output phase head_dim columns tx + 16 j.  Per row the
 // 16 threads of a half-warp share the online statistics m (max), l (sum of p = exp(S - m)),

@@ -380,8 +380,10 @@ int dkv_row_diff_norms(const void *a, const void *b, int32_t dtype, int64_t n_ro
  * A = softmax(S), dS = (dq k^T + q dk^T) * scale, dA = A (.) (dS - rowsum(A (.) dS)):
  *   dctx = dA v + A dv,  ctx = A v (ctx may be NULL).
  * q, dq: [n, n_heads, head_dim] (row stride q_row_stride elements); k, dk, v, dv:
- * [n, n_kv_heads, head_dim] (kv_row_stride); dtype F32, BF16 or F16 (fp32 arithmetic);
- * outputs fp32 [n, n_heads, head_dim] with row stride out_row_stride; head_dim 16/32/64/128.
+ * [n, n_kv_heads, head_dim] (kv_row_stride); dtype F32, BF16 or F16; outputs fp32
+ * [n, n_heads, head_dim] with row stride out_row_stride; head_dim 16/32/64/128.  head_dim 64
+ * and 128 run on tensor cores in a three-term bf16 split (fp32-level accuracy, ~5e-6
+ * relative), 16 and 32 in fp32 SIMT arithmetic.
  */
 int dkv_attn_first_order(const void *q, const void *dq, int64_t q_row_stride, const void *k, const void *dk,
                          const void *v, const void *dv, int64_t kv_row_stride, int32_t dtype, int32_t n_tokens,

@@ -508,18 +508,17 @@ __global__ void __launch_bounds__(256) solve_kernel(const __grid_constant__ Batc
   __syncthreads();
   if (r > 0) {
     // G = B~^T B~ + 1e-6 I: 64-channel tiles of B~ staged in shared memory as fp64 (exact:
-    // bf16 values), fp64 accumulation; the tile area is the not yet used part of Mdyn past [G | I]
+    // bf16 values), fp64 accumulation; the tile area is the not yet used part of Mdyn past
+    // [G | I].  Thread (bi, bj) of a 16 x 16 grid owns the BS x BS block of G at rows BS bi,
+    // columns BS bj (BS = RP / 16), so each staged value it reads feeds BS products.
     double *tile = Mdyn + r * ldm;  // [64][RP]
-    constexpr int EPT = (RP * RP + 255) / 256;
-    double accg[EPT];
-    int gi[EPT], gj[EPT];
+    constexpr int BS = RP / 16;
+    const int bi = threadIdx.x >> 4, bj = threadIdx.x & 15;
+    double accg[BS][BS];
 #pragma unroll
-    for (int u = 0; u < EPT; ++u) {
-      accg[u] = 0.0;
-      const int e = threadIdx.x + 256 * u;
-      gi[u] = e < RP * RP ? e / RP : 0;
-      gj[u] = e < RP * RP ? e % RP : 0;
-    }
+    for (int u = 0; u < BS; ++u)
+#pragma unroll
+      for (int v = 0; v < BS; ++v) accg[u][v] = 0.0;
     for (int64_t c0 = 0; c0 < b.d; c0 += 64) {
       for (int e = threadIdx.x; e < 64 * RP; e += blockDim.x) {
         const int64_t c = c0 + e / RP;
@@ -528,22 +527,29 @@ __global__ void __launch_bounds__(256) solve_kernel(const __grid_constant__ Batc
       __syncthreads();
       for (int cc = 0; cc < 64; ++cc) {
         const double *tr = tile + cc * RP;
+        double xi[BS], xj[BS];
 #pragma unroll
-        for (int u = 0; u < EPT; ++u) accg[u] = fma(tr[gi[u]], tr[gj[u]], accg[u]);
+        for (int u = 0; u < BS; ++u) {
+          xi[u] = tr[BS * bi + u];
+          xj[u] = tr[BS * bj + u];
+        }
+#pragma unroll
+        for (int u = 0; u < BS; ++u)
+#pragma unroll
+          for (int v = 0; v < BS; ++v) accg[u][v] = fma(xi[u], xj[v], accg[u][v]);
       }
       __syncthreads();
     }
 #pragma unroll
-    for (int u = 0; u < EPT; ++u) {
-      const int e = threadIdx.x + 256 * u;
-      if (e < RP * RP) {
-        const int i = gi[u], j = gj[u];
+    for (int u = 0; u < BS; ++u)
+#pragma unroll
+      for (int v = 0; v < BS; ++v) {
+        const int i = BS * bi + u, j = BS * bj + v;
         if (i < r && j < r) {
-          Mdyn[i * ldm + j] = accg[u] + (i == j ? 1e-6 : 0.0);
+          Mdyn[i * ldm + j] = accg[u][v] + (i == j ? 1e-6 : 0.0);
           Mdyn[i * ldm + r + j] = (i == j) ? 1.0 : 0.0;
         }
       }
-    }
     __syncthreads();
     // Gauss-Jordan with partial pivoting on [G | I]; three barriers per column
     const int jj = threadIdx.x & 127, i0 = threadIdx.x >> 7;

@@ -97,6 +97,7 @@ __global__ void __launch_bounds__(kThreads) jacobi_kernel(const double *a_in, in
   for (int e = tid; e < n * n; e += kThreads) A[(e / n) * ld + e % n] *= inv;
   __syncthreads();
 
+  const int m_half = (1 << 20) / half + 1, m_n = (1 << 20) / n + 1;  // e / half, f / n
   int converged = frob == 0.0 ? 1 : 0;
   for (int sweep = 0; sweep < max_sweeps && !converged; ++sweep) {
     for (int round = 0; round < n - 1; ++round) {
@@ -116,10 +117,11 @@ __global__ void __launch_bounds__(kThreads) jacobi_kernel(const double *a_in, in
       }
       __syncthreads();
       // A <- J^T A J one 2x2 block at a time: block (t, u) spans rows {p_t, q_t} and columns
-      // {p_u, q_u} and depends only on rotations t and u; V <- V J alongside.
+      // {p_u, q_u} and depends only on rotations t and u; V <- V J alongside.  The flat index
+      // is split by multiply-shift (exact for these ranges: e < 2^13, divisors <= 96).
       for (int e = tid; e < half * half + n * half; e += kThreads) {
         if (e < half * half) {
-          const int t = e / half, u = e % half;
+          const int t = (e * m_half) >> 20, u = e - t * half;
           const double ct = cs[t], st = cs[half + t], cu = cs[u], su = cs[half + u];
           if (st == 0.0 && su == 0.0) continue;
           const int pt = pq[t], qt = pq[half + t], pu = pq[u], qu = pq[half + u];
@@ -132,7 +134,7 @@ __global__ void __launch_bounds__(kThreads) jacobi_kernel(const double *a_in, in
           A[qt * ld + qu] = su * r2 + cu * r3;
         } else {
           const int f = e - half * half;
-          const int t = f / n, i = f % n;
+          const int t = (f * m_n) >> 20, i = f - t * n;
           const double c = cs[t], s = cs[half + t];
           if (s == 0.0) continue;
           const int p = pq[t], q = pq[half + t];

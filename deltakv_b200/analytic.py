@@ -178,15 +178,17 @@ def mlp_first_order(x: Tensor, dx: Tensor, gate_w: Tensor, up_w: Tensor, down_w:
 
 def rank_truncate(delta: Tensor, rank: int) -> tuple[Tensor, Tensor]:
     """Δ ≈ codes @ basis.T with ``codes [n, r]``, ``basis [d, r]`` (the best rank-r
-    approximation, analytic.py:14-22).  The propagated ΔX has no spectral gap to exploit, so
-    the basis comes straight from the exact path (fp64 Gram matrix and eigensolver,
-    :func:`deltakv_b200.subspace.gram_basis`) rather than a subspace iteration."""
-    from deltakv_b200.subspace import gram_basis
+    approximation, analytic.py:14-22).  The basis is the top-r subspace of the fp64 Gram
+    matrix ΔᵀΔ from :func:`deltakv_b200.subspace.gram_topr_basis` (device subspace iteration
+    and Rayleigh-Ritz, accepted at an estimated 1e-6 of ‖Δ‖ — the reference's fp32 SVD is
+    itself determined only to ~1e-5 where, as for the propagated ΔX, the singular values at
+    the cut differ by ~1 % — else the exact eigensolver)."""
+    from deltakv_b200.subspace import gram_topr_basis
 
     ops._require_cuda(delta)
     flat = delta.reshape(delta.shape[0], -1).float()
     r = max(1, min(int(rank), *flat.shape))
-    basis = gram_basis(flat, r)
+    basis = gram_topr_basis(flat, r)
     codes = flat @ basis
     return codes.to(delta.dtype), basis.to(delta.dtype)
 

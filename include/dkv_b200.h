@@ -412,6 +412,17 @@ int dkv_rope_rows(float *x, int64_t rows, int32_t heads, int32_t head_dim, int64
 int dkv_sym_eig_batched(const double *a, int64_t batch, int32_t k, int64_t a_stride, int32_t max_sweeps,
                         double *evals, double *evecs, int32_t *info, dkv_stream_t stream);
 
+/* Block subspace iteration on a symmetric positive semi-definite fp64 matrix g [d, d]
+   (row-major, exactly symmetric): `iters` steps of q <- orth(g q) by Cholesky QR, q [d, k]
+   row-major (k <= 96, k <= d) holding the start block on entry and the orthonormal result on
+   return; then, if t is not NULL, t [k, k] = q^T g q (the Rayleigh quotient) and y = g q.
+   Workspace: y [d, k], w [2, k, k] (fp64).  status (device int32, zeroed here) gets bit 0 when
+   a Cholesky pivot is not finite or falls below 1e-12 of the first (the block lost rank);
+   the result is then not usable.  The top-k eigen-subspace of the Gram matrix dX^T dX that
+   stands in for the SVD of rank_truncate (patches/analytic.py:14-22). */
+int dkv_gram_subspace_iterate(const double *g, int32_t d, double *q, int32_t k, int32_t iters, double *y,
+                              double *w, double *t, int32_t *status, dkv_stream_t stream);
+
 /*
  * Subspace correction of a KIVI int4 cache (the multi-adapter maintenance step): for each
  * problem (one layer's K or V of one adapter view), reused = dequant(base), then exactly

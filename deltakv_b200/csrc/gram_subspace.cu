@@ -4,16 +4,15 @@
 // iteration, followed by the Rayleigh quotient T = Q^T G Q for a Rayleigh-Ritz step
 // (Golub & Van Loan, Matrix Computations 4th ed., Sec. 8.2.4).
 //
-//   gq_kernel     Y[rows] = G[rows, :] Q for 8 rows per CTA: Q and the CTA's columns of G
-//                 stream through a 5-deep cp.async ring in 32-row chunks, each warp takes 4
-//                 rows of a chunk into an 8 x 96 register tile (every Q value loaded from
-//                 shared memory feeds 8 FMAs, every G value 3), the warps' tiles are summed,
-//                 then the partial
+//   gq_kernel     Y[rows] = G[rows, :] Q for 4 rows per CTA (a grid over all SMs): Q (each
+//                 32-row chunk one contiguous range) and the CTA's columns of G stream through
+//                 a 5-deep cp.async ring, each warp takes 4 rows of a chunk into a 4 x 96
+//                 register tile, the warps' tiles are summed, then the partial
 //                 product A^T Y of those rows added into W with fp64 atomics (A = Y: the
 //                 upper triangle of Y^T Y; A = Q: all of Q^T G Q)
-//   cholqr_kernel W = U^T D^-1 U (right-looking elimination, the trailing matrix in
-//                 registers, one barrier per pivot) and, in the same loop, the forward
-//                 substitution of this CTA's rows of Y: Q = Y R^-1 with R = D^-1/2 U, so
+//   cholqr_kernel W = U^T D^-1 U (right-looking elimination, the trailing matrix in the
+//                 registers of 16 warps, one barrier per pivot) and, in the same loop, the
+//                 forward substitution of this CTA's 16 rows of Y: Q = Y R^-1 with R = D^-1/2 U, so
 //                 Q^T Q = I; every CTA factors W redundantly
 //
 // G is read by columns (G[j][row], contiguous for a CTA's rows): G must be symmetric.
@@ -22,55 +21,73 @@
 namespace dkv {
 namespace gsi {
 
-constexpr int kRows = 8;     // rows of Y / Q per CTA
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
 constexpr int kMaxK = 96;
-constexpr int kCols = kMaxK / 32;    // columns per lane: lane, lane + 32, lane + 64
-constexpr int kWRows = kMaxK / kWarps;  // rows of W per warp in the factorisation
+constexpr int kCols = kMaxK / 32;  // columns per lane: lane, lane + 32, lane + 64
 
-constexpr int kChunk = 32;   // rows j of Q (and of G's columns) per ring stage
-constexpr int kStages = 5;   // ring depth: ~106 KB of Q / G in flight per CTA
-constexpr int kQStage = kChunk * kMaxK;  // doubles
-constexpr int kGStage = kChunk * kRows;  // doubles: G[j][row0 .. row0 + 7] for the chunk's j
+// ---- gq_kernel: 4 rows of Y per CTA, 8 warps splitting each chunk's rows j ----
+constexpr int kGRows = 4;
+constexpr int kGWarps = 8;
+constexpr int kGThreads = kGWarps * 32;
+constexpr int kGWRows = kMaxK / kGWarps;  // rows a of the partial product per warp
+constexpr int kChunk = 32;                // rows j of Q (and of G's columns) per ring stage
+constexpr int kStages = 5;                // ring depth: ~100 KB of Q / G in flight per CTA
+constexpr int kQStage = kChunk * kMaxK;   // doubles (a chunk is 32 * k contiguous doubles of Q)
+constexpr int kGStage = kChunk * kGRows;  // doubles: G[j][row0 .. row0 + 3] for the chunk's j
 constexpr size_t kGqSmem = static_cast<size_t>(kStages) * (kQStage + kGStage) * sizeof(double);
-static_assert(kGqSmem >= sizeof(double) * kWarps * kRows * kMaxK, "the reduction tiles reuse the ring");
-static_assert(kChunk % kWarps == 0, "each warp takes kChunk / kWarps rows of a chunk");
+static_assert(kGqSmem >= sizeof(double) * kGWarps * kGRows * kMaxK, "the reduction tiles reuse the ring");
+static_assert(kChunk % kGWarps == 0, "each warp takes kChunk / kGWarps rows of a chunk");
 
-template <bool kRayleigh>
-__global__ void __launch_bounds__(kThreads) gq_kernel(const double *__restrict__ g, int d,
-                                                      const double *__restrict__ q, int k,
-                                                      double *__restrict__ y, double *__restrict__ w) {
+// ---- cholqr_kernel: 16 warps, one row of Y each; W rows a = warp + 16 ia ----
+constexpr int kCWarps = 16;
+constexpr int kCThreads = kCWarps * 32;
+constexpr int kCRows = kCWarps;
+constexpr int kCWRows = kMaxK / kCWarps;
+
+template <bool kRayleigh, bool kVec16>
+__global__ void __launch_bounds__(kGThreads) gq_kernel(const double *__restrict__ g, int d,
+                                                       const double *__restrict__ q, int k,
+                                                       double *__restrict__ y, double *__restrict__ w) {
   extern __shared__ double smem_d[];
-  double *qs = smem_d;                     // [kStages][kChunk][kMaxK]
-  double *gs = smem_d + kStages * kQStage;  // [kStages][kChunk][kRows]
+  double *qs = smem_d;                      // [kStages][kChunk * k]
+  double *gs = smem_d + kStages * kQStage;  // [kStages][kChunk][kGRows]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = blockIdx.x * kRows;
-  const int nrows = min(kRows, d - row0);
+  const int row0 = blockIdx.x * kGRows;
+  const int nrows = min(kGRows, d - row0);
   const int n_chunks = (d + kChunk - 1) / kChunk;
 
-  // one chunk: Q rows jbase .. jbase + 31 and G[j][row0 .. row0 + 7] (= G[row0 ..][j]);
-  // out-of-range elements are zero-filled
+  // one chunk: Q rows jbase .. jbase + 31 (one contiguous range of 32 k doubles) and
+  // G[j][row0 .. row0 + 3] (= G[row0 ..][j]); out-of-range elements are zero-filled
   auto issue = [&](int ch) {
     const int st = ch % kStages, jbase = ch * kChunk;
     double *qd = qs + st * kQStage, *gd = gs + st * kGStage;
-    for (int e = threadIdx.x; e < kQStage; e += kThreads) {
-      const int jj = e / kMaxK, c = e - jj * kMaxK, j = jbase + jj;
-      const bool ok = j < d && c < k;
-      cp_async8(qd + e, ok ? q + static_cast<int64_t>(j) * k + c : q, ok ? 8u : 0u);
+    const int nvalid = min(kChunk, d - jbase) * k, ntot = kChunk * k;
+    const double *src = q + static_cast<int64_t>(jbase) * k;
+    if (kVec16) {
+      for (int e = 2 * threadIdx.x; e < ntot; e += 2 * kGThreads) {
+        const bool ok = e < nvalid;
+        cp_async16(qd + e, ok ? src + e : q, ok ? 16u : 0u);
+      }
+    } else {
+      for (int e = threadIdx.x; e < ntot; e += kGThreads) {
+        const bool ok = e < nvalid;
+        cp_async8(qd + e, ok ? src + e : q, ok ? 8u : 0u);
+      }
     }
-    for (int e = threadIdx.x; e < kGStage; e += kThreads) {
-      const int jj = e / kRows, r = e - jj * kRows, j = jbase + jj;
+    for (int e = threadIdx.x; e < kGStage; e += kGThreads) {
+      const int jj = e / kGRows, r = e - jj * kGRows, j = jbase + jj;
       const bool ok = j < d && r < nrows;
       cp_async8(gd + e, ok ? g + static_cast<int64_t>(j) * d + row0 + r : g, ok ? 8u : 0u);
     }
   };
 
-  double acc[kRows][kCols];
+  double acc[kGRows][kCols];
 #pragma unroll
-  for (int r = 0; r < kRows; ++r)
+  for (int r = 0; r < kGRows; ++r)
 #pragma unroll
     for (int i = 0; i < kCols; ++i) acc[r][i] = 0.0;
+  bool colv[kCols];
+#pragma unroll
+  for (int i = 0; i < kCols; ++i) colv[i] = lane + 32 * i < k;
 
 #pragma unroll 1
   for (int st = 0; st < kStages - 1; ++st) {
@@ -86,19 +103,19 @@ __global__ void __launch_bounds__(kThreads) gq_kernel(const double *__restrict__
     __syncthreads();
     const double *qd = qs + (ch % kStages) * kQStage, *gd = gs + (ch % kStages) * kGStage;
 #pragma unroll
-    for (int u = 0; u < kChunk / kWarps; ++u) {
-      const int jj = warp * (kChunk / kWarps) + u;
-      double qv[kCols], gv[kRows];
+    for (int u = 0; u < kChunk / kGWarps; ++u) {
+      const int jj = warp * (kChunk / kGWarps) + u;
+      double qv[kCols], gv[kGRows];
 #pragma unroll
-      for (int i = 0; i < kCols; ++i) qv[i] = qd[jj * kMaxK + lane + 32 * i];
+      for (int i = 0; i < kCols; ++i) qv[i] = colv[i] ? qd[jj * k + lane + 32 * i] : 0.0;
 #pragma unroll
-      for (int r = 0; r < kRows; r += 2) {
-        const double2 two = *reinterpret_cast<const double2 *>(gd + jj * kRows + r);
+      for (int r = 0; r < kGRows; r += 2) {
+        const double2 two = *reinterpret_cast<const double2 *>(gd + jj * kGRows + r);
         gv[r] = two.x;
         gv[r + 1] = two.y;
       }
 #pragma unroll
-      for (int r = 0; r < kRows; ++r)
+      for (int r = 0; r < kGRows; ++r)
 #pragma unroll
         for (int i = 0; i < kCols; ++i) acc[r][i] = fma(gv[r], qv[i], acc[r][i]);
     }
@@ -106,20 +123,20 @@ __global__ void __launch_bounds__(kThreads) gq_kernel(const double *__restrict__
   }
   cp_async_wait<0>();  // only empty groups remain; the ring is reused below
 
-  double(*part)[kRows][kMaxK] = reinterpret_cast<double(*)[kRows][kMaxK]>(smem_d);  // [kWarps]
+  double(*part)[kGRows][kMaxK] = reinterpret_cast<double(*)[kGRows][kMaxK]>(smem_d);  // [kGWarps]
 #pragma unroll
-  for (int r = 0; r < kRows; ++r)
+  for (int r = 0; r < kGRows; ++r)
 #pragma unroll
     for (int i = 0; i < kCols; ++i) part[warp][r][lane + 32 * i] = acc[r][i];
   __syncthreads();
 
   // reduce the warps' tiles; element (r, c) has one owner thread, which alone reads
   // part[*][r][c] and then overwrites part[0][r][c] (Y) and part[1][r][c] (A)
-  for (int o = threadIdx.x; o < kRows * kMaxK; o += kThreads) {
+  for (int o = threadIdx.x; o < kGRows * kMaxK; o += kGThreads) {
     const int r = o / kMaxK, c = o - r * kMaxK;
     double s = 0.0;
 #pragma unroll
-    for (int v = 0; v < kWarps; ++v) s += part[v][r][c];
+    for (int v = 0; v < kGWarps; ++v) s += part[v][r][c];
     const bool live = r < nrows && c < k;
     if (!live) s = 0.0;
     if (live) y[static_cast<int64_t>(row0 + r) * k + c] = s;
@@ -130,18 +147,21 @@ __global__ void __launch_bounds__(kThreads) gq_kernel(const double *__restrict__
 
   const double(*ys)[kMaxK] = part[0];
   const double(*as)[kMaxK] = kRayleigh ? part[1] : part[0];
-#pragma unroll 1
-  for (int ia = 0; ia < kWRows; ++ia) {
-    const int a = warp + kWarps * ia;
-    if (a >= k) break;
+#pragma unroll
+  for (int ia = 0; ia < kGWRows; ++ia) {
+    const int a = warp + kGWarps * ia;
+    double av[kGRows];
+#pragma unroll
+    for (int r = 0; r < kGRows; ++r) av[r] = as[r][a];
 #pragma unroll
     for (int i = 0; i < kCols; ++i) {
       const int b = lane + 32 * i;
-      if (b >= k || (!kRayleigh && b < a)) continue;
-      double s = 0.0;
+      if (a < k && b < k && (kRayleigh || b >= a)) {
+        double s = 0.0;
 #pragma unroll
-      for (int r = 0; r < kRows; ++r) s = fma(as[r][a], ys[r][b], s);
-      atomicAdd(w + static_cast<int64_t>(a) * k + b, s);
+        for (int r = 0; r < kGRows; ++r) s = fma(av[r], ys[r][b], s);
+        atomicAdd(w + static_cast<int64_t>(a) * k + b, s);
+      }
     }
   }
 }
@@ -162,22 +182,22 @@ __device__ __forceinline__ double rsqrt_nr(double a) {
   return y * fma(-0.5 * a * y, y, 1.5);
 }
 
-__global__ void __launch_bounds__(kThreads) cholqr_kernel(const double *__restrict__ w, int k,
-                                                          const double *__restrict__ y, int d,
-                                                          double *__restrict__ q, double *__restrict__ w_clear,
-                                                          int32_t *__restrict__ status) {
+__global__ void __launch_bounds__(kCThreads) cholqr_kernel(const double *__restrict__ w, int k,
+                                                           const double *__restrict__ y, int d,
+                                                           double *__restrict__ q, double *__restrict__ w_clear,
+                                                           int32_t *__restrict__ status) {
   __shared__ double prow[2][kMaxK];  // pivot row of the trailing matrix, double-buffered
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kRows + warp;
+  const int row = blockIdx.x * kCRows + warp;
   const bool live = row < d;
 
-  // element (a, b) = (warp + 8 ia, lane + 32 ib) of the symmetric W (stored: upper triangle)
-  double wr[kWRows][kCols];
+  // element (a, b) = (warp + 16 ia, lane + 32 ib) of the symmetric W (stored: upper triangle)
+  double wr[kCWRows][kCols];
 #pragma unroll
-  for (int ia = 0; ia < kWRows; ++ia)
+  for (int ia = 0; ia < kCWRows; ++ia)
 #pragma unroll
     for (int ib = 0; ib < kCols; ++ib) {
-      const int a = warp + kWarps * ia, b = lane + 32 * ib;
+      const int a = warp + kCWarps * ia, b = lane + 32 * ib;
       wr[ia][ib] = (a < k && b < k) ? w[static_cast<int64_t>(min(a, b)) * k + max(a, b)] : 0.0;
     }
   double yv[kCols], qv[kCols];
@@ -188,7 +208,7 @@ __global__ void __launch_bounds__(kThreads) cholqr_kernel(const double *__restri
     qv[ib] = 0.0;
   }
   if (blockIdx.x == 0)
-    for (int e = threadIdx.x; e < k * k; e += kThreads) w_clear[e] = 0.0;
+    for (int e = threadIdx.x; e < k * k; e += kCThreads) w_clear[e] = 0.0;
   if (warp == 0)
 #pragma unroll
     for (int ib = 0; ib < kCols; ++ib) prow[0][lane + 32 * ib] = wr[0][ib];
@@ -196,16 +216,29 @@ __global__ void __launch_bounds__(kThreads) cholqr_kernel(const double *__restri
 
   const double w00 = prow[0][0];
   bool ok = true;
-  // pivot j = 8 jb + jw: the outer loop is unrolled so that the register rows a pivot touches
+  // pivot j = 16 jb + jw: the outer loop is unrolled so that the register rows a pivot touches
   // (ia >= jb), the row it publishes next (ia = jb or jb + 1) and the lane slot of y_j
-  // (jb / 4) are compile-time indices
+  // (jb / 2) are compile-time indices; the updates are branch-free (rows and columns at or
+  // before the pivot get a zero multiplier) so that every shared-memory load of a step is in
+  // flight at once
 #pragma unroll
-  for (int jb = 0; jb < kWRows; ++jb) {
+  for (int jb = 0; jb < kCWRows; ++jb) {
 #pragma unroll 1
-    for (int jw = 0; jw < kWarps; ++jw) {
-      const int j = kWarps * jb + jw;
+    for (int jw = 0; jw < kCWarps; ++jw) {
+      const int j = kCWarps * jb + jw;
       if (j >= k) break;
       const double *pr = prow[j & 1];
+      double pa[kCWRows], pbr[kCols];
+#pragma unroll
+      for (int ia = jb; ia < kCWRows; ++ia) {
+        const int a = warp + kCWarps * ia;
+        pa[ia] = (a > j && a < k) ? pr[a] : 0.0;
+      }
+#pragma unroll
+      for (int ib = 0; ib < kCols; ++ib) {
+        const int b = lane + 32 * ib;
+        pbr[ib] = (b > j && b < k) ? pr[b] : 0.0;
+      }
       const double piv = pr[j];
       // uniform (every thread reads the same pivot); below 1e-12 of the first the block has
       // lost rank (kappa(Y) > 1e6) and Cholesky QR no longer keeps its span
@@ -216,32 +249,25 @@ __global__ void __launch_bounds__(kThreads) cholqr_kernel(const double *__restri
       const double inv = recip(piv), rs = rsqrt_nr(piv);
       double pb[kCols];
 #pragma unroll
-      for (int ib = 0; ib < kCols; ++ib) {
-        const int b = lane + 32 * ib;
-        pb[ib] = b > j && b < k ? pr[b] * inv : 0.0;
-      }
+      for (int ib = 0; ib < kCols; ++ib) pb[ib] = pbr[ib] * inv;
 #pragma unroll
-      for (int ia = jb; ia < kWRows; ++ia) {
-        const int a = warp + kWarps * ia;
-        if (a > j && a < k) {  // warp-uniform
-          const double pa = pr[a];
+      for (int ia = jb; ia < kCWRows; ++ia)
 #pragma unroll
-          for (int ib = 0; ib < kCols; ++ib) wr[ia][ib] = fma(-pa, pb[ib], wr[ia][ib]);
-        }
-      }
+        for (int ib = 0; ib < kCols; ++ib) wr[ia][ib] = fma(-pa[ia], pb[ib], wr[ia][ib]);
       // forward substitution of this warp's row: q_j = y_j / sqrt(piv), y_c -= (y_j / piv) U_jc
-      const int kSlot = jb / 4;  // j / 32 (jb is a compile-time index after unrolling)
+      const int kSlot = jb / 2;  // j / 32 (jb is a compile-time index after unrolling)
       const double yj = __shfl_sync(0xffffffffu, yv[kSlot], j & 31);
       if (lane == (j & 31)) qv[kSlot] = yj * rs;
 #pragma unroll
       for (int ib = 0; ib < kCols; ++ib) yv[ib] = fma(-yj, pb[ib], yv[ib]);
       // the owner warp of row j + 1 publishes it (already updated by this pivot)
       const int nj = j + 1;
-      if (nj < k && warp == (nj & (kWarps - 1))) {
-        if (jw == kWarps - 1) {
-          if (jb + 1 < kWRows)
+      if (nj < k && warp == (nj & (kCWarps - 1))) {
+        if (jw == kCWarps - 1) {
+          if (jb + 1 < kCWRows)
 #pragma unroll
-            for (int ib = 0; ib < kCols; ++ib) prow[nj & 1][lane + 32 * ib] = wr[jb + 1 < kWRows ? jb + 1 : jb][ib];
+            for (int ib = 0; ib < kCols; ++ib)
+              prow[nj & 1][lane + 32 * ib] = wr[jb + 1 < kCWRows ? jb + 1 : jb][ib];
         } else {
 #pragma unroll
           for (int ib = 0; ib < kCols; ++ib) prow[nj & 1][lane + 32 * ib] = wr[jb][ib];
@@ -263,6 +289,23 @@ __global__ void __launch_bounds__(kThreads) cholqr_kernel(const double *__restri
     }
 }
 
+template <bool kRayleigh, bool kVec16>
+int launch_gq(const double *g, int d, const double *q, int k, double *y, double *w, cudaStream_t s) {
+  // the shared-memory attribute, set once per device for this instantiation (a repeated set
+  // from racing threads is harmless)
+  static unsigned long long set_on = 0;
+  int dev = 0;
+  DKV_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev >= 64 || !((set_on >> dev) & 1ull)) {
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(gq_kernel<kRayleigh, kVec16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(kGqSmem)));
+    if (dev < 64) set_on |= 1ull << dev;
+  }
+  const unsigned grid = static_cast<unsigned>((d + kGRows - 1) / kGRows);
+  gq_kernel<kRayleigh, kVec16><<<grid, kGThreads, kGqSmem, s>>>(g, d, q, k, y, w);
+  return DKV_OK;
+}
+
 }  // namespace gsi
 }  // namespace dkv
 
@@ -273,22 +316,27 @@ extern "C" int dkv_gram_subspace_iterate(const double *g, int32_t d, double *q, 
   if (d <= 0 || k <= 0 || k > gsi::kMaxK || k > d || iters < 0) return DKV_ERR_INVALID_ARGUMENT;
   if (!g || !q || !y || !w || !status) return DKV_ERR_INVALID_ARGUMENT;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const unsigned grid = static_cast<unsigned>((d + gsi::kRows - 1) / gsi::kRows);
+  // 16-byte copies of Q's chunks need 16-byte aligned rows
+  const bool vec16 = (k % 2 == 0) && (reinterpret_cast<uintptr_t>(q) % 16 == 0);
+  auto gq = [&](bool rayleigh, double *acc) {
+    if (rayleigh) return vec16 ? gsi::launch_gq<true, true>(g, d, q, k, y, acc, s)
+                               : gsi::launch_gq<true, false>(g, d, q, k, y, acc, s);
+    return vec16 ? gsi::launch_gq<false, true>(g, d, q, k, y, acc, s) : gsi::launch_gq<false, false>(g, d, q, k, y, acc, s);
+  };
+  const unsigned cgrid = static_cast<unsigned>((d + gsi::kCRows - 1) / gsi::kCRows);
   const size_t kk = static_cast<size_t>(k) * k;
-  DKV_CUDA_CHECK(cudaFuncSetAttribute(gsi::gq_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(gsi::kGqSmem)));
-  DKV_CUDA_CHECK(cudaFuncSetAttribute(gsi::gq_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(gsi::kGqSmem)));
   DKV_CUDA_CHECK(cudaMemsetAsync(status, 0, sizeof(int32_t), s));
   DKV_CUDA_CHECK(cudaMemsetAsync(w, 0, 2 * kk * sizeof(double), s));
   for (int it = 0; it < iters; ++it) {
     double *cur = w + (it & 1) * kk, *nxt = w + ((it + 1) & 1) * kk;
-    gsi::gq_kernel<false><<<grid, gsi::kThreads, gsi::kGqSmem, s>>>(g, d, q, k, y, cur);
-    gsi::cholqr_kernel<<<grid, gsi::kThreads, 0, s>>>(cur, k, y, d, q, nxt, status);
+    const int rc = gq(false, cur);
+    if (rc != DKV_OK) return rc;
+    gsi::cholqr_kernel<<<cgrid, gsi::kCThreads, 0, s>>>(cur, k, y, d, q, nxt, status);
   }
   if (t) {
     DKV_CUDA_CHECK(cudaMemsetAsync(t, 0, kk * sizeof(double), s));
-    gsi::gq_kernel<true><<<grid, gsi::kThreads, gsi::kGqSmem, s>>>(g, d, q, k, y, t);
+    const int rc = gq(true, t);
+    if (rc != DKV_OK) return rc;
   }
   DKV_CUDA_CHECK(cudaGetLastError());
   return DKV_OK;

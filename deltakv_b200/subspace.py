@@ -127,6 +127,7 @@ def gram_basis(x: Tensor, rank: int) -> Tensor:
 
 
 GRAM_TOL = 1e-6  # estimated ||x (P - P_exact)||_F / ||x||_F accepted from the iteration
+gram_launches = 0  # kernels of this library launched by gram_topr_basis so far (a running count)
 
 
 def _eigh_top(c: Tensor, rank: int) -> Tensor:
@@ -158,8 +159,10 @@ def gram_topr_basis(x: Tensor, rank: int, *, oversample: int = 32, iters: int = 
     r = max(1, min(int(rank), m, d))
     xd = x.double()
     c = torch.matmul(xd.transpose(0, 1), xd)
+    global gram_launches
     if d <= MAX_RITZ:
         ev, vec, info = sym_eig(c[None])
+        gram_launches += 1
         if int(info[0].item()) == 0:
             return vec[0, :, :r].to(x.dtype).contiguous()
         return _eigh_top(c, r).to(x.dtype).contiguous()
@@ -175,6 +178,8 @@ def gram_topr_basis(x: Tensor, rank: int, *, oversample: int = 32, iters: int = 
     trace = c.diagonal().sum()
 
     def run(n_it: int):
+        global gram_launches
+        gram_launches += 2 * int(n_it) + 2  # n_it x (G Q, Cholesky QR), the Rayleigh quotient, Jacobi
         rc = L.lib().dkv_gram_subspace_iterate(c.data_ptr(), d, q.data_ptr(), k, int(n_it), y.data_ptr(),
                                                w.data_ptr(), t.data_ptr(), st.data_ptr(), ops.stream_ptr())
         L.check(rc, "dkv_gram_subspace_iterate")

@@ -193,34 +193,84 @@ def rank_truncate(delta: Tensor, rank: int) -> tuple[Tensor, Tensor]:
     return codes.to(delta.dtype), basis.to(delta.dtype)
 
 
+_chain_streams: dict[str, list] = {}
+MAX_CHAIN_STREAMS = 8
+
+
+def _streams_for(device: torch.device, n: int) -> list:
+    key = str(device)
+    have = _chain_streams.setdefault(key, [])
+    while len(have) < min(n, MAX_CHAIN_STREAMS):
+        have.append(torch.cuda.Stream(device))
+    return have
+
+
 def analytic_patches(hidden, delta, model, config) -> dict[int, LowRankKVPatch]:
     """The engine's analytic route (engine.py:377-432): per layer RMSNorm, first-order
     attention (the dense ΔK / ΔV patch), the residual update, first-order SwiGLU on the
     stored post-attention residual, and the rank-``propagator_rank`` truncation of ΔX;
-    ΔX restarts from zero every ``hidden_stride`` layers."""
+    ΔX restarts from zero every ``hidden_stride`` layers.
+
+    The layers between two restarts form a chain that depends on no other chain, so the
+    chains run concurrently, each on its own stream (up to eight), with the same operations in
+    the same order as one layer after another; the truncations of one step of every chain
+    share a single host synchronisation (:func:`deltakv_b200.subspace.gram_topr_finish`)."""
+    from deltakv_b200.subspace import gram_topr_begin, gram_topr_finish
+
     cfg = model.cfg
     seq = int(hidden.seq_len)
     x0 = hidden.layer_in(0)
     ops._require_cuda(x0)
-    dx = torch.zeros(seq, cfg.d_model, dtype=torch.float32, device=x0.device)
+    dev = x0.device
     patches: dict[int, LowRankKVPatch] = {}
+    n_layers = len(model.blocks)
     stride = max(1, int(config.hidden_stride))
     prop_r = max(1, min(int(config.propagator_rank), cfg.d_model, seq))
-    for l, block in enumerate(model.blocks):
-        if l > 0 and l % stride == 0:
-            dx = torch.zeros_like(dx)
-        x = hidden.layer_in(l)
-        xn, dxn = rmsnorm_first_order(x, dx, block.attn_norm.weight, cfg.rms_eps)
-        layer = delta.layers.get(l)
-        dh, dk, dv, _ = attention_first_order(
-            xn, dxn, block.q_proj.weight, block.k_proj.weight, block.v_proj.weight, block.o_proj.weight, layer,
-            n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads, head_dim=cfg.head_dim, rope=model.rope)
-        patches[l] = LowRankKVPatch(layer_idx=l, k_codes=None, k_basis=None, v_codes=None, v_basis=None,
-                                    k_dense=dk, v_dense=dv)
-        dx = dx + dh
-        xm, dxm = rmsnorm_first_order(hidden.layer_mid(l), dx, block.mlp_norm.weight, cfg.rms_eps)
-        dx = dx + mlp_first_order(xm, dxm, block.gate_proj.weight, block.up_proj.weight, block.down_proj.weight,
-                                  layer)
-        codes, basis = rank_truncate(dx, prop_r)
-        dx = codes @ basis.t()
+    chains = [range(s0, min(s0 + stride, n_layers)) for s0 in range(0, n_layers, stride)]
+    cur = torch.cuda.current_stream(dev)
+    half_tables(model.rope, dev)  # fill the per-device RoPE table cache on this stream before forking
+    ops.status_word(dev)
+    streams = [cur] if len(chains) == 1 else _streams_for(dev, len(chains))
+    fork = torch.cuda.Event()
+    fork.record(cur)
+    dx: list[Tensor | None] = [None] * len(chains)
+    for step in range(min(stride, n_layers)):
+        jobs = []
+        for c, chain in enumerate(chains):
+            if step >= len(chain):
+                continue
+            l = chain[step]
+            s = streams[c % len(streams)]
+            with torch.cuda.stream(s):
+                if step == 0:
+                    if s != cur:
+                        s.wait_event(fork)
+                    dx[c] = torch.zeros(seq, cfg.d_model, dtype=torch.float32, device=dev)
+                block = model.blocks[l]
+                layer = delta.layers.get(l)
+                xn, dxn = rmsnorm_first_order(hidden.layer_in(l), dx[c], block.attn_norm.weight, cfg.rms_eps)
+                dh, dk, dv, _ = attention_first_order(
+                    xn, dxn, block.q_proj.weight, block.k_proj.weight, block.v_proj.weight, block.o_proj.weight,
+                    layer, n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads, head_dim=cfg.head_dim, rope=model.rope)
+                patches[l] = LowRankKVPatch(layer_idx=l, k_codes=None, k_basis=None, v_codes=None, v_basis=None,
+                                            k_dense=dk, v_dense=dv)
+                d1 = dx[c] + dh
+                xm, dxm = rmsnorm_first_order(hidden.layer_mid(l), d1, block.mlp_norm.weight, cfg.rms_eps)
+                d2 = (d1 + mlp_first_order(xm, dxm, block.gate_proj.weight, block.up_proj.weight,
+                                           block.down_proj.weight, layer)).float()
+                # rank_truncate(d2, prop_r): codes = d2 @ basis, dX = codes @ basis^T
+                jobs.append((c, s, d2, gram_topr_begin(d2, prop_r)))
+        bases = gram_topr_finish([j for _, _, _, j in jobs])
+        for (c, s, d2, _), basis in zip(jobs, bases):
+            with torch.cuda.stream(s):
+                dx[c] = (d2 @ basis) @ basis.t()
+    if streams[0] is not cur or len(streams) > 1:
+        for s in streams:
+            if s != cur:
+                e = torch.cuda.Event()
+                e.record(s)
+                cur.wait_event(e)
+        for p in patches.values():  # made on the chain streams, used on the caller's
+            p.k_dense.record_stream(cur)
+            p.v_dense.record_stream(cur)
     return patches

@@ -135,6 +135,116 @@ def _eigh_top(c: Tensor, rank: int) -> Tensor:
     return v[:, -rank:].flip(-1)
 
 
+class GramJob:
+    """One :func:`gram_topr_begin` computation in flight on the stream it was issued on."""
+
+    __slots__ = ("x_dtype", "r", "k", "d", "c", "q", "y", "w", "t", "st", "trace", "v", "flags", "stream",
+                 "done", "kind", "iters")
+
+
+def _gram_run(job: GramJob, n_it: int) -> None:
+    """``n_it`` more iteration steps from ``job.q``, the Rayleigh-Ritz step, and the device
+    flags ``[estimate, rate, eigensolver info, breakdown status]`` — no synchronisation."""
+    global gram_launches
+    gram_launches += 2 * int(n_it) + 2  # n_it x (G Q, Cholesky QR), the Rayleigh quotient, Jacobi
+    c, q, r, k = job.c, job.q, job.r, job.k
+    rc = L.lib().dkv_gram_subspace_iterate(c.data_ptr(), job.d, q.data_ptr(), k, int(n_it), job.y.data_ptr(),
+                                           job.w.data_ptr(), job.t.data_ptr(), job.st.data_ptr(), ops.stream_ptr())
+    L.check(rc, "dkv_gram_subspace_iterate")
+    ev, vec, info = sym_eig(job.t[None])
+    ev, vec = ev[0], vec[0]
+    v = torch.matmul(q, vec[:, :r])
+    res = torch.matmul(c, v) - v * ev[:r]
+    est = res.norm() / (ev[r - 1] - ev[r]) * torch.sqrt(ev[r - 1].clamp_min(0.0) / job.trace)
+    rate = ev[k - 1] / ev[r - 1]
+    job.v = v
+    job.flags = torch.stack([est, rate, info[0].double(), job.st[0].double()])
+    job.done = torch.cuda.Event()
+    job.done.record(job.stream)
+
+
+def gram_topr_begin(x: Tensor, rank: int, *, oversample: int = 32, iters: int = 28) -> GramJob:
+    """Issue :func:`gram_topr_basis` for ``x [m, d]`` on the current stream without a host
+    synchronisation; :func:`gram_topr_finish` completes any number of such jobs with one."""
+    ops._require_cuda(x)
+    global gram_launches
+    job = GramJob()
+    m, d = int(x.shape[0]), int(x.shape[1])
+    job.x_dtype, job.d, job.r = x.dtype, d, max(1, min(int(rank), m, d))
+    job.stream = torch.cuda.current_stream(x.device)
+    job.iters = int(iters)
+    job.flags = job.done = job.v = None
+    xd = x.double()
+    job.c = torch.matmul(xd.transpose(0, 1), xd)
+    job.k = min(job.r + oversample, MAX_RITZ)
+    if d <= MAX_RITZ:
+        job.kind = "eig"
+        ev, vec, info = sym_eig(job.c[None])
+        gram_launches += 1
+        job.v = vec[0, :, :job.r]
+        job.flags = info[0].double()[None]
+        job.done = torch.cuda.Event()
+        job.done.record(job.stream)
+        return job
+    if job.k - job.r < 8 or m < job.k:  # too little oversampling, or a Gram matrix of rank < k
+        job.kind = "exact"
+        return job
+    job.kind = "iter"
+    dev = x.device
+    job.q = _start_block(1, d, job.k, dev)[0][0].double().contiguous()
+    job.y = torch.empty(d, job.k, dtype=torch.float64, device=dev)
+    job.w = torch.empty(2, job.k, job.k, dtype=torch.float64, device=dev)
+    job.t = torch.empty(job.k, job.k, dtype=torch.float64, device=dev)
+    job.st = torch.empty(1, dtype=torch.int32, device=dev)
+    job.trace = job.c.diagonal().sum()
+    _gram_run(job, job.iters)
+    return job
+
+
+def gram_topr_finish(jobs: list[GramJob], *, tol: float = GRAM_TOL) -> list[Tensor]:
+    """The bases of ``jobs`` (each ``[d, rank]``, in its job's dtype, produced on its job's
+    stream): one host synchronisation reads every job's flags; a job whose estimate misses
+    ``tol`` continues or takes the exact path on its own stream."""
+    if not jobs:
+        return []
+    cur = torch.cuda.current_stream(jobs[0].c.device)
+    live = [j for j in jobs if j.flags is not None]
+    host: list[list[float]] = []
+    if live:
+        for j in live:
+            if j.stream != cur:
+                cur.wait_event(j.done)
+        flat = torch.cat([j.flags for j in live]).cpu().tolist()
+        pos = 0
+        for j in live:
+            host.append(flat[pos:pos + j.flags.numel()])
+            pos += j.flags.numel()
+    out, it = [], iter(host)
+    for j in jobs:
+        f = next(it) if j.flags is not None else None
+        with torch.cuda.stream(j.stream):
+            out.append(_gram_decide(j, f, tol).to(j.x_dtype).contiguous())
+    return out
+
+
+def _gram_decide(job: GramJob, f, tol: float) -> Tensor:
+    if job.kind == "eig":
+        return job.v if f[0] == 0 else _eigh_top(job.c, job.r)
+    if job.kind == "exact":
+        return _eigh_top(job.c, job.r)
+    est, rate, good = f[0], f[1], f[2] == 0 and f[3] == 0 and f[0] == f[0]  # converged, no breakdown, not NaN
+    if good and 0.0 <= est <= tol:
+        return job.v
+    if good and est < float("inf") and 0.0 < rate < 1.0:
+        more = int(math.ceil(math.log(est / tol) / -math.log(rate))) + 2
+        if more <= 2 * job.iters:
+            _gram_run(job, more)
+            g = job.flags.cpu().tolist()
+            if g[2] == 0 and g[3] == 0 and g[0] == g[0] and 0.0 <= g[0] <= tol:
+                return job.v
+    return _eigh_top(job.c, job.r)
+
+
 def gram_topr_basis(x: Tensor, rank: int, *, oversample: int = 32, iters: int = 28, tol: float = GRAM_TOL) -> Tensor:
     """Leading-``rank`` right singular subspace of ``x [m, d]`` as ``[d, rank]`` (Ritz vectors
     of ``x^T x``, descending) for spectra without a gap at ``rank`` — the analytic route's
@@ -154,55 +264,7 @@ def gram_topr_basis(x: Tensor, rank: int, *, oversample: int = 32, iters: int = 
     values' rate predicts, and failing that (or on a Cholesky breakdown) the exact path (library
     eigensolver on C) is used.  One host synchronisation per decision.  ``d <= 96``: the device
     eigensolver on C directly."""
-    ops._require_cuda(x)
-    m, d = int(x.shape[0]), int(x.shape[1])
-    r = max(1, min(int(rank), m, d))
-    xd = x.double()
-    c = torch.matmul(xd.transpose(0, 1), xd)
-    global gram_launches
-    if d <= MAX_RITZ:
-        ev, vec, info = sym_eig(c[None])
-        gram_launches += 1
-        if int(info[0].item()) == 0:
-            return vec[0, :, :r].to(x.dtype).contiguous()
-        return _eigh_top(c, r).to(x.dtype).contiguous()
-    k = min(r + oversample, MAX_RITZ)
-    if k - r < 8 or m < k:  # too little oversampling, or a Gram matrix of rank < k
-        return _eigh_top(c, r).to(x.dtype).contiguous()
-    dev = x.device
-    q = _start_block(1, d, k, dev)[0][0].double().contiguous()
-    y = torch.empty(d, k, dtype=torch.float64, device=dev)
-    w = torch.empty(2, k, k, dtype=torch.float64, device=dev)
-    t = torch.empty(k, k, dtype=torch.float64, device=dev)
-    st = torch.empty(1, dtype=torch.int32, device=dev)
-    trace = c.diagonal().sum()
-
-    def run(n_it: int):
-        global gram_launches
-        gram_launches += 2 * int(n_it) + 2  # n_it x (G Q, Cholesky QR), the Rayleigh quotient, Jacobi
-        rc = L.lib().dkv_gram_subspace_iterate(c.data_ptr(), d, q.data_ptr(), k, int(n_it), y.data_ptr(),
-                                               w.data_ptr(), t.data_ptr(), st.data_ptr(), ops.stream_ptr())
-        L.check(rc, "dkv_gram_subspace_iterate")
-        ev, vec, info = sym_eig(t[None])
-        ev, vec = ev[0], vec[0]
-        v = torch.matmul(q, vec[:, :r])
-        res = torch.matmul(c, v) - v * ev[:r]
-        est = res.norm() / (ev[r - 1] - ev[r]) * torch.sqrt(ev[r - 1].clamp_min(0.0) / trace)
-        rate = ev[k - 1] / ev[r - 1]
-        f = torch.stack([est, rate, info[0].double(), st[0].double()]).cpu().tolist()
-        good = f[2] == 0 and f[3] == 0 and f[0] == f[0]  # converged eigensolve, no breakdown, not NaN
-        return v, f[0], f[1], good
-
-    v, est, rate, good = run(iters)
-    if good and 0.0 <= est <= tol:
-        return v.to(x.dtype).contiguous()
-    if good and est < float("inf") and 0.0 < rate < 1.0:
-        more = int(math.ceil(math.log(est / tol) / -math.log(rate))) + 2
-        if more <= 2 * iters:
-            v, est, rate, good = run(more)
-            if good and 0.0 <= est <= tol:
-                return v.to(x.dtype).contiguous()
-    return _eigh_top(c, r).to(x.dtype).contiguous()
+    return gram_topr_finish([gram_topr_begin(x, rank, oversample=oversample, iters=iters)], tol=tol)[0]
 
 
 def topr_basis(residual: Tensor, rank: int, *, iters: int = 3, min_iters: int = 2, oversample: int = 8) -> Tensor:

@@ -22,6 +22,9 @@ All arithmetic is fp32 (the reference's model dtype for its toy), on the device.
 
 from __future__ import annotations
 
+import time
+import weakref
+
 import torch
 from torch import Tensor
 
@@ -34,6 +37,26 @@ from deltakv_b200.types import LowRankKVPatch
 def _f32(t: Tensor) -> Tensor:
     t = t.float()
     return t if t.is_contiguous() else t.contiguous()
+
+
+_fused_cache: dict[tuple, tuple] = {}
+
+
+def _fused_rows(ws: tuple, device: torch.device) -> Tensor:
+    """``cat([w.float() for w in ws], 0)`` on ``device``, made once per set of weight tensors
+    (the entry holds weak references: a different or modified tensor misses)."""
+    key = tuple(id(w) for w in ws) + (str(device),)
+    hit = _fused_cache.get(key)
+    if hit is not None:
+        refs, versions, fused = hit
+        if all(r() is w for r, w in zip(refs, ws)) and versions == tuple(w._version for w in ws):
+            return fused
+    if len(_fused_cache) >= 512:
+        _fused_cache.clear()
+    fused = torch.cat([_f32(w.to(device)) for w in ws], dim=0)
+    torch.cuda.current_stream(device).synchronize()  # once per weight set: usable from any stream
+    _fused_cache[key] = (tuple(weakref.ref(w) for w in ws), tuple(w._version for w in ws), fused)
+    return fused
 
 
 def rmsnorm_first_order(x: Tensor, dx: Tensor, weight: Tensor, eps: float) -> tuple[Tensor, Tensor]:
@@ -75,7 +98,8 @@ def _apply(fac, x: Tensor) -> Tensor:
 
 
 def _rope_(x: Tensor, rope) -> None:
-    """In-place RoPE at positions 0..n-1 of a contiguous fp32 ``[n, heads, head_dim]``."""
+    """In-place RoPE at positions 0..n-1 of an fp32 ``[n, heads, head_dim]`` whose rows hold
+    ``heads x head_dim`` contiguous values (any row stride)."""
     n, heads, hd = x.shape
     if n == 0:
         return
@@ -102,6 +126,27 @@ def attention_core(q: Tensor, dq: Tensor, k: Tensor, dk: Tensor, v: Tensor, dv: 
     return ctx, dctx
 
 
+def _attention_core_views(q: Tensor, dq: Tensor, k: Tensor, dk: Tensor, v: Tensor, dv: Tensor, *,
+                          want_ctx: bool) -> tuple[Tensor | None, Tensor]:
+    """:func:`attention_core` on fp32 ``[n, heads, head_dim]`` views with dense rows (head
+    stride ``head_dim``) that share one row stride per group (q, dq / k, dk, v, dv)."""
+    n, H, hd = q.shape
+    Hkv = k.shape[1]
+    grp_q, grp_kv = (q, dq), (k, dk, v, dv)
+    ok = all(t.dtype == torch.float32 and t.stride(2) == 1 and t.stride(1) == hd for t in grp_q + grp_kv)
+    ok = ok and dq.stride(0) == q.stride(0) and all(t.stride(0) == k.stride(0) for t in grp_kv)
+    if not ok:
+        return attention_core(q, dq, k, dk, v, dv, want_ctx=want_ctx)
+    dctx = torch.empty(n, H, hd, dtype=torch.float32, device=q.device)
+    ctx = torch.empty_like(dctx) if want_ctx else None
+    rc = L.lib().dkv_attn_first_order(q.data_ptr(), dq.data_ptr(), q.stride(0), k.data_ptr(), dk.data_ptr(),
+                                      v.data_ptr(), dv.data_ptr(), k.stride(0), ops.dkv_dtype(torch.float32), n, H,
+                                      Hkv, hd, float(hd) ** -0.5, ops.ptr(ctx), dctx.data_ptr(), H * hd,
+                                      ops.stream_ptr())
+    L.check(rc, "dkv_attn_first_order")
+    return ctx, dctx
+
+
 def attention_first_order(x: Tensor, dx: Tensor, q_w: Tensor, k_w: Tensor, v_w: Tensor, o_w: Tensor, layer, *,
                           n_heads: int, n_kv_heads: int, head_dim: int, rope, causal_mask: Tensor | None = None,
                           base_weights: bool = False, return_attn: bool = False):
@@ -111,16 +156,18 @@ def attention_first_order(x: Tensor, dx: Tensor, q_w: Tensor, k_w: Tensor, v_w: 
     n = int(x.shape[0])
     xf, dxf = _f32(x), _f32(dx)
     dev = xf.device
-    w_qkv = torch.cat([_f32(w.to(dev)) for w in (q_w, k_w, v_w)], dim=0)
+    w_qkv = _fused_rows((q_w, k_w, v_w), dev)
     dq_o, dk_o = n_heads * head_dim, n_kv_heads * head_dim
     both = torch.cat([xf, dxf], dim=0) @ w_qkv.t()  # one GEMM for the base and the first-order terms
     base, delta = both[:n], both[n:]
-    q = base[:, :dq_o].reshape(n, n_heads, head_dim).contiguous()
-    k = base[:, dq_o:dq_o + dk_o].reshape(n, n_kv_heads, head_dim).contiguous()
-    v = base[:, dq_o + dk_o:].reshape(n, n_kv_heads, head_dim).contiguous()
-    dq = delta[:, :dq_o].reshape(n, n_heads, head_dim).contiguous()
-    dk = delta[:, dq_o:dq_o + dk_o].reshape(n, n_kv_heads, head_dim).contiguous()
-    dv = delta[:, dq_o + dk_o:].reshape(n, n_kv_heads, head_dim).contiguous()
+    # [n, heads, head_dim] views into the product (row stride = its width): RoPE and the core
+    # take row strides, so nothing is copied out
+    q = base[:, :dq_o].view(n, n_heads, head_dim)
+    k = base[:, dq_o:dq_o + dk_o].view(n, n_kv_heads, head_dim)
+    v = base[:, dq_o + dk_o:].view(n, n_kv_heads, head_dim)
+    dq = delta[:, :dq_o].view(n, n_heads, head_dim)
+    dk = delta[:, dq_o:dq_o + dk_o].view(n, n_kv_heads, head_dim)
+    dv = delta[:, dq_o + dk_o:].view(n, n_kv_heads, head_dim)
     if layer is not None:
         for t, name, heads in ((dq, "q_proj", n_heads), (dk, "k_proj", n_kv_heads), (dv, "v_proj", n_kv_heads)):
             fac = layer.get(name)
@@ -132,10 +179,11 @@ def attention_first_order(x: Tensor, dx: Tensor, q_w: Tensor, k_w: Tensor, v_w: 
     for t in (q, k, dq, dk):
         _rope_(t, rope)
     o_fac = layer.get("o_proj") if layer is not None else None
-    ctx, dctx = attention_core(q, dq, k, dk, v, dv, want_ctx=o_fac is not None or return_attn)
+    ctx, dctx = _attention_core_views(q, dq, k, dk, v, dv, want_ctx=o_fac is not None or return_attn)
     dh = dctx.reshape(n, -1) @ _f32(o_w.to(dev)).t()
     if o_fac is not None:
         dh = dh + _apply(o_fac, ctx.reshape(n, -1))
+    dk, dv = dk.contiguous(), dv.contiguous()  # the patch tensors own their storage
     attn = None
     if return_attn:
         rep = n_heads // n_kv_heads
@@ -153,9 +201,8 @@ def mlp_first_order(x: Tensor, dx: Tensor, gate_w: Tensor, up_w: Tensor, down_w:
     n = int(x.shape[0])
     xf, dxf = _f32(x), _f32(dx)
     dev = xf.device
-    gw, uw = _f32(gate_w.to(dev)), _f32(up_w.to(dev))
-    ff = gw.shape[0]
-    both = torch.cat([xf, dxf], dim=0) @ torch.cat([gw, uw], dim=0).t()
+    ff = int(gate_w.shape[0])
+    both = torch.cat([xf, dxf], dim=0) @ _fused_rows((gate_w, up_w), dev).t()
     g, u = both[:n, :ff].contiguous(), both[:n, ff:].contiguous()
     dg, du = both[n:, :ff].contiguous(), both[n:, ff:].contiguous()
     if layer is not None:
@@ -213,8 +260,10 @@ def analytic_patches(hidden, delta, model, config) -> dict[int, LowRankKVPatch]:
 
     The layers between two restarts form a chain that depends on no other chain, so the
     chains run concurrently, each on its own stream (up to eight), with the same operations in
-    the same order as one layer after another; the truncations of one step of every chain
-    share a single host synchronisation (:func:`deltakv_b200.subspace.gram_topr_finish`)."""
+    the same order as one layer after another.  The host polls the chains' truncations
+    (:func:`deltakv_b200.subspace.gram_topr_begin`, whose acceptance test is read on the host)
+    and issues a chain's next layer as soon as its truncation is decided, while the other
+    chains' kernels run."""
     from deltakv_b200.subspace import gram_topr_begin, gram_topr_finish
 
     cfg = model.cfg
@@ -234,37 +283,44 @@ def analytic_patches(hidden, delta, model, config) -> dict[int, LowRankKVPatch]:
     fork = torch.cuda.Event()
     fork.record(cur)
     dx: list[Tensor | None] = [None] * len(chains)
-    for step in range(min(stride, n_layers)):
-        jobs = []
-        for c, chain in enumerate(chains):
-            if step >= len(chain):
-                continue
-            l = chain[step]
-            s = streams[c % len(streams)]
+
+    def issue(c: int, step: int):
+        l = chains[c][step]
+        s = streams[c % len(streams)]
+        with torch.cuda.stream(s):
+            if step == 0:
+                if s != cur:
+                    s.wait_event(fork)
+                dx[c] = torch.zeros(seq, cfg.d_model, dtype=torch.float32, device=dev)
+            block = model.blocks[l]
+            layer = delta.layers.get(l)
+            xn, dxn = rmsnorm_first_order(hidden.layer_in(l), dx[c], block.attn_norm.weight, cfg.rms_eps)
+            dh, dk, dv, _ = attention_first_order(
+                xn, dxn, block.q_proj.weight, block.k_proj.weight, block.v_proj.weight, block.o_proj.weight,
+                layer, n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads, head_dim=cfg.head_dim, rope=model.rope)
+            patches[l] = LowRankKVPatch(layer_idx=l, k_codes=None, k_basis=None, v_codes=None, v_basis=None,
+                                        k_dense=dk, v_dense=dv)
+            d1 = dx[c] + dh
+            xm, dxm = rmsnorm_first_order(hidden.layer_mid(l), d1, block.mlp_norm.weight, cfg.rms_eps)
+            d2 = (d1 + mlp_first_order(xm, dxm, block.gate_proj.weight, block.up_proj.weight,
+                                       block.down_proj.weight, layer)).float()
+            # rank_truncate(d2, prop_r): codes = d2 @ basis, dX = codes @ basis^T
+            return gram_topr_begin(d2, prop_r), d2, s, step
+
+    pending = {c: issue(c, 0) for c in range(len(chains))}
+    while pending:
+        ready = [c for c, (job, _, _, _) in pending.items() if job.ready()]
+        if not ready:
+            time.sleep(2e-5)
+            continue
+        for c in ready:
+            job, d2, s, step = pending.pop(c)
             with torch.cuda.stream(s):
-                if step == 0:
-                    if s != cur:
-                        s.wait_event(fork)
-                    dx[c] = torch.zeros(seq, cfg.d_model, dtype=torch.float32, device=dev)
-                block = model.blocks[l]
-                layer = delta.layers.get(l)
-                xn, dxn = rmsnorm_first_order(hidden.layer_in(l), dx[c], block.attn_norm.weight, cfg.rms_eps)
-                dh, dk, dv, _ = attention_first_order(
-                    xn, dxn, block.q_proj.weight, block.k_proj.weight, block.v_proj.weight, block.o_proj.weight,
-                    layer, n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads, head_dim=cfg.head_dim, rope=model.rope)
-                patches[l] = LowRankKVPatch(layer_idx=l, k_codes=None, k_basis=None, v_codes=None, v_basis=None,
-                                            k_dense=dk, v_dense=dv)
-                d1 = dx[c] + dh
-                xm, dxm = rmsnorm_first_order(hidden.layer_mid(l), d1, block.mlp_norm.weight, cfg.rms_eps)
-                d2 = (d1 + mlp_first_order(xm, dxm, block.gate_proj.weight, block.up_proj.weight,
-                                           block.down_proj.weight, layer)).float()
-                # rank_truncate(d2, prop_r): codes = d2 @ basis, dX = codes @ basis^T
-                jobs.append((c, s, d2, gram_topr_begin(d2, prop_r)))
-        bases = gram_topr_finish([j for _, _, _, j in jobs])
-        for (c, s, d2, _), basis in zip(jobs, bases):
-            with torch.cuda.stream(s):
+                basis = gram_topr_finish([job])[0]
                 dx[c] = (d2 @ basis) @ basis.t()
-    if streams[0] is not cur or len(streams) > 1:
+            if step + 1 < len(chains[c]):
+                pending[c] = issue(c, step + 1)
+    if len(streams) > 1 or streams[0] is not cur:
         for s in streams:
             if s != cur:
                 e = torch.cuda.Event()

@@ -4,10 +4,11 @@
 // iteration, followed by the Rayleigh quotient T = Q^T G Q for a Rayleigh-Ritz step
 // (Golub & Van Loan, Matrix Computations 4th ed., Sec. 8.2.4).
 //
-//   gq_kernel     Y[rows] = G[rows, :] Q for 4 rows per CTA (a grid over all SMs): Q (each
-//                 32-row chunk one contiguous range) and the CTA's columns of G stream through
-//                 a 5-deep cp.async ring, each warp takes 4 rows of a chunk into a 4 x 96
-//                 register tile, the warps' tiles are summed, then the partial
+//   gq_kernel     Y[rows] = G[rows, :] Q for 4 rows per CTA (a grid over all SMs, for the
+//                 shortest launch): Q (each 32-row chunk one contiguous range) and the CTA's
+//                 columns of G stream through a 5-deep cp.async ring, each warp takes 4 rows
+//                 of a chunk into a 4 x 96 register tile, the warps' tiles are summed, then
+//                 the partial
 //                 product A^T Y of those rows added into W with fp64 atomics (A = Y: the
 //                 upper triangle of Y^T Y; A = Q: all of Q^T G Q)
 //   cholqr_kernel W = U^T D^-1 U (right-looking elimination, the trailing matrix in the
@@ -40,7 +41,8 @@ static_assert(kChunk % kGWarps == 0, "each warp takes kChunk / kGWarps rows of a
 // ---- cholqr_kernel: 16 warps, one row of Y each; W rows a = warp + 16 ia ----
 constexpr int kCWarps = 16;
 constexpr int kCThreads = kCWarps * 32;
-constexpr int kCRows = kCWarps;
+constexpr int kCYRows = 1;  // rows of Y per warp (more lengthen the per-pivot chain)
+constexpr int kCRows = kCWarps * kCYRows;
 constexpr int kCWRows = kMaxK / kCWarps;
 
 template <bool kRayleigh, bool kVec16>
@@ -188,8 +190,7 @@ __global__ void __launch_bounds__(kCThreads) cholqr_kernel(const double *__restr
                                                            int32_t *__restrict__ status) {
   __shared__ double prow[2][kMaxK];  // pivot row of the trailing matrix, double-buffered
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kCRows + warp;
-  const bool live = row < d;
+  const int row0 = blockIdx.x * kCRows + warp * kCYRows;  // this warp's rows
 
   // element (a, b) = (warp + 16 ia, lane + 32 ib) of the symmetric W (stored: upper triangle)
   double wr[kCWRows][kCols];
@@ -200,13 +201,15 @@ __global__ void __launch_bounds__(kCThreads) cholqr_kernel(const double *__restr
       const int a = warp + kCWarps * ia, b = lane + 32 * ib;
       wr[ia][ib] = (a < k && b < k) ? w[static_cast<int64_t>(min(a, b)) * k + max(a, b)] : 0.0;
     }
-  double yv[kCols], qv[kCols];
+  double yv[kCYRows][kCols], qv[kCYRows][kCols];
 #pragma unroll
-  for (int ib = 0; ib < kCols; ++ib) {
-    const int c = lane + 32 * ib;
-    yv[ib] = (live && c < k) ? y[static_cast<int64_t>(row) * k + c] : 0.0;
-    qv[ib] = 0.0;
-  }
+  for (int u = 0; u < kCYRows; ++u)
+#pragma unroll
+    for (int ib = 0; ib < kCols; ++ib) {
+      const int c = lane + 32 * ib;
+      yv[u][ib] = (row0 + u < d && c < k) ? y[static_cast<int64_t>(row0 + u) * k + c] : 0.0;
+      qv[u][ib] = 0.0;
+    }
   if (blockIdx.x == 0)
     for (int e = threadIdx.x; e < k * k; e += kCThreads) w_clear[e] = 0.0;
   if (warp == 0)
@@ -254,12 +257,15 @@ __global__ void __launch_bounds__(kCThreads) cholqr_kernel(const double *__restr
       for (int ia = jb; ia < kCWRows; ++ia)
 #pragma unroll
         for (int ib = 0; ib < kCols; ++ib) wr[ia][ib] = fma(-pa[ia], pb[ib], wr[ia][ib]);
-      // forward substitution of this warp's row: q_j = y_j / sqrt(piv), y_c -= (y_j / piv) U_jc
+      // forward substitution of this warp's rows: q_j = y_j / sqrt(piv), y_c -= (y_j / piv) U_jc
       const int kSlot = jb / 2;  // j / 32 (jb is a compile-time index after unrolling)
-      const double yj = __shfl_sync(0xffffffffu, yv[kSlot], j & 31);
-      if (lane == (j & 31)) qv[kSlot] = yj * rs;
 #pragma unroll
-      for (int ib = 0; ib < kCols; ++ib) yv[ib] = fma(-yj, pb[ib], yv[ib]);
+      for (int u = 0; u < kCYRows; ++u) {
+        const double yj = __shfl_sync(0xffffffffu, yv[u][kSlot], j & 31);
+        if (lane == (j & 31)) qv[u][kSlot] = yj * rs;
+#pragma unroll
+        for (int ib = 0; ib < kCols; ++ib) yv[u][ib] = fma(-yj, pb[ib], yv[u][ib]);
+      }
       // the owner warp of row j + 1 publishes it (already updated by this pivot)
       const int nj = j + 1;
       if (nj < k && warp == (nj & (kCWarps - 1))) {
@@ -281,11 +287,12 @@ __global__ void __launch_bounds__(kCThreads) cholqr_kernel(const double *__restr
     if (threadIdx.x == 0) atomicOr(status, 1);
     return;
   }
-  if (live)
+#pragma unroll
+  for (int u = 0; u < kCYRows; ++u)
 #pragma unroll
     for (int ib = 0; ib < kCols; ++ib) {
       const int c = lane + 32 * ib;
-      if (c < k) q[static_cast<int64_t>(row) * k + c] = qv[ib];
+      if (row0 + u < d && c < k) q[static_cast<int64_t>(row0 + u) * k + c] = qv[u][ib];
     }
 }
 

@@ -141,6 +141,10 @@ class GramJob:
     __slots__ = ("x_dtype", "r", "k", "d", "c", "q", "y", "w", "t", "st", "trace", "v", "flags", "stream",
                  "done", "kind", "iters")
 
+    def ready(self) -> bool:
+        """Whether :func:`gram_topr_finish` would find this job's flags computed (no wait)."""
+        return self.done is None or self.done.query()
+
 
 def _gram_run(job: GramJob, n_it: int) -> None:
     """``n_it`` more iteration steps from ``job.q``, the Rayleigh-Ritz step, and the device

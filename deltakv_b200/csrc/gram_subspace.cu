@@ -4,10 +4,11 @@
 // iteration, followed by the Rayleigh quotient T = Q^T G Q for a Rayleigh-Ritz step
 // (Golub & Van Loan, Matrix Computations 4th ed., Sec. 8.2.4).
 //
-//   gq_kernel     Y[rows] = G[rows, :] Q for 4 rows per CTA (a grid over all SMs, for the
-//                 shortest launch): Q (each 32-row chunk one contiguous range) and the CTA's
-//                 columns of G stream through a 5-deep cp.async ring, each warp takes 4 rows
-//                 of a chunk into a 4 x 96 register tile, the warps' tiles are summed, then
+//   gq_kernel     Y[rows] = G[rows, :] Q for 16 rows per CTA: Q (each 32-row chunk one
+//                 contiguous range) and the CTA's columns of G stream through a 3-deep cp.async
+//                 ring (two CTAs fit an SM, so launches of concurrent callers share SMs), each
+//                 warp takes 4 rows of a chunk into a 16 x 96 register tile (every Q value
+//                 loaded from shared memory feeds 16 FMAs), the warps' tiles are summed, then
 //                 the partial
 //                 product A^T Y of those rows added into W with fp64 atomics (A = Y: the
 //                 upper triangle of Y^T Y; A = Q: all of Q^T G Q)
@@ -25,17 +26,17 @@ namespace gsi {
 constexpr int kMaxK = 96;
 constexpr int kCols = kMaxK / 32;  // columns per lane: lane, lane + 32, lane + 64
 
-// ---- gq_kernel: 4 rows of Y per CTA, 8 warps splitting each chunk's rows j ----
-constexpr int kGRows = 4;
+// ---- gq_kernel: 16 rows of Y per CTA, 8 warps splitting each chunk's rows j ----
+constexpr int kGRows = 16;
 constexpr int kGWarps = 8;
 constexpr int kGThreads = kGWarps * 32;
 constexpr int kGWRows = kMaxK / kGWarps;  // rows a of the partial product per warp
 constexpr int kChunk = 32;                // rows j of Q (and of G's columns) per ring stage
-constexpr int kStages = 5;                // ring depth: ~100 KB of Q / G in flight per CTA
+constexpr int kStages = 3;                // ring depth (86 KB of shared memory: two CTAs per SM)
 constexpr int kQStage = kChunk * kMaxK;   // doubles (a chunk is 32 * k contiguous doubles of Q)
-constexpr int kGStage = kChunk * kGRows;  // doubles: G[j][row0 .. row0 + 3] for the chunk's j
+constexpr int kGStage = kChunk * kGRows;  // doubles: G[j][row0 .. row0 + 15] for the chunk's j
 constexpr size_t kGqSmem = static_cast<size_t>(kStages) * (kQStage + kGStage) * sizeof(double);
-static_assert(kGqSmem >= sizeof(double) * kGWarps * kGRows * kMaxK, "the reduction tiles reuse the ring");
+static_assert(kGqSmem >= sizeof(double) * (kGWarps / 2) * kGRows * kMaxK, "the reduction tiles reuse the ring");
 static_assert(kChunk % kGWarps == 0, "each warp takes kChunk / kGWarps rows of a chunk");
 
 // ---- cholqr_kernel: 16 warps, one row of Y each; W rows a = warp + 16 ia ----
@@ -58,7 +59,7 @@ __global__ void __launch_bounds__(kGThreads) gq_kernel(const double *__restrict_
   const int n_chunks = (d + kChunk - 1) / kChunk;
 
   // one chunk: Q rows jbase .. jbase + 31 (one contiguous range of 32 k doubles) and
-  // G[j][row0 .. row0 + 3] (= G[row0 ..][j]); out-of-range elements are zero-filled
+  // G[j][row0 .. row0 + 15] (= G[row0 ..][j]); out-of-range elements are zero-filled
   auto issue = [&](int ch) {
     const int st = ch % kStages, jbase = ch * kChunk;
     double *qd = qs + st * kQStage, *gd = gs + st * kGStage;
@@ -125,20 +126,30 @@ __global__ void __launch_bounds__(kGThreads) gq_kernel(const double *__restrict_
   }
   cp_async_wait<0>();  // only empty groups remain; the ring is reused below
 
-  double(*part)[kGRows][kMaxK] = reinterpret_cast<double(*)[kGRows][kMaxK]>(smem_d);  // [kGWarps]
+  // the warps' tiles, summed in two rounds through kGWarps / 2 tiles: warps 0-3 store, then
+  // warps 4-7 add theirs to the same positions
+  constexpr int kHalf = kGWarps / 2;
+  double(*part)[kGRows][kMaxK] = reinterpret_cast<double(*)[kGRows][kMaxK]>(smem_d);  // [kHalf]
+  if (warp < kHalf)
 #pragma unroll
-  for (int r = 0; r < kGRows; ++r)
+    for (int r = 0; r < kGRows; ++r)
 #pragma unroll
-    for (int i = 0; i < kCols; ++i) part[warp][r][lane + 32 * i] = acc[r][i];
+      for (int i = 0; i < kCols; ++i) part[warp][r][lane + 32 * i] = acc[r][i];
+  __syncthreads();
+  if (warp >= kHalf)
+#pragma unroll
+    for (int r = 0; r < kGRows; ++r)
+#pragma unroll
+      for (int i = 0; i < kCols; ++i) part[warp - kHalf][r][lane + 32 * i] += acc[r][i];
   __syncthreads();
 
-  // reduce the warps' tiles; element (r, c) has one owner thread, which alone reads
-  // part[*][r][c] and then overwrites part[0][r][c] (Y) and part[1][r][c] (A)
+  // element (r, c) has one owner thread, which alone reads part[*][r][c] and then overwrites
+  // part[0][r][c] (Y) and part[1][r][c] (A)
   for (int o = threadIdx.x; o < kGRows * kMaxK; o += kGThreads) {
     const int r = o / kMaxK, c = o - r * kMaxK;
     double s = 0.0;
 #pragma unroll
-    for (int v = 0; v < kGWarps; ++v) s += part[v][r][c];
+    for (int v = 0; v < kHalf; ++v) s += part[v][r][c];
     const bool live = r < nrows && c < k;
     if (!live) s = 0.0;
     if (live) y[static_cast<int64_t>(row0 + r) * k + c] = s;

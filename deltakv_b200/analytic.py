@@ -242,6 +242,7 @@ def rank_truncate(delta: Tensor, rank: int) -> tuple[Tensor, Tensor]:
 
 _chain_streams: dict[str, list] = {}
 MAX_CHAIN_STREAMS = 8
+USE_GRAPHS = True  # replay analytic_patches' layers as CUDA graphs after the first call
 
 
 def _streams_for(device: torch.device, n: int) -> list:
@@ -250,6 +251,101 @@ def _streams_for(device: torch.device, n: int) -> list:
     while len(have) < min(n, MAX_CHAIN_STREAMS):
         have.append(torch.cuda.Stream(device))
     return have
+
+
+_PROJ = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+
+
+def _layer_body(model, delta, l: int, x_in: Tensor, x_mid: Tensor, dx: Tensor, prop_r: int):
+    """One layer of the engine loop from its stored inputs and the chain's ΔX: the dense ΔK / ΔV
+    patch, the propagated ΔX before truncation, and the issued truncation job."""
+    from deltakv_b200.subspace import gram_topr_begin
+
+    cfg = model.cfg
+    block = model.blocks[l]
+    layer = delta.layers.get(l)
+    xn, dxn = rmsnorm_first_order(x_in, dx, block.attn_norm.weight, cfg.rms_eps)
+    dh, dk, dv, _ = attention_first_order(
+        xn, dxn, block.q_proj.weight, block.k_proj.weight, block.v_proj.weight, block.o_proj.weight,
+        layer, n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads, head_dim=cfg.head_dim, rope=model.rope)
+    d1 = dx + dh
+    xm, dxm = rmsnorm_first_order(x_mid, d1, block.mlp_norm.weight, cfg.rms_eps)
+    d2 = (d1 + mlp_first_order(xm, dxm, block.gate_proj.weight, block.up_proj.weight, block.down_proj.weight,
+                               layer)).float()
+    # rank_truncate(d2, prop_r): codes = d2 @ basis, dX = codes @ basis^T
+    return dk, dv, d2, gram_topr_begin(d2, prop_r)
+
+
+def _signature(model, delta) -> tuple[list, tuple]:
+    """Every tensor and scalar a captured layer bakes in: the tensors (checked by identity and
+    version on each call) and the scalars (LoRA scales, shapes, eps, RoPE tables)."""
+    cfg = model.cfg
+    tensors, scalars = [], [float(cfg.rms_eps), int(cfg.n_heads), int(cfg.n_kv_heads), int(cfg.head_dim),
+                            int(cfg.d_model), id(model.rope)]
+    for l, block in enumerate(model.blocks):
+        for name in ("attn_norm", "mlp_norm") + _PROJ:
+            tensors.append(getattr(block, name).weight)
+        layer = delta.layers.get(l)
+        for name in _PROJ:
+            fac = layer.get(name) if layer is not None else None
+            if fac is not None:
+                tensors += [fac.A, fac.B]
+                scalars.append((l, name, float(getattr(fac, "scale", 1.0))))
+    return tensors, tuple(scalars)
+
+
+class _LayerGraphs:
+    """CUDA graphs of every layer of analytic_patches for one (model, delta, shape)."""
+
+    def __init__(self, model, delta):
+        tensors, self.scalars = _signature(model, delta)
+        self.refs = [weakref.ref(t) for t in tensors]
+        self.versions = [t._version for t in tensors]
+        self.layers: dict[int, dict] = {}
+        self.keep: list = []
+
+    def valid(self, model, delta) -> bool:
+        tensors, scalars = _signature(model, delta)
+        return (scalars == self.scalars and len(tensors) == len(self.refs)
+                and all(r() is t and t._version == v for r, t, v in zip(self.refs, tensors, self.versions)))
+
+
+_graph_sets: dict[tuple, object] = {}
+
+
+def _capture(model, delta, hidden, chains, streams, prop_r, dev) -> _LayerGraphs | None:
+    """Capture one graph per layer (each chain's layers in order on its stream): the layer's
+    inputs are static buffers, step 0 starts from ΔX = 0 and step t > 0 from the previous
+    layer's static ΔX and decided basis (``codes @ basis^T``)."""
+    from deltakv_b200.subspace import _start_block
+
+    gs = _LayerGraphs(model, delta)
+    seq, d = int(hidden.seq_len), int(model.cfg.d_model)
+    for c, chain in enumerate(chains):
+        s = streams[c % len(streams)]
+        prev = None
+        for t, l in enumerate(chain):
+            rec = {"x_in": torch.empty_like(hidden.layer_in(l), dtype=torch.float32),
+                   "x_mid": torch.empty_like(hidden.layer_mid(l), dtype=torch.float32),
+                   "basis": torch.zeros(d, prop_r, dtype=torch.float32, device=dev)}
+            rec["x_in"].copy_(hidden.layer_in(l))
+            rec["x_mid"].copy_(hidden.layer_mid(l))
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                if prev is None:
+                    dx = torch.zeros(seq, d, dtype=torch.float32, device=dev)
+                else:
+                    dx = (prev["d2"] @ prev["basis"]) @ prev["basis"].t()
+                dk, dv, d2, job = _layer_body(model, delta, l, rec["x_in"], rec["x_mid"], dx, prop_r)
+            if job.kind not in ("iter", "eig"):
+                return None
+            if job.kind == "iter":
+                gs.keep.append(_start_block(1, d, job.k, dev))
+            rec.update(graph=g, dk=dk, dv=dv, d2=d2, job=job, v=job.v, flags=job.flags)
+            gs.layers[l] = rec
+            prev = rec
+    torch.cuda.synchronize(dev)
+    return gs
 
 
 def analytic_patches(hidden, delta, model, config) -> dict[int, LowRankKVPatch]:
@@ -263,8 +359,10 @@ def analytic_patches(hidden, delta, model, config) -> dict[int, LowRankKVPatch]:
     the same order as one layer after another.  The host polls the chains' truncations
     (:func:`deltakv_b200.subspace.gram_topr_begin`, whose acceptance test is read on the host)
     and issues a chain's next layer as soon as its truncation is decided, while the other
-    chains' kernels run."""
-    from deltakv_b200.subspace import gram_topr_begin, gram_topr_finish
+    chains' kernels run.  From the second call with the same model, delta and shape on, each
+    layer is one CUDA graph replay (captured after the first call; re-captured when a weight,
+    factor or scale changes), so the host issues a handful of operations per layer."""
+    from deltakv_b200.subspace import gram_topr_finish
 
     cfg = model.cfg
     seq = int(hidden.seq_len)
@@ -279,33 +377,37 @@ def analytic_patches(hidden, delta, model, config) -> dict[int, LowRankKVPatch]:
     cur = torch.cuda.current_stream(dev)
     half_tables(model.rope, dev)  # fill the per-device RoPE table cache on this stream before forking
     ops.status_word(dev)
-    streams = [cur] if len(chains) == 1 else _streams_for(dev, len(chains))
+    streams = _streams_for(dev, len(chains))  # side streams (a graph cannot be captured on the default one)
     fork = torch.cuda.Event()
     fork.record(cur)
+    key = (id(model), id(delta), seq, str(dev), stride, prop_r, n_layers, id(streams[0]))
+    gs = _graph_sets.get(key) if USE_GRAPHS else None
+    if gs is not None and not (gs and gs.valid(model, delta)):
+        if gs:  # stale: a weight, factor or scale changed
+            _graph_sets.pop(key, None)
+        gs = None
     dx: list[Tensor | None] = [None] * len(chains)
 
     def issue(c: int, step: int):
         l = chains[c][step]
         s = streams[c % len(streams)]
         with torch.cuda.stream(s):
+            if step == 0 and s != cur:
+                s.wait_event(fork)
+            if gs is not None:
+                rec = gs.layers[l]
+                rec["x_in"].copy_(hidden.layer_in(l))
+                rec["x_mid"].copy_(hidden.layer_mid(l))
+                rec["graph"].replay()
+                job = rec["job"]
+                job.v, job.flags, job.stream = rec["v"], rec["flags"], s
+                job.done = torch.cuda.Event()
+                job.done.record(s)
+                return job, rec, s, step
             if step == 0:
-                if s != cur:
-                    s.wait_event(fork)
                 dx[c] = torch.zeros(seq, cfg.d_model, dtype=torch.float32, device=dev)
-            block = model.blocks[l]
-            layer = delta.layers.get(l)
-            xn, dxn = rmsnorm_first_order(hidden.layer_in(l), dx[c], block.attn_norm.weight, cfg.rms_eps)
-            dh, dk, dv, _ = attention_first_order(
-                xn, dxn, block.q_proj.weight, block.k_proj.weight, block.v_proj.weight, block.o_proj.weight,
-                layer, n_heads=cfg.n_heads, n_kv_heads=cfg.n_kv_heads, head_dim=cfg.head_dim, rope=model.rope)
-            patches[l] = LowRankKVPatch(layer_idx=l, k_codes=None, k_basis=None, v_codes=None, v_basis=None,
-                                        k_dense=dk, v_dense=dv)
-            d1 = dx[c] + dh
-            xm, dxm = rmsnorm_first_order(hidden.layer_mid(l), d1, block.mlp_norm.weight, cfg.rms_eps)
-            d2 = (d1 + mlp_first_order(xm, dxm, block.gate_proj.weight, block.up_proj.weight,
-                                       block.down_proj.weight, layer)).float()
-            # rank_truncate(d2, prop_r): codes = d2 @ basis, dX = codes @ basis^T
-            return gram_topr_begin(d2, prop_r), d2, s, step
+            dk, dv, d2, job = _layer_body(model, delta, l, hidden.layer_in(l), hidden.layer_mid(l), dx[c], prop_r)
+            return job, {"dk": dk, "dv": dv, "d2": d2}, s, step
 
     pending = {c: issue(c, 0) for c in range(len(chains))}
     while pending:
@@ -314,13 +416,21 @@ def analytic_patches(hidden, delta, model, config) -> dict[int, LowRankKVPatch]:
             time.sleep(2e-5)
             continue
         for c in ready:
-            job, d2, s, step = pending.pop(c)
+            job, rec, s, step = pending.pop(c)
+            l = chains[c][step]
             with torch.cuda.stream(s):
                 basis = gram_topr_finish([job])[0]
-                dx[c] = (d2 @ basis) @ basis.t()
+                if gs is not None:
+                    rec["basis"].copy_(basis)  # read by the next layer's graph
+                    dk, dv = rec["dk"].clone(), rec["dv"].clone()
+                else:
+                    dx[c] = (rec["d2"] @ basis) @ basis.t()
+                    dk, dv = rec["dk"], rec["dv"]
+            patches[l] = LowRankKVPatch(layer_idx=l, k_codes=None, k_basis=None, v_codes=None, v_basis=None,
+                                        k_dense=dk, v_dense=dv)
             if step + 1 < len(chains[c]):
                 pending[c] = issue(c, step + 1)
-    if len(streams) > 1 or streams[0] is not cur:
+    if any(s != cur for s in streams):
         for s in streams:
             if s != cur:
                 e = torch.cuda.Event()
@@ -329,4 +439,9 @@ def analytic_patches(hidden, delta, model, config) -> dict[int, LowRankKVPatch]:
         for p in patches.values():  # made on the chain streams, used on the caller's
             p.k_dense.record_stream(cur)
             p.v_dense.record_stream(cur)
+    if USE_GRAPHS and key not in _graph_sets:
+        try:
+            _graph_sets[key] = _capture(model, delta, hidden, chains, streams, prop_r, dev) or False
+        except RuntimeError:
+            _graph_sets[key] = False  # not capturable here: stay on the eager path
     return patches

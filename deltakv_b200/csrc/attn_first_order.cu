@@ -427,8 +427,14 @@ int launch(const Args &a, cudaStream_t st) {
   dim3 grid(static_cast<unsigned>((a.n + kRows - 1) / kRows), static_cast<unsigned>(a.n_heads));
 #define DKV_AFO(HD)                                                                                   \
   if (a.hd == HD) {                                                                                   \
-    DKV_CUDA_CHECK(cudaFuncSetAttribute(afo_kernel<DT, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                        smem_bytes<HD>()));                                           \
+    static unsigned long long set_on = 0; /* the attribute once per device: later launches make */  \
+    int dev = 0;                          /* no other runtime-API call (graph-capturable)          */  \
+    DKV_CUDA_CHECK(cudaGetDevice(&dev));                                                              \
+    if (dev >= 64 || !((set_on >> dev) & 1ull)) {                                                     \
+      DKV_CUDA_CHECK(cudaFuncSetAttribute(afo_kernel<DT, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                          smem_bytes<HD>()));                                         \
+      if (dev < 64) set_on |= 1ull << dev;                                                            \
+    }                                                                                                 \
     afo_kernel<DT, HD><<<grid, kThreads, smem_bytes<HD>(), st>>>(a);                                  \
     DKV_CUDA_CHECK(cudaGetLastError());                                                               \
     return DKV_OK;                                                                                    \
@@ -438,8 +444,14 @@ int launch(const Args &a, cudaStream_t st) {
 #undef DKV_AFO
 #define DKV_AFO_TC(HD)                                                                                   \
   if (a.hd == HD) {                                                                                      \
-    DKV_CUDA_CHECK(cudaFuncSetAttribute(afo_tc_kernel<DT, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                        TcLayout<HD>::bytes()));                                         \
+    static unsigned long long set_on = 0; /* the attribute once per device (as above) */               \
+    int dev = 0;                                                                                         \
+    DKV_CUDA_CHECK(cudaGetDevice(&dev));                                                                 \
+    if (dev >= 64 || !((set_on >> dev) & 1ull)) {                                                        \
+      DKV_CUDA_CHECK(cudaFuncSetAttribute(afo_tc_kernel<DT, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                          TcLayout<HD>::bytes()));                                       \
+      if (dev < 64) set_on |= 1ull << dev;                                                               \
+    }                                                                                                    \
     afo_tc_kernel<DT, HD><<<grid, kThreads, TcLayout<HD>::bytes(), st>>>(a);                              \
     DKV_CUDA_CHECK(cudaGetLastError());                                                                  \
     return DKV_OK;                                                                                       \

@@ -14,8 +14,9 @@
 //                 upper triangle of Y^T Y; A = Q: all of Q^T G Q)
 //   cholqr_kernel W = U^T D^-1 U (right-looking elimination, the trailing matrix in the
 //                 registers of 16 warps, one barrier per pivot) and, in the same loop, the
-//                 forward substitution of this CTA's 16 rows of Y: Q = Y R^-1 with R = D^-1/2 U, so
-//                 Q^T Q = I; every CTA factors W redundantly
+//                 forward substitution of this CTA's 64 rows of Y: Q = Y R^-1 with R = D^-1/2 U, so
+//                 Q^T Q = I; every CTA factors W redundantly (64 rows per CTA keep the
+//                 redundant work, and the SMs a launch holds, small)
 //
 // G is read by columns (G[j][row], contiguous for a CTA's rows): G must be symmetric.
 #include "dkv_common.cuh"
@@ -39,10 +40,10 @@ constexpr size_t kGqSmem = static_cast<size_t>(kStages) * (kQStage + kGStage) * 
 static_assert(kGqSmem >= sizeof(double) * (kGWarps / 2) * kGRows * kMaxK, "the reduction tiles reuse the ring");
 static_assert(kChunk % kGWarps == 0, "each warp takes kChunk / kGWarps rows of a chunk");
 
-// ---- cholqr_kernel: 16 warps, one row of Y each; W rows a = warp + 16 ia ----
+// ---- cholqr_kernel: 16 warps, four rows of Y each; W rows a = warp + 16 ia ----
 constexpr int kCWarps = 16;
 constexpr int kCThreads = kCWarps * 32;
-constexpr int kCYRows = 1;  // rows of Y per warp (more lengthen the per-pivot chain)
+constexpr int kCYRows = 4;  // rows of Y per warp: few CTAs factor W redundantly (SM time)
 constexpr int kCRows = kCWarps * kCYRows;
 constexpr int kCWRows = kMaxK / kCWarps;
 

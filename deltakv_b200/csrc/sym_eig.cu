@@ -189,7 +189,14 @@ extern "C" int dkv_sym_eig_batched(const double *a, int64_t batch, int32_t k, in
                       static_cast<size_t>(n) * sizeof(int);
   const int smem_max = static_cast<int>((2 * eig::kMaxN * (eig::kMaxN + 1) + eig::kMaxN + eig::kThreads / 32) *
                                         sizeof(double) + eig::kMaxN * sizeof(int));
-  DKV_CUDA_CHECK(cudaFuncSetAttribute(eig::jacobi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
+  // set once per device (no runtime-API call on later launches, so they can be graph-captured)
+  static unsigned long long set_on = 0;
+  int dev = 0;
+  DKV_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev >= 64 || !((set_on >> dev) & 1ull)) {
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(eig::jacobi_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max));
+    if (dev < 64) set_on |= 1ull << dev;
+  }
   eig::jacobi_kernel<<<static_cast<unsigned>(batch), eig::kThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       a, a_stride, k, n, max_sweeps, evals, evecs, info);
   DKV_CUDA_CHECK(cudaGetLastError());

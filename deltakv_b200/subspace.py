@@ -103,8 +103,9 @@ def _start_block(n_b: int, d: int, k: int, device: torch.device) -> tuple[Tensor
         torch.cuda.current_stream(device).synchronize()  # once per shape: usable from any stream
         _start_cache[key] = hit
     cur = torch.cuda.current_stream(device)
-    for t in hit:
-        t.record_stream(cur)  # kept from reuse until this stream's work is done, if evicted
+    if not torch.cuda.is_current_stream_capturing():  # a graph holds its own reference instead
+        for t in hit:
+            t.record_stream(cur)  # kept from reuse until this stream's work is done, if evicted
     return hit
 
 
@@ -163,8 +164,10 @@ def _gram_run(job: GramJob, n_it: int) -> None:
     rate = ev[k - 1] / ev[r - 1]
     job.v = v
     job.flags = torch.stack([est, rate, info[0].double(), job.st[0].double()])
-    job.done = torch.cuda.Event()
-    job.done.record(job.stream)
+    job.done = None
+    if not torch.cuda.is_current_stream_capturing():  # a replayed graph's caller records it
+        job.done = torch.cuda.Event()
+        job.done.record(job.stream)
 
 
 def gram_topr_begin(x: Tensor, rank: int, *, oversample: int = 32, iters: int = 28) -> GramJob:
@@ -187,8 +190,9 @@ def gram_topr_begin(x: Tensor, rank: int, *, oversample: int = 32, iters: int = 
         gram_launches += 1
         job.v = vec[0, :, :job.r]
         job.flags = info[0].double()[None]
-        job.done = torch.cuda.Event()
-        job.done.record(job.stream)
+        if not torch.cuda.is_current_stream_capturing():
+            job.done = torch.cuda.Event()
+            job.done.record(job.stream)
         return job
     if job.k - job.r < 8 or m < job.k:  # too little oversampling, or a Gram matrix of rank < k
         job.kind = "exact"

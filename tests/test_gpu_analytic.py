@@ -81,6 +81,46 @@ def test_engine_loop_matches_reference(cuda):
         assert rel(patches[l].v_dense.cpu(), g["dv"][l]) < 1e-4, l
 
 
+def test_engine_loop_replays_as_graphs_and_recaptures(cuda, monkeypatch):
+    # after the first call each layer is a CUDA graph replay: the same patches as the eager path
+    # (to the atomics' summation order) for this and another sequence; an in-place weight
+    # update is detected and re-captured
+    g, W, Ls, cfg = load()
+    model = _model(W, cfg, cuda)
+    h = [torch.from_numpy(x).to(cuda) for x in g["h"]]
+    hm = [torch.from_numpy(x).to(cuda) for x in g["h_mid"]]
+    snap = lambda hh, mm: types.SimpleNamespace(layer_in=lambda l: hh[l], layer_mid=lambda l: mm[l],
+                                                seq_len=hh[0].shape[0])
+    delta = types.SimpleNamespace(layers=_layers(Ls, cuda))
+    conf = types.SimpleNamespace(hidden_stride=cfg["hidden_stride"], propagator_rank=cfg["propagator_rank"])
+    other = snap([x * 0.5 + 0.1 for x in h], [x.flip(0) for x in hm])
+
+    def eager(hidden):
+        monkeypatch.setattr(A, "USE_GRAPHS", False)
+        out = A.analytic_patches(hidden, delta, model, conf)
+        monkeypatch.setattr(A, "USE_GRAPHS", True)
+        return out
+
+    A.analytic_patches(snap(h, hm), delta, model, conf)  # eager, then captured
+    sets = [v for k, v in A._graph_sets.items() if k[0] == id(model) and k[1] == id(delta)]
+    assert sets and sets[0], "the layers were not captured"
+    for hidden in (snap(h, hm), other):
+        want, got = eager(hidden), A.analytic_patches(hidden, delta, model, conf)
+        for l in range(len(W)):
+            assert rel(got[l].k_dense.cpu(), want[l].k_dense.cpu()) < 1e-6, l
+            assert rel(got[l].v_dense.cpu(), want[l].v_dense.cpu()) < 1e-6, l
+    replayed = A.analytic_patches(snap(h, hm), delta, model, conf)
+    for l in range(len(W)):
+        assert rel(replayed[l].k_dense.cpu(), g["dk"][l]) < 1e-4, l
+    model.blocks[0].q_proj.weight.mul_(1.01)
+    want, got = eager(snap(h, hm)), A.analytic_patches(snap(h, hm), delta, model, conf)
+    for l in range(len(W)):
+        assert rel(got[l].k_dense.cpu(), want[l].k_dense.cpu()) < 1e-6, l
+    after = A.analytic_patches(snap(h, hm), delta, model, conf)  # the re-captured graphs
+    for l in range(len(W)):
+        assert rel(after[l].v_dense.cpu(), want[l].v_dense.cpu()) < 1e-6, l
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("n,H,Hkv,hd", [(300, 8, 2, 64), (129, 4, 4, 128), (70, 6, 3, 32), (33, 2, 1, 16)])
 def test_attention_core_matches_oracle(cuda, dtype, n, H, Hkv, hd):

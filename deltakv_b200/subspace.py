@@ -209,12 +209,13 @@ def gram_topr_begin(x: Tensor, rank: int, *, oversample: int = 32, iters: int = 
     return job
 
 
-def gram_topr_finish(jobs: list[GramJob], *, tol: float = GRAM_TOL) -> list[Tensor]:
+def gram_topr_finish(jobs: list[GramJob], *, tol: float | None = None) -> list[Tensor]:
     """The bases of ``jobs`` (each ``[d, rank]``, in its job's dtype, produced on its job's
     stream): one host synchronisation reads every job's flags; a job whose estimate misses
-    ``tol`` continues or takes the exact path on its own stream."""
+    ``tol`` (default :data:`GRAM_TOL`) continues or takes the exact path on its own stream."""
     if not jobs:
         return []
+    tol = GRAM_TOL if tol is None else float(tol)
     cur = torch.cuda.current_stream(jobs[0].c.device)
     live = [j for j in jobs if j.flags is not None]
     host: list[list[float]] = []
@@ -253,7 +254,8 @@ def _gram_decide(job: GramJob, f, tol: float) -> Tensor:
     return _eigh_top(job.c, job.r)
 
 
-def gram_topr_basis(x: Tensor, rank: int, *, oversample: int = 32, iters: int = 28, tol: float = GRAM_TOL) -> Tensor:
+def gram_topr_basis(x: Tensor, rank: int, *, oversample: int = 32, iters: int = 28,
+                    tol: float | None = None) -> Tensor:
     """Leading-``rank`` right singular subspace of ``x [m, d]`` as ``[d, rank]`` (Ritz vectors
     of ``x^T x``, descending) for spectra without a gap at ``rank`` — the analytic route's
     propagated dX, whose singular values at the cut differ by ~1 % (rank_truncate,

@@ -170,3 +170,80 @@ def test_gram_topr_basis_degenerate_and_zero_inputs(cuda):
     assert abs(np.linalg.norm(x64 - x64 @ b @ b.T) - best) <= 1e-5 * best
     z = gram_topr_basis(torch.zeros(400, 200, device=cuda), 16)
     assert z.shape == (200, 16) and torch.isfinite(z).all()
+
+
+def _gapless(cuda, seed=11):
+    d = 576
+    s = np.interp(np.arange(d), _PROFILE_AT, _PROFILE)
+    x = _with_spectrum(2048, d, s, seed)
+    return x, torch.from_numpy(x).to(cuda)
+
+
+def test_gram_topr_basis_continues_by_the_predicted_steps(cuda, monkeypatch):
+    # on this spectrum (subspace rate ~0.3 per step) 7 steps leave an estimate near 4e-4; the
+    # Ritz values' rate predicts ~8 more, within twice the budget: one continuation, no exact
+    # eigensolver, the same accuracy
+    import deltakv_b200.subspace as S
+
+    runs, exact = [], []
+    orig_run, orig_exact = S._gram_run, S._eigh_top
+    monkeypatch.setattr(S, "_gram_run", lambda job, n: runs.append(n) or orig_run(job, n))
+    monkeypatch.setattr(S, "_eigh_top", lambda c, r: exact.append(1) or orig_exact(c, r))
+    x, xd = _gapless(cuda)
+    b = S.gram_topr_basis(xd, 64, iters=7).cpu().numpy()
+    assert len(runs) == 2 and runs[0] == 7 and 0 < runs[1] <= 14 and not exact, runs
+    assert _trunc_err(x, b, 64) <= 1e-6
+
+
+def test_gram_topr_basis_falls_back_when_the_prediction_is_too_long(cuda, monkeypatch):
+    # 2 steps: the predicted continuation (~11) exceeds twice the budget, the exact path is taken
+    import deltakv_b200.subspace as S
+
+    exact = []
+    orig_exact = S._eigh_top
+    monkeypatch.setattr(S, "_eigh_top", lambda c, r: exact.append(1) or orig_exact(c, r))
+    x, xd = _gapless(cuda)
+    b = S.gram_topr_basis(xd, 64, iters=2).cpu().numpy()
+    assert exact == [1]
+    assert _trunc_err(x, b, 64) <= 1e-7  # the exact basis, rounded to fp32
+
+
+def test_analytic_loop_graphs_survive_fallbacks(cuda, monkeypatch):
+    # a tolerance no estimate meets: every truncation continues then takes the exact path, in
+    # the eager call and in graph replays; the replays' captured flags are restored each time
+    import types
+
+    import deltakv_b200.analytic as A
+    import deltakv_b200.subspace as S
+    from deltakv_b200.rope import RotaryEmbedding
+
+    g = torch.Generator(device=cuda).manual_seed(5)
+    d, dff, H, Hkv, hd, n, L_ = 128, 256, 4, 2, 32, 256, 4
+    rnd = lambda *s_, sc=0.05: torch.randn(*s_, generator=g, device=cuda) * sc
+    mod = lambda w: types.SimpleNamespace(weight=w)
+    blocks = [types.SimpleNamespace(attn_norm=mod(1 + rnd(d)), mlp_norm=mod(1 + rnd(d)), q_proj=mod(rnd(H * hd, d)),
+                                    k_proj=mod(rnd(Hkv * hd, d)), v_proj=mod(rnd(Hkv * hd, d)),
+                                    o_proj=mod(rnd(d, H * hd)), gate_proj=mod(rnd(dff, d)), up_proj=mod(rnd(dff, d)),
+                                    down_proj=mod(rnd(d, dff))) for _ in range(L_)]
+    cfg = types.SimpleNamespace(n_heads=H, n_kv_heads=Hkv, head_dim=hd, d_model=d, rms_eps=1e-5)
+    model = types.SimpleNamespace(cfg=cfg, blocks=blocks, rope=RotaryEmbedding(hd, max_seq=n, base=10000.0))
+    from deltakv_b200.types import LayerDelta, LowRankFactors
+
+    lora = lambda fin, fout: LowRankFactors(A=rnd(4, fin, sc=fin ** -0.5), B=rnd(fout, 4, sc=1.0), scale=0.05)
+    delta = types.SimpleNamespace(layers={l: LayerDelta(layer_idx=l, projections={
+        "q_proj": lora(d, H * hd), "k_proj": lora(d, Hkv * hd), "v_proj": lora(d, Hkv * hd),
+        "o_proj": lora(H * hd, d)}) for l in range(L_)})
+    conf = types.SimpleNamespace(hidden_stride=2, propagator_rank=16)
+    h = [torch.randn(n, d, generator=g, device=cuda) for _ in range(L_)]
+    hm = [torch.randn(n, d, generator=g, device=cuda) for _ in range(L_)]
+    hidden = types.SimpleNamespace(layer_in=lambda l: h[l], layer_mid=lambda l: hm[l], seq_len=n)
+    monkeypatch.setattr(A, "USE_GRAPHS", False)
+    want = A.analytic_patches(hidden, delta, model, conf)
+    monkeypatch.setattr(A, "USE_GRAPHS", True)
+    monkeypatch.setattr(S, "GRAM_TOL", 1e-300)
+    for _ in range(3):  # eager + capture, then two replays
+        got = A.analytic_patches(hidden, delta, model, conf)
+        for l in range(L_):
+            assert want[l].k_dense.norm() > 0 and want[l].v_dense.norm() > 0
+            assert ((got[l].k_dense - want[l].k_dense).norm() / want[l].k_dense.norm()).item() < 1e-5, l
+            assert ((got[l].v_dense - want[l].v_dense).norm() / want[l].v_dense.norm()).item() < 1e-5, l

@@ -35,6 +35,7 @@ struct Args {
   int64_t out_row;
   int n, n_heads, n_kv, hd;
   float scale;
+  int kv_vec;  // fp32 K / dK / V / dV with 16-byte aligned rows: staged as float4, one block ahead
 };
 
 // SIMT form.  One pass over the causal keys with online softmax.  Thread (ty, tx) = (tid / 16, tid % 16)
@@ -271,9 +272,53 @@ __global__ void __launch_bounds__(kThreads, 1) afo_tc_kernel(const Args a) {
   const int a_row = 16 * rg + (lane & 15), a_col = (lane >> 4) * 8;                 // A: rows x k
   const int b_key = (lane & 7) + ((lane >> 4) << 3), b_col = ((lane >> 3) & 1) * 8;  // B from K rows
   const int v_key = (lane & 7) + (((lane >> 3) & 1) << 3), v_col = (lane >> 4) * 8;  // B from V rows (trans)
+  // fp32 inputs with 16-byte rows: each thread holds NV float4 of K, dK, V and dV of the next
+  // key block in registers, loaded before the current block's products and split into the
+  // shared tiles after them, so the global loads overlap the tensor-core work
+  // (head_dim <= 64: at 128 the four register blocks would not fit next to the accumulators)
+  constexpr bool kPF = HD <= 64;
+  constexpr int NV = kPF ? kKeys * HD / 4 / kThreads : 1;
+  const bool vec = kPF && a.kv_vec;
+  float4 pk[NV], pdk[NV], pv[NV], pdv[NV];
+  auto fetch = [&](int kbase) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int e4 = tid + i * kThreads, c = e4 / (HD / 4), d4 = e4 - c * (HD / 4);
+      const int key = kbase + c;
+      pk[i] = pdk[i] = pv[i] = pdv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (key < a.n) {
+        const int64_t o = static_cast<int64_t>(key) * a.kv_row + static_cast<int64_t>(hk) * HD + 4 * d4;
+        pk[i] = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(a.k) + o));
+        pdk[i] = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(a.dk) + o));
+        pv[i] = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(a.v) + o));
+        pdv[i] = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(a.dv) + o));
+      }
+    }
+  };
+  auto put4 = [&](__nv_bfloat16 *hi, __nv_bfloat16 *lo, int off, const float4 &x) {
+    uint32_t h01, l01, h23, l23;
+    split2(x.x, x.y, h01, l01);
+    split2(x.z, x.w, h23, l23);
+    *reinterpret_cast<uint2 *>(hi + off) = make_uint2(h01, h23);
+    *reinterpret_cast<uint2 *>(lo + off) = make_uint2(l01, l23);
+  };
+  if constexpr (kPF) {
+    if (vec) fetch(0);
+  }
   for (int kb = 0; kb < n_blocks; ++kb) {
     const int k0 = kb * kKeys;
     __syncthreads();
+    if (vec) {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int e4 = tid + i * kThreads, c = e4 / (HD / 4), d4 = e4 - c * (HD / 4);
+        const int off = c * LD + 4 * d4;
+        put4(Kh, Kl, off, pk[i]);
+        put4(dKh, dKl, off, pdk[i]);
+        put4(Vh, Vl, off, pv[i]);
+        put4(dVh, dVl, off, pdv[i]);
+      }
+    } else
     for (int e = tid; e < kKeys * HD; e += kThreads) {
       const int c = e / HD, d = e - c * HD;
       const int key = k0 + c;
@@ -291,6 +336,9 @@ __global__ void __launch_bounds__(kThreads, 1) afo_tc_kernel(const Args a) {
       split_bf16(dvv, dVh[c * LD + d], dVl[c * LD + d]);
     }
     __syncthreads();
+    if constexpr (kPF) {
+      if (vec && kb + 1 < n_blocks) fetch(k0 + kKeys);
+    }
     // scores of 4 n-tiles (32 keys): S and dS
     float S[4][4], dS[4][4];
 #pragma unroll
@@ -482,8 +530,10 @@ extern "C" int dkv_attn_first_order(const void *q, const void *dq, int64_t q_row
       out_row_stride < static_cast<int64_t>(n_heads) * head_dim)
     return DKV_ERR_INVALID_ARGUMENT;
   if ((n_tokens + afo::kRows - 1) / afo::kRows > 0x7fffffff || n_heads > 65535) return DKV_ERR_UNSUPPORTED;
+  const auto al16 = [](const void *ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 == 0; };
+  const int kv_vec = dtype == DKV_F32 && kv_row_stride % 4 == 0 && al16(k) && al16(dk) && al16(v) && al16(dv);
   afo::Args a{q, dq, k, dk, v, dv, q_row_stride, kv_row_stride, ctx, dctx, out_row_stride,
-              n_tokens, n_heads, n_kv_heads, head_dim, scale};
+              n_tokens, n_heads, n_kv_heads, head_dim, scale, kv_vec};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == DKV_F32) return afo::launch<DKV_F32>(a, st);
   if (dtype == DKV_BF16) return afo::launch<DKV_BF16>(a, st);

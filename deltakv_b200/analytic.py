@@ -310,7 +310,9 @@ class _LayerGraphs:
                 and all(r() is t and t._version == v for r, t, v in zip(self.refs, tensors, self.versions)))
 
 
-_graph_sets: dict[tuple, object] = {}
+_graph_sets: dict[tuple, object] = {}  # key -> _LayerGraphs, or False (not capturable); in LRU order
+_graph_seen: dict[tuple, int] = {}    # eager calls per key (capture from the second one on)
+MAX_GRAPH_SETS = 2                    # a set holds every layer's intermediates (GBs at 2k tokens)
 
 
 def _capture(model, delta, hidden, chains, streams, prop_r, dev) -> _LayerGraphs | None:
@@ -359,9 +361,10 @@ def analytic_patches(hidden, delta, model, config) -> dict[int, LowRankKVPatch]:
     the same order as one layer after another.  The host polls the chains' truncations
     (:func:`deltakv_b200.subspace.gram_topr_begin`, whose acceptance test is read on the host)
     and issues a chain's next layer as soon as its truncation is decided, while the other
-    chains' kernels run.  From the second call with the same model, delta and shape on, each
-    layer is one CUDA graph replay (captured after the first call; re-captured when a weight,
-    factor or scale changes), so the host issues a handful of operations per layer."""
+    chains' kernels run.  From the third call with the same model, delta and shape on, each
+    layer is one CUDA graph replay (captured after the second call; re-captured when a weight,
+    factor or scale changes; at most MAX_GRAPH_SETS shapes keep their graphs), so the host
+    issues a handful of operations per layer."""
     from deltakv_b200.subspace import gram_topr_finish
 
     cfg = model.cfg
@@ -386,6 +389,8 @@ def analytic_patches(hidden, delta, model, config) -> dict[int, LowRankKVPatch]:
         if gs:  # stale: a weight, factor or scale changed
             _graph_sets.pop(key, None)
         gs = None
+    if gs:
+        _graph_sets[key] = _graph_sets.pop(key)  # most recently used last
     dx: list[Tensor | None] = [None] * len(chains)
 
     def issue(c: int, step: int):
@@ -440,8 +445,17 @@ def analytic_patches(hidden, delta, model, config) -> dict[int, LowRankKVPatch]:
             p.k_dense.record_stream(cur)
             p.v_dense.record_stream(cur)
     if USE_GRAPHS and key not in _graph_sets:
-        try:
-            _graph_sets[key] = _capture(model, delta, hidden, chains, streams, prop_r, dev) or False
-        except RuntimeError:
-            _graph_sets[key] = False  # not capturable here: stay on the eager path
+        # a shape seen once is not captured (one-off lengths would each cost a capture and a
+        # set of graph memory); from the second eager call on it is, evicting the least
+        # recently used set beyond MAX_GRAPH_SETS
+        _graph_seen[key] = _graph_seen.get(key, 0) + 1
+        if _graph_seen[key] >= 2:
+            live = [k for k, v in _graph_sets.items() if v]
+            while len(live) >= MAX_GRAPH_SETS:
+                _graph_sets.pop(live.pop(0), None)
+            try:
+                _graph_sets[key] = _capture(model, delta, hidden, chains, streams, prop_r, dev) or False
+            except RuntimeError:
+                _graph_sets[key] = False  # not capturable here: stay on the eager path
+            _graph_seen.pop(key, None)
     return patches

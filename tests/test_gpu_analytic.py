@@ -101,7 +101,8 @@ def test_engine_loop_replays_as_graphs_and_recaptures(cuda, monkeypatch):
         monkeypatch.setattr(A, "USE_GRAPHS", True)
         return out
 
-    A.analytic_patches(snap(h, hm), delta, model, conf)  # eager, then captured
+    for _ in range(2):  # eager; eager, then captured
+        A.analytic_patches(snap(h, hm), delta, model, conf)
     sets = [v for k, v in A._graph_sets.items() if k[0] == id(model) and k[1] == id(delta)]
     assert sets and sets[0], "the layers were not captured"
     for hidden in (snap(h, hm), other):

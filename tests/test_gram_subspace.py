@@ -241,7 +241,7 @@ def test_analytic_loop_graphs_survive_fallbacks(cuda, monkeypatch):
     want = A.analytic_patches(hidden, delta, model, conf)
     monkeypatch.setattr(A, "USE_GRAPHS", True)
     monkeypatch.setattr(S, "GRAM_TOL", 1e-300)
-    for _ in range(3):  # eager + capture, then two replays
+    for _ in range(4):  # eager, eager + capture, then two replays
         got = A.analytic_patches(hidden, delta, model, conf)
         for l in range(L_):
             assert want[l].k_dense.norm() > 0 and want[l].v_dense.norm() > 0

@@ -6,17 +6,16 @@
 //
 //   gq_kernel     Y[rows] = G[rows, :] Q for 16 rows per CTA: Q (each 32-row chunk one
 //                 contiguous range) and the CTA's columns of G stream through a 3-deep cp.async
-//                 ring (two CTAs fit an SM, so launches of concurrent callers share SMs), each
+//                 ring (two CTAs fit an SM, so launches of concurrent callers share SMs); each
 //                 warp takes 4 rows of a chunk into a 16 x 96 register tile (every Q value
-//                 loaded from shared memory feeds 16 FMAs), the warps' tiles are summed, then
-//                 the partial
-//                 product A^T Y of those rows added into W with fp64 atomics (A = Y: the
-//                 upper triangle of Y^T Y; A = Q: all of Q^T G Q)
+//                 loaded from shared memory feeds 16 FMAs); the warps' tiles are summed, then
+//                 the partial product A^T Y of those rows is added into W with fp64 atomics
+//                 (A = Y: the upper triangle of Y^T Y; A = Q: all of Q^T G Q)
 //   cholqr_kernel W = U^T D^-1 U (right-looking elimination, the trailing matrix in the
 //                 registers of 16 warps, one barrier per pivot) and, in the same loop, the
-//                 forward substitution of this CTA's 64 rows of Y: Q = Y R^-1 with R = D^-1/2 U, so
-//                 Q^T Q = I; every CTA factors W redundantly (64 rows per CTA keep the
-//                 redundant work, and the SMs a launch holds, small)
+//                 forward substitution of this CTA's 64 rows of Y: Q = Y R^-1 with
+//                 R = D^-1/2 U, so Q^T Q = I; every CTA factors W redundantly (64 rows per CTA
+//                 keep that redundant work, and the SMs a launch holds, small)
 //
 // G is read by columns (G[j][row], contiguous for a CTA's rows): G must be symmetric.
 #include "dkv_common.cuh"

@@ -40,7 +40,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "patched token·layers/s (Llama-8B shape, rank-16 k/v LoRA)"
 UNIT = "token·layers/s"
-BYTES_PER_UNIT = 4096 + 4 + 4096 + 4096  # X fp8 + scale + K read/write + V read/write
+BYTES_PER_UNIT = 4096 + 4 + 4 + 4096 + 4096  # X fp8 + scale + sum of squares + K read/write + V read/write
 WORKLOAD = ("Llama-3-8B-shaped exact patch: 32 layers, d=4096, 8 KV heads x 128, 64 seqs x 4096 tokens, "
             "rank-16 k/v LoRA (rel. norm 1e-2), fp8-e4m3 stored X + per-token scale, RMSNorm folded, "
             "RoPE (theta 5e5), bf16 paged KV block 16")
@@ -80,7 +80,7 @@ class SmolGeo(Geo):
 
 
 SMOL_METRIC = "patched token·layers/s (SmolLM2-135M shape, rank-8 k/v LoRA)"
-SMOL_BYTES_PER_UNIT = 1152 + 4 + 768 + 768  # X f16 + row scale + K read/write + V read/write
+SMOL_BYTES_PER_UNIT = 1152 + 4 + 4 + 768 + 768  # X f16 + row scale + sum of squares + K read/write + V read/write
 SMOL_WORKLOAD = ("SmolLM2-135M-shaped exact patch: 30 layers, d=576, 3 KV heads x 64, 32 seqs x 2048 tokens, "
                  "rank-8 k/v LoRA (rel. norm 1e-2), f16 stored X + power-of-two row scale, RMSNorm folded, "
                  "RoPE (theta 1e4), bf16 paged KV block 16")
@@ -118,14 +118,16 @@ def make_workload(n_layers, n_seqs, seq_len, device, seed):
     rows = n_seqs * seq_len
     x = torch.empty(n_layers, rows, G.d_model, dtype=G.x_torch, device=device)
     xs = torch.empty(n_layers, rows, dtype=torch.float32, device=device)
+    xq = torch.empty(n_layers, rows, dtype=torch.float32, device=device)  # per-row sum of squared codes
     for l in range(n_layers):
         # residual-stream-like rows: N(0,1) with a per-token magnitude spread
         h = torch.randn(rows, G.d_model, generator=gen, device=device)
         h *= (0.5 + torch.rand(rows, 1, generator=gen, device=device))
-        q, s = dkv.quantize_rows(h, G.x_torch)
+        q, s, ssq = dkv.quantize_rows(h, G.x_torch, with_sumsq=True)
         x[l].copy_(q)
         xs[l].copy_(s)
-        del h, q, s
+        xq[l].copy_(ssq)
+        del h, q, s, ssq
     blocks_per_seq = (seq_len + G.bs - 1) // G.bs
     nb = n_seqs * blocks_per_seq
     perm = torch.randperm(nb, generator=torch.Generator().manual_seed(seed + 2)).to(torch.int32)
@@ -139,7 +141,7 @@ def make_workload(n_layers, n_seqs, seq_len, device, seed):
     cu = torch.arange(0, n_seqs + 1, dtype=torch.int32, device=device) * seq_len
     seqs = ops.SeqBatchTensors(cu_seqlens=cu, block_tables=tables, max_seq_len=seq_len)
     rope = dkv.RotaryEmbedding(G.hd, max_seq=seq_len, base=G.rope_theta)
-    return dict(x=x, xs=xs, caches=caches, facs=facs, norm_w=norm_w, seqs=seqs, rope=rope, tables=tables)
+    return dict(x=x, xs=xs, xq=xq, caches=caches, facs=facs, norm_w=norm_w, seqs=seqs, rope=rope, tables=tables)
 
 
 # ---------------------------------------------------------------------------
@@ -376,7 +378,8 @@ def run_ours(args):
                      norm_weight=wl["norm_w"], out=packed)
         if ev is not None:
             ev[0].record(stream)
-        patcher.apply(wl["x"], packed, kpages, vpages, wl["seqs"], x_scale=wl["xs"], apply_norm=True)
+        patcher.apply(wl["x"], packed, kpages, vpages, wl["seqs"], x_scale=wl["xs"], apply_norm=True,
+                      x_sumsq=wl["xq"])
         if ev is not None:
             ev[1].record(stream)
 
@@ -506,6 +509,7 @@ def run_e2e(args, patcher, dev, world):
     host = {
         "x": cpu["x"].view(torch.uint8).cpu().pin_memory(),
         "xs": cpu["xs"].cpu().pin_memory(),
+        "xq": cpu["xq"].cpu().pin_memory(),
         "caches": torch.stack(cpu["caches"]).cpu().pin_memory(),
         "tables": cpu["tables"].cpu().pin_memory(),
         "a_k": cpu["facs"]["k"][0].cpu().pin_memory(), "b_k": cpu["facs"]["k"][1].cpu().pin_memory(),
@@ -542,6 +546,7 @@ def run_e2e(args, patcher, dev, world):
             for l in range(n_layers):
                 d["x"][l].copy_(host["x"][l], non_blocking=True)
                 d["xs"][l].copy_(host["xs"][l], non_blocking=True)
+                d["xq"][l].copy_(host["xq"][l], non_blocking=True)
                 d["caches"][l].copy_(host["caches"][l], non_blocking=True)
                 e = torch.cuda.Event()
                 e.record(h2d_s)
@@ -552,7 +557,7 @@ def run_e2e(args, patcher, dev, world):
         for l in range(n_layers):
             stream.wait_event(ev_in[l])
             patcher.apply(xv[l:l + 1], packed[l:l + 1], [d["caches"][l][0]], [d["caches"][l][1]], seqs,
-                          x_scale=d["xs"][l:l + 1], apply_norm=True)
+                          x_scale=d["xs"][l:l + 1], apply_norm=True, x_sumsq=d["xq"][l:l + 1])
             e = torch.cuda.Event()
             e.record(stream)
             d2h_s.wait_event(e)

@@ -38,6 +38,7 @@ EXPORTED = (
     "dkv_paged_error_sums",
     "dkv_paged_compare_sums",
     "dkv_quantize_rows",
+    "dkv_quantize_rows_sumsq",
     "dkv_exact_packed_bytes",
     "dkv_pack_exact_factors",
     "dkv_exact_patch_paged",
@@ -147,6 +148,8 @@ class ExactPatchArgs(C.Structure):
         ("v_pages", C.POINTER(PagedCache)),
         ("accumulate", C.c_int32),
         ("status", C.c_void_p),
+        ("x_sumsq", C.c_void_p),
+        ("x_sumsq_layer_stride", C.c_int64),
     ]
 
 
@@ -283,6 +286,8 @@ def _declare(lib: C.CDLL) -> None:
                                            P, P, P]
     lib.dkv_quantize_rows.restype = C.c_int
     lib.dkv_quantize_rows.argtypes = [P, I32, I64, I64, I64, P, I32, I64, I64, P, P]
+    lib.dkv_quantize_rows_sumsq.restype = C.c_int
+    lib.dkv_quantize_rows_sumsq.argtypes = [P, I32, I64, I64, I64, P, I32, I64, I64, P, P, P]
     lib.dkv_exact_packed_bytes.restype = C.c_int
     lib.dkv_exact_packed_bytes.argtypes = [C.POINTER(ExactGeometry), C.POINTER(C.c_int64)]
     lib.dkv_pack_exact_factors.restype = C.c_int

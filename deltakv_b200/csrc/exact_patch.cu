@@ -16,7 +16,9 @@
 //     matching slice of the packed A factors with a bulk copy;
 //   * 8 consumer warps (16 tokens each) compute codes = x.A^T for K and V together with
 //     mma.sync (fp8 X converted to f16 on the fly, fp32 accumulate), plus sum(x^2) for
-//     the RMSNorm via a diagonal X.X^T product on the same fragments;
+//     the RMSNorm via a diagonal X.X^T product on the same fragments (or, when the stored
+//     activations carry it, the per-row sum of squared codes written with them: no extra
+//     tensor work, which under the power cap raises the clock);
 //   * the codes never leave registers: they are re-scaled per token, turned into the
 //     A fragments of a second mma.sync (codes . B^T) that produces dK/dV directly in a
 //     column order chosen so each thread holds 8 contiguous columns and both halves of
@@ -326,6 +328,8 @@ struct alignas(64) Params {
   int64_t packed_stride;
   const float *x_scale;
   int64_t xs_stride;
+  const float *x_sumsq;  // optional per-row sum of squared codes (RMSNorm without the X.X^T product)
+  int64_t xsq_stride;
   const float *rope_cos, *rope_sin;
   int32_t rope_max_pos, has_rope;
   float norm_eps, inv_d;
@@ -467,6 +471,7 @@ struct Chunk<DKV_F32> {
 struct RowInfo {
   int64_t off_k[2], off_v[2];  // element offset of the row inside a layer's K / V pages
   float xs[2];                 // dequantisation scale
+  float ss[2];                 // sum of squared codes from x_sumsq (when given)
   int pos[2];
   bool valid[2];
 };
@@ -745,6 +750,7 @@ __device__ __forceinline__ RowInfo make_row_info(const Params &p, const Tile &t,
     int pos = tok;
     ri.off_k[r] = ri.off_v[r] = 0;
     ri.xs[r] = 1.f;
+    ri.ss[r] = 0.f;
     if (v) {
       if (p.positions) pos = __ldg(p.positions + grow);
       if (p.has_rope && (pos < 0 || pos >= p.rope_max_pos)) {
@@ -769,6 +775,7 @@ __device__ __forceinline__ RowInfo make_row_info(const Params &p, const Tile &t,
         }
       }
       if (p.x_scale) ri.xs[r] = __ldg(p.x_scale + t.layer * p.xs_stride + grow);
+      if (p.x_sumsq) ri.ss[r] = __ldg(p.x_sumsq + t.layer * p.xsq_stride + grow);
     }
     ri.valid[r] = v;
     ri.pos[r] = pos;
@@ -984,7 +991,7 @@ __global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constan
             mma16816(acc[j], a[0][0], a[0][1], a[0][2], a[0][3], bb.x, bb.y);
             mma16816(acc[j], a[1][0], a[1][1], a[1][2], a[1][3], bb.z, bb.w);
           }
-          if (NORM) {
+          if (NORM && !p.x_sumsq) {
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk) {
               mma16816(dg[0], a[kk][0], a[kk][1], a[kk][2], a[kk][3], a[kk][0], a[kk][2]);
@@ -1007,7 +1014,7 @@ __global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constan
             mma16816(acc[j], a[0][0], a[0][1], a[0][2], a[0][3], bb.x, bb.y);
             mma16816(acc[j], a[1][0], a[1][1], a[1][2], a[1][3], bb.z, bb.w);
           }
-          if (NORM) {
+          if (NORM && !p.x_sumsq) {
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk) {
               mma16816(dg[0], a[kk][0], a[kk][1], a[kk][2], a[kk][3], a[kk][0], a[kk][2]);
@@ -1041,7 +1048,7 @@ __global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constan
       const int src = 4 * g + (g >> 1);
       const float s0 = __shfl_sync(0xffffffffu, (g & 1) ? dg[0][1] : dg[0][0], src);
       const float s1 = __shfl_sync(0xffffffffu, (g & 1) ? dg[1][3] : dg[1][2], src);
-      const float ss[2] = {s0, s1};
+      const float ss[2] = {p.x_sumsq ? ri.ss[0] : s0, p.x_sumsq ? ri.ss[1] : s1};
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         const float xs = ri.xs[r];
@@ -1150,7 +1157,7 @@ struct TcSmem {
 
 template <int XT, int R16, bool NORM>
 __device__ __forceinline__ void issue_stage_mmas(uint32_t d_codes, uint32_t d_diag, uint32_t xs,
-                                                 uint32_t as, bool first) {
+                                                 uint32_t as, bool first, bool diag) {
   using C = TcCfg<XT, R16, NORM>;
   const uint64_t adesc = umma_desc_k_sw128(xs);
   const uint64_t bdesc = umma_desc_k_sw128(as);
@@ -1160,10 +1167,10 @@ __device__ __forceinline__ void issue_stage_mmas(uint32_t d_codes, uint32_t d_di
     const uint64_t a = adesc + static_cast<uint64_t>(2 * kk), b = bdesc + static_cast<uint64_t>(2 * kk);
     if (XT == 0) {
       umma_e4m3(d_codes, a, b, C::IDESC_CODES, acc);
-      if (NORM) umma_e4m3(d_diag, a, a, C::IDESC_DIAG, acc);
+      if (NORM && diag) umma_e4m3(d_diag, a, a, C::IDESC_DIAG, acc);
     } else {
       umma_f16(d_codes, a, b, C::IDESC_CODES, acc);
-      if (NORM) umma_f16(d_diag, a, a, C::IDESC_DIAG, acc);
+      if (NORM && diag) umma_f16(d_diag, a, a, C::IDESC_DIAG, acc);
     }
   }
 }
@@ -1195,15 +1202,19 @@ __device__ __forceinline__ bool tc_readout(const Params &p, const Tile &t, int b
   if (p.x_scale && tok < t.len && grow < p.x_rows) xs = __ldg(p.x_scale + t.layer * p.xs_stride + grow);
   float rs = xs;
   if (NORM) {
-    float d0[16], d1[16];
-    tmem_ld16(taddr + C::DIAG + 32 * qw, d0);
-    tmem_ld16(taddr + C::DIAG + 32 * qw + 16, d1);
-    tmem_ld_wait();
     float ss = 0.f;
+    if (p.x_sumsq) {  // warp-uniform: written with the stored activations
+      if (tok < t.len && grow < p.x_rows) ss = __ldg(p.x_sumsq + t.layer * p.xsq_stride + grow);
+    } else {  // the diagonal of the X.X^T accumulator
+      float d0[16], d1[16];
+      tmem_ld16(taddr + C::DIAG + 32 * qw, d0);
+      tmem_ld16(taddr + C::DIAG + 32 * qw + 16, d1);
+      tmem_ld_wait();
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      ss = (i == lane) ? d0[i] : ss;
-      ss = (16 + i == lane) ? d1[i] : ss;
+      for (int i = 0; i < 16; ++i) {
+        ss = (i == lane) ? d0[i] : ss;
+        ss = (16 + i == lane) ? d1[i] : ss;
+      }
     }
     rs = xs * rsqrtf(xs * xs * ss * p.inv_d + p.norm_eps);
   }
@@ -1339,7 +1350,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
           }
           tc_fence_after();
           issue_stage_mmas<XT, R16, NORM>(d_codes, d_diag, smem_u32(sx + stage * kXStageBytes),
-                                          smem_u32(sa + stage * C::A_STAGE), kc == 0);
+                                          smem_u32(sa + stage * C::A_STAGE), kc == 0, p.x_sumsq == nullptr);
           umma_commit(&empty[stage]);  // the slot is free once these MMAs have read it
           if (++stage == STAGES) {
             stage = 0;
@@ -1652,6 +1663,8 @@ extern "C" int dkv_exact_patch_paged(const dkv_exact_patch_args *a, dkv_stream_t
   p.packed_stride = a->packed_layer_stride;
   p.x_scale = a->x_scale;
   p.xs_stride = a->x_scale_layer_stride;
+  p.x_sumsq = a->apply_norm ? a->x_sumsq : nullptr;
+  p.xsq_stride = a->x_sumsq_layer_stride;
   p.rope_cos = rope ? a->rope_cos : nullptr;
   p.rope_sin = rope ? a->rope_sin : nullptr;
   p.rope_max_pos = rope ? a->rope_max_pos : 0;

@@ -19,7 +19,8 @@ __global__ void __launch_bounds__(kThreads) quant_rows_kernel(const void *__rest
                                                               int64_t xs, int64_t cols,
                                                               void *__restrict__ out, int64_t os,
                                                               int64_t out_cols,
-                                                              float *__restrict__ scale) {
+                                                              float *__restrict__ scale,
+                                                              float *__restrict__ sumsq) {
   __shared__ float red[32];
   const int64_t r = blockIdx.x;
   using IT = typename Elem<IDT>::T;
@@ -48,16 +49,33 @@ __global__ void __launch_bounds__(kThreads) quant_rows_kernel(const void *__rest
     inv = 1.f / s;
   }
   if (threadIdx.x == 0) scale[r] = s;
+  float ss = 0.f;  // sum of the squared stored codes (the RMSNorm's sum(x^2) / scale^2)
   for (int64_t c = threadIdx.x; c < out_cols; c += blockDim.x) {
     const float v = c < cols ? Elem<IDT>::to_f(xr[c]) : 0.f;
+    float code;
     if (ODT == DKV_F16) {
-      static_cast<__half *>(out)[r * os + c] = __float2half_rn(v * inv);
+      const __half h = __float2half_rn(v * inv);
+      static_cast<__half *>(out)[r * os + c] = h;
+      code = __half2float(h);
     } else {
       // e4m3 with round-to-nearest-even and saturation to +-448
       const float q = fminf(fmaxf(v / s, -448.f), 448.f);
       uint16_t two;
       asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(two) : "f"(0.f), "f"(q));
       static_cast<uint8_t *>(out)[r * os + c] = static_cast<uint8_t>(two & 0xff);
+      code = e4m3_to_f32(two & 0xffu);
+    }
+    ss = fmaf(code, code, ss);
+  }
+  if (sumsq != nullptr) {  // uniform across the block
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    __syncthreads();  // red[] was read above
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float w = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+      for (int o = 16; o > 0; o >>= 1) w += __shfl_xor_sync(0xffffffffu, w, o);
+      if (threadIdx.x == 0) sumsq[r] = w;
     }
   }
 }
@@ -68,11 +86,12 @@ __global__ void __launch_bounds__(kThreads) quant_rows_kernel(const void *__rest
 using namespace dkv;
 
 /* Quantise rows of x (F32/F16/BF16, row stride x_row_stride elements) into out
-   (DKV_F16 or DKV_E4M3, row stride out_row_stride) with per-row fp32 scales. */
-extern "C" int dkv_quantize_rows(const void *x, int32_t x_dtype, int64_t rows, int64_t cols,
-                                 int64_t x_row_stride, void *out, int32_t out_dtype,
-                                 int64_t out_row_stride, int64_t out_cols, float *scale,
-                                 dkv_stream_t stream) {
+   (DKV_F16 or DKV_E4M3, row stride out_row_stride) with per-row fp32 scales; with sumsq,
+   also each row's sum of squared stored codes. */
+extern "C" int dkv_quantize_rows_sumsq(const void *x, int32_t x_dtype, int64_t rows, int64_t cols,
+                                       int64_t x_row_stride, void *out, int32_t out_dtype,
+                                       int64_t out_row_stride, int64_t out_cols, float *scale,
+                                       float *sumsq, dkv_stream_t stream) {
   if (rows < 0 || cols < 0 || out_cols < cols) return DKV_ERR_INVALID_ARGUMENT;
   if (rows == 0) return DKV_OK;
   if (x == nullptr || out == nullptr || scale == nullptr) return DKV_ERR_INVALID_ARGUMENT;
@@ -81,7 +100,7 @@ extern "C" int dkv_quantize_rows(const void *x, int32_t x_dtype, int64_t rows, i
 #define DKV_Q(I, O)                                                                         \
   if (x_dtype == I && out_dtype == O) {                                                     \
     quant_rows_kernel<I, O><<<static_cast<unsigned>(rows), kThreads, 0, st>>>(              \
-        x, x_row_stride, cols, out, out_row_stride, out_cols, scale);                       \
+        x, x_row_stride, cols, out, out_row_stride, out_cols, scale, sumsq);                \
     DKV_CUDA_CHECK(cudaGetLastError());                                                     \
     return DKV_OK;                                                                          \
   }
@@ -93,6 +112,14 @@ extern "C" int dkv_quantize_rows(const void *x, int32_t x_dtype, int64_t rows, i
   DKV_Q(DKV_BF16, DKV_E4M3)
 #undef DKV_Q
   return DKV_ERR_UNSUPPORTED;
+}
+
+extern "C" int dkv_quantize_rows(const void *x, int32_t x_dtype, int64_t rows, int64_t cols,
+                                 int64_t x_row_stride, void *out, int32_t out_dtype,
+                                 int64_t out_row_stride, int64_t out_cols, float *scale,
+                                 dkv_stream_t stream) {
+  return dkv_quantize_rows_sumsq(x, x_dtype, rows, cols, x_row_stride, out, out_dtype, out_row_stride, out_cols,
+                                 scale, nullptr, stream);
 }
 
 namespace dkv {

@@ -56,7 +56,11 @@ class ExactPatcher:
 
     def apply(self, x: Tensor, packed: Tensor, k_pages: Sequence[Tensor], v_pages: Sequence[Tensor],
               seqs: ops.SeqBatchTensors, *, x_scale: Tensor | None = None, apply_norm: bool = False,
-              accumulate: bool = True, check: bool = False) -> None:
+              accumulate: bool = True, check: bool = False, x_sumsq: Tensor | None = None) -> None:
+        """``x_sumsq``: the per-row sums of squared codes :func:`deltakv_b200.ops.quantize_rows`
+        writes with ``with_sumsq=True``; with ``apply_norm`` the RMSNorm then uses them rather
+        than forming them on the tensor cores (less tensor work, a higher clock under the
+        power cap)."""
         dev = x.device
         cos = sin = None
         if self.rope is not None:
@@ -64,7 +68,7 @@ class ExactPatcher:
         st = ops.status_word(dev)
         ops.exact_patch_paged(self.geom, x, packed, k_pages, v_pages, seqs, x_scale=x_scale,
                               apply_norm=apply_norm, norm_eps=self.norm_eps, rope_cos=cos, rope_sin=sin,
-                              accumulate=accumulate, status=st)
+                              accumulate=accumulate, status=st, x_sumsq=x_sumsq)
         if check:
             st.raise_if_set("ExactPatcher.apply")
 

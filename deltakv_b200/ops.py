@@ -183,10 +183,11 @@ def gather_paged(pages: torch.Tensor, seqs: SeqBatchTensors, out: torch.Tensor,
 # stored-activation format
 # ---------------------------------------------------------------------------
 def quantize_rows(x: torch.Tensor, out_dtype: torch.dtype = torch.float16,
-                  pad_to: int = 16) -> tuple[torch.Tensor, torch.Tensor]:
+                  pad_to: int = 16, with_sumsq: bool = False):
     """``x [..., rows, d]`` (fp32/bf16/f16) -> ``(q [..., rows, d_pad], scale [..., rows])``
     with ``x ~= q * scale``; ``d_pad`` rounds ``d`` up so a row is a multiple of 16 bytes
-    (the padding is zero)."""
+    (the padding is zero).  ``with_sumsq`` adds ``sumsq [..., rows]``, each row's sum of
+    squared stored codes, for the exact patch's RMSNorm (``ExactPatcher.apply(x_sumsq=...)``)."""
     _require_cuda(x)
     lead = x.shape[:-1]
     d = x.shape[-1]
@@ -198,11 +199,14 @@ def quantize_rows(x: torch.Tensor, out_dtype: torch.dtype = torch.float16,
     d_pad = (d + step - 1) // step * step
     q = torch.empty(x2.shape[0], d_pad, dtype=out_dtype, device=x.device)
     scale = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
-    rc = L.lib().dkv_quantize_rows(
+    sumsq = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device) if with_sumsq else None
+    rc = L.lib().dkv_quantize_rows_sumsq(
         x2.data_ptr(), dkv_dtype(x2.dtype), x2.shape[0], d, x2.stride(0), q.data_ptr(),
-        dkv_dtype(out_dtype), q.stride(0), d_pad, scale.data_ptr(), stream_ptr(),
+        dkv_dtype(out_dtype), q.stride(0), d_pad, scale.data_ptr(), ptr(sumsq), stream_ptr(),
     )
-    L.check(rc, "dkv_quantize_rows")
+    L.check(rc, "dkv_quantize_rows_sumsq")
+    if with_sumsq:
+        return q.view(*lead, d_pad), scale.view(*lead), sumsq.view(*lead)
     return q.view(*lead, d_pad), scale.view(*lead)
 
 
@@ -268,13 +272,16 @@ def exact_patch_paged(geom: L.ExactGeometry, x: torch.Tensor, packed: torch.Tens
                       seqs: SeqBatchTensors, *, x_scale: torch.Tensor | None = None,
                       apply_norm: bool = False, norm_eps: float = 1e-6,
                       rope_cos: torch.Tensor | None = None, rope_sin: torch.Tensor | None = None,
-                      accumulate: bool = True, status: StatusWord | None = None) -> None:
+                      accumulate: bool = True, status: StatusWord | None = None,
+                      x_sumsq: torch.Tensor | None = None) -> None:
     """Launch the fused patch over ``L = len(k_pages)`` layers.
 
     ``x`` is ``[L, rows, d]`` (or ``[rows, d]`` for one layer) in fp8-e4m3 or f16;
     ``x_scale`` ``[L, rows]`` fp32; ``k_pages[l]`` / ``v_pages[l]`` are
     ``[num_blocks, block_size, n_kv, head_dim]`` views; ``rope_cos/sin`` are
-    ``[max_pos, head_dim/2]`` fp32 tables.
+    ``[max_pos, head_dim/2]`` fp32 tables.  ``x_sumsq`` ``[L, rows]`` fp32 (from
+    :func:`quantize_rows` ``with_sumsq``): with ``apply_norm`` the RMSNorm takes each row's
+    sum of squared codes from it instead of forming it on the tensor cores.
     """
     n_layers = len(k_pages)
     if len(v_pages) != n_layers:
@@ -284,7 +291,7 @@ def exact_patch_paged(geom: L.ExactGeometry, x: torch.Tensor, packed: torch.Tens
     x3 = x if x.ndim == 3 else x.unsqueeze(0)
     if x3.shape[0] != n_layers:
         raise ValueError("x layers do not match the page lists")
-    _require_cuda(x3, packed, x_scale, rope_cos, rope_sin)
+    _require_cuda(x3, packed, x_scale, rope_cos, rope_sin, x_sumsq)
     if x3.stride(2) != 1:
         raise ValueError("x rows must be contiguous")
     xs = None
@@ -292,6 +299,11 @@ def exact_patch_paged(geom: L.ExactGeometry, x: torch.Tensor, packed: torch.Tens
         xs = x_scale if x_scale.ndim == 2 else x_scale.unsqueeze(0)
         if xs.dtype != torch.float32 or xs.stride(1) != 1:
             raise TypeError("x_scale must be fp32 with contiguous rows")
+    xq = None
+    if x_sumsq is not None:
+        xq = x_sumsq if x_sumsq.ndim == 2 else x_sumsq.unsqueeze(0)
+        if xq.dtype != torch.float32 or xq.stride(1) != 1 or xq.shape[0] != n_layers or xq.shape[1] < x3.shape[1]:
+            raise TypeError("x_sumsq must be fp32 [layers, rows] with contiguous rows")
     kd = (L.PagedCache * n_layers)(*[paged_desc(p) for p in k_pages])
     vd = (L.PagedCache * n_layers)(*[paged_desc(p) for p in v_pages])
     if rope_cos is not None:
@@ -311,6 +323,7 @@ def exact_patch_paged(geom: L.ExactGeometry, x: torch.Tensor, packed: torch.Tens
         k_pages=kd, v_pages=vd,
         accumulate=1 if accumulate else 0,
         status=status.ptr if status else None,
+        x_sumsq=ptr(xq), x_sumsq_layer_stride=xq.stride(0) if xq is not None else 0,
     )
     rc = L.lib().dkv_exact_patch_paged(C.byref(args), stream_ptr())
     L.check(rc, "dkv_exact_patch_paged")

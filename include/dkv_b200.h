@@ -153,6 +153,12 @@ int dkv_paged_compare_sums(const dkv_paged_cache *pages, int32_t n_layers, const
 int dkv_quantize_rows(const void *x, int32_t x_dtype, int64_t rows, int64_t cols,
                       int64_t x_row_stride, void *out, int32_t out_dtype, int64_t out_row_stride,
                       int64_t out_cols, float *scale, dkv_stream_t stream);
+/* The same, also writing sumsq[r] = sum of the squared stored codes of row r (fp32): with
+   the codes' scale, RMSNorm's sum(x^2) = scale^2 * sumsq, which dkv_exact_patch_args.x_sumsq
+   takes so the patch forms no X.X^T product. */
+int dkv_quantize_rows_sumsq(const void *x, int32_t x_dtype, int64_t rows, int64_t cols,
+                            int64_t x_row_stride, void *out, int32_t out_dtype, int64_t out_row_stride,
+                            int64_t out_cols, float *scale, float *sumsq, dkv_stream_t stream);
 
 /* ---- exact / zeroth-order patch (fused) --------------------------------- */
 
@@ -223,6 +229,11 @@ typedef struct dkv_exact_patch_args {
   const dkv_paged_cache *v_pages;
   int32_t accumulate; /* 1: pages += delta (read-add-write); 0: pages = delta */
   int32_t *status;    /* optional device status word */
+  /* optional, with apply_norm: per-row sum of the squared stored codes (fp32, (l, t) at
+     x_sumsq + l*x_sumsq_layer_stride + t), as dkv_quantize_rows writes it; the RMSNorm then
+     uses it instead of forming X.X^T's diagonal on the tensor cores.  NULL: formed here. */
+  const float *x_sumsq;
+  int64_t x_sumsq_layer_stride;
 } dkv_exact_patch_args;
 
 /*

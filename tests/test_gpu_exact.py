@@ -259,15 +259,27 @@ def test_exact_patch_matches_oracle(cuda, d, n_kv, hd, rk, rv, bs, xdt, pdt, nor
     seqs = ops.SeqBatchTensors(cu_seqlens=t(case["cu"]), block_tables=t(case["tables"]), max_seq_len=max(lens),
                                positions=t(case["pos"]) if case["pos"] is not None else None)
     patcher.apply(x, packed, kp, vp, seqs, x_scale=t(case["xs"]), apply_norm=norm, accumulate=acc, check=True)
+    runs = [(kp, vp)]
+    if norm:
+        # the RMSNorm from the stored per-row sums of squared codes instead of X.X^T's diagonal
+        codes = np.stack([OX.dequant_x(case["xbits"][l], xdt, np.ones(case["xbits"].shape[1], np.float32))
+                          for l in range(L_)])
+        ssq = (codes.astype(np.float64) ** 2).sum(-1).astype(np.float32)
+        kp2 = [tt.to(cuda) for tt in base_k]
+        vp2 = [tt.to(cuda) for tt in base_v]
+        patcher.apply(x, packed, kp2, vp2, seqs, x_scale=t(case["xs"]), apply_norm=True, accumulate=acc, check=True,
+                      x_sumsq=t(ssq))
+        runs.append((kp2, vp2))
     tol = REL_TOL if acc else 2e-3
-    for l in range(L_):
-        for got_t, ref in ((kp[l], kref[l]), (vp[l], vref[l])):
-            got = to_np(got_t)
-            if pdt == torch.bfloat16:
-                a, b = bf16_bits_to_f32(got), bf16_bits_to_f32(ref)
-            else:
-                a, b = got.astype(np.float32), ref.astype(np.float32)
-            assert rel_l2(a, b) < tol, (l, rel_l2(a, b))
+    for kps, vps in runs:
+        for l in range(L_):
+            for got_t, ref in ((kps[l], kref[l]), (vps[l], vref[l])):
+                got = to_np(got_t)
+                if pdt == torch.bfloat16:
+                    a, b = bf16_bits_to_f32(got), bf16_bits_to_f32(ref)
+                else:
+                    a, b = got.astype(np.float32), ref.astype(np.float32)
+                assert rel_l2(a, b) < tol, (l, rel_l2(a, b))
 
 
 def test_rope_range_error_reported(cuda):
@@ -286,3 +298,16 @@ def test_rope_range_error_reported(cuda):
         layer = dkv.LayerDelta(0, {"k_proj": dkv.LowRankFactors(torch.randn(4, 64, device=cuda), torch.randn(64, 4, device=cuda))})
         dkv.exact_kv_patch(torch.randn(20, 64, device=cuda), layer, n_kv_heads=1, head_dim=64,
                            rope=(torch.ones(8, 32), torch.zeros(8, 32)))
+
+
+@pytest.mark.parametrize("odt", [torch.float8_e4m3fn, torch.float16])
+def test_quantize_rows_writes_sums_of_squared_codes(cuda, odt):
+    # the stored-activation writer's per-row sum of squared codes (what the patch's RMSNorm
+    # takes through x_sumsq) against the codes it returns; codes and scales are unchanged
+    g = torch.Generator().manual_seed(3)
+    x = (torch.randn(300, 1000, generator=g) * (0.1 + 3 * torch.rand(300, 1, generator=g))).to(cuda)
+    q, s, ss = dkv.quantize_rows(x, odt, with_sumsq=True)
+    want = (q.float().double() ** 2).sum(-1)
+    assert torch.allclose(ss.double(), want, rtol=1e-5, atol=0)
+    q2, s2 = dkv.quantize_rows(x, odt)
+    assert torch.equal(q2.view(torch.uint8), q.view(torch.uint8)) and torch.equal(s2, s)

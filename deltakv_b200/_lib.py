@@ -13,6 +13,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libdkv_b200.so"
 
 # status codes (dkv_b200.h)
 DKV_OK = 0
+ABI_VERSION = 2  # the struct layouts below (dkv_abi_version() of the library must match)
 DKV_ERR_INVALID_ARGUMENT = -1
 DKV_ERR_BLOCK_TABLE_SHORT = -2
 DKV_ERR_LAYOUT = -3
@@ -352,7 +353,7 @@ def lib() -> C.CDLL:
             )
         handle = C.CDLL(str(LIB_PATH))
         _declare(handle)
-        if handle.dkv_abi_version() != 1:
+        if handle.dkv_abi_version() != ABI_VERSION:
             raise ImportError(f"{LIB_PATH.name} ABI version mismatch; rebuild the library")
         _lib = handle
     return _lib

@@ -302,7 +302,7 @@ extern "C" const char *dkv_status_string(int status) {
   }
 }
 
-extern "C" int dkv_abi_version(void) { return 1; }
+extern "C" int dkv_abi_version(void) { return 2; }
 
 namespace dkv {
 static thread_local char g_last_cuda_error[256] = "";

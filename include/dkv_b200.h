@@ -64,7 +64,8 @@ typedef struct CUstream_st *dkv_stream_t;
 
 /* Human-readable text of a status code (static storage). */
 const char *dkv_status_string(int status);
-/* ABI version: bumped when a struct below changes. */
+/* ABI version: bumped when a struct below changes.  2: dkv_exact_patch_args ends with x_sumsq and
+   x_sumsq_layer_stride (a caller built against version 1 passes a shorter struct). */
 int dkv_abi_version(void);
 /* Text of the last CUDA runtime failure behind a DKV_ERR_CUDA on this thread ("" if none). */
 const char *dkv_last_cuda_error(void);

@@ -29,7 +29,7 @@ def test_library_loads_and_exports_all_symbols():
     lib = _lib.lib()
     for name in _declared():
         assert hasattr(lib, name), name
-    assert lib.dkv_abi_version() == 1
+    assert lib.dkv_abi_version() == _lib.ABI_VERSION == 2
     assert lib.dkv_status_string(-2).decode() == "block_table shorter than prefix"
     assert lib.dkv_status_string(-3).decode() == "unsupported paged KV layout"
 

@@ -1,28 +1,36 @@
-"""Throughput of the fused exact KV patch on the Llama-3-8B-shaped workload.
+"""Throughput of ΔKV's cache-maintenance hot path on B200, one JSON line.
 
-One step = one pass of the exact/zeroth-order patch route over a full cache: pack the
-rank-16 k/v LoRA factors of 32 layers, then patch 64 sequences x 4096 tokens x 32 layers
-(8,388,608 token-layers) from fp8-e4m3 stored activations (per-token scale, RMSNorm
-folded in) into bf16 paged K/V (block 16, permuted block table), RoPE on K.
+Default run (the headline): the exact/zeroth-order patch route on the Llama-3-8B-shaped cache
+— 32 layers, d=4096, 8 KV heads x 128, 64 sequences x 4096 tokens, rank-16 k/v LoRA, fp8-e4m3
+stored activations (per-token scale, per-row sums of squared codes stored beside them),
+RMSNorm folded in, RoPE on K, bf16 paged K/V (block 16, permuted block table).  One step =
+pack the factors of the layers this GPU holds, then one fused launch over its (layer,
+sequence) tiles.  The same line carries a ``workloads`` object with the other measured
+configurations, each with its own value, roofline, CPU baseline, end-to-end figure, parity
+spot check and clocks:
 
-    python bench.py [--gpus N --steps K --warmup W]          # this implementation
-    python bench.py --impl reference ...                       # CPU reference arm
-    python bench.py --workload smollm2-exact ...               # exact route, SmolLM2-135M shape
-    python bench.py --workload rl-dense ...                    # dense-dW (RL step) route
-    python bench.py --workload multi-lora-kivi ...             # int4 KIVI subspace route
+* ``smollm2-exact``   exact route, SmolLM2-135M shape (30 layers, d=576, 3 KV heads x 64,
+                      32 x 2048 tokens, rank-8 k/v LoRA, f16 stored activations);
+* ``multi-lora-kivi`` subspace route on a KIVI int4 shared prefix (Llama-3-8B shape,
+                      32768 tokens, 8 adapter views of ranks {8,8,16,16,32,32,64,64});
+* ``rl-dense``        dense-dW route of an RL step (Llama-3-70B shape: 80 layers, d=8192,
+                      16 x 8192 tokens, full-rank dW_K / dW_V), a tcgen05 GEMM.
 
-The rl-dense workload is one GPU's share of the Llama-3-70B-shaped RL step (10 of 80
-layers, d=8192, 8 KV heads x 128, 16 seqs x 8192 tokens, bf16 X, full-rank dW_K / dW_V at
-||dW||/||W|| = 1e-3): one tensor-core GEMM launch of 44 TFLOP per step with RoPE and the
-paged read-add-write fused; its roofline is the measured sustained bf16 GEMM rate.
+    python bench.py [--gpus N --steps K --warmup W]      # this implementation
+    python bench.py --impl reference ...                   # the CPU reference arm
+    python bench.py --workload NAME ...                    # one workload alone (also: analytic)
 
-Under torchrun (N>1) every rank patches its own request shard of the same size (weak
-scaling; no data-path collective).  Rank 0 prints one JSON line.
+Under torchrun (N > 1) the fixed workload is split across the ranks without any data-path
+collective (strong scaling): layers round-robin (layer l on rank l mod N) for the exact and
+dense routes, adapter views for the int4 route (the shared base cache broadcast once over
+NCCL before timing).  The per-layer error scalars are all-gathered after the timed region.
+Rank 0 prints the line; ``value`` = all units of the step / the slowest rank's time.
 """
 
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import math
 import os
@@ -30,6 +38,7 @@ import statistics
 import sys
 import threading
 import time
+import traceback
 from pathlib import Path
 
 import numpy as np
@@ -38,15 +47,10 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-METRIC = "patched token·layers/s (Llama-8B shape, rank-16 k/v LoRA)"
 UNIT = "token·layers/s"
-BYTES_PER_UNIT = 4096 + 4 + 4 + 4096 + 4096  # X fp8 + scale + sum of squares + K read/write + V read/write
-WORKLOAD = ("Llama-3-8B-shaped exact patch: 32 layers, d=4096, 8 KV heads x 128, 64 seqs x 4096 tokens, "
-            "rank-16 k/v LoRA (rel. norm 1e-2), fp8-e4m3 stored X + per-token scale, RMSNorm folded, "
-            "RoPE (theta 5e5), bf16 paged KV block 16")
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -54,99 +58,63 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama8b-exact",
                     choices=["llama8b-exact", "smollm2-exact", "rl-dense", "multi-lora-kivi", "analytic"])
+    ap.add_argument("--shard", default="layer", choices=["layer", "request"],
+                    help="N>1 split of the exact / dense routes: layers of one fixed cache (strong "
+                         "scaling) or a request shard of the same size per rank (weak scaling)")
     ap.add_argument("--adapters", type=int, default=8)
     ap.add_argument("--layers", type=int, default=None)
     ap.add_argument("--seqs", type=int, default=None)
     ap.add_argument("--seq-len", type=int, default=None)
     ap.add_argument("--e2e-seqs", type=int, default=4)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--sub-cpu-seconds", type=float, default=6.0)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    return ap.parse_args()
-
-
-class Geo:
-    """The exact-route workload being measured (rebound by --workload)."""
-    d_model, n_kv, hd, rank, bs, eps, rope_theta = 4096, 8, 128, 16, 16, 1e-5, 500000.0
-    layers, seqs, seq_len = 32, 64, 4096
-    x_torch, x_kind = torch.float8_e4m3fn, "e4m3"
-
-
-class SmolGeo(Geo):
-    """SmolLM2-135M shape: 30 layers, d=576, 3 KV heads x 64, rank-8 k/v LoRA, fp16 stored X."""
-    d_model, n_kv, hd, rank, bs, eps, rope_theta = 576, 3, 64, 8, 16, 1e-5, 10000.0
-    layers, seqs, seq_len = 30, 32, 2048
-    x_torch, x_kind = torch.float16, "f16"
-
-
-SMOL_METRIC = "patched token·layers/s (SmolLM2-135M shape, rank-8 k/v LoRA)"
-SMOL_BYTES_PER_UNIT = 1152 + 4 + 4 + 768 + 768  # X f16 + row scale + sum of squares + K read/write + V read/write
-SMOL_WORKLOAD = ("SmolLM2-135M-shaped exact patch: 30 layers, d=576, 3 KV heads x 64, 32 seqs x 2048 tokens, "
-                 "rank-8 k/v LoRA (rel. norm 1e-2), f16 stored X + power-of-two row scale, RMSNorm folded, "
-                 "RoPE (theta 1e4), bf16 paged KV block 16")
-
-
-class DenseGeo:
-    """One GPU's share (10 of 80 layers) of the Llama-3-70B-shaped RL step."""
-    layers, seqs, seq_len, d_model, n_kv, hd, bs, rope_theta = 10, 16, 8192, 8192, 8, 128, 16, 500000.0
+    ap.add_argument("--no-workloads", action="store_true", help="headline only (no workloads object)")
+    return ap.parse_args(argv)
 
 
 # ---------------------------------------------------------------------------
-# workload
+# ranks, timing, clocks, peaks
 # ---------------------------------------------------------------------------
-def make_factors(n_layers, device, gen):
-    G = Geo
-    d, d_kv, r = G.d_model, G.n_kv * G.hd, G.rank
-    w_norm = 0.02 * math.sqrt(d_kv * d)  # ||W_k|| of an N(0, 0.02^2) projection
-    out = {}
-    for name in ("k", "v"):
-        A = torch.randn(n_layers, r, d, generator=gen, device=device) / math.sqrt(d)
-        B = torch.randn(n_layers, d_kv, r, generator=gen, device=device)
-        # scale so ||s B A||_F / ||W||_F = 1e-2 per layer (use the mean over layers)
-        ba = torch.stack([(B[l] @ A[l]).norm() for l in range(n_layers)]).mean().item()
-        out[name] = (A, B, 1e-2 * w_norm / ba)
-    norm_w = 1.0 + 0.05 * torch.randn(n_layers, d, generator=gen, device=device)
-    return out, norm_w
+class Dist:
+    """One process per GPU; NCCL process group when WORLD_SIZE > 1."""
+
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.dev = None
+
+    def init(self):
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=self.dev)
+        return self
+
+    def barrier(self):
+        if self.world > 1:
+            torch.distributed.barrier()
+
+    def reduce(self, x: float, op) -> float:
+        if self.world == 1:
+            return float(x)
+        t = torch.tensor([float(x)], device=self.dev, dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=op)
+        return float(t.item())
+
+    def max(self, x: float) -> float:
+        return self.reduce(x, torch.distributed.ReduceOp.MAX if self.world > 1 else None)
+
+    def min(self, x: float) -> float:
+        return self.reduce(x, torch.distributed.ReduceOp.MIN if self.world > 1 else None)
+
+    def finish(self):
+        if self.world > 1:
+            torch.distributed.destroy_process_group()
 
 
-def make_workload(n_layers, n_seqs, seq_len, device, seed):
-    import deltakv_b200 as dkv
-    from deltakv_b200 import ops
-
-    G = Geo
-    gen = torch.Generator(device=device).manual_seed(seed)
-    rows = n_seqs * seq_len
-    x = torch.empty(n_layers, rows, G.d_model, dtype=G.x_torch, device=device)
-    xs = torch.empty(n_layers, rows, dtype=torch.float32, device=device)
-    xq = torch.empty(n_layers, rows, dtype=torch.float32, device=device)  # per-row sum of squared codes
-    for l in range(n_layers):
-        # residual-stream-like rows: N(0,1) with a per-token magnitude spread
-        h = torch.randn(rows, G.d_model, generator=gen, device=device)
-        h *= (0.5 + torch.rand(rows, 1, generator=gen, device=device))
-        q, s, ssq = dkv.quantize_rows(h, G.x_torch, with_sumsq=True)
-        x[l].copy_(q)
-        xs[l].copy_(s)
-        xq[l].copy_(ssq)
-        del h, q, s, ssq
-    blocks_per_seq = (seq_len + G.bs - 1) // G.bs
-    nb = n_seqs * blocks_per_seq
-    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(seed + 2)).to(torch.int32)
-    tables = perm.view(n_seqs, blocks_per_seq).to(device)
-    caches = []  # vLLM flash-attention layout per layer: [2, num_blocks, block, n_kv, head_dim]
-    for _ in range(n_layers):
-        c = torch.empty(2, nb, G.bs, G.n_kv, G.hd, dtype=torch.bfloat16, device=device)
-        c.normal_(generator=gen)
-        caches.append(c)
-    facs, norm_w = make_factors(n_layers, device, gen)
-    cu = torch.arange(0, n_seqs + 1, dtype=torch.int32, device=device) * seq_len
-    seqs = ops.SeqBatchTensors(cu_seqlens=cu, block_tables=tables, max_seq_len=seq_len)
-    rope = dkv.RotaryEmbedding(G.hd, max_seq=seq_len, base=G.rope_theta)
-    return dict(x=x, xs=xs, xq=xq, caches=caches, facs=facs, norm_w=norm_w, seqs=seqs, rope=rope, tables=tables)
-
-
-# ---------------------------------------------------------------------------
-# clocks during the timed region (NVML, polled in a thread)
-# ---------------------------------------------------------------------------
 class ClockSampler:
     REASONS = {
         "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
@@ -201,16 +169,61 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
-# ---------------------------------------------------------------------------
-# CPU oracle port (cpu_baseline and the reference arm)
-# ---------------------------------------------------------------------------
-def cpu_pool_threads() -> int:
-    """Host threads for the CPU arm: every core, capped so each worker's ~0.5 GB of
-    fp32 temporaries (one 4096-token sequence of one layer) fits in free memory."""
+def timed(dist: Dist, step, steps: int, kernel_events: bool = True):
+    """Exactly ``steps`` steps between a barrier + synchronize on each side; returns
+    (max-over-ranks ms of the whole region, this rank's per-step kernel ms, clocks)."""
+    stream = torch.cuda.current_stream()
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dist.local) as clk:
+        t0.record(stream)
+        for i in range(steps):
+            step(kev[i] if kernel_events else None)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    dist.barrier()
+    ms = dist.max(t0.elapsed_time(t1))
+    kern = [a.elapsed_time(b) for a, b in kev] if kernel_events else []
+    return ms, kern, clk.summary()
+
+
+def peaks() -> dict:
     try:
-        cores = len(os.sched_getaffinity(0))
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        return {}
+
+
+def hbm_peak():
+    p = peaks().get("hbm_gbs")
+    if p:
+        return p, "of measured (MEASURED_PEAKS.json hbm_gbs, burst copy)"
+    return 6650.0, "of fallback (6650 GB/s)"
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
     except AttributeError:
-        cores = os.cpu_count() or 1
+        return os.cpu_count() or 1
+
+
+def cpu_pool_threads() -> int:
+    """Host threads for the CPU arm: every core, capped so each worker's ~0.5 GB of fp32
+    temporaries (one 4096-token sequence of one layer) fits in free memory."""
+    cores = host_threads()
     try:
         import psutil
 
@@ -220,36 +233,160 @@ def cpu_pool_threads() -> int:
         return cores
 
 
-class CpuSample:
-    """A bounded sample of the workload on the host: P distinct (layer, sequence) inputs,
-    one private paged K/V per worker thread (a single sequence's blocks)."""
+def my_layers(n_layers: int, dist: Dist, shard: str) -> list[int]:
+    """Layer l on rank l mod N (layer sharding); every layer on every rank otherwise."""
+    if dist.world == 1 or shard != "layer":
+        return list(range(n_layers))
+    return [l for l in range(n_layers) if l % dist.world == dist.rank]
 
-    def __init__(self, n_inputs: int, seq_len: int, seed: int = 5):
+
+def rel_l2(a: torch.Tensor, b: torch.Tensor) -> float:
+    a, b = a.double(), b.double()
+    return float((a - b).norm() / (b.norm() + 1e-30))
+
+
+# ---------------------------------------------------------------------------
+# exact route (Llama-3-8B and SmolLM2-135M shapes)
+# ---------------------------------------------------------------------------
+class Llama8B:
+    name = "llama8b-exact"
+    metric = "patched token·layers/s (Llama-8B shape, rank-16 k/v LoRA)"
+    d_model, n_kv, hd, rank, bs, eps, rope_theta = 4096, 8, 128, 16, 16, 1e-5, 500000.0
+    layers, seqs, seq_len = 32, 64, 4096
+    x_torch, x_kind = torch.float8_e4m3fn, "e4m3"
+    bytes_per_unit = 4096 + 4 + 4 + 4096 + 4096  # X fp8 + scale + sum of squares + K read/write + V read/write
+    workload = ("Llama-3-8B-shaped exact patch: 32 layers, d=4096, 8 KV heads x 128, 64 seqs x 4096 tokens, "
+                "rank-16 k/v LoRA (rel. norm 1e-2), fp8-e4m3 stored X + per-token scale + per-row sum of squared "
+                "codes (formed when the activations are stored), RMSNorm folded, RoPE (theta 5e5), bf16 paged KV "
+                "block 16, permuted block table")
+    profile = "exact_patch_kernel.md"
+    dtype = "f16 tensor-core products, fp32 accumulate (e4m3 X, bf16 pages)"
+
+
+class Smol135M(Llama8B):
+    name = "smollm2-exact"
+    metric = "patched token·layers/s (SmolLM2-135M shape, rank-8 k/v LoRA)"
+    d_model, n_kv, hd, rank, bs, eps, rope_theta = 576, 3, 64, 8, 16, 1e-5, 10000.0
+    layers, seqs, seq_len = 30, 32, 2048
+    x_torch, x_kind = torch.float16, "f16"
+    bytes_per_unit = 1152 + 4 + 4 + 768 + 768  # X f16 + row scale + sum of squares + K read/write + V read/write
+    workload = ("SmolLM2-135M-shaped exact patch: 30 layers, d=576, 3 KV heads x 64, 32 seqs x 2048 tokens, "
+                "rank-8 k/v LoRA (rel. norm 1e-2), f16 stored X + power-of-two row scale + per-row sum of squared "
+                "codes, RMSNorm folded, RoPE (theta 1e4), bf16 paged KV block 16, permuted block table")
+    profile = None
+    dtype = "f16 tensor-core products, fp32 accumulate (f16 X, bf16 pages)"
+
+
+def lora_scale(G) -> float:
+    """LoRA scale with E||s B A||_F = 1e-2 ||W||_F for W ~ N(0, 0.02^2), A ~ N(0, 1/d), B ~ N(0, 1)
+    (E||B A||_F^2 = d_kv * r): the same for every layer, whatever the split across ranks."""
+    d_kv = G.n_kv * G.hd
+    return 1e-2 * 0.02 * math.sqrt(d_kv * G.d_model) / math.sqrt(d_kv * G.rank)
+
+
+def make_exact_workload(G, layers, n_seqs, seq_len, device, seed):
+    """Synthetic inputs of the given layers; each layer's data comes from its own seed, so a
+    layer holds the same values whichever rank it lands on."""
+    import deltakv_b200 as dkv
+    from deltakv_b200 import ops
+
+    rows = n_seqs * seq_len
+    nl = len(layers)
+    d_kv = G.n_kv * G.hd
+    x = None
+    xs = torch.empty(nl, rows, dtype=torch.float32, device=device)
+    xq = torch.empty(nl, rows, dtype=torch.float32, device=device)  # per-row sum of squared codes
+    blocks_per_seq = (seq_len + G.bs - 1) // G.bs
+    nb = n_seqs * blocks_per_seq
+    caches = []
+    a_k = torch.empty(nl, G.rank, G.d_model, device=device)
+    b_k = torch.empty(nl, d_kv, G.rank, device=device)
+    a_v = torch.empty_like(a_k)
+    b_v = torch.empty_like(b_k)
+    norm_w = torch.empty(nl, G.d_model, device=device)
+    for i, l in enumerate(layers):
+        gen = torch.Generator(device=device).manual_seed(seed + 7919 * l)
+        # residual-stream-like rows: N(0,1) with a per-token magnitude spread
+        h = torch.randn(rows, G.d_model, generator=gen, device=device)
+        h *= (0.5 + torch.rand(rows, 1, generator=gen, device=device))
+        q, s, ssq = dkv.quantize_rows(h, G.x_torch, with_sumsq=True)
+        if x is None:
+            x = torch.empty(nl, rows, q.shape[-1], dtype=q.dtype, device=device)
+        x[i].copy_(q)
+        xs[i].copy_(s)
+        xq[i].copy_(ssq)
+        del h, q, s, ssq
+        c = torch.empty(2, nb, G.bs, G.n_kv, G.hd, dtype=torch.bfloat16, device=device)
+        c.normal_(generator=gen)
+        caches.append(c)
+        a_k[i] = torch.randn(G.rank, G.d_model, generator=gen, device=device) / math.sqrt(G.d_model)
+        b_k[i] = torch.randn(d_kv, G.rank, generator=gen, device=device)
+        a_v[i] = torch.randn(G.rank, G.d_model, generator=gen, device=device) / math.sqrt(G.d_model)
+        b_v[i] = torch.randn(d_kv, G.rank, generator=gen, device=device)
+        norm_w[i] = 1.0 + 0.05 * torch.randn(G.d_model, generator=gen, device=device)
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(seed + 2)).to(torch.int32)
+    tables = perm.view(n_seqs, blocks_per_seq).to(device)
+    s = lora_scale(G)
+    cu = torch.arange(0, n_seqs + 1, dtype=torch.int32, device=device) * seq_len
+    seqs = ops.SeqBatchTensors(cu_seqlens=cu, block_tables=tables, max_seq_len=seq_len)
+    rope = dkv.RotaryEmbedding(G.hd, max_seq=seq_len, base=G.rope_theta)
+    return dict(x=x, xs=xs, xq=xq, caches=caches, a_k=a_k, b_k=b_k, a_v=a_v, b_v=b_v, s=s, norm_w=norm_w,
+                seqs=seqs, rope=rope, tables=tables)
+
+
+def exact_reference_delta(G, wl, i, r0, r1, rope_tabs):
+    """Plain PyTorch fp32 restatement of the reference's exact branch for rows [r0, r1) of
+    held layer i: dequantise, RMSNorm (x * rsqrt(mean(x^2) + eps) * w, src/deltakv/model.py:
+    48-56), codes = s x A^T and delta = codes B^T (deltas/factors.py:61-67), RoPE on K with the
+    rotate-half pairing at positions 0.. (rope.py:9-25).  Returns (dK, dV) [n, n_kv, hd] fp32."""
+    n = r1 - r0
+    x = wl["x"][i, r0:r1, :G.d_model].float() * wl["xs"][i, r0:r1, None]
+    x = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + G.eps) * wl["norm_w"][i]
+    s = wl["s"]
+    dk = ((s * (x @ wl["a_k"][i].T)) @ wl["b_k"][i].T).view(n, G.n_kv, G.hd)
+    dv = ((s * (x @ wl["a_v"][i].T)) @ wl["b_v"][i].T).view(n, G.n_kv, G.hd)
+    cos, sin = rope_tabs
+    c, sn = cos[:n, None, :], sin[:n, None, :]
+    h = G.hd // 2
+    k1, k2 = dk[..., :h], dk[..., h:]
+    dk = torch.cat([k1 * c - k2 * sn, k2 * c + k1 * sn], dim=-1)
+    return dk, dv
+
+
+class CpuSample:
+    """A bounded sample of the exact workload on the host: P distinct (layer, sequence)
+    inputs, one private paged K/V per worker thread (a single sequence's blocks)."""
+
+    def __init__(self, G, n_inputs: int, seq_len: int, seed: int = 5):
         from oracle import exact as OX
 
-        G = Geo
+        self.G = G
         g = torch.Generator().manual_seed(seed)
         self.seq_len = seq_len
         self.inputs = []
-        facs, norm_w = make_factors(n_inputs, "cpu", g)
-        for i in range(n_inputs):
+        d_kv = G.n_kv * G.hd
+        s = lora_scale(G)
+        for _ in range(n_inputs):
             h = torch.randn(seq_len, G.d_model, generator=g) * (0.5 + torch.rand(seq_len, 1, generator=g))
             amax = h.abs().amax(-1).clamp_min(1e-12)
-            s = (amax / 448.0).float()
+            sc = (amax / 448.0).float()
             if G.x_kind == "e4m3":
-                xb = (h / s[:, None]).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+                xb = (h / sc[:, None]).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
             else:
-                xb = (h / s[:, None]).to(torch.float16).numpy()
-            fk = (facs["k"][0][i].numpy(), facs["k"][1][i].numpy(), facs["k"][2])
-            fv = (facs["v"][0][i].numpy(), facs["v"][1][i].numpy(), facs["v"][2])
-            self.inputs.append((xb, s.numpy(), norm_w[i].numpy(), fk, fv))
+                xb = (h / sc[:, None]).to(torch.float16).numpy()
+            fk = ((torch.randn(G.rank, G.d_model, generator=g) / math.sqrt(G.d_model)).numpy(),
+                  torch.randn(d_kv, G.rank, generator=g).numpy(), s)
+            fv = ((torch.randn(G.rank, G.d_model, generator=g) / math.sqrt(G.d_model)).numpy(),
+                  torch.randn(d_kv, G.rank, generator=g).numpy(), s)
+            w = (1.0 + 0.05 * torch.randn(G.d_model, generator=g)).numpy()
+            self.inputs.append((xb, sc.numpy(), w, fk, fv))
         self.rope = OX.rope_tables(G.hd, seq_len, G.rope_theta)
         nblk = (seq_len + G.bs - 1) // G.bs
         self.table = list(np.random.default_rng(seed).permutation(nblk))
         self.nblk = nblk
 
     def new_pages(self):
-        G = Geo
+        G = self.G
         rng = np.random.default_rng(0)
         shape = (self.nblk, G.bs, G.n_kv, G.hd)
         return (rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16),
@@ -260,7 +397,7 @@ class CpuSample:
         exact_kv_patch -> materialize -> scatter_into_paged (K and V).  Returns units."""
         from oracle import exact as OX
 
-        G = Geo
+        G = self.G
         xb, s, w, fk, fv = self.inputs[i % len(self.inputs)]
         x = OX.dequant_x(xb, G.x_kind, s)
         x = OX.rmsnorm(x, w, G.eps)
@@ -268,6 +405,22 @@ class CpuSample:
         OX.scatter_into_paged(dk, kp, self.table, G.bs, kind="bf16")
         OX.scatter_into_paged(dv, vp, self.table, G.bs, kind="bf16")
         return self.seq_len
+
+    def dequant_share(self, reps: int = 2) -> float:
+        """Fraction of one pair's single-thread time spent in the fp8/f16 dequantisation
+        (which has no counterpart in the reference, whose activations are fp32)."""
+        from oracle import exact as OX
+
+        kp, vp = self.new_pages()
+        xb, s, *_ = self.inputs[0]
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            OX.dequant_x(xb, self.G.x_kind, s)
+        t_deq = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            self.patch_one(0, kp, vp)
+        return t_deq / (time.perf_counter() - t0)
 
     def run(self, threads: int, seconds: float | None = None, pairs: int | None = None):
         """Process pairs on `threads` workers for `seconds` (or `pairs` pairs); returns
@@ -301,81 +454,48 @@ class CpuSample:
         return units, el
 
 
-def cpu_baseline(seconds: float, seq_len: int) -> dict:
+def exact_cpu_baseline(G, seconds: float, seq_len: int) -> dict:
+    from threadpoolctl import threadpool_limits
+
     threads = cpu_pool_threads()
-    sample = CpuSample(n_inputs=4, seq_len=seq_len)
+    sample = CpuSample(G, n_inputs=4, seq_len=seq_len)
+    with threadpool_limits(1):
+        share = sample.dequant_share()
     sample.run(threads, pairs=threads)  # warm-up: every thread once
     units, el = sample.run(threads, seconds=seconds)
-    return {"value": units / el, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{units // seq_len} (layer, sequence) pairs of {seq_len} tokens in {el:.1f} s "
-                      f"(oracle numpy port of the reference's exact branch, {threads} threads)"}
+    return {"value": units / el, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
+            "sample": f"{units // seq_len} (layer, sequence) pairs of {seq_len} tokens in {el:.1f} s (oracle "
+                      f"numpy port of the reference's exact branch: dequant, RMSNorm, exact_kv_patch, materialize, "
+                      f"scatter_into_paged; {threads} threads, one pair per thread)",
+            "dequant_share": share,
+            "dequant_note": "fraction of a pair's time in the stored-activation dequantisation, timed on its own "
+                            "(the reference keeps fp32 activations and has no such step)",
+            "sumsq_note": "the CPU port forms RMSNorm's sum of squares from X; the GPU arm reads the per-row sums "
+                          "stored with X"}
 
 
-# ---------------------------------------------------------------------------
-# arms
-# ---------------------------------------------------------------------------
-def dist_setup(args):
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
-
-
-def run_reference(args):
-    world, rank, _ = dist_setup(args)
-    if rank != 0:
-        return 0
-    threads = cpu_pool_threads()
-    sample = CpuSample(n_inputs=4, seq_len=args.seq_len)
-    for _ in range(args.warmup):
-        sample.run(threads, pairs=threads)
-    units_tot, el_tot = 0, 0.0
-    for _ in range(args.steps):
-        u, el = sample.run(threads, pairs=threads)
-        units_tot += u
-        el_tot += el
-    value = units_tot / el_tot
-    line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el_tot / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "step": f"{threads} (layer, sequence) pairs of {args.seq_len} tokens "
-                   "(bounded sample of the workload)"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{threads} (layer, sequence) pairs per step, oracle numpy port of the "
-                                   "reference's exact branch (dequant, RMSNorm, exact_kv_patch, materialize, "
-                                   "scatter_into_paged)"},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-    return 0
-
-
-def run_ours(args):
+def run_exact(args, dist: Dist, G) -> dict:
     import deltakv_b200 as dkv
+    from deltakv_b200 import metrics, ops
 
-    world, rank, local = dist_setup(args)
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                             device_id=dev)
-    G = Geo
-    wl = make_workload(args.layers, args.seqs, args.seq_len, dev, seed=1000 + rank)
-    facs = wl["facs"]
-    patcher = dkv.ExactPatcher(G.d_model, G.n_kv, G.hd, rank_k=G.rank, rank_v=G.rank,
-                               x_dtype=G.x_torch, rope=wl["rope"], norm_eps=G.eps)
-    packed = torch.empty(args.layers, patcher.packed_bytes, dtype=torch.uint8, device=dev)
+    dev = dist.dev
+    L_total, n_seqs, n = args.layers, args.seqs, args.seq_len
+    layers = my_layers(L_total, dist, args.shard)
+    weak = args.shard != "layer" and dist.world > 1
+    seed = 1000 + (dist.rank * 100003 if weak else 0)
+    wl = make_exact_workload(G, layers, n_seqs, n, dev, seed)
+    patcher = dkv.ExactPatcher(G.d_model, G.n_kv, G.hd, rank_k=G.rank, rank_v=G.rank, x_dtype=G.x_torch,
+                               rope=wl["rope"], norm_eps=G.eps)
+    packed = torch.empty(len(layers), patcher.packed_bytes, dtype=torch.uint8, device=dev)
     kpages = [c[0] for c in wl["caches"]]
     vpages = [c[1] for c in wl["caches"]]
-    units = args.layers * args.seqs * args.seq_len
+    units_rank = len(layers) * n_seqs * n
+    units_step = (L_total * n_seqs * n) if not weak else units_rank * dist.world
     stream = torch.cuda.current_stream()
 
     def step(ev=None):
-        patcher.pack(facs["k"][0], facs["k"][1], facs["v"][0], facs["v"][1], facs["k"][2], facs["v"][2],
-                     norm_weight=wl["norm_w"], out=packed)
+        patcher.pack(wl["a_k"], wl["b_k"], wl["a_v"], wl["b_v"], wl["s"], wl["s"], norm_weight=wl["norm_w"],
+                     out=packed)
         if ev is not None:
             ev[0].record(stream)
         patcher.apply(wl["x"], packed, kpages, vpages, wl["seqs"], x_scale=wl["xs"], apply_norm=True,
@@ -383,155 +503,174 @@ def run_ours(args):
         if ev is not None:
             ev[1].record(stream)
 
-    # correctness guard before timing: device status clean after one step
     step()
     torch.cuda.synchronize()
-    from deltakv_b200 import ops
-
     ops.status_word(dev).raise_if_set("bench warm-up")
     for _ in range(max(0, args.warmup - 1)):
         step()
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        t_start.record(stream)
-        for i in range(args.steps):
-            step(kev[i])
-        t_end.record(stream)
-        torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    ms = t_start.elapsed_time(t_end)
-    kern_ms = [a.elapsed_time(b) for a, b in kev]
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
+    ms, kern, clocks = timed(dist, step, args.steps)
     ops.status_word(dev).raise_if_set("bench timed region")
     ms_step = ms / args.steps
-    value = units * world / (ms_step / 1e3)
-    kmean = sum(kern_ms) / len(kern_ms)
-    achieved = units * BYTES_PER_UNIT / (kmean / 1e3) / 1e9
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except Exception:
-        pass
-    peak = peaks.get("hbm_gbs")
-    peak_kind = "of measured (MEASURED_PEAKS.json hbm_gbs, burst copy)" if peak else "of fallback (6650 GB/s)"
-    peak = peak or 6650.0
-    traffic = None  # DRAM bytes per launch from the committed ncu summary (full workload)
-    tfile = ROOT / "profiles" / "exact_patch_kernel.md"
-    if tfile.exists() and args.layers == 32 and args.seqs == 64 and args.seq_len == 4096:
-        for line in tfile.read_text().splitlines():
-            if line.startswith("traffic_bytes_per_launch_full_workload:"):
-                traffic = int(line.split(":", 1)[1])
+    kmean = sum(kern) / len(kern)
+    kmax = dist.max(kmean)
+    achieved = units_rank * G.bytes_per_unit / (kmean / 1e3) / 1e9
+    peak, peak_kind = hbm_peak()
+    frac_min = dist.min(achieved / peak)
+    traffic = traffic_from_profile(G.profile, units_rank)
 
-    layer_errors = measure_layer_errors(args, wl["seqs"], kpages, vpages, step, dev, world)
-    e2e = None
-    if not args.no_e2e:
-        e2e = run_e2e(args, patcher, dev, world)
-    del wl, kpages, vpages
-    torch.cuda.empty_cache()
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(args.cpu_seconds, args.seq_len)
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16 tensor-core products, fp32 accumulate (e4m3 X, bf16 pages)",
-            "data": "synthetic",
-            "config": {"workload": WORKLOAD, "layers": args.layers, "seqs_per_gpu": args.seqs,
-                       "seq_len": args.seq_len, "units_per_step_per_gpu": units,
-                       "parallelism": f"request shards x{world} (weak)",
-                       "l2": f"inputs {units * BYTES_PER_UNIT / 1e9:.1f} GB per GPU >> 126 MB L2, no flush needed",
-                       "launches_per_step": 2},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
-                         "kernel": "patch_kernel", "kernel_ms": kmean,
-                         "algorithmic_bytes_per_unit": BYTES_PER_UNIT},
-            "cpu_baseline": cpu,
-            "e2e": e2e,
-            "gpu_launches": 2 * args.steps,
-            "clocks": clk.summary(),
-            "layer_errors": layer_errors,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
-    return 0
-
-
-def measure_layer_errors(args, seqs, kpages, vpages, step, dev, world):
-    """After the timed region: per-layer measured error (compose.py:147-163 formula) of one
-    more patch step on sequence 0 — the stale pages against the patched ones, i.e. the error a
-    cache would carry without the patch — then the NCCL all-gather of those scalars over the
-    ranks (the path's only collective)."""
-    from deltakv_b200 import metrics, ops
-
-    n = args.seq_len
-    one = ops.SeqBatchTensors(cu_seqlens=seqs.cu_seqlens[:2].clone(), block_tables=seqs.block_tables[:1].contiguous(),
-                              max_seq_len=n)
-    L_ = len(kpages)
-    nkv, hd = kpages[0].shape[2], kpages[0].shape[3]
-    stale_k = torch.empty(L_, n, nkv, hd, dtype=kpages[0].dtype, device=dev)
+    # --- after the timed region: one more step with sequence 0 of every held layer gathered
+    # before and after it -> the parity spot check and the per-layer measured errors
+    one = ops.SeqBatchTensors(cu_seqlens=wl["seqs"].cu_seqlens[:2].clone(),
+                              block_tables=wl["seqs"].block_tables[:1].contiguous(), max_seq_len=n)
+    nl = len(layers)
+    stale_k = torch.empty(nl, n, G.n_kv, G.hd, dtype=torch.bfloat16, device=dev)
     stale_v = torch.empty_like(stale_k)
-    for l in range(L_):
-        ops.gather_paged(kpages[l], one, stale_k[l])
-        ops.gather_paged(vpages[l], one, stale_v[l])
+    for i in range(nl):
+        ops.gather_paged(kpages[i], one, stale_k[i])
+        ops.gather_paged(vpages[i], one, stale_v[i])
     step()
-    local = metrics.measured_error_paged(kpages, vpages, stale_k, stale_v, one, check=True)
+    local_err = metrics.measured_error_paged(kpages, vpages, stale_k, stale_v, one, check=True)
     t0 = time.perf_counter()
-    gathered = metrics.gather_layer_errors(local)
+    if weak:  # every rank holds the same layer indices of its own cache
+        full_err = metrics.gather_layer_errors(local_err).reshape(-1)
+    else:
+        full_err = metrics.gather_sharded_layer_errors(local_err, layers, L_total)
     torch.cuda.synchronize()
     gather_ms = 1e3 * (time.perf_counter() - t0)
-    g = gathered.cpu()
-    return {"what": "per-layer relative KV change of one patch step on sequence 0 (stale vs patched)",
-            "max": float(g.max()), "mean": float(g.mean()), "ranks": world, "layers_per_rank": L_,
-            "collective": "all_gather_into_tensor (nccl)" if world > 1 else "none (single rank)",
-            "gather_wall_ms": gather_ms}
+    fe = full_err.cpu()
+    layer_errors = {"what": "per-layer relative KV change of one patch step on sequence 0 (stale vs patched), "
+                            "compose.py:147-163's formula summed from the pages",
+                    "layers": int(fe.numel()), "max": float(fe.max()), "mean": float(fe.mean()),
+                    "ranks": dist.world, "layers_per_rank": nl,
+                    "collective": ("all_gather_into_tensor (nccl) of [layers] vectors over disjoint layer sets"
+                                   if dist.world > 1 else "none (single rank)"),
+                    "gather_wall_ms": gather_ms}
+    parity = exact_parity(G, wl, patcher, packed, kpages, vpages, stale_k, stale_v, layers, n, dev)
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_exact_e2e(args, G, patcher, dist, layers, weak)
+    del wl, kpages, vpages, stale_k, stale_v
+    torch.cuda.empty_cache()
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+        cpu = exact_cpu_baseline(G, args.cpu_seconds if G is Llama8B else args.sub_cpu_seconds, n)
+    return {
+        "metric": G.metric, "value": units_step / (ms_step / 1e3), "unit": UNIT, "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": G.dtype, "data": "synthetic",
+        "config": {"workload": G.workload, "layers": L_total, "seqs": n_seqs, "seq_len": n,
+                   "units_per_step": units_step, "layers_per_rank": nl,
+                   "parallelism": (f"request shards x{dist.world} (weak)" if weak else
+                                   f"layer shards x{dist.world}: layer l on rank l mod {dist.world} (strong)"),
+                   "l2": f"inputs {units_rank * G.bytes_per_unit / 1e9:.1f} GB per GPU >> 126 MB L2, no flush needed",
+                   "launches_per_step": 2,
+                   "e2e_sample": None if e2e is None else e2e["sample"]},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "peak_source": peak_kind, "kernel": "exact::patch_kernel_tc",
+                     "kernel_ms": kmean, "kernel_ms_max_over_ranks": kmax, "frac_min_over_ranks": frac_min,
+                     "algorithmic_bytes_per_unit": G.bytes_per_unit, "units_per_launch": units_rank},
+        "parity": parity,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks,
+        "layer_errors": layer_errors,
+    }
 
 
-def run_e2e(args, patcher, dev, world):
+def traffic_from_profile(name, units_rank):
+    """DRAM bytes per launch from the committed ncu summary, scaled to this launch's units
+    (the summary states bytes per token-layer measured on a capture whose writes exceed L2)."""
+    if not name:
+        return None
+    f = ROOT / "profiles" / name
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.startswith("dram_bytes_per_unit:"):
+            try:
+                return int(float(line.split(":", 1)[1]) * units_rank)
+            except ValueError:
+                return None
+    return None
+
+
+def exact_parity(G, wl, patcher, packed, kpages, vpages, stale_k, stale_v, layers, n, dev):
+    """Spot check of the timed workload: held layer 0, sequence 0, after the step above.
+    (1) the bf16 pages against round_bf16(stale + delta_ref); (2) the delta alone, written by
+    the same kernel into zeroed fp32 pages, against delta_ref (a plain PyTorch fp32
+    restatement of the reference's exact branch)."""
+    from deltakv_b200 import ops
+    from deltakv_b200.rope import half_tables
+
+    i = 0
+    tabs = half_tables(wl["rope"], dev)
+    one = ops.SeqBatchTensors(cu_seqlens=wl["seqs"].cu_seqlens[:2].clone(),
+                              block_tables=wl["seqs"].block_tables[:1].contiguous(), max_seq_len=n)
+    dk, dv = exact_reference_delta(G, wl, i, 0, n, tabs)
+    got_k = torch.empty(n, G.n_kv, G.hd, dtype=torch.bfloat16, device=dev)
+    got_v = torch.empty_like(got_k)
+    ops.gather_paged(kpages[i], one, got_k)
+    ops.gather_paged(vpages[i], one, got_v)
+    out = {}
+    eq, err = [], []
+    for got, stale, d in ((got_k, stale_k[i], dk), (got_v, stale_v[i], dv)):
+        want = (stale.float() + d).to(torch.bfloat16)
+        err.append(rel_l2(got.float(), want.float()))
+        eq.append(float((got.view(torch.int16) == want.view(torch.int16)).float().mean()))
+    out["pages_rel_l2"] = max(err)
+    out["pages_bit_equal"] = min(eq)
+    # (2) delta alone into fp32 pages
+    nblk = (n + G.bs - 1) // G.bs
+    kp32 = torch.zeros(nblk, G.bs, G.n_kv, G.hd, device=dev)
+    vp32 = torch.zeros_like(kp32)
+    tab = ops.SeqBatchTensors(cu_seqlens=wl["seqs"].cu_seqlens[:2].clone(),
+                              block_tables=torch.arange(nblk, dtype=torch.int32, device=dev)[None].contiguous(),
+                              max_seq_len=n)
+    patcher.apply(wl["x"][i:i + 1], packed[i:i + 1], [kp32], [vp32], tab, x_scale=wl["xs"][i:i + 1],
+                  apply_norm=True, x_sumsq=wl["xq"][i:i + 1], check=True)
+    dk_got = kp32.view(-1, G.n_kv, G.hd)[:n]
+    dv_got = vp32.view(-1, G.n_kv, G.hd)[:n]
+    out["delta_rel_l2"] = max(rel_l2(dk_got, dk), rel_l2(dv_got, dv))
+    out["tolerance"] = 1e-3
+    out["pass"] = bool(out["pages_rel_l2"] <= 1e-3 and out["delta_rel_l2"] <= 1e-3)
+    out["sample"] = f"layer {layers[i]}, sequence 0 ({n} tokens), K and V"
+    out["reference"] = "plain PyTorch fp32 restatement of RMSNorm -> exact_kv_patch -> materialize (+ scatter)"
+    return out
+
+
+def run_exact_e2e(args, G, patcher, dist: Dist, layers, weak):
     """Same metric through the public API with host buffers: every step copies the step's
-    stored activations, scales, factors, block tables and the touched pages host->device,
-    patches, and copies the pages back."""
-    import deltakv_b200 as dkv
+    stored activations, scales, sums of squares, factors, block tables and the touched pages
+    host->device, patches, and copies the pages back (pipelined by layer)."""
     from deltakv_b200 import ops
 
-    G = Geo
+    dev = dist.dev
     n_seqs = args.e2e_seqs
-    cpu = make_workload(args.layers, n_seqs, args.seq_len, dev, seed=77)
+    cpu = make_exact_workload(G, layers, n_seqs, args.seq_len, dev, seed=77)
     host = {
         "x": cpu["x"].view(torch.uint8).cpu().pin_memory(),
         "xs": cpu["xs"].cpu().pin_memory(),
         "xq": cpu["xq"].cpu().pin_memory(),
         "caches": torch.stack(cpu["caches"]).cpu().pin_memory(),
         "tables": cpu["tables"].cpu().pin_memory(),
-        "a_k": cpu["facs"]["k"][0].cpu().pin_memory(), "b_k": cpu["facs"]["k"][1].cpu().pin_memory(),
-        "a_v": cpu["facs"]["v"][0].cpu().pin_memory(), "b_v": cpu["facs"]["v"][1].cpu().pin_memory(),
+        "a_k": cpu["a_k"].cpu().pin_memory(), "b_k": cpu["b_k"].cpu().pin_memory(),
+        "a_v": cpu["a_v"].cpu().pin_memory(), "b_v": cpu["b_v"].cpu().pin_memory(),
         "norm_w": cpu["norm_w"].cpu().pin_memory(),
     }
-    sk, sv = cpu["facs"]["k"][2], cpu["facs"]["v"][2]
+    s = cpu["s"]
     del cpu
     torch.cuda.empty_cache()
     d = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
-    packed = torch.empty(args.layers, patcher.packed_bytes, dtype=torch.uint8, device=dev)
+    nl = len(layers)
+    packed = torch.empty(nl, patcher.packed_bytes, dtype=torch.uint8, device=dev)
     cu = torch.arange(0, n_seqs + 1, dtype=torch.int32, device=dev) * args.seq_len
     stream = torch.cuda.current_stream()
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = host["caches"].numel() * host["caches"].element_size()
-
-    # Layer-pipelined: host->device copies of layer l+1 (one copy engine), the patch of layer l
-    # (compute stream) and the device->host copy of layer l-1 (the other copy engine) overlap.
     h2d_s, d2h_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     seqs = ops.SeqBatchTensors(cu_seqlens=cu, block_tables=d["tables"], max_seq_len=args.seq_len)
     small = ("tables", "a_k", "b_k", "a_v", "b_v", "norm_w")
-    n_layers = args.layers
 
     def step():
         start = torch.cuda.Event()
@@ -543,18 +682,16 @@ def run_e2e(args, patcher, dev, world):
             ev_small = torch.cuda.Event()
             ev_small.record(h2d_s)
             ev_in = []
-            for l in range(n_layers):
-                d["x"][l].copy_(host["x"][l], non_blocking=True)
-                d["xs"][l].copy_(host["xs"][l], non_blocking=True)
-                d["xq"][l].copy_(host["xq"][l], non_blocking=True)
-                d["caches"][l].copy_(host["caches"][l], non_blocking=True)
+            for l in range(nl):
+                for k in ("x", "xs", "xq", "caches"):
+                    d[k][l].copy_(host[k][l], non_blocking=True)
                 e = torch.cuda.Event()
                 e.record(h2d_s)
                 ev_in.append(e)
         stream.wait_event(ev_small)
-        patcher.pack(d["a_k"], d["b_k"], d["a_v"], d["b_v"], sk, sv, norm_weight=d["norm_w"], out=packed)
+        patcher.pack(d["a_k"], d["b_k"], d["a_v"], d["b_v"], s, s, norm_weight=d["norm_w"], out=packed)
         xv = d["x"].view(G.x_torch)
-        for l in range(n_layers):
+        for l in range(nl):
             stream.wait_event(ev_in[l])
             patcher.apply(xv[l:l + 1], packed[l:l + 1], [d["caches"][l][0]], [d["caches"][l][1]], seqs,
                           x_scale=d["xs"][l:l + 1], apply_norm=True, x_sumsq=d["xq"][l:l + 1])
@@ -570,65 +707,100 @@ def run_e2e(args, patcher, dev, world):
     for _ in range(2):
         step()
     torch.cuda.synchronize()
-    n = 3
+    reps = 3
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        torch.distributed.barrier()
+    dist.barrier()
     a.record(stream)
-    for _ in range(n):
+    for _ in range(reps):
         step()
     b.record(stream)
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / n
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    units = args.layers * n_seqs * args.seq_len * world
+    ms = dist.max(a.elapsed_time(b) / reps)
+    # layer shards (or one GPU): all layers of the sample across the ranks; request shards: every rank's
+    units = (nl * dist.world if weak else args.layers) * n_seqs * args.seq_len
     del d, host
     torch.cuda.empty_cache()
     return {"value": units / (ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "ms_per_step": ms, "sample": f"{n_seqs} seqs x {args.layers} layers per GPU, pinned host buffers, "
-                                        "host->device / patch / device->host pipelined by layer"}
+            "ms_per_step": ms,
+            "sample": f"{n_seqs} seqs x {nl} layers per GPU ({n_seqs} of {args.seqs} sequences), pinned host "
+                      "buffers, host->device / patch / device->host pipelined by layer"}
+
+
+def run_exact_reference(args, G) -> dict:
+    threads = cpu_pool_threads()
+    sample = CpuSample(G, n_inputs=4, seq_len=args.seq_len)
+    for _ in range(args.warmup):
+        sample.run(threads, pairs=threads)
+    units_tot, el_tot = 0, 0.0
+    for _ in range(args.steps):
+        u, el = sample.run(threads, pairs=threads)
+        units_tot += u
+        el_tot += el
+    value = units_tot / el_tot
+    return {
+        "impl": "reference", "metric": G.metric, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el_tot / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": G.workload, "step": f"{threads} (layer, sequence) pairs of {args.seq_len} tokens "
+                   "(bounded sample of the workload)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
+                         "sample": f"{threads} (layer, sequence) pairs per step, oracle numpy port of the "
+                                   "reference's exact branch (dequant, RMSNorm, exact_kv_patch, materialize, "
+                                   "scatter_into_paged), one pair per thread"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
 
 
 # ---------------------------------------------------------------------------
 # rl-dense workload: full-rank dW on k_proj / v_proj (tensor-core GEMM route)
 # ---------------------------------------------------------------------------
-DENSE_METRIC = "patched token·layers/s (Llama-70B shape, dense dW RL step)"
-DENSE_WORKLOAD = ("Llama-3-70B-shaped RL-step dense delta, one GPU's share: 10 of 80 layers, d=8192, 8 KV heads "
-                  "x 128, 16 seqs x 8192 tokens, bf16 stored X (post-norm), full-rank dW_K/dW_V Gaussian with "
-                  "||dW||/||W|| = 1e-3, RoPE (theta 5e5) on K, bf16 paged KV block 16, permuted block table")
+class Dense70B:
+    name = "rl-dense"
+    metric = "patched token·layers/s (Llama-70B shape, dense dW RL step)"
+    layers, seqs, seq_len, d_model, n_kv, hd, bs, rope_theta = 80, 16, 8192, 8192, 8, 128, 16, 500000.0
+    x_buffers = 10  # distinct stored-X buffers; layer l reads buffer l mod 10
+    layers_per_launch = 10
+    workload = ("Llama-3-70B-shaped RL-step dense delta: 80 layers, d=8192, 8 KV heads x 128, 16 seqs x 8192 "
+                "tokens, bf16 stored X (post-norm), full-rank dW_K/dW_V Gaussian with ||dW||/||W|| = 1e-3, RoPE "
+                "(theta 5e5) on K, bf16 paged KV block 16, permuted block table")
 
 
 def dense_flops_per_unit() -> float:
-    G = DenseGeo
+    G = Dense70B
     return 2.0 * G.d_model * 2 * G.n_kv * G.hd
 
 
-def make_dense_workload(n_layers, n_seqs, seq_len, device, seed):
+def make_dense_workload(layers, n_seqs, seq_len, device, seed, x_buffers: int | None = None):
+    """Pages and dW of the given layers (per-layer seeds) and the stored X.  The 80 layers'
+    X would take 172 GB; ``x_buffers`` distinct [tokens, d] buffers stand in for it and
+    layer l reads buffer l mod x_buffers (2.1 GB each, far beyond L2, so every layer's
+    launch still streams its X from HBM)."""
     import deltakv_b200 as dkv
     from deltakv_b200 import ops
 
-    G = DenseGeo
-    gen = torch.Generator(device=device).manual_seed(seed)
+    G = Dense70B
     rows = n_seqs * seq_len
     d_kv = G.n_kv * G.hd
-    x = torch.empty(n_layers, rows, G.d_model, dtype=torch.bfloat16, device=device)
-    for l in range(n_layers):
-        x[l].normal_(generator=gen)
+    nxb = x_buffers or len(layers)
+    x = torch.empty(nxb, rows, G.d_model, dtype=torch.bfloat16, device=device)
+    for j in range(nxb):
+        x[j].normal_(generator=torch.Generator(device=device).manual_seed(seed + 31 * j))
     sigma = 1e-3 * 0.02  # ||dW|| / ||W|| = 1e-3 for W ~ N(0, 0.02^2)
-    dw_k = (torch.randn(n_layers, d_kv, G.d_model, generator=gen, device=device) * sigma).to(torch.bfloat16)
-    dw_v = (torch.randn(n_layers, d_kv, G.d_model, generator=gen, device=device) * sigma).to(torch.bfloat16)
+    nl = len(layers)
+    dw_k = torch.empty(nl, d_kv, G.d_model, dtype=torch.bfloat16, device=device)
+    dw_v = torch.empty_like(dw_k)
     blocks_per_seq = (seq_len + G.bs - 1) // G.bs
     nb = n_seqs * blocks_per_seq
-    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(seed + 2)).to(torch.int32)
-    tables = perm.view(n_seqs, blocks_per_seq).to(device)
     caches = []
-    for _ in range(n_layers):
+    for i, l in enumerate(layers):
+        gen = torch.Generator(device=device).manual_seed(seed + 7919 * (l + 1))
+        dw_k[i] = (torch.randn(d_kv, G.d_model, generator=gen, device=device) * sigma).to(torch.bfloat16)
+        dw_v[i] = (torch.randn(d_kv, G.d_model, generator=gen, device=device) * sigma).to(torch.bfloat16)
         c = torch.empty(2, nb, G.bs, G.n_kv, G.hd, dtype=torch.bfloat16, device=device)
         c.normal_(generator=gen)
         caches.append(c)
+    perm = torch.randperm(nb, generator=torch.Generator().manual_seed(seed + 2)).to(torch.int32)
+    tables = perm.view(n_seqs, blocks_per_seq).to(device)
     cu = torch.arange(0, n_seqs + 1, dtype=torch.int32, device=device) * seq_len
     seqs = ops.SeqBatchTensors(cu_seqlens=cu, block_tables=tables, max_seq_len=seq_len)
     rope = dkv.RotaryEmbedding(G.hd, max_seq=seq_len, base=G.rope_theta)
@@ -645,7 +817,7 @@ class DenseCpuSample:
         from oracle import dense as OD
         from oracle import exact as OX
 
-        G = DenseGeo
+        G = Dense70B
         g = torch.Generator().manual_seed(seed)
         d_kv = G.n_kv * G.hd
         self.x = (torch.randn(self.CHUNK, G.d_model, generator=g)).to(torch.bfloat16).float().numpy()
@@ -657,7 +829,7 @@ class DenseCpuSample:
         self.table = list(np.random.default_rng(seed).permutation(self.nblk))
 
     def new_pages(self):
-        G = DenseGeo
+        G = Dense70B
         rng = np.random.default_rng(0)
         shape = (self.nblk, G.bs, G.n_kv, G.hd)
         return (rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16),
@@ -666,7 +838,7 @@ class DenseCpuSample:
     def patch_one(self, kp, vp) -> int:
         from oracle import exact as OX
 
-        G = DenseGeo
+        G = Dense70B
         dk, dv = OX.exact_kv_delta(self.x, self.fk, self.fv, G.n_kv, G.hd, self.rope)
         OX.scatter_into_paged(dk, kp, self.table, G.bs, kind="bf16")
         OX.scatter_into_paged(dv, vp, self.table, G.bs, kind="bf16")
@@ -701,18 +873,8 @@ class DenseCpuSample:
         return units, el
 
 
-def dense_cpu_threads() -> int:
-    try:
-        return len(os.sched_getaffinity(0))
-    except AttributeError:
-        return os.cpu_count() or 1
-
-
-def run_dense_reference(args):
-    world, rank, _ = dist_setup(args)
-    if rank != 0:
-        return 0
-    threads = dense_cpu_threads()
+def run_dense_reference(args) -> dict:
+    threads = host_threads()
     sample = DenseCpuSample()
     for _ in range(args.warmup):
         sample.run(threads, items=threads)
@@ -722,46 +884,49 @@ def run_dense_reference(args):
         units_tot += u
         el_tot += el
     value = units_tot / el_tot
-    line = {
-        "impl": "reference", "metric": DENSE_METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+    return {
+        "impl": "reference", "metric": Dense70B.metric, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el_tot / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": DENSE_WORKLOAD, "step": f"{threads} (layer, {DenseCpuSample.CHUNK}-token chunk) "
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": Dense70B.workload, "step": f"{threads} (layer, {DenseCpuSample.CHUNK}-token chunk) "
                    "items (bounded sample of the workload)"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
                          "sample": f"{threads} items per step, oracle numpy port of the reference's exact route "
                                    "with A=dW, B=I (x @ dW^T, RoPE, scatter_into_paged)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
-    return 0
 
 
-def run_dense_ours(args):
+def run_dense(args, dist: Dist) -> dict:
     import deltakv_b200 as dkv
     from deltakv_b200 import ops
+    from deltakv_b200.rope import half_tables
 
-    world, rank, local = dist_setup(args)
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    G = DenseGeo
-    wl = make_dense_workload(args.layers, args.seqs, args.seq_len, dev, seed=2000 + rank)
+    G = Dense70B
+    dev = dist.dev
+    weak = args.shard != "layer" and dist.world > 1
+    layers = my_layers(args.layers, dist, args.shard)
+    nl = len(layers)
+    per = min(G.layers_per_launch, nl)
+    nxb = min(G.x_buffers, per)
+    wl = make_dense_workload(layers, args.seqs, args.seq_len, dev,
+                             seed=2000 + (dist.rank * 100003 if weak else 0), x_buffers=nxb)
     patcher = dkv.DensePatcher(G.d_model, G.n_kv, G.hd, rope=wl["rope"])
-    packed = torch.empty(args.layers, 2 * G.n_kv * G.hd, G.d_model, dtype=torch.bfloat16, device=dev)
+    packed = torch.empty(nl, 2 * G.n_kv * G.hd, G.d_model, dtype=torch.bfloat16, device=dev)
     kpages = [c[0] for c in wl["caches"]]
     vpages = [c[1] for c in wl["caches"]]
-    units = args.layers * args.seqs * args.seq_len
+    units_rank = nl * args.seqs * args.seq_len
+    units_step = units_rank * dist.world if weak else args.layers * args.seqs * args.seq_len
     stream = torch.cuda.current_stream()
+    groups = [list(range(j, min(j + per, nl))) for j in range(0, nl, per)]
 
     def step(ev=None):
         patcher.pack(wl["dw_k"], wl["dw_v"], out=packed)
         if ev is not None:
             ev[0].record(stream)
-        patcher.apply(wl["x"], packed, kpages, vpages, wl["seqs"])
+        for grp in groups:  # each launch: `per` layers, layer g reads X buffer g mod nxb
+            patcher.apply(wl["x"][:len(grp)], packed[grp[0]:grp[-1] + 1], kpages[grp[0]:grp[-1] + 1],
+                          vpages[grp[0]:grp[-1] + 1], wl["seqs"])
         if ev is not None:
             ev[1].record(stream)
 
@@ -770,99 +935,101 @@ def run_dense_ours(args):
     ops.status_word(dev).raise_if_set("bench warm-up")
     for _ in range(max(0, args.warmup - 1)):
         step()
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        t_start.record(stream)
-        for i in range(args.steps):
-            step(kev[i])
-        t_end.record(stream)
-        torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
-    ms = t_start.elapsed_time(t_end)
-    kern_ms = [a.elapsed_time(b) for a, b in kev]
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
+    ms, kern, clocks = timed(dist, step, args.steps)
     ops.status_word(dev).raise_if_set("bench timed region")
     ms_step = ms / args.steps
-    value = units * world / (ms_step / 1e3)
-    kmean = sum(kern_ms) / len(kern_ms)
-    achieved = units * dense_flops_per_unit() / (kmean / 1e3) / 1e12
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except Exception:
-        pass
-    peak = peaks.get("bf16_tflops_sustained")
-    peak_kind = ("of measured (MEASURED_PEAKS.json bf16_tflops_sustained: a seconds-long step)" if peak
-                 else "of fallback (1400 TFLOP/s sustained)")
-    peak = peak or 1400.0
-    traffic = None
-    tfile = ROOT / "profiles" / "dense_patch_kernel.md"
-    if tfile.exists() and args.layers == G.layers and args.seqs == G.seqs and args.seq_len == G.seq_len:
-        for line in tfile.read_text().splitlines():
-            if line.startswith("traffic_bytes_per_launch_full_workload:"):
-                traffic = int(line.split(":", 1)[1])
+    kmean = sum(kern) / len(kern)
+    achieved = units_rank * dense_flops_per_unit() / (kmean / 1e3) / 1e12
+    pk = peaks()
+    burst = pk.get("bf16_tflops") or 1590.0
+    sustained = pk.get("bf16_tflops_sustained") or 1400.0
+    src = "of measured (MEASURED_PEAKS.json bf16_tflops, burst)" if pk.get("bf16_tflops") else "of fallback (1590)"
+    parity = dense_parity(G, wl, patcher, packed, kpages, vpages, layers, args.seq_len, dev)
     e2e = None
     if not args.no_e2e:
-        e2e = run_dense_e2e(args, patcher, dev, world)
+        e2e = run_dense_e2e(args, patcher, dist, weak)
     del wl, kpages, vpages
     torch.cuda.empty_cache()
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        threads = dense_cpu_threads()
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+        threads = host_threads()
         sample = DenseCpuSample()
         sample.run(threads, items=threads)
-        u, el = sample.run(threads, seconds=args.cpu_seconds)
-        cpu = {"value": u / el, "unit": UNIT, "cores": threads, "kind": "port",
+        u, el = sample.run(threads, seconds=args.sub_cpu_seconds)
+        cpu = {"value": u / el, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
                "sample": f"{u // DenseCpuSample.CHUNK} (layer, {DenseCpuSample.CHUNK}-token chunk) items in "
                          f"{el:.1f} s (oracle numpy port of the reference's exact route with A=dW, B=I, "
                          f"{threads} threads)"}
-    if rank == 0:
-        line = {
-            "metric": DENSE_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16 tensor-core products, fp32 accumulate (bf16 X and pages)",
-            "data": "synthetic",
-            "config": {"workload": DENSE_WORKLOAD, "layers": args.layers, "seqs_per_gpu": args.seqs,
-                       "seq_len": args.seq_len, "units_per_step_per_gpu": units,
-                       "parallelism": f"layer shards x{world} (weak)",
-                       "l2": f"X {units * G.d_model * 2 / 1e9:.1f} GB per GPU >> 126 MB L2, no flush needed",
-                       "launches_per_step": 2},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": traffic, "peak_source": peak_kind,
-                         "kernel": "dense_patch_kernel", "kernel_ms": kmean,
-                         "algorithmic_flops_per_unit": dense_flops_per_unit()},
-            "cpu_baseline": cpu,
-            "e2e": e2e,
-            "gpu_launches": 2 * args.steps,
-            "clocks": clk.summary(),
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
-    return 0
+    return {
+        "metric": G.metric, "value": units_step / (ms_step / 1e3), "unit": UNIT, "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak" if weak else "strong", "vs_baseline": None,
+        "dtype": "bf16 tensor-core products, fp32 accumulate (bf16 X and pages)", "data": "synthetic",
+        "config": {"workload": G.workload, "layers": args.layers, "seqs": args.seqs, "seq_len": args.seq_len,
+                   "units_per_step": units_step, "layers_per_rank": nl,
+                   "parallelism": (f"request shards x{dist.world} (weak)" if weak else
+                                   f"layer shards x{dist.world}: layer l on rank l mod {dist.world} (strong)"),
+                   "stored_x": f"{nxb} distinct X buffers on this GPU, held layer i reads buffer i mod {nxb} "
+                               "(the 80 layers' X would not fit: 172 GB)",
+                   "l2": f"X {args.seqs * args.seq_len * G.d_model * 2 / 1e9:.1f} GB per buffer >> 126 MB L2",
+                   "launches_per_step": 1 + len(groups),
+                   "e2e_sample": None if e2e is None else e2e["sample"]},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": burst, "unit": "TFLOP/s",
+                     "frac": achieved / burst, "peak_source": src,
+                     "frac_of_sustained": achieved / sustained,
+                     "sustained_peak": sustained, "traffic": traffic_from_profile("dense_patch_kernel.md", units_rank),
+                     "kernel": "dense_patch_kernel", "kernel_ms": kmean,
+                     "algorithmic_flops_per_unit": dense_flops_per_unit(), "units_per_step_this_gpu": units_rank},
+        "parity": parity,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": (1 + len(groups)) * args.steps,
+        "clocks": clocks,
+    }
 
 
-def run_dense_e2e(args, patcher, dev, world):
+def dense_parity(G, wl, patcher, packed, kpages, vpages, layers, n, dev):
+    """Spot check: held layer 0, sequence 0 — the delta written by the same kernel in store
+    mode into f16 pages against a plain PyTorch fp32 x @ dW^T (+ RoPE on K)."""
+    from deltakv_b200 import ops
+    from deltakv_b200.rope import half_tables
+
+    i = 0
+    x = wl["x"][0, :n].float()
+    d_kv = G.n_kv * G.hd
+    dk = (x @ wl["dw_k"][i].float().T).view(n, G.n_kv, G.hd)
+    dv = (x @ wl["dw_v"][i].float().T).view(n, G.n_kv, G.hd)
+    cos, sin = half_tables(wl["rope"], dev)
+    h = G.hd // 2
+    c, sn = cos[:n, None, :], sin[:n, None, :]
+    dk = torch.cat([dk[..., :h] * c - dk[..., h:] * sn, dk[..., h:] * c + dk[..., :h] * sn], dim=-1)
+    nblk = (n + G.bs - 1) // G.bs
+    kp = torch.zeros(nblk, G.bs, G.n_kv, G.hd, dtype=torch.float16, device=dev)
+    vp = torch.zeros_like(kp)
+    tab = ops.SeqBatchTensors(cu_seqlens=wl["seqs"].cu_seqlens[:2].clone(),
+                              block_tables=torch.arange(nblk, dtype=torch.int32, device=dev)[None].contiguous(),
+                              max_seq_len=n)
+    patcher.apply(wl["x"][0:1], packed[i:i + 1], [kp], [vp], tab, accumulate=False, check=True)
+    err = max(rel_l2(kp.view(-1, G.n_kv, G.hd)[:n].float(), dk), rel_l2(vp.view(-1, G.n_kv, G.hd)[:n].float(), dv))
+    return {"delta_rel_l2": err, "tolerance": 1e-3, "pass": bool(err <= 1e-3),
+            "sample": f"layer {layers[i]}, sequence 0 ({n} tokens), K and V, store mode into f16 pages",
+            "reference": "plain PyTorch fp32 x @ dW^T with rotate-half RoPE on K"}
+
+
+def run_dense_e2e(args, patcher, dist: Dist, weak):
     """Same metric through DensePatcher with pinned host buffers: X, dW, tables and pages
     copied in, pages copied back, every step (1 layer x 2 sequences per GPU)."""
     from deltakv_b200 import ops
 
+    dev = dist.dev
     n_layers, n_seqs = 1, 2
-    cpu = make_dense_workload(n_layers, n_seqs, args.seq_len, dev, seed=78)
+    cpu = make_dense_workload([0], n_seqs, args.seq_len, dev, seed=78)
     host = {k: cpu[k].cpu().pin_memory() for k in ("x", "dw_k", "dw_v", "tables")}
     host["caches"] = torch.stack(cpu["caches"]).cpu().pin_memory()
     del cpu
     torch.cuda.empty_cache()
     d = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
-    G = DenseGeo
+    G = Dense70B
     packed = torch.empty(n_layers, 2 * G.n_kv * G.hd, G.d_model, dtype=torch.bfloat16, device=dev)
     cu = torch.arange(0, n_seqs + 1, dtype=torch.int32, device=dev) * args.seq_len
     stream = torch.cuda.current_stream()
@@ -880,26 +1047,20 @@ def run_dense_e2e(args, patcher, dev, world):
     for _ in range(2):
         step()
     torch.cuda.synchronize()
-    n = 3
+    reps = 3
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        torch.distributed.barrier()
+    dist.barrier()
     a.record(stream)
-    for _ in range(n):
+    for _ in range(reps):
         step()
     b.record(stream)
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / n
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    units = n_layers * n_seqs * args.seq_len * world
+    ms = dist.max(a.elapsed_time(b) / reps)
+    units = n_layers * n_seqs * args.seq_len * dist.world
     del d, host
     torch.cuda.empty_cache()
     return {"value": units / (ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": ms, "sample": f"{n_seqs} seqs x {n_layers} layer per GPU, pinned host buffers"}
-
 
 
 # ---------------------------------------------------------------------------
@@ -907,7 +1068,7 @@ def run_dense_e2e(args, patcher, dev, world):
 # ---------------------------------------------------------------------------
 KIVI_METRIC = "patched token·layers/s (Llama-8B shape, int4 KIVI prefix, subspace route per adapter view)"
 KIVI_WORKLOAD = ("Multi-LoRA shared prefix on the Llama-3-8B shape: 32 layers, 8 KV heads x 128, one 32768-token "
-                 "prefix stored KIVI int4 (K per-channel, V per-token, group 32, fp16 scale/zero); adapter views "
+                 "prefix stored KIVI int4 (K per-channel, V per-token, group 32, fp16 scale/zero); 8 adapter views "
                  "with k/v ranks {8,8,16,16,32,32,64,64}; per view and layer: K basis = top-r right singular "
                  "subspace of the probe residual, V basis = the adapter's LoRA B; probes 10 %; dequant -> subspace "
                  "correction -> requant into the view's own int4 cache")
@@ -919,46 +1080,76 @@ class KiviGeo:
     layers, seq_len, n_kv, hd, probe_ratio = 32, 32768, 8, 128, 0.10
 
 
-def make_kivi_workload(args, device, rank_ids):
-    """Base int4 prefix (shared), and per adapter view: fresh bf16 K/V per layer, V basis,
-    probes.  fresh = dequant(base) + rank-r structure + 10 % drift on the non-probes."""
+def kivi_owner(n_views: int, world: int) -> dict[int, int]:
+    """Adapter views dealt to ranks in a snake order of their rank (8, 8, 16, 16, ...), so each
+    GPU gets a similar mix of cheap and costly views."""
+    order = sorted(range(n_views), key=lambda v: (KIVI_RANKS[v % len(KIVI_RANKS)], v))
+    owner = {}
+    for i, v in enumerate(order):
+        cyc, pos = divmod(i, world)
+        owner[v] = pos if cyc % 2 == 0 else world - 1 - pos
+    return owner
+
+
+def make_kivi_base(args, dist: Dist):
+    """The shared int4 prefix: made on rank 0 and broadcast once over NCCL to the others."""
+    from deltakv_b200 import kivi as K
+
+    G = KiviGeo
+    dev = dist.dev
+    n, d = args.seq_len, G.n_kv * G.hd
+    base = []
+    if dist.rank == 0:
+        gen = torch.Generator(device=dev).manual_seed(4000)
+        for _ in range(args.layers):
+            kv = []
+            for mode in ("k", "v"):
+                x = torch.randn(n, d, generator=gen, device=dev)
+                kv.append(K.quantize(x, mode))
+                del x
+            base.append(kv)
+    else:
+        base = [[K.KiviTensor.empty(n, d, mode, dev) for mode in ("k", "v")] for _ in range(args.layers)]
+    if dist.world > 1:
+        for kv in base:
+            for t in kv:
+                for part in (t.codes, t.scale, t.zero):
+                    torch.distributed.broadcast(part, src=0)
+        torch.cuda.synchronize()
+    return base
+
+
+def make_kivi_views(args, base, dev, view_ids):
+    """Per adapter view: fresh bf16 K/V per layer, V basis, probes.  fresh = dequant(base) +
+    rank-r structure + 10 % drift on the non-probes."""
     from deltakv_b200 import kivi as K
 
     G = KiviGeo
     n, d = args.seq_len, G.n_kv * G.hd
-    gen = torch.Generator(device=device).manual_seed(4000)
-    base = []
-    for _ in range(args.layers):
-        kv = []
-        for mode in ("k", "v"):
-            x = torch.randn(n, d, generator=gen, device=device)
-            kv.append(K.quantize(x, mode))
-            del x
-        base.append(kv)
     n_p = int(round(G.probe_ratio * n))
     adapters = []
-    for a in rank_ids:
+    for a in view_ids:
         r = KIVI_RANKS[a % len(KIVI_RANKS)]
-        g = torch.Generator(device=device).manual_seed(5000 + a)
-        probes = torch.unique(torch.cat([torch.zeros(1, dtype=torch.long, device=device),
-                                         torch.randperm(n, generator=g, device=device)[: n_p - 1]]))
+        g = torch.Generator(device=dev).manual_seed(5000 + a)
+        probes = torch.unique(torch.cat([torch.zeros(1, dtype=torch.long, device=dev),
+                                         torch.randperm(n, generator=g, device=dev)[: n_p - 1]]))
         layers = []
         for l in range(args.layers):
             views = []
             for m, mode in enumerate(("k", "v")):
-                B = torch.randn(d, r, generator=g, device=device) / math.sqrt(d)
-                codes = torch.randn(n, r, generator=g, device=device) * 0.5
+                B = torch.randn(d, r, generator=g, device=dev) / math.sqrt(d)
+                codes = torch.randn(n, r, generator=g, device=dev) * 0.5
                 fresh = K.dequantize(base[l][m])
                 fresh += codes @ B.T
-                drift = 0.1 * fresh.std() * torch.randn(n, d, generator=g, device=device)
+                drift = 0.1 * fresh.std() * torch.randn(n, d, generator=g, device=dev)
                 drift[probes] = 0
                 fresh += drift
                 views.append({"fresh": fresh.to(torch.bfloat16), "basis": B if mode == "v" else None,
-                              "out": K.KiviTensor.empty(n, d, mode, device)})
+                              "out": K.KiviTensor.empty(n, d, mode, dev)})
                 del codes, drift, fresh
             layers.append(views)
-        adapters.append({"rank": r, "probes": probes, "layers": layers})
-    return base, adapters
+        adapters.append({"id": a, "rank": r, "probes": probes, "layers": layers})
+    return adapters
 
 
 def kivi_problems(base, adapter, k_bases=None):
@@ -974,13 +1165,14 @@ def kivi_problems(base, adapter, k_bases=None):
     return probs
 
 
-def kivi_e2e(args, base, adapter, dev, world, stream, n_layers: int = 4) -> dict:
+def kivi_e2e(args, base, adapter, dist: Dist, stream, n_layers: int = 4) -> dict:
     """The same metric through the public call from pinned host buffers, on a bounded sample:
     one adapter view's first ``n_layers`` layers — its fresh bf16 K / V copied in, corrected by
     ``subspace_correct_views``, the corrected int4 K / V (codes, scales, zeros) copied out; the
     shared base cache stays resident."""
     from deltakv_b200 import kivi as K
 
+    dev = dist.dev
     nl = min(n_layers, args.layers)
     views = [adapter["layers"][l][m] for l in range(nl) for m in range(2)]
     fresh_host = [v["fresh"].cpu().pin_memory() for v in views]
@@ -1003,68 +1195,47 @@ def kivi_e2e(args, base, adapter, dev, world, stream, n_layers: int = 4) -> dict
 
     step()  # untimed: the pinned buffers' first transfers
     torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
+    dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n = 3
+    reps = 3
     a.record(stream)
-    for _ in range(n):
+    for _ in range(reps):
         step()
     b.record(stream)
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / n
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    units = nl * args.seq_len * world
+    ms = dist.max(a.elapsed_time(b) / reps)
+    units = nl * args.seq_len * dist.world
     return {"value": units / (ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": ms, "sample": f"1 adapter view (rank {adapter['rank']}) x {nl} layers x "
                                         f"{args.seq_len} tokens per GPU, pinned host buffers"}
 
 
-def run_kivi_ours(args):
+def run_kivi(args, dist: Dist) -> dict:
     from deltakv_b200 import kivi as K
     from deltakv_b200 import ops
 
-    world, rank, local = dist_setup(args)
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    # weak scaling: every rank maintains its own `--adapters` views (distinct adapters, the same
-    # rank mix {8, 8, 16, 16, 32, 32, 64, 64} on each GPU, so the ranks stay balanced)
-    per_rank = max(1, args.adapters)
-    ids = [rank * per_rank + i for i in range(per_rank)]
-    base, adapters = make_kivi_workload(args, dev, ids)
-    units = args.layers * args.seq_len * per_rank
+    dev = dist.dev
+    n_views = max(1, args.adapters)
+    owner = kivi_owner(n_views, dist.world)
+    mine = [v for v in range(n_views) if owner[v] == dist.rank]
+    base = make_kivi_base(args, dist)
+    adapters = make_kivi_views(args, base, dev, mine)
+    units_rank = args.layers * args.seq_len * len(mine)
+    units_step = args.layers * args.seq_len * n_views
     stream = torch.cuda.current_stream()
-
     problems = [kivi_problems(base, ad) for ad in adapters]
 
-    def step():
-        # all views; view v + 1's K bases overlap view v's route (side stream)
-        K.subspace_correct_views(problems, check=False)
+    def step(ev=None):
+        # all held views; view v + 1's K bases overlap view v's route (side stream)
+        if problems:
+            K.subspace_correct_views(problems, check=False)
 
     step()
     torch.cuda.synchronize()
     ops.status_word(dev).raise_if_set("bench warm-up")
     for _ in range(max(0, args.warmup - 1)):
         step()
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        t_start.record(stream)
-        for i in range(args.steps):
-            step()
-        t_end.record(stream)
-        torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
+    ms, _, clocks = timed(dist, step, args.steps, kernel_events=False)
     # the two halves alone (after the timed region, same work, one stream): K bases, route
     split = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     n_split = 2
@@ -1080,53 +1251,42 @@ def run_kivi_ours(args):
         if it:
             basis_ms += split[0].elapsed_time(split[1]) / n_split
             route_ms += split[1].elapsed_time(split[2]) / n_split
-    ms = t_start.elapsed_time(t_end)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
     ops.status_word(dev).raise_if_set("bench timed region")
     ms_step = ms / args.steps
-    value = units * world / (ms_step / 1e3)
-    achieved = units * KIVI_BYTES_PER_UNIT / (route_ms / 1e3) / 1e9
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except Exception:
-        pass
-    peak = peaks.get("hbm_gbs") or 6650.0
+    achieved = units_rank * KIVI_BYTES_PER_UNIT / (route_ms / 1e3) / 1e9 if route_ms > 0 else 0.0
+    peak, peak_kind = hbm_peak()
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = kivi_cpu_sample(args.cpu_seconds)
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+        cpu = kivi_cpu_sample(args.sub_cpu_seconds)
     e2e = None
-    if not args.no_e2e:
-        e2e = kivi_e2e(args, base, adapters[0], dev, world, stream)
-    if rank == 0:
-        line = {
-            "metric": KIVI_METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int4 KIVI cache, bf16 tensor-core products, fp32 accumulate",
-            "data": "synthetic",
-            "config": {"workload": KIVI_WORKLOAD, "layers": args.layers, "prefix_tokens": args.seq_len,
-                       "adapter_views_per_gpu": per_rank, "ranks": [a["rank"] for a in adapters],
-                       "units_per_step_per_gpu": units, "parallelism": f"adapter shards x{world}",
-                       "l2": f"{units * KIVI_BYTES_PER_UNIT / 1e9:.1f} GB per step per GPU >> 126 MB L2",
-                       "k_basis_ms_per_step": basis_ms, "subspace_route_ms_per_step": route_ms},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": None, "peak_source": "of measured (MEASURED_PEAKS.json hbm_gbs, burst copy)",
-                         "kernel": "int4 subspace route (flags, pack, pass1 x2, psum, solve, fitb, pass2 x2) per view",
-                         "kernel_ms": route_ms, "algorithmic_bytes_per_unit": KIVI_BYTES_PER_UNIT},
-            "cpu_baseline": cpu,
-            "e2e": e2e,
-            # per view: flags, pack, pass1 K/V, psum, solve, fitb, pass2 K/V (9) + the K bases'
-            # batched probe residual and Jacobi eigensolver (2); library calls not counted
-            "gpu_launches": args.steps * len(adapters) * 11,
-            "clocks": clk.summary(),
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
-    return 0
+    if not args.no_e2e and adapters:
+        e2e = kivi_e2e(args, base, adapters[0], dist, stream)
+    del problems, adapters, base
+    torch.cuda.empty_cache()
+    return {
+        "metric": KIVI_METRIC, "value": units_step / (ms_step / 1e3), "unit": UNIT, "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int4 KIVI cache, bf16 tensor-core products, fp32 accumulate",
+        "data": "synthetic",
+        "config": {"workload": KIVI_WORKLOAD, "layers": args.layers, "prefix_tokens": args.seq_len,
+                   "adapter_views": n_views, "views_this_gpu": mine,
+                   "ranks_this_gpu": [KIVI_RANKS[v % len(KIVI_RANKS)] for v in mine],
+                   "units_per_step": units_step,
+                   "parallelism": f"adapter shards x{dist.world} (base int4 cache broadcast once over NCCL)",
+                   "l2": f"{units_rank * KIVI_BYTES_PER_UNIT / 1e9:.1f} GB per step per GPU >> 126 MB L2",
+                   "k_basis_ms_per_step": basis_ms, "subspace_route_ms_per_step": route_ms,
+                   "e2e_sample": None if e2e is None else e2e["sample"]},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "peak_source": peak_kind,
+                     "kernel": "int4 subspace route (flags, pack, pass1 x2, psum, solve, fitb, pass2 x2) per view",
+                     "kernel_ms": route_ms, "algorithmic_bytes_per_unit": KIVI_BYTES_PER_UNIT},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        # per view: flags, pack, pass1 K/V, psum, solve, fitb, pass2 K/V (9) + the K bases'
+        # batched probe residual and Jacobi eigensolver (2); library calls not counted
+        "gpu_launches": args.steps * len(mine) * 11,
+        "clocks": clocks,
+    }
 
 
 def kivi_cpu_sample(seconds: float, n: int = 4096) -> dict:
@@ -1146,7 +1306,7 @@ def kivi_cpu_sample(seconds: float, n: int = 4096) -> dict:
     B = (rng.standard_normal((d, 16), dtype=np.float32) / np.sqrt(d)).astype(np.float32)
     fresh = (OK.dequantize(*base, "v") + (rng.standard_normal((n, 16), dtype=np.float32) * 0.5) @ B.T).astype(np.float32)
     probes = np.unique(np.concatenate([[0], rng.permutation(n)[: int(0.1 * n)]]))
-    threads = dense_cpu_threads()
+    threads = host_threads()
 
     def item():
         reused = OK.dequantize(*base, "v")
@@ -1172,27 +1332,22 @@ def kivi_cpu_sample(seconds: float, n: int = 4096) -> dict:
         with ThreadPoolExecutor(threads) as ex:
             list(ex.map(worker, range(threads)))
         el = time.perf_counter() - t0
-    return {"value": done[0] / el, "unit": UNIT, "cores": threads, "kind": "port",
+    return {"value": done[0] / el, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
             "sample": f"{done[0] // n} (layer, view) items of {n} tokens, rank 16, V grouping, in {el:.1f} s "
                       f"(oracle numpy port: dequant, subspace_correct, requant; {threads} threads)"}
 
 
-def run_kivi_reference(args):
-    world, rank, _ = dist_setup(args)
-    if rank != 0:
-        return 0
+def run_kivi_reference(args) -> dict:
     res = [kivi_cpu_sample(max(2.0, args.cpu_seconds / max(1, args.steps))) for _ in range(args.steps)]
     value = sum(r["value"] for r in res) / len(res)
-    line = {
+    return {
         "impl": "reference", "metric": KIVI_METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": KIVI_WORKLOAD, "step": res[0]["sample"]},
         "cpu_baseline": {**res[0], "value": value},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
-    return 0
 
 
 # ---------------------------------------------------------------------------
@@ -1281,28 +1436,24 @@ def analytic_cpu_sample(seconds: float, n: int = 2048, layers: int = 1) -> dict:
         el = time.perf_counter() - t0
         if el >= seconds:
             break
-    return {"value": done * layers * n / el, "unit": UNIT, "cores": cpu_pool_threads(), "kind": "port",
+    return {"value": done * layers * n / el, "unit": UNIT, "cores": cpu_pool_threads(), "cpu_model": cpu_model(),
+            "kind": "port",
             "sample": f"{done} x ({layers} layer x {n} tokens) of the engine's analytic loop in {el:.1f} s "
                       "(oracle numpy fp64 port, attention materialised; BLAS threads for the matrix products)"}
 
 
-def run_analytic_ours(args):
+def run_analytic(args, dist: Dist) -> dict:
     from deltakv_b200 import analytic as AN
     from deltakv_b200 import ops
+    from deltakv_b200 import subspace as SUB
 
-    world, rank, local = dist_setup(args)
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     G = AnalyticGeo
-    model, delta, conf, hidden = make_analytic_workload(args, dev, 7000 + rank)
+    dev = dist.dev
+    model, delta, conf, hidden = make_analytic_workload(args, dev, 7000 + dist.rank)
     units = args.layers * args.seq_len * args.seqs
     stream = torch.cuda.current_stream()
 
-    def step():
+    def step(ev=None):
         for h, hm in hidden:
             AN.analytic_patches(_snapshot(h, hm), delta, model, conf)
 
@@ -1310,27 +1461,9 @@ def run_analytic_ours(args):
         step()
     torch.cuda.synchronize()
     ops.status_word(dev).raise_if_set("bench warm-up")
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    from deltakv_b200 import subspace as SUB
-
     trunc0 = SUB.gram_launches
-    with ClockSampler(local) as clk:
-        t_start.record(stream)
-        for _ in range(args.steps):
-            step()
-        t_end.record(stream)
-        torch.cuda.synchronize()
+    ms, _, clocks = timed(dist, step, args.steps, kernel_events=False)
     trunc_launches = SUB.gram_launches - trunc0
-    if world > 1:
-        torch.distributed.barrier()
-    ms = t_start.elapsed_time(t_end)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
     ms_step = ms / args.steps
     # the attention core alone on one layer's tensors (same shapes as inside the loop)
     n = args.seq_len
@@ -1348,18 +1481,12 @@ def run_analytic_ours(args):
     core_ms = e0.elapsed_time(e1) / reps
     core_flops = 2 * 6 * G.hd * (n * (n + 1) / 2) * G.n_heads  # S, dS (2), O, OS, OD MACs per causal pair
     achieved = core_flops / (core_ms / 1e3) / 1e12
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except Exception:
-        pass
-    bf16_peak = peaks.get("bf16_tflops") or 1590.0
+    bf16_peak = peaks().get("bf16_tflops") or 1590.0
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
         cpu = analytic_cpu_sample(args.cpu_seconds)
     e2e = None
     if not args.no_e2e:
-        # through the public API from pinned host buffers: hidden states in, the K / V patches out
         h_host = [(h.cpu().pin_memory(), hm.cpu().pin_memory()) for h, hm in hidden]
         out_bytes = 2 * args.layers * n * G.n_kv * G.hd * 4
         outs = [torch.empty(2, args.layers, n, G.n_kv, G.hd).pin_memory() for _ in hidden]
@@ -1373,59 +1500,42 @@ def run_analytic_ours(args):
 
         e2e_step()  # untimed: the pinned buffers' first transfers
         torch.cuda.synchronize()
-        if world > 1:
-            torch.distributed.barrier()
+        dist.barrier()
         e2 = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         e2[0].record(stream)
         e2e_step()
         e2[1].record(stream)
         torch.cuda.synchronize()
-        e2e_ms = e2[0].elapsed_time(e2[1])
-        if world > 1:
-            t = torch.tensor([e2e_ms], device=dev)
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-            e2e_ms = float(t.item())
-        e2e = {"value": units * world / (e2e_ms / 1e3), "unit": UNIT,
+        e2e_ms = dist.max(e2[0].elapsed_time(e2[1]))
+        e2e = {"value": units * dist.world / (e2e_ms / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": sum(a.numel() * 4 + b.numel() * 4 for a, b in h_host),
                "d2h_bytes_per_step": out_bytes * len(hidden), "ms_per_step": e2e_ms}
-    if rank == 0:
-        line = {
-            "metric": ANALYTIC_METRIC, "value": units * world / (ms_step / 1e3), "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": ANALYTIC_WORKLOAD, "layers": args.layers, "seqs_per_gpu": args.seqs,
-                       "seq_len": n, "parallelism": f"request shards x{world}",
-                       "l2": "per sequence 283 MB of stored hidden states >> 126 MB L2"},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16_peak, "unit": "TFLOP/s",
-                         "frac": achieved / bf16_peak, "traffic": None,
-                         "peak_source": "of measured (MEASURED_PEAKS.json bf16_tflops, burst)",
-                         "kernel": "attention core (dkv_attn_first_order, mma.sync bf16 three-term split), one layer",
-                         "kernel_ms": core_ms, "algorithmic_flops_per_launch": core_flops,
-                         # the split issues 3 bf16 products per fp32-level product; S / dS are formed by
-                         # both column-half warps of a row group
-                         "issued_mma_flops_per_launch": core_flops * (3 * 3 * 2 + 3 * 3) / 6,
-                         "fp32_fma_equivalent": {"peak": FP32_FMA_NOMINAL_TFLOPS,
-                                                 "frac": achieved / FP32_FMA_NOMINAL_TFLOPS,
-                                                 "peak_source": "of nominal (148 SMs x 128 lanes x 2 x 1965 MHz)"}},
-            "cpu_baseline": cpu, "e2e": e2e,
-            # per layer and sequence: rmsnorm x2, rope x4, attention core, swiglu; plus the rank
-            # truncations' subspace-iteration and Jacobi kernels, as counted
-            "gpu_launches": args.steps * args.seqs * args.layers * 8 + trunc_launches,
-            "clocks": clk.summary(),
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
-    return 0
+    return {
+        "metric": ANALYTIC_METRIC, "value": units * dist.world / (ms_step / 1e3), "unit": UNIT, "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": ANALYTIC_WORKLOAD, "layers": args.layers, "seqs_per_gpu": args.seqs,
+                   "seq_len": n, "parallelism": f"request shards x{dist.world}",
+                   "l2": "per sequence 283 MB of stored hidden states >> 126 MB L2"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": bf16_peak, "unit": "TFLOP/s",
+                     "frac": achieved / bf16_peak, "traffic": None,
+                     "peak_source": "of measured (MEASURED_PEAKS.json bf16_tflops, burst)",
+                     "kernel": "attention core (dkv_attn_first_order, mma.sync bf16 three-term split), one layer",
+                     "kernel_ms": core_ms, "algorithmic_flops_per_launch": core_flops,
+                     "issued_mma_flops_per_launch": core_flops * (3 * 3 * 2 + 3 * 3) / 6,
+                     "fp32_fma_equivalent": {"peak": FP32_FMA_NOMINAL_TFLOPS,
+                                             "frac": achieved / FP32_FMA_NOMINAL_TFLOPS,
+                                             "peak_source": "of nominal (148 SMs x 128 lanes x 2 x 1965 MHz)"}},
+        "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": args.steps * args.seqs * args.layers * 8 + trunc_launches,
+        "clocks": clocks,
+    }
 
 
-def run_analytic_reference(args):
-    world, rank, _ = dist_setup(args)
-    if rank != 0:
-        return 0
+def run_analytic_reference(args) -> dict:
     res = [analytic_cpu_sample(max(2.0, args.cpu_seconds / max(1, args.steps))) for _ in range(args.steps)]
     value = sum(r["value"] for r in res) / len(res)
-    line = {
+    return {
         "impl": "reference", "metric": ANALYTIC_METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
@@ -1433,35 +1543,87 @@ def run_analytic_reference(args):
         "cpu_baseline": {**res[0], "value": value},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
-    return 0
 
 
-def main():
-    args = parse()
-    if args.workload == "analytic":
-        for k, v in (("layers", AnalyticGeo.layers), ("seqs", AnalyticGeo.seqs), ("seq_len", AnalyticGeo.seq_len)):
-            if getattr(args, k) is None:
-                setattr(args, k, v)
-        return run_analytic_reference(args) if args.impl == "reference" else run_analytic_ours(args)
-    if args.workload == "multi-lora-kivi":
-        for k, v in (("layers", KiviGeo.layers), ("seqs", 1), ("seq_len", KiviGeo.seq_len)):
-            if getattr(args, k) is None:
-                setattr(args, k, v)
-        return run_kivi_reference(args) if args.impl == "reference" else run_kivi_ours(args)
-    if args.workload == "smollm2-exact":
-        global Geo, METRIC, WORKLOAD, BYTES_PER_UNIT
-        Geo, METRIC, WORKLOAD, BYTES_PER_UNIT = SmolGeo, SMOL_METRIC, SMOL_WORKLOAD, SMOL_BYTES_PER_UNIT
-    dense = args.workload == "rl-dense"
-    for k, v in (("layers", DenseGeo.layers if dense else Geo.layers), ("seqs", DenseGeo.seqs if dense else Geo.seqs),
-                 ("seq_len", DenseGeo.seq_len if dense else Geo.seq_len)):
-        if getattr(args, k) is None:
-            setattr(args, k, v)
-    if dense:
-        return run_dense_reference(args) if args.impl == "reference" else run_dense_ours(args)
+# ---------------------------------------------------------------------------
+# driver
+# ---------------------------------------------------------------------------
+DEFAULTS = {
+    "llama8b-exact": (Llama8B.layers, Llama8B.seqs, Llama8B.seq_len),
+    "smollm2-exact": (Smol135M.layers, Smol135M.seqs, Smol135M.seq_len),
+    "rl-dense": (Dense70B.layers, Dense70B.seqs, Dense70B.seq_len),
+    "multi-lora-kivi": (KiviGeo.layers, 1, KiviGeo.seq_len),
+    "analytic": (AnalyticGeo.layers, AnalyticGeo.seqs, AnalyticGeo.seq_len),
+}
+
+
+def with_defaults(args, workload):
+    import copy
+
+    a = copy.copy(args)
+    a.workload = workload
+    L_, S, N = DEFAULTS[workload]
+    a.layers = args.layers if args.layers is not None else L_
+    a.seqs = args.seqs if args.seqs is not None else S
+    a.seq_len = args.seq_len if args.seq_len is not None else N
+    return a
+
+
+def run_one(args, dist: Dist) -> dict:
+    w = args.workload
+    if w == "llama8b-exact":
+        return run_exact(args, dist, Llama8B)
+    if w == "smollm2-exact":
+        return run_exact(args, dist, Smol135M)
+    if w == "rl-dense":
+        return run_dense(args, dist)
+    if w == "multi-lora-kivi":
+        return run_kivi(args, dist)
+    return run_analytic(args, dist)
+
+
+def run_reference(args) -> dict:
+    w = args.workload
+    if w == "llama8b-exact":
+        return run_exact_reference(args, Llama8B)
+    if w == "smollm2-exact":
+        return run_exact_reference(args, Smol135M)
+    if w == "rl-dense":
+        return run_dense_reference(args)
+    if w == "multi-lora-kivi":
+        return run_kivi_reference(args)
+    return run_analytic_reference(args)
+
+
+SUB_WORKLOADS = ("smollm2-exact", "multi-lora-kivi", "rl-dense")
+
+
+def main(argv=None):
+    args = parse(argv)
     if args.impl == "reference":
-        return run_reference(args)
-    return run_ours(args)
+        # the CPU reference arm: rank 0 alone times the host path; other ranks exit at once
+        if int(os.environ.get("RANK", "0")) != 0:
+            return 0
+        print(json.dumps(run_reference(with_defaults(args, args.workload))), flush=True)
+        return 0
+    dist = Dist().init()
+    line = run_one(with_defaults(args, args.workload), dist)
+    if args.workload == "llama8b-exact" and not args.no_workloads:
+        # the other configurations, one after another on the same GPUs (each frees its memory)
+        sub_args = argparse.Namespace(**{**vars(args), "layers": None, "seqs": None, "seq_len": None})
+        workloads = {}
+        for w in SUB_WORKLOADS:
+            try:
+                workloads[w] = run_one(with_defaults(sub_args, w), dist)
+            except Exception as e:  # recorded, not hidden: the line says which workload failed and why
+                workloads[w] = {"error": f"{type(e).__name__}: {e}", "trace": traceback.format_exc()[-2000:]}
+                torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+        line["workloads"] = workloads
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.finish()
+    return 0
 
 
 if __name__ == "__main__":

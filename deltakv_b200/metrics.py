@@ -187,3 +187,28 @@ def gather_layer_errors(local: Tensor, group=None) -> Tensor:
     out = torch.empty(world * flat.numel(), dtype=flat.dtype, device=flat.device)
     dist.all_gather_into_tensor(out, flat, group=group)
     return out.view(world, -1)
+
+
+def gather_sharded_layer_errors(local: Tensor, layer_ids: Sequence[int], n_layers: int, group=None) -> Tensor:
+    """The full ``[n_layers]`` per-layer error list (the ``per_layer`` of
+    src/deltakv/patches/compose.py:147-163) when the layers are split across ranks.
+
+    Each rank passes the errors of its own layers (``local[i]`` belongs to layer
+    ``layer_ids[i]``); the layer sets of the ranks must be disjoint and together cover
+    ``0..n_layers-1``.  One ``all_gather_into_tensor`` of ``[n_layers]`` vectors (NaN where a
+    rank holds no layer) on the default or given process group; every rank gets the list.
+    """
+    import torch.distributed as dist
+
+    ids = torch.as_tensor(list(layer_ids), dtype=torch.long, device=local.device)
+    if ids.numel() != local.numel():
+        raise ValueError("one error per layer id")
+    if ids.numel() and (int(ids.min()) < 0 or int(ids.max()) >= n_layers):
+        raise ValueError(f"layer ids must lie in [0, {n_layers})")
+    mine = torch.full((n_layers,), float("nan"), dtype=local.dtype, device=local.device)
+    mine[ids] = local.reshape(-1)
+    every = gather_layer_errors(mine, group) if dist.is_available() and dist.is_initialized() else mine[None]
+    held = (~torch.isnan(every)).sum(0)
+    if not bool((held == 1).all()):
+        raise ValueError("the ranks' layer sets must be disjoint and cover every layer")
+    return torch.nan_to_num(every, nan=0.0).sum(0)

@@ -301,9 +301,13 @@ def exact_patch_paged(geom: L.ExactGeometry, x: torch.Tensor, packed: torch.Tens
             raise TypeError("x_scale must be fp32 with contiguous rows")
     xq = None
     if x_sumsq is not None:
+        if not apply_norm:
+            raise ValueError("x_sumsq feeds the RMSNorm: pass it only with apply_norm=True")
         xq = x_sumsq if x_sumsq.ndim == 2 else x_sumsq.unsqueeze(0)
-        if xq.dtype != torch.float32 or xq.stride(1) != 1 or xq.shape[0] != n_layers or xq.shape[1] < x3.shape[1]:
-            raise TypeError("x_sumsq must be fp32 [layers, rows] with contiguous rows")
+        if xq.dtype != torch.float32:
+            raise TypeError("x_sumsq must be fp32")
+        if xq.stride(1) != 1 or xq.shape[0] != n_layers or xq.shape[1] < x3.shape[1]:
+            raise ValueError("x_sumsq must be [layers, rows] with contiguous rows, matching x")
     kd = (L.PagedCache * n_layers)(*[paged_desc(p) for p in k_pages])
     vd = (L.PagedCache * n_layers)(*[paged_desc(p) for p in v_pages])
     if rope_cos is not None:

@@ -22,7 +22,7 @@
  *                          patches/compose.py:29-34, engine.py:263-288, connectors/vllm.py:70-81
  *
  * The reference has no FFI of its own (it is pure Python/PyTorch); these are the
- * entry points its Python operators bind through ctypes (see INTEGRATION.md).
+ * entry points its Python operators bind through ctypes.
  */
 #ifndef DKV_B200_H
 #define DKV_B200_H
@@ -231,8 +231,10 @@ typedef struct dkv_exact_patch_args {
   int32_t accumulate; /* 1: pages += delta (read-add-write); 0: pages = delta */
   int32_t *status;    /* optional device status word */
   /* optional, with apply_norm: per-row sum of the squared stored codes (fp32, (l, t) at
-     x_sumsq + l*x_sumsq_layer_stride + t), as dkv_quantize_rows writes it; the RMSNorm then
-     uses it instead of forming X.X^T's diagonal on the tensor cores.  NULL: formed here. */
+     x_sumsq + l*x_sumsq_layer_stride + t), as dkv_quantize_rows_sumsq writes it beside the
+     codes; the RMSNorm then uses it instead of forming X.X^T's diagonal on the tensor
+     cores.  The sums must come from the same codes as x: nothing checks that, and stale
+     sums silently give a wrong norm.  Ignored without apply_norm.  NULL: formed here. */
   const float *x_sumsq;
   int64_t x_sumsq_layer_stride;
 } dkv_exact_patch_args;
@@ -507,8 +509,10 @@ int dkv_subspace_correct(const dkv_subspace_args *args, dkv_stream_t stream);
  * library, present on every GPU that loads it until the process exits; args->workspace
  * and args->workspace_bytes are ignored.
  *   - Limit: the problem's scratch, dkv_subspace_workspace_bytes(n_tokens, d, rank), must
- *     fit in 16 MiB (e.g. 32768 tokens x d=1024 at rank 64); larger problems are rejected
- *     with DKV_ERR_WORKSPACE before anything is launched.
+ *     fit in 16 MiB.  That is 4*r + 5 bytes per token (r = rank rounded up to a multiple
+ *     of 16) plus a few KB that grow with d: about 64K tokens at rank 64 and 240K tokens at
+ *     rank 16 for d = 1024.  Larger problems are rejected with DKV_ERR_WORKSPACE before
+ *     anything is launched.
  *   - The first call made while a given device is current looks up the array's device
  *     address (cudaGetSymbolAddress) and caches it; make that first call before any
  *     stream capture on that device.

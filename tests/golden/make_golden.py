@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference source is available:
 
-    python tests/golden/make_golden.py /root/reference/src
+    python tests/golden/make_golden.py <reference checkout>/src [case ...]
 
 It imports the reference read-only (no bytecode written), drives its own functions on
 seeded inputs and stores inputs and outputs as ``tests/golden/*.npz``.  The tests read
@@ -540,4 +540,6 @@ def main(ref_src: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py <reference checkout>/src")
+    main(sys.argv[1])

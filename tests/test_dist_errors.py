@@ -85,3 +85,32 @@ def test_gather_single_process_is_identity():
         pytest.skip("a process group is already initialised")
     x = torch.tensor([0.5, 0.25])
     assert torch.equal(gather_layer_errors(x), x.view(1, -1))
+
+
+def _sharded_worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    from deltakv_b200.metrics import gather_sharded_layer_errors
+
+    _init(rank, world, port, 30)
+    # 5 layers round-robin over 2 ranks (layer l on rank l mod 2): an uneven split
+    mine = [l for l in range(5) if l % world == rank]
+    local = torch.tensor([100.0 + l for l in mine], dtype=torch.float64)
+    got = gather_sharded_layer_errors(local, mine, 5)
+    torch.save(got, os.path.join(out_dir, f"s{rank}.pt"))
+    status = "no error"
+    try:  # both ranks claim layer 0: overlapping sets are rejected on every rank
+        gather_sharded_layer_errors(torch.zeros(1, dtype=torch.float64), [0], 5)
+    except ValueError:
+        status = "rejected"
+    with open(os.path.join(out_dir, f"s{rank}.txt"), "w") as f:
+        f.write(status)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_gather_sharded_layer_errors_two_ranks(tmp_path):
+    port = _free_port()
+    mp.start_processes(_sharded_worker, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    want = torch.tensor([100.0, 101, 102, 103, 104], dtype=torch.float64)
+    for r in range(2):
+        assert torch.equal(torch.load(tmp_path / f"s{r}.pt"), want)
+        assert (tmp_path / f"s{r}.txt").read_text() == "rejected"

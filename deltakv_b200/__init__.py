@@ -21,7 +21,7 @@ All computation runs in ``libdkv_b200.so``; a missing library raises (no CPU pat
 
 from __future__ import annotations
 
-from deltakv_b200 import analytic, kivi
+from deltakv_b200 import analytic, kivi, routes
 from deltakv_b200._lib import DkvError
 from deltakv_b200.dense import DensePatcher
 from deltakv_b200.exact import (
@@ -74,6 +74,7 @@ __all__ = [
     "quantize_rows",
     "replay",
     "residual_gate",
+    "routes",
     "scatter_into_paged",
     "scatter_into_paged_batched",
     "select_probes",
@@ -97,7 +98,8 @@ _INSTALL_MAP = {
                                  "softmax_jacobian_product": analytic.softmax_jacobian_product},
     # modules that imported the names with `from ... import`
     "deltakv.engine": {"zeroth_order_patches": zeroth_order_patches, "exact_kv_patch": exact_kv_patch,
-                       "apply_layer_patches": apply_layer_patches, "apply_probe_to_cache": apply_probe_to_cache,
+                       "apply_layer_patches": apply_layer_patches,
+                       "apply_probe_to_cache": routes.engine_apply_probe_to_cache,
                        "select_probes": select_probes, "weight_axis_scores": weight_axis_scores,
                        "compare_kv": compare_kv, "measured_error": measured_error,
                        "rmsnorm_first_order": analytic.rmsnorm_first_order,
@@ -118,7 +120,10 @@ def install(modules: dict | None = None) -> list[str]:
 
     Rebinds the operator names in the reference's modules (and in the modules that
     imported them by name), so ``DeltaKVEngine`` and ``DeltaKVConnector`` run the B200
-    path unchanged.  Returns the ``module.attribute`` names that were replaced.
+    path unchanged, and gives ``DeltaKVEngine.materialize`` (hence ``evaluate_against_fresh``
+    and ``maintain_all``) the ``route="subspace"`` the reference accepts but drops: the probe
+    route with the residual gate off on every layer (:mod:`deltakv_b200.routes`).  Returns
+    the ``module.attribute`` names that were replaced.
     """
     import importlib
     import sys
@@ -135,4 +140,8 @@ def install(modules: dict | None = None) -> list[str]:
             if hasattr(mod, attr):
                 setattr(mod, attr, fn)
                 done.append(f"{mod_name}.{attr}")
+        engine_cls = getattr(mod, "DeltaKVEngine", None) if mod_name == "deltakv.engine" else None
+        if engine_cls is not None and hasattr(engine_cls, "materialize"):
+            engine_cls.materialize = routes.wrap_materialize(engine_cls.materialize)
+            done.append(f"{mod_name}.DeltaKVEngine.materialize")
     return done

@@ -43,6 +43,23 @@ Cases:
   kivi.npz         metrics._minmax_quantize (4 bits, group 32) on the last dimension (the
                    per-token V grouping) and on the transposed tensor (per-channel K
                    grouping), plus kivi_noise_floor on a small KVCache.
+  engine.npz       DeltaKVEngine end to end on the CPU toy (4 layers, d=64, GQA 4/2, 64
+                   tokens, rank-4 q/k/v LoRA at scale 0.01 as the reference's `bench`
+                   command builds it): prefill, commit_delta, evaluate_against_fresh for
+                   route exact, hybrid and subspace (the probe route with
+                   apply_probe_to_cache(..., probe_layers=set())), with the arguments and
+                   results of every hot-path call the engine made (recorded by wrapping the
+                   engine module's names), the report, and DeltaKVConnector.patch_paged of the
+                   exact view into bf16 paged caches.
+  smol_kl.npz      SmolLM2-135M-shaped decoder (tests/_smol_model.py: seeded weights, 4 of
+                   30 layers, 2048 tokens, rank-8 q/k/v/o LoRA at relative norm 0.01): the
+                   reference's prefill, rmsnorm_tensors -> zeroth_order_patches ->
+                   apply_layer_patches, apply_delta, fresh prefill, last-token logits of the
+                   fresh and patched caches, next_token_kl, and pins of the prefill (rows and
+                   norms of the stored activations and K/V).
+
+Usage: ``make_golden.py <reference>/src`` writes every file; ``make_golden.py <reference>/src
+engine smol_kl`` only the named ones (``core`` = the files above engine.npz).
 """
 
 from __future__ import annotations
@@ -62,7 +79,7 @@ def bf16_bits(t) -> np.ndarray:
     return t.to(torch.bfloat16).contiguous().view(torch.int16).numpy().view(np.uint16).copy()
 
 
-def main(ref_src: str) -> None:
+def core_cases(ref_src: str) -> None:
     sys.path.insert(0, ref_src)
     import torch
 
@@ -536,10 +553,216 @@ def main(ref_src: str) -> None:
     np.savez_compressed(OUT / "kivi.npz", xv=xv.numpy(), xv_q=_minmax_quantize(xv, 4, 32).numpy(),
                         xk=xk.numpy(), xk_q=kq.numpy(), floor_k=kvc.k.numpy(), floor_v=kvc.v.numpy(),
                         floor=np.float64(kivi_noise_floor(kvc, bits=4, group_size=32)))
+
+
+def _state_from_oracle(model, w: dict) -> None:
+    """Load oracle-named numpy weights into a reference ToyTransformer."""
+    import torch
+
+    sd = model.state_dict()
+    for key in sd:
+        name = key.replace(".", "_")
+        if name == "lm_head_weight" and name not in w:
+            name = "embed_weight"
+        sd[key] = torch.from_numpy(np.ascontiguousarray(w[name]))
+    model.load_state_dict(sd)
+
+
+def smol_kl_case(ref_src: str) -> None:
+    sys.path.insert(0, ref_src)
+    sys.path.insert(0, str(OUT.parent.parent))
+    import torch
+
+    from deltakv.deltas.descriptor import lora_layer
+    from deltakv.deltas.factors import LowRankFactors
+    from deltakv.deltas.lora import lora_delta
+    from deltakv.metrics import next_token_kl
+    from deltakv.model import ToyConfig, ToyTransformer
+    from deltakv.patches.compose import apply_layer_patches
+    from deltakv.patches.exact import zeroth_order_patches
+    from deltakv.types import WeightVersion
+    from tests import _smol_model as SM
+
+    torch.set_num_threads(8)
+    torch.set_grad_enabled(False)
+    cfg = ToyConfig(vocab_size=SM.VOCAB, d_model=SM.D, n_layers=SM.N_LAYERS, n_heads=SM.N_HEADS, n_kv_heads=SM.N_KV,
+                    d_ff=SM.D_FF, max_seq=SM.SEQ, rms_eps=SM.EPS, rope_base=SM.ROPE_BASE)
+    model = ToyTransformer(cfg)
+    w = SM.weights()
+    _state_from_oracle(model, w)
+    tokens = torch.from_numpy(SM.tokens())
+    _, kv_base, hidden = model.prefill(tokens)
+    dl = SM.delta(w)
+    layers = {i: lora_layer(i, **{name[0]: LowRankFactors(A=torch.from_numpy(A), B=torch.from_numpy(B), scale=s,
+                                                          name=name)
+                                  for name, (A, B, s) in projs.items()})
+              for i, projs in dl.items()}
+    delta = lora_delta(source=WeightVersion(id="base"), target=WeightVersion(id="lora", parent_id="base", kind="lora"),
+                       layers=layers)
+    xn = model.rmsnorm_tensors(hidden)
+    patches = zeroth_order_patches(xn, delta, n_kv_heads=cfg.n_kv_heads, head_dim=cfg.head_dim, rope=model.rope)
+    patched = apply_layer_patches(kv_base, patches)
+    stale_logits = model.logits_from_kv(tokens, kv_base)
+    model.apply_delta(delta, version=WeightVersion(id="lora"))
+    fresh_logits, kv_fresh, _ = model.prefill(tokens)
+    patched_logits = model.logits_from_kv(tokens, patched)
+    h = torch.stack(list(hidden.h))
+    norms = lambda t: np.array([float(t[l].double().norm()) for l in range(t.shape[0])])
+    np.savez_compressed(
+        OUT / "smol_kl.npz",
+        tokens=tokens.numpy(), fresh_logits=fresh_logits[-1].numpy(), patched_logits=patched_logits.numpy(),
+        kl_ref=np.float64(next_token_kl(fresh_logits[-1], patched_logits)),
+        kl_stale=np.float64(next_token_kl(fresh_logits[-1], stale_logits)),
+        h_head=h[:, :4].numpy(), h_tail=h[:, -4:].numpy(), h_norms=norms(h),
+        k_tail=kv_base.k[:, -4:].numpy(), v_tail=kv_base.v[:, -4:].numpy(),
+        k_norms=norms(kv_base.k), v_norms=norms(kv_base.v),
+        patched_k_norms=norms(patched.k), patched_v_norms=norms(patched.v),
+        fresh_k_norms=norms(kv_fresh.k), fresh_v_norms=norms(kv_fresh.v),
+    )
+
+
+def engine_case(ref_src: str) -> None:
+    sys.path.insert(0, ref_src)
+    import copy
+
+    import torch
+
+    import deltakv.engine as E
+    from deltakv.config import DeltaKVConfig
+    from deltakv.connectors.vllm import DeltaKVConnector
+    from deltakv.deltas.descriptor import lora_layer
+    from deltakv.deltas.factors import random_lora_factors
+    from deltakv.deltas.lora import lora_delta
+    from deltakv.model import ToyConfig, ToyTransformer
+    from deltakv.types import CompatibilityLevel, WeightVersion
+
+    torch.set_num_threads(4)
+    torch.set_grad_enabled(False)
+    cfg = ToyConfig(n_layers=4, d_model=64, n_heads=4, n_kv_heads=2, d_ff=128, vocab_size=256)
+    torch.manual_seed(0)
+    model0 = ToyTransformer(cfg)
+    state0 = copy.deepcopy(model0.state_dict())
+    tokens = torch.randint(0, 256, (64,), generator=torch.Generator().manual_seed(0))
+    rng = torch.Generator().manual_seed(1)
+    d_kv, d_q = cfg.n_kv_heads * cfg.head_dim, cfg.n_heads * cfg.head_dim
+    layers, fac = {}, {}
+    for i in range(cfg.n_layers):
+        k = random_lora_factors(cfg.d_model, d_kv, 4, scale=0.01, generator=rng, name="k_proj")
+        v = random_lora_factors(cfg.d_model, d_kv, 4, scale=0.01, generator=rng, name="v_proj")
+        q = random_lora_factors(cfg.d_model, d_q, 4, scale=0.01, generator=rng, name="q_proj")
+        layers[i] = lora_layer(i, k=k, v=v, q=q)
+        for n_, f in (("k", k), ("v", v), ("q", q)):
+            fac.setdefault(f"a_{n_}", []).append(f.A.numpy())
+            fac.setdefault(f"b_{n_}", []).append(f.B.numpy())
+            fac.setdefault(f"s_{n_}", []).append(float(f.scale))
+    delta = lora_delta(source=WeightVersion(id="base"), target=WeightVersion(id="lora-v1", parent_id="base",
+                                                                              kind="lora"), layers=layers)
+    out = {k: np.stack(v) if k[0] in "ab" else np.array(v, np.float32) for k, v in fac.items()}
+    out["tokens"] = tokens.numpy()
+    names = ("zeroth_order_patches", "weight_axis_scores", "select_probes", "apply_probe_to_cache")
+    orig = {n: getattr(E, n) for n in names}
+    for route, request, gate_off in (("exact", "exact", False), ("hybrid", "hybrid", False),
+                                     ("subspace", "probe", True)):
+        rec = {}
+
+        def zeroth(xn, d, **kw):
+            rec["xn"] = np.stack([xn[l].numpy() for l in sorted(xn)])
+            return orig["zeroth_order_patches"](xn, d, **kw)
+
+        def scores(x, d, layer_idx=0):
+            rec["score_x"], rec["score_layer"] = x.numpy().copy(), np.int32(layer_idx)
+            r = orig["weight_axis_scores"](x, d, layer_idx)
+            rec["scores"] = r.numpy().copy()
+            return r
+
+        def select(sc, ratio, mn=4, mx=0.5):
+            rec["ratio"], rec["min_tokens"], rec["max_ratio"] = np.float64(ratio), np.int32(mn), np.float64(mx)
+            r = orig["select_probes"](sc, ratio, mn, mx)
+            rec["probes"] = r.numpy().copy()
+            return r
+
+        def probe(kv, fresh, probes, thr=0.15, maxr=0.40, *, layer_deltas=None, subspace_rank=8,
+                  probe_layers=None, skip_layers=None):
+            if gate_off:
+                probe_layers = set()
+            rec["kv_in_k"], rec["kv_in_v"] = kv.k.numpy().copy(), kv.v.numpy().copy()
+            ls = sorted(fresh)
+            rec["fresh_layers"] = np.array(ls, np.int32)
+            rec["fresh_k"] = np.stack([fresh[l][0].numpy() for l in ls])
+            rec["fresh_v"] = np.stack([fresh[l][1].numpy() for l in ls])
+            rec["thr"], rec["maxr"], rec["subspace_rank"] = np.float64(thr), np.float64(maxr), np.int32(subspace_rank)
+            enc = lambda s_: np.array([-1], np.int32) if s_ is None else np.array(sorted(s_), np.int32)
+            rec["probe_layers"], rec["skip_layers"] = enc(probe_layers), enc(skip_layers)
+            res = orig["apply_probe_to_cache"](kv, fresh, probes, thr, maxr, layer_deltas=layer_deltas,
+                                               subspace_rank=subspace_rank, probe_layers=probe_layers,
+                                               skip_layers=skip_layers)
+            rec["kv_out_k"], rec["kv_out_v"], rec["extra"] = res[0].k.numpy().copy(), res[0].v.numpy().copy(), \
+                res[2].numpy().copy()
+            return res
+
+        model = ToyTransformer(cfg)
+        model.load_state_dict(state0)
+        eng = E.DeltaKVEngine(model, DeltaKVConfig())
+        eng.prefill(tokens)
+        entry = next(iter(eng.store.items()))
+        base_k, base_v = entry.base.k.numpy().copy(), entry.base.v.numpy().copy()
+        eng.commit_delta(delta)
+        for n_, fn in zip(names, (zeroth, scores, select, probe)):
+            setattr(E, n_, fn)
+        try:
+            res = eng.evaluate_against_fresh(tokens, route=request)
+        finally:
+            for n_ in names:
+                setattr(E, n_, orig[n_])
+        assert res.decision.level is CompatibilityLevel.PATCHED, res.decision
+        _, fresh_kv, _ = model.prefill(tokens)
+        out[f"{route}_base_k"], out[f"{route}_base_v"] = base_k, base_v
+        out[f"{route}_k"], out[f"{route}_v"] = res.kv.k.numpy(), res.kv.v.numpy()
+        out[f"{route}_kl"] = np.float64(res.report.next_token_kl)
+        out[f"{route}_max_rel_l2"] = np.float64(res.report.max_relative_l2)
+        out[f"{route}_decision_route"] = np.array(res.decision.route.value)
+        for k, v in rec.items():
+            out[f"{route}_{k}"] = v
+        if route == "exact":
+            out["fresh_k"], out["fresh_v"] = fresh_kv.k.numpy(), fresh_kv.v.numpy()
+            sd = model.state_dict()
+            for key, t in sd.items():
+                out["w_" + key.replace(".", "_")] = t.numpy().copy()
+            out["rope_cos"] = model.rope.cos_cached[:, : cfg.head_dim // 2].numpy()
+            out["rope_sin"] = model.rope.sin_cached[:, : cfg.head_dim // 2].numpy()
+            # the connector writes the materialised view into vLLM's paged buffers
+            bs, nb = 16, 9
+            gp = torch.Generator().manual_seed(3)
+            table = torch.randperm(nb, generator=gp)[:4].tolist()
+            kc = [torch.randn(nb, bs, cfg.n_kv_heads, cfg.head_dim, generator=gp).to(torch.bfloat16)
+                  for _ in range(cfg.n_layers)]
+            vc = [torch.randn(nb, bs, cfg.n_kv_heads, cfg.head_dim, generator=gp).to(torch.bfloat16)
+                  for _ in range(cfg.n_layers)]
+            out["conn_k_in"] = np.stack([bf16_bits(c) for c in kc])
+            out["conn_v_in"] = np.stack([bf16_bits(c) for c in vc])
+            # unbound: with vLLM 0.22 installed the connector's constructor fails (it assigns the
+            # base class's read-only `role` property); patch_paged itself does not use `self`
+            DeltaKVConnector.patch_paged(None, res.kv, kc, vc, table, bs)
+            out["conn_k_out"] = np.stack([bf16_bits(c) for c in kc])
+            out["conn_v_out"] = np.stack([bf16_bits(c) for c in vc])
+            out["conn_table"] = np.array(table, np.int32)
+            out["conn_bs"] = np.int32(bs)
+    for key in ("n_heads", "n_kv_heads", "head_dim", "n_layers"):
+        out[key] = np.int32(getattr(cfg, key))
+    out["eps"] = np.float32(cfg.rms_eps)
+    np.savez_compressed(OUT / "engine.npz", **out)
+
+
+CASES = {"core": core_cases, "engine": engine_case, "smol_kl": smol_kl_case}
+
+
+def main(ref_src: str, cases=None) -> None:
+    for name in cases or list(CASES):
+        CASES[name](ref_src)
     print("wrote", sorted(p.name for p in OUT.glob("*.npz")))
 
 
 if __name__ == "__main__":
     if len(sys.argv) < 2:
-        sys.exit("usage: make_golden.py <reference checkout>/src")
-    main(sys.argv[1])
+        sys.exit("usage: make_golden.py <reference checkout>/src [core|engine|smol_kl ...]")
+    main(sys.argv[1], sys.argv[2:] or None)

@@ -1,0 +1,79 @@
+"""Next-token KL of the patched cache beyond the 4-layer toy: the SmolLM2-135M shape.
+
+Weights, tokens and the rank-8 q/k/v/o LoRA come from seeds (tests/_smol_model.py: d=576,
+9 / 3 heads of 64, SwiGLU 1536, vocab 49152, 2048 tokens; 4 of the 30 layers so the fp32
+oracle prefill stays within a test's time).  The oracle prefill gives the stored layer
+inputs and the stale K/V (pinned against the reference's own run by
+tests/test_oracle_golden.py::test_smol_prefill_and_kl_golden).  This build then patches the
+way the throughput run does: layer inputs stored as f16 codes with power-of-two row scales
+and per-row sums of squared codes, RMSNorm folded, rank-8 k/v factors, RoPE, bf16 paged K/V
+through a permuted block table, one fused launch.  The patched pages are scored by the
+oracle's last-token pass under the updated weights.
+
+Bars (src/deltakv/metrics.py:92-98): KL(fresh || patched) within 1e-4 nats of the
+reference's KL(fresh || patched_reference); and, tighter, KL(patched_reference || patched)
+below 1e-6 nats — 25x what storing the reference's own patched cache in bf16 costs (4e-8),
+while the unpatched cache sits 6.5e-5 from fresh.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import deltakv_b200 as dkv
+from deltakv_b200 import ops
+from oracle import exact as OX
+from oracle import model as OM
+from tests import _smol_model as SM
+from tests.conftest import golden
+from tests.helpers import bits_from_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def test_smollm2_shape_next_token_kl(cuda):
+    g = golden("smol_kl")
+    w = SM.weights()
+    dl = SM.delta(w)
+    toks = g["tokens"]
+    tabs = OX.rope_tables(SM.HD, SM.SEQ, SM.ROPE_BASE)
+    kw = dict(n_layers=SM.N_LAYERS, n_heads=SM.N_HEADS, n_kv=SM.N_KV, hd=SM.HD, eps=SM.EPS, rope=tabs)
+    _, k0, v0, h = OM.prefill(w, toks, **kw)
+    L_, n = SM.N_LAYERS, SM.SEQ
+    # stored activations as the engine would keep them: f16 codes, row scale, sums of squares
+    xq, xs, ssq = dkv.quantize_rows(torch.from_numpy(h).to(cuda), torch.float16, with_sumsq=True)
+    # the stale cache in bf16 pages through a permuted block table
+    bs = 16
+    nblk = n // bs
+    perm = np.random.default_rng(9).permutation(nblk + 3)[:nblk].astype(np.int32)
+    pages = []
+    for src in (k0, v0):
+        p = torch.randn(L_, nblk + 3, bs, SM.N_KV, SM.HD, generator=torch.Generator().manual_seed(4))
+        p[:, torch.from_numpy(perm).long()] = torch.from_numpy(src).view(L_, nblk, bs, SM.N_KV, SM.HD)
+        pages.append(p.to(torch.bfloat16).to(cuda))
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    patcher = dkv.ExactPatcher(SM.D, SM.N_KV, SM.HD, rank_k=SM.RANK, rank_v=SM.RANK, x_dtype=torch.float16,
+                               rope=(torch.from_numpy(tabs[0]), torch.from_numpy(tabs[1])), norm_eps=SM.EPS)
+    fac = lambda p, i: np.stack([dl[l][p][i] for l in range(L_)])
+    scaled_b = lambda p: np.stack([dl[l][p][1] * dl[l][p][2] for l in range(L_)])
+    packed = patcher.pack(t(fac("k_proj", 0)), t(scaled_b("k_proj")), t(fac("v_proj", 0)), t(scaled_b("v_proj")),
+                          1.0, 1.0, norm_weight=t(np.stack([w[f"blocks_{l}_attn_norm_weight"] for l in range(L_)])))
+    seqs = ops.SeqBatchTensors(cu_seqlens=torch.tensor([0, n], dtype=torch.int32, device=cuda),
+                               block_tables=t(perm[None]), max_seq_len=n)
+    patcher.apply(xq, packed, [pages[0][l] for l in range(L_)], [pages[1][l] for l in range(L_)], seqs,
+                  x_scale=xs, apply_norm=True, x_sumsq=ssq, check=True)
+    torch.cuda.synchronize()
+    got = []
+    for p in pages:
+        bits = bits_from_bf16(p)
+        f = (bits.astype(np.uint32) << 16).view(np.float32).reshape(p.shape)
+        got.append(f[:, perm].reshape(L_, n, SM.N_KV, SM.HD))
+    logits = OM.logits_from_kv(SM.merged(w, dl), toks, got[0], got[1], **kw)
+    kl = OM.next_token_kl(g["fresh_logits"], logits)
+    assert abs(kl - float(g["kl_ref"])) < 1e-4, (kl, float(g["kl_ref"]))
+    assert OM.next_token_kl(g["patched_logits"], logits) < 1e-6
+    # the patch moved the cache: the stale cache is measurably further from fresh
+    stale = OM.logits_from_kv(SM.merged(w, dl), toks, k0, v0, **kw)
+    assert OM.next_token_kl(g["patched_logits"], stale) > 10 * OM.next_token_kl(g["patched_logits"], logits)

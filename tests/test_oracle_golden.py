@@ -282,3 +282,55 @@ def test_probe_and_replay_oracle_golden():
     r = golden("replay")
     k, v = OP.replay(r["base_k"], r["base_v"], _replay_chain(r))
     assert np.abs(k - r["out_k"]).max() < 1e-5 and np.abs(v - r["out_v"]).max() < 1e-5
+
+
+def _smol_patched(w, dl, h, k, v):
+    """The oracle's exact branch on the SmolLM2-shaped stack: RMSNorm -> exact_kv_delta (k/v
+    factors) added to the cached K/V."""
+    from tests import _smol_model as SM
+
+    tabs = OX.rope_tables(SM.HD, SM.SEQ, SM.ROPE_BASE)
+    kp, vp = k.copy(), v.copy()
+    for l in range(SM.N_LAYERS):
+        xn = OX.rmsnorm(h[l], w[f"blocks_{l}_attn_norm_weight"], SM.EPS)
+        dk, dv = OX.exact_kv_delta(xn, dl[l]["k_proj"], dl[l]["v_proj"], SM.N_KV, SM.HD, tabs)
+        kp[l] += dk
+        vp[l] += dv
+    return kp, vp
+
+
+def test_smol_prefill_and_kl_golden():
+    """The oracle prefill and exact branch at the SmolLM2-135M shape (4 of 30 layers, 2048
+    tokens) against the reference's own run; also the size of the error that storing the
+    patched cache in bf16 pages adds to the next-token distribution."""
+    from oracle import model as OM
+    from tests import _smol_model as SM
+
+    g = golden("smol_kl")
+    assert np.array_equal(g["tokens"], SM.tokens())
+    w = SM.weights()
+    dl = SM.delta(w)
+    kw = dict(n_layers=SM.N_LAYERS, n_heads=SM.N_HEADS, n_kv=SM.N_KV, hd=SM.HD, eps=SM.EPS,
+              rope=OX.rope_tables(SM.HD, SM.SEQ, SM.ROPE_BASE))
+    _, k, v, h = OM.prefill(w, g["tokens"], **kw)
+    rel = lambda a, b: float(np.linalg.norm(a - b) / np.linalg.norm(b))
+    # fp32 summation order (2048-key softmax sums, 576/1536-long products) differs from torch's:
+    # ~1e-5 relative after four blocks
+    assert rel(h[:, :4], g["h_head"]) < 5e-5 and rel(h[:, -4:], g["h_tail"]) < 5e-5
+    assert rel(k[:, -4:], g["k_tail"]) < 5e-5 and rel(v[:, -4:], g["v_tail"]) < 5e-5
+    norms = lambda t: np.array([np.linalg.norm(t[l].astype(np.float64)) for l in range(t.shape[0])])
+    for got, key in ((h, "h_norms"), (k, "k_norms"), (v, "v_norms")):
+        assert np.allclose(norms(got), g[key], rtol=1e-5)
+    kp, vp = _smol_patched(w, dl, h, k, v)
+    assert np.allclose(norms(kp), g["patched_k_norms"], rtol=1e-5)
+    assert np.allclose(norms(vp), g["patched_v_norms"], rtol=1e-5)
+    w1 = SM.merged(w, dl)
+    logits = OM.logits_from_kv(w1, g["tokens"], kp, vp, **kw)
+    assert OM.next_token_kl(g["patched_logits"], logits) < 1e-8
+    assert abs(OM.next_token_kl(g["fresh_logits"], logits) - float(g["kl_ref"])) < 1e-6
+    # the same cache rounded to bf16 pages: bf16 storage alone moves the next-token
+    # distribution by ~4e-8 nats, the floor of the GPU test's 1e-6 bound
+    kb = bf16_bits_to_f32(f32_to_bf16_bits(kp)).reshape(kp.shape)
+    vb = bf16_bits_to_f32(f32_to_bf16_bits(vp)).reshape(vp.shape)
+    lb = OM.logits_from_kv(w1, g["tokens"], kb, vb, **kw)
+    assert OM.next_token_kl(g["patched_logits"], lb) < 2e-7

@@ -90,6 +90,15 @@ class SeqBatchTensors:
     table_lens: torch.Tensor | None = None
     positions: torch.Tensor | None = None
 
+    def __post_init__(self):
+        bt = self.block_tables
+        if self.table_lens is None and bt.ndim == 2 and bt.shape[0] > 0 and bt.stride(0) != bt.shape[1]:
+            # Without per-row lengths the C ABI takes a row's length from the row stride, so
+            # the rows get standard strides here (numpy's x[None] gives a one-row table row
+            # stride 0; a column slice has a stride above its width).  Kept in the dataclass,
+            # the copy lives as long as the launches that read it.
+            self.block_tables = torch.empty(bt.shape, dtype=bt.dtype, device=bt.device).copy_(bt)
+
     def struct(self) -> L.SeqBatch:
         _require_cuda(self.cu_seqlens, self.block_tables, self.table_lens, self.positions)
         for t in (self.cu_seqlens, self.block_tables, self.table_lens, self.positions):

@@ -84,3 +84,24 @@ def test_cpu_tensors_are_rejected():
 
     with pytest.raises(ValueError, match="CUDA"):
         dkv.scatter_into_paged(torch.zeros(4, 1, 8), torch.zeros(1, 8, 1, 8), [0], 8)
+
+
+def test_block_table_rows_get_standard_strides():
+    """Without per-row lengths the ABI reads a row's length from its stride: one-row tables
+    from numpy's x[None] (row stride 0) and column slices are given standard strides."""
+    import numpy as np
+    import torch
+
+    from deltakv_b200.ops import SeqBatchTensors
+
+    cu = torch.tensor([0, 80], dtype=torch.int32)
+    one = torch.from_numpy(np.arange(5, dtype=np.int32)[None])
+    s = SeqBatchTensors(cu_seqlens=cu, block_tables=one, max_seq_len=80)
+    assert s.block_tables.stride(0) == 5 and torch.equal(s.block_tables, one)
+    wide = torch.arange(30, dtype=torch.int32).view(3, 10)[:, :4]
+    s = SeqBatchTensors(cu_seqlens=torch.tensor([0, 1, 2, 3], dtype=torch.int32), block_tables=wide, max_seq_len=1)
+    assert s.block_tables.stride(0) == 4 and torch.equal(s.block_tables, wide)
+    lens = torch.tensor([4, 4, 4], dtype=torch.int32)
+    s = SeqBatchTensors(cu_seqlens=torch.tensor([0, 1, 2, 3], dtype=torch.int32), block_tables=wide, max_seq_len=1,
+                        table_lens=lens)
+    assert s.block_tables.stride(0) == 10  # explicit lengths: the caller's strides are kept

@@ -65,6 +65,13 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
+// a pair of fp32 values as two bf16 terms each: hi = RN_bf16(x), lo = RN_bf16(x - hi), so
+// x = hi + lo to within 2^-16 |x|; (hi, lo) pairs feed split-precision tensor-core products
+// (a b ~ ah bh + ah bl + al bh, fp32 accumulation)
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t &hi, uint32_t &lo) {
+  hi = pack_bf16x2(a, b);
+  lo = pack_bf16x2(__fsub_rn(a, bf16lo(hi)), __fsub_rn(b, bf16hi(hi)));
+}
 __device__ __forceinline__ float f16lo(uint32_t w) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xffffu)));
 }

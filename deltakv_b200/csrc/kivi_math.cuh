@@ -58,6 +58,25 @@ __device__ __forceinline__ uint32_t quant_recip(float y) {
   return q < 15u ? q : 15u;
 }
 
+// quant_one's codes for a pair, through the reciprocal: y = (x - z) * RN(1/s) lies within 2 ulp
+// (< 4e-6 for |y| < 16) of the IEEE quotient, so rint(y) equals rint(quotient) unless y is
+// that close to a rounding tie; where either value of the pair is within 1e-5 of a tie
+// (|y - rint(y)| > 1/2 - 1e-5) both quotients are formed exactly.  a2 = the (x - z) pair,
+// s = the group's fp16 scale as a float, inv = RN(1/s) (0 when s = 0: every code is 0).
+__device__ __forceinline__ void quant_pair(uint64_t a2, float s, float inv, uint32_t &q0, uint32_t &q1) {
+  float y0, y1;
+  f2unpack(mul2(a2, f2pack(inv, inv)), y0, y1);
+  const float d0 = fabsf(__fsub_rn(y0, rintf(y0))), d1 = fabsf(__fsub_rn(y1, rintf(y1)));
+  if (__builtin_expect(fmaxf(d0, d1) > 0.49999f, 0)) {
+    float a0, a1;
+    f2unpack(a2, a0, a1);
+    y0 = exact_quotient(a0, s);
+    y1 = exact_quotient(a1, s);
+  }
+  q0 = quant_recip(y0);
+  q1 = quant_recip(y1);
+}
+
 __device__ __forceinline__ void quant_group(const float (&x)[kG], int cnt, uint8_t (&q)[kG], __half &s16,
                                             __half &z16) {
   float lo = x[0], hi = x[0];

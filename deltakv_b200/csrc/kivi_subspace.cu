@@ -11,15 +11,16 @@
 // All problems of a call share d; each has its own token count, probes, basis (rank <= 64)
 // and caches.  Launches (all problems at once; the two passes once per grouping mode):
 //   flags   probe flags, deduplicated probe list and count
-//   pack    basis -> bf16 in pass1's MMA fragment order, and a plain row copy
-//   pass1   per warp of 32 tokens: dequant, R, ||R||, rhs = R B (mma.sync bf16, fp32
-//           accumulate), per-tile column sums — no shared memory, no block barrier
+//   pack    basis -> split bf16 terms in pass1's MMA fragment order, and an fp32 row copy
+//   pass1   per warp of 32 tokens: dequant, R, ||R||, rhs = R B (mma.sync on split bf16
+//           terms, fp32 accumulate), per-tile column sums — no block barrier
 //   psum    sums over the probes of R and of rhs
 //   solve   one CTA per problem: G^-1 = (B^T B + 1e-6 I)^-1 in fp64, orth_mu, subspace,
 //           mean ||R||
-//   fitb    B G^-1 (= B G^-T, G symmetric) -> bf16 in pass2's MMA fragment order, so that
-//           fitted = codes B^T = rhs (B G^-1)^T needs no per-token solve
-//   pass2   per warp of 32 tokens: fitted = rhs (B G^-1)^T (mma.sync), corr, requantise —
+//   fitb    B G^-1 (= B G^-T, G symmetric) -> split bf16 terms in pass2's MMA fragment
+//           order, so that fitted = codes B^T = rhs (B G^-1)^T needs no per-token solve
+//   pass2   per warp of 32 tokens: fitted = rhs (B G^-1)^T (mma.sync on split bf16 terms),
+//           corr, requantise (tie-exact: the IEEE quotient of the division form) —
 //           V groups reduced across the 4 lanes of a row, K groups
 //           across the 8 row-lanes of the warp (a warp tile is exactly one K group)
 // Lane (g, q) of a warp owns rows g + 8i (i = 0..3) and, in every block of 32 channels, the
@@ -27,9 +28,14 @@
 // permuting k inside the block (both operands use the same permutation, which leaves R B
 // unchanged), and pass2's basis image permutes output columns so that the accumulator
 // fragments land on those same 8 channels.
-// The products use the basis rounded to bf16 (B~) throughout — G is formed from B~ as well —
-// so `fitted` is the least-squares projection onto col(B~); R, rhs and B~ G^-1 are rounded to
-// bf16 as MMA operands.  These roundings sit far below the int4 step of the output.
+// Precision: the reference computes in fp32.  Every tensor-core operand here is carried as
+// two bf16 terms (x = hi + lo to 2^-16 |x|) and each product as ah bh + ah bl + al bh in fp32
+// accumulation (the dropped al bl is below 2^-16 of the product), so R B and rhs (B G^-1)^T
+// are within ~2^-15 relative of their fp32 values; G = B^T B and its inverse are formed in
+// fp64 from the fp32 basis.  The corrected values then differ from an fp32 evaluation by
+// ~1e-5 of the fitted part, ~1e-6 of an int4 step here, and the requantised codes and fp16
+// scale / zero agree with an fp32 evaluation except where a value lies that close to a
+// rounding tie.
 #include <algorithm>
 #include <cstring>
 #include <vector>
@@ -65,7 +71,8 @@ struct Prob {
   float *rhs, *dist, *part, *sums, *ginv, *mu, *subv;
   uint32_t *flag;
   int32_t *uprobe, *ucount;
-  __nv_bfloat16 *b1, *b2, *bb;
+  __nv_bfloat16 *b1, *b1l, *b2, *b2l;  // MMA B operands: high and low bf16 terms
+  float *bb;                           // the basis as [d][RP] fp32 rows (zero past the rank)
   const float *basis;
   int64_t tile0;
   int r, mode;
@@ -137,15 +144,16 @@ __global__ void flags_kernel(const __grid_constant__ Batch b) {
   }
 }
 
-// basis value B~[c][k] (zero beyond the problem's rank)
-__device__ __forceinline__ __nv_bfloat16 basis_at(const Prob &P, int64_t c, int k) {
-  return __float2bfloat16_rn((k < P.r && P.basis != nullptr) ? P.basis[c * P.r + k] : 0.f);
+// basis value B[c][k] (zero beyond the problem's rank)
+__device__ __forceinline__ float basis_at(const Prob &P, int64_t c, int k) {
+  return (k < P.r && P.basis != nullptr) ? P.basis[c * P.r + k] : 0.f;
 }
 
-// b1 (pass1 B operand): [block][n-tile][lane][8]: B~[32 block + 8q + j][8 nt + g]
-// b2 (pass2 B operand, written by fitb): [block][k-step][n-tile][lane][4]:
-//     (B~ G^-1)[ch][16 ks + 2q + {0, 1, 8, 9}], ch = 32 block + 8 (g >> 1) + 2 nt + (g & 1)
-// bb: [d][RP] rows
+// b1 / b1l (pass1 B operand, high / low bf16 terms): [block][n-tile][lane][8]:
+//     B[32 block + 8q + j][8 nt + g]
+// b2 / b2l (pass2 B operand, written by fitb): [block][k-step][n-tile][lane][4]:
+//     (B G^-1)[ch][16 ks + 2q + {0, 1, 8, 9}], ch = 32 block + 8 (g >> 1) + 2 nt + (g & 1)
+// bb: [d][RP] fp32 rows
 __global__ void pack_kernel(const __grid_constant__ Batch b, int rp) {
   const Prob &P = b.probs[blockIdx.y];
   const int64_t total = b.d * rp;
@@ -164,7 +172,10 @@ __global__ void pack_kernel(const __grid_constant__ Batch b, int rp) {
       const int nt = static_cast<int>(rest % nt_n);
       const int64_t blk = rest / nt_n;
       const int g = lane >> 2, q = lane & 3;
-      P.b1[e] = basis_at(P, kCB * blk + 8 * q + j, 8 * nt + g);
+      const float x = basis_at(P, kCB * blk + 8 * q + j, 8 * nt + g);
+      const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+      P.b1[e] = hi;
+      P.b1l[e] = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
     }
   }
 }
@@ -199,7 +210,7 @@ constexpr int p1_smem_bytes() {
 template <int RP, int MODE>
 constexpr int p1_min_blocks() {
   constexpr bool k = MODE == DKV_KIVI_PER_CHANNEL;
-  return RP == 16 ? (k ? 4 : 6) : RP == 32 ? (k ? 4 : 5) : RP == 48 ? 4 : (k ? 3 : 4);
+  return RP == 16 ? (k ? 4 : 5) : RP == 32 ? 4 : 3;
 }
 
 template <int RP, int FDT, int MODE>
@@ -226,6 +237,7 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
     rv[i] = row[i] < n;
   }
   const uint4 *b1 = reinterpret_cast<const uint4 *>(P.b1) + lane;
+  const uint4 *b1l = reinterpret_cast<const uint4 *>(P.b1l) + lane;
   const int n_blocks = static_cast<int>(b.d / kCB);
   const int64_t krow = t0 / kivi::kG;
   // per-warp staging ring: each lane copies (cp.async) and later reads back only its own
@@ -284,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
         kz8[2 * p] = f16lo(zw[p]), kz8[2 * p + 1] = f16hi(zw[p]);
       }
     }
-    uint32_t a[2][2][4];  // [m-tile][k-step][reg]
+    uint32_t a[2][2][4], al[2][2][4];  // [m-tile][k-step][reg]: R's high and low bf16 terms
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       float r[8];
@@ -331,16 +343,21 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
         for (int j = 0; j < 8; ++j) r[j] = 0.f;
       }
       const int m = i >> 1, h = i & 1;
-      a[m][0][h] = pack_bf16x2(r[0], r[1]);
-      a[m][0][2 + h] = pack_bf16x2(r[2], r[3]);
-      a[m][1][h] = pack_bf16x2(r[4], r[5]);
-      a[m][1][2 + h] = pack_bf16x2(r[6], r[7]);
+      split_bf16x2(r[0], r[1], a[m][0][h], al[m][0][h]);
+      split_bf16x2(r[2], r[3], a[m][0][2 + h], al[m][0][2 + h]);
+      split_bf16x2(r[4], r[5], a[m][1][h], al[m][1][h]);
+      split_bf16x2(r[6], r[7], a[m][1][2 + h], al[m][1][2 + h]);
     }
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const uint4 bv = b1[(static_cast<int64_t>(cb) * NT + nt) * 32];
+      const int64_t fo = (static_cast<int64_t>(cb) * NT + nt) * 32;
+      const uint4 bv = b1[fo], bl = b1l[fo];
 #pragma unroll
-      for (int m = 0; m < 2; ++m) {
+      for (int m = 0; m < 2; ++m) {  // R B ~ Rh Bh + Rh Bl + Rl Bh, small terms first
+        mma16816_bf16(acc[m][nt], al[m][0][0], al[m][0][1], al[m][0][2], al[m][0][3], bv.x, bv.y);
+        mma16816_bf16(acc[m][nt], al[m][1][0], al[m][1][1], al[m][1][2], al[m][1][3], bv.z, bv.w);
+        mma16816_bf16(acc[m][nt], a[m][0][0], a[m][0][1], a[m][0][2], a[m][0][3], bl.x, bl.y);
+        mma16816_bf16(acc[m][nt], a[m][1][0], a[m][1][1], a[m][1][2], a[m][1][3], bl.z, bl.w);
         mma16816_bf16(acc[m][nt], a[m][0][0], a[m][0][1], a[m][0][2], a[m][0][3], bv.x, bv.y);
         mma16816_bf16(acc[m][nt], a[m][1][0], a[m][1][1], a[m][1][2], a[m][1][3], bv.z, bv.w);
       }
@@ -507,8 +524,8 @@ __global__ void __launch_bounds__(256) solve_kernel(const __grid_constant__ Batc
   }
   __syncthreads();
   if (r > 0) {
-    // G = B~^T B~ + 1e-6 I: 64-channel tiles of B~ staged in shared memory as fp64 (exact:
-    // bf16 values), fp64 accumulation; the tile area is the not yet used part of Mdyn past
+    // G = B^T B + 1e-6 I: 64-channel tiles of B staged in shared memory as fp64 (exact:
+    // fp32 values), fp64 accumulation; the tile area is the not yet used part of Mdyn past
     // [G | I].  Thread (bi, bj) of a 16 x 16 grid owns the BS x BS block of G at rows BS bi,
     // columns BS bj (BS = RP / 16), so each staged value it reads feeds BS products.
     double *tile = Mdyn + r * ldm;  // [64][RP]
@@ -522,7 +539,7 @@ __global__ void __launch_bounds__(256) solve_kernel(const __grid_constant__ Batc
     for (int64_t c0 = 0; c0 < b.d; c0 += 64) {
       for (int e = threadIdx.x; e < 64 * RP; e += blockDim.x) {
         const int64_t c = c0 + e / RP;
-        tile[e] = c < b.d ? static_cast<double>(__bfloat162float(P.bb[c * RP + e % RP])) : 0.0;
+        tile[e] = c < b.d ? static_cast<double>(P.bb[c * RP + e % RP]) : 0.0;
       }
       __syncthreads();
       for (int cc = 0; cc < 64; ++cc) {
@@ -623,7 +640,7 @@ __global__ void __launch_bounds__(256) solve_kernel(const __grid_constant__ Batc
   for (int64_t c = threadIdx.x; c < b.d; c += blockDim.x) {
     float fp = 0.f, fa = 0.f;
     for (int i = 0; i < r; ++i) {
-      const float bv = __bfloat162float(P.bb[c * RP + i]);
+      const float bv = P.bb[c * RP + i];
       fp = fmaf(cp[i], bv, fp);
       fa = fmaf(ca[i], bv, fa);
     }
@@ -637,7 +654,8 @@ __global__ void __launch_bounds__(256) solve_kernel(const __grid_constant__ Batc
 }
 
 // ---------------------------------------------------------------------------------------
-// fitb: pass2's B operand, B~ G^-1 in the b2 fragment order; one CTA per 32-channel block
+// fitb: pass2's B operand, B G^-1 as high / low bf16 terms in the b2 fragment order; one CTA
+// per 32-channel block
 // ---------------------------------------------------------------------------------------
 template <int RP>
 __global__ void __launch_bounds__(256) fitb_kernel(const __grid_constant__ Batch b) {
@@ -647,7 +665,7 @@ __global__ void __launch_bounds__(256) fitb_kernel(const __grid_constant__ Batch
   const int64_t blk = blockIdx.x;
   for (int e = threadIdx.x; e < RP * RP; e += blockDim.x) Gf[e / RP][e % RP] = P.ginv[e];  // zero past r
   for (int e = threadIdx.x; e < kCB * RP; e += blockDim.x)
-    Bs[e / RP][e % RP] = __bfloat162float(P.bb[(blk * kCB + e / RP) * RP + e % RP]);
+    Bs[e / RP][e % RP] = P.bb[(blk * kCB + e / RP) * RP + e % RP];
   __syncthreads();
   constexpr int KS = RP / 16;
   for (int f = threadIdx.x; f < KS * 512; f += blockDim.x) {
@@ -658,7 +676,9 @@ __global__ void __launch_bounds__(256) fitb_kernel(const __grid_constant__ Batch
     float acc = 0.f;
 #pragma unroll 8
     for (int j = 0; j < RP; ++j) acc = fmaf(Gf[k][j], Bs[cl][j], acc);
-    P.b2[blk * (KS * 512) + f] = __float2bfloat16_rn(acc);
+    const __nv_bfloat16 hi = __float2bfloat16_rn(acc);
+    P.b2[blk * (KS * 512) + f] = hi;
+    P.b2l[blk * (KS * 512) + f] = __float2bfloat16_rn(__fsub_rn(acc, __bfloat162float(hi)));
   }
 }
 
@@ -667,13 +687,14 @@ __global__ void __launch_bounds__(256) fitb_kernel(const __grid_constant__ Batch
 // ---------------------------------------------------------------------------------------
 constexpr int kP2Stages = 3;  // pass2 staging depth (blocks in flight per warp)
 
-// pass2's basis fragments are staged with the other operands while they are small (RP <= 32)
+// pass2's basis fragments (high and low terms) are staged with the other operands while they
+// are small (RP <= 32)
 template <int RP>
 constexpr int p2_bq() {
-  return RP / 16 <= 2 ? (RP / 16) * 4 : 1;
+  return RP / 16 <= 2 ? (RP / 16) * 8 : 1;
 }
 // one block's operands for one warp in pass2: codes (4 B per lane and row), the K group's
-// scale / zero (16 B each per lane), the lane's basis fragments (8 B each)
+// scale / zero (16 B each per lane), the lane's basis fragments (8 B each, high then low)
 template <int RP, bool K>
 struct P2Stage {
   uint32_t cd[4][32];
@@ -695,7 +716,7 @@ constexpr int p2_ring_bytes() {
 template <int RP, int MODE>
 constexpr int p2_min_blocks() {
   constexpr bool k = MODE == DKV_KIVI_PER_CHANNEL;
-  return RP <= 32 ? (k ? 4 : 5) : RP == 48 ? 4 : 3;
+  return RP == 16 ? (k ? 4 : 5) : RP == 32 ? (k ? 3 : 4) : 3;
 }
 
 template <int RP, int FDT, int MODE>
@@ -728,8 +749,9 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
     fl[i] = rv[i] && P.flag[row[i]] != 0u;
     w[i] = rv[i] ? fminf(P.dist[row[i]] / mean_dist, 1.f) : 0.f;
   }
-  // A fragments: the row's rhs at this lane's positions k = 16 ks + 2q + {0, 1, 8, 9}, bf16
-  uint32_t a[2][KS][4];
+  // A fragments: the row's rhs at this lane's positions k = 16 ks + 2q + {0, 1, 8, 9}, as
+  // high and low bf16 terms
+  uint32_t a[2][KS][4], al[2][KS][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int m = i >> 1, h = i & 1;
@@ -741,12 +763,13 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
         lo = *reinterpret_cast<const float2 *>(rr);
         hi = *reinterpret_cast<const float2 *>(rr + 8);
       }
-      a[m][ks][h] = pack_bf16x2(lo.x, lo.y);
-      a[m][ks][2 + h] = pack_bf16x2(hi.x, hi.y);
+      split_bf16x2(lo.x, lo.y, a[m][ks][h], al[m][ks][h]);
+      split_bf16x2(hi.x, hi.y, a[m][ks][2 + h], al[m][ks][2 + h]);
     }
   }
 
   const uint2 *b2 = reinterpret_cast<const uint2 *>(P.b2) + lane;
+  const uint2 *b2l = reinterpret_cast<const uint2 *>(P.b2l) + lane;
   const int n_blocks = static_cast<int>(b.d / kCB);
   const int64_t krow = t0 / kivi::kG;
   // per-warp staging ring (cp.async, kP2Stages - 1 blocks ahead): each lane copies and later
@@ -764,8 +787,11 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
       }
       if constexpr (kStageB) {
 #pragma unroll
-        for (int f = 0; f < KS * 4; ++f)
-          cp_async8(&S.bq[f][lane], b2 + (static_cast<int64_t>(cb) * KS * 4 + f) * 32, 8u);
+        for (int f = 0; f < KS * 4; ++f) {
+          const int64_t fo = (static_cast<int64_t>(cb) * KS * 4 + f) * 32;
+          cp_async8(&S.bq[2 * f][lane], b2 + fo, 8u);
+          cp_async8(&S.bq[2 * f + 1][lane], b2l + fo, 8u);
+        }
       }
     }
     cp_async_commit();
@@ -782,15 +808,23 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
     for (int ks = 0; ks < KS; ++ks) {
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
-        uint2 bv;
-        if constexpr (kStageB) bv = S.bq[kStageB ? ks * 4 + nt : 0][lane];
-        else bv = b2[((static_cast<int64_t>(cb) * KS + ks) * 4 + nt) * 32];
+        uint2 bv, bw;  // high and low terms of (B G^-1)
+        if constexpr (kStageB) {
+          bv = S.bq[kStageB ? 2 * (ks * 4 + nt) : 0][lane];
+          bw = S.bq[kStageB ? 2 * (ks * 4 + nt) + 1 : 0][lane];
+        } else {
+          const int64_t fo = ((static_cast<int64_t>(cb) * KS + ks) * 4 + nt) * 32;
+          bv = b2[fo];
+          bw = b2l[fo];
+        }
 #pragma unroll
-        for (int m = 0; m < 2; ++m) {
+        for (int m = 0; m < 2; ++m) {  // rhs (B G^-1)^T ~ ah bh + ah bl + al bh, small terms first
           if (ks == 0)
-            mma16816_bf16_zc(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], bv.x, bv.y);
+            mma16816_bf16_zc(acc[m][nt], al[m][ks][0], al[m][ks][1], al[m][ks][2], al[m][ks][3], bv.x, bv.y);
           else
-            mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], bv.x, bv.y);
+            mma16816_bf16(acc[m][nt], al[m][ks][0], al[m][ks][1], al[m][ks][2], al[m][ks][3], bv.x, bv.y);
+          mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], bw.x, bw.y);
+          mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], bv.x, bv.y);
         }
       }
     }
@@ -892,14 +926,14 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
         const float inv = __shfl_sync(0xffffffffu, inv_own, 4 * g + i);
         const float s = __half2float(__ushort_as_half(static_cast<unsigned short>(sz & 0xffffu)));
         const float z = __half2float(__ushort_as_half(static_cast<unsigned short>(sz >> 16)));
-        const uint64_t z2 = f2pack(z, z), inv2 = f2pack(inv, inv);
+        const uint64_t z2 = f2pack(z, z);
         uint32_t wq = 0u;
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-          float y0, y1;
-          f2unpack(mul2(sub2(f2pack(v[i][2 * p], v[i][2 * p + 1]), z2), inv2), y0, y1);
-          wq |= kivi::quant_recip(y0) << (8 * p);
-          wq |= kivi::quant_recip(y1) << (8 * p + 4);
+          uint32_t q0, q1;
+          kivi::quant_pair(sub2(f2pack(v[i][2 * p], v[i][2 * p + 1]), z2), s, inv, q0, q1);
+          wq |= q0 << (8 * p);
+          wq |= q1 << (8 * p + 4);
         }
         if (rv[i]) *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = wq;
       }
@@ -960,13 +994,13 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
         const float inv = __shfl_sync(0xffffffffu, inv_own, 4 * j + q);
         const float s = __half2float(__ushort_as_half(static_cast<unsigned short>(sz & 0xffffu)));
         const float z = __half2float(__ushort_as_half(static_cast<unsigned short>(sz >> 16)));
-        const uint64_t z2 = f2pack(z, z), inv2 = f2pack(inv, inv);
+        const uint64_t z2 = f2pack(z, z);
 #pragma unroll
         for (int i = 0; i < 4; i += 2) {
-          float y0, y1;
-          f2unpack(mul2(sub2(f2pack(v[i][j], v[i + 1][j]), z2), inv2), y0, y1);
-          wq[i] |= kivi::quant_recip(y0) << (4 * j);
-          wq[i + 1] |= kivi::quant_recip(y1) << (4 * j);
+          uint32_t q0, q1;
+          kivi::quant_pair(sub2(f2pack(v[i][j], v[i + 1][j]), z2), s, inv, q0, q1);
+          wq[i] |= q0 << (4 * j);
+          wq[i + 1] |= q1 << (4 * j);
         }
       }
 #pragma unroll
@@ -984,7 +1018,7 @@ inline int64_t al(int64_t x) { return (x + 255) / 256 * 256; }
 
 struct Layout {
   int64_t zero_begin, zero_end, total;
-  std::vector<int64_t> flag, ucount, sums, uprobe, rhs, dist, part, ginv, mu, subv, b1, b2, bb;
+  std::vector<int64_t> flag, ucount, sums, uprobe, rhs, dist, part, ginv, mu, subv, b1, b1l, b2, b2l, bb;
 };
 
 inline int padded_rank(const dkv_kivi_subspace_problem *p, int np) {
@@ -1027,10 +1061,14 @@ inline Layout layout(const dkv_kivi_subspace_problem *p, int np, int64_t d, int 
     o = al(o + (d + 1) * 4);
     L.b1.push_back(o);
     o = al(o + rp * d * 2);
+    L.b1l.push_back(o);
+    o = al(o + rp * d * 2);
     L.b2.push_back(o);
     o = al(o + rp * d * 2);
-    L.bb.push_back(o);
+    L.b2l.push_back(o);
     o = al(o + rp * d * 2);
+    L.bb.push_back(o);
+    o = al(o + rp * d * 4);
   }
   L.total = o;
   return L;
@@ -1219,8 +1257,10 @@ extern "C" int dkv_kivi_subspace_correct(const dkv_kivi_subspace_problem *proble
     P.mu = reinterpret_cast<float *>(ws + L.mu[i]);
     P.subv = reinterpret_cast<float *>(ws + L.subv[i]);
     P.b1 = reinterpret_cast<__nv_bfloat16 *>(ws + L.b1[i]);
+    P.b1l = reinterpret_cast<__nv_bfloat16 *>(ws + L.b1l[i]);
     P.b2 = reinterpret_cast<__nv_bfloat16 *>(ws + L.b2[i]);
-    P.bb = reinterpret_cast<__nv_bfloat16 *>(ws + L.bb[i]);
+    P.b2l = reinterpret_cast<__nv_bfloat16 *>(ws + L.b2l[i]);
+    P.bb = reinterpret_cast<float *>(ws + L.bb[i]);
     P.tile0 = tiles;
     tiles += (P.n + kTM - 1) / kTM;
     if (P.mode == DKV_KIVI_PER_CHANNEL) k_tiles = tiles;

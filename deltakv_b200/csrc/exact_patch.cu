@@ -586,9 +586,10 @@ struct PageRing {
 };
 
 // Expand, RoPE, scale and write back one pass.  `pg` holds the current page chunks when
-// accumulating.
-template <int R16, int PDT>
-__device__ __forceinline__ void expand_pass(const uint4 *__restrict__ bfrag,
+// accumulating.  The pass's B fragments come from shared memory at `bsm` (a per-warp slot the
+// caller staged) when BS, otherwise from global memory at `bfrag`.
+template <int R16, int PDT, bool BS>
+__device__ __forceinline__ void expand_pass(const uint4 *__restrict__ bfrag, uint32_t bsm,
                                             const uint32_t (&cf)[R16][4], const float (&cs)[2][8],
                                             const float (&sn)[2][8], bool rope, int e_lo, int e_hi,
                                             uint8_t *const (&rows)[2], const float (&om)[2],
@@ -600,7 +601,9 @@ __device__ __forceinline__ void expand_pass(const uint4 *__restrict__ bfrag,
   for (int ks = 0; ks < R16; ++ks) {
     uint4 b[4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) b[c] = ldg128_nc(bfrag + (ks * 4 + c) * 32 + lane);
+    for (int c = 0; c < 4; ++c)
+      b[c] = BS ? lds128(bsm + static_cast<uint32_t>(((ks * 4 + c) * 32 + lane) * 16))
+                : ldg128_nc(bfrag + (ks * 4 + c) * 32 + lane);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       if (ks == 0) {
@@ -675,18 +678,33 @@ __device__ __forceinline__ void load_rope(const Params &p, const RowInfo &ri, in
   }
 }
 
+// A CTA-wide ring of B-fragment slots, one pass (16 B x 4 x R16 per lane) per slot.  A
+// producer thread fills the slots with the passes of the CTA's tiles in the order the
+// epilogue consumes them, as far ahead as the ring allows; every epilogue warp reads a slot
+// and releases it (empty: kEpiWarps arrivals).  Fetching the fragments inside the pass
+// (mma.sync operands straight from L2) left every pass's MMAs waiting on L2 latency.
+struct BRing {
+  uint8_t *base;
+  uint64_t *full, *empty;
+  int slot;
+  uint32_t phase;
+};
+
 // All expand passes of one tile (K then V), consuming the page ring whose first `depth`
-// passes the caller has already issued.
-template <int R16, int PDT, int DEPTH>
-__device__ __forceinline__ void phase2(const Params &p, const Tile &t, const RowInfo &ri,
+// passes the caller has already issued.  With BS the passes' B fragments come from the
+// CTA's B ring; returns false when a slot never filled (abort raised).
+template <int R16, int PDT, int DEPTH, bool BS = false>
+__device__ __forceinline__ bool phase2(const Params &p, const Tile &t, const RowInfo &ri,
                                        const RowPtrs &rp, PageRing<PDT> &ring,
                                        const uint32_t (&ck)[R16][4], const uint32_t (&cv)[R16][4],
-                                       const float (&om_k)[2], const float (&om_v)[2], int lane) {
+                                       const float (&om_k)[2], const float (&om_v)[2], int lane,
+                                       BRing *br = nullptr, int n_bslots = 0, volatile int *abort = nullptr) {
   const uint8_t *img = p.packed + t.layer * p.packed_stride;
   const uint4 *bfk = reinterpret_cast<const uint4 *>(img + p.bk_off);
   const uint4 *bfv = reinterpret_cast<const uint4 *>(img + p.bv_off);
   const int q = lane & 3;
   const bool acc = p.accumulate != 0;
+  constexpr uint32_t kBBytes = 16u * 4 * 32 * R16;
   float cs[2][8], sn[2][8];
   int cur_ip = -1;
   Cursor c;
@@ -702,13 +720,21 @@ __device__ __forceinline__ void phase2(const Params &p, const Tile &t, const Row
       cur_ip = c.ip;
     }
     const uint4 *bf = (is_k ? bfk : bfv) + ch.pk * R16 * 4 * 32;
-    {  // pull the next pass's B fragments into L1 (16 lines of 128 B per k-step block)
-      Cursor nx = c;
-      nx.next(p);
-      if (nx.kv < 2 && lane < 16 * R16) {
-        const Chunks nc = chunks_of(p, nx, 0, 0);
-        const uint8_t *nb = reinterpret_cast<const uint8_t *>((nx.kv == 0 ? bfk : bfv) + nc.pk * R16 * 4 * 32);
-        asm volatile("prefetch.global.L1 [%0];" ::"l"(nb + lane * 128));
+    Cursor nx = c;
+    nx.next(p);
+    if (!BS && nx.kv < 2 && lane < 16 * R16) {
+      // pull the next pass's B fragments into L1 (16 lines of 128 B per k-step block)
+      const uint8_t *nb = reinterpret_cast<const uint8_t *>(
+          (nx.kv == 0 ? bfk : bfv) + chunks_of(p, nx, 0, 0).pk * R16 * 4 * 32);
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(nb + lane * 128));
+    }
+    if (BS) {
+      const bool ok = mbar_wait_bounded(&br->full[br->slot], br->phase, abort);
+      if (!__all_sync(0xffffffffu, ok)) {
+        record_error(p.status, DKV_ERR_TIMEOUT);
+        *abort = 1;
+        cp_async_wait<0>();
+        return false;
       }
     }
     cp_async_wait<DEPTH - 1>();
@@ -722,16 +748,26 @@ __device__ __forceinline__ void phase2(const Params &p, const Tile &t, const Row
           pg[r][1].lds(ring.piece(slot, 2 * r + 1, 0, lane));
         }
     }
+    const uint32_t bsm = BS ? smem_u32(br->base) + static_cast<uint32_t>(br->slot) * kBBytes : 0u;
     if (is_k)
-      expand_pass<R16, PDT>(bf, ck, cs, sn, rope, ch.e_lo, ch.e_hi, rp.k, om_k, v2, acc, lane, pg);
+      expand_pass<R16, PDT, BS>(bf, bsm, ck, cs, sn, rope, ch.e_lo, ch.e_hi, rp.k, om_k, v2, acc, lane, pg);
     else
-      expand_pass<R16, PDT>(bf, cv, cs, sn, false, ch.e_lo, ch.e_hi, rp.v, om_v, v2, acc, lane, pg);
+      expand_pass<R16, PDT, BS>(bf, bsm, cv, cs, sn, false, ch.e_lo, ch.e_hi, rp.v, om_v, v2, acc, lane, pg);
+    if (BS) {  // the slot's fragments went into this pass's MMAs: release it
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&br->empty[br->slot]);
+      if (++br->slot == n_bslots) {
+        br->slot = 0;
+        br->phase ^= 1u;
+      }
+    }
     // the chunks read from this slot have been consumed: refill it with the pass DEPTH ahead
     ring.issue(p, rp, lane);
     if (++slot == DEPTH) slot = 0;
     c.next(p);
   }
   cp_async_wait<0>();
+  return true;
 }
 
 // Validity, RoPE position and page offsets of rows g and g+8 of warp `warp` in tile t;
@@ -1120,9 +1156,11 @@ __global__ void __launch_bounds__(kThreads, 1) patch_kernel(const __grid_constan
 // columns, e4m3 x e4m3 or f16 x f16 -> fp32 in TMEM) and, with RMSNorm, for X.X^T whose
 // diagonal is sum(x^2).  Accumulators are double-buffered across tiles when they fit, so
 // the tensor cores and the X stream work on tile i+1 while the epilogue patches tile i.
-constexpr int kTcWarps = 12;
+constexpr int kTcWarps = 12;  // 8 epilogue, TMA producer, MMA issuer, B-fragment producer, idle
 constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kEpiWarps = 8;
+constexpr int kBProdWarp = 10;
+constexpr int kBSlots = 8;  // passes of B fragments in flight or waiting in shared memory
 
 template <int XT, int R16, bool NORM>
 struct TcCfg {
@@ -1149,8 +1187,14 @@ struct TcSmem {
   static constexpr int P_OFF = A_OFF + C::STAGES * C::A_STAGE;
   static constexpr int CODES_OFF = P_OFF + kEpiWarps * RING;
   static constexpr int OM_OFF = CODES_OFF + 2 * 128 * C::CROW;
-  static constexpr int BAR_OFF = OM_OFF + 2 * 2 * 128 * 4;
-  static constexpr int N_BARS = 2 * C::STAGES + 4 + 1 + 4;
+  // the CTA's B-fragment ring (kBSlots passes), when it fits next to the other rings
+  static constexpr int BSLOT = 16 * 4 * 32 * R16;
+  static constexpr int B_OFF = OM_OFF + 2 * 2 * 128 * 4;
+  static constexpr int BASE_BARS = 2 * C::STAGES + 4 + 1 + 4;
+  static constexpr bool BSMEM =
+      1024 + B_OFF + kBSlots * BSLOT + (BASE_BARS + 2 * kBSlots) * 8 + 16 <= 227 * 1024;
+  static constexpr int BAR_OFF = B_OFF + (BSMEM ? kBSlots * BSLOT : 0);
+  static constexpr int N_BARS = BASE_BARS + (BSMEM ? 2 * kBSlots : 0);
   static constexpr int MISC_OFF = BAR_OFF + N_BARS * 8;
   static constexpr int BYTES = MISC_OFF + 16;
 };
@@ -1278,6 +1322,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
   uint64_t *done = tempty + 2;
   uint64_t *cready = done + 1;   // [2] codes buffer written by all epilogue warps
   uint64_t *cfree = cready + 2;  // [2] codes buffer read by all epilogue warps
+  uint64_t *bfull = cfree + 2;       // [kBSlots] B ring slot filled (BSMEM)
+  uint64_t *bempty = bfull + kBSlots; // [kBSlots] B ring slot read by every epilogue warp
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + S::MISC_OFF);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + S::MISC_OFF + 4);
 
@@ -1296,6 +1342,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
       mbar_init(&cready[b], kEpiWarps);
       mbar_init(&cfree[b], kEpiWarps);
     }
+    if (S::BSMEM)
+      for (int i = 0; i < kBSlots; ++i) {
+        mbar_init(&bfull[i], 1);
+        mbar_init(&bempty[i], kEpiWarps);
+      }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -1379,6 +1430,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
     PageRing<PDT> ring;
     ring.base = smem_u32(smem + S::P_OFF) + warp * S::RING;
     ring.depth = DEPTH;
+    BRing bring{smem + S::B_OFF, bfull, bempty, 0, 0u};
     auto next_valid = [&](int64_t tile, Tile &t) -> int64_t {
       for (; tile < p.n_tiles; tile += gridDim.x)
         if (decode_tile(p, tile, t)) return tile;
@@ -1439,12 +1491,65 @@ __global__ void __launch_bounds__(kTcThreads, 1) patch_kernel_tc(const __grid_co
         __syncwarp();
         if (lane == 0) mbar_arrive(&cready[np1]);
       }
-      phase2<R16, PDT, DEPTH>(p, tc, ri, rp, ring, ck, cv, om_k, om_v, lane);
+      if (!phase2<R16, PDT, DEPTH, S::BSMEM>(p, tc, ri, rp, ring, ck, cv, om_k, om_v, lane, &bring, kBSlots,
+                                               abort_flag))
+        break;
       tile = ntile;
       tc = tn;
       ++j;
     }
     cp_async_wait<0>();
+  } else if (S::BSMEM && warp == kBProdWarp) {
+    // --------------------------- B-fragment producer ---------------------------
+    // Walks the tiles and passes in the epilogue's order and fills each ring slot as soon as
+    // all epilogue warps have released it.
+    if (lane == 0) {
+      constexpr uint32_t kBBytes = S::BSLOT;
+      int slot = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0, parity = 0;  // slots with a copy issued, and its phase (drain below)
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; tile < p.n_tiles && ok; tile += gridDim.x) {
+        Tile t;
+        if (!decode_tile(p, tile, t)) continue;
+        const uint8_t *img = p.packed + t.layer * p.packed_stride;
+        const uint4 *bfk = reinterpret_cast<const uint4 *>(img + p.bk_off);
+        const uint4 *bfv = reinterpret_cast<const uint4 *>(img + p.bv_off);
+        Cursor c;
+        c.begin(p);
+        while (c.kv < 2) {
+          if (!mbar_wait_bounded(&bempty[slot], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&bfull[slot], kBBytes);
+          bulk_load(smem + S::B_OFF + slot * S::BSLOT,
+                    (c.kv == 0 ? bfk : bfv) + chunks_of(p, c, 0, 0).pk * R16 * 4 * 32, kBBytes, &bfull[slot]);
+          issued |= 1u << slot;
+          parity = (parity & ~(1u << slot)) | (phase << slot);
+          c.next(p);
+          if (++slot == kBSlots) {
+            slot = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && !*abort_flag) {
+        record_error(p.status, DKV_ERR_TIMEOUT);
+        *abort_flag = 1;
+      }
+      // never exit with a copy still landing in shared memory
+      for (int i = 0; i < kBSlots; ++i) {
+        if (!(issued & (1u << i))) continue;
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&bfull[i], (parity >> i) & 1u)) {
+          if (clock64() - t0 > kWaitLimitCycles) {
+            record_error(p.status, DKV_ERR_TIMEOUT);
+            break;
+          }
+        }
+      }
+    }
   }
 
   // ------------------------------- teardown -------------------------------

@@ -77,3 +77,61 @@ def test_smollm2_shape_next_token_kl(cuda):
     # the patch moved the cache: the stale cache is measurably further from fresh
     stale = OM.logits_from_kv(SM.merged(w, dl), toks, k0, v0, **kw)
     assert OM.next_token_kl(g["patched_logits"], stale) > 10 * OM.next_token_kl(g["patched_logits"], logits)
+
+
+def test_smollm2_shape_int4_subspace_route_kl(cuda):
+    """The multi-adapter maintenance route on a real stack: the stale cache of the SmolLM2-shaped
+    decoder (4 layers, 2048 tokens, d_kv 192) stored KIVI int4, corrected per layer toward the
+    fresh prefill under the LoRA'd weights from every 10th token (K basis: the probe residual's
+    top-8 subspace; V basis: the adapter's LoRA B), stored int4 again; scored by next-token KL
+    against the fresh logits.  Held to the oracle composition (KIVI dequantise ->
+    subspace_correct -> quantise, fp32): KL within 1e-4 nats of the oracle's, and the two
+    corrected caches' next-token distributions within 1e-6 nats of each other."""
+    from deltakv_b200 import kivi as K
+    from oracle import kivi as OK
+    from oracle import subspace as OS
+
+    g = golden("smol_kl")
+    w = SM.weights()
+    dl = SM.delta(w)
+    w1 = SM.merged(w, dl)
+    toks = g["tokens"]
+    tabs = OX.rope_tables(SM.HD, SM.SEQ, SM.ROPE_BASE)
+    kw = dict(n_layers=SM.N_LAYERS, n_heads=SM.N_HEADS, n_kv=SM.N_KV, hd=SM.HD, eps=SM.EPS, rope=tabs)
+    _, k0, v0, _ = OM.prefill(w, toks, **kw)
+    _, k1, v1, _ = OM.prefill(w1, toks, **kw)
+    L_, n, d = SM.N_LAYERS, SM.SEQ, SM.N_KV * SM.HD
+    probes = np.arange(0, n, 10)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    ours, ref = {"k": [], "v": []}, {"k": [], "v": []}
+    probs = []
+    for l in range(L_):
+        for mode, stale, fresh in (("k", k0[l], k1[l]), ("v", v0[l], v1[l])):
+            c, s, z = OK.quantize(stale.reshape(n, d), mode)
+            basis = dl[l]["v_proj"][1] if mode == "v" else None  # the adapter's LoRA B [d_kv, r]
+            reused = OK.dequantize(c, s, z, mode)
+            corr, _, _ = OS.subspace_correct(reused.reshape(n, SM.N_KV, SM.HD), fresh, probes, basis=basis,
+                                             rank=SM.RANK)
+            ref[mode].append(OK.dequantize(*OK.quantize(corr.reshape(n, d), mode), mode).reshape(n, SM.N_KV, SM.HD))
+            probs.append(K.SubspaceProblem(base=K.KiviTensor(t(c), t(s), t(z), mode), fresh=t(fresh.reshape(n, d)),
+                                           probe_index=t(probes), basis=None if basis is None else t(basis),
+                                           rank=SM.RANK, out=K.KiviTensor.empty(n, d, mode, cuda)))
+    K.subspace_correct(probs)
+    torch.cuda.synchronize()
+    for i, pb in enumerate(probs):
+        mode = "k" if i % 2 == 0 else "v"
+        ours[mode].append(K.dequantize(pb.out).cpu().numpy().reshape(n, SM.N_KV, SM.HD))
+    stack = lambda m: np.stack(m)
+    lo = OM.logits_from_kv(w1, toks, stack(ours["k"]), stack(ours["v"]), **kw)
+    lr = OM.logits_from_kv(w1, toks, stack(ref["k"]), stack(ref["v"]), **kw)
+    kl_ours = OM.next_token_kl(g["fresh_logits"], lo)
+    kl_ref = OM.next_token_kl(g["fresh_logits"], lr)
+    stale = [OK.dequantize(*OK.quantize(x[l].reshape(n, d), m), m).reshape(n, SM.N_KV, SM.HD)
+             for x, m in ((k0, "k"), (v0, "v")) for l in range(L_)]
+    kl_stale = OM.next_token_kl(g["fresh_logits"], OM.logits_from_kv(w1, toks, np.stack(stale[:L_]),
+                                                                      np.stack(stale[L_:]), **kw))
+    print("int4 route KL: ours", kl_ours, "oracle", kl_ref, "stale int4", kl_stale,
+          "ours vs oracle", OM.next_token_kl(lr, lo))
+    assert abs(kl_ours - kl_ref) < 1e-4
+    assert OM.next_token_kl(lr, lo) < 1e-6
+    assert kl_ours < kl_stale  # the correction moved the int4 cache toward fresh

@@ -68,3 +68,33 @@ def merged(w: dict[str, np.ndarray], dl: dict) -> dict[str, np.ndarray]:
             key = f"blocks_{i}_{name}_weight"
             out[key] = (w[key] + np.float32(s) * (B @ A)).astype(np.float32)
     return out
+
+
+def dense_delta(w: dict[str, np.ndarray], seed: int = 3, rel: float = 0.02) -> dict[int, dict[str, np.ndarray]]:
+    """A full-rank dW on k_proj and v_proj of every layer (an RL step's delta), Gaussian with
+    ||dW||_F = rel ||W||_F, rounded to bf16 values (the dense route's operand type)."""
+    rng = np.random.default_rng(seed)
+    out = {}
+    for i in range(N_LAYERS):
+        out[i] = {}
+        for name in ("k_proj", "v_proj"):
+            W = w[f"blocks_{i}_{name}_weight"]
+            dw = rng.standard_normal(W.shape).astype(np.float32)
+            dw *= np.float32(rel * np.linalg.norm(W) / np.linalg.norm(dw))
+            out[i][name] = _to_bf16(dw)
+    return out
+
+
+def merged_dense(w: dict[str, np.ndarray], dd: dict) -> dict[str, np.ndarray]:
+    out = dict(w)
+    for i, projs in dd.items():
+        for name, dw in projs.items():
+            key = f"blocks_{i}_{name}_weight"
+            out[key] = (w[key] + dw).astype(np.float32)
+    return out
+
+
+def _to_bf16(x: np.ndarray) -> np.ndarray:
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32)
+    r = ((u + (((u >> 16) & 1) + np.uint32(0x7FFF))) & np.uint32(0xFFFF0000)).view(np.float32)
+    return r.astype(np.float32)

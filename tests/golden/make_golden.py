@@ -51,6 +51,9 @@ Cases:
                    results of every hot-path call the engine made (recorded by wrapping the
                    engine module's names), the report, and DeltaKVConnector.patch_paged of the
                    exact view into bf16 paged caches.
+  smol_dense.npz   the same stack with a full-rank dW on k/v of every layer (relative norm 0.02,
+                   bf16 values) through the reference's exact route with A=dW, B=I: fresh,
+                   patched and stale last-token logits and their KL.
   smol_kl.npz      SmolLM2-135M-shaped decoder (tests/_smol_model.py: seeded weights, 4 of
                    30 layers, 2048 tokens, rank-8 q/k/v/o LoRA at relative norm 0.01): the
                    reference's prefill, rmsnorm_tensors -> zeroth_order_patches ->
@@ -753,7 +756,55 @@ def engine_case(ref_src: str) -> None:
     np.savez_compressed(OUT / "engine.npz", **out)
 
 
-CASES = {"core": core_cases, "engine": engine_case, "smol_kl": smol_kl_case}
+def smol_dense_case(ref_src: str) -> None:
+    """smol_dense.npz: a full-rank dW on k/v of every layer of the SmolLM2-shaped stack through
+    the reference's exact route as LowRankFactors(A=dW, B=I, scale=1) (rmsnorm_tensors ->
+    zeroth_order_patches -> apply_layer_patches), then apply_delta and a fresh prefill."""
+    sys.path.insert(0, ref_src)
+    sys.path.insert(0, str(OUT.parent.parent))
+    import torch
+
+    from deltakv.deltas.descriptor import lora_layer
+    from deltakv.deltas.factors import LowRankFactors
+    from deltakv.deltas.lora import lora_delta
+    from deltakv.metrics import next_token_kl
+    from deltakv.model import ToyConfig, ToyTransformer
+    from deltakv.patches.compose import apply_layer_patches
+    from deltakv.patches.exact import zeroth_order_patches
+    from deltakv.types import WeightVersion
+    from tests import _smol_model as SM
+
+    torch.set_num_threads(8)
+    torch.set_grad_enabled(False)
+    cfg = ToyConfig(vocab_size=SM.VOCAB, d_model=SM.D, n_layers=SM.N_LAYERS, n_heads=SM.N_HEADS, n_kv_heads=SM.N_KV,
+                    d_ff=SM.D_FF, max_seq=SM.SEQ, rms_eps=SM.EPS, rope_base=SM.ROPE_BASE)
+    model = ToyTransformer(cfg)
+    w = SM.weights()
+    _state_from_oracle(model, w)
+    tokens = torch.from_numpy(SM.tokens())
+    _, kv_base, hidden = model.prefill(tokens)
+    dd = SM.dense_delta(w)
+    d_kv = SM.N_KV * SM.HD
+    eye = torch.eye(d_kv)
+    layers = {i: lora_layer(i, k=LowRankFactors(A=torch.from_numpy(p["k_proj"]), B=eye, scale=1.0, name="k_proj"),
+                            v=LowRankFactors(A=torch.from_numpy(p["v_proj"]), B=eye, scale=1.0, name="v_proj"))
+              for i, p in dd.items()}
+    delta = lora_delta(source=WeightVersion(id="base"), target=WeightVersion(id="rl", parent_id="base", kind="rl_step"),
+                       layers=layers)
+    xn = model.rmsnorm_tensors(hidden)
+    patches = zeroth_order_patches(xn, delta, n_kv_heads=cfg.n_kv_heads, head_dim=cfg.head_dim, rope=model.rope)
+    patched = apply_layer_patches(kv_base, patches)
+    stale_logits = model.logits_from_kv(tokens, kv_base)
+    model.apply_delta(delta, version=WeightVersion(id="rl"))
+    fresh_logits, _, _ = model.prefill(tokens)
+    patched_logits = model.logits_from_kv(tokens, patched)
+    np.savez_compressed(OUT / "smol_dense.npz", tokens=tokens.numpy(), fresh_logits=fresh_logits[-1].numpy(),
+                        patched_logits=patched_logits.numpy(), stale_logits=stale_logits.numpy(),
+                        kl_ref=np.float64(next_token_kl(fresh_logits[-1], patched_logits)),
+                        kl_stale=np.float64(next_token_kl(fresh_logits[-1], stale_logits)))
+
+
+CASES = {"core": core_cases, "engine": engine_case, "smol_kl": smol_kl_case, "smol_dense": smol_dense_case}
 
 
 def main(ref_src: str, cases=None) -> None:
@@ -764,5 +815,5 @@ def main(ref_src: str, cases=None) -> None:
 
 if __name__ == "__main__":
     if len(sys.argv) < 2:
-        sys.exit("usage: make_golden.py <reference checkout>/src [core|engine|smol_kl ...]")
+        sys.exit("usage: make_golden.py <reference checkout>/src [core|engine|smol_kl|smol_dense ...]")
     main(sys.argv[1], sys.argv[2:] or None)

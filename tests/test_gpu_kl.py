@@ -1,4 +1,5 @@
-"""Next-token KL of the patched cache beyond the 4-layer toy: the SmolLM2-135M shape.
+"""Next-token KL of the patched cache beyond the 4-layer toy: the SmolLM2-135M shape, for the
+exact route (below), the int4 subspace route and the dense-dW route (their own docstrings).
 
 Weights, tokens and the rank-8 q/k/v/o LoRA come from seeds (tests/_smol_model.py: d=576,
 9 / 3 heads of 64, SwiGLU 1536, vocab 49152, 2048 tokens; 4 of the 30 layers so the fp32
@@ -135,3 +136,52 @@ def test_smollm2_shape_int4_subspace_route_kl(cuda):
     assert abs(kl_ours - kl_ref) < 1e-4
     assert OM.next_token_kl(lr, lo) < 1e-6
     assert kl_ours < kl_stale  # the correction moved the int4 cache toward fresh
+
+
+def test_smollm2_shape_dense_route_kl(cuda):
+    """The RL-step route on the same stack (reduced depth; the Llama-3-70B stack itself has no
+    fp32 oracle that fits): a full-rank dW on k/v of every layer (relative norm 0.02, bf16
+    values), stored layer inputs in bf16 with the RMSNorm weight folded into the packed dW and
+    the per-row 1/rms computed from them, one tensor-core GEMM launch into bf16 pages.  Against
+    the reference's exact route with A=dW, B=I (tests/golden/smol_dense.npz): KL(fresh ||
+    patched) within 1e-4 nats of the reference's, KL(patched_reference || patched) below 1e-6
+    (bf16 storage of X and of the pages alone costs 3.5e-8)."""
+    g = golden("smol_dense")
+    w = SM.weights()
+    dd = SM.dense_delta(w)
+    w1 = SM.merged_dense(w, dd)
+    toks = g["tokens"]
+    tabs = OX.rope_tables(SM.HD, SM.SEQ, SM.ROPE_BASE)
+    kw = dict(n_layers=SM.N_LAYERS, n_heads=SM.N_HEADS, n_kv=SM.N_KV, hd=SM.HD, eps=SM.EPS, rope=tabs)
+    _, k0, v0, h = OM.prefill(w, toks, **kw)
+    L_, n = SM.N_LAYERS, SM.SEQ
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    x = t(h).to(torch.bfloat16)
+    bs = 16
+    nblk = n // bs
+    perm = np.random.default_rng(11).permutation(nblk + 2)[:nblk].astype(np.int32)
+    pages = []
+    for src in (k0, v0):
+        p = torch.randn(L_, nblk + 2, bs, SM.N_KV, SM.HD, generator=torch.Generator().manual_seed(6))
+        p[:, torch.from_numpy(perm).long()] = torch.from_numpy(src).view(L_, nblk, bs, SM.N_KV, SM.HD)
+        pages.append(p.to(torch.bfloat16).to(cuda))
+    patcher = dkv.DensePatcher(SM.D, SM.N_KV, SM.HD, rope=(torch.from_numpy(tabs[0]), torch.from_numpy(tabs[1])),
+                               norm_eps=SM.EPS)
+    packed = patcher.pack(t(np.stack([dd[l]["k_proj"] for l in range(L_)])),
+                          t(np.stack([dd[l]["v_proj"] for l in range(L_)])),
+                          norm_weight=t(np.stack([w[f"blocks_{l}_attn_norm_weight"] for l in range(L_)])))
+    seqs = ops.SeqBatchTensors(cu_seqlens=torch.tensor([0, n], dtype=torch.int32, device=cuda),
+                               block_tables=t(perm[None]), max_seq_len=n)
+    patcher.apply(x, packed, [pages[0][l] for l in range(L_)], [pages[1][l] for l in range(L_)], seqs,
+                  x_scale=patcher.norm_scale(x), check=True)
+    torch.cuda.synchronize()
+    got = []
+    for p in pages:
+        f = (bits_from_bf16(p).astype(np.uint32) << 16).view(np.float32).reshape(p.shape)
+        got.append(f[:, perm].reshape(L_, n, SM.N_KV, SM.HD))
+    logits = OM.logits_from_kv(w1, toks, got[0], got[1], **kw)
+    kl = OM.next_token_kl(g["fresh_logits"], logits)
+    assert abs(kl - float(g["kl_ref"])) < 1e-4, (kl, float(g["kl_ref"]))
+    assert OM.next_token_kl(g["patched_logits"], logits) < 1e-6
+    stale = OM.next_token_kl(g["patched_logits"], g["stale_logits"])
+    assert stale > 10 * OM.next_token_kl(g["patched_logits"], logits)

@@ -334,3 +334,26 @@ def test_smol_prefill_and_kl_golden():
     vb = bf16_bits_to_f32(f32_to_bf16_bits(vp)).reshape(vp.shape)
     lb = OM.logits_from_kv(w1, g["tokens"], kb, vb, **kw)
     assert OM.next_token_kl(g["patched_logits"], lb) < 2e-7
+
+
+def test_smol_dense_route_golden():
+    """The oracle's dense route (exact_kv_delta with A=dW, B=I) on the SmolLM2-shaped stack
+    against the reference's run (tests/golden/smol_dense.npz)."""
+    from oracle import dense as OD
+    from oracle import model as OM
+    from tests import _smol_model as SM
+
+    g = golden("smol_dense")
+    w = SM.weights()
+    dd = SM.dense_delta(w)
+    tabs = OX.rope_tables(SM.HD, SM.SEQ, SM.ROPE_BASE)
+    kw = dict(n_layers=SM.N_LAYERS, n_heads=SM.N_HEADS, n_kv=SM.N_KV, hd=SM.HD, eps=SM.EPS, rope=tabs)
+    _, k, v, h = OM.prefill(w, g["tokens"], **kw)
+    for l in range(SM.N_LAYERS):
+        xn = OX.rmsnorm(h[l], w[f"blocks_{l}_attn_norm_weight"], SM.EPS)
+        dk, dv = OX.exact_kv_delta(xn, *OD.dense_factors(dd[l]["k_proj"], dd[l]["v_proj"]), SM.N_KV, SM.HD, tabs)
+        k[l] += dk
+        v[l] += dv
+    logits = OM.logits_from_kv(SM.merged_dense(w, dd), g["tokens"], k, v, **kw)
+    assert OM.next_token_kl(g["patched_logits"], logits) < 1e-8
+    assert abs(OM.next_token_kl(g["fresh_logits"], logits) - float(g["kl_ref"])) < 1e-6

@@ -14,7 +14,9 @@ spot check and clocks:
 * ``multi-lora-kivi`` subspace route on a KIVI int4 shared prefix (Llama-3-8B shape,
                       32768 tokens, 8 adapter views of ranks {8,8,16,16,32,32,64,64});
 * ``rl-dense``        dense-dW route of an RL step (Llama-3-70B shape: 80 layers, d=8192,
-                      16 x 8192 tokens, full-rank dW_K / dW_V), a tcgen05 GEMM.
+                      16 x 8192 tokens, full-rank dW_K / dW_V), a tcgen05 GEMM;
+* ``analytic``        the analytic route's engine loop (SmolLM2-135M shape, 30 layers, 4 x 2048
+                      tokens, rank-8 q/k/v/o LoRA, propagator rank 64).
 
     python bench.py [--gpus N --steps K --warmup W]      # this implementation
     python bench.py --impl reference ...                   # the CPU reference arm
@@ -1484,7 +1486,7 @@ def run_analytic(args, dist: Dist) -> dict:
     bf16_peak = peaks().get("bf16_tflops") or 1590.0
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
-        cpu = analytic_cpu_sample(args.cpu_seconds)
+        cpu = analytic_cpu_sample(args.sub_cpu_seconds)
     e2e = None
     if not args.no_e2e:
         h_host = [(h.cpu().pin_memory(), hm.cpu().pin_memory()) for h, hm in hidden]
@@ -1595,7 +1597,7 @@ def run_reference(args) -> dict:
     return run_analytic_reference(args)
 
 
-SUB_WORKLOADS = ("smollm2-exact", "multi-lora-kivi", "rl-dense")
+SUB_WORKLOADS = ("smollm2-exact", "multi-lora-kivi", "rl-dense", "analytic")
 
 
 def main(argv=None):
@@ -1617,8 +1619,14 @@ def main(argv=None):
                 workloads[w] = run_one(with_defaults(sub_args, w), dist)
             except Exception as e:  # recorded, not hidden: the line says which workload failed and why
                 workloads[w] = {"error": f"{type(e).__name__}: {e}", "trace": traceback.format_exc()[-2000:]}
-                torch.cuda.synchronize()
-            torch.cuda.empty_cache()
+                try:
+                    torch.cuda.synchronize()
+                except Exception:
+                    pass
+            try:
+                torch.cuda.empty_cache()
+            except Exception:
+                pass
         line["workloads"] = workloads
     if dist.rank == 0:
         print(json.dumps(line), flush=True)

@@ -43,38 +43,71 @@ __device__ __forceinline__ uint32_t quant_one_fast(float x, float s, float z, fl
 // a 4-bit code as a float (exact): 2^23 + q built in the mantissa, minus 2^23
 __device__ __forceinline__ float code_to_f(uint32_t q) { return __int_as_float(0x4B000000u | q) - 8388608.f; }
 
-// codes 2p, 2p+1 of a packed word as an fp32 pair (exact)
-__device__ __forceinline__ uint64_t codes_to_f2(uint32_t w, int p) {
-  const uint32_t lo = 0x4B000000u | ((w >> (8 * p)) & 0xFu), hi = 0x4B000000u | ((w >> (8 * p + 4)) & 0xFu);
-  return sub2(f2pack(__uint_as_float(lo), __uint_as_float(hi)), f2pack(8388608.f, 8388608.f));
+// ---- packed forms for the fused route (one word = 8 codes, element j in bits 4j..4j+3) ----
+//
+// Decode without per-code shifts: nibble j of w (j < 4) or of w >> 16 (j >= 4) is masked in
+// place and ORed under the exponent of 2^23, giving the float 2^23 + n_j 16^e (e = j mod 4,
+// n_j 16^e < 2^16, so the float is exact); subtracting 2^23 is exact.  The factor 16^e is
+// folded into the scale, s 16^-e (an exact power-of-two rescaling of an fp16 value), so
+// fma(n_j 16^e, s 16^-e, z) = RN(n_j s + z): n_j s is exact in fp32 (4 x 11 significant bits),
+// which makes this single rounding the reference's q * s + z.
+// Pairs p = 0..3 hold elements (2p, 2p + 1), rescaled by 16^-e = (1, 1/16) for even p and
+// (1/256, 1/4096) for odd p (pair_rescale).
+__device__ __forceinline__ void code_pairs(uint32_t w, uint64_t (&raw)[4]) {
+  const uint32_t h = w >> 16, m = 0x4B000000u;
+  const uint64_t bias = f2pack(8388608.f, 8388608.f);
+  raw[0] = sub2(f2pack(__uint_as_float((w & 0xFu) | m), __uint_as_float((w & 0xF0u) | m)), bias);
+  raw[1] = sub2(f2pack(__uint_as_float((w & 0xF00u) | m), __uint_as_float((w & 0xF000u) | m)), bias);
+  raw[2] = sub2(f2pack(__uint_as_float((h & 0xFu) | m), __uint_as_float((h & 0xF0u) | m)), bias);
+  raw[3] = sub2(f2pack(__uint_as_float((h & 0xF00u) | m), __uint_as_float((h & 0xF000u) | m)), bias);
+}
+__device__ __forceinline__ uint64_t pair_rescale(int p) {
+  return (p & 1) ? f2pack(0.00390625f, 0.000244140625f) : f2pack(1.f, 0.0625f);
 }
 
-// The reciprocal form alone: rint(y) clamped to [0, 15] for y = (x - z) * RN(1/s) (y = 0 when
-// s = 0).  Equal to the division form except where y lies within ~2 ulp of a rounding tie
-// (a few in a million codes); for outputs that are not held to bit equality with the
-// division form.
-__device__ __forceinline__ uint32_t quant_recip(float y) {
-  const uint32_t q = __float2uint_rn(y);
-  return q < 15u ? q : 15u;
+// round to nearest even (ties to even, as rintf) as a signed integer
+__device__ __forceinline__ int rni(float y) {
+  int r;
+  asm("cvt.rni.s32.f32 %0, %1;" : "=r"(r) : "f"(y));
+  return r;
 }
-
-// quant_one's codes for a pair, through the reciprocal: y = (x - z) * RN(1/s) lies within 2 ulp
-// (< 4e-6 for |y| < 16) of the IEEE quotient, so rint(y) equals rint(quotient) unless y is
-// that close to a rounding tie; where either value of the pair is within 1e-5 of a tie
-// (|y - rint(y)| > 1/2 - 1e-5) both quotients are formed exactly.  a2 = the (x - z) pair,
-// s = the group's fp16 scale as a float, inv = RN(1/s) (0 when s = 0: every code is 0).
-__device__ __forceinline__ void quant_pair(uint64_t a2, float s, float inv, uint32_t &q0, uint32_t &q1) {
-  float y0, y1;
-  f2unpack(mul2(a2, f2pack(inv, inv)), y0, y1);
-  const float d0 = fabsf(__fsub_rn(y0, rintf(y0))), d1 = fabsf(__fsub_rn(y1, rintf(y1)));
-  if (__builtin_expect(fmaxf(d0, d1) > 0.49999f, 0)) {
-    float a0, a1;
-    f2unpack(a2, a0, a1);
-    y0 = exact_quotient(a0, s);
-    y1 = exact_quotient(a1, s);
+// (c << 8) | (clamp(a, 0, 15) << 4) | clamp(b, 0, 15): two codes saturated to [0, 15] and
+// shifted in below c (PTX cvt.pack.sat.u4.s32.b32)
+__device__ __forceinline__ uint32_t pack_u4(int a, int b, uint32_t c) {
+  uint32_t d;
+  asm("cvt.pack.sat.u4.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// the word of 8 codes clamp(rint((x_j - z_j) * inv_j), 0, 15) for the value pairs v[p] =
+// (x_2p, x_2p+1) with the pairs' (z, inv) in z2[p], i2[p]
+__device__ __forceinline__ uint32_t quant_word(const uint64_t (&v)[4], const uint64_t (&z2)[4],
+                                               const uint64_t (&i2)[4]) {
+  uint32_t w = 0u;
+#pragma unroll
+  for (int p = 3; p >= 0; --p) {
+    float y0, y1;
+    f2unpack(mul2(sub2(v[p], z2[p]), i2[p]), y0, y1);
+    w = pack_u4(rni(y1), rni(y0), w);
   }
-  q0 = quant_recip(y0);
-  q1 = quant_recip(y1);
+  return w;
+}
+
+// three-input minimum / maximum (sm_100)
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fmin8(const float (&x)[8]) {
+  return fminf(fmin3(fmin3(x[0], x[1], x[2]), fmin3(x[3], x[4], x[5]), x[6]), x[7]);
+}
+__device__ __forceinline__ float fmax8(const float (&x)[8]) {
+  return fmaxf(fmax3(fmax3(x[0], x[1], x[2]), fmax3(x[3], x[4], x[5]), x[6]), x[7]);
 }
 
 __device__ __forceinline__ void quant_group(const float (&x)[kG], int cnt, uint8_t (&q)[kG], __half &s16,

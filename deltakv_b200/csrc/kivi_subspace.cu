@@ -13,16 +13,23 @@
 //   flags   probe flags, deduplicated probe list and count
 //   pack    basis -> split bf16 terms in pass1's MMA fragment order, and an fp32 row copy
 //   pass1   per warp of 32 tokens: dequant, R, ||R||, rhs = R B (mma.sync on split bf16
-//           terms, fp32 accumulate), per-tile column sums — no block barrier
+//           terms, fp32 accumulate), per-tile column sums
 //   psum    sums over the probes of R and of rhs
 //   solve   one CTA per problem: G^-1 = (B^T B + 1e-6 I)^-1 in fp64, orth_mu, subspace,
 //           mean ||R||
 //   fitb    B G^-1 (= B G^-T, G symmetric) -> split bf16 terms in pass2's MMA fragment
 //           order, so that fitted = codes B^T = rhs (B G^-1)^T needs no per-token solve
 //   pass2   per warp of 32 tokens: fitted = rhs (B G^-1)^T (mma.sync on split bf16 terms),
-//           corr, requantise —
-//           V groups reduced across the 4 lanes of a row, K groups
-//           across the 8 row-lanes of the warp (a warp tile is exactly one K group)
+//           corr, requantise — group extrema gathered through the warp's scratch: V groups
+//           from the 4 lanes of a row, K groups from the 8 row-lanes of the warp (a warp
+//           tile is exactly one K group)
+// Both passes walk the channels in blocks of 32.  Per block, each warp stages its codes (one
+// 16-B row per lane), the K group's scale / zero and its fresh rows (pass1) with cp.async two
+// blocks ahead; the basis fragments, the same for the CTA's four warps, arrive once per CTA
+// by bulk copy (cp.async.bulk, an mbarrier per slot) into a ring of kBSlots blocks that
+// every warp releases after reading.  Codes are decoded without per-code shifts and
+// dequantised with one fma (kivi::code_pairs), and requantised words are packed with
+// cvt.pack.sat (kivi::quant_word).
 // Lane (g, q) of a warp owns rows g + 8i (i = 0..3) and, in every block of 32 channels, the
 // 8 contiguous channels 8q..8q+7: pass1 forms its R directly as MMA A fragments by
 // permuting k inside the block (both operands use the same permutation, which leaves R B
@@ -36,9 +43,9 @@
 // ~1e-5 of the fitted part, ~1e-6 of an int4 step here, and the requantised codes and fp16
 // scale / zero agree with an fp32 evaluation except where a value lies that close to a
 // rounding tie.  For the same reason pass2 quantises with the group's reciprocal alone
-// (kivi::quant_recip): it departs from the IEEE quotient only within 4e-6 of a tie, inside the
-// window the upstream differences already leave, and the exact-quotient fix-up near ties
-// (kivi::quant_pair) cost 8 % of the route's time for no measurable change in its output.
+// (kivi::quant_word): it departs from the IEEE quotient only within 4e-6 of a tie, inside the
+// window the upstream differences already leave, and an exact-quotient fix-up near ties cost
+// 8 % of the route's time for no measurable change in its output.
 #include <algorithm>
 #include <cstring>
 #include <vector>
@@ -74,7 +81,7 @@ struct Prob {
   float *rhs, *dist, *part, *sums, *ginv, *mu, *subv;
   uint32_t *flag;
   int32_t *uprobe, *ucount;
-  __nv_bfloat16 *b1, *b1l, *b2, *b2l;  // MMA B operands: high and low bf16 terms
+  __nv_bfloat16 *b1, *b1l, *b2;  // MMA B operands: high and low bf16 terms
   float *bb;                           // the basis as [d][RP] fp32 rows (zero past the rank)
   const float *basis;
   int64_t tile0;
@@ -154,8 +161,9 @@ __device__ __forceinline__ float basis_at(const Prob &P, int64_t c, int k) {
 
 // b1 / b1l (pass1 B operand, high / low bf16 terms): [block][n-tile][lane][8]:
 //     B[32 block + 8q + j][8 nt + g]
-// b2 / b2l (pass2 B operand, written by fitb): [block][k-step][n-tile][lane][4]:
-//     (B G^-1)[ch][16 ks + 2q + {0, 1, 8, 9}], ch = 32 block + 8 (g >> 1) + 2 nt + (g & 1)
+// b2 (pass2 B operand, written by fitb): [block][k-step][n-tile][lane][high 4, low 4]:
+//     (B G^-1)[ch][16 ks + 2q + {0, 1, 8, 9}], ch = 32 block + 8 (g >> 1) + 2 nt + (g & 1);
+//     one block's fragments are contiguous (RP / 16 x 2 KB), the unit of pass2's bulk copies
 // bb: [d][RP] fp32 rows
 __global__ void pack_kernel(const __grid_constant__ Batch b, int rp) {
   const Prob &P = b.probs[blockIdx.y];
@@ -186,34 +194,54 @@ __global__ void pack_kernel(const __grid_constant__ Batch b, int rp) {
 // ---------------------------------------------------------------------------------------
 // pass 1
 // ---------------------------------------------------------------------------------------
-constexpr int kP1Stages = 3;  // pass1 staging depth (blocks in flight per warp)
+constexpr int kP1Stages = 3;  // per-warp staging depth (blocks in flight)
+constexpr int kBSlots = 4;    // CTA-wide ring of basis fragment blocks (both passes)
 
-// one block's operands for one warp in pass1: fresh (16 or 32 B per lane and row), codes
-// (4 B per lane and row) and, for K, the group's scale / zero (16 B each per lane)
-template <int FDT, int MODE>
+// Bounded wait on a phase without the abort word (draining copies already issued).
+__device__ __forceinline__ void mbar_wait_drain(uint64_t *bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity) && clock64() - t0 < kWaitLimitCycles) {
+  }
+}
+
+// r = hi + lo: hi = RN_bf16(r), lo = RN_bf16(r - hi) for a pair, as packed bf16 words
+__device__ __forceinline__ void split2(uint64_t r2, uint32_t &hi, uint32_t &lo) {
+  float x, y;
+  f2unpack(r2, x, y);
+  hi = pack_bf16x2(x, y);
+  f2unpack(sub2(r2, f2pack(bf16lo(hi), bf16hi(hi))), x, y);
+  lo = pack_bf16x2(x, y);
+}
+
+// one block's per-warp operands: fresh (16 or 32 B per lane and row, copied by that lane),
+// the codes (row r's 16 B, copied by lane r) and, for K, the group's scale / zero (16 B per
+// 8 channels, copied by lanes 0-7)
+template <int FDT>
 struct P1Stage {
   static constexpr int kFB = FDT == DKV_F32 ? 2 : 1;
   uint4 fr[4][kFB][32];
-  uint32_t cd[4][32];
-  uint4 sz[2][32];
+  uint32_t cd[kWT][4];
+  uint4 sz[2][4];
 };
-template <int FDT>
-struct P1Stage<FDT, DKV_KIVI_PER_TOKEN> {  // V: the rows' scale / zero are read directly
-  static constexpr int kFB = FDT == DKV_F32 ? 2 : 1;
-  uint4 fr[4][kFB][32];
-  uint32_t cd[4][32];
+// V: the rows' scale / zero, 4 blocks (8 B per row) per buffer, two buffers
+struct P1VStage {
+  uint2 s[2][kWT], z[2][kWT];
 };
 
-template <int FDT, int MODE>
+template <int RP>
+constexpr int p1_bq_bytes() {  // one block's basis fragments: high terms, then low terms
+  return (RP / 8) * 32 * 16 * 2;
+}
+template <int RP, int FDT, int MODE>
 constexpr int p1_smem_bytes() {
-  return static_cast<int>(sizeof(P1Stage<FDT, MODE>)) * kP1Stages * kWarps;
+  return kBSlots * p1_bq_bytes<RP>() + kWarps * kP1Stages * static_cast<int>(sizeof(P1Stage<FDT>)) +
+         (MODE == DKV_KIVI_PER_TOKEN ? kWarps * static_cast<int>(sizeof(P1VStage)) : 0) + 2 * kBSlots * 8 + 16;
 }
 
 // CTAs per SM that pass1 is compiled for (its register budget; measured per rank tile)
 template <int RP, int MODE>
 constexpr int p1_min_blocks() {
-  constexpr bool k = MODE == DKV_KIVI_PER_CHANNEL;
-  return RP == 16 ? (k ? 4 : 5) : RP == 32 ? 4 : 3;
+  return RP == 16 ? 5 : RP == 32 ? 4 : 3;
 }
 
 template <int RP, int FDT, int MODE>
@@ -221,11 +249,57 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
     pass1_kernel(const __grid_constant__ Batch b, int64_t tile_lo) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   const Prob &P = b.probs[find_prob(b, tile_lo + blockIdx.x)];
-  const int64_t t0 = (tile_lo + blockIdx.x - P.tile0) * kTM + warp * kWT;
+  const int64_t tile_t0 = (tile_lo + blockIdx.x - P.tile0) * kTM;
+  const int64_t t0 = tile_t0 + warp * kWT;
   const int64_t n = P.n;
-  if (t0 >= n) return;
   constexpr int NT = RP / 8;
   constexpr bool kmode = MODE == DKV_KIVI_PER_CHANNEL;
+  constexpr int BQ = p1_bq_bytes<RP>();
+  const int n_blocks = static_cast<int>(b.d / kCB);
+  // shared: [fragment ring][per-warp stage rings][V rows][barriers, abort]
+  using Stage = P1Stage<FDT>;
+  extern __shared__ __align__(16) unsigned char p1_smem[];
+  unsigned char *const bq_ring = p1_smem;
+  unsigned char *sp = p1_smem + kBSlots * BQ;
+  Stage *const ring = reinterpret_cast<Stage *>(sp) + warp * kP1Stages;
+  sp += kWarps * kP1Stages * sizeof(Stage);
+  P1VStage *const vst = reinterpret_cast<P1VStage *>(sp) + warp;
+  if constexpr (!kmode) sp += kWarps * sizeof(P1VStage);
+  uint64_t *const bq_full = reinterpret_cast<uint64_t *>(sp);
+  uint64_t *const bq_empty = bq_full + kBSlots;
+  volatile int *const abort_flag = reinterpret_cast<volatile int *>(bq_empty + kBSlots);
+
+  // the warps with tokens (every tile has at least one token, so warp 0 is one of them)
+  const int active = static_cast<int>((n - tile_t0 + kWT - 1) / kWT < kWarps ? (n - tile_t0 + kWT - 1) / kWT : kWarps);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBSlots; ++s) {
+      mbar_init(&bq_full[s], 1);
+      mbar_init(&bq_empty[s], active);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (t0 >= n) return;
+
+  // basis fragments: two bulk copies per block (high, low terms) by lane 0 of warp 0 into the
+  // CTA-wide ring; every warp with tokens releases a slot after reading it
+  const bool producer = warp == 0 && lane == 0;
+  int bq_issued = 0;
+  auto bq_issue = [&]() -> bool {
+    const int blk = bq_issued, s = blk % kBSlots;
+    if (blk >= kBSlots && !mbar_wait_bounded(&bq_empty[s], ((blk / kBSlots) - 1) & 1, abort_flag)) return false;
+    mbar_arrive_expect_tx(&bq_full[s], BQ);
+    const int64_t off = static_cast<int64_t>(blk) * (BQ / 2);
+    bulk_load(bq_ring + s * BQ, reinterpret_cast<const unsigned char *>(P.b1) + off, BQ / 2, &bq_full[s]);
+    bulk_load(bq_ring + s * BQ + BQ / 2, reinterpret_cast<const unsigned char *>(P.b1l) + off, BQ / 2, &bq_full[s]);
+    ++bq_issued;
+    return true;
+  };
+  bool ok = true;
+  if (producer)
+    while (bq_issued < kBSlots - 1 && bq_issued < n_blocks) bq_issue();
+
   float acc[2][NT][4];
 #pragma unroll
   for (int m = 0; m < 2; ++m)
@@ -239,18 +313,16 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
     row[i] = t0 + g + 8 * i;
     rv[i] = row[i] < n;
   }
-  const uint4 *b1 = reinterpret_cast<const uint4 *>(P.b1) + lane;
-  const uint4 *b1l = reinterpret_cast<const uint4 *>(P.b1l) + lane;
-  const int n_blocks = static_cast<int>(b.d / kCB);
   const int64_t krow = t0 / kivi::kG;
-  // per-warp staging ring: each lane copies (cp.async) and later reads back only its own
-  // bytes — fresh, codes and the K group's scale/zero of the block kP1Stages - 1 ahead — so
-  // no barrier is needed and the loads stay in flight across blocks without registers
-  using Stage = P1Stage<FDT, MODE>;
-  extern __shared__ __align__(16) unsigned char p1_smem[];
-  Stage *ring = reinterpret_cast<Stage *>(p1_smem) + warp * kP1Stages;
+  const int64_t my_row = t0 + lane;
+  const bool my_valid = my_row < n;
+  const uint8_t *const my_codes = P.codes + (my_valid ? my_row : t0) * P.crs;
+  // V: the rows' scale / zero staged 4 blocks at a time where the rows allow 8-B copies,
+  // otherwise read directly
+  const bool vstage = !kmode && n_blocks % 4 == 0 && P.szrs % 4 == 0;
   constexpr int kFB = Stage::kFB;
   constexpr int kEs = FDT == DKV_F32 ? 4 : 2;
+  // per-warp staging ring (cp.async, kP1Stages - 1 blocks ahead)
   auto issue = [&](int cb) {
     if (cb < n_blocks) {
       Stage &S = ring[cb % kP1Stages];
@@ -261,48 +333,57 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
         const unsigned char *fp = static_cast<const unsigned char *>(P.fresh) + (rr * P.frs + c) * kEs;
 #pragma unroll
         for (int f = 0; f < kFB; ++f) cp_async16(&S.fr[i][f][lane], fp + 16 * f, rv[i] ? 16u : 0u);
-        cp_async4(&S.cd[i][lane], P.codes + rr * P.crs + c / 2, rv[i] ? 4u : 0u);
       }
+      cp_async16(&S.cd[lane][0], my_codes + static_cast<int64_t>(cb) * (kCB / 2), my_valid ? 16u : 0u);
       if constexpr (kmode) {
-        cp_async16(&S.sz[0][lane], P.scale + krow * P.szrs + c, 16u);
-        cp_async16(&S.sz[1][lane], P.zero + krow * P.szrs + c, 16u);
+        if (lane < 8)
+          cp_async16(&S.sz[lane >> 2][lane & 3],
+                     (lane < 4 ? P.scale : P.zero) + krow * P.szrs + static_cast<int64_t>(cb) * kCB + 8 * (lane & 3),
+                     16u);
+      } else {
+        if (vstage && cb % 4 == 0) {
+          const int buf = (cb >> 2) & 1;
+          const int64_t off = (my_valid ? my_row : t0) * P.szrs + cb;
+          cp_async8(&vst->s[buf][lane], P.scale + off, my_valid ? 8u : 0u);
+          cp_async8(&vst->z[buf][lane], P.zero + off, my_valid ? 8u : 0u);
+        }
       }
     }
     cp_async_commit();  // possibly empty: keeps the group count per block fixed
   };
 #pragma unroll
   for (int s0 = 0; s0 < kP1Stages - 1; ++s0) issue(s0);
-  // V: the rows' scale / zero — loaded one block ahead into registers for the wider rank
-  // tiles (latency-bound), at the point of use for RP 16 (occupancy-bound); measured choice
-  constexpr bool kVPre = !kmode && RP >= 32;
-  uint32_t vsz[4], vsz_next[4];
-  auto load_vsz = [&](int cb, uint32_t (&o)[4]) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      o[i] = (cb < n_blocks && rv[i]) ? (static_cast<uint32_t>(__half_as_ushort(P.scale[row[i] * P.szrs + cb])) |
-                                         (static_cast<uint32_t>(__half_as_ushort(P.zero[row[i] * P.szrs + cb])) << 16))
-                                      : 0u;
-  };
-  if constexpr (kVPre) load_vsz(0, vsz);
-  for (int cb = 0; cb < n_blocks; ++cb) {
+
+  const uint64_t rs_lo = kivi::pair_rescale(0), rs_hi = kivi::pair_rescale(1);
+  int cb = 0;
+  for (; cb < n_blocks; ++cb) {
+    __syncwarp();  // every lane is done with the slot the next copy overwrites
+    if (warp == 0) {  // the producer's outcome, for the whole warp (exits stay warp-uniform)
+      int pok = 1;
+      if (producer && bq_issued < n_blocks) pok = bq_issue() ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, pok, 0)) {
+        ok = false;
+        break;
+      }
+    }
     issue(cb + kP1Stages - 1);
-    if constexpr (kVPre) load_vsz(cb + 1, vsz_next);
     cp_async_wait<kP1Stages - 1>();
+    __syncwarp();  // the other lanes' copies of this block are visible
     const Stage &S = ring[cb % kP1Stages];
-    float ks8[8], kz8[8];
+    uint64_t ks2[4], kz2[4];  // K: this lane's channels' rescaled scale and zero, in pairs
     if constexpr (kmode) {
-      const uint4 sv = S.sz[0][lane], zv = S.sz[1][lane];
+      const uint4 sv = S.sz[0][q], zv = S.sz[1][q];
       const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, zw[4] = {zv.x, zv.y, zv.z, zv.w};
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
-        ks8[2 * p] = f16lo(sw[p]), ks8[2 * p + 1] = f16hi(sw[p]);
-        kz8[2 * p] = f16lo(zw[p]), kz8[2 * p + 1] = f16hi(zw[p]);
+        ks2[p] = mul2(f2pack(f16lo(sw[p]), f16hi(sw[p])), (p & 1) ? rs_hi : rs_lo);
+        kz2[p] = f2pack(f16lo(zw[p]), f16hi(zw[p]));
       }
     }
     uint32_t a[2][2][4], al[2][2][4];  // [m-tile][k-step][reg]: R's high and low bf16 terms
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      float r[8];
+      uint64_t r2[4] = {0, 0, 0, 0};
       if (rv[i]) {
         float f[8];
         if (FDT == DKV_F32) {
@@ -319,42 +400,49 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
             f[2 * j + 1] = FDT == DKV_BF16 ? bf16hi(w4[j]) : f16hi(w4[j]);
           }
         }
-        const uint32_t w = S.cd[i][lane];
-        float vs = 0.f, vz = 0.f;
-        if constexpr (kVPre) {
-          vs = f16lo(vsz[i]);
-          vz = f16hi(vsz[i]);
-        } else if constexpr (!kmode) {  // small scattered reads: cheaper direct than as 4-byte async copies
-          vs = __half2float(P.scale[row[i] * P.szrs + cb]);
-          vz = __half2float(P.zero[row[i] * P.szrs + cb]);
+        uint64_t raw[4];
+        kivi::code_pairs(S.cd[g + 8 * i][q], raw);
+        uint64_t vs_lo = 0, vs_hi = 0, vz2 = 0;
+        if constexpr (!kmode) {
+          float vs, vz;
+          if (vstage) {
+            const int buf = (cb >> 2) & 1;
+            vs = __half2float(reinterpret_cast<const __half *>(&vst->s[buf][g + 8 * i])[cb & 3]);
+            vz = __half2float(reinterpret_cast<const __half *>(&vst->z[buf][g + 8 * i])[cb & 3]);
+          } else {
+            vs = __half2float(P.scale[row[i] * P.szrs + cb]);
+            vz = __half2float(P.zero[row[i] * P.szrs + cb]);
+          }
+          vs_lo = mul2(f2pack(vs, vs), rs_lo);
+          vs_hi = mul2(f2pack(vs, vs), rs_hi);
+          vz2 = f2pack(vz, vz);
         }
         uint64_t dd2 = 0;
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-          const uint64_t s2 = kmode ? f2pack(ks8[2 * p], ks8[2 * p + 1]) : f2pack(vs, vs);
-          const uint64_t z2 = kmode ? f2pack(kz8[2 * p], kz8[2 * p + 1]) : f2pack(vz, vz);
-          const uint64_t reused2 = add2(mul2(kivi::codes_to_f2(w, p), s2), z2);
-          const uint64_t r2 = sub2(f2pack(f[2 * p], f[2 * p + 1]), reused2);
-          dd2 = fma2(r2, r2, dd2);
-          f2unpack(r2, r[2 * p], r[2 * p + 1]);
+          const uint64_t reused2 = fma2(raw[p], kmode ? ks2[p] : ((p & 1) ? vs_hi : vs_lo), kmode ? kz2[p] : vz2);
+          r2[p] = sub2(f2pack(f[2 * p], f[2 * p + 1]), reused2);
+          dd2 = fma2(r2[p], r2[p], dd2);
         }
         float e0, e1;
         f2unpack(dd2, e0, e1);
         d2[i] += e0 + e1;
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) r[j] = 0.f;
       }
       const int m = i >> 1, h = i & 1;
-      split_bf16x2(r[0], r[1], a[m][0][h], al[m][0][h]);
-      split_bf16x2(r[2], r[3], a[m][0][2 + h], al[m][0][2 + h]);
-      split_bf16x2(r[4], r[5], a[m][1][h], al[m][1][h]);
-      split_bf16x2(r[6], r[7], a[m][1][2 + h], al[m][1][2 + h]);
+      split2(r2[0], a[m][0][h], al[m][0][h]);
+      split2(r2[1], a[m][0][2 + h], al[m][0][2 + h]);
+      split2(r2[2], a[m][1][h], al[m][1][h]);
+      split2(r2[3], a[m][1][2 + h], al[m][1][2 + h]);
     }
+    const int slot = cb % kBSlots;
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bq_full[slot], (cb / kBSlots) & 1, abort_flag))) {
+      ok = false;
+      break;
+    }
+    const uint4 *const bq = reinterpret_cast<const uint4 *>(bq_ring + slot * BQ) + lane;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      const int64_t fo = (static_cast<int64_t>(cb) * NT + nt) * 32;
-      const uint4 bv = b1[fo], bl = b1l[fo];
+      const uint4 bv = bq[nt * 32], bl = bq[(NT + nt) * 32];
 #pragma unroll
       for (int m = 0; m < 2; ++m) {  // R B ~ Rh Bh + Rh Bl + Rl Bh, small terms first
         mma16816_bf16(acc[m][nt], al[m][0][0], al[m][0][1], al[m][0][2], al[m][0][3], bv.x, bv.y);
@@ -365,12 +453,18 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
         mma16816_bf16(acc[m][nt], a[m][1][0], a[m][1][1], a[m][1][2], a[m][1][3], bv.z, bv.w);
       }
     }
-    if constexpr (kVPre) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i) vsz[i] = vsz_next[i];
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bq_empty[slot]);
   }
   cp_async_wait<0>();
+  if (!ok) {
+    record_error(b.status, DKV_ERR_TIMEOUT);
+    *abort_flag = 1;
+  }
+  // copies this CTA issued and warp 0 has not waited for complete before the CTA exits
+  if (producer)
+    for (int blk = cb; blk < bq_issued; ++blk) mbar_wait_drain(&bq_full[blk % kBSlots], (blk / kBSlots) & 1);
+  if (!ok) return;
 
   // ||R|| per row (4 lanes per row) and the tile's sum
   float dsum = 0.f;
@@ -657,8 +751,8 @@ __global__ void __launch_bounds__(256) solve_kernel(const __grid_constant__ Batc
 }
 
 // ---------------------------------------------------------------------------------------
-// fitb: pass2's B operand, B G^-1 as high / low bf16 terms in the b2 fragment order; one CTA
-// per 32-channel block
+// fitb: pass2's B operand, B G^-1 as high / low bf16 terms in the b2 fragment order (per
+// fragment 16 B: the 4 high terms, then the 4 low terms); one CTA per 32-channel block
 // ---------------------------------------------------------------------------------------
 template <int RP>
 __global__ void __launch_bounds__(256) fitb_kernel(const __grid_constant__ Batch b) {
@@ -680,46 +774,52 @@ __global__ void __launch_bounds__(256) fitb_kernel(const __grid_constant__ Batch
 #pragma unroll 8
     for (int j = 0; j < RP; ++j) acc = fmaf(Gf[k][j], Bs[cl][j], acc);
     const __nv_bfloat16 hi = __float2bfloat16_rn(acc);
-    P.b2[blk * (KS * 512) + f] = hi;
-    P.b2l[blk * (KS * 512) + f] = __float2bfloat16_rn(__fsub_rn(acc, __bfloat162float(hi)));
+    __nv_bfloat16 *o = P.b2 + blk * (KS * 1024) + (f >> 2) * 8 + x;
+    o[0] = hi;
+    o[4] = __float2bfloat16_rn(__fsub_rn(acc, __bfloat162float(hi)));
   }
 }
 
 // ---------------------------------------------------------------------------------------
 // pass 2
 // ---------------------------------------------------------------------------------------
-constexpr int kP2Stages = 3;  // pass2 staging depth (blocks in flight per warp)
+constexpr int kP2Stages = 3;  // per-warp staging depth of codes and K scale / zero (blocks)
 
-// pass2's basis fragments (high and low terms) are staged with the other operands while they
-// are small (RP <= 32)
-template <int RP>
-constexpr int p2_bq() {
-  return RP / 16 <= 2 ? (RP / 16) * 8 : 1;
-}
-// one block's operands for one warp in pass2: codes (4 B per lane and row), the K group's
-// scale / zero (16 B each per lane), the lane's basis fragments (8 B each, high then low)
-template <int RP, bool K>
+// one block's per-warp operands: the codes (row r's 16 B, copied by lane r) and, for K, the
+// group's scale / zero (16 B per 8 channels, copied by lanes 0-7)
 struct P2Stage {
-  uint32_t cd[4][32];
-  uint4 sz[2][32];
-  uint2 bq[p2_bq<RP>()][32];
+  uint32_t cd[kWT][4];
+  uint4 sz[2][4];
 };
-template <int RP>
-struct P2Stage<RP, false> {  // V: the rows' scale / zero are read directly
-  uint32_t cd[4][32];
-  uint2 bq[p2_bq<RP>()][32];
+// per-warp scratch: group extrema partials, then the groups' (zero, 1 / scale)
+constexpr int kRedK = 136;  // K: floats per q-row, [g][j] (lo, hi) pairs + 8 floats of pad
+constexpr int kRedV = 40;   // V: floats per g-row, [q][i] (lo, hi) pairs + 8 floats of pad
+struct P2Scratch {
+  float red[4 * kRedK];
+  float pz[32], pinv[32];
+};
+// V: the rows' scale / zero, 8 blocks (16 B per row) per buffer, two buffers
+struct P2VStage {
+  uint4 s[2][kWT], z[2][kWT];
 };
 
+template <int RP>
+constexpr int p2_bq_bytes() {  // one block's (B G^-1) fragments, high and low terms
+  return (RP / 16) * 4 * 32 * 16;
+}
+// shared memory besides orth_mu [d]: fragment ring, per-warp rings and scratch, V rows,
+// barriers and the abort word
 template <int RP, int MODE>
-constexpr int p2_ring_bytes() {
-  return static_cast<int>(sizeof(P2Stage<RP, MODE == DKV_KIVI_PER_CHANNEL>)) * kP2Stages * kWarps;
+constexpr int p2_smem_fixed() {
+  return kBSlots * p2_bq_bytes<RP>() +
+         kWarps * (kP2Stages * static_cast<int>(sizeof(P2Stage)) + static_cast<int>(sizeof(P2Scratch))) +
+         (MODE == DKV_KIVI_PER_TOKEN ? kWarps * static_cast<int>(sizeof(P2VStage)) : 0) + 2 * kBSlots * 8 + 16;
 }
 
 // CTAs per SM that pass2 is compiled for (its register budget; measured per rank tile)
 template <int RP, int MODE>
 constexpr int p2_min_blocks() {
-  constexpr bool k = MODE == DKV_KIVI_PER_CHANNEL;
-  return RP == 16 ? (k ? 4 : 5) : RP == 32 ? (k ? 3 : 4) : 3;
+  return RP == 16 ? 5 : RP == 32 ? 4 : 3;
 }
 
 template <int RP, int FDT, int MODE>
@@ -727,20 +827,60 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
     pass2_kernel(const __grid_constant__ Batch b, int64_t tile_lo) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
   const Prob &P = b.probs[find_prob(b, tile_lo + blockIdx.x)];
-  const int64_t t0 = (tile_lo + blockIdx.x - P.tile0) * kTM + warp * kWT;
+  const int64_t tile_t0 = (tile_lo + blockIdx.x - P.tile0) * kTM;
+  const int64_t t0 = tile_t0 + warp * kWT;
   const int64_t n = P.n;
   constexpr int KS = RP / 16;
   constexpr bool kmode = MODE == DKV_KIVI_PER_CHANNEL;
-  constexpr bool kStageB = KS <= 2;
-  // shared: orth_mu [d] for the whole CTA, then each warp's staging ring
+  constexpr int BQ = p2_bq_bytes<RP>();
+  const int n_blocks = static_cast<int>(b.d / kCB);
+  // shared: [fragment ring][per-warp stage rings][per-warp scratch][V rows][barriers, abort][orth_mu]
   extern __shared__ __align__(16) unsigned char p2_smem[];
-  float *mu_s = reinterpret_cast<float *>(p2_smem);
+  unsigned char *const bq_ring = p2_smem;
+  unsigned char *sp = p2_smem + kBSlots * BQ;
+  P2Stage *const ring = reinterpret_cast<P2Stage *>(sp) + warp * kP2Stages;
+  sp += kWarps * kP2Stages * sizeof(P2Stage);
+  P2Scratch &X = reinterpret_cast<P2Scratch *>(sp)[warp];
+  sp += kWarps * sizeof(P2Scratch);
+  P2VStage *const vst = reinterpret_cast<P2VStage *>(sp) + warp;
+  if constexpr (!kmode) sp += kWarps * sizeof(P2VStage);
+  uint64_t *const bq_full = reinterpret_cast<uint64_t *>(sp);
+  uint64_t *const bq_empty = bq_full + kBSlots;
+  volatile int *const abort_flag = reinterpret_cast<volatile int *>(bq_empty + kBSlots);
+  float *const mu_s = reinterpret_cast<float *>(sp + 2 * kBSlots * 8 + 16);
+
+  // the warps with tokens (every tile has at least one token, so warp 0 is one of them)
+  const int active = static_cast<int>((n - tile_t0 + kWT - 1) / kWT < kWarps ? (n - tile_t0 + kWT - 1) / kWT : kWarps);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBSlots; ++s) {
+      mbar_init(&bq_full[s], 1);
+      mbar_init(&bq_empty[s], active);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
   for (int64_t e = threadIdx.x; e < b.d / 4; e += kThreads)
     reinterpret_cast<float4 *>(mu_s)[e] = reinterpret_cast<const float4 *>(P.mu)[e];
   __syncthreads();
   if (t0 >= n) return;
-  using Stage = P2Stage<RP, kmode>;
-  Stage *ring = reinterpret_cast<Stage *>(p2_smem + b.d * 4) + warp * kP2Stages;
+
+  // (B G^-1) fragments: one bulk copy per block by lane 0 of warp 0 into the CTA-wide ring;
+  // every warp with tokens releases a slot after reading it
+  const bool producer = warp == 0 && lane == 0;
+  const unsigned char *const bq_src = reinterpret_cast<const unsigned char *>(P.b2);
+  int bq_issued = 0;
+  auto bq_issue = [&]() -> bool {
+    const int blk = bq_issued, s = blk % kBSlots;
+    if (blk >= kBSlots && !mbar_wait_bounded(&bq_empty[s], ((blk / kBSlots) - 1) & 1, abort_flag)) return false;
+    mbar_arrive_expect_tx(&bq_full[s], BQ);
+    bulk_load(bq_ring + s * BQ, bq_src + static_cast<int64_t>(blk) * BQ, BQ, &bq_full[s]);
+    ++bq_issued;
+    return true;
+  };
+  bool ok = true;
+  if (producer)
+    while (bq_issued < kBSlots - 1 && bq_issued < n_blocks) bq_issue();
+
   const float mean_dist = P.subv[b.d];
   int64_t row[4];
   bool rv[4], fl[4];
@@ -752,6 +892,7 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
     fl[i] = rv[i] && P.flag[row[i]] != 0u;
     w[i] = rv[i] ? fminf(P.dist[row[i]] / mean_dist, 1.f) : 0.f;
   }
+  const bool full = t0 + kWT <= n;
   // A fragments: the row's rhs at this lane's positions k = 16 ks + 2q + {0, 1, 8, 9}, as
   // high and low bf16 terms
   uint32_t a[2][KS][4], al[2][KS][4];
@@ -771,85 +912,99 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
     }
   }
 
-  const uint2 *b2 = reinterpret_cast<const uint2 *>(P.b2) + lane;
-  const uint2 *b2l = reinterpret_cast<const uint2 *>(P.b2l) + lane;
-  const int n_blocks = static_cast<int>(b.d / kCB);
   const int64_t krow = t0 / kivi::kG;
-  // per-warp staging ring (cp.async, kP2Stages - 1 blocks ahead): each lane copies and later
-  // reads back only its own bytes, so no barrier is needed
+  const int64_t my_row = t0 + lane;
+  const bool my_valid = my_row < n;
+  const uint8_t *const my_codes = P.codes + (my_valid ? my_row : t0) * P.crs;
+  // V: the rows' scale / zero staged 8 blocks at a time where the rows allow 16-B copies,
+  // otherwise read directly
+  const bool vstage = !kmode && n_blocks % 8 == 0 && P.szrs % 8 == 0;
+  // per-warp staging ring (cp.async, kP2Stages - 1 blocks ahead)
   auto issue = [&](int cb) {
     if (cb < n_blocks) {
-      Stage &S = ring[cb % kP2Stages];
-      const int64_t c = static_cast<int64_t>(cb) * kCB + 8 * q;
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        cp_async4(&S.cd[i][lane], P.codes + (rv[i] ? row[i] : t0) * P.crs + c / 2, rv[i] ? 4u : 0u);
+      P2Stage &S = ring[cb % kP2Stages];
+      cp_async16(&S.cd[lane][0], my_codes + static_cast<int64_t>(cb) * (kCB / 2), my_valid ? 16u : 0u);
       if constexpr (kmode) {
-        cp_async16(&S.sz[0][lane], P.scale + krow * P.szrs + c, 16u);
-        cp_async16(&S.sz[1][lane], P.zero + krow * P.szrs + c, 16u);
-      }
-      if constexpr (kStageB) {
-#pragma unroll
-        for (int f = 0; f < KS * 4; ++f) {
-          const int64_t fo = (static_cast<int64_t>(cb) * KS * 4 + f) * 32;
-          cp_async8(&S.bq[2 * f][lane], b2 + fo, 8u);
-          cp_async8(&S.bq[2 * f + 1][lane], b2l + fo, 8u);
+        if (lane < 8)
+          cp_async16(&S.sz[lane >> 2][lane & 3],
+                     (lane < 4 ? P.scale : P.zero) + krow * P.szrs + static_cast<int64_t>(cb) * kCB + 8 * (lane & 3),
+                     16u);
+      } else {
+        if (vstage && cb % 8 == 0) {
+          const int buf = (cb >> 3) & 1;
+          const int64_t off = (my_valid ? my_row : t0) * P.szrs + cb;
+          cp_async16(&vst->s[buf][lane], P.scale + off, my_valid ? 16u : 0u);
+          cp_async16(&vst->z[buf][lane], P.zero + off, my_valid ? 16u : 0u);
         }
       }
     }
-    cp_async_commit();
+    cp_async_commit();  // possibly empty: keeps the group count per block fixed
   };
 #pragma unroll
   for (int s0 = 0; s0 < kP2Stages - 1; ++s0) issue(s0);
-  for (int cb = 0; cb < n_blocks; ++cb) {
+
+  const uint64_t rs_lo = kivi::pair_rescale(0), rs_hi = kivi::pair_rescale(1);
+  int cb = 0;
+  for (; cb < n_blocks; ++cb) {
+    __syncwarp();  // every lane is done with the slot the next copy overwrites
+    if (warp == 0) {  // the producer's outcome, for the whole warp (exits stay warp-uniform)
+      int pok = 1;
+      if (producer && bq_issued < n_blocks) pok = bq_issue() ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, pok, 0)) {
+        ok = false;
+        break;
+      }
+    }
     issue(cb + kP2Stages - 1);
     cp_async_wait<kP2Stages - 1>();
-    const Stage &S = ring[cb % kP2Stages];
+    __syncwarp();  // the other lanes' copies of this block are visible
+    const int slot = cb % kBSlots;
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bq_full[slot], (cb / kBSlots) & 1, abort_flag))) {
+      ok = false;
+      break;
+    }
+    const P2Stage &S = ring[cb % kP2Stages];
+    const uint4 *const bq = reinterpret_cast<const uint4 *>(bq_ring + slot * BQ) + lane;
     const int64_t c = static_cast<int64_t>(cb) * kCB + 8 * q;
     float acc[2][4][4];
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
 #pragma unroll
       for (int nt = 0; nt < 4; ++nt) {
-        uint2 bv, bw;  // high and low terms of (B G^-1)
-        if constexpr (kStageB) {
-          bv = S.bq[kStageB ? 2 * (ks * 4 + nt) : 0][lane];
-          bw = S.bq[kStageB ? 2 * (ks * 4 + nt) + 1 : 0][lane];
-        } else {
-          const int64_t fo = ((static_cast<int64_t>(cb) * KS + ks) * 4 + nt) * 32;
-          bv = b2[fo];
-          bw = b2l[fo];
-        }
+        const uint4 f = bq[(ks * 4 + nt) * 32];  // high terms (x, y), low terms (z, w)
 #pragma unroll
         for (int m = 0; m < 2; ++m) {  // rhs (B G^-1)^T ~ ah bh + ah bl + al bh, small terms first
           if (ks == 0)
-            mma16816_bf16_zc(acc[m][nt], al[m][ks][0], al[m][ks][1], al[m][ks][2], al[m][ks][3], bv.x, bv.y);
+            mma16816_bf16_zc(acc[m][nt], al[m][ks][0], al[m][ks][1], al[m][ks][2], al[m][ks][3], f.x, f.y);
           else
-            mma16816_bf16(acc[m][nt], al[m][ks][0], al[m][ks][1], al[m][ks][2], al[m][ks][3], bv.x, bv.y);
-          mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], bw.x, bw.y);
-          mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], bv.x, bv.y);
+            mma16816_bf16(acc[m][nt], al[m][ks][0], al[m][ks][1], al[m][ks][2], al[m][ks][3], f.x, f.y);
+          mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], f.z, f.w);
+          mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], f.x, f.y);
         }
       }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bq_empty[slot]);
+
     uint64_t mu2[4];
     {
       const float4 *mp = reinterpret_cast<const float4 *>(mu_s + c);
       const float4 x = mp[0], y = mp[1];
       mu2[0] = f2pack(x.x, x.y), mu2[1] = f2pack(x.z, x.w), mu2[2] = f2pack(y.x, y.y), mu2[3] = f2pack(y.z, y.w);
     }
-    uint64_t ks2[4], kz2[4];  // K: scale / zero of channels (2p, 2p+1)
+    uint64_t ks2[4], kz2[4];  // K: this lane's channels' rescaled scale and zero, in pairs
     if constexpr (kmode) {
-      const uint4 sv = S.sz[0][lane], zv = S.sz[1][lane];
+      const uint4 sv = S.sz[0][q], zv = S.sz[1][q];
       const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, zw[4] = {zv.x, zv.y, zv.z, zv.w};
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
-        ks2[p] = f2pack(f16lo(sw[p]), f16hi(sw[p]));
+        ks2[p] = mul2(f2pack(f16lo(sw[p]), f16hi(sw[p])), (p & 1) ? rs_hi : rs_lo);
         kz2[p] = f2pack(f16lo(zw[p]), f16hi(zw[p]));
       }
     }
-    // corrected values: rows g + 8i, channels 8q + j; (reused + fitted) + w orth_mu in packed
-    // fp32 pairs, each operation rounded as the scalar form
-    float v[4][8];
+    // corrected values of rows g + 8i, channels 8q + 2p + {0, 1}: (reused + fitted) + w orth_mu,
+    // each operation rounded as the reference's fp32 form
+    uint64_t v2[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int m = i >> 1, h = i & 1;
@@ -857,159 +1012,151 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
         float f[8];
         load8<FDT>(P.fresh, row[i] * P.frs + c, f);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] = f[j];
-      } else if (rv[i]) {
-        const uint32_t wq = S.cd[i][lane];
-        uint64_t vs2 = 0, vz2 = 0;
-        if constexpr (!kmode) {  // small scattered reads: cheaper direct than as 4-byte async copies
-          const float vs = __half2float(P.scale[row[i] * P.szrs + cb]);
-          const float vz = __half2float(P.zero[row[i] * P.szrs + cb]);
-          vs2 = f2pack(vs, vs);
+        for (int p = 0; p < 4; ++p) v2[i][p] = f2pack(f[2 * p], f[2 * p + 1]);
+      } else {
+        uint64_t raw[4];
+        kivi::code_pairs(S.cd[g + 8 * i][q], raw);
+        uint64_t vs_lo = 0, vs_hi = 0, vz2 = 0;
+        if constexpr (!kmode) {
+          float vs = 0.f, vz = 0.f;
+          if (vstage) {
+            const int buf = (cb >> 3) & 1;
+            vs = __half2float(reinterpret_cast<const __half *>(&vst->s[buf][g + 8 * i])[cb & 7]);
+            vz = __half2float(reinterpret_cast<const __half *>(&vst->z[buf][g + 8 * i])[cb & 7]);
+          } else if (rv[i]) {
+            vs = __half2float(P.scale[row[i] * P.szrs + cb]);
+            vz = __half2float(P.zero[row[i] * P.szrs + cb]);
+          }
+          vs_lo = mul2(f2pack(vs, vs), rs_lo);
+          vs_hi = mul2(f2pack(vs, vs), rs_hi);
           vz2 = f2pack(vz, vz);
         }
         const uint64_t w2 = f2pack(w[i], w[i]);
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-          const uint64_t r2 = add2(mul2(kivi::codes_to_f2(wq, p), kmode ? ks2[p] : vs2), kmode ? kz2[p] : vz2);
-          const uint64_t c2 = add2(add2(r2, f2pack(acc[m][p][2 * h], acc[m][p][2 * h + 1])), mul2(w2, mu2[p]));
-          f2unpack(c2, v[i][2 * p], v[i][2 * p + 1]);
+          const uint64_t r2 = fma2(raw[p], kmode ? ks2[p] : ((p & 1) ? vs_hi : vs_lo), kmode ? kz2[p] : vz2);
+          v2[i][p] = add2(add2(r2, f2pack(acc[m][p][2 * h], acc[m][p][2 * h + 1])), mul2(w2, mu2[p]));
         }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
       }
     }
-    // requantise.  Group extrema are reduce-scattered over the lanes that share a group, so
-    // each lane derives one group's scale / zero / reciprocal and broadcasts it back.
-    if (!kmode) {
-      // V: group = (row g + 8i, 32 channels) spread over the 4 lanes q; lane q owns row i = q
+    // requantise: group extrema partials go through the warp's scratch to the lane that owns
+    // the group, which forms its fp16 scale / zero and publishes (zero, 1 / scale)
+    if constexpr (!kmode) {
+      // V: group = (row g + 8i, the block's 32 channels) over the lanes q; lane q owns row i = q
       float lo[4], hi[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        lo[i] = hi[i] = v[i][0];
+        float x[8];
 #pragma unroll
-        for (int j = 1; j < 8; ++j) {
-          lo[i] = fminf(lo[i], v[i][j]);
-          hi[i] = fmaxf(hi[i], v[i][j]);
-        }
+        for (int p = 0; p < 4; ++p) f2unpack(v2[i][p], x[2 * p], x[2 * p + 1]);
+        lo[i] = kivi::fmin8(x);
+        hi[i] = kivi::fmax8(x);
       }
-      {
-        const bool up = (q & 2) != 0;
-#pragma unroll
-        for (int ii = 0; ii < 2; ++ii) {
-          const float rl = __shfl_xor_sync(0xffffffffu, up ? lo[ii] : lo[ii + 2], 2);
-          const float rh = __shfl_xor_sync(0xffffffffu, up ? hi[ii] : hi[ii + 2], 2);
-          lo[ii] = fminf(up ? lo[ii + 2] : lo[ii], rl);
-          hi[ii] = fmaxf(up ? hi[ii + 2] : hi[ii], rh);
-        }
-      }
-      {
-        const bool up = (q & 1) != 0;
-        const float rl = __shfl_xor_sync(0xffffffffu, up ? lo[0] : lo[1], 1);
-        const float rh = __shfl_xor_sync(0xffffffffu, up ? hi[0] : hi[1], 1);
-        lo[0] = fminf(up ? lo[1] : lo[0], rl);
-        hi[0] = fmaxf(up ? hi[1] : hi[0], rh);
-      }
+      float *const wr = X.red + g * kRedV + q * 8;
+      *reinterpret_cast<float4 *>(wr) = make_float4(lo[0], hi[0], lo[1], hi[1]);
+      *reinterpret_cast<float4 *>(wr + 4) = make_float4(lo[2], hi[2], lo[3], hi[3]);
+      __syncwarp();
+      const float2 *const rd = reinterpret_cast<const float2 *>(X.red + g * kRedV) + q;
+      const float2 e0 = rd[0], e1 = rd[4], e2 = rd[8], e3 = rd[12];
+      const float glo = fminf(kivi::fmin3(e0.x, e1.x, e2.x), e3.x);
+      const float ghi = fmaxf(kivi::fmax3(e0.y, e1.y, e2.y), e3.y);
       __half s16, z16;
-      kivi::group_params(lo[0], hi[0], s16, z16);
+      kivi::group_params(glo, ghi, s16, z16);
       const float s_own = __half2float(s16);
-      const float inv_own = s_own > 0.f ? __frcp_rn(s_own) : 0.f;
-      const uint32_t sz_own = static_cast<uint32_t>(__half_as_ushort(s16)) |
-                              (static_cast<uint32_t>(__half_as_ushort(z16)) << 16);
-      {
-        const int64_t orow = t0 + g + 8 * q;
-        if (orow < n) {
-          P.o_scale[orow * P.o_szrs + cb] = s16;
-          P.o_zero[orow * P.o_szrs + cb] = z16;
-        }
+      const int64_t orow = t0 + g + 8 * q;
+      if (orow < n) {
+        P.o_scale[orow * P.o_szrs + cb] = s16;
+        P.o_zero[orow * P.o_szrs + cb] = z16;
       }
+      X.pz[4 * g + q] = __half2float(z16);
+      X.pinv[4 * g + q] = s_own > 0.f ? __frcp_rn(s_own) : 0.f;
+      __syncwarp();
+      const float4 zz = *reinterpret_cast<const float4 *>(&X.pz[4 * g]);
+      const float4 ii = *reinterpret_cast<const float4 *>(&X.pinv[4 * g]);
+      const float zr[4] = {zz.x, zz.y, zz.z, zz.w}, ir[4] = {ii.x, ii.y, ii.z, ii.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const uint32_t sz = __shfl_sync(0xffffffffu, sz_own, 4 * g + i);
-        const float inv = __shfl_sync(0xffffffffu, inv_own, 4 * g + i);
-        const float z = __half2float(__ushort_as_half(static_cast<unsigned short>(sz >> 16)));
-        const uint64_t z2 = f2pack(z, z), inv2 = f2pack(inv, inv);
-        uint32_t wq = 0u;
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          float y0, y1;
-          f2unpack(mul2(sub2(f2pack(v[i][2 * p], v[i][2 * p + 1]), z2), inv2), y0, y1);
-          wq |= kivi::quant_recip(y0) << (8 * p);
-          wq |= kivi::quant_recip(y1) << (8 * p + 4);
-        }
-        if (rv[i]) *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = wq;
+        const uint64_t z2 = f2pack(zr[i], zr[i]), i2 = f2pack(ir[i], ir[i]);
+        const uint64_t zp[4] = {z2, z2, z2, z2}, ip[4] = {i2, i2, i2, i2};
+        const uint32_t word = kivi::quant_word(v2[i], zp, ip);
+        if (rv[i]) *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = word;
       }
     } else {
-      // K: group = (32 rows of the warp tile, channel 8q + j) spread over the 8 lanes g;
-      // lane g owns channel j = g
+      // K: group = (the warp tile's 32 rows, channel 8q + j) over the lanes g; lane g owns j = g
       float lo[8], hi[8];
+      if (full) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        lo[j] = INFINITY;
-        hi[j] = -INFINITY;
+        for (int p = 0; p < 4; ++p) {
+          float x0[4], x1[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) f2unpack(v2[i][p], x0[i], x1[i]);
+          lo[2 * p] = fminf(kivi::fmin3(x0[0], x0[1], x0[2]), x0[3]);
+          hi[2 * p] = fmaxf(kivi::fmax3(x0[0], x0[1], x0[2]), x0[3]);
+          lo[2 * p + 1] = fminf(kivi::fmin3(x1[0], x1[1], x1[2]), x1[3]);
+          hi[2 * p + 1] = fmaxf(kivi::fmax3(x1[0], x1[1], x1[2]), x1[3]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          lo[j] = INFINITY;
+          hi[j] = -INFINITY;
+        }
 #pragma unroll
         for (int i = 0; i < 4; ++i)
           if (rv[i]) {
-            lo[j] = fminf(lo[j], v[i][j]);
-            hi[j] = fmaxf(hi[j], v[i][j]);
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+              float x0, x1;
+              f2unpack(v2[i][p], x0, x1);
+              lo[2 * p] = fminf(lo[2 * p], x0);
+              hi[2 * p] = fmaxf(hi[2 * p], x0);
+              lo[2 * p + 1] = fminf(lo[2 * p + 1], x1);
+              hi[2 * p + 1] = fmaxf(hi[2 * p + 1], x1);
+            }
           }
       }
-      {
-        const bool up = (g & 4) != 0;
+      float *const wr = X.red + q * kRedK + g * 16;
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const float rl = __shfl_xor_sync(0xffffffffu, up ? lo[jj] : lo[jj + 4], 16);
-          const float rh = __shfl_xor_sync(0xffffffffu, up ? hi[jj] : hi[jj + 4], 16);
-          lo[jj] = fminf(up ? lo[jj + 4] : lo[jj], rl);
-          hi[jj] = fmaxf(up ? hi[jj + 4] : hi[jj], rh);
-        }
-      }
-      {
-        const bool up = (g & 2) != 0;
+      for (int jj = 0; jj < 4; ++jj)
+        *reinterpret_cast<float4 *>(wr + 4 * jj) = make_float4(lo[2 * jj], hi[2 * jj], lo[2 * jj + 1], hi[2 * jj + 1]);
+      __syncwarp();
+      const float2 *const rd = reinterpret_cast<const float2 *>(X.red + q * kRedK) + g;
+      float2 e[8];
 #pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          const float rl = __shfl_xor_sync(0xffffffffu, up ? lo[jj] : lo[jj + 2], 8);
-          const float rh = __shfl_xor_sync(0xffffffffu, up ? hi[jj] : hi[jj + 2], 8);
-          lo[jj] = fminf(up ? lo[jj + 2] : lo[jj], rl);
-          hi[jj] = fmaxf(up ? hi[jj + 2] : hi[jj], rh);
-        }
-      }
-      {
-        const bool up = (g & 1) != 0;
-        const float rl = __shfl_xor_sync(0xffffffffu, up ? lo[0] : lo[1], 4);
-        const float rh = __shfl_xor_sync(0xffffffffu, up ? hi[0] : hi[1], 4);
-        lo[0] = fminf(up ? lo[1] : lo[0], rl);
-        hi[0] = fmaxf(up ? hi[1] : hi[0], rh);
-      }
+      for (int s = 0; s < 8; ++s) e[s] = rd[8 * s];
+      const float glo =
+          fminf(kivi::fmin3(kivi::fmin3(e[0].x, e[1].x, e[2].x), kivi::fmin3(e[3].x, e[4].x, e[5].x), e[6].x), e[7].x);
+      const float ghi =
+          fmaxf(kivi::fmax3(kivi::fmax3(e[0].y, e[1].y, e[2].y), kivi::fmax3(e[3].y, e[4].y, e[5].y), e[6].y), e[7].y);
       __half s16, z16;
-      kivi::group_params(lo[0], hi[0], s16, z16);
+      kivi::group_params(glo, ghi, s16, z16);
       const float s_own = __half2float(s16);
-      const float inv_own = s_own > 0.f ? __frcp_rn(s_own) : 0.f;
-      const uint32_t sz_own = static_cast<uint32_t>(__half_as_ushort(s16)) |
-                              (static_cast<uint32_t>(__half_as_ushort(z16)) << 16);
       P.o_scale[krow * P.o_szrs + c + g] = s16;
       P.o_zero[krow * P.o_szrs + c + g] = z16;
-      uint32_t wq[4] = {0u, 0u, 0u, 0u};
+      X.pz[8 * q + g] = __half2float(z16);
+      X.pinv[8 * q + g] = s_own > 0.f ? __frcp_rn(s_own) : 0.f;
+      __syncwarp();
+      const float4 za = *reinterpret_cast<const float4 *>(&X.pz[8 * q]);
+      const float4 zb = *reinterpret_cast<const float4 *>(&X.pz[8 * q + 4]);
+      const float4 ia = *reinterpret_cast<const float4 *>(&X.pinv[8 * q]);
+      const float4 ib = *reinterpret_cast<const float4 *>(&X.pinv[8 * q + 4]);
+      const uint64_t zp[4] = {f2pack(za.x, za.y), f2pack(za.z, za.w), f2pack(zb.x, zb.y), f2pack(zb.z, zb.w)};
+      const uint64_t ip[4] = {f2pack(ia.x, ia.y), f2pack(ia.z, ia.w), f2pack(ib.x, ib.y), f2pack(ib.z, ib.w)};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint32_t sz = __shfl_sync(0xffffffffu, sz_own, 4 * j + q);
-        const float inv = __shfl_sync(0xffffffffu, inv_own, 4 * j + q);
-        const float z = __half2float(__ushort_as_half(static_cast<unsigned short>(sz >> 16)));
-        const uint64_t z2 = f2pack(z, z), inv2 = f2pack(inv, inv);
-#pragma unroll
-        for (int i = 0; i < 4; i += 2) {
-          float y0, y1;
-          f2unpack(mul2(sub2(f2pack(v[i][j], v[i + 1][j]), z2), inv2), y0, y1);
-          wq[i] |= kivi::quant_recip(y0) << (4 * j);
-          wq[i + 1] |= kivi::quant_recip(y1) << (4 * j);
-        }
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t word = kivi::quant_word(v2[i], zp, ip);
+        if (rv[i]) *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = word;
       }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (rv[i]) *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = wq[i];
     }
   }
   cp_async_wait<0>();
+  if (!ok) {
+    record_error(b.status, DKV_ERR_TIMEOUT);
+    *abort_flag = 1;
+  }
+  // copies this CTA issued and warp 0 has not waited for complete before the CTA exits
+  if (producer)
+    for (int blk = cb; blk < bq_issued; ++blk) mbar_wait_drain(&bq_full[blk % kBSlots], (blk / kBSlots) & 1);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1019,7 +1166,7 @@ inline int64_t al(int64_t x) { return (x + 255) / 256 * 256; }
 
 struct Layout {
   int64_t zero_begin, zero_end, total;
-  std::vector<int64_t> flag, ucount, sums, uprobe, rhs, dist, part, ginv, mu, subv, b1, b1l, b2, b2l, bb;
+  std::vector<int64_t> flag, ucount, sums, uprobe, rhs, dist, part, ginv, mu, subv, b1, b1l, b2, bb;
 };
 
 inline int padded_rank(const dkv_kivi_subspace_problem *p, int np) {
@@ -1065,9 +1212,7 @@ inline Layout layout(const dkv_kivi_subspace_problem *p, int np, int64_t d, int 
     L.b1l.push_back(o);
     o = al(o + rp * d * 2);
     L.b2.push_back(o);
-    o = al(o + rp * d * 2);
-    L.b2l.push_back(o);
-    o = al(o + rp * d * 2);
+    o = al(o + rp * d * 4);
     L.bb.push_back(o);
     o = al(o + rp * d * 4);
   }
@@ -1131,16 +1276,22 @@ int launch(const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStre
   }
   // the table holds the K (per-channel) problems first (tiles [0, k_tiles)), then the V ones
   if (k_tiles > 0) {
-    constexpr int sm = p1_smem_bytes<FDT, DKV_KIVI_PER_CHANNEL>();
+    constexpr int sm = p1_smem_bytes<RP, FDT, DKV_KIVI_PER_CHANNEL>();
     DKV_CUDA_CHECK(cudaFuncSetAttribute(pass1_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(pass1_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL>,
+                                        cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        cudaSharedmemCarveoutMaxShared));
     pass1_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL><<<static_cast<unsigned>(k_tiles), kThreads, sm, st>>>(b, 0);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   if (b.n_tiles > k_tiles) {
-    constexpr int sm = p1_smem_bytes<FDT, DKV_KIVI_PER_TOKEN>();
+    constexpr int sm = p1_smem_bytes<RP, FDT, DKV_KIVI_PER_TOKEN>();
     DKV_CUDA_CHECK(cudaFuncSetAttribute(pass1_kernel<RP, FDT, DKV_KIVI_PER_TOKEN>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(pass1_kernel<RP, FDT, DKV_KIVI_PER_TOKEN>,
+                                        cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        cudaSharedmemCarveoutMaxShared));
     pass1_kernel<RP, FDT, DKV_KIVI_PER_TOKEN><<<static_cast<unsigned>(b.n_tiles - k_tiles), kThreads, sm, st>>>(
         b, k_tiles);
     DKV_CUDA_CHECK(cudaGetLastError());
@@ -1158,16 +1309,22 @@ int launch(const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStre
   fitb_kernel<RP><<<dim3(static_cast<unsigned>(b.d / kCB), np), 256, 0, st>>>(b);
   DKV_CUDA_CHECK(cudaGetLastError());
   if (k_tiles > 0) {
-    const int sm = static_cast<int>(b.d * 4) + p2_ring_bytes<RP, DKV_KIVI_PER_CHANNEL>();
+    const int sm = static_cast<int>(b.d * 4) + p2_smem_fixed<RP, DKV_KIVI_PER_CHANNEL>();
     DKV_CUDA_CHECK(cudaFuncSetAttribute(pass2_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(pass2_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL>,
+                                        cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        cudaSharedmemCarveoutMaxShared));
     pass2_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL><<<static_cast<unsigned>(k_tiles), kThreads, sm, st>>>(b, 0);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   if (b.n_tiles > k_tiles) {
-    const int sm = static_cast<int>(b.d * 4) + p2_ring_bytes<RP, DKV_KIVI_PER_TOKEN>();
+    const int sm = static_cast<int>(b.d * 4) + p2_smem_fixed<RP, DKV_KIVI_PER_TOKEN>();
     DKV_CUDA_CHECK(cudaFuncSetAttribute(pass2_kernel<RP, FDT, DKV_KIVI_PER_TOKEN>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(pass2_kernel<RP, FDT, DKV_KIVI_PER_TOKEN>,
+                                        cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        cudaSharedmemCarveoutMaxShared));
     pass2_kernel<RP, FDT, DKV_KIVI_PER_TOKEN><<<static_cast<unsigned>(b.n_tiles - k_tiles), kThreads, sm, st>>>(
         b, k_tiles);
     DKV_CUDA_CHECK(cudaGetLastError());
@@ -1260,7 +1417,6 @@ extern "C" int dkv_kivi_subspace_correct(const dkv_kivi_subspace_problem *proble
     P.b1 = reinterpret_cast<__nv_bfloat16 *>(ws + L.b1[i]);
     P.b1l = reinterpret_cast<__nv_bfloat16 *>(ws + L.b1l[i]);
     P.b2 = reinterpret_cast<__nv_bfloat16 *>(ws + L.b2[i]);
-    P.b2l = reinterpret_cast<__nv_bfloat16 *>(ws + L.b2l[i]);
     P.bb = reinterpret_cast<float *>(ws + L.bb[i]);
     P.tile0 = tiles;
     tiles += (P.n + kTM - 1) / kTM;

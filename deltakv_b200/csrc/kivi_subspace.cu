@@ -22,7 +22,8 @@
 //   pass2   per warp of 32 tokens: fitted = rhs (B G^-1)^T (mma.sync on split bf16 terms),
 //           corr, requantise — group extrema gathered through the warp's scratch: V groups
 //           from the 4 lanes of a row, K groups from the 8 row-lanes of the warp (a warp
-//           tile is exactly one K group)
+//           tile is exactly one K group); V probe rows are left to vprobe
+//   vprobe  the V problems' probe rows requantised from fresh (per-token groups are a row's own)
 // Both passes walk the channels in blocks of 32.  Per block, each warp stages its codes (one
 // 16-B row per lane), the K group's scale / zero and its fresh rows (pass1) with cp.async two
 // blocks ahead; the basis fragments, the same for the CTA's four warps, arrive once per CTA
@@ -786,10 +787,14 @@ __global__ void __launch_bounds__(256) fitb_kernel(const __grid_constant__ Batch
 constexpr int kP2Stages = 3;  // per-warp staging depth of codes and K scale / zero (blocks)
 
 // one block's per-warp operands: the codes (row r's 16 B, copied by lane r) and, for K, the
-// group's scale / zero (16 B per 8 channels, copied by lanes 0-7)
+// group's scale / zero (16 B per 8 channels, copied by lanes 0-7) and the fresh values of the
+// lane's first two probe rows (16 or 32 B each)
+template <int FDT>
 struct P2Stage {
+  static constexpr int kFB = FDT == DKV_F32 ? 2 : 1;
   uint32_t cd[kWT][4];
   uint4 sz[2][4];
+  uint4 pf[2][kFB][32];
 };
 // per-warp scratch: group extrema partials, then the groups' (zero, 1 / scale)
 constexpr int kRedK = 136;  // K: floats per q-row, [g][j] (lo, hi) pairs + 8 floats of pad
@@ -809,10 +814,10 @@ constexpr int p2_bq_bytes() {  // one block's (B G^-1) fragments, high and low t
 }
 // shared memory besides orth_mu [d]: fragment ring, per-warp rings and scratch, V rows,
 // barriers and the abort word
-template <int RP, int MODE>
+template <int RP, int FDT, int MODE>
 constexpr int p2_smem_fixed() {
   return kBSlots * p2_bq_bytes<RP>() +
-         kWarps * (kP2Stages * static_cast<int>(sizeof(P2Stage)) + static_cast<int>(sizeof(P2Scratch))) +
+         kWarps * (kP2Stages * static_cast<int>(sizeof(P2Stage<FDT>)) + static_cast<int>(sizeof(P2Scratch))) +
          (MODE == DKV_KIVI_PER_TOKEN ? kWarps * static_cast<int>(sizeof(P2VStage)) : 0) + 2 * kBSlots * 8 + 16;
 }
 
@@ -838,8 +843,11 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
   extern __shared__ __align__(16) unsigned char p2_smem[];
   unsigned char *const bq_ring = p2_smem;
   unsigned char *sp = p2_smem + kBSlots * BQ;
-  P2Stage *const ring = reinterpret_cast<P2Stage *>(sp) + warp * kP2Stages;
-  sp += kWarps * kP2Stages * sizeof(P2Stage);
+  using Stage = P2Stage<FDT>;
+  constexpr int kFB = Stage::kFB;
+  constexpr int kEs = FDT == DKV_F32 ? 4 : 2;
+  Stage *const ring = reinterpret_cast<Stage *>(sp) + warp * kP2Stages;
+  sp += kWarps * kP2Stages * sizeof(Stage);
   P2Scratch &X = reinterpret_cast<P2Scratch *>(sp)[warp];
   sp += kWarps * sizeof(P2Scratch);
   P2VStage *const vst = reinterpret_cast<P2VStage *>(sp) + warp;
@@ -885,13 +893,20 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
   int64_t row[4];
   bool rv[4], fl[4];
   float w[4];
+  int pslot[4];  // K: the row's slot among the lane's prefetched probe rows (-1: read directly)
+  int n_pf = 0;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     row[i] = t0 + g + 8 * i;
     rv[i] = row[i] < n;
     fl[i] = rv[i] && P.flag[row[i]] != 0u;
     w[i] = rv[i] ? fminf(P.dist[row[i]] / mean_dist, 1.f) : 0.f;
+    pslot[i] = -1;
+    if (kmode && fl[i] && n_pf < 2) pslot[i] = n_pf++;
   }
+  // V: a probe row's groups are the fresh row's alone; vprobe_kernel writes them, and here
+  // the row is skipped (the owner lane of row g + 8q checks its own flag)
+  const bool own_probe = !kmode && t0 + g + 8 * q < n && P.flag[t0 + g + 8 * q] != 0u;
   const bool full = t0 + kWT <= n;
   // A fragments: the row's rhs at this lane's positions k = 16 ks + 2q + {0, 1, 8, 9}, as
   // high and low bf16 terms
@@ -922,13 +937,21 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
   // per-warp staging ring (cp.async, kP2Stages - 1 blocks ahead)
   auto issue = [&](int cb) {
     if (cb < n_blocks) {
-      P2Stage &S = ring[cb % kP2Stages];
+      Stage &S = ring[cb % kP2Stages];
       cp_async16(&S.cd[lane][0], my_codes + static_cast<int64_t>(cb) * (kCB / 2), my_valid ? 16u : 0u);
       if constexpr (kmode) {
         if (lane < 8)
           cp_async16(&S.sz[lane >> 2][lane & 3],
                      (lane < 4 ? P.scale : P.zero) + krow * P.szrs + static_cast<int64_t>(cb) * kCB + 8 * (lane & 3),
                      16u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (pslot[i] >= 0) {
+            const unsigned char *fp = static_cast<const unsigned char *>(P.fresh) +
+                                      (row[i] * P.frs + static_cast<int64_t>(cb) * kCB + 8 * q) * kEs;
+#pragma unroll
+            for (int f = 0; f < kFB; ++f) cp_async16(&S.pf[pslot[i]][f][lane], fp + 16 * f, 16u);
+          }
       } else {
         if (vstage && cb % 8 == 0) {
           const int buf = (cb >> 3) & 1;
@@ -963,7 +986,7 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
       ok = false;
       break;
     }
-    const P2Stage &S = ring[cb % kP2Stages];
+    const Stage &S = ring[cb % kP2Stages];
     const uint4 *const bq = reinterpret_cast<const uint4 *>(bq_ring + slot * BQ) + lane;
     const int64_t c = static_cast<int64_t>(cb) * kCB + 8 * q;
     float acc[2][4][4];
@@ -1008,9 +1031,26 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int m = i >> 1, h = i & 1;
-      if (fl[i]) {
+      if (kmode && fl[i]) {
         float f[8];
-        load8<FDT>(P.fresh, row[i] * P.frs + c, f);
+        if (pslot[i] >= 0) {
+          if (FDT == DKV_F32) {
+            const uint4 u0 = S.pf[pslot[i]][0][lane], u1 = S.pf[pslot[i]][kFB - 1][lane];
+            f[0] = __uint_as_float(u0.x), f[1] = __uint_as_float(u0.y), f[2] = __uint_as_float(u0.z);
+            f[3] = __uint_as_float(u0.w), f[4] = __uint_as_float(u1.x), f[5] = __uint_as_float(u1.y);
+            f[6] = __uint_as_float(u1.z), f[7] = __uint_as_float(u1.w);
+          } else {
+            const uint4 u = S.pf[pslot[i]][0][lane];
+            const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              f[2 * j] = FDT == DKV_BF16 ? bf16lo(w4[j]) : f16lo(w4[j]);
+              f[2 * j + 1] = FDT == DKV_BF16 ? bf16hi(w4[j]) : f16hi(w4[j]);
+            }
+          }
+        } else {
+          load8<FDT>(P.fresh, row[i] * P.frs + c, f);
+        }
 #pragma unroll
         for (int p = 0; p < 4; ++p) v2[i][p] = f2pack(f[2 * p], f[2 * p + 1]);
       } else {
@@ -1064,7 +1104,7 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
       kivi::group_params(glo, ghi, s16, z16);
       const float s_own = __half2float(s16);
       const int64_t orow = t0 + g + 8 * q;
-      if (orow < n) {
+      if (orow < n && !own_probe) {
         P.o_scale[orow * P.o_szrs + cb] = s16;
         P.o_zero[orow * P.o_szrs + cb] = z16;
       }
@@ -1079,7 +1119,7 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
         const uint64_t z2 = f2pack(zr[i], zr[i]), i2 = f2pack(ir[i], ir[i]);
         const uint64_t zp[4] = {z2, z2, z2, z2}, ip[4] = {i2, i2, i2, i2};
         const uint32_t word = kivi::quant_word(v2[i], zp, ip);
-        if (rv[i]) *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = word;
+        if (rv[i] && !fl[i]) *reinterpret_cast<uint32_t *>(P.o_codes + row[i] * P.o_crs + c / 2) = word;
       }
     } else {
       // K: group = (the warp tile's 32 rows, channel 8q + j) over the lanes g; lane g owns j = g
@@ -1157,6 +1197,54 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
   // copies this CTA issued and warp 0 has not waited for complete before the CTA exits
   if (producer)
     for (int blk = cb; blk < bq_issued; ++blk) mbar_wait_drain(&bq_full[blk % kBSlots], (blk / kBSlots) & 1);
+}
+
+// ---------------------------------------------------------------------------------------
+// vprobe: the probe rows of the V (per-token) problems.  There corr = fresh, and a per-token
+// group holds one row's channels only, so each probe row is requantised from its fresh values
+// alone (pass2 leaves these rows untouched): one warp per row, one lane per 32-channel group,
+// with the IEEE quotient (kivi::quant_one)
+// ---------------------------------------------------------------------------------------
+template <int FDT>
+__global__ void __launch_bounds__(128) vprobe_kernel(const __grid_constant__ Batch b, int first_v) {
+  const Prob &P = b.probs[first_v + blockIdx.y];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int count = *P.ucount;
+  const int n_blocks = static_cast<int>(b.d / kCB);
+  for (int k = blockIdx.x * 4 + warp; k < count; k += gridDim.x * 4) {
+    const int64_t t = P.uprobe[k];
+    for (int cb = lane; cb < n_blocks; cb += 32) {
+      float x[kCB];
+#pragma unroll
+      for (int j = 0; j < kCB; j += 8) {
+        float f[8];
+        load8<FDT>(P.fresh, t * P.frs + static_cast<int64_t>(cb) * kCB + j, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[j + e] = f[e];
+      }
+      float lo = x[0], hi = x[0];
+#pragma unroll
+      for (int j = 1; j < kCB; ++j) {
+        lo = fminf(lo, x[j]);
+        hi = fmaxf(hi, x[j]);
+      }
+      __half s16, z16;
+      kivi::group_params(lo, hi, s16, z16);
+      const float sf = __half2float(s16), zf = __half2float(z16);
+      uint32_t wd[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        uint32_t word = 0u;
+#pragma unroll
+        for (int j = 7; j >= 0; --j) word = (word << 4) | kivi::quant_one(x[8 * w + j], sf, zf);
+        wd[w] = word;
+      }
+      *reinterpret_cast<uint4 *>(P.o_codes + t * P.o_crs + static_cast<int64_t>(cb) * (kCB / 2)) =
+          make_uint4(wd[0], wd[1], wd[2], wd[3]);
+      P.o_scale[t * P.o_szrs + cb] = s16;
+      P.o_zero[t * P.o_szrs + cb] = z16;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1262,7 +1350,7 @@ int validate(const dkv_kivi_subspace_problem *p, int np, int64_t &d, int &fdt) {
 }
 
 template <int RP, int FDT>
-int launch(const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStream_t st) {
+int launch(const Batch &b, int np, int n_kprob, int64_t max_probes, int64_t k_tiles, cudaStream_t st) {
   if (max_probes > 0) {
     const int bx = static_cast<int>((max_probes + 255) / 256 < 64 ? (max_probes + 255) / 256 : 64);
     flags_kernel<<<dim3(bx, np), 256, 0, st>>>(b);
@@ -1309,7 +1397,7 @@ int launch(const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStre
   fitb_kernel<RP><<<dim3(static_cast<unsigned>(b.d / kCB), np), 256, 0, st>>>(b);
   DKV_CUDA_CHECK(cudaGetLastError());
   if (k_tiles > 0) {
-    const int sm = static_cast<int>(b.d * 4) + p2_smem_fixed<RP, DKV_KIVI_PER_CHANNEL>();
+    const int sm = static_cast<int>(b.d * 4) + p2_smem_fixed<RP, FDT, DKV_KIVI_PER_CHANNEL>();
     DKV_CUDA_CHECK(cudaFuncSetAttribute(pass2_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
     DKV_CUDA_CHECK(cudaFuncSetAttribute(pass2_kernel<RP, FDT, DKV_KIVI_PER_CHANNEL>,
@@ -1319,7 +1407,7 @@ int launch(const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStre
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   if (b.n_tiles > k_tiles) {
-    const int sm = static_cast<int>(b.d * 4) + p2_smem_fixed<RP, DKV_KIVI_PER_TOKEN>();
+    const int sm = static_cast<int>(b.d * 4) + p2_smem_fixed<RP, FDT, DKV_KIVI_PER_TOKEN>();
     DKV_CUDA_CHECK(cudaFuncSetAttribute(pass2_kernel<RP, FDT, DKV_KIVI_PER_TOKEN>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
     DKV_CUDA_CHECK(cudaFuncSetAttribute(pass2_kernel<RP, FDT, DKV_KIVI_PER_TOKEN>,
@@ -1329,16 +1417,21 @@ int launch(const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStre
         b, k_tiles);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
+  if (max_probes > 0 && np > n_kprob) {
+    const int bx = static_cast<int>((max_probes + 3) / 4 < 64 ? (max_probes + 3) / 4 : 64);
+    vprobe_kernel<FDT><<<dim3(bx, np - n_kprob), 128, 0, st>>>(b, n_kprob);
+    DKV_CUDA_CHECK(cudaGetLastError());
+  }
   return DKV_OK;
 }
 
 template <int FDT>
-int launch_rp(int rp, const Batch &b, int np, int64_t max_probes, int64_t k_tiles, cudaStream_t st) {
+int launch_rp(int rp, const Batch &b, int np, int n_kprob, int64_t max_probes, int64_t k_tiles, cudaStream_t st) {
   switch (rp) {
-    case 16: return launch<16, FDT>(b, np, max_probes, k_tiles, st);
-    case 32: return launch<32, FDT>(b, np, max_probes, k_tiles, st);
-    case 48: return launch<48, FDT>(b, np, max_probes, k_tiles, st);
-    case 64: return launch<64, FDT>(b, np, max_probes, k_tiles, st);
+    case 16: return launch<16, FDT>(b, np, n_kprob, max_probes, k_tiles, st);
+    case 32: return launch<32, FDT>(b, np, n_kprob, max_probes, k_tiles, st);
+    case 48: return launch<48, FDT>(b, np, n_kprob, max_probes, k_tiles, st);
+    case 64: return launch<64, FDT>(b, np, n_kprob, max_probes, k_tiles, st);
     default: return DKV_ERR_UNSUPPORTED;
   }
 }
@@ -1379,6 +1472,7 @@ extern "C" int dkv_kivi_subspace_correct(const dkv_kivi_subspace_problem *proble
     for (int i = 0; i < n_problems; ++i)
       if ((problems[i].base.mode == DKV_KIVI_PER_CHANNEL) == (pass == 0)) order.push_back(i);
   int64_t tiles = 0, max_probes = 0, k_tiles = 0;
+  int n_kprob = 0;
   for (int slot = 0; slot < n_problems; ++slot) {
     const int i = order[slot];
     const dkv_kivi_subspace_problem &q = problems[i];
@@ -1420,7 +1514,10 @@ extern "C" int dkv_kivi_subspace_correct(const dkv_kivi_subspace_problem *proble
     P.bb = reinterpret_cast<float *>(ws + L.bb[i]);
     P.tile0 = tiles;
     tiles += (P.n + kTM - 1) / kTM;
-    if (P.mode == DKV_KIVI_PER_CHANNEL) k_tiles = tiles;
+    if (P.mode == DKV_KIVI_PER_CHANNEL) {
+      k_tiles = tiles;
+      ++n_kprob;
+    }
     if (P.n_probes > max_probes) max_probes = P.n_probes;
   }
   if (tiles > 0x7fffffffLL) return DKV_ERR_UNSUPPORTED;
@@ -1431,9 +1528,9 @@ extern "C" int dkv_kivi_subspace_correct(const dkv_kivi_subspace_problem *proble
   b.n_tiles = tiles;
   b.status = status;
   switch (fdt) {
-    case DKV_BF16: rc = launch_rp<DKV_BF16>(rp, b, n_problems, max_probes, k_tiles, st); break;
-    case DKV_F16: rc = launch_rp<DKV_F16>(rp, b, n_problems, max_probes, k_tiles, st); break;
-    default: rc = launch_rp<DKV_F32>(rp, b, n_problems, max_probes, k_tiles, st); break;
+    case DKV_BF16: rc = launch_rp<DKV_BF16>(rp, b, n_problems, n_kprob, max_probes, k_tiles, st); break;
+    case DKV_F16: rc = launch_rp<DKV_F16>(rp, b, n_problems, n_kprob, max_probes, k_tiles, st); break;
+    default: rc = launch_rp<DKV_F32>(rp, b, n_problems, n_kprob, max_probes, k_tiles, st); break;
   }
   return rc;
 }

@@ -1240,19 +1240,28 @@ def run_kivi(args, dist: Dist) -> dict:
     ms, _, clocks = timed(dist, step, args.steps, kernel_events=False)
     # the two halves alone (after the timed region, same work, one stream): K bases, route
     split = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    per_view = [torch.cuda.Event(enable_timing=True) for _ in range(len(problems) + 1)]
     n_split = 2
-    basis_ms = route_ms = 0.0
+    basis_ms = route_ms = host_ms = 0.0
+    view_ms = [0.0] * len(problems)
     for it in range(n_split + 1):  # the first pass warms the main stream's allocator pool
         split[0].record(stream)
         kbs = [K.k_bases(pb) for pb in problems]
         split[1].record(stream)
-        for pb, kb in zip(problems, kbs):
+        per_view[0].record(stream)
+        h0 = time.perf_counter()
+        for j, (pb, kb) in enumerate(zip(problems, kbs)):
             K.subspace_correct(pb, check=False, bases=kb)
+            per_view[j + 1].record(stream)
+        h1 = time.perf_counter()
         split[2].record(stream)
         torch.cuda.synchronize()
         if it:
+            host_ms += (h1 - h0) * 1e3 / n_split
             basis_ms += split[0].elapsed_time(split[1]) / n_split
             route_ms += split[1].elapsed_time(split[2]) / n_split
+            for j in range(len(problems)):
+                view_ms[j] += per_view[j].elapsed_time(per_view[j + 1]) / n_split
     ops.status_word(dev).raise_if_set("bench timed region")
     ms_step = ms / args.steps
     achieved = units_rank * KIVI_BYTES_PER_UNIT / (route_ms / 1e3) / 1e9 if route_ms > 0 else 0.0
@@ -1277,6 +1286,8 @@ def run_kivi(args, dist: Dist) -> dict:
                    "parallelism": f"adapter shards x{dist.world} (base int4 cache broadcast once over NCCL)",
                    "l2": f"{units_rank * KIVI_BYTES_PER_UNIT / 1e9:.1f} GB per step per GPU >> 126 MB L2",
                    "k_basis_ms_per_step": basis_ms, "subspace_route_ms_per_step": route_ms,
+                   "route_ms_per_view": [round(x, 3) for x in view_ms],
+                   "route_host_enqueue_ms_per_step": host_ms,
                    "e2e_sample": None if e2e is None else e2e["sample"]},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": None, "peak_source": peak_kind,

@@ -789,12 +789,18 @@ constexpr int kP2Stages = 3;  // per-warp staging depth of codes and K scale / z
 // one block's per-warp operands: the codes (row r's 16 B, copied by lane r) and, for K, the
 // group's scale / zero (16 B per 8 channels, copied by lanes 0-7) and the fresh values of the
 // lane's first two probe rows (16 or 32 B each)
-template <int FDT>
+template <int FDT, bool K>
 struct P2Stage {
   static constexpr int kFB = FDT == DKV_F32 ? 2 : 1;
   uint32_t cd[kWT][4];
   uint4 sz[2][4];
   uint4 pf[2][kFB][32];
+};
+template <int FDT>
+struct P2Stage<FDT, false> {  // V: probe rows are not read here
+  static constexpr int kFB = FDT == DKV_F32 ? 2 : 1;
+  uint32_t cd[kWT][4];
+  uint4 sz[2][4];
 };
 // per-warp scratch: group extrema partials, then the groups' (zero, 1 / scale)
 constexpr int kRedK = 136;  // K: floats per q-row, [g][j] (lo, hi) pairs + 8 floats of pad
@@ -817,7 +823,8 @@ constexpr int p2_bq_bytes() {  // one block's (B G^-1) fragments, high and low t
 template <int RP, int FDT, int MODE>
 constexpr int p2_smem_fixed() {
   return kBSlots * p2_bq_bytes<RP>() +
-         kWarps * (kP2Stages * static_cast<int>(sizeof(P2Stage<FDT>)) + static_cast<int>(sizeof(P2Scratch))) +
+         kWarps * (kP2Stages * static_cast<int>(sizeof(P2Stage<FDT, MODE == DKV_KIVI_PER_CHANNEL>)) +
+                   static_cast<int>(sizeof(P2Scratch))) +
          (MODE == DKV_KIVI_PER_TOKEN ? kWarps * static_cast<int>(sizeof(P2VStage)) : 0) + 2 * kBSlots * 8 + 16;
 }
 
@@ -843,7 +850,7 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
   extern __shared__ __align__(16) unsigned char p2_smem[];
   unsigned char *const bq_ring = p2_smem;
   unsigned char *sp = p2_smem + kBSlots * BQ;
-  using Stage = P2Stage<FDT>;
+  using Stage = P2Stage<FDT, kmode>;
   constexpr int kFB = Stage::kFB;
   constexpr int kEs = FDT == DKV_F32 ? 4 : 2;
   Stage *const ring = reinterpret_cast<Stage *>(sp) + warp * kP2Stages;
@@ -1031,29 +1038,34 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int m = i >> 1, h = i & 1;
-      if (kmode && fl[i]) {
-        float f[8];
-        if (pslot[i] >= 0) {
-          if (FDT == DKV_F32) {
-            const uint4 u0 = S.pf[pslot[i]][0][lane], u1 = S.pf[pslot[i]][kFB - 1][lane];
-            f[0] = __uint_as_float(u0.x), f[1] = __uint_as_float(u0.y), f[2] = __uint_as_float(u0.z);
-            f[3] = __uint_as_float(u0.w), f[4] = __uint_as_float(u1.x), f[5] = __uint_as_float(u1.y);
-            f[6] = __uint_as_float(u1.z), f[7] = __uint_as_float(u1.w);
-          } else {
-            const uint4 u = S.pf[pslot[i]][0][lane];
-            const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+      bool taken = false;  // K: a probe row takes its fresh values
+      if constexpr (kmode) {
+        if (fl[i]) {
+          taken = true;
+          float f[8];
+          if (pslot[i] >= 0) {
+            if (FDT == DKV_F32) {
+              const uint4 u0 = S.pf[pslot[i]][0][lane], u1 = S.pf[pslot[i]][kFB - 1][lane];
+              f[0] = __uint_as_float(u0.x), f[1] = __uint_as_float(u0.y), f[2] = __uint_as_float(u0.z);
+              f[3] = __uint_as_float(u0.w), f[4] = __uint_as_float(u1.x), f[5] = __uint_as_float(u1.y);
+              f[6] = __uint_as_float(u1.z), f[7] = __uint_as_float(u1.w);
+            } else {
+              const uint4 u = S.pf[pslot[i]][0][lane];
+              const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              f[2 * j] = FDT == DKV_BF16 ? bf16lo(w4[j]) : f16lo(w4[j]);
-              f[2 * j + 1] = FDT == DKV_BF16 ? bf16hi(w4[j]) : f16hi(w4[j]);
+              for (int j = 0; j < 4; ++j) {
+                f[2 * j] = FDT == DKV_BF16 ? bf16lo(w4[j]) : f16lo(w4[j]);
+                f[2 * j + 1] = FDT == DKV_BF16 ? bf16hi(w4[j]) : f16hi(w4[j]);
+              }
             }
+          } else {
+            load8<FDT>(P.fresh, row[i] * P.frs + c, f);
           }
-        } else {
-          load8<FDT>(P.fresh, row[i] * P.frs + c, f);
-        }
 #pragma unroll
-        for (int p = 0; p < 4; ++p) v2[i][p] = f2pack(f[2 * p], f[2 * p + 1]);
-      } else {
+          for (int p = 0; p < 4; ++p) v2[i][p] = f2pack(f[2 * p], f[2 * p + 1]);
+        }
+      }
+      if (!taken) {
         uint64_t raw[4];
         kivi::code_pairs(S.cd[g + 8 * i][q], raw);
         uint64_t vs_lo = 0, vs_hi = 0, vz2 = 0;

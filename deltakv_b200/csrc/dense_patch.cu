@@ -434,351 +434,6 @@ __global__ void __launch_bounds__(kThreads, 1) dense_patch_kernel(const __grid_c
 }
 
 // ----------------------------------------------------------------------------
-// CTA-pair form: a 256-token x 256-column tile on two SMs (a cluster of 2).  Each CTA loads
-// its own 128 token rows of X and its own 128 of the tile's 256 W rows (plain TMA loads,
-// no multicast) into the same shared-memory offsets; the leader (cluster rank 0) issues
-// tcgen05.mma.cta_group::2 with M = 256, N = 256, which reads both CTAs' operands and
-// accumulates each CTA's 128 rows x 256 columns in that CTA's tensor memory.  Per stage a
-// CTA moves 32 KB instead of 48 KB for the same MACs as the one-CTA tile.  Barriers: the
-// leader's `full` counts both CTAs' bytes (the peer's loads complete on it); the MMAs'
-// commits arrive on `empty`, `tfull` and `done` in both CTAs (commit multicast); the peer's
-// epilogue releases an accumulator buffer on the leader's `tempty`.  Every wait is bounded.
-// ----------------------------------------------------------------------------
-constexpr int kPStages = 6;
-constexpr int kPBBytes = (kBN / 2) * kBK * 2;  // this CTA's half of the W tile
-constexpr int kPStageBytes = kABytes + kPBBytes;
-constexpr int kPBarOff = kPStages * kPStageBytes;
-constexpr int kPSmemBytes = kPBarOff + 256;
-static_assert(kPSmemBytes + 1024 <= 227 * 1024, "pair kernel shared memory");
-
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t caddr) {
-  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
-}
-// 3-D tiled TMA load into this CTA's shared memory, completing on a barrier of either CTA of
-// the pair (`bar` is a shared::cluster address)
-__device__ __forceinline__ void tma_load_3d_pair(void *dst, const CUtensorMap *map, uint32_t bar, int c0, int c1,
-                                                 int c2) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
-      : "memory");
-}
-__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                              uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}\n" ::
-          "r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0)
-      : "memory");
-}
-// arrive on `bar` in both CTAs of the pair once the MMAs issued so far have completed
-__device__ __forceinline__ void umma_commit_pair(uint64_t *bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_u32(bar)),
-      "h"(static_cast<uint16_t>(3))
-      : "memory");
-}
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {  // whole warp, both CTAs
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
-               "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// bounded wait that ignores the abort word (teardown)
-__device__ __forceinline__ bool mbar_wait_cycles(uint64_t *bar, uint32_t parity) {
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity))
-    if (clock64() - t0 > kWaitLimitCycles) return false;
-  return true;
-}
-
-// tile = (layer, sequence, 256-token chunk, 256-column block); this CTA's rows start at
-// chunk * 256 + rank * 128.  Both CTAs of a pair skip the same tiles.
-__device__ __forceinline__ bool decode_pair_tile(const Params &p, int64_t tile, uint32_t rank, Tile &t) {
-  t.n = static_cast<int>(tile % p.n_tiles_n);
-  int64_t rest = tile / p.n_tiles_n;
-  const int chunk = static_cast<int>(rest % p.max_chunks);
-  rest /= p.max_chunks;
-  t.seq = static_cast<int>(rest % p.n_seqs);
-  t.layer = static_cast<int>(rest / p.n_seqs);
-  const int s0 = __ldg(p.cu_seqlens + t.seq);
-  t.len = __ldg(p.cu_seqlens + t.seq + 1) - s0;
-  t.c0 = chunk * (2 * kBM) + static_cast<int>(rank) * kBM;
-  t.row0 = s0 + t.c0;
-  return chunk * (2 * kBM) < t.len;
-}
-
-template <int PDT>
-__global__ void __launch_bounds__(kThreads, 1) dense_pair_kernel(const __grid_constant__ Params p) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                              ~static_cast<uintptr_t>(1023));
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kPBarOff);
-  uint64_t *empty = full + kPStages;
-  uint64_t *tfull = empty + kPStages;  // [2]
-  uint64_t *tempty = tfull + 2;        // [2]: the leader's counts both CTAs' epilogue warps
-  uint64_t *done = tempty + 2;
-  uint64_t *dealloc_bar = done + 1;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(dealloc_bar + 1);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_rank();
-  const bool leader = rank == 0;
-  const int64_t pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kPStages; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 2 * kEpiWarps);
-    }
-    mbar_init(done, 1);
-    mbar_init(dealloc_bar, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc_pair(tmem_slot, kTmemCols);
-    tmem_relinquish_pair();
-  }
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();  // both CTAs' barriers exist before either CTA signals the other's
-  tc_fence_after();
-  const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
-
-  if (warp == 0) {
-    // ------------------------------ TMA producer (both CTAs) ------------------------------
-    if (lane == 0) {
-      prefetch_tensormap(&p.x_map);
-      prefetch_tensormap(&p.w_map);
-      int stage = 0;
-      uint32_t phase = 0, issued = 0, parity = 0;
-      bool ok = true;
-      for (int64_t tile = pair; tile < p.n_tiles && ok; tile += n_pairs) {
-        Tile t;
-        if (!decode_pair_tile(p, tile, rank, t)) continue;
-        const int wrow = p.col_lo + t.n * kBN + static_cast<int>(rank) * (kBN / 2);
-        for (int kc = 0; kc < p.kc; ++kc) {
-          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          uint8_t *sa = smem + stage * kPStageBytes;
-          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kPStageBytes);
-          const uint32_t bar = cluster_addr(&full[stage], 0);
-          tma_load_3d_pair(sa, &p.x_map, bar, kc * kBK, t.row0, t.layer);
-          tma_load_3d_pair(sa + kABytes, &p.w_map, bar, kc * kBK, wrow, t.layer);
-          issued |= 1u << stage;
-          parity = (parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == kPStages) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-      }
-      if (!ok) {
-        record_error(p.status, DKV_ERR_TIMEOUT);
-        *abort_flag = 1;
-      }
-      // the leader sees every copy of both CTAs land on its `full` barriers
-      if (leader)
-        for (int s = 0; s < kPStages; ++s)
-          if ((issued & (1u << s)) && !mbar_wait_cycles(&full[s], (parity >> s) & 1u))
-            record_error(p.status, DKV_ERR_TIMEOUT);
-    }
-  } else if (warp == 1) {
-    // --------------------------- MMA issuer (leader only) ---------------------------
-    if (lane == 0 && leader) {
-      constexpr uint32_t idesc = umma_idesc(1 /* bf16 */, 2 * kBM, kBN);
-      int stage = 0;
-      uint32_t phase = 0;
-      int64_t j = 0;
-      bool ok = true;
-      for (int64_t tile = pair; tile < p.n_tiles && ok; tile += n_pairs) {
-        Tile t;
-        if (!decode_pair_tile(p, tile, rank, t)) continue;
-        const int b = static_cast<int>(j & 1);
-        const int64_t use = j >> 1;
-        if (use > 0 && !mbar_wait_bounded(&tempty[b], static_cast<uint32_t>((use - 1) & 1), abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d = tmem + b * kBN;
-        for (int kc = 0; kc < p.kc; ++kc) {
-          if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * kPStageBytes);
-          const uint64_t da = umma_desc_k_sw128(sa), db = umma_desc_k_sw128(sa + kABytes);
-#pragma unroll
-          for (int k = 0; k < kBK / 16; ++k)  // +32 bytes along K = +2 in the start-address field
-            umma_f16_pair(d, da + 2 * k, db + 2 * k, idesc, (kc | k) != 0);
-          umma_commit_pair(&empty[stage]);
-          if (++stage == kPStages) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-        if (!ok) break;
-        umma_commit_pair(&tfull[b]);
-        ++j;
-      }
-      if (!ok) {
-        record_error(p.status, DKV_ERR_TIMEOUT);
-        *abort_flag = 1;
-      }
-      umma_commit_pair(done);
-    }
-  } else {
-    // ------------------------------ epilogue (both CTAs) ------------------------------
-    const int q = warp & 3;
-    const int half = (warp - 2) >> 2;
-    const int row = 32 * q + lane;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(32 * q) << 16) + half * 128;
-    int64_t j = 0;
-    for (int64_t tile = pair; tile < p.n_tiles; tile += n_pairs) {
-      Tile t;
-      if (!decode_pair_tile(p, tile, rank, t)) continue;
-      const int b = static_cast<int>(j & 1);
-      const int64_t use = j >> 1;
-      const int col0 = p.col_lo + t.n * kBN + half * 128;
-      const RowCtx rc = row_ctx<PDT>(p, t, row);
-
-      Page16 pg[8];
-      uint8_t *ptr[8];
-      bool isk[8];
-      int fi[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        isk[i] = false;
-        ptr[i] = chunk_ptr(p, rc, col0, i, isk[i], fi[i]);
-        if (ptr[i] != nullptr && p.accumulate) {
-          pg[i].a = ldg128_stream(ptr[i]);
-          pg[i].b = ldg128_stream(ptr[i] + 16);
-        } else {
-          pg[i].a = pg[i].b = make_uint4(0, 0, 0, 0);
-        }
-      }
-
-      const bool ok = mbar_wait_bounded(&tfull[b], static_cast<uint32_t>(use & 1), abort_flag);
-      if (!__all_sync(0xffffffffu, ok)) {
-        record_error(p.status, DKV_ERR_TIMEOUT);
-        *abort_flag = 1;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t base = lane_addr + b * kBN;
-      const int half_hd = p.hd >> 1;
-#pragma unroll
-      for (int pr = 0; pr < 4; ++pr) {
-        const int per_head = half_hd >> 4;
-        const int hh = pr / per_head, jb = pr - hh * per_head;
-        const uint32_t clo = base + hh * p.hd + jb * 16;
-        float lo[16], hi[16];
-        __syncwarp();
-        tmem_ld16(clo, lo);
-        tmem_ld16(clo + half_hd, hi);
-        tmem_ld_wait();
-        uint8_t *plo = ptr[2 * pr], *phi = ptr[2 * pr + 1];
-        if (plo != nullptr) {
-          const float xs = rc.xs;
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            lo[e] *= xs;
-            hi[e] *= xs;
-          }
-          if (isk[2 * pr] && p.has_rope) {
-            const int64_t tb = static_cast<int64_t>(rc.pos) * half_hd + fi[2 * pr];
-            const float4 *cs = reinterpret_cast<const float4 *>(p.rope_cos + tb);
-            const float4 *sn = reinterpret_cast<const float4 *>(p.rope_sin + tb);
-#pragma unroll
-            for (int v4 = 0; v4 < 4; ++v4) {
-              const float4 c4 = __ldg(cs + v4), s4 = __ldg(sn + v4);
-              const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                const int e = 4 * v4 + u;
-                const float a = lo[e], bb = hi[e];
-                lo[e] = fmaf(a, cc[u], -bb * ss[u]);
-                hi[e] = fmaf(bb, cc[u], a * ss[u]);
-              }
-            }
-          }
-          if (p.accumulate) {
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              lo[e] += page_get<PDT>(pg[2 * pr], e);
-              hi[e] += page_get<PDT>(pg[2 * pr + 1], e);
-            }
-          }
-          page_put<PDT>(plo, lo);
-          page_put<PDT>(phi, hi);
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (leader)
-          mbar_arrive(&tempty[b]);
-        else
-          mbar_arrive_remote(cluster_addr(&tempty[b], 0));
-      }
-      ++j;
-    }
-  }
-
-  // ------------------------------- teardown -------------------------------
-  // The peer leaves only after the leader's last MMA (which reads the peer's shared memory
-  // and writes its tensor memory) has completed; the leader only after the peer's epilogue
-  // and loads are over (the handshake below).  Both then free their tensor memory.
-  __syncthreads();
-  if (warp == 1) {
-    if (lane == 0) {
-      if (!mbar_wait_cycles(done, 0)) record_error(p.status, DKV_ERR_TIMEOUT);
-      if (leader) {
-        if (!mbar_wait_cycles(dealloc_bar, 0)) record_error(p.status, DKV_ERR_TIMEOUT);
-        mbar_arrive_remote(cluster_addr(dealloc_bar, 1));
-      } else {
-        mbar_arrive_remote(cluster_addr(dealloc_bar, 0));
-        if (!mbar_wait_cycles(dealloc_bar, 0)) record_error(p.status, DKV_ERR_TIMEOUT);
-      }
-    }
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc_pair(tmem, kTmemCols);
-  }
-}
-
-// ----------------------------------------------------------------------------
 // packing: dW_K, dW_V (any float dtype) -> bf16 [layers][2 d_kv][d_model], with the RMSNorm
 // weight folded in (dW . diag(w)) and the projection scales applied
 // ----------------------------------------------------------------------------
@@ -816,58 +471,6 @@ PFN_cuTensorMapEncodeTiled_v12000 encoder() {
 }
 
 bool aligned16(const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
-
-// Clusters of two the pair kernel can keep resident on this device (0: use the one-CTA form).
-constexpr bool kUsePair = true;
-template <int PDT>
-int pair_clusters() {
-  static int cached = -1;
-  if (cached >= 0) return cached;
-  cached = 0;
-  const int smem = 1024 + kPSmemBytes;
-  if (cudaFuncSetAttribute(dense_pair_kernel<PDT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-      cudaSuccess) {
-    cudaGetLastError();
-    return cached;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cudaLaunchAttribute at;
-  at.id = cudaLaunchAttributeClusterDimension;
-  at.val.clusterDim.x = 2;
-  at.val.clusterDim.y = 1;
-  at.val.clusterDim.z = 1;
-  cfg.attrs = &at;
-  cfg.numAttrs = 1;
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, dense_pair_kernel<PDT>, &cfg) != cudaSuccess) {
-    cudaGetLastError();
-    n = 0;
-  }
-  cached = n;
-  return cached;
-}
-
-template <int PDT>
-int launch_pair(const Params &p, int clusters, cudaStream_t st) {
-  const int64_t want = p.n_tiles < clusters ? p.n_tiles : clusters;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(2 * want));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = 1024 + kPSmemBytes;
-  cfg.stream = st;
-  cudaLaunchAttribute at;
-  at.id = cudaLaunchAttributeClusterDimension;
-  at.val.clusterDim.x = 2;
-  at.val.clusterDim.y = 1;
-  at.val.clusterDim.z = 1;
-  cfg.attrs = &at;
-  cfg.numAttrs = 1;
-  DKV_CUDA_CHECK(cudaLaunchKernelEx(&cfg, dense_pair_kernel<PDT>, p));
-  return DKV_OK;
-}
 
 bool geometry_ok(const dkv_dense_geometry &g) {
   return g.d_model > 0 && g.d_model % kBK == 0 && g.n_kv_heads > 0 &&
@@ -935,12 +538,6 @@ extern "C" int dkv_dense_patch_paged(const dkv_dense_patch_args *a, dkv_stream_t
     return DKV_ERR_ALIGNMENT;
   if (a->x_rows <= 0 || a->x_rows > 0x7fffffffLL) return DKV_ERR_INVALID_ARGUMENT;
 
-  // the CTA-pair form where the device can hold pairs of this kernel, else the one-CTA form
-  const int clusters =
-      !kUsePair ? 0 : kp.dtype == DKV_BF16 ? pair_clusters<DKV_BF16>() : pair_clusters<DKV_F16>();
-  const bool pair = clusters > 0;
-  const int chunk_rows = pair ? 2 * kBM : kBM;
-
   Params p;
   memset(&p, 0, sizeof(p));
   auto enc = encoder();
@@ -965,7 +562,7 @@ extern "C" int dkv_dense_patch_paged(const dkv_dense_patch_args *a, dkv_stream_t
                           static_cast<cuuint64_t>(a->n_layers)};
     const int64_t ls = a->n_layers > 1 ? a->packed_layer_stride : static_cast<int64_t>(2) * d_kv * g.d_model;
     cuuint64_t strides[2] = {static_cast<cuuint64_t>(g.d_model * 2), static_cast<cuuint64_t>(ls * 2)};
-    cuuint32_t box[3] = {kBK, static_cast<cuuint32_t>(pair ? kBN / 2 : kBN), 1};
+    cuuint32_t box[3] = {kBK, kBN, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     if (enc(&p.w_map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(a->packed), dims, strides,
             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -984,7 +581,7 @@ extern "C" int dkv_dense_patch_paged(const dkv_dense_patch_args *a, dkv_stream_t
   p.positions = s.positions;
   p.table_stride = s.table_stride;
   p.n_seqs = s.n_seqs;
-  p.max_chunks = (s.max_seq_len + chunk_rows - 1) / chunk_rows;
+  p.max_chunks = (s.max_seq_len + kBM - 1) / kBM;
   p.col_lo = a->do_k ? 0 : d_kv;
   p.col_hi = a->do_v ? 2 * d_kv : d_kv;
   p.n_tiles_n = (p.col_hi - p.col_lo + kBN - 1) / kBN;
@@ -1011,19 +608,12 @@ extern "C" int dkv_dense_patch_paged(const dkv_dense_patch_args *a, dkv_stream_t
   }
   p.n_tiles = static_cast<int64_t>(a->n_layers) * s.n_seqs * p.max_chunks * p.n_tiles_n;
 
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (pair) {
-    const int rc2 =
-        kp.dtype == DKV_BF16 ? launch_pair<DKV_BF16>(p, clusters, st) : launch_pair<DKV_F16>(p, clusters, st);
-    if (rc2) return rc2;
-    DKV_CUDA_CHECK(cudaGetLastError());
-    return DKV_OK;
-  }
   int dev = 0, sms = 0;
   DKV_CUDA_CHECK(cudaGetDevice(&dev));
   DKV_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int grid = static_cast<int>(p.n_tiles < sms ? p.n_tiles : sms);
   const size_t smem = 1024 + kSmemBytes;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (kp.dtype == DKV_BF16) {
     DKV_CUDA_CHECK(cudaFuncSetAttribute(dense_patch_kernel<DKV_BF16>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));

@@ -63,7 +63,10 @@ def test_dense_paged_golden(cuda):
             dg = bf16_bits_to_f32(got) - bf16_bits_to_f32(in_bits)
             dr = bf16_bits_to_f32(ref_bits) - bf16_bits_to_f32(in_bits)
             assert rel_l2(bf16_bits_to_f32(got), bf16_bits_to_f32(ref_bits)) < REL_TOL
-            assert rel_l2(dg, dr) < 2e-2  # the delta alone, with bf16 rounding of both sides
+            # the delta alone, with the bf16 rounding of both pages (~1e-2 of a delta of 20 % of the
+            # page); the delta itself, stored into f16 pages, is held to 1e-3 of the oracle's fp32
+            # x.dW^T at the Llama-70B shape (test_gpu_fullshape.py)
+            assert rel_l2(dg, dr) < 2e-2
             assert (got == ref_bits).mean() > 0.95
 
 

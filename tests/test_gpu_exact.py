@@ -59,7 +59,10 @@ def test_fp8_paged_golden(cuda):
             dg = bf16_bits_to_f32(got) - bf16_bits_to_f32(in_bits)
             dr = bf16_bits_to_f32(ref_bits) - bf16_bits_to_f32(in_bits)
             assert rel_l2(bf16_bits_to_f32(got), bf16_bits_to_f32(ref_bits)) < REL_TOL
-            assert rel_l2(dg, dr) < 2e-2  # delta alone, including bf16 rounding of both sides
+            # delta alone, including the bf16 rounding of both pages: ~2^-9 |page| per element is
+            # ~1e-2 of a delta of 20 % of the page; the delta itself is held to 1e-3 on fp32 pages
+            # (test_gpu_fullshape.py)
+            assert rel_l2(dg, dr) < 2e-2
             assert (got == ref_bits).mean() > 0.98
 
 

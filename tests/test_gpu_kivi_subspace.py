@@ -148,6 +148,24 @@ def test_kivi_subspace_matches_oracle(cuda, mode, n, n_kv, hd, r, fdt, inplace):
     _check(cs, o, sub, mu, (mode, n, r))
 
 
+@pytest.mark.parametrize("mode", ["v", "k"])
+@pytest.mark.parametrize("n,n_kv,hd,r,ratio", [
+    (200, 8, 128, 16, 1.0),  # every token a probe: K rows all fresh (two staged per lane, the rest read
+                             # directly), V rows all requantised from fresh on their own
+    (333, 3, 64, 8, 0.6),    # d = 192 (6 blocks: V scale / zero read directly), a ragged last K group
+])
+def test_kivi_subspace_probe_heavy(cuda, mode, n, n_kv, hd, r, ratio):
+    gen = torch.Generator().manual_seed(n + r + 17 * (mode == "k"))
+    cs = _case(gen, n, n_kv, hd, r, mode, probe_ratio=ratio)
+    cs["fresh"] = cs["fresh"].to(torch.bfloat16).float()
+    out = K.KiviTensor.empty(n, cs["d"], mode, cuda)
+    pb = K.SubspaceProblem(base=_device_base(cs, cuda), fresh=cs["fresh"].to(torch.bfloat16).to(cuda),
+                           probe_index=cs["probes"].to(cuda), basis=cs["B"].to(cuda), rank=r, out=out)
+    (o, sub, mu), = K.subspace_correct([pb], stats=True)
+    torch.cuda.synchronize()
+    _check(cs, o, sub, mu, ("probe-heavy", mode, n, ratio))
+
+
 def test_kivi_subspace_batch_of_mixed_problems(cuda):
     """K and V views of several layers with different lengths and ranks in one call."""
     gen = torch.Generator().manual_seed(5)

@@ -66,12 +66,33 @@ constexpr int kMaxRank = 64;
 constexpr int kPsumCtas = 8;  // fewest probe-sum CTAs (of 8 warps) per problem
 
 struct Prob {
-  const uint8_t *codes;
-  const __half *scale, *zero;
-  int64_t crs, szrs;
-  uint8_t *o_codes;
+  union {
+    const uint8_t *codes;  // int4: the base codes
+    const void *reused;    // dense: the reused rows (fresh dtype)
+  };
+  union {
+    const __half *scale;  // int4: the base scales
+    const float *tw;      // dense: the caller's token weights (or null)
+  };
+  const __half *zero;
+  union {
+    int64_t crs;  // int4: bytes per code row
+    int64_t rrs;  // dense: elements per reused row
+  };
+  union {
+    int64_t szrs;  // int4: elements per scale / zero row
+    int64_t odt;   // dense: output dtype
+  };
+  union {
+    uint8_t *o_codes;  // int4: the corrected codes
+    void *out;         // dense: the corrected rows (output dtype odt)
+  };
   __half *o_scale, *o_zero;
-  int64_t o_crs, o_szrs;
+  union {
+    int64_t o_crs;  // int4: bytes per output code row
+    int64_t ors;    // dense: elements per output row
+  };
+  int64_t o_szrs;
   const void *fresh;
   int64_t frs;
   int64_t n;
@@ -126,6 +147,23 @@ __device__ __forceinline__ void load8(const void *base, int64_t off, float (&v)[
     for (int j = 0; j < 4; ++j) {
       v[2 * j] = FDT == DKV_BF16 ? bf16lo(w[j]) : f16lo(w[j]);
       v[2 * j + 1] = FDT == DKV_BF16 ? bf16hi(w[j]) : f16hi(w[j]);
+    }
+  }
+}
+
+// 8 staged values (one 16-B chunk, or two for f32) -> floats
+template <int FDT>
+__device__ __forceinline__ void unpack8(const uint4 &u0, const uint4 &u1, float (&f)[8]) {
+  if (FDT == DKV_F32) {
+    f[0] = __uint_as_float(u0.x), f[1] = __uint_as_float(u0.y), f[2] = __uint_as_float(u0.z);
+    f[3] = __uint_as_float(u0.w), f[4] = __uint_as_float(u1.x), f[5] = __uint_as_float(u1.y);
+    f[6] = __uint_as_float(u1.z), f[7] = __uint_as_float(u1.w);
+  } else {
+    const uint32_t w4[4] = {u0.x, u0.y, u0.z, u0.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      f[2 * j] = FDT == DKV_BF16 ? bf16lo(w4[j]) : f16lo(w4[j]);
+      f[2 * j + 1] = FDT == DKV_BF16 ? bf16hi(w4[j]) : f16hi(w4[j]);
     }
   }
 }
@@ -217,12 +255,18 @@ __device__ __forceinline__ void split2(uint64_t r2, uint32_t &hi, uint32_t &lo) 
 // one block's per-warp operands: fresh (16 or 32 B per lane and row, copied by that lane),
 // the codes (row r's 16 B, copied by lane r) and, for K, the group's scale / zero (16 B per
 // 8 channels, copied by lanes 0-7)
-template <int FDT>
+template <int FDT, bool DENSE>
 struct P1Stage {
   static constexpr int kFB = FDT == DKV_F32 ? 2 : 1;
   uint4 fr[4][kFB][32];
   uint32_t cd[kWT][4];
   uint4 sz[2][4];
+};
+template <int FDT>
+struct P1Stage<FDT, true> {  // dense caches: the reused rows staged like the fresh ones
+  static constexpr int kFB = FDT == DKV_F32 ? 2 : 1;
+  uint4 fr[4][kFB][32];
+  uint4 rr[4][kFB][32];
 };
 // V: the rows' scale / zero, 4 blocks (8 B per row) per buffer, two buffers
 struct P1VStage {
@@ -233,10 +277,11 @@ template <int RP>
 constexpr int p1_bq_bytes() {  // one block's basis fragments: high terms, then low terms
   return (RP / 8) * 32 * 16 * 2;
 }
-template <int RP, int FDT, int MODE>
+template <int RP, int FDT, int MODE, bool DENSE = false>
 constexpr int p1_smem_bytes() {
-  return kBSlots * p1_bq_bytes<RP>() + kWarps * kP1Stages * static_cast<int>(sizeof(P1Stage<FDT>)) +
-         (MODE == DKV_KIVI_PER_TOKEN ? kWarps * static_cast<int>(sizeof(P1VStage)) : 0) + 2 * kBSlots * 8 + 16;
+  return kBSlots * p1_bq_bytes<RP>() + kWarps * kP1Stages * static_cast<int>(sizeof(P1Stage<FDT, DENSE>)) +
+         (MODE == DKV_KIVI_PER_TOKEN && !DENSE ? kWarps * static_cast<int>(sizeof(P1VStage)) : 0) +
+         2 * kBSlots * 8 + 16;
 }
 
 // CTAs per SM that pass1 is compiled for (its register budget; measured per rank tile)
@@ -245,7 +290,7 @@ constexpr int p1_min_blocks() {
   return RP == 16 ? 5 : RP == 32 ? 4 : 3;
 }
 
-template <int RP, int FDT, int MODE>
+template <int RP, int FDT, int MODE, bool DENSE = false>
 __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
     pass1_kernel(const __grid_constant__ Batch b, int64_t tile_lo) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
@@ -258,14 +303,14 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
   constexpr int BQ = p1_bq_bytes<RP>();
   const int n_blocks = static_cast<int>(b.d / kCB);
   // shared: [fragment ring][per-warp stage rings][V rows][barriers, abort]
-  using Stage = P1Stage<FDT>;
+  using Stage = P1Stage<FDT, DENSE>;
   extern __shared__ __align__(16) unsigned char p1_smem[];
   unsigned char *const bq_ring = p1_smem;
   unsigned char *sp = p1_smem + kBSlots * BQ;
   Stage *const ring = reinterpret_cast<Stage *>(sp) + warp * kP1Stages;
   sp += kWarps * kP1Stages * sizeof(Stage);
   P1VStage *const vst = reinterpret_cast<P1VStage *>(sp) + warp;
-  if constexpr (!kmode) sp += kWarps * sizeof(P1VStage);
+  if constexpr (!kmode && !DENSE) sp += kWarps * sizeof(P1VStage);
   uint64_t *const bq_full = reinterpret_cast<uint64_t *>(sp);
   uint64_t *const bq_empty = bq_full + kBSlots;
   volatile int *const abort_flag = reinterpret_cast<volatile int *>(bq_empty + kBSlots);
@@ -317,10 +362,10 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
   const int64_t krow = t0 / kivi::kG;
   const int64_t my_row = t0 + lane;
   const bool my_valid = my_row < n;
-  const uint8_t *const my_codes = P.codes + (my_valid ? my_row : t0) * P.crs;
+  const uint8_t *const my_codes = DENSE ? nullptr : P.codes + (my_valid ? my_row : t0) * P.crs;
   // V: the rows' scale / zero staged 4 blocks at a time where the rows allow 8-B copies,
   // otherwise read directly
-  const bool vstage = !kmode && n_blocks % 4 == 0 && P.szrs % 4 == 0;
+  const bool vstage = !DENSE && !kmode && n_blocks % 4 == 0 && P.szrs % 4 == 0;
   constexpr int kFB = Stage::kFB;
   constexpr int kEs = FDT == DKV_F32 ? 4 : 2;
   // per-warp staging ring (cp.async, kP1Stages - 1 blocks ahead)
@@ -334,19 +379,27 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
         const unsigned char *fp = static_cast<const unsigned char *>(P.fresh) + (rr * P.frs + c) * kEs;
 #pragma unroll
         for (int f = 0; f < kFB; ++f) cp_async16(&S.fr[i][f][lane], fp + 16 * f, rv[i] ? 16u : 0u);
+        if constexpr (DENSE) {
+          const unsigned char *rp = static_cast<const unsigned char *>(P.reused) + (rr * P.rrs + c) * kEs;
+#pragma unroll
+          for (int f = 0; f < kFB; ++f) cp_async16(&S.rr[i][f][lane], rp + 16 * f, rv[i] ? 16u : 0u);
+        }
       }
-      cp_async16(&S.cd[lane][0], my_codes + static_cast<int64_t>(cb) * (kCB / 2), my_valid ? 16u : 0u);
-      if constexpr (kmode) {
-        if (lane < 8)
-          cp_async16(&S.sz[lane >> 2][lane & 3],
-                     (lane < 4 ? P.scale : P.zero) + krow * P.szrs + static_cast<int64_t>(cb) * kCB + 8 * (lane & 3),
-                     16u);
-      } else {
-        if (vstage && cb % 4 == 0) {
-          const int buf = (cb >> 2) & 1;
-          const int64_t off = (my_valid ? my_row : t0) * P.szrs + cb;
-          cp_async8(&vst->s[buf][lane], P.scale + off, my_valid ? 8u : 0u);
-          cp_async8(&vst->z[buf][lane], P.zero + off, my_valid ? 8u : 0u);
+      if constexpr (!DENSE) {
+        cp_async16(&S.cd[lane][0], my_codes + static_cast<int64_t>(cb) * (kCB / 2), my_valid ? 16u : 0u);
+        if constexpr (kmode) {
+          if (lane < 8)
+            cp_async16(&S.sz[lane >> 2][lane & 3],
+                       (lane < 4 ? P.scale : P.zero) + krow * P.szrs + static_cast<int64_t>(cb) * kCB +
+                           8 * (lane & 3),
+                       16u);
+        } else {
+          if (vstage && cb % 4 == 0) {
+            const int buf = (cb >> 2) & 1;
+            const int64_t off = (my_valid ? my_row : t0) * P.szrs + cb;
+            cp_async8(&vst->s[buf][lane], P.scale + off, my_valid ? 8u : 0u);
+            cp_async8(&vst->z[buf][lane], P.zero + off, my_valid ? 8u : 0u);
+          }
         }
       }
     }
@@ -372,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
     __syncwarp();  // the other lanes' copies of this block are visible
     const Stage &S = ring[cb % kP1Stages];
     uint64_t ks2[4], kz2[4];  // K: this lane's channels' rescaled scale and zero, in pairs
-    if constexpr (kmode) {
+    if constexpr (kmode && !DENSE) {
       const uint4 sv = S.sz[0][q], zv = S.sz[1][q];
       const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, zw[4] = {zv.x, zv.y, zv.z, zv.w};
 #pragma unroll
@@ -387,47 +440,49 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
       uint64_t r2[4] = {0, 0, 0, 0};
       if (rv[i]) {
         float f[8];
-        if (FDT == DKV_F32) {
-          const uint4 u0 = S.fr[i][0][lane], u1 = S.fr[i][kFB - 1][lane];
-          f[0] = __uint_as_float(u0.x), f[1] = __uint_as_float(u0.y), f[2] = __uint_as_float(u0.z);
-          f[3] = __uint_as_float(u0.w), f[4] = __uint_as_float(u1.x), f[5] = __uint_as_float(u1.y);
-          f[6] = __uint_as_float(u1.z), f[7] = __uint_as_float(u1.w);
+        unpack8<FDT>(S.fr[i][0][lane], S.fr[i][kFB - 1][lane], f);
+        if constexpr (DENSE) {
+          float x[8];
+          unpack8<FDT>(S.rr[i][0][lane], S.rr[i][kFB - 1][lane], x);
+          uint64_t dd2 = 0;
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            r2[p] = sub2(f2pack(f[2 * p], f[2 * p + 1]), f2pack(x[2 * p], x[2 * p + 1]));
+            dd2 = fma2(r2[p], r2[p], dd2);
+          }
+          float e0, e1;
+          f2unpack(dd2, e0, e1);
+          d2[i] += e0 + e1;
         } else {
-          const uint4 u = S.fr[i][0][lane];
-          const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            f[2 * j] = FDT == DKV_BF16 ? bf16lo(w4[j]) : f16lo(w4[j]);
-            f[2 * j + 1] = FDT == DKV_BF16 ? bf16hi(w4[j]) : f16hi(w4[j]);
+          uint64_t raw[4];
+          kivi::code_pairs(S.cd[g + 8 * i][q], raw);
+          uint64_t vs_lo = 0, vs_hi = 0, vz2 = 0;
+          if constexpr (!kmode) {
+            float vs, vz;
+            if (vstage) {
+              const int buf = (cb >> 2) & 1;
+              vs = __half2float(reinterpret_cast<const __half *>(&vst->s[buf][g + 8 * i])[cb & 3]);
+              vz = __half2float(reinterpret_cast<const __half *>(&vst->z[buf][g + 8 * i])[cb & 3]);
+            } else {
+              vs = __half2float(P.scale[row[i] * P.szrs + cb]);
+              vz = __half2float(P.zero[row[i] * P.szrs + cb]);
+            }
+            vs_lo = mul2(f2pack(vs, vs), rs_lo);
+            vs_hi = mul2(f2pack(vs, vs), rs_hi);
+            vz2 = f2pack(vz, vz);
           }
-        }
-        uint64_t raw[4];
-        kivi::code_pairs(S.cd[g + 8 * i][q], raw);
-        uint64_t vs_lo = 0, vs_hi = 0, vz2 = 0;
-        if constexpr (!kmode) {
-          float vs, vz;
-          if (vstage) {
-            const int buf = (cb >> 2) & 1;
-            vs = __half2float(reinterpret_cast<const __half *>(&vst->s[buf][g + 8 * i])[cb & 3]);
-            vz = __half2float(reinterpret_cast<const __half *>(&vst->z[buf][g + 8 * i])[cb & 3]);
-          } else {
-            vs = __half2float(P.scale[row[i] * P.szrs + cb]);
-            vz = __half2float(P.zero[row[i] * P.szrs + cb]);
-          }
-          vs_lo = mul2(f2pack(vs, vs), rs_lo);
-          vs_hi = mul2(f2pack(vs, vs), rs_hi);
-          vz2 = f2pack(vz, vz);
-        }
-        uint64_t dd2 = 0;
+          uint64_t dd2 = 0;
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          const uint64_t reused2 = fma2(raw[p], kmode ? ks2[p] : ((p & 1) ? vs_hi : vs_lo), kmode ? kz2[p] : vz2);
-          r2[p] = sub2(f2pack(f[2 * p], f[2 * p + 1]), reused2);
-          dd2 = fma2(r2[p], r2[p], dd2);
+          for (int p = 0; p < 4; ++p) {
+            const uint64_t reused2 =
+                fma2(raw[p], kmode ? ks2[p] : ((p & 1) ? vs_hi : vs_lo), kmode ? kz2[p] : vz2);
+            r2[p] = sub2(f2pack(f[2 * p], f[2 * p + 1]), reused2);
+            dd2 = fma2(r2[p], r2[p], dd2);
+          }
+          float e0, e1;
+          f2unpack(dd2, e0, e1);
+          d2[i] += e0 + e1;
         }
-        float e0, e1;
-        f2unpack(dd2, e0, e1);
-        d2[i] += e0 + e1;
       }
       const int m = i >> 1, h = i & 1;
       split2(r2[0], a[m][0][h], al[m][0][h]);
@@ -518,7 +573,7 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
 // time with 16-byte loads (8 channels per lane), the CTA's warps are summed in shared memory
 // and one atomic per channel and CTA goes to the problem's sums.
 // ---------------------------------------------------------------------------------------
-template <int RP, int FDT>
+template <int RP, int FDT, bool DENSE = false>
 __global__ void __launch_bounds__(256) psum_kernel(const __grid_constant__ Batch b, int ctas) {
   __shared__ float red[8][256];
   const Prob &P = b.probs[blockIdx.y];
@@ -533,20 +588,28 @@ __global__ void __launch_bounds__(256) psum_kernel(const __grid_constant__ Batch
     if (c < b.d) {
       for (int i = w0; i < cnt; i += wstep) {
         const int64_t t = P.uprobe[i];
-        float f[8], sc[8], zr[8];
+        float f[8];
         load8<FDT>(P.fresh, t * P.frs + c, f);
-        const uint32_t w = *reinterpret_cast<const uint32_t *>(P.codes + t * P.crs + c / 2);
-        if (kmode) {
-          halves8(P.scale + (t / kivi::kG) * P.szrs + c, sc);
-          halves8(P.zero + (t / kivi::kG) * P.szrs + c, zr);
+        if constexpr (DENSE) {
+          float x[8];
+          load8<FDT>(P.reused, t * P.rrs + c, x);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] += f[j] - x[j];
         } else {
-          const float vs = __half2float(P.scale[t * P.szrs + c / kivi::kG]);
-          const float vz = __half2float(P.zero[t * P.szrs + c / kivi::kG]);
+          float sc[8], zr[8];
+          const uint32_t w = *reinterpret_cast<const uint32_t *>(P.codes + t * P.crs + c / 2);
+          if (kmode) {
+            halves8(P.scale + (t / kivi::kG) * P.szrs + c, sc);
+            halves8(P.zero + (t / kivi::kG) * P.szrs + c, zr);
+          } else {
+            const float vs = __half2float(P.scale[t * P.szrs + c / kivi::kG]);
+            const float vz = __half2float(P.zero[t * P.szrs + c / kivi::kG]);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) sc[j] = vs, zr[j] = vz;
+            for (int j = 0; j < 8; ++j) sc[j] = vs, zr[j] = vz;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] += f[j] - kivi::deq((w >> (4 * j)) & 0xFu, sc[j], zr[j]);
         }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] += f[j] - kivi::deq((w >> (4 * j)) & 0xFu, sc[j], zr[j]);
       }
     }
 #pragma unroll
@@ -1212,6 +1275,229 @@ __global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, MODE>())
 }
 
 // ---------------------------------------------------------------------------------------
+// Dense caches (dkv_subspace_correct on f32 / f16 / bf16 rows): the same pipeline with the
+// reused rows read directly — pass1<..., DENSE>, psum<..., DENSE>, solve, fitb, then dpass2
+// (corr = (reused + fitted) + w orth_mu for the non-probe rows, stored in the output dtype)
+// and dprobe (the probe rows take the fresh values, corr[P] = fresh[P]).
+// ---------------------------------------------------------------------------------------
+// 8 values to a row of the output dtype (16-B aligned: 32 B for f32, 16 B otherwise)
+__device__ __forceinline__ void store8(void *base, int dt, int64_t off, const float (&v)[8]) {
+  if (dt == DKV_F32) {
+    float4 *o = reinterpret_cast<float4 *>(static_cast<float *>(base) + off);
+    o[0] = make_float4(v[0], v[1], v[2], v[3]);
+    o[1] = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    uint4 u;
+    if (dt == DKV_BF16) {
+      u.x = pack_bf16x2(v[0], v[1]), u.y = pack_bf16x2(v[2], v[3]);
+      u.z = pack_bf16x2(v[4], v[5]), u.w = pack_bf16x2(v[6], v[7]);
+    } else {
+      u.x = pack_f16x2(v[0], v[1]), u.y = pack_f16x2(v[2], v[3]);
+      u.z = pack_f16x2(v[4], v[5]), u.w = pack_f16x2(v[6], v[7]);
+    }
+    *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(base) + off) = u;
+  }
+}
+
+// one block's per-warp operands in dpass2: the reused rows (16 or 32 B per lane and row)
+template <int FDT>
+struct D2Stage {
+  static constexpr int kFB = FDT == DKV_F32 ? 2 : 1;
+  uint4 rr[4][kFB][32];
+};
+template <int RP, int FDT>
+constexpr int d2_smem_fixed() {  // everything but orth_mu [d]
+  return kBSlots * p2_bq_bytes<RP>() + kWarps * kP2Stages * static_cast<int>(sizeof(D2Stage<FDT>)) +
+         2 * kBSlots * 8 + 16;
+}
+
+template <int RP, int FDT>
+__global__ void __launch_bounds__(kThreads, p2_min_blocks<RP, DKV_KIVI_PER_TOKEN>())
+    dpass2_kernel(const __grid_constant__ Batch b) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+  const Prob &P = b.probs[find_prob(b, blockIdx.x)];
+  const int64_t tile_t0 = (blockIdx.x - P.tile0) * kTM;
+  const int64_t t0 = tile_t0 + warp * kWT;
+  const int64_t n = P.n;
+  constexpr int KS = RP / 16;
+  constexpr int BQ = p2_bq_bytes<RP>();
+  const int n_blocks = static_cast<int>(b.d / kCB);
+  using Stage = D2Stage<FDT>;
+  constexpr int kFB = Stage::kFB;
+  constexpr int kEs = FDT == DKV_F32 ? 4 : 2;
+  // shared: [fragment ring][per-warp stage rings][barriers, abort][orth_mu]
+  extern __shared__ __align__(16) unsigned char d2_smem[];
+  unsigned char *const bq_ring = d2_smem;
+  Stage *const ring = reinterpret_cast<Stage *>(d2_smem + kBSlots * BQ) + warp * kP2Stages;
+  unsigned char *const sp = d2_smem + kBSlots * BQ + kWarps * kP2Stages * sizeof(Stage);
+  uint64_t *const bq_full = reinterpret_cast<uint64_t *>(sp);
+  uint64_t *const bq_empty = bq_full + kBSlots;
+  volatile int *const abort_flag = reinterpret_cast<volatile int *>(bq_empty + kBSlots);
+  float *const mu_s = reinterpret_cast<float *>(sp + 2 * kBSlots * 8 + 16);
+
+  const int active = static_cast<int>((n - tile_t0 + kWT - 1) / kWT < kWarps ? (n - tile_t0 + kWT - 1) / kWT : kWarps);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBSlots; ++s) {
+      mbar_init(&bq_full[s], 1);
+      mbar_init(&bq_empty[s], active);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  for (int64_t e = threadIdx.x; e < b.d / 4; e += kThreads)
+    reinterpret_cast<float4 *>(mu_s)[e] = reinterpret_cast<const float4 *>(P.mu)[e];
+  __syncthreads();
+  if (t0 >= n) return;
+
+  const bool producer = warp == 0 && lane == 0;
+  const unsigned char *const bq_src = reinterpret_cast<const unsigned char *>(P.b2);
+  int bq_issued = 0;
+  auto bq_issue = [&]() -> bool {
+    const int blk = bq_issued, s = blk % kBSlots;
+    if (blk >= kBSlots && !mbar_wait_bounded(&bq_empty[s], ((blk / kBSlots) - 1) & 1, abort_flag)) return false;
+    mbar_arrive_expect_tx(&bq_full[s], BQ);
+    bulk_load(bq_ring + s * BQ, bq_src + static_cast<int64_t>(blk) * BQ, BQ, &bq_full[s]);
+    ++bq_issued;
+    return true;
+  };
+  bool ok = true;
+  if (producer)
+    while (bq_issued < kBSlots - 1 && bq_issued < n_blocks) bq_issue();
+
+  const float mean_dist = P.subv[b.d];
+  int64_t row[4];
+  bool st[4];  // rows this lane stores (valid, not a probe)
+  float w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    row[i] = t0 + g + 8 * i;
+    const bool rv = row[i] < n;
+    st[i] = rv && P.flag[row[i]] == 0u;
+    w[i] = !rv ? 0.f : P.tw != nullptr ? P.tw[row[i]] : fminf(P.dist[row[i]] / mean_dist, 1.f);
+  }
+  // A fragments: the row's rhs at this lane's positions k = 16 ks + 2q + {0, 1, 8, 9}, as
+  // high and low bf16 terms
+  uint32_t a[2][KS][4], al[2][KS][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = i >> 1, h = i & 1;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      float2 lo = make_float2(0.f, 0.f), hi = make_float2(0.f, 0.f);
+      if (row[i] < n) {
+        const float *rr = P.rhs + row[i] * RP + 16 * ks + 2 * q;
+        lo = *reinterpret_cast<const float2 *>(rr);
+        hi = *reinterpret_cast<const float2 *>(rr + 8);
+      }
+      split_bf16x2(lo.x, lo.y, a[m][ks][h], al[m][ks][h]);
+      split_bf16x2(hi.x, hi.y, a[m][ks][2 + h], al[m][ks][2 + h]);
+    }
+  }
+  // per-warp staging ring: each lane copies and reads back only its own reused chunks
+  auto issue = [&](int blk) {
+    if (blk < n_blocks) {
+      Stage &S = ring[blk % kP2Stages];
+      const int64_t c = static_cast<int64_t>(blk) * kCB + 8 * q;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const unsigned char *rp =
+            static_cast<const unsigned char *>(P.reused) + ((st[i] ? row[i] : t0) * P.rrs + c) * kEs;
+#pragma unroll
+        for (int f = 0; f < kFB; ++f) cp_async16(&S.rr[i][f][lane], rp + 16 * f, st[i] ? 16u : 0u);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int s0 = 0; s0 < kP2Stages - 1; ++s0) issue(s0);
+
+  int cb = 0;
+  for (; cb < n_blocks; ++cb) {
+    if (warp == 0) {
+      int pok = 1;
+      if (producer && bq_issued < n_blocks) pok = bq_issue() ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, pok, 0)) {
+        ok = false;
+        break;
+      }
+    }
+    issue(cb + kP2Stages - 1);
+    cp_async_wait<kP2Stages - 1>();
+    const int slot = cb % kBSlots;
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bq_full[slot], (cb / kBSlots) & 1, abort_flag))) {
+      ok = false;
+      break;
+    }
+    const Stage &S = ring[cb % kP2Stages];
+    const uint4 *const bq = reinterpret_cast<const uint4 *>(bq_ring + slot * BQ) + lane;
+    const int64_t c = static_cast<int64_t>(cb) * kCB + 8 * q;
+    float acc[2][4][4];
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const uint4 f = bq[(ks * 4 + nt) * 32];  // high terms (x, y), low terms (z, w)
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {  // rhs (B G^-1)^T ~ ah bh + ah bl + al bh, small terms first
+          if (ks == 0)
+            mma16816_bf16_zc(acc[m][nt], al[m][ks][0], al[m][ks][1], al[m][ks][2], al[m][ks][3], f.x, f.y);
+          else
+            mma16816_bf16(acc[m][nt], al[m][ks][0], al[m][ks][1], al[m][ks][2], al[m][ks][3], f.x, f.y);
+          mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], f.z, f.w);
+          mma16816_bf16(acc[m][nt], a[m][ks][0], a[m][ks][1], a[m][ks][2], a[m][ks][3], f.x, f.y);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bq_empty[slot]);
+    uint64_t mu2[4];
+    {
+      const float4 *mp = reinterpret_cast<const float4 *>(mu_s + c);
+      const float4 x = mp[0], y = mp[1];
+      mu2[0] = f2pack(x.x, x.y), mu2[1] = f2pack(x.z, x.w), mu2[2] = f2pack(y.x, y.y), mu2[3] = f2pack(y.z, y.w);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (!st[i]) continue;
+      const int m = i >> 1, h = i & 1;
+      float x[8], v[8];
+      unpack8<FDT>(S.rr[i][0][lane], S.rr[i][kFB - 1][lane], x);
+      const uint64_t w2 = f2pack(w[i], w[i]);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const uint64_t c2 = add2(add2(f2pack(x[2 * p], x[2 * p + 1]), f2pack(acc[m][p][2 * h], acc[m][p][2 * h + 1])),
+                                 mul2(w2, mu2[p]));
+        f2unpack(c2, v[2 * p], v[2 * p + 1]);
+      }
+      store8(P.out, P.odt, row[i] * P.ors + c, v);
+    }
+  }
+  cp_async_wait<0>();
+  if (!ok) {
+    record_error(b.status, DKV_ERR_TIMEOUT);
+    *abort_flag = 1;
+  }
+  if (producer)
+    for (int blk = cb; blk < bq_issued; ++blk) mbar_wait_drain(&bq_full[blk % kBSlots], (blk / kBSlots) & 1);
+}
+
+// corr[P] = fresh[P]: one warp per unique probe row
+template <int FDT>
+__global__ void __launch_bounds__(128) dprobe_kernel(const __grid_constant__ Batch b) {
+  const Prob &P = b.probs[blockIdx.y];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int count = *P.ucount;
+  for (int k = blockIdx.x * 4 + warp; k < count; k += gridDim.x * 4) {
+    const int64_t t = P.uprobe[k];
+    for (int64_t c = 8 * lane; c < b.d; c += 256) {
+      float f[8];
+      load8<FDT>(P.fresh, t * P.frs + c, f);
+      store8(P.out, P.odt, t * P.ors + c, f);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
 // vprobe: the probe rows of the V (per-token) problems.  There corr = fresh, and a per-token
 // group holds one row's channels only, so each probe row is requantised from its fresh values
 // alone (pass2 leaves these rows untouched): one warp per row, one lane per 32-channel group,
@@ -1446,6 +1732,153 @@ int launch_rp(int rp, const Batch &b, int np, int n_kprob, int64_t max_probes, i
     case 64: return launch<64, FDT>(b, np, n_kprob, max_probes, k_tiles, st);
     default: return DKV_ERR_UNSUPPORTED;
   }
+}
+
+// ---------------------------------------------------------------------------------------
+// dense caches: one problem per call (dkv_subspace_correct), d a multiple of 32 and 16-byte
+// rows; other shapes stay on the general kernels of subspace.cu
+// ---------------------------------------------------------------------------------------
+template <int RP, int FDT>
+int launch_dense(const Batch &b, int64_t max_probes, cudaStream_t st) {
+  if (max_probes > 0) {
+    const int bx = static_cast<int>((max_probes + 255) / 256 < 64 ? (max_probes + 255) / 256 : 64);
+    flags_kernel<<<dim3(bx, 1), 256, 0, st>>>(b);
+    DKV_CUDA_CHECK(cudaGetLastError());
+  }
+  {
+    const int64_t total = b.d * RP;
+    const int bx = static_cast<int>((total + 255) / 256 < 256 ? (total + 255) / 256 : 256);
+    pack_kernel<<<dim3(bx, 1), 256, 0, st>>>(b, RP);
+    DKV_CUDA_CHECK(cudaGetLastError());
+  }
+  const unsigned tiles = static_cast<unsigned>(b.n_tiles);
+  {
+    constexpr int sm = p1_smem_bytes<RP, FDT, DKV_KIVI_PER_TOKEN, true>();
+    auto fn = pass1_kernel<RP, FDT, DKV_KIVI_PER_TOKEN, true>;
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        cudaSharedmemCarveoutMaxShared));
+    fn<<<tiles, kThreads, sm, st>>>(b, 0);
+    DKV_CUDA_CHECK(cudaGetLastError());
+  }
+  if (max_probes > 0) {
+    const int ctas = 4 * 148 < 64 ? 4 * 148 : 64;
+    psum_kernel<RP, FDT, true><<<dim3(ctas, 1), 256, 0, st>>>(b, ctas);
+    DKV_CUDA_CHECK(cudaGetLastError());
+  }
+  const int solve_smem = kMaxRank * (2 * kMaxRank + 1) * 8 + 64 * RP * 8;
+  DKV_CUDA_CHECK(cudaFuncSetAttribute(solve_kernel<RP>, cudaFuncAttributeMaxDynamicSharedMemorySize, solve_smem));
+  solve_kernel<RP><<<1, 256, solve_smem, st>>>(b);
+  DKV_CUDA_CHECK(cudaGetLastError());
+  fitb_kernel<RP><<<dim3(static_cast<unsigned>(b.d / kCB), 1), 256, 0, st>>>(b);
+  DKV_CUDA_CHECK(cudaGetLastError());
+  {
+    const int sm = static_cast<int>(b.d * 4) + d2_smem_fixed<RP, FDT>();
+    auto fn = dpass2_kernel<RP, FDT>;
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, sm));
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        cudaSharedmemCarveoutMaxShared));
+    fn<<<tiles, kThreads, sm, st>>>(b);
+    DKV_CUDA_CHECK(cudaGetLastError());
+  }
+  if (max_probes > 0) {
+    const int bx = static_cast<int>((max_probes + 3) / 4 < 64 ? (max_probes + 3) / 4 : 64);
+    dprobe_kernel<FDT><<<dim3(bx, 1), 128, 0, st>>>(b);
+    DKV_CUDA_CHECK(cudaGetLastError());
+  }
+  return DKV_OK;
+}
+
+template <int FDT>
+int launch_dense_rp(int rp, const Batch &b, int64_t max_probes, cudaStream_t st) {
+  switch (rp) {
+    case 16: return launch_dense<16, FDT>(b, max_probes, st);
+    case 32: return launch_dense<32, FDT>(b, max_probes, st);
+    case 48: return launch_dense<48, FDT>(b, max_probes, st);
+    case 64: return launch_dense<64, FDT>(b, max_probes, st);
+    default: return DKV_ERR_UNSUPPORTED;
+  }
+}
+
+inline Layout dense_layout(int64_t n, int64_t d, int rp) {
+  dkv_kivi_subspace_problem q;
+  memset(&q, 0, sizeof(q));
+  q.base.n_tokens = n;
+  q.n_probes = n;  // unique probe rows never exceed the token count
+  return layout(&q, 1, d, rp);
+}
+
+inline int dense_rp(int rank) { return rank <= 16 ? 16 : (rank + 15) / 16 * 16; }
+
+bool dense_applies(const dkv_subspace_args &a) {
+  if (a.n_tokens <= 0 || a.n_tokens > 0x7fffffffLL || a.d <= 0 || a.d % kCB) return false;
+  if (a.rank < 0 || a.rank > kMaxRank) return false;
+  auto esz = [](int dt) { return dt == DKV_F32 ? 4 : (dt == DKV_F16 || dt == DKV_BF16) ? 2 : 0; };
+  const int ke = esz(a.kv_dtype), oe = esz(a.out_dtype);
+  if (ke == 0 || oe == 0) return false;
+  if (!a16(a.reused) || !a16(a.fresh) || !a16(a.corrected)) return false;
+  if ((a.reused_row_stride * ke) % 16 || (a.fresh_row_stride * ke) % 16 || (a.out_row_stride * oe) % 16) return false;
+  return a.reused_row_stride >= a.d && a.fresh_row_stride >= a.d && a.out_row_stride >= a.d;
+}
+
+// The dense form: DKV_ERR_UNSUPPORTED when the shape or layout is not one it takes.
+int dense_correct(const dkv_subspace_args *a, uint8_t *ws, int64_t ws_bytes, cudaStream_t st) {
+  if (a == nullptr || !dense_applies(*a)) return DKV_ERR_UNSUPPORTED;
+  const int rp = dense_rp(a->rank);
+  const Layout L = dense_layout(a->n_tokens, a->d, rp);
+  if (ws == nullptr || ws_bytes < L.total || !a16(ws)) return DKV_ERR_UNSUPPORTED;
+  if (a->n_probes < 0 || (a->n_probes > 0 && a->probe_index == nullptr)) return DKV_ERR_INVALID_ARGUMENT;
+  if (a->rank > 0 && a->basis == nullptr) return DKV_ERR_INVALID_ARGUMENT;
+  static thread_local Batch b;
+  memset(&b, 0, sizeof(b));
+  Prob &P = b.probs[0];
+  P.fresh = a->fresh;
+  P.frs = a->fresh_row_stride;
+  P.n = a->n_tokens;
+  P.probes = a->probe_index;
+  P.n_probes = a->n_probes;
+  P.sub_out = a->subspace_out;
+  P.mu_out = a->orth_mu_out;
+  P.mode = DKV_KIVI_PER_TOKEN;
+  // the reference applies the column-space fit only with a basis and at least one probe
+  P.r = (a->n_probes > 0 && a->basis != nullptr) ? a->rank : 0;
+  P.basis = a->basis;
+  P.flag = reinterpret_cast<uint32_t *>(ws + L.flag[0]);
+  P.ucount = reinterpret_cast<int32_t *>(ws + L.ucount[0]);
+  P.sums = reinterpret_cast<float *>(ws + L.sums[0]);
+  P.uprobe = reinterpret_cast<int32_t *>(ws + L.uprobe[0]);
+  P.rhs = reinterpret_cast<float *>(ws + L.rhs[0]);
+  P.dist = reinterpret_cast<float *>(ws + L.dist[0]);
+  P.part = reinterpret_cast<float *>(ws + L.part[0]);
+  P.ginv = reinterpret_cast<float *>(ws + L.ginv[0]);
+  P.mu = reinterpret_cast<float *>(ws + L.mu[0]);
+  P.subv = reinterpret_cast<float *>(ws + L.subv[0]);
+  P.b1 = reinterpret_cast<__nv_bfloat16 *>(ws + L.b1[0]);
+  P.b1l = reinterpret_cast<__nv_bfloat16 *>(ws + L.b1l[0]);
+  P.b2 = reinterpret_cast<__nv_bfloat16 *>(ws + L.b2[0]);
+  P.bb = reinterpret_cast<float *>(ws + L.bb[0]);
+  P.reused = a->reused;
+  P.rrs = a->reused_row_stride;
+  P.out = a->corrected;
+  P.ors = a->out_row_stride;
+  P.odt = a->out_dtype;
+  P.tw = a->token_weights;
+  P.tile0 = 0;
+  DKV_CUDA_CHECK(cudaMemsetAsync(ws + L.zero_begin, 0, L.zero_end - L.zero_begin, st));
+  b.n_probs = 1;
+  b.d = a->d;
+  b.n_tiles = (a->n_tokens + kTM - 1) / kTM;
+  b.status = nullptr;
+  switch (a->kv_dtype) {
+    case DKV_BF16: return launch_dense_rp<DKV_BF16>(rp, b, a->n_probes, st);
+    case DKV_F16: return launch_dense_rp<DKV_F16>(rp, b, a->n_probes, st);
+    default: return launch_dense_rp<DKV_F32>(rp, b, a->n_probes, st);
+  }
+}
+
+int64_t dense_workspace_bytes(int64_t n, int64_t d, int rank) {
+  if (n <= 0 || d <= 0 || d % kCB || rank < 0 || rank > kMaxRank) return 0;
+  return dense_layout(n, d, dense_rp(rank)).total;
 }
 
 }  // namespace ksub

@@ -9,6 +9,10 @@
 //   corr = reused + fitted + w * orth_mu;  corr[P] = fresh[P]
 // Without a basis: corr = reused + w * mean_P(R), subspace = 0.
 //
+// Where d is a multiple of 32 and the rows are 16-byte aligned the call runs on the batched
+// tensor-core pipeline of kivi_subspace.cu (ksub::dense_correct: R B and rhs (B G^-1)^T on
+// split-bf16 mma.sync, the probe sums one warp per probe row, the solve register-blocked);
+// the kernels below take every other shape.
 // Four launches on the caller's stream, all arithmetic fp32 (the r x r inverse in fp64):
 //   sub_pass1    R, ||R||, rhs = R B per token (CTA-tiled small GEMM), CTA-reduced sums
 //   sub_probes   probe flags, sum_P R, sum_P rhs
@@ -20,6 +24,10 @@
 #include "dkv_common.cuh"
 
 namespace dkv {
+namespace ksub {
+int dense_correct(const dkv_subspace_args *a, uint8_t *ws, int64_t ws_bytes, cudaStream_t st);
+int64_t dense_workspace_bytes(int64_t n, int64_t d, int rank);
+}  // namespace ksub
 namespace sub {
 
 constexpr int kTM = 64;   // tokens per CTA tile
@@ -419,7 +427,8 @@ extern "C" int dkv_subspace_workspace_bytes(int64_t n_tokens, int64_t d, int32_t
   if (bytes == nullptr || n_tokens < 0 || d <= 0 || rank < 0 || rank > sub::kMaxRank)
     return DKV_ERR_INVALID_ARGUMENT;
   const int rp = rank == 0 ? 0 : (rank + 15) / 16 * 16;
-  *bytes = sub::layout(n_tokens, d, rp).total;
+  const int64_t general = sub::layout(n_tokens, d, rp).total, dense = ksub::dense_workspace_bytes(n_tokens, d, rank);
+  *bytes = dense > general ? dense : general;
   return DKV_OK;
 }
 
@@ -478,6 +487,11 @@ static int subspace_run(const sub::P &p, cudaStream_t st) {
 }
 
 extern "C" int dkv_subspace_correct(const dkv_subspace_args *a, dkv_stream_t stream) {
+  if (a != nullptr) {
+    const int rc = ksub::dense_correct(a, static_cast<uint8_t *>(a->workspace), a->workspace_bytes,
+                                       reinterpret_cast<cudaStream_t>(stream));
+    if (rc != DKV_ERR_UNSUPPORTED) return rc;
+  }
   sub::P p;
   int rc = subspace_params(a, static_cast<uint8_t *>(a ? a->workspace : nullptr),
                            a ? a->workspace_bytes : 0, p);
@@ -558,10 +572,18 @@ extern "C" int dkv_subspace_correct_noalloc(const dkv_subspace_args *a, dkv_stre
   if (a == nullptr) return DKV_ERR_INVALID_ARGUMENT;
   const int rp = a->rank <= 0 ? 0 : (a->rank + 15) / 16 * 16;
   if (a->n_tokens < 0 || a->d <= 0 || a->rank < 0 || a->rank > sub::kMaxRank) return DKV_ERR_INVALID_ARGUMENT;
-  if (sub::layout(a->n_tokens, a->d, rp).total > kNoAllocScratchBytes) return DKV_ERR_WORKSPACE;
+  const int64_t general = sub::layout(a->n_tokens, a->d, rp).total;
+  const int64_t dense = ksub::dense_workspace_bytes(a->n_tokens, a->d, a->rank);
+  if (general > kNoAllocScratchBytes && (dense == 0 || dense > kNoAllocScratchBytes)) return DKV_ERR_WORKSPACE;
   void *scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc != DKV_OK) return rc;
+  if (dense > 0 && dense <= kNoAllocScratchBytes) {
+    rc = ksub::dense_correct(a, static_cast<uint8_t *>(scratch), kNoAllocScratchBytes,
+                             reinterpret_cast<cudaStream_t>(stream));
+    if (rc != DKV_ERR_UNSUPPORTED) return rc;
+  }
+  if (general > kNoAllocScratchBytes) return DKV_ERR_WORKSPACE;
   sub::P p;
   rc = subspace_params(a, static_cast<uint8_t *>(scratch), kNoAllocScratchBytes, p);
   if (rc != DKV_OK) return rc;

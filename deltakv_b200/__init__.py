@@ -44,7 +44,7 @@ from deltakv_b200.probe import (
 )
 from deltakv_b200.paged import gather_from_paged, scatter_into_paged, scatter_into_paged_batched
 from deltakv_b200.rope import RotaryEmbedding
-from deltakv_b200.subspace import subspace_correct, svd_basis
+from deltakv_b200.subspace import subspace_correct, subspace_correct_batched, svd_basis
 from deltakv_b200.types import KVCache, LayerDelta, LowRankFactors, LowRankKVPatch
 
 __version__ = "0.1.0"
@@ -79,6 +79,7 @@ __all__ = [
     "scatter_into_paged_batched",
     "select_probes",
     "subspace_correct",
+    "subspace_correct_batched",
     "svd_basis",
     "weight_axis_scores",
     "zeroth_order_patches",

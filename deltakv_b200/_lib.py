@@ -64,6 +64,8 @@ EXPORTED = (
     "dkv_subspace_workspace_bytes",
     "dkv_subspace_correct",
     "dkv_subspace_correct_noalloc",
+    "dkv_subspace_correct_batched_workspace_bytes",
+    "dkv_subspace_correct_batched",
     "dkv_subspace_probe_residual",
 )
 
@@ -338,6 +340,10 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_subspace_correct.argtypes = [C.POINTER(SubspaceArgs), P]
     lib.dkv_subspace_correct_noalloc.restype = C.c_int
     lib.dkv_subspace_correct_noalloc.argtypes = [C.POINTER(SubspaceArgs), P]
+    lib.dkv_subspace_correct_batched_workspace_bytes.restype = C.c_int
+    lib.dkv_subspace_correct_batched_workspace_bytes.argtypes = [C.POINTER(SubspaceArgs), I32, C.POINTER(C.c_int64)]
+    lib.dkv_subspace_correct_batched.restype = C.c_int
+    lib.dkv_subspace_correct_batched.argtypes = [C.POINTER(SubspaceArgs), I32, P, I64, P]
     lib.dkv_subspace_probe_residual.restype = C.c_int
     lib.dkv_subspace_probe_residual.argtypes = [P, P, I32, I64, I64, I64, I64, P, I64, P, P]
 

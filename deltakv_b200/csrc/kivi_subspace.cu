@@ -1742,13 +1742,13 @@ template <int RP, int FDT>
 int launch_dense(const Batch &b, int64_t max_probes, cudaStream_t st) {
   if (max_probes > 0) {
     const int bx = static_cast<int>((max_probes + 255) / 256 < 64 ? (max_probes + 255) / 256 : 64);
-    flags_kernel<<<dim3(bx, 1), 256, 0, st>>>(b);
+    flags_kernel<<<dim3(bx, b.n_probs), 256, 0, st>>>(b);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   {
     const int64_t total = b.d * RP;
     const int bx = static_cast<int>((total + 255) / 256 < 256 ? (total + 255) / 256 : 256);
-    pack_kernel<<<dim3(bx, 1), 256, 0, st>>>(b, RP);
+    pack_kernel<<<dim3(bx, b.n_probs), 256, 0, st>>>(b, RP);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   const unsigned tiles = static_cast<unsigned>(b.n_tiles);
@@ -1762,15 +1762,16 @@ int launch_dense(const Batch &b, int64_t max_probes, cudaStream_t st) {
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   if (max_probes > 0) {
-    const int ctas = 4 * 148 < 64 ? 4 * 148 : 64;
-    psum_kernel<RP, FDT, true><<<dim3(ctas, 1), 256, 0, st>>>(b, ctas);
+    // about four CTAs per SM in all, at least kPsumCtas per problem
+    const int ctas = std::max(kPsumCtas, std::min(64, 4 * 148 / b.n_probs));
+    psum_kernel<RP, FDT, true><<<dim3(ctas, b.n_probs), 256, 0, st>>>(b, ctas);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   const int solve_smem = kMaxRank * (2 * kMaxRank + 1) * 8 + 64 * RP * 8;
   DKV_CUDA_CHECK(cudaFuncSetAttribute(solve_kernel<RP>, cudaFuncAttributeMaxDynamicSharedMemorySize, solve_smem));
-  solve_kernel<RP><<<1, 256, solve_smem, st>>>(b);
+  solve_kernel<RP><<<b.n_probs, 256, solve_smem, st>>>(b);
   DKV_CUDA_CHECK(cudaGetLastError());
-  fitb_kernel<RP><<<dim3(static_cast<unsigned>(b.d / kCB), 1), 256, 0, st>>>(b);
+  fitb_kernel<RP><<<dim3(static_cast<unsigned>(b.d / kCB), b.n_probs), 256, 0, st>>>(b);
   DKV_CUDA_CHECK(cudaGetLastError());
   {
     const int sm = static_cast<int>(b.d * 4) + d2_smem_fixed<RP, FDT>();
@@ -1783,7 +1784,7 @@ int launch_dense(const Batch &b, int64_t max_probes, cudaStream_t st) {
   }
   if (max_probes > 0) {
     const int bx = static_cast<int>((max_probes + 3) / 4 < 64 ? (max_probes + 3) / 4 : 64);
-    dprobe_kernel<FDT><<<dim3(bx, 1), 128, 0, st>>>(b);
+    dprobe_kernel<FDT><<<dim3(bx, b.n_probs), 128, 0, st>>>(b);
     DKV_CUDA_CHECK(cudaGetLastError());
   }
   return DKV_OK;
@@ -1800,14 +1801,6 @@ int launch_dense_rp(int rp, const Batch &b, int64_t max_probes, cudaStream_t st)
   }
 }
 
-inline Layout dense_layout(int64_t n, int64_t d, int rp) {
-  dkv_kivi_subspace_problem q;
-  memset(&q, 0, sizeof(q));
-  q.base.n_tokens = n;
-  q.n_probes = n;  // unique probe rows never exceed the token count
-  return layout(&q, 1, d, rp);
-}
-
 inline int dense_rp(int rank) { return rank <= 16 ? 16 : (rank + 15) / 16 * 16; }
 
 bool dense_applies(const dkv_subspace_args &a) {
@@ -1821,64 +1814,103 @@ bool dense_applies(const dkv_subspace_args &a) {
   return a.reused_row_stride >= a.d && a.fresh_row_stride >= a.d && a.out_row_stride >= a.d;
 }
 
-// The dense form: DKV_ERR_UNSUPPORTED when the shape or layout is not one it takes.
-int dense_correct(const dkv_subspace_args *a, uint8_t *ws, int64_t ws_bytes, cudaStream_t st) {
-  if (a == nullptr || !dense_applies(*a)) return DKV_ERR_UNSUPPORTED;
-  const int rp = dense_rp(a->rank);
-  const Layout L = dense_layout(a->n_tokens, a->d, rp);
+// problems of one dense batch: all dense-applicable, one d and fresh dtype, at most
+// kMaxProblems; their padded rank
+bool dense_batch_ok(const dkv_subspace_args *a, int np, int &rp) {
+  if (a == nullptr || np <= 0 || np > kMaxProblems) return false;
+  rp = 16;
+  for (int i = 0; i < np; ++i) {
+    if (!dense_applies(a[i]) || a[i].d != a[0].d || a[i].kv_dtype != a[0].kv_dtype) return false;
+    rp = std::max(rp, dense_rp(a[i].rank));
+  }
+  return true;
+}
+
+inline Layout dense_layout(const dkv_subspace_args *a, int np, int rp) {
+  std::vector<dkv_kivi_subspace_problem> q(np);
+  for (int i = 0; i < np; ++i) {
+    memset(&q[i], 0, sizeof(q[i]));
+    q[i].base.n_tokens = a[i].n_tokens;
+    q[i].n_probes = a[i].n_tokens;  // unique probe rows never exceed the token count
+  }
+  return layout(q.data(), np, a[0].d, rp);
+}
+
+// The dense form over `np` problems: DKV_ERR_UNSUPPORTED when one of them is not a shape or
+// layout it takes (the caller then runs them on the general kernels).
+int dense_correct(const dkv_subspace_args *a, int np, uint8_t *ws, int64_t ws_bytes, cudaStream_t st) {
+  int rp = 16;
+  if (!dense_batch_ok(a, np, rp)) return DKV_ERR_UNSUPPORTED;
+  const Layout L = dense_layout(a, np, rp);
   if (ws == nullptr || ws_bytes < L.total || !a16(ws)) return DKV_ERR_UNSUPPORTED;
-  if (a->n_probes < 0 || (a->n_probes > 0 && a->probe_index == nullptr)) return DKV_ERR_INVALID_ARGUMENT;
-  if (a->rank > 0 && a->basis == nullptr) return DKV_ERR_INVALID_ARGUMENT;
+  int64_t max_probes = 0, tiles = 0;
+  for (int i = 0; i < np; ++i) {
+    if (a[i].n_probes < 0 || (a[i].n_probes > 0 && a[i].probe_index == nullptr)) return DKV_ERR_INVALID_ARGUMENT;
+    if (a[i].rank > 0 && a[i].basis == nullptr) return DKV_ERR_INVALID_ARGUMENT;
+    max_probes = std::max<int64_t>(max_probes, a[i].n_probes);
+  }
   static thread_local Batch b;
   memset(&b, 0, sizeof(b));
-  Prob &P = b.probs[0];
-  P.fresh = a->fresh;
-  P.frs = a->fresh_row_stride;
-  P.n = a->n_tokens;
-  P.probes = a->probe_index;
-  P.n_probes = a->n_probes;
-  P.sub_out = a->subspace_out;
-  P.mu_out = a->orth_mu_out;
-  P.mode = DKV_KIVI_PER_TOKEN;
-  // the reference applies the column-space fit only with a basis and at least one probe
-  P.r = (a->n_probes > 0 && a->basis != nullptr) ? a->rank : 0;
-  P.basis = a->basis;
-  P.flag = reinterpret_cast<uint32_t *>(ws + L.flag[0]);
-  P.ucount = reinterpret_cast<int32_t *>(ws + L.ucount[0]);
-  P.sums = reinterpret_cast<float *>(ws + L.sums[0]);
-  P.uprobe = reinterpret_cast<int32_t *>(ws + L.uprobe[0]);
-  P.rhs = reinterpret_cast<float *>(ws + L.rhs[0]);
-  P.dist = reinterpret_cast<float *>(ws + L.dist[0]);
-  P.part = reinterpret_cast<float *>(ws + L.part[0]);
-  P.ginv = reinterpret_cast<float *>(ws + L.ginv[0]);
-  P.mu = reinterpret_cast<float *>(ws + L.mu[0]);
-  P.subv = reinterpret_cast<float *>(ws + L.subv[0]);
-  P.b1 = reinterpret_cast<__nv_bfloat16 *>(ws + L.b1[0]);
-  P.b1l = reinterpret_cast<__nv_bfloat16 *>(ws + L.b1l[0]);
-  P.b2 = reinterpret_cast<__nv_bfloat16 *>(ws + L.b2[0]);
-  P.bb = reinterpret_cast<float *>(ws + L.bb[0]);
-  P.reused = a->reused;
-  P.rrs = a->reused_row_stride;
-  P.out = a->corrected;
-  P.ors = a->out_row_stride;
-  P.odt = a->out_dtype;
-  P.tw = a->token_weights;
-  P.tile0 = 0;
-  DKV_CUDA_CHECK(cudaMemsetAsync(ws + L.zero_begin, 0, L.zero_end - L.zero_begin, st));
-  b.n_probs = 1;
-  b.d = a->d;
-  b.n_tiles = (a->n_tokens + kTM - 1) / kTM;
-  b.status = nullptr;
-  switch (a->kv_dtype) {
-    case DKV_BF16: return launch_dense_rp<DKV_BF16>(rp, b, a->n_probes, st);
-    case DKV_F16: return launch_dense_rp<DKV_F16>(rp, b, a->n_probes, st);
-    default: return launch_dense_rp<DKV_F32>(rp, b, a->n_probes, st);
+  for (int i = 0; i < np; ++i) {
+    Prob &P = b.probs[i];
+    P.fresh = a[i].fresh;
+    P.frs = a[i].fresh_row_stride;
+    P.n = a[i].n_tokens;
+    P.probes = a[i].probe_index;
+    P.n_probes = a[i].n_probes;
+    P.sub_out = a[i].subspace_out;
+    P.mu_out = a[i].orth_mu_out;
+    P.mode = DKV_KIVI_PER_TOKEN;
+    // the reference applies the column-space fit only with a basis and at least one probe
+    P.r = (a[i].n_probes > 0 && a[i].basis != nullptr) ? a[i].rank : 0;
+    P.basis = a[i].basis;
+    P.flag = reinterpret_cast<uint32_t *>(ws + L.flag[i]);
+    P.ucount = reinterpret_cast<int32_t *>(ws + L.ucount[i]);
+    P.sums = reinterpret_cast<float *>(ws + L.sums[i]);
+    P.uprobe = reinterpret_cast<int32_t *>(ws + L.uprobe[i]);
+    P.rhs = reinterpret_cast<float *>(ws + L.rhs[i]);
+    P.dist = reinterpret_cast<float *>(ws + L.dist[i]);
+    P.part = reinterpret_cast<float *>(ws + L.part[i]);
+    P.ginv = reinterpret_cast<float *>(ws + L.ginv[i]);
+    P.mu = reinterpret_cast<float *>(ws + L.mu[i]);
+    P.subv = reinterpret_cast<float *>(ws + L.subv[i]);
+    P.b1 = reinterpret_cast<__nv_bfloat16 *>(ws + L.b1[i]);
+    P.b1l = reinterpret_cast<__nv_bfloat16 *>(ws + L.b1l[i]);
+    P.b2 = reinterpret_cast<__nv_bfloat16 *>(ws + L.b2[i]);
+    P.bb = reinterpret_cast<float *>(ws + L.bb[i]);
+    P.reused = a[i].reused;
+    P.rrs = a[i].reused_row_stride;
+    P.out = a[i].corrected;
+    P.ors = a[i].out_row_stride;
+    P.odt = a[i].out_dtype;
+    P.tw = a[i].token_weights;
+    P.tile0 = tiles;
+    tiles += (P.n + kTM - 1) / kTM;
   }
+  if (tiles > 0x7fffffffLL) return DKV_ERR_UNSUPPORTED;
+  DKV_CUDA_CHECK(cudaMemsetAsync(ws + L.zero_begin, 0, L.zero_end - L.zero_begin, st));
+  b.n_probs = np;
+  b.d = a[0].d;
+  b.n_tiles = tiles;
+  b.status = nullptr;
+  switch (a[0].kv_dtype) {
+    case DKV_BF16: return launch_dense_rp<DKV_BF16>(rp, b, max_probes, st);
+    case DKV_F16: return launch_dense_rp<DKV_F16>(rp, b, max_probes, st);
+    default: return launch_dense_rp<DKV_F32>(rp, b, max_probes, st);
+  }
+}
+
+int dense_correct(const dkv_subspace_args *a, uint8_t *ws, int64_t ws_bytes, cudaStream_t st) {
+  return dense_correct(a, 1, ws, ws_bytes, st);
 }
 
 int64_t dense_workspace_bytes(int64_t n, int64_t d, int rank) {
   if (n <= 0 || d <= 0 || d % kCB || rank < 0 || rank > kMaxRank) return 0;
-  return dense_layout(n, d, dense_rp(rank)).total;
+  dkv_subspace_args a;
+  memset(&a, 0, sizeof(a));
+  a.n_tokens = n;
+  a.d = d;
+  return dense_layout(&a, 1, dense_rp(rank)).total;
 }
 
 }  // namespace ksub
@@ -1886,6 +1918,20 @@ int64_t dense_workspace_bytes(int64_t n, int64_t d, int rank) {
 
 using namespace dkv;
 using namespace dkv::ksub;
+
+extern "C" int dkv_subspace_correct_batched_workspace_bytes(const dkv_subspace_args *args, int32_t n,
+                                                           int64_t *bytes) {
+  int rp = 16;
+  if (bytes == nullptr || !dense_batch_ok(args, n, rp)) return DKV_ERR_UNSUPPORTED;
+  *bytes = dense_layout(args, n, rp).total;
+  return DKV_OK;
+}
+
+extern "C" int dkv_subspace_correct_batched(const dkv_subspace_args *args, int32_t n, void *workspace,
+                                            int64_t workspace_bytes, dkv_stream_t stream) {
+  return dense_correct(args, n, static_cast<uint8_t *>(workspace), workspace_bytes,
+                       static_cast<cudaStream_t>(stream));
+}
 
 extern "C" int dkv_kivi_subspace_workspace_bytes(const dkv_kivi_subspace_problem *problems, int32_t n_problems,
                                                  int64_t *bytes) {

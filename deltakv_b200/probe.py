@@ -22,7 +22,7 @@ from torch import Tensor
 
 from deltakv_b200 import _lib as L
 from deltakv_b200 import ops
-from deltakv_b200.subspace import subspace_correct
+from deltakv_b200.subspace import subspace_correct_batched
 from deltakv_b200.types import KVCache, LowRankKVPatch
 
 
@@ -170,15 +170,21 @@ def apply_probe_to_cache(kv, fresh_layers: dict, probe_index: Tensor, blend_thre
     patches: dict[int, LowRankKVPatch] = {}
     extra_all: list[Tensor] = []
     k_bases = _k_bases(out, fresh_layers, probe_index, layer_deltas, subspace_rank, skip_layers)
-    for l, (fk, fv) in fresh_layers.items():
-        if skip_layers is not None and l in skip_layers:
-            continue
-        rk, rv = out.k[l], out.v[l]
+    # every layer's K and V correction in one batched call (each reads only its own layer)
+    layers = [l for l in fresh_layers if skip_layers is None or l not in skip_layers]
+    probs = []
+    for l in layers:
+        fk, fv = fresh_layers[l]
         layer = None if layer_deltas is None else layer_deltas.get(l)
         k_b, v_b = bases_for_layer(layer)
         k_rank = int(k_b.shape[1]) if k_b is not None else subspace_rank
-        k_c, _, _ = subspace_correct(rk, fk, probe_index, basis=k_bases.get(l), rank=k_rank)
-        v_c, _, _ = subspace_correct(rv, fv, probe_index, basis=v_b, rank=subspace_rank)
+        probs.append(dict(reused=out.k[l], fresh=fk, probe_index=probe_index, basis=k_bases.get(l), rank=k_rank))
+        probs.append(dict(reused=out.v[l], fresh=fv, probe_index=probe_index, basis=v_b, rank=subspace_rank))
+    corrected = subspace_correct_batched(probs)
+    for j, l in enumerate(layers):
+        fk, fv = fresh_layers[l]
+        rk, rv = out.k[l], out.v[l]
+        k_c, v_c = corrected[2 * j][0], corrected[2 * j + 1][0]
         gated = probe_layers is None or l in probe_layers
         if gated:
             extra = residual_gate(rk, k_c, fk, probe_index, blend_threshold, blend_max_ratio)

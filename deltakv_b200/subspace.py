@@ -358,12 +358,10 @@ def _rows(t: Tensor) -> Tensor:
     return r
 
 
-def subspace_correct(reused: Tensor, fresh: Tensor, probe_index: Tensor, *, basis: Tensor | None = None,
-                     rank: int = 8, token_weights: Tensor | None = None) -> tuple[Tensor, Tensor, Tensor]:
-    """Correct ``reused`` toward ``fresh`` in a rank-r subspace plus an orthogonal shift.
-
-    Returns ``(corrected [seq, n_kv, hd], subspace_offset [d], orth_mu [d])`` like the reference.
-    """
+def _prepare(reused: Tensor, fresh: Tensor, probe_index: Tensor, basis: Tensor | None, rank: int,
+             token_weights: Tensor | None):
+    """Checks and device views of one problem: ``(args without workspace, tensors to keep alive,
+    (corrected, subspace, orth_mu, shape, result dtype))``."""
     ops._require_cuda(reused, fresh)
     seq, n_kv, hd = reused.shape
     dev = reused.device
@@ -399,16 +397,65 @@ def subspace_correct(reused: Tensor, fresh: Tensor, probe_index: Tensor, *, basi
     tw = None
     if token_weights is not None:
         tw = token_weights.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
-    nbytes = workspace_bytes(seq, d, r)
-    ws = _workspace(dev, nbytes)
     args = L.SubspaceArgs(
         reused=rf.data_ptr(), fresh=ff.data_ptr(), kv_dtype=ops.dkv_dtype(rf.dtype), n_tokens=seq, d=d,
         reused_row_stride=rf.stride(0), fresh_row_stride=ff.stride(0),
         probe_index=idx.data_ptr() if idx.numel() else None, n_probes=idx.numel(),
         basis=ops.ptr(b32), rank=r, token_weights=ops.ptr(tw),
         corrected=corr.data_ptr(), out_dtype=ops.dkv_dtype(out_dtype), out_row_stride=corr.stride(0),
-        subspace_out=sub.data_ptr(), orth_mu_out=mu.data_ptr(), workspace=ws.data_ptr(), workspace_bytes=ws.numel(),
+        subspace_out=sub.data_ptr(), orth_mu_out=mu.data_ptr(), workspace=None, workspace_bytes=0,
     )
-    L.check(L.lib().dkv_subspace_correct(C.byref(args), ops.stream_ptr()), "dkv_subspace_correct")
-    res_dtype = reused.dtype
+    return args, (rf, ff, idx, b32, tw), (corr, sub, mu, (seq, n_kv, hd), reused.dtype)
+
+
+def _finish(out):
+    corr, sub, mu, (seq, n_kv, hd), res_dtype = out
     return corr.view(seq, n_kv, hd).to(res_dtype), sub.to(res_dtype), mu.to(res_dtype)
+
+
+def _run_one(args, dev) -> None:
+    nbytes = workspace_bytes(args.n_tokens, args.d, args.rank)
+    ws = _workspace(dev, nbytes)
+    args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+    L.check(L.lib().dkv_subspace_correct(C.byref(args), ops.stream_ptr()), "dkv_subspace_correct")
+
+
+def subspace_correct(reused: Tensor, fresh: Tensor, probe_index: Tensor, *, basis: Tensor | None = None,
+                     rank: int = 8, token_weights: Tensor | None = None) -> tuple[Tensor, Tensor, Tensor]:
+    """Correct ``reused`` toward ``fresh`` in a rank-r subspace plus an orthogonal shift.
+
+    Returns ``(corrected [seq, n_kv, hd], subspace_offset [d], orth_mu [d])`` like the reference.
+    """
+    args, keep, out = _prepare(reused, fresh, probe_index, basis, rank, token_weights)
+    _run_one(args, reused.device)
+    return _finish(out)
+
+
+MAX_BATCH = 112  # problems per batched launch set
+
+
+def subspace_correct_batched(problems: list[dict]) -> list[tuple[Tensor, Tensor, Tensor]]:
+    """:func:`subspace_correct` for many problems (keyword dicts of its arguments: ``reused``,
+    ``fresh``, ``probe_index``, optional ``basis``, ``rank``, ``token_weights``) in one set of
+    launches (``dkv_subspace_correct_batched``) — the per-layer K / V loop of the reference's
+    apply_probe_to_cache (src/deltakv/patches/probe.py:112-165).  Problems the batched form
+    does not take (d not a multiple of 32, unaligned rows, mixed d or dtype) run one by one."""
+    if not problems:
+        return []
+    preps = [_prepare(p["reused"], p["fresh"], p["probe_index"], p.get("basis"), p.get("rank", 8),
+                      p.get("token_weights")) for p in problems]
+    dev = problems[0]["reused"].device
+    for lo in range(0, len(preps), MAX_BATCH):
+        chunk = preps[lo:lo + MAX_BATCH]
+        arr = (L.SubspaceArgs * len(chunk))(*[a for a, _, _ in chunk])
+        nbytes = C.c_int64()
+        rc = L.lib().dkv_subspace_correct_batched_workspace_bytes(arr, len(chunk), C.byref(nbytes))
+        if rc == L.DKV_ERR_UNSUPPORTED:
+            for a, _, _ in chunk:
+                _run_one(a, dev)
+            continue
+        L.check(rc, "dkv_subspace_correct_batched_workspace_bytes")
+        ws = _workspace(dev, nbytes.value)
+        L.check(L.lib().dkv_subspace_correct_batched(arr, len(chunk), ws.data_ptr(), ws.numel(), ops.stream_ptr()),
+                "dkv_subspace_correct_batched")
+    return [_finish(out) for _, _, out in preps]

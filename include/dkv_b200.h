@@ -11,6 +11,8 @@
  *   dkv_gather_paged       deltakv.paged.gather_from_paged           src/deltakv/paged.py:46-70
  *   dkv_pack_exact_factors LowRankFactors.codes/.apply operands      src/deltakv/deltas/factors.py:61-67
  *   dkv_subspace_correct   deltakv.patches.subspace.subspace_correct src/deltakv/patches/subspace.py:45-106
+ *   dkv_subspace_correct_batched  the per-layer loop over it in apply_probe_to_cache
+ *                          src/deltakv/patches/probe.py:112-165
  *   dkv_subspace_probe_residual  the probe residual R[P] whose SVD is svd_basis's input
  *                          src/deltakv/patches/subspace.py:37-42,69-73
  *   dkv_kivi_*             KIVI int4 cache (the reference has only the fake-quant
@@ -500,6 +502,19 @@ typedef struct dkv_subspace_args {
 
 int dkv_subspace_workspace_bytes(int64_t n_tokens, int64_t d, int32_t rank, int64_t *bytes);
 int dkv_subspace_correct(const dkv_subspace_args *args, dkv_stream_t stream);
+/*
+ * n independent dkv_subspace_correct problems in one set of launches — the reference's
+ * per-layer K / V loop of apply_probe_to_cache (src/deltakv/patches/probe.py:112-165) as one
+ * call.  Every problem: n_tokens > 0, d a multiple of 32 and the same for all, the same
+ * kv_dtype, 16-byte aligned reused / fresh / corrected with rows of a multiple of 16 bytes,
+ * rank <= 64; at most 112 problems.  Otherwise both functions return DKV_ERR_UNSUPPORTED and
+ * nothing runs (call dkv_subspace_correct per problem instead).  Each problem's own
+ * workspace fields are ignored: the call uses `workspace`, at least
+ * dkv_subspace_correct_batched_workspace_bytes(args, n) bytes, 16-byte aligned.
+ */
+int dkv_subspace_correct_batched_workspace_bytes(const dkv_subspace_args *args, int32_t n, int64_t *bytes);
+int dkv_subspace_correct_batched(const dkv_subspace_args *args, int32_t n, void *workspace,
+                                 int64_t workspace_bytes, dkv_stream_t stream);
 /*
  * dkv_subspace_correct without a caller workspace and without any allocation.  It has no
  * counterpart in the reference; it exists for callers that cannot allocate device memory

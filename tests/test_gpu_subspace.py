@@ -84,3 +84,35 @@ def test_subspace_errors(cuda):
         dkv.subspace_correct(x, x + 1, torch.tensor([0, 1], device=cuda), basis=torch.randn(5, 2, device=cuda))
     with pytest.raises(IndexError):
         dkv.subspace_correct(x, x + 1, torch.tensor([0, 10], device=cuda), basis=torch.randn(16, 2, device=cuda))
+
+
+def test_subspace_batched_matches_single_calls(cuda):
+    """One batched call over problems of mixed rank, dtype and weights gives the single calls'
+    results; a batch the batched form does not take (d = 16) runs one problem at a time."""
+    gen = torch.Generator().manual_seed(31)
+    probs, d = [], 256
+    for j, (r, dt, weights) in enumerate([(8, torch.bfloat16, False), (64, torch.float32, True),
+                                          (0, torch.float16, False), (16, torch.bfloat16, False)]):
+        n = 300 + 97 * j
+        reused = torch.randn(n, 4, 64, generator=gen).to(dt)
+        fresh = (reused.float() + 0.1 * torch.randn(n, 4, 64, generator=gen)).to(dt)
+        probes = torch.unique(torch.randperm(n, generator=gen)[: n // 8])
+        probs.append(dict(reused=reused.to(cuda), fresh=fresh.to(cuda), probe_index=probes.to(cuda),
+                          basis=(torch.randn(d, r, generator=gen) / 16).to(cuda) if r else None, rank=max(r, 4),
+                          token_weights=torch.rand(n, generator=gen).to(cuda) if weights else None))
+    for group in (probs[:2], [probs[0], probs[3]]):  # same dtype per batched launch; mixed falls back
+        got = dkv.subspace_correct_batched(group)
+        for p, (corr, sub, mu) in zip(group, got):
+            ref = dkv.subspace_correct(p["reused"], p["fresh"], p["probe_index"], basis=p["basis"],
+                                       rank=p["rank"], token_weights=p["token_weights"])
+            # the probe sums are atomics over a grid sized by the batch: equal up to summation
+            # order (fp32 ~1e-7, which can move a 16-bit output across a rounding boundary)
+            tol = 1e-5 if p["reused"].dtype == torch.float32 else 1e-4
+            for a, b in zip((corr, sub, mu), ref):
+                a, b = a.float().cpu().numpy(), b.float().cpu().numpy()
+                assert rel_l2(a, b) < tol, rel_l2(a, b)
+    small = [dict(reused=torch.randn(40, 2, 8, device=cuda), fresh=torch.randn(40, 2, 8, device=cuda),
+                  probe_index=torch.tensor([1, 5, 9], device=cuda), rank=2)]
+    got = dkv.subspace_correct_batched(small)
+    ref = dkv.subspace_correct(small[0]["reused"], small[0]["fresh"], small[0]["probe_index"], rank=2)
+    assert torch.allclose(got[0][0], ref[0], atol=1e-5)

@@ -59,7 +59,8 @@ def parse(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="llama8b-exact",
-                    choices=["llama8b-exact", "smollm2-exact", "rl-dense", "multi-lora-kivi", "analytic"])
+                    choices=["llama8b-exact", "smollm2-exact", "rl-dense", "multi-lora-kivi", "dense-subspace",
+                             "analytic"])
     ap.add_argument("--shard", default="layer", choices=["layer", "request"],
                     help="N>1 split of the exact / dense routes: layers of one fixed cache (strong "
                          "scaling) or a request shard of the same size per rank (weak scaling)")
@@ -1364,6 +1365,210 @@ def run_kivi_reference(args) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# subspace route on a dense bf16 cache: the probe path's per-layer K / V correction
+# ---------------------------------------------------------------------------
+DSUB_METRIC = "patched token·layers/s (subspace route on a bf16 KV cache, Llama-8B shape)"
+
+
+class DsubGeo:
+    layers, seq_len, n_kv, hd, rank, probe_ratio = 32, 32768, 8, 128, 16, 0.10
+
+
+# K and V per token·layer: read reused + fresh, write corrected, bf16, d = n_kv * hd
+DSUB_BYTES_PER_UNIT = 2 * 3 * DsubGeo.n_kv * DsubGeo.hd * 2
+DSUB_WORKLOAD = ("Subspace route (subspace_correct) on a dense bf16 KV cache, Llama-3-8B shape: 32 layers x (K, V), "
+                 "8 KV heads x 128, one 32768-token sequence, rank-16 bases (V: the adapter's LoRA B; K: a given "
+                 "top-16 basis), 10 % probes; each rank's layers in one dkv_subspace_correct_batched call per step")
+
+
+def make_dsub_problems(args, dist: Dist, layer_ids) -> list[dict]:
+    """Per layer a K and a V problem from the layer's own seed: reused ~ N(0, 1) bf16, fresh =
+    reused + codes B^T (B orthonormal, rank 16) + 1 % noise, bf16; one shared probe set."""
+    G = DsubGeo
+    d, n, dev = G.n_kv * G.hd, args.seq_len, dist.dev
+    pg = torch.Generator(device=dev).manual_seed(4999)
+    probes = torch.randperm(n, generator=pg, device=dev)[: int(G.probe_ratio * n)].sort().values
+    probs = []
+    for l in layer_ids:
+        gen = torch.Generator(device=dev).manual_seed(5000 + 7919 * l)
+        for _ in range(2):
+            reused = torch.randn(n, G.n_kv, G.hd, generator=gen, device=dev).to(torch.bfloat16)
+            B = torch.linalg.qr(torch.randn(d, G.rank, generator=gen, device=dev))[0].contiguous()
+            codes = torch.randn(n, G.rank, generator=gen, device=dev) * 0.3
+            noise = 0.01 * torch.randn(n, d, generator=gen, device=dev)
+            fresh = (reused.float().view(n, d) + codes @ B.T + noise).view(n, G.n_kv, G.hd).to(torch.bfloat16)
+            del codes, noise
+            probs.append(dict(reused=reused, fresh=fresh, probe_index=probes, basis=B, rank=G.rank))
+    return probs
+
+
+def dsub_parity(probs) -> dict:
+    """One problem of the timed batch (layer 0's V) recomputed by a plain PyTorch fp32
+    restatement of subspace_correct (src/deltakv/patches/subspace.py:45-106) and compared."""
+    import deltakv_b200 as dkv
+
+    p = probs[1]
+    got = dkv.subspace_correct_batched([p])[0][0].float()
+    rf, ff = p["reused"].float().flatten(1), p["fresh"].float().flatten(1)
+    idx, B = p["probe_index"], p["basis"]
+    R = ff - rf
+    codes = torch.linalg.solve(B.T @ B + 1e-6 * torch.eye(B.shape[1], device=B.device), (R @ B).T).T
+    fitted = codes @ B.T
+    mu = (R[idx] - fitted[idx]).mean(0)
+    dist_ = R.norm(dim=-1)
+    w = (dist_ / dist_.mean().clamp_min(1e-8)).clamp(max=1.0)
+    ref = rf + fitted + w[:, None] * mu[None]
+    ref[idx] = ff[idx]
+    ref = ref.to(torch.bfloat16).float()
+    err = float((got.flatten(1) - ref).norm() / ref.norm())
+    return {"corrected_rel_l2": err, "tolerance": 2e-3, "pass": err < 2e-3,
+            "sample": "layer 0, V (32768 tokens)", "reference": "plain PyTorch fp32 restatement of subspace_correct"}
+
+
+def dsub_cpu_sample(seconds: float, n: int = 4096) -> dict:
+    """Oracle port of subspace_correct on (layer, K|V) items of `n` tokens, one per thread."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from threadpoolctl import threadpool_limits
+
+    from oracle import subspace as OS
+
+    G = DsubGeo
+    d = G.n_kv * G.hd
+    rng = np.random.default_rng(11)
+    reused = rng.standard_normal((n, d), dtype=np.float32)
+    B = np.linalg.qr(rng.standard_normal((d, G.rank)))[0].astype(np.float32)
+    fresh = (reused + (rng.standard_normal((n, G.rank), dtype=np.float32) * 0.3) @ B.T).astype(np.float32)
+    probes = np.sort(rng.permutation(n)[: int(G.probe_ratio * n)])
+    threads = host_threads()
+
+    def item():
+        OS.subspace_correct(reused.reshape(n, G.n_kv, G.hd), fresh.reshape(n, G.n_kv, G.hd), probes, basis=B,
+                            rank=G.rank)
+        return n
+
+    deadline = time.perf_counter() + seconds
+    lock = threading.Lock()
+    done = [0]
+
+    def worker(_):
+        u = 0
+        while time.perf_counter() < deadline:
+            u += item()
+        with lock:
+            done[0] += u
+        return u
+
+    with threadpool_limits(1):
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(threads) as ex:
+            list(ex.map(worker, range(threads)))
+        el = time.perf_counter() - t0
+    # one item is one of a token·layer's two problems (K or V)
+    return {"value": done[0] / 2 / el, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
+            "sample": f"{done[0] // n} (layer, K|V) items of {n} tokens, rank 16, in {el:.1f} s "
+                      f"(oracle numpy port of subspace_correct; {threads} threads)"}
+
+
+def dsub_e2e(args, probs, dist: Dist, stream, n_layers: int = 4) -> dict:
+    """The same metric through the public call from pinned host buffers on a bounded sample:
+    the first `n_layers` layers' reused and fresh K / V copied in, corrected, copied out."""
+    import deltakv_b200 as dkv
+
+    sample = probs[: 2 * min(n_layers, len(probs) // 2)]
+    host = [(p["reused"].cpu().pin_memory(), p["fresh"].cpu().pin_memory()) for p in sample]
+    outs = [torch.empty(p["reused"].shape, dtype=p["reused"].dtype).pin_memory() for p in sample]
+    h2d = sum(a.numel() * a.element_size() + b.numel() * b.element_size() for a, b in host)
+    d2h = sum(o.numel() * o.element_size() for o in outs)
+
+    def step():
+        dev_probs = [dict(p, reused=r.to(dist.dev, non_blocking=True), fresh=f.to(dist.dev, non_blocking=True))
+                     for p, (r, f) in zip(sample, host)]
+        res = dkv.subspace_correct_batched(dev_probs)
+        for o, (corr, _, _) in zip(outs, res):
+            o.copy_(corr, non_blocking=True)
+
+    step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    a.record(stream)
+    for _ in range(reps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = dist.max(a.elapsed_time(b) / reps)
+    units = len(sample) // 2 * args.seq_len * dist.world
+    return {"value": units / (ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": ms, "sample": f"{len(sample) // 2} layers x {args.seq_len} tokens per GPU (K and V), "
+                                        "pinned host buffers"}
+
+
+def run_dsub(args, dist: Dist) -> dict:
+    import deltakv_b200 as dkv
+
+    mine = [l for l in range(args.layers) if l % dist.world == dist.rank]
+    probs = make_dsub_problems(args, dist, mine)
+    units_step = args.layers * args.seq_len
+    stream = torch.cuda.current_stream()
+
+    def step(ev=None):
+        dkv.subspace_correct_batched(probs)
+
+    step()
+    torch.cuda.synchronize()
+    for _ in range(max(0, args.warmup - 1)):
+        step()
+    ms, _, clocks = timed(dist, step, args.steps, kernel_events=False)
+    ms_step = ms / args.steps
+    units_rank = len(mine) * args.seq_len
+    achieved = units_rank * DSUB_BYTES_PER_UNIT / (ms_step / 1e3) / 1e9
+    peak, peak_kind = hbm_peak()
+    parity = dsub_parity(probs) if dist.rank == 0 else None
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+        cpu = dsub_cpu_sample(args.sub_cpu_seconds)
+    e2e = None if args.no_e2e else dsub_e2e(args, probs, dist, stream)
+    del probs
+    torch.cuda.empty_cache()
+    return {
+        "metric": DSUB_METRIC, "value": units_step / (ms_step / 1e3), "unit": UNIT, "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 cache, split-bf16 tensor-core products, fp32",
+        "data": "synthetic",
+        "config": {"workload": DSUB_WORKLOAD, "layers": args.layers, "seq_len": args.seq_len,
+                   "layers_this_gpu": len(mine), "units_per_step": units_step,
+                   "parallelism": f"layer shards x{dist.world}: layer l on rank l mod {dist.world} (strong)",
+                   "l2": f"{units_rank * DSUB_BYTES_PER_UNIT / 1e9:.1f} GB per step per GPU >> 126 MB L2",
+                   "e2e_sample": None if e2e is None else e2e["sample"]},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": None, "peak_source": peak_kind,
+                     "kernel": "subspace route, dense form (flags, pack, pass1, psum, solve, fitb, dpass2, dprobe) "
+                               "over this rank's layers, host wrapper included",
+                     "algorithmic_bytes_per_unit": DSUB_BYTES_PER_UNIT},
+        "parity": parity,
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": args.steps * 8,
+        "clocks": clocks,
+    }
+
+
+def run_dsub_reference(args) -> dict:
+    res = [dsub_cpu_sample(max(2.0, args.cpu_seconds / max(1, args.steps))) for _ in range(args.steps)]
+    value = sum(r["value"] for r in res) / len(res)
+    return {
+        "impl": "reference", "metric": DSUB_METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": DSUB_WORKLOAD, "step": res[0]["sample"]},
+        "cpu_baseline": {**res[0], "value": value},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ---------------------------------------------------------------------------
 # analytic route (Route A): first-order propagation through the stack
 # ---------------------------------------------------------------------------
 ANALYTIC_METRIC = "patched token·layers/s (analytic route, SmolLM2-135M shape)"
@@ -1566,6 +1771,7 @@ DEFAULTS = {
     "smollm2-exact": (Smol135M.layers, Smol135M.seqs, Smol135M.seq_len),
     "rl-dense": (Dense70B.layers, Dense70B.seqs, Dense70B.seq_len),
     "multi-lora-kivi": (KiviGeo.layers, 1, KiviGeo.seq_len),
+    "dense-subspace": (DsubGeo.layers, 1, DsubGeo.seq_len),
     "analytic": (AnalyticGeo.layers, AnalyticGeo.seqs, AnalyticGeo.seq_len),
 }
 
@@ -1592,6 +1798,8 @@ def run_one(args, dist: Dist) -> dict:
         return run_dense(args, dist)
     if w == "multi-lora-kivi":
         return run_kivi(args, dist)
+    if w == "dense-subspace":
+        return run_dsub(args, dist)
     return run_analytic(args, dist)
 
 
@@ -1605,10 +1813,12 @@ def run_reference(args) -> dict:
         return run_dense_reference(args)
     if w == "multi-lora-kivi":
         return run_kivi_reference(args)
+    if w == "dense-subspace":
+        return run_dsub_reference(args)
     return run_analytic_reference(args)
 
 
-SUB_WORKLOADS = ("smollm2-exact", "multi-lora-kivi", "rl-dense", "analytic")
+SUB_WORKLOADS = ("smollm2-exact", "multi-lora-kivi", "rl-dense", "dense-subspace", "analytic")
 
 
 def main(argv=None):

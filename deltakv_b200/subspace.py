@@ -358,21 +358,33 @@ def _rows(t: Tensor) -> Tensor:
     return r
 
 
-def _prepare(reused: Tensor, fresh: Tensor, probe_index: Tensor, basis: Tensor | None, rank: int,
-             token_weights: Tensor | None):
-    """Checks and device views of one problem: ``(args without workspace, tensors to keep alive,
-    (corrected, subspace, orth_mu, shape, result dtype))``."""
-    ops._require_cuda(reused, fresh)
-    seq, n_kv, hd = reused.shape
-    dev = reused.device
+def _probe_rows(probe_index: Tensor, seq: int, dev: torch.device) -> Tensor:
+    """The probe index as int32 rows in [0, seq) (negative entries count from the end, as torch
+    indexing does); out-of-range entries raise the reference's IndexError."""
     idx = probe_index.to(device=dev, dtype=torch.int64).reshape(-1)
     if idx.numel():
         lo, hi = int(idx.min()), int(idx.max())
         if lo < -seq or hi >= seq:
             bad = hi if hi >= seq else lo
             raise IndexError(f"index {bad} is out of bounds for dimension 0 with size {seq}")
-        idx = torch.where(idx < 0, idx + seq, idx)  # torch indexing semantics
-    idx = idx.to(torch.int32).contiguous()
+        idx = torch.where(idx < 0, idx + seq, idx)
+    return idx.to(torch.int32).contiguous()
+
+
+def _prepare(reused: Tensor, fresh: Tensor, probe_index: Tensor, basis: Tensor | None, rank: int,
+             token_weights: Tensor | None, rows_cache: dict | None = None):
+    """Checks and device views of one problem: ``(args without workspace, tensors to keep alive,
+    (corrected, subspace, orth_mu, shape, result dtype))``.  ``rows_cache`` shares one probe
+    index's checked rows between the problems of a batch (one host round trip, not one each)."""
+    ops._require_cuda(reused, fresh)
+    seq, n_kv, hd = reused.shape
+    dev = reused.device
+    key = (probe_index.data_ptr(), probe_index.numel(), probe_index.dtype, seq, str(dev))
+    idx = None if rows_cache is None else rows_cache.get(key)
+    if idx is None:
+        idx = _probe_rows(probe_index, seq, dev)
+        if rows_cache is not None:
+            rows_cache[key] = idx
     rf, ff = _rows(reused), _rows(fresh)
     if ff.dtype != rf.dtype:
         ff = ff.to(rf.dtype)
@@ -442,8 +454,9 @@ def subspace_correct_batched(problems: list[dict]) -> list[tuple[Tensor, Tensor,
     does not take (d not a multiple of 32, unaligned rows, mixed d or dtype) run one by one."""
     if not problems:
         return []
+    rows_cache: dict = {}
     preps = [_prepare(p["reused"], p["fresh"], p["probe_index"], p.get("basis"), p.get("rank", 8),
-                      p.get("token_weights")) for p in problems]
+                      p.get("token_weights"), rows_cache) for p in problems]
     dev = problems[0]["reused"].device
     for lo in range(0, len(preps), MAX_BATCH):
         chunk = preps[lo:lo + MAX_BATCH]

@@ -523,11 +523,14 @@ int dkv_subspace_correct_batched(const dkv_subspace_args *args, int32_t n, void 
  * wait on the allocator).  The scratch is one fixed 16 MiB device array inside this
  * library, present on every GPU that loads it until the process exits; args->workspace
  * and args->workspace_bytes are ignored.
- *   - Limit: the problem's scratch, dkv_subspace_workspace_bytes(n_tokens, d, rank), must
- *     fit in 16 MiB.  That is 4*r + 5 bytes per token (r = rank rounded up to a multiple
- *     of 16) plus a few KB that grow with d: about 64K tokens at rank 64 and 240K tokens at
- *     rank 16 for d = 1024.  Larger problems are rejected with DKV_ERR_WORKSPACE before
- *     anything is launched.
+ *   - Limit: the scratch of one of the two forms must fit in 16 MiB.  The tensor-core form
+ *     (d a multiple of 32, 16-byte rows) needs about 4*r + 12 + (r + 1)/8 bytes per token
+ *     plus 12*r*d + 8*d bytes (r = rank rounded up to a multiple of 16): about 58K tokens
+ *     at rank 64 and 212K at rank 16 for d = 1024; the general form needs 4*r + 5 bytes per
+ *     token plus a few KB: about 64K tokens at rank 64 and 240K at rank 16.  A problem
+ *     between the two limits runs on the general kernels; larger problems are rejected
+ *     with DKV_ERR_WORKSPACE before anything is launched.  (dkv_subspace_workspace_bytes
+ *     reports the larger of the two needs.)
  *   - The first call made while a given device is current looks up the array's device
  *     address (cudaGetSymbolAddress) and caches it; make that first call before any
  *     stream capture on that device.

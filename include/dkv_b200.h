@@ -525,7 +525,7 @@ int dkv_subspace_correct_batched(const dkv_subspace_args *args, int32_t n, void 
  * and args->workspace_bytes are ignored.
  *   - Limit: the scratch of one of the two forms must fit in 16 MiB.  The tensor-core form
  *     (d a multiple of 32, 16-byte rows) needs about 4*r + 12 + (r + 1)/8 bytes per token
- *     plus 12*r*d + 8*d bytes (r = rank rounded up to a multiple of 16): about 58K tokens
+ *     plus about 12*(r + 1)*d bytes (r = rank rounded up to a multiple of 16): about 58K tokens
  *     at rank 64 and 212K at rank 16 for d = 1024; the general form needs 4*r + 5 bytes per
  *     token plus a few KB: about 64K tokens at rank 64 and 240K at rank 16.  A problem
  *     between the two limits runs on the general kernels; larger problems are rejected

@@ -234,6 +234,12 @@ __global__ void pack_kernel(const __grid_constant__ Batch b, int rp) {
 // pass 1
 // ---------------------------------------------------------------------------------------
 constexpr int kP1Stages = 3;  // per-warp staging depth (blocks in flight)
+// the dense form stages two rows per token (fresh and reused): two blocks deep keeps the
+// shared memory of five CTAs per SM
+template <bool DENSE>
+constexpr int p1_stages() {
+  return DENSE ? 2 : kP1Stages;
+}
 constexpr int kBSlots = 4;    // CTA-wide ring of basis fragment blocks (both passes)
 
 // Bounded wait on a phase without the abort word (draining copies already issued).
@@ -279,7 +285,7 @@ constexpr int p1_bq_bytes() {  // one block's basis fragments: high terms, then 
 }
 template <int RP, int FDT, int MODE, bool DENSE = false>
 constexpr int p1_smem_bytes() {
-  return kBSlots * p1_bq_bytes<RP>() + kWarps * kP1Stages * static_cast<int>(sizeof(P1Stage<FDT, DENSE>)) +
+  return kBSlots * p1_bq_bytes<RP>() + kWarps * p1_stages<DENSE>() * static_cast<int>(sizeof(P1Stage<FDT, DENSE>)) +
          (MODE == DKV_KIVI_PER_TOKEN && !DENSE ? kWarps * static_cast<int>(sizeof(P1VStage)) : 0) +
          2 * kBSlots * 8 + 16;
 }
@@ -307,8 +313,9 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
   extern __shared__ __align__(16) unsigned char p1_smem[];
   unsigned char *const bq_ring = p1_smem;
   unsigned char *sp = p1_smem + kBSlots * BQ;
-  Stage *const ring = reinterpret_cast<Stage *>(sp) + warp * kP1Stages;
-  sp += kWarps * kP1Stages * sizeof(Stage);
+  constexpr int S1 = p1_stages<DENSE>();
+  Stage *const ring = reinterpret_cast<Stage *>(sp) + warp * S1;
+  sp += kWarps * S1 * sizeof(Stage);
   P1VStage *const vst = reinterpret_cast<P1VStage *>(sp) + warp;
   if constexpr (!kmode && !DENSE) sp += kWarps * sizeof(P1VStage);
   uint64_t *const bq_full = reinterpret_cast<uint64_t *>(sp);
@@ -368,10 +375,10 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
   const bool vstage = !DENSE && !kmode && n_blocks % 4 == 0 && P.szrs % 4 == 0;
   constexpr int kFB = Stage::kFB;
   constexpr int kEs = FDT == DKV_F32 ? 4 : 2;
-  // per-warp staging ring (cp.async, kP1Stages - 1 blocks ahead)
+  // per-warp staging ring (cp.async, S1 - 1 blocks ahead)
   auto issue = [&](int cb) {
     if (cb < n_blocks) {
-      Stage &S = ring[cb % kP1Stages];
+      Stage &S = ring[cb % S1];
       const int64_t c = static_cast<int64_t>(cb) * kCB + 8 * q;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -406,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
     cp_async_commit();  // possibly empty: keeps the group count per block fixed
   };
 #pragma unroll
-  for (int s0 = 0; s0 < kP1Stages - 1; ++s0) issue(s0);
+  for (int s0 = 0; s0 < S1 - 1; ++s0) issue(s0);
 
   const uint64_t rs_lo = kivi::pair_rescale(0), rs_hi = kivi::pair_rescale(1);
   int cb = 0;
@@ -420,10 +427,10 @@ __global__ void __launch_bounds__(kThreads, p1_min_blocks<RP, MODE>())
         break;
       }
     }
-    issue(cb + kP1Stages - 1);
-    cp_async_wait<kP1Stages - 1>();
+    issue(cb + S1 - 1);
+    cp_async_wait<S1 - 1>();
     __syncwarp();  // the other lanes' copies of this block are visible
-    const Stage &S = ring[cb % kP1Stages];
+    const Stage &S = ring[cb % S1];
     uint64_t ks2[4], kz2[4];  // K: this lane's channels' rescaled scale and zero, in pairs
     if constexpr (kmode && !DENSE) {
       const uint4 sv = S.sz[0][q], zv = S.sz[1][q];

@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
+import weakref
 
 import torch
 from torch import Tensor
@@ -358,9 +359,31 @@ def _rows(t: Tensor) -> Tensor:
     return r
 
 
+_rows_seen: dict[int, tuple] = {}  # id(probe tensor) -> (weakref, version, seq, device, rows)
+
+
 def _probe_rows(probe_index: Tensor, seq: int, dev: torch.device) -> Tensor:
     """The probe index as int32 rows in [0, seq) (negative entries count from the end, as torch
-    indexing does); out-of-range entries raise the reference's IndexError."""
+    indexing does); out-of-range entries raise the reference's IndexError.  The check reads
+    the index on the host; its result is kept for as long as the same tensor lives unmodified
+    (its in-place version counter), so a caller that passes one probe set to many calls pays
+    the host round trip once."""
+    key = id(probe_index)
+    hit = _rows_seen.get(key)
+    if (hit is not None and hit[0]() is probe_index and hit[1] == probe_index._version and hit[2] == seq
+            and hit[3] == str(dev)):
+        return hit[4]
+    rows = _check_probe_rows(probe_index, seq, dev)
+    if len(_rows_seen) >= 64:
+        _rows_seen.clear()
+    try:
+        _rows_seen[key] = (weakref.ref(probe_index), probe_index._version, seq, str(dev), rows)
+    except TypeError:  # not weak-referenceable: no caching
+        pass
+    return rows
+
+
+def _check_probe_rows(probe_index: Tensor, seq: int, dev: torch.device) -> Tensor:
     idx = probe_index.to(device=dev, dtype=torch.int64).reshape(-1)
     if idx.numel():
         lo, hi = int(idx.min()), int(idx.max())

@@ -1168,6 +1168,54 @@ def kivi_problems(base, adapter, k_bases=None):
     return probs
 
 
+def kivi_parity(base, adapter) -> dict:
+    """One problem of the timed work (the view's layer 0, V) corrected alone into a fresh int4
+    cache and checked against a plain PyTorch fp32 restatement of the composition the oracle
+    pins: KIVI dequantise -> subspace_correct (src/deltakv/patches/subspace.py:45-106) ->
+    KIVI quantise (scale = fp16((max - min) / 15), zero = fp16(min), q = rint((x - zero) /
+    scale) clamped to [0, 15]).  Codes agree except next to rounding ties."""
+    from deltakv_b200 import kivi as K
+
+    view, b = adapter["layers"][0][1], base[0][1]
+    n, d = b.n_tokens, b.d
+    out = K.KiviTensor.empty(n, d, "v", b.codes.device)
+    pb = K.SubspaceProblem(base=b, fresh=view["fresh"], probe_index=adapter["probes"], basis=view["basis"],
+                           rank=adapter["rank"], out=out)
+    K.subspace_correct([pb], check=True)
+
+    def unpack(c):
+        c = c.to(torch.int32)
+        return torch.stack([c & 15, c >> 4], dim=-1).flatten(1).float()
+
+    g = 32
+    reused = (unpack(b.codes).view(n, d // g, g) * b.scale.float()[..., None] + b.zero.float()[..., None]).view(n, d)
+    fresh = view["fresh"].float().view(n, d)
+    idx = torch.unique(adapter["probes"].long())
+    B = view["basis"].float()
+    R = fresh - reused
+    G = (B.double().T @ B.double() + 1e-6 * torch.eye(B.shape[1], device=B.device, dtype=torch.float64))
+    codes = torch.linalg.solve(G, (R @ B).double().T).T.float()
+    fitted = codes @ B.T
+    mu = (R[idx] - fitted[idx]).mean(0)
+    dist_ = R.norm(dim=-1)
+    w = (dist_ / dist_.mean().clamp_min(1e-8)).clamp(max=1.0)
+    corr = reused + fitted + w[:, None] * mu[None]
+    corr[idx] = fresh[idx]
+    grp = corr.view(n, d // g, g)
+    lo, hi = grp.min(-1).values, grp.max(-1).values
+    s16 = ((hi - lo).clamp_min(1e-8) / 15).half()
+    z16 = lo.half()
+    q = torch.where(s16.float()[..., None] > 0, torch.round((grp - z16.float()[..., None]) / s16.float()[..., None]),
+                    torch.zeros_like(grp)).clamp(0, 15).view(n, d)
+    got = unpack(out.codes)
+    codes_eq = float((got == q).float().mean())
+    sz_eq = float(((out.scale == s16) & (out.zero == z16)).float().mean())
+    return {"codes_equal": codes_eq, "scale_zero_equal": sz_eq, "pass": codes_eq >= 0.999,
+            "tolerance": "codes equal on >= 99.9 % (the rest at rounding ties)",
+            "sample": f"view {adapter['id']} (rank {adapter['rank']}), layer 0, V ({n} tokens)",
+            "reference": "plain PyTorch fp32 restatement of dequantise -> subspace_correct -> quantise"}
+
+
 def kivi_e2e(args, base, adapter, dist: Dist, stream, n_layers: int = 4) -> dict:
     """The same metric through the public call from pinned host buffers, on a bounded sample:
     one adapter view's first ``n_layers`` layers — its fresh bf16 K / V copied in, corrected by
@@ -1270,6 +1318,7 @@ def run_kivi(args, dist: Dist) -> dict:
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
         cpu = kivi_cpu_sample(args.sub_cpu_seconds)
+    parity = kivi_parity(base, adapters[0]) if adapters else None
     e2e = None
     if not args.no_e2e and adapters:
         e2e = kivi_e2e(args, base, adapters[0], dist, stream)
@@ -1294,6 +1343,7 @@ def run_kivi(args, dist: Dist) -> dict:
                      "traffic": None, "peak_source": peak_kind,
                      "kernel": "int4 subspace route (flags, pack, pass1 x2, psum, solve, fitb, pass2 x2) per view",
                      "kernel_ms": route_ms, "algorithmic_bytes_per_unit": KIVI_BYTES_PER_UNIT},
+        "parity": parity,
         "cpu_baseline": cpu,
         "e2e": e2e,
         # per view: flags, pack, pass1 K/V, psum, solve, fitb, pass2 K/V (9) + the K bases'

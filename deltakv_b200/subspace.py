@@ -395,10 +395,12 @@ def _check_probe_rows(probe_index: Tensor, seq: int, dev: torch.device) -> Tenso
 
 
 def _prepare(reused: Tensor, fresh: Tensor, probe_index: Tensor, basis: Tensor | None, rank: int,
-             token_weights: Tensor | None, rows_cache: dict | None = None):
+             token_weights: Tensor | None, rows_cache: dict | None = None, sub_mu: tuple | None = None):
     """Checks and device views of one problem: ``(args without workspace, tensors to keep alive,
     (corrected, subspace, orth_mu, shape, result dtype))``.  ``rows_cache`` shares one probe
-    index's checked rows between the problems of a batch (one host round trip, not one each)."""
+    index's checked rows between the problems of a batch (one host round trip, not one each);
+    ``sub_mu`` gives zeroed fp32 ``[d]`` outputs for subspace and orth_mu (views of a batch's
+    arrays) instead of two fresh ones."""
     ops._require_cuda(reused, fresh)
     seq, n_kv, hd = reused.shape
     dev = reused.device
@@ -427,8 +429,11 @@ def _prepare(reused: Tensor, fresh: Tensor, probe_index: Tensor, basis: Tensor |
         b32, r = None, 0
     out_dtype = reused.dtype if reused.dtype in (torch.float32, torch.float16, torch.bfloat16) else torch.float32
     corr = torch.empty(seq, d, dtype=out_dtype, device=dev)
-    sub = torch.zeros(d, dtype=torch.float32, device=dev)
-    mu = torch.zeros(d, dtype=torch.float32, device=dev)
+    if sub_mu is None:
+        sub = torch.zeros(d, dtype=torch.float32, device=dev)
+        mu = torch.zeros(d, dtype=torch.float32, device=dev)
+    else:
+        sub, mu = sub_mu
     tw = None
     if token_weights is not None:
         tw = token_weights.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
@@ -478,8 +483,22 @@ def subspace_correct_batched(problems: list[dict]) -> list[tuple[Tensor, Tensor,
     if not problems:
         return []
     rows_cache: dict = {}
+    # one zeroed [count, d] array per (d, device) for every problem's subspace and orth_mu
+    # outputs, instead of two small allocations (and fills) per problem
+    groups: dict = {}
+    for i, p in enumerate(problems):
+        r = p["reused"]
+        groups.setdefault((r.shape[-2] * r.shape[-1], str(r.device)), []).append(i)
+    sub_mu = [None] * len(problems)
+    blocks = []
+    for (d, _), ids in groups.items():
+        dev_ = problems[ids[0]]["reused"].device
+        sm = torch.zeros(2, len(ids), d, dtype=torch.float32, device=dev_)
+        blocks.append((ids, sm))
+        for j, i in enumerate(ids):
+            sub_mu[i] = (sm[0, j], sm[1, j])
     preps = [_prepare(p["reused"], p["fresh"], p["probe_index"], p.get("basis"), p.get("rank", 8),
-                      p.get("token_weights"), rows_cache) for p in problems]
+                      p.get("token_weights"), rows_cache, sub_mu[i]) for i, p in enumerate(problems)]
     dev = problems[0]["reused"].device
     for lo in range(0, len(preps), MAX_BATCH):
         chunk = preps[lo:lo + MAX_BATCH]
@@ -494,4 +513,15 @@ def subspace_correct_batched(problems: list[dict]) -> list[tuple[Tensor, Tensor,
         ws = _workspace(dev, nbytes.value)
         L.check(L.lib().dkv_subspace_correct_batched(arr, len(chunk), ws.data_ptr(), ws.numel(), ops.stream_ptr()),
                 "dkv_subspace_correct_batched")
-    return [_finish(out) for _, _, out in preps]
+    # subspace and orth_mu in each problem's dtype: one conversion per block and dtype
+    conv: dict = {}
+    for ids, sm in blocks:
+        for dt in {problems[i]["reused"].dtype for i in ids}:
+            conv[(id(sm), dt)] = sm if dt == torch.float32 else sm.to(dt)
+    results = [None] * len(problems)
+    for ids, sm in blocks:
+        for j, i in enumerate(ids):
+            corr, _, _, (seq, n_kv, hd), res_dtype = preps[i][2]
+            c = conv[(id(sm), res_dtype)]
+            results[i] = (corr.view(seq, n_kv, hd).to(res_dtype), c[0, j], c[1, j])
+    return results

@@ -149,7 +149,13 @@ def probe_residuals(bases: list[KiviTensor], freshes: list[Tensor], probe_indice
         raise ValueError("no caches")
     fr = [_rows(f) for f in freshes]
     dev = fr[0].device
-    rows = [p.to(device=dev, dtype=torch.int32).contiguous() for p in probe_indices]
+    conv: dict = {}  # one int32 copy per distinct probe tensor
+    rows = []
+    for p in probe_indices:
+        key = (p.data_ptr(), p.numel(), p.dtype)
+        if key not in conv:
+            conv[key] = p.to(device=dev, dtype=torch.int32).contiguous()
+        rows.append(conv[key])
     m, d = rows[0].numel(), bases[0].d
     if any(r.numel() != m for r in rows) or any(f.dtype != fr[0].dtype for f in fr):
         raise ValueError("probe_residuals: every job needs the same probe count and fresh dtype")
@@ -202,13 +208,18 @@ def subspace_correct(problems: list[SubspaceProblem], *, stats: bool = False, ch
     descs = []
     results = []
     svd = k_bases(problems) if bases is None else bases
+    probe_rows: dict = {}  # one int32 copy per distinct probe tensor of the call
     for i, pb in enumerate(problems):
         fresh = _rows(pb.fresh)
         ops._require_cuda(fresh, pb.probe_index)
         n, d = pb.base.n_tokens, pb.base.d
         if fresh.shape != (n, d):
             raise ValueError(f"fresh {tuple(fresh.shape)} does not match the int4 base ({n}, {d})")
-        probes = pb.probe_index.to(device=dev, dtype=torch.int32).contiguous()
+        pk = (pb.probe_index.data_ptr(), pb.probe_index.numel(), pb.probe_index.dtype)
+        probes = probe_rows.get(pk)
+        if probes is None:
+            probes = pb.probe_index.to(device=dev, dtype=torch.int32).contiguous()
+            probe_rows[pk] = probes
         basis = pb.basis if pb.basis is not None else svd.get(i)  # svd_basis keeps at least rank 1
         if basis is not None:
             if basis.shape[0] != d:

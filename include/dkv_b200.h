@@ -481,6 +481,9 @@ int dkv_kivi_subspace_correct(const dkv_kivi_subspace_problem *problems, int32_t
  * w * mean_P(R), subspace = 0.  basis is fp32 [d, rank] row-major, rank <= 64.
  * subspace_out / orth_mu_out (fp32 [d]) may be NULL.  Scratch: workspace of at least
  * dkv_subspace_workspace_bytes(n_tokens, d, rank); nothing in it needs clearing.
+ * probe_index entries must lie in [0, n_tokens) (checked by the Python drop-in; the kernels
+ * skip others).  These calls have no status word: a device-side wait that gives up (bounded,
+ * ~1-2 s; it happens only on a broken device) leaves the outputs undefined unreported.
  */
 typedef struct dkv_subspace_args {
   const void *reused, *fresh;

@@ -276,7 +276,7 @@ class Smol135M(Llama8B):
     workload = ("SmolLM2-135M-shaped exact patch: 30 layers, d=576, 3 KV heads x 64, 32 seqs x 2048 tokens, "
                 "rank-8 k/v LoRA (rel. norm 1e-2), f16 stored X + power-of-two row scale + per-row sum of squared "
                 "codes, RMSNorm folded, RoPE (theta 1e4), bf16 paged KV block 16, permuted block table")
-    profile = None
+    profile = "smollm2_exact_patch.md"
     dtype = "f16 tensor-core products, fp32 accumulate (f16 X, bf16 pages)"
 
 

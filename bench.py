@@ -236,6 +236,76 @@ def cpu_pool_threads() -> int:
         return cores
 
 
+class torch_threads:
+    """torch's intra-op thread count set to `n` inside the block, restored after"""
+
+    def __init__(self, n: int):
+        self.n = n
+
+    def __enter__(self):
+        self.old = torch.get_num_threads()
+        torch.set_num_threads(self.n)
+
+    def __exit__(self, *exc):
+        torch.set_num_threads(self.old)
+
+
+def _pool_run(item, threads: int, seconds: float | None = None, count: int | None = None):
+    """`item()` (returns units) on `threads` workers, one intra-op thread each, for `seconds` or
+    `count` items; returns (units, elapsed_s)"""
+    from concurrent.futures import ThreadPoolExecutor
+
+    lock = threading.Lock()
+    started = [0]
+    deadline = None if seconds is None else time.perf_counter() + seconds
+
+    def worker(_):
+        u = 0
+        while True:
+            with lock:
+                if count is not None and started[0] >= count:
+                    return u
+                if deadline is not None and time.perf_counter() >= deadline:
+                    return u
+                started[0] += 1
+            u += item()
+
+    with torch_threads(1):
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(threads) as ex:
+            units = sum(ex.map(worker, range(threads)))
+        return units, time.perf_counter() - t0
+
+
+def _serial_run(item, threads: int, seconds: float | None = None, count: int | None = None):
+    """`item()` one after another with `threads` intra-op threads inside each operation"""
+    with torch_threads(threads):
+        t0 = time.perf_counter()
+        units = k = 0
+        while (count is None or k < count) and (seconds is None or time.perf_counter() - t0 < seconds):
+            units += item()
+            k += 1
+        return units, time.perf_counter() - t0
+
+
+HOST_MODES = {"pool": (_pool_run, "one item per thread"),
+              "serial": (_serial_run, "items in turn, every thread inside each operation")}
+
+
+def host_rate(item, threads: int, seconds: float):
+    """Runs `item` for `seconds` the faster of the two ways to spread it over the cores (each
+    warmed up and timed on `threads` items first); returns (units, elapsed_s, mode text)."""
+    rate = {}
+    for mode, (run, _) in HOST_MODES.items():
+        run(item, threads, count=threads)
+        u, el = run(item, threads, count=threads)
+        rate[mode] = u / el
+    mode = max(rate, key=rate.get)
+    run, text = HOST_MODES[mode]
+    u, el = run(item, threads, seconds=seconds)
+    return u, el, text
+
+
 def my_layers(n_layers: int, dist: Dist, shard: str) -> list[int]:
     """Layer l on rank l mod N (layer sharding); every layer on every rank otherwise."""
     if dist.world == 1 or shard != "layer":
@@ -358,10 +428,12 @@ def exact_reference_delta(G, wl, i, r0, r1, rope_tabs):
 
 class CpuSample:
     """A bounded sample of the exact workload on the host: P distinct (layer, sequence)
-    inputs, one private paged K/V per worker thread (a single sequence's blocks)."""
+    inputs, one private paged K/V per worker (a single sequence's blocks).  The work is the
+    reference's exact branch in its own torch CPU operations (`oracle.exact_torch`)."""
 
     def __init__(self, G, n_inputs: int, seq_len: int, seed: int = 5):
         from oracle import exact as OX
+        from oracle import exact_torch as OT
 
         self.G = G
         g = torch.Generator().manual_seed(seed)
@@ -374,68 +446,82 @@ class CpuSample:
             amax = h.abs().amax(-1).clamp_min(1e-12)
             sc = (amax / 448.0).float()
             if G.x_kind == "e4m3":
-                xb = (h / sc[:, None]).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+                xb = (h / sc[:, None]).to(torch.float8_e4m3fn).view(torch.uint8)
             else:
-                xb = (h / sc[:, None]).to(torch.float16).numpy()
-            fk = ((torch.randn(G.rank, G.d_model, generator=g) / math.sqrt(G.d_model)).numpy(),
-                  torch.randn(d_kv, G.rank, generator=g).numpy(), s)
-            fv = ((torch.randn(G.rank, G.d_model, generator=g) / math.sqrt(G.d_model)).numpy(),
-                  torch.randn(d_kv, G.rank, generator=g).numpy(), s)
-            w = (1.0 + 0.05 * torch.randn(G.d_model, generator=g)).numpy()
-            self.inputs.append((xb, sc.numpy(), w, fk, fv))
-        self.rope = OX.rope_tables(G.hd, seq_len, G.rope_theta)
+                xb = (h / sc[:, None]).to(torch.float16)
+            fk = (torch.randn(G.rank, G.d_model, generator=g) / math.sqrt(G.d_model),
+                  torch.randn(d_kv, G.rank, generator=g), s)
+            fv = (torch.randn(G.rank, G.d_model, generator=g) / math.sqrt(G.d_model),
+                  torch.randn(d_kv, G.rank, generator=g), s)
+            w = 1.0 + 0.05 * torch.randn(G.d_model, generator=g)
+            self.inputs.append((xb, sc, w, fk, fv))
+        cos_h, sin_h = OX.rope_tables(G.hd, seq_len, G.rope_theta)
+        self.rope = OT.rope_full(torch.from_numpy(cos_h), torch.from_numpy(sin_h), seq_len)
         nblk = (seq_len + G.bs - 1) // G.bs
-        self.table = list(np.random.default_rng(seed).permutation(nblk))
+        self.table = torch.from_numpy(np.random.default_rng(seed).permutation(nblk))
         self.nblk = nblk
 
     def new_pages(self):
         G = self.G
-        rng = np.random.default_rng(0)
+        g = torch.Generator().manual_seed(0)
         shape = (self.nblk, G.bs, G.n_kv, G.hd)
-        return (rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16),
-                rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16))
+        return ((1.0 + torch.rand(shape, generator=g)).to(torch.bfloat16),
+                (1.0 + torch.rand(shape, generator=g)).to(torch.bfloat16))
 
     def patch_one(self, i: int, kp, vp) -> int:
         """The reference's exact branch on one (layer, sequence): dequant -> RMSNorm ->
         exact_kv_patch -> materialize -> scatter_into_paged (K and V).  Returns units."""
-        from oracle import exact as OX
+        from oracle import exact_torch as OT
 
         G = self.G
         xb, s, w, fk, fv = self.inputs[i % len(self.inputs)]
-        x = OX.dequant_x(xb, G.x_kind, s)
-        x = OX.rmsnorm(x, w, G.eps)
-        dk, dv = OX.exact_kv_delta(x, fk, fv, G.n_kv, G.hd, self.rope)
-        OX.scatter_into_paged(dk, kp, self.table, G.bs, kind="bf16")
-        OX.scatter_into_paged(dv, vp, self.table, G.bs, kind="bf16")
+        with torch.no_grad():
+            x = OT.dequant_x(xb, G.x_kind, s)
+            x = OT.rmsnorm(x, w, G.eps)
+            dk, dv = OT.exact_kv_delta(x, fk, fv, G.n_kv, G.hd, self.rope)
+            OT.scatter_into_paged(dk, kp, self.table, G.bs)
+            OT.scatter_into_paged(dv, vp, self.table, G.bs)
         return self.seq_len
 
-    def dequant_share(self, reps: int = 2) -> float:
-        """Fraction of one pair's single-thread time spent in the fp8/f16 dequantisation
-        (which has no counterpart in the reference, whose activations are fp32)."""
-        from oracle import exact as OX
+    def dequant_share(self, threads: int, reps: int = 2) -> float:
+        """Fraction of one pair's time (all `threads` inside each operation) spent in the
+        fp8/f16 dequantisation (which has no counterpart in the reference, whose activations
+        are fp32)."""
+        from oracle import exact_torch as OT
 
         kp, vp = self.new_pages()
         xb, s, *_ = self.inputs[0]
-        t0 = time.perf_counter()
-        for _ in range(reps):
-            OX.dequant_x(xb, self.G.x_kind, s)
-        t_deq = time.perf_counter() - t0
-        t0 = time.perf_counter()
-        for _ in range(reps):
-            self.patch_one(0, kp, vp)
-        return t_deq / (time.perf_counter() - t0)
+        with torch_threads(threads):
+            OT.dequant_x(xb, self.G.x_kind, s)
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                OT.dequant_x(xb, self.G.x_kind, s)
+            t_deq = time.perf_counter() - t0
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                self.patch_one(0, kp, vp)
+            return t_deq / (time.perf_counter() - t0)
 
-    def run(self, threads: int, seconds: float | None = None, pairs: int | None = None):
-        """Process pairs on `threads` workers for `seconds` (or `pairs` pairs); returns
-        (units, elapsed_s)."""
+    def run(self, threads: int, seconds: float | None = None, pairs: int | None = None,
+            mode: str = "pool"):
+        """Process pairs for `seconds` (or `pairs` pairs); returns (units, elapsed_s).
+        mode "pool": one pair per worker on `threads` workers, one intra-op thread each;
+        "serial": pairs one after another, `threads` intra-op threads inside each operation."""
         from concurrent.futures import ThreadPoolExecutor
 
-        from threadpoolctl import threadpool_limits
-
+        deadline = None if seconds is None else time.perf_counter() + seconds
+        if mode == "serial":
+            kp, vp = self.new_pages()
+            units, k = 0, 0
+            with torch_threads(threads):
+                t0 = time.perf_counter()
+                while (pairs is None or k < pairs) and (deadline is None or time.perf_counter() < deadline):
+                    units += self.patch_one(k, kp, vp)
+                    k += 1
+                return units, time.perf_counter() - t0
         pages = [self.new_pages() for _ in range(threads)]
         counter = [0]
         lock = threading.Lock()
-        deadline = None if seconds is None else time.perf_counter() + seconds
 
         def worker(wi):
             done = 0
@@ -449,27 +535,37 @@ class CpuSample:
                     counter[0] += 1
                 done += self.patch_one(k, *pages[wi])
 
-        with threadpool_limits(1):
+        with torch_threads(1):
             t0 = time.perf_counter()
             with ThreadPoolExecutor(threads) as ex:
                 units = sum(ex.map(worker, range(threads)))
             el = time.perf_counter() - t0
         return units, el
 
+    def best_mode(self, threads: int) -> str:
+        """The faster of the two ways to spread the sample over the cores (each warmed up and
+        timed on `threads` pairs)."""
+        rate = {}
+        for mode in ("pool", "serial"):
+            self.run(threads, pairs=threads, mode=mode)
+            u, el = self.run(threads, pairs=threads, mode=mode)
+            rate[mode] = u / el
+        return max(rate, key=rate.get)
+
+
+MODE_TEXT = {"pool": "one pair per thread", "serial": "pairs in turn, every thread inside each operation"}
+
 
 def exact_cpu_baseline(G, seconds: float, seq_len: int) -> dict:
-    from threadpoolctl import threadpool_limits
-
     threads = cpu_pool_threads()
     sample = CpuSample(G, n_inputs=4, seq_len=seq_len)
-    with threadpool_limits(1):
-        share = sample.dequant_share()
-    sample.run(threads, pairs=threads)  # warm-up: every thread once
-    units, el = sample.run(threads, seconds=seconds)
+    share = sample.dequant_share(threads)
+    mode = sample.best_mode(threads)
+    units, el = sample.run(threads, seconds=seconds, mode=mode)
     return {"value": units / el, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
-            "sample": f"{units // seq_len} (layer, sequence) pairs of {seq_len} tokens in {el:.1f} s (oracle "
-                      f"numpy port of the reference's exact branch: dequant, RMSNorm, exact_kv_patch, materialize, "
-                      f"scatter_into_paged; {threads} threads, one pair per thread)",
+            "sample": f"{units // seq_len} (layer, sequence) pairs of {seq_len} tokens in {el:.1f} s (the "
+                      f"reference's exact branch in its own torch CPU operations: dequant, RMSNorm, exact_kv_patch, "
+                      f"materialize, scatter_into_paged; {threads} threads, {MODE_TEXT[mode]})",
             "dequant_share": share,
             "dequant_note": "fraction of a pair's time in the stored-activation dequantisation, timed on its own "
                             "(the reference keeps fp32 activations and has no such step)",
@@ -732,11 +828,12 @@ def run_exact_e2e(args, G, patcher, dist: Dist, layers, weak):
 def run_exact_reference(args, G) -> dict:
     threads = cpu_pool_threads()
     sample = CpuSample(G, n_inputs=4, seq_len=args.seq_len)
+    mode = sample.best_mode(threads)
     for _ in range(args.warmup):
-        sample.run(threads, pairs=threads)
+        sample.run(threads, pairs=threads, mode=mode)
     units_tot, el_tot = 0, 0.0
     for _ in range(args.steps):
-        u, el = sample.run(threads, pairs=threads)
+        u, el = sample.run(threads, pairs=threads, mode=mode)
         units_tot += u
         el_tot += el
     value = units_tot / el_tot
@@ -747,9 +844,9 @@ def run_exact_reference(args, G) -> dict:
         "config": {"workload": G.workload, "step": f"{threads} (layer, sequence) pairs of {args.seq_len} tokens "
                    "(bounded sample of the workload)"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
-                         "sample": f"{threads} (layer, sequence) pairs per step, oracle numpy port of the "
-                                   "reference's exact branch (dequant, RMSNorm, exact_kv_patch, materialize, "
-                                   "scatter_into_paged), one pair per thread"},
+                         "sample": f"{threads} (layer, sequence) pairs per step, the reference's exact branch in "
+                                   "its own torch CPU operations (dequant, RMSNorm, exact_kv_patch, materialize, "
+                                   f"scatter_into_paged), {MODE_TEXT[mode]}"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -812,90 +909,62 @@ def make_dense_workload(layers, n_seqs, seq_len, device, seed, x_buffers: int | 
 
 class DenseCpuSample:
     """Bounded host sample of the dense route: (layer, 256-token chunk) items through the
-    oracle port of the reference's exact route with A = dW, B = I (one chunk per worker)."""
+    reference's exact route with A = dW, B = I in its torch CPU operations (`oracle.exact_torch`)."""
 
     CHUNK = 256
 
     def __init__(self, seed: int = 5):
-        from oracle import dense as OD
         from oracle import exact as OX
+        from oracle import exact_torch as OT
 
         G = Dense70B
         g = torch.Generator().manual_seed(seed)
         d_kv = G.n_kv * G.hd
-        self.x = (torch.randn(self.CHUNK, G.d_model, generator=g)).to(torch.bfloat16).float().numpy()
+        self.x = torch.randn(self.CHUNK, G.d_model, generator=g).to(torch.bfloat16).float()
         sig = 1e-3 * 0.02
-        self.fk, self.fv = OD.dense_factors((torch.randn(d_kv, G.d_model, generator=g) * sig).numpy(),
-                                            (torch.randn(d_kv, G.d_model, generator=g) * sig).numpy())
-        self.rope = OX.rope_tables(G.hd, self.CHUNK, G.rope_theta)
+        eye = torch.eye(d_kv)
+        self.fk = (torch.randn(d_kv, G.d_model, generator=g) * sig, eye, 1.0)
+        self.fv = (torch.randn(d_kv, G.d_model, generator=g) * sig, eye, 1.0)
+        cos_h, sin_h = OX.rope_tables(G.hd, self.CHUNK, G.rope_theta)
+        self.rope = OT.rope_full(torch.from_numpy(cos_h), torch.from_numpy(sin_h), self.CHUNK)
         self.nblk = self.CHUNK // G.bs
-        self.table = list(np.random.default_rng(seed).permutation(self.nblk))
+        self.table = torch.from_numpy(np.random.default_rng(seed).permutation(self.nblk))
+        self.pages = threading.local()
 
-    def new_pages(self):
-        G = Dense70B
-        rng = np.random.default_rng(0)
-        shape = (self.nblk, G.bs, G.n_kv, G.hd)
-        return (rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16),
-                rng.integers(0x3C00, 0x3F80, size=shape, dtype=np.uint16))
-
-    def patch_one(self, kp, vp) -> int:
-        from oracle import exact as OX
+    def item(self) -> int:
+        from oracle import exact_torch as OT
 
         G = Dense70B
-        dk, dv = OX.exact_kv_delta(self.x, self.fk, self.fv, G.n_kv, G.hd, self.rope)
-        OX.scatter_into_paged(dk, kp, self.table, G.bs, kind="bf16")
-        OX.scatter_into_paged(dv, vp, self.table, G.bs, kind="bf16")
+        pg = getattr(self.pages, "kv", None)
+        if pg is None:  # one private paged K / V per worker thread
+            shape = (self.nblk, G.bs, G.n_kv, G.hd)
+            pg = self.pages.kv = ((1.0 + torch.rand(shape)).to(torch.bfloat16),
+                                  (1.0 + torch.rand(shape)).to(torch.bfloat16))
+        with torch.no_grad():
+            dk, dv = OT.exact_kv_delta(self.x, self.fk, self.fv, G.n_kv, G.hd, self.rope)
+            OT.scatter_into_paged(dk, pg[0], self.table, G.bs)
+            OT.scatter_into_paged(dv, pg[1], self.table, G.bs)
         return self.CHUNK
 
-    def run(self, threads: int, seconds: float | None = None, items: int | None = None):
-        from concurrent.futures import ThreadPoolExecutor
-
-        from threadpoolctl import threadpool_limits
-
-        pages = [self.new_pages() for _ in range(threads)]
-        counter = [0]
-        lock = threading.Lock()
-        deadline = None if seconds is None else time.perf_counter() + seconds
-
-        def worker(wi):
-            done = 0
-            while True:
-                with lock:
-                    if items is not None and counter[0] >= items:
-                        return done
-                    if deadline is not None and time.perf_counter() >= deadline:
-                        return done
-                    counter[0] += 1
-                done += self.patch_one(*pages[wi])
-
-        with threadpool_limits(1):
-            t0 = time.perf_counter()
-            with ThreadPoolExecutor(threads) as ex:
-                units = sum(ex.map(worker, range(threads)))
-            el = time.perf_counter() - t0
-        return units, el
+    def measure(self, threads: int, seconds: float) -> dict:
+        u, el, how = host_rate(self.item, threads, seconds)
+        return {"value": u / el, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
+                "sample": f"{u // self.CHUNK} (layer, {self.CHUNK}-token chunk) items in {el:.1f} s (the "
+                          f"reference's exact route with A=dW, B=I in its torch CPU operations: x @ dW^T, RoPE, "
+                          f"scatter_into_paged; {threads} threads, {how})"}
 
 
 def run_dense_reference(args) -> dict:
     threads = host_threads()
     sample = DenseCpuSample()
-    for _ in range(args.warmup):
-        sample.run(threads, items=threads)
-    units_tot, el_tot = 0, 0.0
-    for _ in range(args.steps):
-        u, el = sample.run(threads, items=threads)
-        units_tot += u
-        el_tot += el
-    value = units_tot / el_tot
+    res = [sample.measure(threads, max(2.0, args.cpu_seconds / max(1, args.steps))) for _ in range(args.steps)]
+    value = sum(r["value"] for r in res) / len(res)
     return {
         "impl": "reference", "metric": Dense70B.metric, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el_tot / args.steps,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": Dense70B.workload, "step": f"{threads} (layer, {DenseCpuSample.CHUNK}-token chunk) "
-                   "items (bounded sample of the workload)"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
-                         "sample": f"{threads} items per step, oracle numpy port of the reference's exact route "
-                                   "with A=dW, B=I (x @ dW^T, RoPE, scatter_into_paged)"},
+        "config": {"workload": Dense70B.workload, "step": res[0]["sample"]},
+        "cpu_baseline": {**res[0], "value": value},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -955,14 +1024,7 @@ def run_dense(args, dist: Dist) -> dict:
     torch.cuda.empty_cache()
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
-        threads = host_threads()
-        sample = DenseCpuSample()
-        sample.run(threads, items=threads)
-        u, el = sample.run(threads, seconds=args.sub_cpu_seconds)
-        cpu = {"value": u / el, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
-               "sample": f"{u // DenseCpuSample.CHUNK} (layer, {DenseCpuSample.CHUNK}-token chunk) items in "
-                         f"{el:.1f} s (oracle numpy port of the reference's exact route with A=dW, B=I, "
-                         f"{threads} threads)"}
+        cpu = DenseCpuSample().measure(host_threads(), args.sub_cpu_seconds)
     return {
         "metric": G.metric, "value": units_step / (ms_step / 1e3), "unit": UNIT, "n_gpus": dist.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -1354,51 +1416,34 @@ def run_kivi(args, dist: Dist) -> dict:
 
 
 def kivi_cpu_sample(seconds: float, n: int = 4096) -> dict:
-    """Oracle port of the route (dequant, subspace_correct, requant) on (layer, view) items of
-    `n` tokens, one item per worker thread."""
-    from concurrent.futures import ThreadPoolExecutor
-
-    from threadpoolctl import threadpool_limits
-
-    from oracle import kivi as OK
-    from oracle import subspace as OS
+    """The route on the host (dequantise, subspace_correct, requantise; K and V of one (layer,
+    view) of `n` tokens per item) in the reference's torch CPU operations (`oracle.subspace_torch`)."""
+    from oracle import subspace_torch as OST
 
     G = KiviGeo
     d = G.n_kv * G.hd
-    rng = np.random.default_rng(7)
-    base = OK.quantize(rng.standard_normal((n, d), dtype=np.float32), "v")
-    B = (rng.standard_normal((d, 16), dtype=np.float32) / np.sqrt(d)).astype(np.float32)
-    fresh = (OK.dequantize(*base, "v") + (rng.standard_normal((n, 16), dtype=np.float32) * 0.5) @ B.T).astype(np.float32)
-    probes = np.unique(np.concatenate([[0], rng.permutation(n)[: int(0.1 * n)]]))
+    g = torch.Generator().manual_seed(7)
+    B = torch.randn(d, 16, generator=g) / math.sqrt(d)
+    probes = torch.unique(torch.cat([torch.zeros(1, dtype=torch.int64), torch.randperm(n, generator=g)[: n // 10]]))
+    problems = []
+    for mode in ("k", "v"):
+        base = OST.quantize(torch.randn(n, d, generator=g), mode)
+        fresh = OST.dequantize(*base, mode) + (torch.randn(n, 16, generator=g) * 0.5) @ B.T
+        problems.append((mode, base, fresh))
     threads = host_threads()
 
     def item():
-        reused = OK.dequantize(*base, "v")
-        corr, _, _ = OS.subspace_correct(reused.reshape(n, G.n_kv, G.hd), fresh.reshape(n, G.n_kv, G.hd), probes,
-                                         basis=B, rank=16)
-        OK.quantize(corr.reshape(n, d), "v")
+        with torch.no_grad():
+            for mode, base, fresh in problems:
+                corr, _, _ = OST.subspace_correct(OST.dequantize(*base, mode), fresh, probes, B)
+                OST.quantize(corr, mode)
         return n
 
-    deadline = time.perf_counter() + seconds
-    lock = threading.Lock()
-    done = [0]
-
-    def worker(_):
-        u = 0
-        while time.perf_counter() < deadline:
-            u += item()
-        with lock:
-            done[0] += u
-        return u
-
-    with threadpool_limits(1):
-        t0 = time.perf_counter()
-        with ThreadPoolExecutor(threads) as ex:
-            list(ex.map(worker, range(threads)))
-        el = time.perf_counter() - t0
-    return {"value": done[0] / el, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
-            "sample": f"{done[0] // n} (layer, view) items of {n} tokens, rank 16, V grouping, in {el:.1f} s "
-                      f"(oracle numpy port: dequant, subspace_correct, requant; {threads} threads)"}
+    units, el, how = host_rate(item, threads, seconds)
+    return {"value": units / el, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
+            "sample": f"{units // n} (layer, view) items of {n} tokens (K and V), rank 16, in {el:.1f} s (the "
+                      f"route in the reference's torch CPU operations: dequant, subspace_correct, requant; "
+                      f"{threads} threads, {how})"}
 
 
 def run_kivi_reference(args) -> dict:
@@ -1476,48 +1521,31 @@ def dsub_parity(probs) -> dict:
 
 
 def dsub_cpu_sample(seconds: float, n: int = 4096) -> dict:
-    """Oracle port of subspace_correct on (layer, K|V) items of `n` tokens, one per thread."""
-    from concurrent.futures import ThreadPoolExecutor
-
-    from threadpoolctl import threadpool_limits
-
-    from oracle import subspace as OS
+    """subspace_correct on the host (K and V of one layer of `n` tokens per item) in the
+    reference's torch CPU operations (`oracle.subspace_torch`)."""
+    from oracle import subspace_torch as OST
 
     G = DsubGeo
     d = G.n_kv * G.hd
-    rng = np.random.default_rng(11)
-    reused = rng.standard_normal((n, d), dtype=np.float32)
-    B = np.linalg.qr(rng.standard_normal((d, G.rank)))[0].astype(np.float32)
-    fresh = (reused + (rng.standard_normal((n, G.rank), dtype=np.float32) * 0.3) @ B.T).astype(np.float32)
-    probes = np.sort(rng.permutation(n)[: int(G.probe_ratio * n)])
+    g = torch.Generator().manual_seed(11)
+    probes = torch.sort(torch.randperm(n, generator=g)[: int(G.probe_ratio * n)]).values
+    problems = []
+    for _ in range(2):
+        reused = torch.randn(n, d, generator=g)
+        B = torch.linalg.qr(torch.randn(d, G.rank, generator=g))[0]
+        problems.append((reused, reused + (torch.randn(n, G.rank, generator=g) * 0.3) @ B.T, B))
     threads = host_threads()
 
     def item():
-        OS.subspace_correct(reused.reshape(n, G.n_kv, G.hd), fresh.reshape(n, G.n_kv, G.hd), probes, basis=B,
-                            rank=G.rank)
+        with torch.no_grad():
+            for reused, fresh, B in problems:
+                OST.subspace_correct(reused, fresh, probes, B)
         return n
 
-    deadline = time.perf_counter() + seconds
-    lock = threading.Lock()
-    done = [0]
-
-    def worker(_):
-        u = 0
-        while time.perf_counter() < deadline:
-            u += item()
-        with lock:
-            done[0] += u
-        return u
-
-    with threadpool_limits(1):
-        t0 = time.perf_counter()
-        with ThreadPoolExecutor(threads) as ex:
-            list(ex.map(worker, range(threads)))
-        el = time.perf_counter() - t0
-    # one item is one of a token·layer's two problems (K or V)
-    return {"value": done[0] / 2 / el, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
-            "sample": f"{done[0] // n} (layer, K|V) items of {n} tokens, rank 16, in {el:.1f} s "
-                      f"(oracle numpy port of subspace_correct; {threads} threads)"}
+    units, el, how = host_rate(item, threads, seconds)
+    return {"value": units / el, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
+            "sample": f"{units // n} layers of {n} tokens (K and V), rank 16, in {el:.1f} s (subspace_correct in "
+                      f"the reference's torch CPU operations; {threads} threads, {how})"}
 
 
 def dsub_e2e(args, probs, dist: Dist, stream, n_layers: int = 4) -> dict:
@@ -1678,13 +1706,14 @@ def _snapshot(h, hm):
 
 
 def analytic_cpu_sample(seconds: float, n: int = 2048, layers: int = 1) -> dict:
-    """The oracle port (numpy fp64) of the engine's analytic loop on ``layers`` layers of one
-    ``n``-token sequence of the same shape, repeated for about ``seconds``."""
-    from oracle import analytic as OA
+    """The engine's analytic loop on ``layers`` layers of one ``n``-token sequence of the same
+    shape, in the reference's fp32 torch CPU operations (`oracle.analytic_torch`), repeated for
+    about ``seconds``."""
+    from oracle import analytic_torch as OAT
 
     G = AnalyticGeo
-    rng = np.random.default_rng(0)
-    rnd = lambda *shape, s=0.02: rng.standard_normal(shape) * s
+    g = torch.Generator().manual_seed(0)
+    rnd = lambda *shape, s=0.02: torch.randn(*shape, generator=g) * s  # noqa: E731
     dq, dkv = G.n_heads * G.hd, G.n_kv * G.hd
     W, Ls = [], {}
     for l in range(layers):
@@ -1696,18 +1725,26 @@ def analytic_cpu_sample(seconds: float, n: int = 2048, layers: int = 1) -> dict:
                                         ("o", (dq, G.d_model)))}
     cfg = dict(n_heads=G.n_heads, n_kv=G.n_kv, hd=G.hd, d_model=G.d_model, eps=G.eps, rope_base=G.rope_theta,
                hidden_stride=G.hidden_stride, propagator_rank=G.propagator_rank)
-    h, hm = rng.standard_normal((layers, n, G.d_model)), rng.standard_normal((layers, n, G.d_model))
-    t0, done = time.perf_counter(), 0
-    while True:
-        OA.analytic_patches(h, hm, W, Ls, cfg)
-        done += 1
-        el = time.perf_counter() - t0
-        if el >= seconds:
-            break
-    return {"value": done * layers * n / el, "unit": UNIT, "cores": cpu_pool_threads(), "cpu_model": cpu_model(),
-            "kind": "port",
-            "sample": f"{done} x ({layers} layer x {n} tokens) of the engine's analytic loop in {el:.1f} s "
-                      "(oracle numpy fp64 port, attention materialised; BLAS threads for the matrix products)"}
+    h, hm = torch.randn(layers, n, G.d_model, generator=g), torch.randn(layers, n, G.d_model, generator=g)
+
+    def item():
+        with torch.no_grad():
+            OAT.analytic_patches(h, hm, W, Ls, cfg)
+        return layers * n
+
+    # each item holds ~1 GB of [heads, n, n] fp32 matrices
+    threads = host_threads()
+    try:
+        import psutil
+
+        threads = max(1, min(threads, int(psutil.virtual_memory().available * 0.5 // (1 << 30))))
+    except Exception:
+        pass
+    units, el, how = host_rate(item, threads, seconds)
+    return {"value": units / el, "unit": UNIT, "cores": threads, "cpu_model": cpu_model(), "kind": "port",
+            "sample": f"{units // (layers * n)} x ({layers} layer x {n} tokens) of the engine's analytic loop in "
+                      f"{el:.1f} s (the reference's fp32 torch CPU operations, attention materialised; {threads} "
+                      f"threads, {how})"}
 
 
 def run_analytic(args, dist: Dist) -> dict:
@@ -1806,7 +1843,7 @@ def run_analytic_reference(args) -> dict:
     return {
         "impl": "reference", "metric": ANALYTIC_METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": ANALYTIC_WORKLOAD, "step": res[0]["sample"]},
         "cpu_baseline": {**res[0], "value": value},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

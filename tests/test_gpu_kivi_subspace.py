@@ -236,10 +236,12 @@ def test_kivi_probe_residuals_batched(cuda, fdt, d):
         np.testing.assert_array_equal(got[j], K.probe_residual(bases[j], freshes[j], probes[j]).cpu().numpy())
 
 
-def test_kivi_subspace_views_pipelined_matches_sequential(cuda):
+@pytest.mark.parametrize("last_in_place", [True, False])
+def test_kivi_subspace_views_pipelined_matches_sequential(cuda, last_in_place):
     # three adapter views over one shared int4 prefix (K bases from the probe residual, V the
-    # adapter's B), the last correcting its own copy in place: the side-stream pipeline gives
-    # what view-by-view calls give (probe sums are atomics, so up to float summation order)
+    # adapter's B): the side-stream pipeline gives what view-by-view calls give (probe sums are
+    # atomics, so up to float summation order) — with the last view correcting its own copy in
+    # place and with every view writing its own output
     gen = torch.Generator().manual_seed(99)
     n, n_kv, hd = 512, 2, 64
     d = n_kv * hd
@@ -256,7 +258,7 @@ def test_kivi_subspace_views_pipelined_matches_sequential(cuda):
                 base = _device_base(cs, cuda)
                 fresh = (cs["fresh"] + 0.05 * torch.randn(n, d, generator=g)).to(torch.bfloat16).to(cuda)
                 B = (torch.randn(d, 8, generator=g) / d ** 0.5).to(cuda)
-                dst = None if a == 2 else K.KiviTensor.empty(n, d, m, cuda)
+                dst = None if a == 2 and last_in_place else K.KiviTensor.empty(n, d, m, cuda)
                 probs.append(K.SubspaceProblem(base=base, fresh=fresh, probe_index=probes.to(cuda),
                                                basis=None if m == "k" else B, rank=8, out=dst))
             out.append(probs)

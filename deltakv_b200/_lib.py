@@ -57,6 +57,7 @@ EXPORTED = (
     "dkv_row_diff_norms",
     "dkv_sym_eig_batched",
     "dkv_gram_subspace_iterate",
+    "dkv_split_gemm_batched",
     "dkv_attn_first_order",
     "dkv_rmsnorm_first_order",
     "dkv_swiglu_first_order",
@@ -325,6 +326,8 @@ def _declare(lib: C.CDLL) -> None:
     lib.dkv_sym_eig_batched.argtypes = [P, I64, I32, I64, I32, P, P, P, P]
     lib.dkv_gram_subspace_iterate.restype = C.c_int
     lib.dkv_gram_subspace_iterate.argtypes = [P, I32, P, I32, I32, P, P, P, P, P]
+    lib.dkv_split_gemm_batched.restype = C.c_int
+    lib.dkv_split_gemm_batched.argtypes = [P, I64, I64, I32, P, I64, I64, P, I64, I64, I64, I32, I32, I32, P]
     lib.dkv_attn_first_order.restype = C.c_int
     lib.dkv_attn_first_order.argtypes = [P, P, I64, P, P, P, P, I64, I32, I32, I32, I32, I32, C.c_float, P, P, I64,
                                          P]

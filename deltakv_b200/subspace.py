@@ -110,9 +110,40 @@ def _start_block(n_b: int, d: int, k: int, device: torch.device) -> tuple[Tensor
     return hit
 
 
+THIN_MAX_N = 96  # widest product the split-precision thin GEMM takes
+
+
+def thin_mm(a: Tensor, b: Tensor, *, trans_a: bool = False) -> Tensor:
+    """``op(a) @ b`` for fp32 ``a [bt, m, k]`` (``trans_a``: ``a [bt, k, m]``, used transposed)
+    and ``b [bt, k, n]``: the subspace iteration's thin products on the tensor cores with
+    split-precision operands (``dkv_split_gemm_batched``, within ~1e-5 relative of fp32).  The
+    result is ``[bt, m, n16]`` with ``n16`` = n rounded up to 16 (columns past n are zero, so it
+    can be passed on as the next product's ``b`` as it is); shapes the kernel does not take go to
+    the library GEMM and come back ``[bt, m, n]``."""
+    bt = int(a.shape[0])
+    m, k = (int(a.shape[2]), int(a.shape[1])) if trans_a else (int(a.shape[1]), int(a.shape[2]))
+    n = int(b.shape[2])
+    n16 = (n + 15) // 16 * 16
+    ok = (a.is_cuda and a.dtype == torch.float32 and b.dtype == torch.float32 and 0 < n16 <= THIN_MAX_N
+          and bt <= 65535 and a.stride(2) == 1 and a.stride(1) % 4 == 0 and a.stride(0) % 4 == 0
+          and a.data_ptr() % 16 == 0 and (m % 4 == 0 if trans_a else k % 4 == 0))
+    if not ok:
+        return torch.matmul(a.transpose(1, 2) if trans_a else a, b)
+    if (b.shape[2] != n16 or b.stride(2) != 1 or b.stride(1) % 4 or b.stride(0) % 4 or b.data_ptr() % 16):
+        bp = torch.zeros(bt, k, n16, dtype=torch.float32, device=b.device)
+        bp[:, :, :n] = b
+        b = bp
+    out = torch.empty(bt, m, n16, dtype=torch.float32, device=a.device)
+    rc = L.lib().dkv_split_gemm_batched(a.data_ptr(), a.stride(0), a.stride(1), int(trans_a), b.data_ptr(),
+                                        b.stride(0), b.stride(1), out.data_ptr(), out.stride(0), out.stride(1), bt,
+                                        m, n16, k, ops.stream_ptr())
+    L.check(rc, "dkv_split_gemm_batched")
+    return out
+
+
 def _ritz(x: Tensor, q: Tensor, r: int) -> tuple[Tensor, Tensor, Tensor]:
     """Rayleigh-Ritz on span(q): the top-``r`` Ritz vectors of ``x^T x`` and all Ritz values."""
-    w = torch.matmul(x, q)
+    w = thin_mm(x, q)[:, :, :q.shape[2]]
     ev, vec, info = sym_eig(torch.matmul(w.transpose(1, 2), w))
     return torch.matmul(q, vec[:, :, :r].float()), ev, info
 
@@ -287,7 +318,8 @@ def topr_basis(residual: Tensor, rank: int, *, iters: int = 3, min_iters: int = 
     ``C = R^T R`` — applied as ``R^T (R Q)``, never formed — with re-orthonormalisation and a
     Rayleigh-Ritz step (Golub & Van Loan, Matrix Computations, 4th ed., Sec. 8.2.4; Halko,
     Martinsson & Tropp, SIAM Review 2011, Alg. 4.4) on ``k = rank + oversample`` columns
-    instead of a full SVD; the k x k Rayleigh-Ritz eigenproblem runs on the device
+    instead of a full SVD; the thin products run on the tensor cores with split-precision
+    operands (:func:`thin_mm`) and the k x k Rayleigh-Ritz eigenproblem on the device
     (:func:`sym_eig`).  The subspace converges as ``(l_k / l_rank)^i`` after ``i`` products
     (eigenvalues of C); the least-squares correction depends on the basis only through its
     column space, so the rotation within the subspace is immaterial.  Every element gets
@@ -312,9 +344,9 @@ def topr_basis(residual: Tensor, rank: int, *, iters: int = 3, min_iters: int = 
     tol = 1e-5
 
     def iterate(xb: Tensor, q: Tensor, bad: Tensor, n: int) -> tuple[Tensor, Tensor]:
-        xt = xb.transpose(1, 2)
         for _ in range(n):
-            q, b2 = _orthonormalize(torch.matmul(xt, torch.matmul(xb, q)))
+            z = thin_mm(xb, thin_mm(xb, q), trans_a=True)[:, :, :q.shape[2]]  # X^T (X Q)
+            q, b2 = _orthonormalize(z)
             bad = bad | b2
         return q, bad
 

@@ -439,6 +439,19 @@ int dkv_sym_eig_batched(const double *a, int64_t batch, int32_t k, int64_t a_str
 int dkv_gram_subspace_iterate(const double *g, int32_t d, double *q, int32_t k, int32_t iters, double *y,
                               double *w, double *t, int32_t *status, dkv_stream_t stream);
 
+/* c[i] = op(a[i]) b[i] for i < batch, fp32 in and out, on the tensor cores with every operand
+   split into two bf16 terms (products lo*hi + hi*lo + hi*hi, fp32 accumulation; within ~1e-5
+   relative of an fp32 product).  a[i] is [m, k] row-major (lda) or, with trans_a, stored
+   [k, m] row-major (lda) and used transposed; b[i] is [k, n], c[i] is [m, n], row-major.
+   n is a multiple of 16, at most 96 (pad with zero columns); a and b 16-byte aligned, c 8-byte;
+   lda, ldb and the batch strides of a and b multiples of 4, ldc and c's batch stride even;
+   k % 4 == 0 (m % 4 == 0 with trans_a).  The thin products X Q, X^T (X Q) of the subspace
+   iteration and the Rayleigh-Ritz step that stand in for svd_basis (patches/subspace.py:37-42),
+   X the probe residual of one layer. */
+int dkv_split_gemm_batched(const float *a, int64_t a_batch_stride, int64_t lda, int32_t trans_a, const float *b,
+                           int64_t b_batch_stride, int64_t ldb, float *c, int64_t c_batch_stride, int64_t ldc,
+                           int64_t batch, int32_t m, int32_t n, int32_t k, dkv_stream_t stream);
+
 /*
  * Subspace correction of a KIVI int4 cache (the multi-adapter maintenance step): for each
  * problem (one layer's K or V of one adapter view), reused = dequant(base), then exactly

@@ -64,6 +64,18 @@ def test_calls_without_a_gpu_fail_cleanly_on_bad_arguments():
     lib = L.lib()
     assert lib.dkv_scatter_paged(None, 0, 0, 0, None, None, None, None) == L.DKV_ERR_INVALID_ARGUMENT
     assert lib.dkv_exact_patch_paged(None, None) == L.DKV_ERR_INVALID_ARGUMENT
+    # the split-precision thin GEMM checks its shape and layout before touching memory
+    sg = lambda a, lda, tr, b, ldb, c, ldc, m, n, k: lib.dkv_split_gemm_batched(a, 0, lda, tr, b, 0, ldb, c, 0, ldc,
+                                                                               1, m, n, k, None)
+    p16 = 1 << 20  # a 16-byte-aligned stand-in address, never dereferenced on these paths
+    assert sg(p16, 64, 0, p16, 24, p16, 24, 8, 24, 64) == L.DKV_ERR_UNSUPPORTED    # n not a multiple of 16
+    assert sg(p16, 64, 0, p16, 112, p16, 112, 8, 112, 64) == L.DKV_ERR_UNSUPPORTED  # n above 96
+    assert sg(p16 + 4, 64, 0, p16, 16, p16, 16, 8, 16, 64) == L.DKV_ERR_ALIGNMENT  # a not 16-byte aligned
+    assert sg(p16, 66, 0, p16, 16, p16, 16, 8, 16, 64) == L.DKV_ERR_ALIGNMENT      # lda not whole float4s
+    assert sg(p16, 64, 0, p16, 16, p16, 16, 8, 16, 62) == L.DKV_ERR_ALIGNMENT      # k % 4
+    assert sg(p16, 64, 1, p16, 16, p16, 16, 6, 16, 64) == L.DKV_ERR_ALIGNMENT      # m % 4 with trans_a
+    assert sg(None, 64, 0, p16, 16, p16, 16, 8, 16, 64) == L.DKV_ERR_INVALID_ARGUMENT
+    assert sg(p16, 64, 0, p16, 16, p16, 16, 0, 16, 64) == L.DKV_OK                 # nothing to do
 
 
 def test_page_view_matches_reference_layout_dispatch():

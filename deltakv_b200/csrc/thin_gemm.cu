@@ -14,11 +14,12 @@
 //
 // Layout: A[b] is [M, K] row-major (lda) or, with trans_a, stored [K, M] row-major (lda) and
 // used transposed; B[b] is [K, N] row-major (ldb) with N a multiple of 16 (at most 96); C[b] is
-// [M, N] row-major (ldc).  One CTA of 4 warps computes 64 rows of C x all N columns; K is walked
-// in chunks of 32 staged by cp.async two deep.  Within a 16-wide k-step lane (g, q) holds
+// [M, N] row-major (ldc).  One CTA of 4 warps computes 64 rows of C (128 for a wide A [M, K]:
+// two m-tiles per warp share each B fragment) x all N columns; K is walked in chunks of 32 staged
+// by cp.async two deep.  Within a 16-wide k-step lane (g, q) holds
 // physical k = 4q..4q+3 of its rows (a float4), and the B fragments are permuted the same way,
 // which leaves the product unchanged; each chunk's B is split into bf16 fragment images once per
-// CTA, the A fragments by each warp for its own 16 rows.
+// CTA, the A fragments by each warp for its own rows.
 #include <algorithm>
 
 #include "dkv_common.cuh"
@@ -27,25 +28,36 @@ namespace dkv {
 namespace tg {
 
 constexpr int kThreads = 128;
-constexpr int kTM = 64;         // rows of C per CTA (16 per warp)
 constexpr int kKC = 32;         // k per staged chunk: two 16-wide MMA k-steps
 constexpr int kStrideN = 36;    // floats per staged A row, A [M, K]: 32 k + 4 of padding
-constexpr int kStrideT = 68;    // floats per staged A row, A stored [K, M]: 64 m + 4 of padding
-constexpr int kAStage = std::max(kTM * kStrideN, kKC * kStrideT);  // floats
 constexpr int kMaxN = 96;
 
-template <int NP>
+// MT m-tiles of 16 rows per warp: a CTA computes 64 MT rows of C
+template <int MT>
+constexpr int tile_m() {
+  return 64 * MT;
+}
+template <int MT>
+constexpr int stride_t() {  // floats per staged A row, A stored [K, M]: 64 MT m + 4 of padding
+  return tile_m<MT>() + 4;
+}
+template <int MT>
+constexpr int a_stage() {  // floats
+  return std::max(tile_m<MT>() * kStrideN, kKC * stride_t<MT>());
+}
+template <int MT, int NP>
 constexpr int smem_bytes() {
   // two stages of A and B (fp32), then the B fragment image [2 terms][2 k-steps][NP/8][32] (uint2)
-  return 2 * (kAStage + kKC * NP) * 4 + 2 * 2 * (NP / 8) * 32 * 8;
+  return 2 * (a_stage<MT>() + kKC * NP) * 4 + 2 * 2 * (NP / 8) * 32 * 8;
 }
 
-template <bool TRANS, int NP>
+template <bool TRANS, int MT, int NP>
 __global__ void __launch_bounds__(kThreads) split_gemm_kernel(const float *__restrict__ A, int64_t a_bs,
                                                               int64_t lda, const float *__restrict__ B,
                                                               int64_t b_bs, int64_t ldb, float *__restrict__ Cm,
                                                               int64_t c_bs, int64_t ldc, int M, int K) {
   constexpr int NT = NP / 8;
+  constexpr int kTM = tile_m<MT>(), kStrideT = stride_t<MT>(), kAStage = a_stage<MT>();
   extern __shared__ __align__(16) float tg_smem[];
   float *const a_st = tg_smem;                       // [2][kAStage]
   float *const b_st = tg_smem + 2 * kAStage;         // [2][kKC * NP]
@@ -64,14 +76,15 @@ __global__ void __launch_bounds__(kThreads) split_gemm_kernel(const float *__res
     const int k0 = ch * kKC;
     float *const as = a_st + buf * kAStage;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 4 * MT; ++i) {
       if constexpr (!TRANS) {
         const int r = (tid >> 3) + 16 * i, c4 = tid & 7;
         const int gm = m0 + r, gk = k0 + 4 * c4;
         const bool ok = gm < M && gk < K;
         cp_async16(as + r * kStrideN + 4 * c4, ok ? A + static_cast<int64_t>(gm) * lda + gk : A, ok ? 16u : 0u);
       } else {
-        const int r = (tid >> 4) + 8 * i, c4 = tid & 15;
+        constexpr int kRow4 = kTM / 4;  // float4s per staged row
+        const int e = tid + kThreads * i, r = e / kRow4, c4 = e - r * kRow4;
         const int gk = k0 + r, gm = m0 + 4 * c4;
         const bool ok = gk < K && gm < M;
         cp_async16(as + r * kStrideT + 4 * c4, ok ? A + static_cast<int64_t>(gk) * lda + gm : A, ok ? 16u : 0u);
@@ -88,9 +101,11 @@ __global__ void __launch_bounds__(kThreads) split_gemm_kernel(const float *__res
     cp_async_commit();
   };
 
-  float acc[NT][4];
+  float acc[MT][NT][4];
 #pragma unroll
-  for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+  for (int t = 0; t < MT; ++t)
+#pragma unroll
+    for (int j = 0; j < NT; ++j) acc[t][j][0] = acc[t][j][1] = acc[t][j][2] = acc[t][j][3] = 0.f;
 
   if (nchunks > 0) stage(0, 0);
   for (int ch = 0; ch < nchunks; ++ch) {
@@ -115,65 +130,83 @@ __global__ void __launch_bounds__(kThreads) split_gemm_kernel(const float *__res
       bimg[(s * NT + j) * 32 + ln] = make_uint2(h01, h23);
       bimg[((2 + s) * NT + j) * 32 + ln] = make_uint2(l01, l23);
     }
-    // this warp's A fragments: rows 16 warp + g and + 8, physical k = 16 s + 4 q .. + 3
-    uint32_t ah[2][4], al[2][4];
+    // this warp's A fragments: m-tile t covers rows 16 (MT warp + t) + g and + 8, physical
+    // k = 16 s + 4 q .. + 3
+    uint32_t ah[MT][2][4], al[MT][2][4];
 #pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      float x0[4], x1[4];
-      if constexpr (!TRANS) {
-        const float4 u = *reinterpret_cast<const float4 *>(as + (16 * warp + g) * kStrideN + 16 * s + 4 * q);
-        const float4 w = *reinterpret_cast<const float4 *>(as + (16 * warp + g + 8) * kStrideN + 16 * s + 4 * q);
-        x0[0] = u.x, x0[1] = u.y, x0[2] = u.z, x0[3] = u.w;
-        x1[0] = w.x, x1[1] = w.y, x1[2] = w.z, x1[3] = w.w;
-      } else {
+    for (int t = 0; t < MT; ++t)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          x0[i] = as[(16 * s + 4 * q + i) * kStrideT + 16 * warp + g];
-          x1[i] = as[(16 * s + 4 * q + i) * kStrideT + 16 * warp + g + 8];
+      for (int s = 0; s < 2; ++s) {
+        const int rw = 16 * (MT * warp + t) + g;
+        float x0[4], x1[4];
+        if constexpr (!TRANS) {
+          const float4 u = *reinterpret_cast<const float4 *>(as + rw * kStrideN + 16 * s + 4 * q);
+          const float4 w = *reinterpret_cast<const float4 *>(as + (rw + 8) * kStrideN + 16 * s + 4 * q);
+          x0[0] = u.x, x0[1] = u.y, x0[2] = u.z, x0[3] = u.w;
+          x1[0] = w.x, x1[1] = w.y, x1[2] = w.z, x1[3] = w.w;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            x0[i] = as[(16 * s + 4 * q + i) * kStrideT + rw];
+            x1[i] = as[(16 * s + 4 * q + i) * kStrideT + rw + 8];
+          }
         }
+        split_bf16x2(x0[0], x0[1], ah[t][s][0], al[t][s][0]);
+        split_bf16x2(x1[0], x1[1], ah[t][s][1], al[t][s][1]);
+        split_bf16x2(x0[2], x0[3], ah[t][s][2], al[t][s][2]);
+        split_bf16x2(x1[2], x1[3], ah[t][s][3], al[t][s][3]);
       }
-      split_bf16x2(x0[0], x0[1], ah[s][0], al[s][0]);
-      split_bf16x2(x1[0], x1[1], ah[s][1], al[s][1]);
-      split_bf16x2(x0[2], x0[3], ah[s][2], al[s][2]);
-      split_bf16x2(x1[2], x1[3], ah[s][3], al[s][3]);
-    }
     __syncthreads();  // the image is complete
 #pragma unroll
     for (int s = 0; s < 2; ++s)
 #pragma unroll
       for (int j = 0; j < NT; ++j) {
         const uint2 bh = bimg[(s * NT + j) * 32 + lane], bl = bimg[((2 + s) * NT + j) * 32 + lane];
-        mma16816_bf16(acc[j], al[s][0], al[s][1], al[s][2], al[s][3], bh.x, bh.y);
-        mma16816_bf16(acc[j], ah[s][0], ah[s][1], ah[s][2], ah[s][3], bl.x, bl.y);
-        mma16816_bf16(acc[j], ah[s][0], ah[s][1], ah[s][2], ah[s][3], bh.x, bh.y);
+#pragma unroll
+        for (int t = 0; t < MT; ++t) {
+          mma16816_bf16(acc[t][j], al[t][s][0], al[t][s][1], al[t][s][2], al[t][s][3], bh.x, bh.y);
+          mma16816_bf16(acc[t][j], ah[t][s][0], ah[t][s][1], ah[t][s][2], ah[t][s][3], bl.x, bl.y);
+          mma16816_bf16(acc[t][j], ah[t][s][0], ah[t][s][1], ah[t][s][2], ah[t][s][3], bh.x, bh.y);
+        }
       }
     __syncthreads();  // every warp is done with this stage and the image before they are reused
   }
 
-  const int r0 = m0 + 16 * warp + g, r1 = r0 + 8;
 #pragma unroll
-  for (int j = 0; j < NT; ++j) {
-    const int col = 8 * j + 2 * q;
-    if (r0 < M) *reinterpret_cast<float2 *>(Cm + static_cast<int64_t>(r0) * ldc + col) = make_float2(acc[j][0], acc[j][1]);
-    if (r1 < M) *reinterpret_cast<float2 *>(Cm + static_cast<int64_t>(r1) * ldc + col) = make_float2(acc[j][2], acc[j][3]);
+  for (int t = 0; t < MT; ++t) {
+    const int r0 = m0 + 16 * (MT * warp + t) + g, r1 = r0 + 8;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int col = 8 * j + 2 * q;
+      if (r0 < M)
+        *reinterpret_cast<float2 *>(Cm + static_cast<int64_t>(r0) * ldc + col) = make_float2(acc[t][j][0], acc[t][j][1]);
+      if (r1 < M)
+        *reinterpret_cast<float2 *>(Cm + static_cast<int64_t>(r1) * ldc + col) = make_float2(acc[t][j][2], acc[t][j][3]);
+    }
   }
 }
 
 template <bool TRANS, int NP>
 int launch(const float *a, int64_t a_bs, int64_t lda, const float *b, int64_t b_bs, int64_t ldb, float *c,
            int64_t c_bs, int64_t ldc, int64_t batch, int m, int k, cudaStream_t st) {
-  constexpr int smem = smem_bytes<NP>();
+  // A [M, K] with 48 or more columns (the tall X Q products at ranks 32 and 64, bound by the
+  // per-chunk fragment work): 128 rows per CTA, so each chunk's B image serves twice the rows
+  // (measured 0.81 -> 0.64 ms for three products at 80 columns); narrower products, bound by
+  // memory, keep 64 rows and twice the CTAs (0.29 vs 0.34 ms at 16 columns); A stored [K, M]
+  // (X^T Y, M = d): 64, for enough CTAs over d
+  constexpr int MT = (TRANS || NP <= 32) ? 1 : 2;
+  constexpr int smem = smem_bytes<MT, NP>();
   // set once per device (no runtime-API call on later launches)
   static unsigned long long set_on = 0;
   int dev = 0;
   DKV_CUDA_CHECK(cudaGetDevice(&dev));
   if (dev >= 64 || !((set_on >> dev) & 1ull)) {
-    DKV_CUDA_CHECK(cudaFuncSetAttribute(split_gemm_kernel<TRANS, NP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        smem));
+    DKV_CUDA_CHECK(cudaFuncSetAttribute(split_gemm_kernel<TRANS, MT, NP>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     if (dev < 64) set_on |= 1ull << dev;
   }
-  const dim3 grid(static_cast<unsigned>((m + kTM - 1) / kTM), static_cast<unsigned>(batch));
-  split_gemm_kernel<TRANS, NP><<<grid, kThreads, smem, st>>>(a, a_bs, lda, b, b_bs, ldb, c, c_bs, ldc, m, k);
+  const dim3 grid(static_cast<unsigned>((m + tile_m<MT>() - 1) / tile_m<MT>()), static_cast<unsigned>(batch));
+  split_gemm_kernel<TRANS, MT, NP><<<grid, kThreads, smem, st>>>(a, a_bs, lda, b, b_bs, ldb, c, c_bs, ldc, m, k);
   DKV_CUDA_CHECK(cudaGetLastError());
   return DKV_OK;
 }

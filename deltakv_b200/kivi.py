@@ -267,8 +267,9 @@ def subspace_correct_views(views: list[list[SubspaceProblem]], *, stats: bool = 
     """:func:`subspace_correct` for several adapter views in turn (the reference's per-view
     ``apply_probe_to_cache`` loop, src/deltakv/patches/probe.py:112-165), with the K bases of
     view v + 1 computed on a side stream while view v's route runs: the bases' small solver
-    kernels fill the route's idle SM time.  A view that corrects a cache in place is finished
-    before the next view's bases read anything.  Returns one result list per view."""
+    kernels fill the route's idle SM time; view 0's problems that need no such basis run while
+    view 0's bases are computed.  A view that corrects a cache in place is finished before the
+    next view's bases read anything.  Returns one result list per view."""
     views = [v for v in views]
     if not views or not any(views):
         return [[] for _ in views]
@@ -288,14 +289,36 @@ def subspace_correct_views(views: list[list[SubspaceProblem]], *, stats: bool = 
     def in_place(probs: list[SubspaceProblem]) -> bool:
         return any(pb.out is None or pb.out.codes.data_ptr() == pb.base.codes.data_ptr() for pb in probs)
 
+    # view 0's problems that need no basis from the probe residual (V, whose basis is the
+    # adapter's B) go first, so the main stream is busy while view 0's K bases are computed —
+    # unless one of their outputs is a cache those bases read
+    first = views[0]
+    kpos = [i for i, pb in enumerate(first) if pb.basis is None and pb.probe_index.numel() >= 2]
+    opos = [i for i in range(len(first)) if i not in set(kpos)]
+    reads = {first[i].base.codes.data_ptr() for i in kpos}
+    writes = {(first[i].out or first[i].base).codes.data_ptr() for i in opos}
+    ahead = {}
+    if kpos and opos and not (reads & writes):
+        ready = torch.cuda.Event()
+        ready.record(main)  # the inputs were produced on main
+        ahead = dict(zip(opos, subspace_correct([first[i] for i in opos], stats=stats, check=False, bases={})))
+        side.wait_event(ready)
+        nxt = launch_bases(0, False)
+    else:
+        nxt = launch_bases(0, True)  # the inputs were produced on main
     out = []
-    nxt = launch_bases(0, True)  # the inputs were produced on main
     for v, probs in enumerate(views):
         kb, ev = nxt
         main.wait_event(ev)
         for t in kb.values():
             t.record_stream(main)
-        out.append(subspace_correct(probs, stats=stats, check=False, bases=kb) if probs else [])
+        if v == 0 and ahead:
+            rest = subspace_correct([first[i] for i in kpos], stats=stats, check=False,
+                                    bases={j: kb[i] for j, i in enumerate(kpos) if i in kb})
+            ahead.update(zip(kpos, rest))
+            out.append([ahead[i] for i in range(len(first))])
+        else:
+            out.append(subspace_correct(probs, stats=stats, check=False, bases=kb) if probs else [])
         if v + 1 < len(views):
             nxt = launch_bases(v + 1, in_place(probs))
     if check:

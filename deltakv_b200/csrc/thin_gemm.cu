@@ -14,8 +14,8 @@
 //
 // Layout: A[b] is [M, K] row-major (lda) or, with trans_a, stored [K, M] row-major (lda) and
 // used transposed; B[b] is [K, N] row-major (ldb) with N a multiple of 16 (at most 96); C[b] is
-// [M, N] row-major (ldc).  One CTA of 4 warps computes 64 rows of C (128 for a wide A [M, K]:
-// two m-tiles per warp share each B fragment) x all N columns; K is walked in chunks of 32 staged
+// [M, N] row-major (ldc).  One CTA of 4 warps computes 64 rows of C (128 when N >= 48: two
+// m-tiles per warp share each B fragment) x all N columns; K is walked in chunks of 32 staged
 // by cp.async two deep.  Within a 16-wide k-step lane (g, q) holds
 // physical k = 4q..4q+3 of its rows (a float4), and the B fragments are permuted the same way,
 // which leaves the product unchanged; each chunk's B is split into bf16 fragment images once per
@@ -189,12 +189,12 @@ __global__ void __launch_bounds__(kThreads) split_gemm_kernel(const float *__res
 template <bool TRANS, int NP>
 int launch(const float *a, int64_t a_bs, int64_t lda, const float *b, int64_t b_bs, int64_t ldb, float *c,
            int64_t c_bs, int64_t ldc, int64_t batch, int m, int k, cudaStream_t st) {
-  // A [M, K] with 48 or more columns (the tall X Q products at ranks 32 and 64, bound by the
-  // per-chunk fragment work): 128 rows per CTA, so each chunk's B image serves twice the rows
-  // (measured 0.81 -> 0.64 ms for three products at 80 columns); narrower products, bound by
-  // memory, keep 64 rows and twice the CTAs (0.29 vs 0.34 ms at 16 columns); A stored [K, M]
-  // (X^T Y, M = d): 64, for enough CTAs over d
-  constexpr int MT = (TRANS || NP <= 32) ? 1 : 2;
+  // 48 or more columns (the products at ranks 32 and 64, bound by the per-chunk fragment
+  // work): 128 rows per CTA, so each chunk's B image serves twice the rows (measured for one
+  // rank-64 view: three X Q products 0.81 -> 0.64 ms, two X^T Y 0.60 -> 0.48 ms); narrower
+  // products, bound by memory, keep 64 rows and twice the CTAs (three X Q at 16 columns: 0.29
+  // vs 0.34 ms)
+  constexpr int MT = NP <= 32 ? 1 : 2;
   constexpr int smem = smem_bytes<MT, NP>();
   // set once per device (no runtime-API call on later launches)
   static unsigned long long set_on = 0;
